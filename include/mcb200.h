@@ -1,0 +1,162 @@
+/*
+ * mcb200.h -- C ABI of the B200 (sm_100a) KV-cache decode path for modelcore.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, returns an int status
+ * (MCB_OK == 0, a negative mcb_status otherwise) and enqueues its work on the caller's CUDA
+ * stream (`stream` is a cudaStream_t passed as void*; NULL means the legacy default stream).
+ * Nothing here allocates device memory, synchronises the stream or keeps a pointer past the
+ * call, so every launch entry point can be recorded into a CUDA graph.  A failed host-side check
+ * returns before anything is enqueued; mcb_last_error() then returns the message (per thread).
+ *
+ * Tensor conventions (all device pointers, bf16 = IEEE bfloat16 stored as uint16):
+ *   cache slot   (B, Tmax, Hkv, D) contiguous bf16 -- one slot of modelcore's
+ *                (n_slots, B, Tmax, Hkv, D) KVCache.k_cache / v_cache, modelcore/cache.py:22-23.
+ *                Base 16-byte aligned; D a multiple of 16 in [16, 256] for decode attention.
+ *   q / k / v    (B, T, H, D) bf16 with arbitrary element strides for (b, t, h) and unit
+ *                stride on d (the view c_q(x).view(B, T, H, D) of modelcore/components/attention.py:139-143).
+ *   cache_seqlens (B,) int32 -- KVCache.cache_seqlens, modelcore/cache.py:25.  Row b's new
+ *                tokens sit at positions [cache_seqlens[b], cache_seqlens[b] + T).
+ *
+ * The reference interfaces each entry point replaces are cited beside it (paths relative to
+ * the modelcore project root).
+ */
+#ifndef MCB200_H
+#define MCB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MCB_ABI_VERSION 1
+
+typedef enum {
+  MCB_OK = 0,
+  MCB_ERR_INVALID_ARG = -1,   /* a NULL pointer, a negative or inconsistent size         */
+  MCB_ERR_UNSUPPORTED = -2,   /* a head_dim / group shape the kernels are not built for  */
+  MCB_ERR_ALIGNMENT = -3,     /* a pointer or stride that breaks the 16-byte layout rule */
+  MCB_ERR_WORKSPACE = -4,     /* workspace missing or smaller than required              */
+  MCB_ERR_CUDA = -5           /* a CUDA runtime / driver call failed                     */
+} mcb_status;
+
+/* Bits of mcb_append_args.flags. */
+#define MCB_APPEND_ROTATE_Q 1u  /* q_out = 1.2 * rms_norm(rope(q))   (attention.py:147-150, :156-158) */
+#define MCB_APPEND_ROTATE_K 2u  /* k' = 1.2 * rms_norm(rope(k)) before it is written             */
+#define MCB_APPEND_WRITE_KV 4u  /* write k' (or raw k) and v at rows' positions, flash_attn.py:337-346 */
+
+/* Version of this ABI (MCB_ABI_VERSION of the library that was loaded). */
+int mcb_abi_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to len) into buf.
+ * Returns the full message length. */
+int mcb_last_error(char* buf, size_t len);
+
+/* ---------------------------------------------------------------------------------------------
+ * Piece 1: per-step K/V append fused with rotary, QK-norm and the 1.2 scale.
+ * Replaces, for one attention layer on the decode path:
+ *   RotaryEmbedding._cos_sin / forward / apply_to_q   modelcore/components/rotary.py:43-81
+ *   apply_rotary_emb                                  modelcore/components/rope.py:4-12
+ *   norm(q), norm(k) (F.rms_norm), q*1.2, k*1.2       modelcore/components/attention.py:147-150
+ *   the cache insert in flash_attn_with_kvcache      modelcore/kernels/flash_attn.py:337-346
+ * Rounding follows the reference op by op: every rope product and sum is rounded to bf16; the
+ * norm accumulates in fp32 and rounds once; the scale multiplies in fp32 and rounds once.
+ * Does NOT advance cache_seqlens (Model.forward does that once per forward, model.py:99-100).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;              /* (B,T,Hq,D)  bf16, read when ROTATE_Q                       */
+  const void* k;              /* (B,T,Hkv,D) bf16, read when ROTATE_K or WRITE_KV           */
+  const void* v;              /* (B,T,Hkv,D) bf16, read when WRITE_KV                       */
+  int64_t q_stride[3];        /* element strides of q for b, t, h                           */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  void* q_out;                /* (B,T,Hq,D) bf16 contiguous, written when ROTATE_Q          */
+  void* k_cache;              /* cache slot (B,Tmax,Hkv,D), written when WRITE_KV           */
+  void* v_cache;
+  const int32_t* cache_seqlens; /* (B,) positions before this step                          */
+  const void* cos;            /* (rot_len, D/2) bf16 rotary table rows, rope.py:15-27       */
+  const void* sin;
+  int32_t B, T, Hq, Hkv, D, Tmax, rot_len;
+  float eps;                  /* rms_norm epsilon as fp32 (torch: fp32 machine eps when None) */
+  float scale;                /* 1.2f in modelcore                                          */
+  uint32_t flags;             /* MCB_APPEND_* bits                                          */
+} mcb_append_args;
+
+int mcb_kv_append_rope(const mcb_append_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Piece 2: prefill -> broadcast cache copy, and the single-row copy.
+ * Replaces KVCache.prefill   (modelcore/cache.py:75-90: k/v slice copy + cache_seqlens.fill_)
+ *          KVCache.prefill_row (modelcore/cache.py:92-119: row copy + cache_seqlens[row] = P)
+ * Copies positions [0, n_pos) of source row src_row in every slot into destination rows
+ * [dst_row_begin, dst_row_begin + dst_row_count); the source is read once and written to every
+ * destination row.  When dst_seqlens is not NULL, dst_seqlens[row] = n_pos for those rows in
+ * the same launch.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  void* dst_k;  void* dst_v;           /* (n_slots, dst_batch, dst_tmax, Hkv, D) bf16          */
+  const void* src_k; const void* src_v;/* (n_slots, src_batch, src_tmax, Hkv, D) bf16          */
+  int32_t n_slots;
+  int32_t src_batch, src_row, src_tmax;
+  int32_t dst_batch, dst_row_begin, dst_row_count, dst_tmax;
+  int32_t n_pos;                       /* positions copied                                     */
+  int32_t row_elems;                   /* Hkv * D                                              */
+  int32_t* dst_seqlens;                /* optional (dst_batch,) int32                          */
+} mcb_copy_args;
+
+int mcb_kv_copy_rows(const mcb_copy_args* args, void* stream);
+
+/* cache_seqlens[b] += n for every row.  Replaces KVCache.advance's device half,
+ * modelcore/cache.py:71 (the host mirror, :72-73, stays with the caller). */
+int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Piece 3: decode attention over the cache (split-K flash-decode).
+ * Replaces the attention half of flash_attn_with_kvcache's SDPA path,
+ * modelcore/kernels/flash_attn.py:348-366 with _sdpa_attention (:203-244) and
+ * _ragged_decode_mask (:246-264):
+ *   out[b,t,h] = softmax_c(q[b,t,h] . K[b,c,h/G] * softmax_scale) . V[b,c,h/G]
+ * over keys c with c <= L_b + t and (window < 0 or L_b + t - c <= window), L_b = cache_seqlens[b]
+ * and G = Hq / Hkv (SDPA's enable_gqa mapping q head h -> kv head h / G).  The new tokens'
+ * keys/values must already be in the cache (mcb_kv_append_rope with WRITE_KV).
+ * Keys are streamed once per (row, kv head, split) by TMA into a shared-memory ring that the
+ * G grouped query heads share; partial results of the splits are merged by a second kernel.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;              /* (B,T,Hq,D) bf16                                            */
+  int64_t q_stride[3];        /* element strides of q for b, t, h                           */
+  const void* k_cache;        /* cache slot (B,Tmax,Hkv,D) bf16                             */
+  const void* v_cache;
+  const int32_t* cache_seqlens;
+  void* out;                  /* (B,T,Hq,D) bf16 contiguous                                 */
+  int32_t B, T, Hq, Hkv, D, Tmax;
+  int32_t window;             /* left window; < 0 = full context                            */
+  float softmax_scale;        /* 1/sqrt(D) in modelcore (SDPA default)                      */
+  int32_t num_splits;         /* 0 = choose from the shape                                  */
+  void* workspace;            /* device scratch of mcb_decode_attn_workspace_size() bytes   */
+  size_t workspace_bytes;
+} mcb_attn_args;
+
+/* Bytes of workspace mcb_decode_attn needs for this shape (0 when no split is used). */
+size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
+
+int mcb_decode_attn(const mcb_attn_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
+ * overflow) or a timed-out pipeline wait sets a device error word and skips the access.
+ * mcb_device_error synchronises `stream`, returns the word in *code and clears it.
+ * Codes: 0 none, 1 position beyond Tmax, 2 position beyond the rotary table, 3 pipeline wait
+ * timed out.
+ * ------------------------------------------------------------------------------------------- */
+int mcb_device_error(int32_t* code, void* stream);
+
+/* Kernels this library has enqueued in this process (host-side count, for launch accounting). */
+uint64_t mcb_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MCB200_H */

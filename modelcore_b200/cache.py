@@ -1,0 +1,150 @@
+"""KVCache for the B200 decode path: modelcore's KVCache API and layout over libmcb200 kernels.
+
+Same constructor, attributes and methods as modelcore.cache.KVCache (modelcore/cache.py:13-119):
+k_cache / v_cache (n_slots, B, T_max, H_kv, D), cache_seqlens (B,) int32, state, reset, get_pos,
+uniform_pos, get_slot_cache, advance, prefill, prefill_row -- so modelcore's Model, Decoder and
+Attention use it unchanged.  Differences, all on the host side:
+
+* Layout (piece 4 of the decode path): bf16 on a CUDA device only, base addresses 256-byte
+  aligned (every (slot, row, position) vector then starts on a 16-byte boundary, which the TMA
+  loads of the attention kernel require).  Anything else raises: there is no CPU path.
+* A host mirror of every row's length (`_host_lens`) is kept by this class's own methods, so
+  prefill_row's checks and the overflow checks never read cache_seqlens back (the reference syncs
+  at modelcore/cache.py:102 and :118).  As in the reference, only KVCache's own methods may
+  mutate cache_seqlens.
+* prefill / prefill_row copy with one kernel that also sets cache_seqlens for the rows it fills.
+"""
+import numpy as np
+import torch
+
+from . import ops
+
+CACHE_ALIGN = 256
+
+
+def _aligned_zeros(shape, device):
+    t = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+    if t.numel() and t.data_ptr() % CACHE_ALIGN:
+        raise RuntimeError(f"KV cache base {t.data_ptr():#x} is not {CACHE_ALIGN}-byte aligned")
+    return t
+
+
+class KVCache:
+    def __init__(self, batch_size, n_kv_head, seq_len, head_dim, num_kv_slots, device, dtype):
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError(f"modelcore_b200.KVCache lives on a CUDA device, got {device}")
+        if dtype != torch.bfloat16:
+            raise RuntimeError(f"modelcore_b200.KVCache stores bf16, got {dtype}")
+        if num_kv_slots and (head_dim % 8):
+            raise RuntimeError(f"head_dim {head_dim} must be a multiple of 8 (16-byte cache rows)")
+        self.batch_size = batch_size
+        self.max_seq_len = seq_len
+        self.n_slots = num_kv_slots
+        self.n_kv_head = n_kv_head
+        self.head_dim = head_dim
+        shape = (num_kv_slots, batch_size, seq_len, n_kv_head, head_dim)
+        self.k_cache = _aligned_zeros(shape, device)
+        self.v_cache = _aligned_zeros(shape, device)
+        self.cache_seqlens = torch.zeros(batch_size, dtype=torch.int32, device=device)
+        self._pos_uniform = 0
+        self._host_lens = np.zeros(batch_size, dtype=np.int64)
+        self.state = {}
+
+    # -- the reference API -------------------------------------------------------------------
+    def reset(self):
+        """Rows back to length 0; k/v are not zeroed (stale KV is unreachable: every kernel masks
+        keys beyond a row's own position), as in modelcore/cache.py:38-45."""
+        self.cache_seqlens.zero_()
+        self.state = {}
+        self._pos_uniform = 0
+        self._host_lens[:] = 0
+
+    def get_pos(self):
+        assert self._pos_uniform is not None, \
+            "get_pos() on a right-ragged KV cache; read cache_seqlens or check uniform_pos()"
+        return self._pos_uniform
+
+    def uniform_pos(self):
+        return self._pos_uniform
+
+    def get_slot_cache(self, slot):
+        return self.k_cache[slot], self.v_cache[slot]
+
+    def advance(self, num_tokens):
+        """cache_seqlens += num_tokens on the device, and the host mirrors with it
+        (modelcore/cache.py:62-73)."""
+        ops.kv_advance(self.cache_seqlens, num_tokens)
+        self._host_lens += num_tokens
+        if self._pos_uniform is not None:
+            self._pos_uniform += num_tokens
+
+    def prefill(self, other):
+        """Broadcast a batch-1 cache into every row (modelcore/cache.py:75-90): one kernel reads
+        the source once, writes it to all rows and sets cache_seqlens."""
+        assert self.get_pos() == 0, "Cannot prefill a non-empty KV cache"
+        assert self.n_slots == other.n_slots and self.n_kv_head == other.n_kv_head and self.head_dim == other.head_dim
+        assert self.max_seq_len >= other.max_seq_len
+        other_pos = other.get_pos()
+        if self.n_slots:
+            ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=0,
+                             dst_row_begin=0, dst_row_count=self.batch_size, n_pos=other_pos,
+                             dst_seqlens=self.cache_seqlens)
+        else:
+            self.cache_seqlens.fill_(other_pos)
+        self._pos_uniform = other_pos
+        self._host_lens[:] = other_pos
+        for key, value in other.state.items():
+            self.state[key] = value.expand(self.batch_size, *([-1] * (value.dim() - 1))).clone()
+
+    def prefill_row(self, row, other):
+        """Copy a batch-1 prefilled cache into row `row` (modelcore/cache.py:92-119), checked
+        against the host mirror instead of a device read."""
+        assert other.batch_size == 1, "prefill_row copies from a batch=1 cache"
+        assert 0 <= row < self.batch_size, f"row {row} out of range for batch_size {self.batch_size}"
+        assert self._host_lens[row] == 0, "Cannot prefill a non-empty KV cache row"
+        assert self.n_slots == other.n_slots and self.n_kv_head == other.n_kv_head and self.head_dim == other.head_dim
+        other_pos = other.get_pos()
+        assert other_pos <= self.max_seq_len, f"prompt of {other_pos} tokens exceeds cache length {self.max_seq_len}"
+        if self.n_slots:
+            ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=0,
+                             dst_row_begin=row, dst_row_count=1, n_pos=other_pos,
+                             dst_seqlens=self.cache_seqlens)
+        else:
+            self.cache_seqlens[row] = other_pos
+        for key, value in other.state.items():
+            buf = self.state.get(key)
+            if buf is None:
+                buf = value.new_zeros((self.batch_size,) + tuple(value.shape[1:]))
+                self.state[key] = buf
+            buf[row] = value[0]
+        self._host_lens[row] = other_pos
+        lens = self._host_lens
+        self._pos_uniform = int(lens[0]) if bool((lens == lens[0]).all()) else None
+
+    # -- host-side helpers ---------------------------------------------------------------------
+    def host_lens(self):
+        """Row lengths as this cache's methods have set them (no device read)."""
+        return self._host_lens.copy()
+
+    def max_len(self):
+        return int(self._host_lens.max()) if self.batch_size else 0
+
+    def check_room(self, num_tokens, rot_len=None):
+        """Raises before a step that would write past T_max or past the rotary table (the
+        reference asserts the latter at modelcore/components/rotary.py:55 and :62)."""
+        end = self.max_len() + num_tokens
+        assert end <= self.max_seq_len, \
+            f"KV cache overflow: positions up to {end} > cache length {self.max_seq_len}"
+        if rot_len is not None:
+            assert end <= rot_len, \
+                f"Sequence length grew beyond the rotary embeddings cache: {end} > {rot_len}"
+
+    def host_state(self):
+        """Snapshot of the host mirrors (used around CUDA-graph capture, which records kernels
+        without running them)."""
+        return (self._host_lens.copy(), self._pos_uniform)
+
+    def restore_host_state(self, snap):
+        self._host_lens[:] = snap[0]
+        self._pos_uniform = snap[1]

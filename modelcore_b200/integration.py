@@ -1,0 +1,271 @@
+"""modelcore glue: the B200 decode path behind modelcore's own API.
+
+    from modelcore_b200 import ModelManager          # instead of modelcore.ModelManager
+    manager = ModelManager()
+    model = manager.create_model(config, device=torch.device("cuda"), seed=0).to(torch.bfloat16)
+    decoder = manager.new_decoder(model, prompts, max_tokens=512)   # modelcore's Decoder
+    logits = decoder.step(tokens)                                    # or model(idx, kv_cache=...)
+
+* `ModelManager` is modelcore.ModelManager with new_kv_cache returning modelcore_b200.KVCache on
+  CUDA devices, and create_model / load_model installing the B200 attention forward on every
+  Attention module of the model they return.  Everything else is the reference's.
+* `install(model)` binds `attention_forward` to each modelcore Attention module (an instance
+  attribute; the class and the catalog are untouched, modelcore/catalog.py:25 forbids
+  re-registering "attention").  With kv_cache=None (training) the module's original forward runs.
+* `GraphDecoder` is modelcore's Decoder whose steps replay a CUDA graph of the decode forward.
+"""
+import types
+
+import torch
+
+from . import ops
+from .cache import KVCache
+from .flash_attn import flash_attn_with_kvcache
+
+_ORIGINAL_FORWARD = "_mcb_original_forward"
+
+
+def _fusable(attn, x):
+    """The fused append applies when QK-norm is modelcore's RMSNorm and the position encoding is
+    its RotaryEmbedding with bf16 tables on x's device."""
+    from modelcore.components.norm import RMSNorm
+    from modelcore.components.rotary import RotaryEmbedding
+    rope = attn.rope
+    return (isinstance(attn.norm, RMSNorm) and isinstance(rope, RotaryEmbedding)
+            and rope.cos.dtype == torch.bfloat16 and rope.cos.device == x.device
+            and attn.head_dim % 2 == 0 and attn.head_dim <= 256)
+
+
+def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
+    """modelcore Attention.forward (modelcore/components/attention.py:135-184) with the KV-cache
+    branch on libmcb200.  Same projections, hooks (`values` after c_v, `output` before c_proj),
+    window and kv_slot semantics; same state-dict keys.
+
+    Fused mode (RMSNorm QK-norm + RotaryEmbedding): one kernel does rope + norm + x1.2 for q and
+    k and writes k, v into the slot at each row's position (a consumer layer, produces_kv=False,
+    rotates only its q and reads the producer's slot, which the producer wrote earlier in the
+    same forward); then the decode-attention kernel.  Composed mode (any other norm or position
+    encoding): the module's own torch ops compute q, k as the reference does, then the insert and
+    the attention run on libmcb200.  In both modes kv_bus is not used: consumers read the slot."""
+    if kv_cache is None or not isinstance(kv_cache, KVCache):
+        return getattr(self, _ORIGINAL_FORWARD)(x, idx, kv_cache, kv_bus, doc_args)
+    B, T, C = x.size()
+    q = self.c_q(x).view(B, T, self.n_head, self.head_dim)
+    k_cache, v_cache = kv_cache.get_slot_cache(self.kv_slot)
+    seqlens = kv_cache.cache_seqlens
+    if _fusable(self, x):
+        rope = self.rope
+        kv_cache.check_room(T, rope.cos.size(1))
+        if self.produces_kv:
+            k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
+            v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
+            v = self._hook("values", v, x, idx)
+            q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
+                                   rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
+                                   scale=1.2)
+        else:
+            q = ops.kv_append_rope(q, None, None, None, None, seqlens, rope.cos, rope.sin,
+                                   rotate_q=True, rotate_k=False, write_kv=False,
+                                   eps=self.norm.eps, scale=1.2)
+        y = ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window)
+    else:
+        kv_cache.check_room(T)
+        if self.produces_kv:
+            k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
+            v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
+            v = self._hook("values", v, x, idx)
+            q, k = self.rope(q, k, kv_cache)
+            q, k = self.norm(q), self.norm(k)
+            q = q * 1.2
+            k = k * 1.2
+            y = flash_attn_with_kvcache(q, k_cache, v_cache, k=k, v=v, cache_seqlens=seqlens,
+                                        causal=True, window_size=(self.window, 0))
+        else:
+            q = self.rope.apply_to_q(q, kv_cache)
+            q = self.norm(q)
+            q = q * 1.2
+            y = flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=seqlens, causal=True,
+                                        window_size=(self.window, 0))
+    y = self._hook("output", y, x)
+    y = y.contiguous().view(B, T, -1)
+    return self.c_proj(y)
+
+
+def install(model):
+    """Binds attention_forward to every modelcore Attention module of `model`; returns the
+    number of modules changed.  Idempotent."""
+    from modelcore.components.attention import Attention
+    n = 0
+    for m in model.modules():
+        if isinstance(m, Attention) and not hasattr(m, _ORIGINAL_FORWARD):
+            object.__setattr__(m, _ORIGINAL_FORWARD, m.forward)
+            object.__setattr__(m, "forward", types.MethodType(attention_forward, m))
+            n += 1
+    return n
+
+
+def uninstall(model):
+    from modelcore.components.attention import Attention
+    for m in model.modules():
+        if isinstance(m, Attention) and hasattr(m, _ORIGINAL_FORWARD):
+            object.__setattr__(m, "forward", getattr(m, _ORIGINAL_FORWARD))
+            object.__delattr__(m, _ORIGINAL_FORWARD)
+
+
+def _manager_base():
+    from modelcore.manager import ModelManager as RefManager
+    return RefManager
+
+
+class _ManagerMixin:
+    def create_model(self, *args, **kwargs):
+        model = super().create_model(*args, **kwargs)
+        install(model)
+        return model
+
+    def load_model(self, *args, **kwargs):
+        model = super().load_model(*args, **kwargs)
+        install(model)
+        return model
+
+    def new_kv_cache(self, model, *, batch_size, seq_len, device=None):
+        """modelcore's new_kv_cache (modelcore/manager.py:286-291) returning the B200 KVCache
+        for CUDA devices; the cache dtype is the model's activation dtype (bf16)."""
+        from modelcore.stats import kv_cache_spec
+        device = torch.device(device) if device is not None else model.get_device()
+        if device.type != "cuda":
+            return super().new_kv_cache(model, batch_size=batch_size, seq_len=seq_len, device=device)
+        spec = kv_cache_spec(model.layer_specs())
+        return KVCache(batch_size=batch_size, seq_len=seq_len, device=device, dtype=torch.bfloat16,
+                       **spec)
+
+    def new_decoder(self, model, tokens, *, num_samples=1, max_tokens=None, device=None,
+                    cuda_graph=False):
+        """modelcore's Decoder (modelcore/generate.py:37-94) over the B200 cache; with
+        cuda_graph=True, a GraphDecoder."""
+        if cuda_graph:
+            return GraphDecoder(model, self, tokens, num_samples=num_samples, max_tokens=max_tokens,
+                                device=device)
+        from modelcore.generate import Decoder
+        return Decoder(model, self, tokens, num_samples=num_samples, max_tokens=max_tokens,
+                       device=device)
+
+
+def make_manager_class():
+    return type("ModelManager", (_ManagerMixin, _manager_base()), {
+        "__doc__": "modelcore.ModelManager with the B200 KV-cache decode path installed.",
+        "__module__": __name__,
+    })
+
+
+class GraphDecoder:
+    """modelcore's Decoder (same constructor, .logits, .step, .kv_cache) whose decode steps replay
+    one CUDA graph of `model.forward(ids (B, 1), kv_cache)` instead of launching each op from
+    Python.  The first step runs eagerly (it warms up cuBLAS and the kernels); the second
+    captures the graph; every step after replays it.  The graph holds fixed pointers, so the
+    cache must not be reallocated while it lives.
+
+    greedy_steps(n) additionally keeps the argmax on the device: each replay feeds its own
+    greedy token to the next step (no host round trip), returning the (B, n) tokens."""
+
+    def __init__(self, model, manager, tokens, *, num_samples=1, max_tokens=None, device=None):
+        from modelcore.generate import Decoder
+        self._dec = Decoder(model, manager, tokens, num_samples=num_samples, max_tokens=max_tokens,
+                            device=device)
+        self.model = model
+        self.kv_cache = self._dec.kv_cache
+        if not isinstance(self.kv_cache, KVCache):
+            raise RuntimeError("GraphDecoder needs the modelcore_b200 KVCache (a CUDA model)")
+        self._logits = self._dec.logits
+        self._graph = None
+        self._greedy_graph = None
+        self._eager_steps = 0
+        B = self.kv_cache.batch_size
+        dev = self.kv_cache.cache_seqlens.device
+        self._ids = torch.zeros((B, 1), dtype=torch.long, device=dev)
+        self._ids_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
+        self._static_logits = None
+        self._next = None
+
+    @property
+    def logits(self):
+        return self._logits
+
+    def _room(self, n):
+        self.kv_cache.check_room(n)
+
+    def _capture(self, greedy):
+        cache = self.kv_cache
+        snap = cache.host_state()
+        state_snap = dict(cache.state)
+        g = torch.cuda.CUDAGraph()
+        with torch.inference_mode():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=side):
+                logits = self.model.forward(self._ids, kv_cache=cache)[:, -1, :]
+                nxt = None
+                if greedy:
+                    nxt = torch.argmax(logits, dim=-1, keepdim=True)
+                    self._ids.copy_(nxt)
+            torch.cuda.current_stream().wait_stream(side)
+        cache.restore_host_state(snap)
+        cache.state.update(state_snap)
+        return g, logits, nxt
+
+    def _eager(self, ids):
+        logits = self.model.forward(ids, kv_cache=self.kv_cache)[:, -1, :]
+        self._eager_steps += 1
+        return logits
+
+    def _replayed(self):
+        cache = self.kv_cache
+        cache._host_lens += 1
+        if cache._pos_uniform is not None:
+            cache._pos_uniform += 1
+
+    @torch.inference_mode()
+    def step(self, token_column):
+        """Advance every row by one position; returns the new (B, vocab) logits."""
+        self._room(1)
+        if isinstance(token_column, torch.Tensor) and token_column.is_cuda:
+            self._ids.copy_(token_column.view(-1, 1))
+        else:
+            self._ids_host.copy_(torch.as_tensor(token_column, dtype=torch.long).view(-1, 1))
+            self._ids.copy_(self._ids_host, non_blocking=True)
+        if self._graph is None and self._eager_steps == 0:
+            self._logits = self._eager(self._ids.clone())
+            return self._logits
+        if self._graph is None:
+            self._graph, self._static_logits, _ = self._capture(greedy=False)
+        self._graph.replay()
+        self._replayed()
+        self._logits = self._static_logits
+        return self._logits
+
+    @torch.inference_mode()
+    def greedy_steps(self, n, first_tokens=None, out=None):
+        """n device-resident greedy steps.  Step i feeds token t_i and computes
+        t_{i+1} = argmax(logits); t_0 = first_tokens (default: argmax of the current logits).
+        Returns out (B, n) int64 on the device holding t_0 .. t_{n-1}, the same stream modelcore's
+        greedy loop produces; .logits afterwards are those of the last step."""
+        B = self.kv_cache.batch_size
+        if first_tokens is None:
+            first_tokens = torch.argmax(self._logits, dim=-1)
+        self._ids.copy_(first_tokens.view(-1, 1))
+        if out is None:
+            out = torch.empty((B, n), dtype=torch.long, device=self._ids.device)
+        for i in range(n):
+            out[:, i] = self._ids[:, 0]
+            self._room(1)
+            if self._greedy_graph is None and self._eager_steps == 0:
+                logits = self._eager(self._ids.clone())
+                self._ids.copy_(torch.argmax(logits, dim=-1, keepdim=True))
+                self._logits = logits
+                continue
+            if self._greedy_graph is None:
+                self._greedy_graph, self._greedy_logits, _ = self._capture(greedy=True)
+            self._greedy_graph.replay()
+            self._replayed()
+            self._logits = self._greedy_logits
+        return out

@@ -1,0 +1,240 @@
+"""Torch-facing wrappers of the C-ABI entry points.
+
+Each wrapper checks device, dtype, shape and layout on the host (no device sync), passes raw
+pointers and the current CUDA stream to libmcb200 and returns.  All of them are safe inside
+CUDA-graph capture: they only enqueue kernels, and the one allocation (the split-K workspace)
+comes from torch's caching allocator.  None has a CPU path: non-CUDA or non-bf16 tensors raise.
+"""
+import ctypes
+import math
+
+import torch
+
+from . import _native
+from ._native import AppendArgs, AttnArgs, CopyArgs, check
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(name, t, ndim=None, dtype=torch.bfloat16):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: modelcore_b200 has no CPU path (got {t.device})")
+    if dtype is not None and t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
+    if ndim is not None and t.dim() != ndim:
+        raise RuntimeError(f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
+
+
+def _bthd_strides(name, t):
+    if t.stride(3) != 1:
+        raise RuntimeError(f"{name} must have unit stride on head_dim, got strides {t.stride()}")
+    return (t.stride(0), t.stride(1), t.stride(2))
+
+
+def _check_slot_cache(name, c, B, Hkv, D):
+    _need(name, c, 4)
+    if not c.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous (B, T_max, H_kv, D) cache slot")
+    if c.size(0) != B or c.size(2) != Hkv or c.size(3) != D:
+        raise RuntimeError(f"{name} has shape {tuple(c.shape)}, expected ({B}, T_max, {Hkv}, {D})")
+    if c.data_ptr() % 16:
+        raise RuntimeError(f"{name} must be 16-byte aligned")
+
+
+def _check_seqlens(cache_seqlens, B, device):
+    _need("cache_seqlens", cache_seqlens, 1, torch.int32)
+    if cache_seqlens.numel() != B or not cache_seqlens.is_contiguous():
+        raise RuntimeError(f"cache_seqlens must be a contiguous ({B},) int32 tensor")
+    if cache_seqlens.device != device:
+        raise RuntimeError("cache_seqlens is on another device")
+
+
+def rms_norm_eps(eps):
+    """The epsilon torch's F.rms_norm applies to bf16 input: fp32 machine epsilon when None
+    (the opmath type's epsilon), otherwise the given value in fp32."""
+    return torch.finfo(torch.float32).eps if eps is None else float(eps)
+
+
+def kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, rotate_q=True,
+                   rotate_k=True, write_kv=True, eps=None, scale=1.2, q_out=None):
+    """Fused rope + QK-norm + scale for q (and k), and the insert of k, v at each row's position.
+
+    q: (B, T, Hq, D) bf16 or None; k, v: (B, T, Hkv, D) bf16 or None; k_cache/v_cache: one slot
+    (B, T_max, Hkv, D); cos/sin: the rotary buffers (1, rot_len, 1, D/2) bf16 of
+    modelcore.components.rotary.RotaryEmbedding.  Returns the rotated q (a new (B, T, Hq, D)
+    tensor, or q_out) when rotate_q, else None.  cache_seqlens is not advanced."""
+    flags = 0
+    ref = q if rotate_q else k
+    if ref is None:
+        raise RuntimeError("kv_append_rope: nothing to do")
+    _need("q" if rotate_q else "k", ref, 4)
+    B, T = ref.shape[0], ref.shape[1]
+    D = ref.shape[3]
+    args = AppendArgs()
+    if rotate_q:
+        flags |= _native.MCB_APPEND_ROTATE_Q
+        Hq = q.shape[2]
+        if q_out is None:
+            q_out = torch.empty((B, T, Hq, D), dtype=torch.bfloat16, device=q.device)
+        else:
+            _need("q_out", q_out, 4)
+            if tuple(q_out.shape) != (B, T, Hq, D) or not q_out.is_contiguous():
+                raise RuntimeError("q_out must be a contiguous tensor shaped like q")
+        args.q = q.data_ptr()
+        args.q_stride[:] = _bthd_strides("q", q)
+        args.q_out = q_out.data_ptr()
+        args.Hq = Hq
+    if rotate_k:
+        flags |= _native.MCB_APPEND_ROTATE_K
+    if write_kv:
+        flags |= _native.MCB_APPEND_WRITE_KV
+        _need("k", k, 4)
+        _need("v", v, 4)
+        Hkv = k.shape[2]
+        if tuple(k.shape) != (B, T, Hkv, D) or tuple(v.shape) != (B, T, Hkv, D):
+            raise RuntimeError(f"k and v must be ({B}, {T}, H_kv, {D}), got {tuple(k.shape)}, {tuple(v.shape)}")
+        _check_slot_cache("k_cache", k_cache, B, Hkv, D)
+        _check_slot_cache("v_cache", v_cache, B, Hkv, D)
+        if v_cache.size(1) != k_cache.size(1):
+            raise RuntimeError("k_cache and v_cache lengths differ")
+        args.k = k.data_ptr()
+        args.v = v.data_ptr()
+        args.k_stride[:] = _bthd_strides("k", k)
+        args.v_stride[:] = _bthd_strides("v", v)
+        args.k_cache = k_cache.data_ptr()
+        args.v_cache = v_cache.data_ptr()
+        args.Hkv = Hkv
+        args.Tmax = k_cache.size(1)
+    elif rotate_k:
+        raise RuntimeError("rotate_k requires write_kv")
+    _check_seqlens(cache_seqlens, B, ref.device)
+    if rotate_q or rotate_k:
+        for name, tab in (("cos", cos), ("sin", sin)):
+            _need(name, tab)
+            if not tab.is_contiguous() or tab.shape[-1] != D // 2:
+                raise RuntimeError(f"rotary {name} table must be contiguous with D/2={D // 2} columns")
+        args.cos = cos.data_ptr()
+        args.sin = sin.data_ptr()
+        args.rot_len = cos.numel() // (D // 2)
+    args.cache_seqlens = cache_seqlens.data_ptr()
+    args.B, args.T, args.D = B, T, D
+    args.eps = rms_norm_eps(eps)
+    args.scale = scale
+    args.flags = flags
+    check(_native.load().mcb_kv_append_rope(ctypes.byref(args), _stream(ref)))
+    return q_out
+
+
+def kv_write(k, v, k_cache, v_cache, cache_seqlens):
+    """Inserts already-processed k, v (B, T, Hkv, D) at rows' positions [L_b, L_b + T): the
+    in-place cache write of flash_attn_with_kvcache (modelcore/kernels/flash_attn.py:337-346)."""
+    kv_append_rope(None, k, v, k_cache, v_cache, cache_seqlens, None, None, rotate_q=False,
+                   rotate_k=False, write_kv=True)
+
+
+def kv_copy_rows(dst_k, dst_v, src_k, src_v, *, src_row, dst_row_begin, dst_row_count, n_pos,
+                 dst_seqlens=None):
+    """Copies positions [0, n_pos) of source row src_row, every slot, into destination rows
+    [dst_row_begin, dst_row_begin + dst_row_count); optionally sets dst_seqlens for those rows.
+    Caches are full (n_slots, B, T_max, Hkv, D) tensors."""
+    for name, t in (("dst_k", dst_k), ("dst_v", dst_v), ("src_k", src_k), ("src_v", src_v)):
+        _need(name, t, 5)
+        if not t.is_contiguous():
+            raise RuntimeError(f"{name} must be contiguous")
+    if dst_k.shape != dst_v.shape or src_k.shape != src_v.shape:
+        raise RuntimeError("k and v caches must have equal shapes")
+    S, Bd, Td, H, D = dst_k.shape
+    Ss, Bs, Ts, Hs, Ds = src_k.shape
+    if (S, H, D) != (Ss, Hs, Ds):
+        raise RuntimeError(f"cache layouts differ: dst {tuple(dst_k.shape)} vs src {tuple(src_k.shape)}")
+    args = CopyArgs()
+    args.dst_k, args.dst_v = dst_k.data_ptr(), dst_v.data_ptr()
+    args.src_k, args.src_v = src_k.data_ptr(), src_v.data_ptr()
+    args.n_slots = S
+    args.src_batch, args.src_row, args.src_tmax = Bs, src_row, Ts
+    args.dst_batch, args.dst_row_begin, args.dst_row_count, args.dst_tmax = Bd, dst_row_begin, dst_row_count, Td
+    args.n_pos = n_pos
+    args.row_elems = H * D
+    if dst_seqlens is not None:
+        _check_seqlens(dst_seqlens, Bd, dst_k.device)
+        args.dst_seqlens = dst_seqlens.data_ptr()
+    check(_native.load().mcb_kv_copy_rows(ctypes.byref(args), _stream(dst_k)))
+
+
+def kv_advance(cache_seqlens, n):
+    """cache_seqlens += n on the device (KVCache.advance, modelcore/cache.py:71)."""
+    _need("cache_seqlens", cache_seqlens, 1, torch.int32)
+    check(_native.load().mcb_kv_advance(ctypes.c_void_p(cache_seqlens.data_ptr()),
+                                        cache_seqlens.numel(), int(n), _stream(cache_seqlens)))
+
+
+def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out):
+    _need("q", q, 4)
+    B, T, Hq, D = q.shape
+    Hkv = k_cache.shape[2] if k_cache.dim() == 4 else -1
+    _check_slot_cache("k_cache", k_cache, B, Hkv, D)
+    _check_slot_cache("v_cache", v_cache, B, Hkv, D)
+    if v_cache.shape != k_cache.shape:
+        raise RuntimeError("k_cache and v_cache shapes differ")
+    _check_seqlens(cache_seqlens, B, q.device)
+    if Hq % Hkv:
+        raise RuntimeError(f"n_head ({Hq}) must be divisible by n_kv_head ({Hkv})")
+    args = AttnArgs()
+    args.q = q.data_ptr()
+    args.q_stride[:] = _bthd_strides("q", q)
+    args.k_cache, args.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    args.cache_seqlens = cache_seqlens.data_ptr()
+    args.out = out.data_ptr() if out is not None else 0
+    args.B, args.T, args.Hq, args.Hkv, args.D, args.Tmax = B, T, Hq, Hkv, D, k_cache.shape[1]
+    args.window = -1 if window is None or window < 0 else int(window)
+    args.softmax_scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
+    args.num_splits = int(num_splits)
+    return args
+
+
+def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_splits=0):
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_splits, None)
+    return int(_native.load().mcb_decode_attn_workspace_size(ctypes.byref(args)))
+
+
+def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
+                num_splits=0, out=None, workspace=None):
+    """softmax(q . K^T * scale) . V over each row's visible keys of one cache slot.
+
+    q: (B, T, Hq, D) bf16; k_cache/v_cache: (B, T_max, Hkv, D) bf16 slot; query t of row b sits at
+    cache_seqlens[b] + t and sees keys c <= that position within `window` (< 0: all).  The new
+    tokens must already be in the cache.  Returns out (B, T, Hq, D) bf16."""
+    if out is None:
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    else:
+        _need("out", out, 4)
+        if out.shape != q.shape or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous tensor shaped like q")
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out)
+    lib = _native.load()
+    need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
+    if need:
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        args.workspace = workspace.data_ptr()
+        args.workspace_bytes = workspace.numel()
+    check(lib.mcb_decode_attn(ctypes.byref(args), _stream(q)))
+    return out
+
+
+def device_error(device=None):
+    """Reads and clears the library's device error word (synchronises the current stream).
+    Returns (code, description)."""
+    code = ctypes.c_int32(0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    check(_native.load().mcb_device_error(ctypes.byref(code), stream))
+    return code.value, _native.DEVICE_ERRORS.get(code.value, "unknown")
+
+
+def launch_count():
+    """Kernels libmcb200 has enqueued in this process."""
+    return int(_native.load().mcb_launch_count())

@@ -1,0 +1,217 @@
+"""CPU oracle for modelcore's KV-cache decode path -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product: only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg may import it.  The product path (modelcore_b200) never calls it and
+has no CPU fallback.
+
+It restates, in numpy, what modelcore computes on the decode path (file:line cited per function,
+relative to the modelcore project root).  bf16 values travel as uint16 bit patterns; every
+place where the reference rounds a tensor op's result to bf16, this code rounds with IEEE
+round-to-nearest-even.  Parity is pinned by tests/test_oracle_golden.py against golden vectors
+that tests/golden/make_golden.py produced by running the reference itself.
+
+The one place where bit-exactness against torch is not defined is the fp32 sum of squares
+inside rms_norm: torch's reduction order is an implementation detail.  `rms_norm_scale` fixes an
+order (the one the CUDA kernel uses: per-lane partial sums over pairs (i, i + D/2), i = lane +
+32*u, then an xor butterfly over 32 lanes), so the kernel matches this oracle bit for bit and the
+reference to within one bf16 ulp on rare elements.
+"""
+import numpy as np
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------------------------------------
+# bf16 <-> fp32
+def bf16_to_f32(bits):
+    """uint16 bf16 bit patterns -> float32 values (exact)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(x):
+    """float32 -> uint16 bf16 bits, IEEE round-to-nearest-even (what torch's .to(bfloat16) and
+    every bf16 tensor op's output store do)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    lsb = (u >> 16) & np.uint32(1)
+    return ((u + np.uint32(0x7FFF) + lsb) >> 16).astype(np.uint16)
+
+
+def round_bf16(x):
+    """float32 -> float32 rounded to the nearest bf16 value."""
+    return bf16_to_f32(f32_to_bf16(x))
+
+
+# ---------------------------------------------------------------------------------------------
+# Rotary tables: modelcore/components/rope.py:15-27
+def rotary_tables(seq_len, head_dim, base=100000):
+    """(cos, sin) bf16 bits of shape (seq_len, head_dim/2): theta_{t,i} = t * base^(-2i/D) in
+    fp32, cos/sin in fp32, then rounded to bf16 (rope.py:19-25).  numpy's fp32 cos/sin may differ
+    from torch's by one fp32 ulp, which can move a bf16 rounding; the CUDA path never recomputes
+    the tables (it reads the RotaryEmbedding module's own buffers)."""
+    ch = np.arange(0, head_dim, 2, dtype=np.float32)
+    inv_freq = (F32(1.0) / (F32(base) ** (ch / F32(head_dim)))).astype(np.float32)
+    t = np.arange(seq_len, dtype=np.float32)
+    freqs = np.outer(t, inv_freq).astype(np.float32)
+    return f32_to_bf16(np.cos(freqs)), f32_to_bf16(np.sin(freqs))
+
+
+# ---------------------------------------------------------------------------------------------
+# apply_rotary_emb: modelcore/components/rope.py:4-12
+def rope(x_bits, cos_bits, sin_bits):
+    """x (..., D) bf16 bits; cos/sin (..., D/2) bf16 bits broadcastable to x's halves.
+    y1 = x1*cos + x2*sin, y2 = x1*(-sin) + x2*cos, every product and sum rounded to bf16."""
+    x = bf16_to_f32(x_bits)
+    d = x.shape[-1] // 2
+    x1, x2 = x[..., :d], x[..., d:]
+    c, s = bf16_to_f32(cos_bits), bf16_to_f32(sin_bits)
+    y1 = round_bf16(round_bf16(x1 * c) + round_bf16(x2 * s))
+    y2 = round_bf16(round_bf16(x1 * (-s)) + round_bf16(x2 * c))
+    return f32_to_bf16(np.concatenate([y1, y2], axis=-1))
+
+
+# ---------------------------------------------------------------------------------------------
+# RMSNorm + scale: modelcore/components/norm.py:43-44 (F.rms_norm, eps=None -> the fp32 machine
+# epsilon for bf16 input) and modelcore/components/attention.py:149-150 (x 1.2)
+def sum_squares_kernel_order(y):
+    """fp32 sum of y^2 over the last axis in the CUDA kernel's fixed order (see module doc)."""
+    y = np.asarray(y, dtype=np.float32)
+    D = y.shape[-1]
+    half = D // 2
+    lead = y.shape[:-1]
+    acc = np.zeros(lead + (32,), dtype=np.float32)
+    for u in range(4):
+        for lane in range(32):
+            i = lane + 32 * u
+            if i < half:
+                a = y[..., i]
+                b = y[..., i + half]
+                acc[..., lane] = acc[..., lane] + a * a
+                acc[..., lane] = acc[..., lane] + b * b
+    for m in (16, 8, 4, 2, 1):
+        acc = acc + acc[..., np.arange(32) ^ m]
+    return acc[..., 0]
+
+
+def rms_norm_scale(y_bits, eps=None, scale=1.2):
+    """bf16(bf16(y * rsqrt(mean(y^2) + eps)) * scale) with fp32 arithmetic; rsqrt correctly
+    rounded; the mean's sum in the kernel's order."""
+    y = bf16_to_f32(y_bits)
+    D = y.shape[-1]
+    e = F32(np.finfo(np.float32).eps if eps is None else eps)
+    ms = (sum_squares_kernel_order(y) / F32(D)).astype(np.float32)
+    v = (ms + e).astype(np.float32)
+    r = (np.longdouble(1.0) / np.sqrt(v.astype(np.longdouble))).astype(np.float32)
+    z = round_bf16((y * r[..., None]).astype(np.float32))
+    return f32_to_bf16((z * F32(scale)).astype(np.float32))
+
+
+def rope_norm_scale(x_bits, cos_bits, sin_bits, eps=None, scale=1.2):
+    """The fused chain of modelcore/components/attention.py:147-150 for one tensor."""
+    return rms_norm_scale(rope(x_bits, cos_bits, sin_bits), eps=eps, scale=scale)
+
+
+def positions(cache_seqlens, T):
+    """(B, T) absolute positions cache_seqlens[b] + t (rotary.py:60-67, flash_attn.py:341-346)."""
+    return np.asarray(cache_seqlens, dtype=np.int64)[:, None] + np.arange(T)[None, :]
+
+
+def rope_tables_at(cos_bits, sin_bits, cache_seqlens, T):
+    """Per-row table rows gathered at each row's own positions: (B, T, 1, D/2)."""
+    pos = positions(cache_seqlens, T)
+    return cos_bits[pos][:, :, None, :], sin_bits[pos][:, :, None, :]
+
+
+# ---------------------------------------------------------------------------------------------
+# The insert of flash_attn_with_kvcache: modelcore/kernels/flash_attn.py:337-346
+def kv_insert(k_cache, v_cache, k, v, cache_seqlens):
+    """In place: row b's new tokens land at [cache_seqlens[b], cache_seqlens[b] + T)."""
+    T = k.shape[1]
+    pos = positions(cache_seqlens, T)
+    for b in range(k.shape[0]):
+        k_cache[b, pos[b]] = k[b]
+        v_cache[b, pos[b]] = v[b]
+
+
+def append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos_bits, sin_bits, *, rotate_q=True,
+                rotate_k=True, write_kv=True, eps=None, scale=1.2):
+    """Restatement of one producer layer's decode-side chain (attention.py:147-153 + the insert):
+    returns the processed q (bf16 bits) and writes the processed k and raw v into the caches."""
+    T = (q if q is not None else k).shape[1]
+    c, s = rope_tables_at(cos_bits, sin_bits, cache_seqlens, T)
+    q_out = rope_norm_scale(q, c, s, eps, scale) if rotate_q else None
+    if write_kv:
+        k_new = rope_norm_scale(k, c, s, eps, scale) if rotate_k else k
+        kv_insert(k_cache, v_cache, k_new, v, cache_seqlens)
+    return q_out
+
+
+# ---------------------------------------------------------------------------------------------
+# KVCache.prefill / prefill_row: modelcore/cache.py:75-90, :92-119
+def prefill_broadcast(dst_k, dst_v, src_k, src_v, n_pos):
+    """dst[:, :, :n_pos] = src[:, :, :n_pos] with src batch 1 broadcast (cache.py:84-85)."""
+    dst_k[:, :, :n_pos] = src_k[:, :, :n_pos]
+    dst_v[:, :, :n_pos] = src_v[:, :, :n_pos]
+
+
+def prefill_row(dst_k, dst_v, row, src_k, src_v, n_pos):
+    """dst[:, row, :n_pos] = src[:, 0, :n_pos] (cache.py:106-107)."""
+    dst_k[:, row, :n_pos] = src_k[:, 0, :n_pos]
+    dst_v[:, row, :n_pos] = src_v[:, 0, :n_pos]
+
+
+# ---------------------------------------------------------------------------------------------
+# Decode attention: modelcore/kernels/flash_attn.py:348-366 with _ragged_decode_mask (:246-264)
+def visible_range(L, t, window):
+    """Keys c visible to query t of a row at L: c <= L + t and (window < 0 or L + t - c <= window)."""
+    qpos = L + t
+    lo = 0 if window is None or window < 0 else max(0, qpos - window)
+    return lo, qpos
+
+
+def decode_attention(q, k_cache, v_cache, cache_seqlens, window=-1, scale=None):
+    """float64 attention of q (B, T, Hq, D) over each row's visible cache keys; k/v caches
+    (B, Tmax, Hkv, D) as float arrays; q head h reads kv head h // (Hq // Hkv) (SDPA enable_gqa);
+    scale defaults to 1/sqrt(D) (SDPA's default, flash_attn.py:364)."""
+    q = np.asarray(q, dtype=np.float64)
+    kc = np.asarray(k_cache, dtype=np.float64)
+    vc = np.asarray(v_cache, dtype=np.float64)
+    B, T, Hq, D = q.shape
+    Hkv = kc.shape[2]
+    G = Hq // Hkv
+    sc = 1.0 / np.sqrt(D) if scale is None else scale
+    out = np.zeros((B, T, Hq, D), dtype=np.float64)
+    for b in range(B):
+        L = int(cache_seqlens[b])
+        for t in range(T):
+            lo, hi = visible_range(L, t, window)
+            K = kc[b, lo:hi + 1]            # (n, Hkv, D)
+            V = vc[b, lo:hi + 1]
+            Kg = np.repeat(K, G, axis=1)    # (n, Hq, D)
+            Vg = np.repeat(V, G, axis=1)
+            s = np.einsum("hd,nhd->hn", q[b, t], Kg) * sc
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=1, keepdims=True)
+            out[b, t] = np.einsum("hn,nhd->hd", p, Vg)
+    return out
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens, window=-1):
+    """Insert then attend, as the reference's SDPA path does (flash_attn.py:330-366); the caller
+    advances cache_seqlens."""
+    if k is not None and v is not None:
+        kv_insert(k_cache, v_cache, k, v, cache_seqlens)
+    return decode_attention(q, k_cache, v_cache, cache_seqlens, window)
+
+
+def kv_read_bytes(cache_seqlens, T, Hkv, D, window, itemsize=2):
+    """Algorithmic KV bytes one attention call reads: 2 * Hkv * D * itemsize per visible key,
+    keys counted exactly (n_keys = min(pos + 1, window + 1)), per row for its last query token
+    (the union of its queries' ranges).  The reference's own model of this number is
+    modelcore/stats.py:98-107."""
+    total = 0
+    for L in np.asarray(cache_seqlens).tolist():
+        lo, _ = visible_range(L, 0, window)
+        hi = L + T - 1
+        total += (hi - lo + 1)
+    return total * 2 * Hkv * D * itemsize

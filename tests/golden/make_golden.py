@@ -1,0 +1,236 @@
+"""Writes the golden fixtures under tests/golden/ by running the reference (modelcore) itself.
+
+    python tests/golden/make_golden.py [--ref PATH]
+
+PATH is a directory from which `import modelcore` loads the reference: the MODELCORE_REF_PATH
+environment variable, else the repository's baseline/_ref install of it.  The fixtures are small
+.npz files; bf16 tensors are stored as uint16 bit patterns.  Every value written is what the
+reference's own code returned for the stated inputs, so the oracle (oracle/kv_path.py) is pinned
+against the reference through tests/test_oracle_golden.py, and the GPU tests compare the CUDA path
+against the same numbers without needing the reference at run time.
+
+Fixtures:
+  rope_norm_D{64,128}.npz   RotaryEmbedding._cos_sin on a right-ragged cache + apply_rotary_emb +
+                            RMSNorm(eps=None) + x1.2 in bf16 (modelcore/components/rotary.py:43-67,
+                            rope.py:4-12, norm.py:43-44, attention.py:147-150)
+  kv_attn_*.npz             flash_attn_with_kvcache's SDPA path in fp32 on bf16-representable
+                            inputs: the cache after the insert and the attention output
+                            (modelcore/kernels/flash_attn.py:306-366), ragged and uniform rows,
+                            windows -1 / 8, T_new 1 / 3, MHA and GQA
+  prefill.npz               KVCache.prefill broadcast and prefill_row (modelcore/cache.py:75-119)
+  decode_cfg1.npz           the README quickstart model (fp32, seed 0), prompts (2, 16) from seed 1,
+                            64 greedy steps through Decoder: the token streams, for the plain
+                            random init and for the awake init of
+                            modelcore/tests/test_generate.py:187-201
+"""
+import argparse
+import os
+import sys
+import zlib
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+
+def _import_reference(path):
+    sys.path.insert(0, path)
+    import torch  # noqa: F401
+    import modelcore  # noqa: F401
+    return modelcore
+
+
+def bits(t):
+    """bf16 tensor -> uint16 numpy bits."""
+    import torch
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def bf16_representable(t):
+    import torch
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def make_rope_norm(out_dir):
+    import torch
+    from modelcore.cache import KVCache
+    from modelcore.components.norm import RMSNorm
+    from modelcore.components.rope import apply_rotary_emb
+    from modelcore.components.rotary import RotaryEmbedding
+    from modelcore.runtime import Runtime
+
+    for D in (64, 128):
+        g = torch.Generator().manual_seed(100 + D)
+        rot = RotaryEmbedding(head_dim=D, sequence_len=64, over_compute=2,
+                              runtime=Runtime(compute_dtype=torch.bfloat16))
+        rot.init_weights()
+        B, T, H = 3, 2, 5
+        cache = KVCache(batch_size=B, n_kv_head=H, seq_len=128, head_dim=D, num_kv_slots=1,
+                        device="cpu", dtype=torch.bfloat16)
+        seqlens = torch.tensor([5, 40, 117], dtype=torch.int32)
+        cache.cache_seqlens.copy_(seqlens)
+        cache._pos_uniform = None
+        x = (torch.randn(B, T, H, D, generator=g) * 2.0).to(torch.bfloat16)
+        cos, sin = rot._cos_sin(T, cache)
+        y = apply_rotary_emb(x, cos, sin)
+        n = RMSNorm(eps=None)(y)
+        z = n * 1.2
+        np.savez_compressed(os.path.join(out_dir, f"rope_norm_D{D}.npz"),
+                 x=bits(x), seqlens=seqlens.numpy(), cos_table=bits(rot.cos[0, :, 0]),
+                 sin_table=bits(rot.sin[0, :, 0]), rope=bits(y), norm=bits(n), out=bits(z))
+
+
+def make_kv_attn(out_dir):
+    import torch
+    import modelcore.kernels.flash_attn as fa
+
+    cases = [
+        # name, seqlens, Hq, Hkv, D, T_new, window, Tmax
+        ("ragged_mha_d16_t1_wfull", [4, 17, 31, 9], 4, 4, 16, 1, -1, 48),
+        ("ragged_mha_d16_t1_w8", [4, 17, 31, 9], 4, 4, 16, 1, 8, 48),
+        ("ragged_mha_d16_t3_wfull", [4, 17, 31, 9], 4, 4, 16, 3, -1, 48),
+        ("ragged_mha_d16_t3_w8", [4, 17, 31, 9], 4, 4, 16, 3, 8, 48),
+        ("uniform_mha_d16_t1_w8", [13, 13], 4, 4, 16, 1, 8, 48),
+        ("ragged_gqa_d64_t1_wfull", [0, 5, 70, 129], 8, 2, 64, 1, -1, 160),
+        ("ragged_gqa_d128_t1_w33", [1, 40, 100], 8, 2, 128, 1, 33, 128),
+        ("ragged_gqa_d128_t2_wfull", [3, 64, 65], 16, 4, 128, 2, -1, 80),
+        ("uniform_mha_d64_t1_wfull", [77, 77], 12, 12, 64, 1, -1, 96),
+        ("ragged_mha_d32_t1_w0", [6, 2], 4, 4, 32, 1, 0, 16),
+        ("ragged_gqa_d256_t1_w20", [30, 7], 4, 1, 256, 1, 20, 40),
+    ]
+    fa._override_impl = "sdpa"
+    for name, seqlens, Hq, Hkv, D, T, window, Tmax in cases:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        B = len(seqlens)
+        r = lambda *s: bf16_representable(torch.randn(*s, generator=g))
+        k_cache = torch.zeros(B, Tmax, Hkv, D)
+        v_cache = torch.zeros_like(k_cache)
+        for i, L in enumerate(seqlens):
+            k_cache[i, :L] = r(L, Hkv, D)
+            v_cache[i, :L] = r(L, Hkv, D)
+        # stale garbage past each row's content: must be unreachable (test_kernels.py:487-498)
+        for i, L in enumerate(seqlens):
+            k_cache[i, L + T:] = bf16_representable(torch.full((Tmax - L - T, Hkv, D), 3.0))
+            v_cache[i, L + T:] = bf16_representable(torch.full((Tmax - L - T, Hkv, D), -3.0))
+        q, k, v = r(B, T, Hq, D), r(B, T, Hkv, D), r(B, T, Hkv, D)
+        cs = torch.tensor(seqlens, dtype=torch.int32)
+        kc0, vc0 = k_cache.clone(), v_cache.clone()
+        y = fa.flash_attn_with_kvcache(q, k_cache, v_cache, k=k, v=v, cache_seqlens=cs,
+                                       causal=True, window_size=(window, 0))
+        b16 = lambda t: bits(t.to(torch.bfloat16))
+        np.savez_compressed(os.path.join(out_dir, f"kv_attn_{name}.npz"),
+                 seqlens=cs.numpy(), window=np.int64(window), q=b16(q), k=b16(k), v=b16(v),
+                 k_cache_before=b16(kc0), v_cache_before=b16(vc0),
+                 k_cache_after=b16(k_cache), v_cache_after=b16(v_cache), y=y.numpy())
+    fa._override_impl = None
+
+
+def make_prefill(out_dir):
+    import torch
+    from modelcore.cache import KVCache
+
+    g = torch.Generator().manual_seed(7)
+    S, H, D = 2, 2, 16
+
+    def filled(n):
+        c = KVCache(batch_size=1, n_kv_head=H, seq_len=n, head_dim=D, num_kv_slots=S, device="cpu",
+                    dtype=torch.float32)
+        c.k_cache.copy_(bf16_representable(torch.randn(c.k_cache.shape, generator=g)))
+        c.v_cache.copy_(bf16_representable(torch.randn(c.v_cache.shape, generator=g)))
+        c.advance(n)
+        return c
+
+    src = filled(7)
+    dst = KVCache(batch_size=4, n_kv_head=H, seq_len=24, head_dim=D, num_kv_slots=S, device="cpu",
+                  dtype=torch.float32)
+    dst.prefill(src)
+    a, b = filled(5), filled(11)
+    rows = KVCache(batch_size=3, n_kv_head=H, seq_len=24, head_dim=D, num_kv_slots=S, device="cpu",
+                   dtype=torch.float32)
+    rows.prefill_row(1, a)
+    rows.prefill_row(2, b)
+    b16 = lambda t: bits(t.to(torch.bfloat16))
+    np.savez_compressed(os.path.join(out_dir, "prefill.npz"),
+             src_k=b16(src.k_cache), src_v=b16(src.v_cache), bcast_k=b16(dst.k_cache),
+             bcast_v=b16(dst.v_cache), bcast_seqlens=dst.cache_seqlens.numpy(),
+             row_a_k=b16(a.k_cache), row_a_v=b16(a.v_cache), row_b_k=b16(b.k_cache),
+             row_b_v=b16(b.v_cache), rows_k=b16(rows.k_cache), rows_v=b16(rows.v_cache),
+             rows_seqlens=rows.cache_seqlens.numpy())
+
+
+def quickstart_config():
+    from modelcore import ComponentSpec, ModelConfig
+    head_dim = 64
+    return ModelConfig(
+        sequence_len=1024, vocab_size=32768, n_embd=768, pad_vocab_size_to=64, template="base",
+        shared={"rope": ComponentSpec("rotary", {"head_dim": head_dim, "over_compute": 10}),
+                "norm": ComponentSpec("rms_norm", {"eps": None})},
+        input=ComponentSpec("token_embedding", {"smear": False}),
+        body=ComponentSpec("stack", {"features": [], "blocks": [
+            ComponentSpec("block", {
+                "layer_idx": i, "features": [],
+                "mixer": ComponentSpec("attention", {"n_head": 12, "n_kv_head": 12, "head_dim": head_dim,
+                                                     "window": -1, "kv_slot": None, "produces_kv": True,
+                                                     "features": []}),
+                "ffn": ComponentSpec("gated_mlp", {"activation": "silu", "hidden_dim": 2048}),
+            })
+            for i in range(12)
+        ]}),
+        output=ComponentSpec("lm_head", {"softcap": 15}),
+    )
+
+
+def make_decode_cfg1(out_dir, steps=64):
+    import torch
+    from modelcore import ModelManager
+    from modelcore.generate import sample_next_token
+
+    manager = ModelManager()
+    out = {}
+    for variant in ("random", "awake"):
+        model = manager.create_model(quickstart_config(), device=torch.device("cpu"), seed=0)
+        if variant == "awake":
+            g = torch.Generator().manual_seed(1)
+            with torch.no_grad():
+                for p in model.parameters():
+                    if p.numel() and p.abs().sum() == 0:
+                        p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+        model.eval()
+        prompts = torch.randint(0, 32768, (2, 16), generator=torch.Generator().manual_seed(1))
+        dec = manager.new_decoder(model, prompts.tolist(), max_tokens=steps)
+        toks, margins = [], []
+        for _ in range(steps):
+            logits = dec.logits
+            top2 = torch.topk(logits, 2, dim=-1).values
+            margins.append((top2[:, 0] - top2[:, 1]).numpy())
+            nxt = sample_next_token(logits, rng=None, temperature=0.0)[:, 0]
+            toks.append(nxt.numpy())
+            dec.step(nxt.tolist())
+        out[f"{variant}_tokens"] = np.stack(toks, axis=1)
+        out[f"{variant}_margins"] = np.stack(margins, axis=1).astype(np.float32)
+        out["prompts"] = prompts.numpy()
+    np.savez_compressed(os.path.join(out_dir, "decode_cfg1.npz"), **out)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--ref", default=os.environ.get("MODELCORE_REF_PATH",
+                                                    os.path.join(REPO, "baseline", "_ref")))
+    ap.add_argument("--out", default=HERE)
+    ap.add_argument("--skip-decode", action="store_true")
+    args = ap.parse_args()
+    os.environ.setdefault("MODELCORE_DTYPE", "float32")
+    _import_reference(args.ref)
+    import torch
+    torch.manual_seed(0)
+    make_rope_norm(args.out)
+    make_kv_attn(args.out)
+    make_prefill(args.out)
+    if not args.skip_decode:
+        make_decode_cfg1(args.out)
+    print("wrote fixtures to", args.out)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+"""The C-ABI library on the CPU: it loads without a GPU, exports every symbol include/mcb200.h
+declares, its ctypes structures match the C layout (checked against gcc), and host-side argument
+checks reject bad input with a status and a message before anything touches a device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import REPO
+from modelcore_b200 import _native
+from modelcore_b200._native import AppendArgs, AttnArgs, CopyArgs
+
+HEADER = os.path.join(REPO, "include", "mcb200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t)\s+(mcb_\w+)\s*\(", text, re.M)))
+
+
+def test_library_loads_and_reports_its_abi_version():
+    lib = _native.load()
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 1
+
+
+def test_every_declared_symbol_is_exported():
+    lib = _native.load()
+    declared = declared_functions()
+    assert len(declared) >= 9
+    assert sorted(_native.EXPORTED_SYMBOLS) == declared
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def _c_layout(struct, fields):
+    src = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
+           f'printf("%zu\\n", sizeof({struct}));']
+    src += [f'printf("%zu\\n", offsetof({struct}, {f}));' for f in fields]
+    src += ["return 0;}"]
+    tmp = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"mcb_layout_{struct}_{os.getpid()}")
+    with open(tmp + ".c", "w") as fh:
+        fh.write("\n".join(src))
+    subprocess.run(["gcc", "-O0", "-o", tmp, tmp + ".c"], check=True)
+    out = subprocess.run([tmp], check=True, capture_output=True, text=True).stdout.split()
+    os.unlink(tmp)
+    os.unlink(tmp + ".c")
+    return [int(x) for x in out]
+
+
+@pytest.mark.parametrize("cls,cname", [(AppendArgs, "mcb_append_args"), (CopyArgs, "mcb_copy_args"),
+                                       (AttnArgs, "mcb_attn_args")])
+def test_ctypes_structures_match_the_c_layout(cls, cname):
+    fields = [f for f, _ in cls._fields_]
+    c = _c_layout(cname, fields)
+    assert c[0] == ctypes.sizeof(cls)
+    assert c[1:] == [getattr(cls, f).offset for f in fields]
+
+
+def _err(status):
+    return status, _native.last_error()
+
+
+def test_append_rejects_bad_arguments_on_the_host():
+    lib = _native.load()
+    st, msg = _err(lib.mcb_kv_append_rope(None, None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
+    a = AppendArgs()
+    a.B, a.T, a.D = 1, 1, 64
+    a.flags = 0
+    st, msg = _err(lib.mcb_kv_append_rope(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "flags 0" in msg
+    a.flags = _native.MCB_APPEND_ROTATE_K
+    st, msg = _err(lib.mcb_kv_append_rope(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "WRITE_KV" in msg
+    a.flags = 1 << 7
+    st, msg = _err(lib.mcb_kv_append_rope(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "unknown flags" in msg
+    a.flags = _native.MCB_APPEND_WRITE_KV
+    a.cache_seqlens = 16
+    st, msg = _err(lib.mcb_kv_append_rope(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "WRITE_KV needs" in msg
+
+
+def test_copy_rejects_out_of_range_rows_and_lengths():
+    lib = _native.load()
+    a = CopyArgs()
+    a.n_slots, a.src_batch, a.src_row, a.src_tmax = 2, 1, 0, 8
+    a.dst_batch, a.dst_row_begin, a.dst_row_count, a.dst_tmax = 4, 3, 2, 16
+    a.n_pos, a.row_elems = 4, 64
+    st, msg = _err(lib.mcb_kv_copy_rows(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "out of range" in msg
+    a.dst_row_begin, a.dst_row_count, a.n_pos = 0, 4, 9
+    st, msg = _err(lib.mcb_kv_copy_rows(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "exceed cache length" in msg
+    a.n_pos, a.row_elems = 4, 12
+    st, msg = _err(lib.mcb_kv_copy_rows(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_ALIGNMENT
+
+
+def _attn(**kw):
+    a = AttnArgs()
+    a.B, a.T, a.Hq, a.Hkv, a.D, a.Tmax, a.window = 2, 1, 8, 2, 128, 64, -1
+    a.softmax_scale = 0.088
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_attention_rejects_unsupported_shapes_without_a_device():
+    lib = _native.load()
+    a = _attn(D=48)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "head_dim 48" in msg
+    assert lib.mcb_decode_attn_workspace_size(ctypes.byref(a)) == 0
+    a = _attn(Hq=6, Hkv=4)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "divisible" in msg
+    a = _attn()  # NULL pointers
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
+
+
+def test_attention_workspace_grows_with_forced_splits():
+    lib = _native.load()
+    one = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=1, Tmax=1024)))
+    four = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=4, Tmax=1024)))
+    # splits are capped by the key tiles a row can span: Tmax 64 -> at most 2
+    capped = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=4, Tmax=64)))
+    assert capped == 16 * 2 * 128 * 4 + 256
+    assert one == 0
+    # (B*T*Hq rows) x splits x (D + 1) fp32, each part rounded up to 256 bytes
+    rows = 2 * 1 * 8
+    assert four == ((rows * 4 * 128 * 4 + 255) // 256 * 256) + ((rows * 4 * 4 + 255) // 256 * 256)
+
+
+def test_attention_checks_the_workspace_before_launching():
+    lib = _native.load()
+    a = _attn(num_splits=4, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000,
+              cache_seqlens=0x5000)
+    a.q_stride[:] = (8 * 128, 8 * 128, 128)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_WORKSPACE and "workspace" in msg
+    a.q_stride[:] = (8 * 128, 8 * 128, 100)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_ALIGNMENT
+
+
+def test_advance_rejects_null():
+    lib = _native.load()
+    st, _ = _err(lib.mcb_kv_advance(None, 4, 1, None))
+    assert st == _native.MCB_ERR_INVALID_ARG

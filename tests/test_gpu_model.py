@@ -1,0 +1,166 @@
+"""End-to-end parity through modelcore's own API on the GPU: the reference (modelcore's SDPA path,
+unmodified) and the B200 path decode the same weights and prompts in bf16 on the same device.
+
+* greedy token streams are identical for 64 steps (README quickstart architecture, awake weights)
+* logits agree within LOGIT_TOL at every step
+* multi-prompt right-ragged decode agrees on every reference test flavor that has attention
+  (windows, cross-layer KV sharing, GQA, gates, value embeddings, smear, layer_norm QK-norm)
+* the CUDA-graph decoder reproduces the eager decoder bit for bit
+"""
+import copy
+
+import pytest
+import torch
+
+from conftest import have_modelcore, load_golden
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def env():
+    if not have_modelcore():
+        raise RuntimeError("modelcore (the reference package) is not importable: install it into "
+                           "baseline/_ref (see DESIGN.md) to run the end-to-end parity tests")
+    import modelcore
+    import modelcore_b200
+    return modelcore, modelcore_b200
+
+
+def _pair(env, config, awake=True):
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    ref_mgr = modelcore.ModelManager()
+    cpu = ref_mgr.create_model(config, device=torch.device("cpu"), seed=0)
+    if awake:
+        workloads.awaken(cpu)
+    cpu.eval()
+    ref = copy.deepcopy(cpu).to("cuda")
+    mine = copy.deepcopy(cpu).to("cuda")
+    assert mcb.install(mine) > 0
+    return ref_mgr, ref, mcb.ModelManager(), mine
+
+
+@torch.inference_mode()
+def _greedy(mgr, model, prompts, steps):
+    dec = mgr.new_decoder(model, prompts, max_tokens=steps)
+    toks, logits = [], []
+    for _ in range(steps):
+        lg = dec.logits.float().clone()
+        logits.append(lg)
+        nxt = torch.argmax(lg, dim=-1)
+        toks.append(nxt)
+        dec.step(nxt.tolist())
+    logits.append(dec.logits.float().clone())
+    return torch.stack(toks, 1).cpu(), logits, dec
+
+
+@pytest.mark.parametrize("awake", [True, False], ids=["awake", "random-init"])
+def test_quickstart_greedy_stream_matches_the_reference_for_64_steps(env, awake):
+    """Measurement config 1's model and prompts (2 x 16 tokens from seed 1), 64 greedy steps.
+    With modelcore's plain init (zero c_proj) attention cannot reach the logits, so the awake
+    variant is the one that tests the decode path; both must match the reference."""
+    from modelcore_b200 import workloads
+    z = load_golden("decode_cfg1.npz")
+    prompts = z["prompts"].tolist()
+    ref_mgr, ref, mgr, mine = _pair(env, workloads.quickstart_config(), awake=awake)
+    t_ref, l_ref, _ = _greedy(ref_mgr, ref, prompts, 64)
+    t_mine, l_mine, dec = _greedy(mgr, mine, prompts, 64)
+    import modelcore_b200
+    assert isinstance(dec.kv_cache, modelcore_b200.KVCache)
+    worst = max((a - b).abs().max().item() for a, b in zip(l_ref, l_mine))
+    print(f"quickstart awake={awake}: max |logit diff| over 65 steps = {worst:.3e}")
+    assert torch.equal(t_ref, t_mine)
+    assert worst <= LOGIT_TOL
+
+
+def _attention_flavors():
+    from modelcore.tests.conftest import FLAVORS
+    out = []
+    for name, make in FLAVORS.items():
+        cfg = make()
+        if any(b.params["mixer"].type == "attention" for b in cfg.body.params["blocks"]):
+            out.append(name)
+    return out
+
+
+def _flavor_names():
+    try:
+        return _attention_flavors()
+    except Exception:  # collection without modelcore: the env fixture reports it
+        return ["plain_kvshare_win"]
+
+
+@pytest.mark.parametrize("flavor", _flavor_names())
+def test_multi_prompt_ragged_decode_matches_the_reference(env, flavor):
+    """modelcore/tests/test_generate.py:298-320 run as reference-vs-B200 on the GPU: right-ragged
+    prompts, fixed token columns, logits compared at every step."""
+    from modelcore.tests.conftest import FLAVORS
+    from modelcore.tests.test_generate import RAGGED_PROMPTS
+    ref_mgr, ref, mgr, mine = _pair(env, FLAVORS[flavor]())
+    steps = 12
+    with torch.inference_mode():
+        a = ref_mgr.new_decoder(ref, RAGGED_PROMPTS, max_tokens=steps)
+        b = mgr.new_decoder(mine, RAGGED_PROMPTS, max_tokens=steps)
+        assert b.kv_cache.cache_seqlens.tolist() == [len(p) for p in RAGGED_PROMPTS]
+        for step in range(steps + 1):
+            d = (a.logits.float() - b.logits.float()).abs().max().item()
+            assert d <= LOGIT_TOL, (flavor, step, d)
+            if step == steps:
+                break
+            column = [(step * 7 + i * 3) % 100 + 1 for i in range(len(RAGGED_PROMPTS))]
+            a.step(column)
+            b.step(column)
+        assert b.kv_cache.cache_seqlens.tolist() == [len(p) + steps for p in RAGGED_PROMPTS]
+
+
+def test_graph_decoder_reproduces_the_eager_decoder_bit_for_bit(env):
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    mgr = mcb.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
+                                              device=torch.device("cuda"), seed=0))
+    model.eval()
+    prompts = workloads.prompts(3, 20, seed=1).tolist()
+    prompts[1] = prompts[1][:7]  # ragged rows
+    eager = mgr.new_decoder(model, prompts, max_tokens=16)
+    graph = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+    with torch.inference_mode():
+        for step in range(10):
+            col = [(step * 5 + i) % 1000 for i in range(3)]
+            le = eager.step(col).clone()
+            lg = graph.step(col).clone()
+            assert torch.equal(le, lg), step
+        assert graph.kv_cache.cache_seqlens.tolist() == eager.kv_cache.cache_seqlens.tolist()
+        assert graph.kv_cache.host_lens().tolist() == eager.kv_cache.cache_seqlens.tolist()
+        # device-resident greedy loop == host-driven greedy loop
+        g2 = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+        e2 = mgr.new_decoder(model, prompts, max_tokens=16)
+        dev_tokens = g2.greedy_steps(12).cpu()
+        host = []
+        for _ in range(12):
+            nxt = torch.argmax(e2.logits, dim=-1)
+            host.append(nxt.cpu())
+            e2.step(nxt.tolist())
+        assert torch.equal(dev_tokens, torch.stack(host, 1))
+
+
+def test_config4_broadcast_and_kv_sharing_decode_matches_the_reference(env):
+    """Config 4's structure at reduced depth and width of prompt: one prompt prefilled once,
+    broadcast to every row, odd layers reading the even layers' slots, windowed layers."""
+    from modelcore_b200 import workloads
+    cfg = workloads.gqa_window_config(n_layer=4, kv_share=True, window=64)
+    ref_mgr, ref, mgr, mine = _pair(env, cfg)
+    prompt = workloads.prompts(1, 150, seed=3)[0].tolist()
+    with torch.inference_mode():
+        a = ref_mgr.new_decoder(ref, prompt, num_samples=4, max_tokens=40)
+        b = mgr.new_decoder(mine, prompt, num_samples=4, max_tokens=40)
+        assert b.kv_cache.get_pos() == 150 and b.kv_cache.n_slots == 2
+        for step in range(40):
+            d = (a.logits.float() - b.logits.float()).abs().max().item()
+            assert d <= LOGIT_TOL, (step, d)
+            col = [(step * 11 + i) % 30000 for i in range(4)]
+            a.step(col)
+            b.step(col)

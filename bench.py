@@ -1,0 +1,455 @@
+"""Decode benchmark of modelcore's KV-cache path on B200: tokens/s and KV-read HBM GB/s.
+
+    python bench.py [--gpus N --steps K --warmup W]            # this implementation
+    python bench.py --impl reference [--steps K --warmup W]    # the reference on the host CPU
+    torchrun --nproc-per-node N bench.py --gpus N ...           # N > 1: one rank per GPU
+
+Workload (measurement config 2): modelcore's README quickstart architecture (12 blocks, n_embd
+768, 12 q / 12 kv heads of 64, gated SiLU MLP 2048, vocab 32768) with bf16 random-init weights
+(seed 0); 64 prompts per GPU of 512 tokens uniform in [0, 32768) (seed 1); KV cache of 1024
+positions; prefill through modelcore's Decoder, then greedy decode.  A step is one decode step of
+all 64 rows (every layer, the LM head and the greedy pick).  Scaling is weak: every rank decodes
+its own 64 rows (rows r*64 .. r*64+63 of one seeded 64*N-prompt batch) with no collective on the
+hot path; the sampled tokens are gathered with NCCL at the end of the timed region.
+
+value      64*N*K / max-over-ranks(device time of K CUDA-graph replays), tokens/s; the graph
+           feeds each step's greedy token to the next on the device.
+e2e        the same through the public step() call: per step a pinned host->device copy of the
+           token column, the replayed step, and the device->host read of the greedy tokens.
+roofline   the decode-attention kernel: algorithmic KV bytes (exact keys per row and layer,
+           2*Hkv*D*2 bytes each) / its mean launch time, timed with CUDA events on its stream
+           over the 12 cache slots in rotation (1.6 GB, far above L2), against the measured HBM
+           copy bandwidth in MEASURED_PEAKS.json.
+kv_read_sweep  measurement config 5 (32 q / 8 kv heads of 128, lengths U[1, 32768] from seed 5,
+           window -1 / 4096): one step = fused rope append + decode attention; L2 flushed before
+           every timed launch.
+cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
+           sample of the same workload (rank 0, N = 1).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+ROWS_PER_GPU = 64
+PROMPT_LEN = 512
+DECODE_LEN = 512
+CPU_SAMPLE_ROWS = 8
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode tokens/sec + KV-read HBM GB/s (% of peak) at 1/2/4/8 B200"
+
+
+def _ensure_modelcore():
+    try:
+        import modelcore  # noqa: F401
+    except ImportError:
+        ref = os.path.join(REPO, "baseline", "_ref")
+        if os.path.isdir(ref):
+            sys.path.append(ref)
+        import modelcore  # noqa: F401
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks during the timed region
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "25", "-i", str(self.gpu_id)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, which):
+        """Records the host time at which the timed region starts ('start') or ends ('end');
+        the summary keeps the samples taken between the two marks (all, if too few)."""
+        setattr(self, which, time.time())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        lo, hi = getattr(self, "start", 0.0), getattr(self, "end", float("inf"))
+        inside = [ln for t, ln in self.lines if lo <= t <= hi + 0.05]
+        if len(inside) < 3:
+            inside = [ln for _, ln in self.lines]
+        for line in inside:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                sm.append(float(parts[2]))
+                mx = float(parts[3])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[6:10]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+def _dist_setup(n_gpus):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def _max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _build_decoder(rank, world, steps_needed):
+    import torch
+    import modelcore_b200
+    from modelcore_b200 import workloads
+    mgr = modelcore_b200.ModelManager()
+    model = mgr.create_model(workloads.quickstart_config(), device=torch.device("cuda"), seed=0)
+    model = model.to(torch.bfloat16).eval()
+    all_prompts = workloads.prompts(ROWS_PER_GPU * world, PROMPT_LEN, seed=1)
+    mine = all_prompts[rank * ROWS_PER_GPU:(rank + 1) * ROWS_PER_GPU].tolist()
+    with torch.inference_mode():
+        dec = mgr.new_decoder(model, mine, max_tokens=DECODE_LEN, cuda_graph=True)
+    assert steps_needed <= DECODE_LEN, "more decode steps than the configured 512"
+    return mgr, model, dec
+
+
+def _attention_roofline(dec, peak, reps=4):
+    """Mean launch time of the decode-attention kernel on the bench's own cache (current
+    lengths), rotating over the 12 slots; algorithmic bytes = exact keys x 2 x Hkv x D x 2."""
+    import torch
+    from modelcore_b200 import ops
+    cache = dec.kv_cache
+    B, H, D, S = cache.batch_size, cache.n_kv_head, cache.head_dim, cache.n_slots
+    q = torch.randn(B, 1, H, D, device="cuda").to(torch.bfloat16)
+    lens = cache.host_lens()
+    keys = int(sum(L + 1 for L in lens))
+    bytes_per_launch = keys * 2 * H * D * 2
+    out = torch.empty_like(q)
+    for s in range(S):  # warm
+        ops.decode_attn(q, cache.k_cache[s], cache.v_cache[s], cache.cache_seqlens, out=out)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    n = 0
+    for _ in range(reps):
+        for s in range(S):
+            ops.decode_attn(q, cache.k_cache[s], cache.v_cache[s], cache.cache_seqlens, out=out)
+            n += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    gbs = bytes_per_launch / (us * 1e-6) / 1e9
+    return {"bytes_per_launch": bytes_per_launch, "us_per_launch": us, "achieved_gbs": gbs,
+            "frac": gbs / peak, "mean_context": keys / B}
+
+
+def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
+    """Config 5: fused rope append + decode attention per step, cold L2 per launch."""
+    import numpy as np
+    import torch
+    from modelcore_b200 import ops
+    Hq, Hkv, D, Tmax = 32, 8, 128, 32769
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rows = []
+    max_b = max(batches)
+    kc = torch.randn(max_b, Tmax, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(max_b, Tmax, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    ang = torch.arange(Tmax + 1, device="cuda", dtype=torch.float32)[:, None] * \
+        (100000.0 ** (-torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))[None]
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    for B in batches:
+        lens = np.random.default_rng(5).integers(1, 32769, size=B) - 1
+        sl = torch.from_numpy(lens).to(torch.int32).cuda()
+        q = torch.randn(B, 1, Hq, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        kcb, vcb = kc[:B], vc[:B]
+        for w in windows:
+            keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
+            nbytes = keys * 2 * Hkv * D * 2
+            t_att, t_step = [], []
+            for it in range(6):
+                flush.zero_()
+                a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                a0.record(stream)
+                qr = ops.kv_append_rope(q, k, v, kcb, vcb, sl, cos, sin)
+                a1.record(stream)
+                ops.decode_attn(qr, kcb, vcb, sl, window=w)
+                a2.record(stream)
+                torch.cuda.synchronize()
+                if it:
+                    t_att.append(a1.elapsed_time(a2))
+                    t_step.append(a0.elapsed_time(a2))
+            ta, ts = statistics.median(t_att), statistics.median(t_step)
+            gbs = nbytes / (ta * 1e-3) / 1e9
+            rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
+                         "attn_us": round(ta * 1e3, 1), "step_us": round(ts * 1e3, 1),
+                         "kv_gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
+    del kc, vc, flush
+    torch.cuda.empty_cache()
+    return rows
+
+
+def _cpu_reference_decode(rows, steps, warmup, threads=None):
+    """The reference itself (modelcore's Decoder over its KVCache and SDPA path, fp32 on the host
+    cores) on `rows` of the same prompts; returns (tokens/s, seconds per step, cores)."""
+    import torch
+    _ensure_modelcore()
+    import modelcore
+    from modelcore_b200 import workloads
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    mgr = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
+    model = mgr.create_model(workloads.quickstart_config(), device=torch.device("cpu"), seed=0).eval()
+    prompts = workloads.prompts(rows, PROMPT_LEN, seed=1).tolist()
+    with torch.inference_mode():
+        dec = mgr.new_decoder(model, prompts, max_tokens=DECODE_LEN)
+        tok = torch.argmax(dec.logits, dim=-1)
+        for _ in range(warmup):
+            tok = torch.argmax(dec.step(tok.tolist()), dim=-1)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok = torch.argmax(dec.step(tok.tolist()), dim=-1)
+        dt = time.perf_counter() - t0
+    return rows * steps / dt, dt / steps, threads
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    rows = CPU_SAMPLE_ROWS
+    tps, sps, cores = _cpu_reference_decode(rows, args.steps, args.warmup)
+    sample = (f"{rows} of the 64 rows per GPU, 512-token prompts, {args.steps} timed greedy decode "
+              f"steps after {args.warmup} warm-up steps, modelcore SDPA path in fp32 on "
+              f"{cores} threads ({_cpu_model()})")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 2), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded uniform token ids)",
+        "config": _config(args.gpus),
+        "cpu_baseline": {"value": round(tps, 2), "unit": "tokens/s", "cores": cores,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config(n):
+    return {"workload": "config 2: README quickstart model (12 x 768, 12/12 heads of 64), bf16 weights, "
+                        "64 prompts x 512 tokens per GPU, KV cache 1024, greedy decode",
+            "model": "modelcore quickstart 12x768", "global_batch": ROWS_PER_GPU * n,
+            "seq_len": PROMPT_LEN + DECODE_LEN, "prompt_len": PROMPT_LEN,
+            "parallelism": f"batch-sharded replicas x{n}",
+            "l2": "inputs larger than L2: 1.2-2.4 GB of KV + 0.2 GB of weights per step per GPU"}
+
+
+def run_b200(args):
+    import torch
+    _ensure_modelcore()
+    import modelcore_b200
+    from modelcore_b200 import ops
+    rank, world, local = _dist_setup(args.gpus)
+    peak, peak_kind = _peaks()
+    steps_needed = 1 + args.warmup + args.steps + args.e2e_steps
+    mgr, model, dec = _build_decoder(rank, world, steps_needed)
+    cache = dec.kv_cache
+    B = cache.batch_size
+
+    # warm-up: the first step runs eagerly, the second captures the CUDA graph, the rest replay it
+    with torch.inference_mode():
+        dec.greedy_steps(1 + args.warmup)
+    tokens = torch.empty((B, args.steps), dtype=torch.long, device="cuda")
+    ctx_before = cache.host_lens().copy()
+
+    _barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_uuid = torch.cuda.get_device_properties(local).uuid
+    with ClockSampler(f"GPU-{gpu_uuid}" if gpu_uuid else local) as clocks:
+        time.sleep(0.3)  # let the sampler start before the timed region
+        clocks.mark("start")
+        e0.record(stream)
+        with torch.inference_mode():
+            dec.greedy_steps(args.steps, first_tokens=None, out=tokens)
+            if world > 1:
+                import torch.distributed as dist
+                gathered = torch.empty((B * world, args.steps), dtype=torch.long, device="cuda")
+                dist.all_gather_into_tensor(gathered, tokens)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clocks.mark("end")
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    _barrier(world)
+    ctx_after = cache.host_lens().copy()
+    value = B * world * args.steps / (ms * 1e-3)
+    kv_bytes_step = float(((ctx_before + ctx_after) / 2 + 1).sum()) * cache.n_slots * 2 * \
+        cache.n_kv_head * cache.head_dim * 2
+
+    # e2e: the public step() with host token columns in pinned memory, tokens read back per step
+    with torch.inference_mode():
+        host_tok = torch.argmax(dec.logits, dim=-1).cpu().pin_memory()
+        _barrier(world)
+        t0 = time.perf_counter()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            logits = dec.step(host_tok)
+            host_tok = torch.argmax(logits, dim=-1).to("cpu")
+        f1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
+    e2e_value = B * world * args.e2e_steps / (e2e_ms * 1e-3)
+
+    roof = _attention_roofline(dec, peak)
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = _kv_read_sweep(peak)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
+        cpu = {"value": round(tps, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
+               "sample": f"{CPU_SAMPLE_ROWS} of the 64 rows, 512-token prompts, 5 timed greedy "
+                         f"steps, modelcore SDPA path fp32 ({_cpu_model()})"}
+
+    if rank != 0:
+        return
+    launches_per_step = dec.launches_per_step  # libmcb200 kernels in one captured step
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded uniform token ids, random-init weights)",
+        "config": _config(world),
+        "kv_read": {"bytes_per_step": int(kv_bytes_step),
+                    "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
+                    "attention_kernel_gbs": round(roof["achieved_gbs"], 1),
+                    "attention_frac_of_peak": round(roof["frac"], 3),
+                    "mean_context": round(roof["mean_context"], 1)},
+        "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(roof["frac"], 4),
+                     "traffic": None, "kernel": "mcb::decode_attn_kernel<64,1,16,4>",
+                     "algorithmic_bytes_per_launch": roof["bytes_per_launch"],
+                     "us_per_launch": round(roof["us_per_launch"], 2),
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+                "wall_s": round(wall, 4)},
+        "gpu_launches": int(launches_per_step * args.steps) if launches_per_step else None,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "kv_read_sweep": sweep,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description="modelcore KV-cache decode benchmark (B200)")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

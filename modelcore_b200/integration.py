@@ -185,7 +185,7 @@ class GraphDecoder:
         self._ids = torch.zeros((B, 1), dtype=torch.long, device=dev)
         self._ids_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
         self._static_logits = None
-        self._next = None
+        self.launches_per_step = None  # libmcb200 kernels recorded in one captured step
 
     @property
     def logits(self):
@@ -199,6 +199,7 @@ class GraphDecoder:
         snap = cache.host_state()
         state_snap = dict(cache.state)
         g = torch.cuda.CUDAGraph()
+        launches = ops.launch_count()
         with torch.inference_mode():
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
@@ -209,6 +210,7 @@ class GraphDecoder:
                     nxt = torch.argmax(logits, dim=-1, keepdim=True)
                     self._ids.copy_(nxt)
             torch.cuda.current_stream().wait_stream(side)
+        self.launches_per_step = ops.launch_count() - launches
         cache.restore_host_state(snap)
         cache.state.update(state_snap)
         return g, logits, nxt

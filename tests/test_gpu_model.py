@@ -57,23 +57,68 @@ def _greedy(mgr, model, prompts, steps):
     return torch.stack(toks, 1).cpu(), logits, dec
 
 
-@pytest.mark.parametrize("awake", [True, False], ids=["awake", "random-init"])
-def test_quickstart_greedy_stream_matches_the_reference_for_64_steps(env, awake):
-    """Measurement config 1's model and prompts (2 x 16 tokens from seed 1), 64 greedy steps.
-    With modelcore's plain init (zero c_proj) attention cannot reach the logits, so the awake
-    variant is the one that tests the decode path; both must match the reference."""
+def test_quickstart_random_init_greedy_stream_matches_the_reference_for_64_steps(env):
+    """Measurement config 1 as stated (README quickstart, modelcore's random init, seed 0;
+    prompts 2 x 16 from seed 1): 64 greedy steps identical to the reference's on the same GPU."""
     from modelcore_b200 import workloads
     z = load_golden("decode_cfg1.npz")
     prompts = z["prompts"].tolist()
-    ref_mgr, ref, mgr, mine = _pair(env, workloads.quickstart_config(), awake=awake)
+    ref_mgr, ref, mgr, mine = _pair(env, workloads.quickstart_config(), awake=False)
     t_ref, l_ref, _ = _greedy(ref_mgr, ref, prompts, 64)
     t_mine, l_mine, dec = _greedy(mgr, mine, prompts, 64)
     import modelcore_b200
     assert isinstance(dec.kv_cache, modelcore_b200.KVCache)
-    worst = max((a - b).abs().max().item() for a, b in zip(l_ref, l_mine))
-    print(f"quickstart awake={awake}: max |logit diff| over 65 steps = {worst:.3e}")
     assert torch.equal(t_ref, t_mine)
-    assert worst <= LOGIT_TOL
+    assert max((a - b).abs().max().item() for a, b in zip(l_ref, l_mine)) <= LOGIT_TOL
+
+
+@torch.inference_mode()
+def _forced(mgr, model, prompts, columns):
+    """Logits before each forced step (teacher forcing), plus the final ones."""
+    dec = mgr.new_decoder(model, prompts, max_tokens=columns.shape[1])
+    out = []
+    for i in range(columns.shape[1]):
+        out.append(dec.logits.float().clone())
+        dec.step(columns[:, i].tolist())
+    out.append(dec.logits.float().clone())
+    return torch.stack(out, 1)
+
+
+def test_quickstart_awake_decode_is_as_accurate_as_the_reference(env):
+    """Config 1's model with modelcore's test wake-up (attention reaches the logits).  Its logits
+    are small (lm_head init std 1e-3), so greedy top-2 margins are often below bf16 noise and the
+    reference's own bf16 stream departs from its fp32 stream within a few steps.  So, under
+    identical contexts (the reference's bf16 greedy tokens, forced on every path):
+      * B200 logits are within 2e-2 of the reference evaluated in fp32 on the GPU, and no
+        further from it than the reference's bf16 SDPA path (x1.25 + 1e-3);
+      * wherever B200 and the reference pick different greedy tokens, the fp32 top-2 margin is
+        within the two paths' combined error (a genuine near-tie)."""
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    z = load_golden("decode_cfg1.npz")
+    prompts = z["prompts"].tolist()
+    ref_mgr, ref, mgr, mine = _pair(env, workloads.quickstart_config(), awake=True)
+    m32 = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
+    ref32 = m32.create_model(workloads.quickstart_config(), device=torch.device("cpu"), seed=0)
+    ref32.load_state_dict({k: v.float().cpu() for k, v in ref.state_dict().items()})
+    ref32 = ref32.to("cuda").eval()
+    t_ref, _, _ = _greedy(ref_mgr, ref, prompts, 64)
+    l_ref = _forced(ref_mgr, ref, prompts, t_ref)
+    l_mine = _forced(mgr, mine, prompts, t_ref)
+    l32 = _forced(m32, ref32, prompts, t_ref)
+    err_mine = (l_mine - l32).abs().max().item()
+    err_ref = (l_ref - l32).abs().max().item()
+    top2 = torch.topk(l32, 2, dim=-1).values
+    margin = top2[..., 0] - top2[..., 1]
+    a_mine, a_ref, a32 = l_mine.argmax(-1), l_ref.argmax(-1), l32.argmax(-1)
+    differ = a_mine != a_ref
+    print(f"awake quickstart: max|B200 - fp32| = {err_mine:.3e}, max|ref bf16 - fp32| = {err_ref:.3e}; "
+          f"greedy picks: B200 != ref at {int(differ.sum())}/{differ.numel()}, "
+          f"B200 != fp32 at {int((a_mine != a32).sum())}, ref != fp32 at {int((a_ref != a32).sum())}")
+    assert err_mine <= LOGIT_TOL
+    assert err_mine <= 1.25 * err_ref + 1e-3
+    assert bool((margin[differ] <= 2 * (err_mine + err_ref)).all())
+    assert int((a_mine != a32).sum()) <= int((a_ref != a32).sum())
 
 
 def _attention_flavors():

@@ -10,13 +10,12 @@ Public surface (mirrors modelcore's names for this path):
   ops                       the torch-facing wrappers of the C ABI (include/mcb200.h)
 
 The kernels live in libmcb200.so next to this file (build: `python -m modelcore_b200.build`).
-Importing this package loads it and fails loudly if it is missing.
+The library is loaded on first use (any op, any KVCache) and its absence is an error: nothing
+here has a CPU or pure-Python fallback.
 """
 from . import _native, ops
 from .cache import KVCache
 from .flash_attn import flash_attn, flash_attn_with_kvcache
-
-_native.load()
 
 __all__ = ["KVCache", "flash_attn", "flash_attn_with_kvcache", "ModelManager", "install",
            "uninstall", "GraphDecoder", "ops"]

@@ -17,7 +17,7 @@ Attention use it unchanged.  Differences, all on the host side:
 import numpy as np
 import torch
 
-from . import ops
+from . import _native, ops
 
 CACHE_ALIGN = 256
 
@@ -31,6 +31,7 @@ def _aligned_zeros(shape, device):
 
 class KVCache:
     def __init__(self, batch_size, n_kv_head, seq_len, head_dim, num_kv_slots, device, dtype):
+        _native.load()
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError(f"modelcore_b200.KVCache lives on a CUDA device, got {device}")

@@ -174,8 +174,10 @@ def _build_decoder(rank, world, steps_needed):
     mgr = modelcore_b200.ModelManager()
     model = mgr.create_model(workloads.quickstart_config(), device=torch.device("cuda"), seed=0)
     model = model.to(torch.bfloat16).eval()
+    from modelcore_b200.sharding import contiguous_rows
     all_prompts = workloads.prompts(ROWS_PER_GPU * world, PROMPT_LEN, seed=1)
-    mine = all_prompts[rank * ROWS_PER_GPU:(rank + 1) * ROWS_PER_GPU].tolist()
+    begin, end = contiguous_rows(ROWS_PER_GPU * world, world, rank)
+    mine = all_prompts[begin:end].tolist()
     with torch.inference_mode():
         dec = mgr.new_decoder(model, mine, max_tokens=DECODE_LEN, cuda_graph=True)
     assert steps_needed <= DECODE_LEN, "more decode steps than the configured 512"
@@ -359,9 +361,8 @@ def run_b200(args):
         with torch.inference_mode():
             dec.greedy_steps(args.steps, first_tokens=None, out=tokens)
             if world > 1:
-                import torch.distributed as dist
-                gathered = torch.empty((B * world, args.steps), dtype=torch.long, device="cuda")
-                dist.all_gather_into_tensor(gathered, tokens)
+                from modelcore_b200.sharding import gather_tokens
+                gather_tokens(tokens)
         e1.record(stream)
         torch.cuda.synchronize()
         clocks.mark("end")

@@ -143,6 +143,29 @@ size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
 
 int mcb_decode_attn(const mcb_attn_args* args, void* stream);
 
+/* mcb_decode_attn for callers that cannot allocate device memory.  No counterpart in the
+ * reference: modelcore allocates through torch and has no such caller.
+ *
+ * Some hosts hand this library only the tensors they already own -- a serving engine that has
+ * carved all of HBM into its own pools up front, or a foreign-language binding with no device
+ * allocator at hand -- and cannot produce the workspace mcb_decode_attn asks for; a cudaMalloc
+ * of their own inside a decode step would also synchronise the device.  This entry point keeps
+ * the split partials in a static device array compiled into the library instead:
+ * MCB_NOALLOC_SCRATCH_BYTES (8 MiB) per GPU, held by every GPU that loads the library until the
+ * process exits.  args->workspace and args->workspace_bytes are ignored; a shape whose split
+ * plan needs more scratch than that (mcb_decode_attn_workspace_size() > the limit) is rejected
+ * with MCB_ERR_WORKSPACE before anything is enqueued -- lower num_splits, or use mcb_decode_attn.
+ * Nothing is allocated: no cudaMalloc, no cudaFree, no allocating library call.
+ *
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current, which may load the library's kernels); make that first call before any
+ * stream capture on the device.  Every call on a device shares the one array, so calls whose
+ * kernels can overlap on the GPU (other streams, other host threads) race on it: serialise them
+ * on one stream.  No part of the array needs to start at zero: every partial a call reads is
+ * written earlier in the same call. */
+#define MCB_NOALLOC_SCRATCH_BYTES (8u << 20)
+int mcb_decode_attn_noalloc(const mcb_attn_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
  * overflow) or a timed-out pipeline wait sets a device error word and skips the access.

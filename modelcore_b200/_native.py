@@ -37,6 +37,9 @@ DEVICE_ERRORS = {
 
 ABI_VERSION = 1
 
+# Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 8 << 20
+
 # Every entry point include/mcb200.h declares.
 EXPORTED_SYMBOLS = (
     "mcb_abi_version",
@@ -46,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "mcb_kv_advance",
     "mcb_decode_attn_workspace_size",
     "mcb_decode_attn",
+    "mcb_decode_attn_noalloc",
     "mcb_device_error",
     "mcb_launch_count",
 )
@@ -123,6 +127,8 @@ def _declare(lib):
     lib.mcb_decode_attn_workspace_size.argtypes = [P(AttnArgs)]
     lib.mcb_decode_attn.restype = ctypes.c_int
     lib.mcb_decode_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]
+    lib.mcb_decode_attn_noalloc.restype = ctypes.c_int
+    lib.mcb_decode_attn_noalloc.argtypes = [P(AttnArgs), ctypes.c_void_p]
     lib.mcb_device_error.restype = ctypes.c_int
     lib.mcb_device_error.argtypes = [P(ctypes.c_int32), ctypes.c_void_p]
     lib.mcb_launch_count.restype = ctypes.c_uint64
@@ -147,6 +153,10 @@ def load():
                 f"libmcb200.so not found at {path}: build it with `python -m modelcore_b200.build` "
                 "(the KV decode path has no fallback without it)")
         lib = ctypes.CDLL(path)
+        missing = [n for n in EXPORTED_SYMBOLS if not hasattr(lib, n)]
+        if missing:
+            raise RuntimeError(f"{path} is stale (missing {', '.join(missing)}); rebuild it with "
+                               "`python -m modelcore_b200.build`")
         _declare(lib)
         ver = lib.mcb_abi_version()
         if ver != ABI_VERSION:

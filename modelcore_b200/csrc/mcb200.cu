@@ -386,6 +386,105 @@ int mcb_decode_attn(const mcb_attn_args* a, void* stream) {
   return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: head_dim %d", a->D);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free decode attention (mcb_decode_attn_noalloc): the split partials live in this
+// file-scope device array instead of a caller-provided workspace.  In host code the name
+// g_noalloc_scratch is only a host-side stand-in; its device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MCB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+int noalloc_scratch_ptr(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "mcb_decode_attn_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn_noalloc: device ordinal %d >= 64", dev);
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "mcb_decode_attn_noalloc: cudaGetSymbolAddress(scratch)");
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return MCB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mcb_decode_attn_noalloc(const mcb_attn_args* a, void* stream) {
+  AttnPlan pl;
+  int rc = plan_attn(a, &pl);
+  if (rc != MCB_OK) return rc;
+  if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->out == nullptr ||
+      a->cache_seqlens == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_decode_attn_noalloc: NULL pointer argument");
+  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || !aligned(a->q, 16) ||
+      !aligned(a->out, 16))
+    return fail(MCB_ERR_ALIGNMENT,
+                "mcb_decode_attn_noalloc: q, out and cache pointers must be 16-byte aligned");
+  for (int i = 0; i < 3; ++i)
+    if (a->q_stride[i] < 0 || (a->q_stride[i] % 8) != 0)
+      return fail(MCB_ERR_ALIGNMENT,
+                  "mcb_decode_attn_noalloc: q strides must be non-negative multiples of 8 elements");
+  if (pl.ws_bytes > MCB_NOALLOC_SCRATCH_BYTES)
+    return fail(MCB_ERR_WORKSPACE,
+                "mcb_decode_attn_noalloc: this shape's %d-way split needs %zu bytes of scratch, more "
+                "than the %u-byte static scratch; pass a smaller num_splits or use mcb_decode_attn "
+                "with a workspace",
+                pl.nsplit, pl.ws_bytes, MCB_NOALLOC_SCRATCH_BYTES);
+  if (a->B == 0 || a->T == 0) return MCB_OK;
+  void* scratch = nullptr;
+  if (pl.ws_bytes > 0) {
+    rc = noalloc_scratch_ptr(&scratch);
+    if (rc != MCB_OK) return rc;
+  }
+
+  CUtensorMap km, vm;
+  rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  if (rc != MCB_OK) return rc;
+  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  if (rc != MCB_OK) return rc;
+
+  mcb::AttnParams p;
+  p.q = static_cast<const uint16_t*>(a->q);
+  for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
+  p.cache_seqlens = a->cache_seqlens;
+  p.out = static_cast<uint16_t*>(a->out);
+  p.part_o = pl.nsplit > 1 ? static_cast<float*>(scratch) : nullptr;
+  p.part_lse = pl.nsplit > 1
+                   ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + pl.part_o_bytes)
+                   : nullptr;
+  p.B = a->B;
+  p.T = a->T;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.G = a->Hq / a->Hkv;
+  p.Tmax = a->Tmax;
+  p.window = a->window;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.nsplit = pl.nsplit;
+  p.tiles_per_split = pl.tps;
+  p.nqb = pl.nqb;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (a->D) {
+    case 16: return pl.nqt == 1 ? launch_attn_variant<16, 1>(pl, km, vm, p, st) : launch_attn_variant<16, 2>(pl, km, vm, p, st);
+    case 32: return pl.nqt == 1 ? launch_attn_variant<32, 1>(pl, km, vm, p, st) : launch_attn_variant<32, 2>(pl, km, vm, p, st);
+    case 64: return pl.nqt == 1 ? launch_attn_variant<64, 1>(pl, km, vm, p, st) : launch_attn_variant<64, 2>(pl, km, vm, p, st);
+    case 128: return pl.nqt == 1 ? launch_attn_variant<128, 1>(pl, km, vm, p, st) : launch_attn_variant<128, 2>(pl, km, vm, p, st);
+    case 256: return launch_attn_variant<256, 1>(pl, km, vm, p, st);
+  }
+  return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn_noalloc: head_dim %d", a->D);
+}
+
 int mcb_device_error(int32_t* code, void* stream) {
   if (code == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_device_error: code is NULL");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

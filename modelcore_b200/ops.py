@@ -226,6 +226,25 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     return out
 
 
+def decode_attn_noalloc(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
+                        num_splits=0, out=None):
+    """decode_attn through mcb_decode_attn_noalloc: for callers that cannot allocate device
+    memory (a host whose HBM is all carved into its own pools, or a binding without a device
+    allocator).  The split partials go to the library's static 8 MiB per-GPU scratch instead of a
+    workspace; shapes whose split plan needs more raise McbError(MCB_ERR_WORKSPACE).  Calls that
+    can overlap on the GPU share that scratch and race: keep them on one stream.  `out` must be
+    given by such a caller; when it is None this wrapper allocates it (torch), for tests."""
+    if out is None:
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    else:
+        _need("out", out, 4)
+        if out.shape != q.shape or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous tensor shaped like q")
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out)
+    check(_native.load().mcb_decode_attn_noalloc(ctypes.byref(args), _stream(q)))
+    return out
+
+
 def device_error(device=None):
     """Reads and clears the library's device error word (synchronises the current stream).
     Returns (code, description)."""

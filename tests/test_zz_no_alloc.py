@@ -1,0 +1,81 @@
+"""mcb_decode_attn_noalloc: decode attention for callers that cannot allocate device memory.
+
+A host that owns all of its device memory up front (a serving engine with pre-carved pools) or a
+binding with no device allocator cannot hand mcb_decode_attn a workspace; this entry point keeps
+the split partials in the library's static 8 MiB per-GPU scratch instead.  These tests call it
+through the C ABI twice in a row, on new inputs each time (the scratch keeps the previous call's
+contents), and compare each result with the existing entry point's (mcb_decode_attn with a
+workspace) within the attention tolerance of the other tests.  The file sorts last so a run that
+stops at the first failure has already run every other test.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from modelcore_b200 import _native, ops
+
+pytestmark = pytest.mark.gpu
+
+ATTN_TOL = 2e-2  # max-abs, bf16 output, as in test_gpu_kernels.py
+
+
+def _inputs(seed, B, Hq, Hkv, D, Tmax):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    lens = np.random.default_rng(seed).integers(0, Tmax, size=B)
+    q = torch.randn(B, 1, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    return q, kc, vc, torch.from_numpy(lens).to(torch.int32).cuda()
+
+
+def _call_noalloc(q, kc, vc, sl, out, window, num_splits):
+    """One call of the new entry point through the C ABI (ctypes, raw pointers, current stream)."""
+    args = ops._attn_args(q, kc, vc, sl, window, None, num_splits, out)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return _native.load().mcb_decode_attn_noalloc(ctypes.byref(args), stream)
+
+
+SHAPES = [
+    # B, Hq, Hkv, D, Tmax, window, num_splits (0 = automatic)
+    (8, 32, 8, 128, 8192, -1, 0),
+    (4, 12, 12, 64, 3000, 100, 3),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto-split", "mha-d64-window-3-split"])
+def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape):
+    B, Hq, Hkv, D, Tmax, window, splits = shape
+    for call, seed in enumerate((11, 12)):
+        q, kc, vc, sl = _inputs(seed, B, Hq, Hkv, D, Tmax)
+        need = ops.decode_attn_workspace_bytes(q, kc, vc, sl, window=window, num_splits=splits)
+        assert 0 < need <= _native.NOALLOC_SCRATCH_BYTES  # the split path, i.e. the scratch, is used
+        expected = ops.decode_attn(q, kc, vc, sl, window=window, num_splits=splits)
+        out = torch.full_like(q, float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        st = _call_noalloc(q, kc, vc, sl, out, window, splits)
+        assert st == _native.MCB_OK, _native.last_error()
+        torch.cuda.synchronize()
+        if call == 1:  # after the first call has set up the scratch address on this device
+            assert torch.cuda.mem_get_info()[0] >= free_before - (2 << 20)
+        err = (out.float() - expected.float()).abs().max().item()
+        assert err <= ATTN_TOL, (call, err)
+        assert ops.device_error()[0] == 0
+
+
+def test_noalloc_rejects_a_split_plan_larger_than_its_scratch():
+    B, Hq, Hkv, D, Tmax = 64, 32, 8, 128, 4096
+    q, kc, vc, sl = _inputs(3, B, Hq, Hkv, D, Tmax)
+    assert ops.decode_attn_workspace_bytes(q, kc, vc, sl, num_splits=16) > _native.NOALLOC_SCRATCH_BYTES
+    out = torch.zeros_like(q)
+    st = _call_noalloc(q, kc, vc, sl, out, -1, 16)
+    assert st == _native.MCB_ERR_WORKSPACE
+    assert "static scratch" in _native.last_error()
+    torch.cuda.synchronize()
+    assert out.abs().sum().item() == 0  # nothing was enqueued
+    # with fewer splits the same shape fits and matches
+    out2 = ops.decode_attn_noalloc(q, kc, vc, sl, num_splits=2)
+    ref = ops.decode_attn(q, kc, vc, sl, num_splits=2)
+    assert (out2.float() - ref.float()).abs().max().item() <= ATTN_TOL

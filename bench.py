@@ -242,6 +242,7 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
             keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
             nbytes = keys * 2 * Hkv * D * 2
             t_att, t_step = [], []
+            torch.cuda.nvtx.range_push(f"sweep_b{B}_w{w}")
             for it in range(6):
                 flush.zero_()
                 a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
@@ -254,6 +255,7 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
                 if it:
                     t_att.append(a1.elapsed_time(a2))
                     t_step.append(a0.elapsed_time(a2))
+            torch.cuda.nvtx.range_pop()
             ta, ts = statistics.median(t_att), statistics.median(t_step)
             gbs = nbytes / (ta * 1e-3) / 1e9
             rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
@@ -332,6 +334,15 @@ def _config(n):
             "l2": "inputs larger than L2: 1.2-2.4 GB of KV + 0.2 GB of weights per step per GPU"}
 
 
+def run_sweep_only(args):
+    """--sweep-only: the config-5 sweep alone (used for small ncu captures)."""
+    import torch
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    peak, _ = _peaks()
+    rows = _kv_read_sweep(peak, batches=tuple(args.sweep_batches), windows=tuple(args.sweep_windows))
+    print(json.dumps({"kv_read_sweep": rows, "peak_gbs": peak}), flush=True)
+
+
 def run_b200(args):
     import torch
     _ensure_modelcore()
@@ -357,6 +368,7 @@ def run_b200(args):
     with ClockSampler(f"GPU-{gpu_uuid}" if gpu_uuid else local) as clocks:
         time.sleep(0.3)  # let the sampler start before the timed region
         clocks.mark("start")
+        torch.cuda.nvtx.range_push("timed_decode")
         e0.record(stream)
         with torch.inference_mode():
             dec.greedy_steps(args.steps, first_tokens=None, out=tokens)
@@ -364,6 +376,7 @@ def run_b200(args):
                 from modelcore_b200.sharding import gather_tokens
                 gather_tokens(tokens)
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         clocks.mark("end")
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
@@ -392,7 +405,8 @@ def run_b200(args):
     roof = _attention_roofline(dec, peak)
     sweep = None
     if world == 1 and not args.no_sweep:
-        sweep = _kv_read_sweep(peak)
+        sweep = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
+                               windows=tuple(args.sweep_windows))
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
@@ -440,11 +454,16 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")
+    ap.add_argument("--sweep-batches", type=int, nargs="+", default=[1, 8, 64, 256, 512])
+    ap.add_argument("--sweep-windows", type=int, nargs="+", default=[-1, 4096])
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep_only:
+        run_sweep_only(args)
     else:
         run_b200(args)
         import torch.distributed as dist

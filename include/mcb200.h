@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 1
+#define MCB_ABI_VERSION 2
 
 typedef enum {
   MCB_OK = 0,
@@ -112,7 +112,7 @@ int mcb_kv_copy_rows(const mcb_copy_args* args, void* stream);
 int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
- * Piece 3: decode attention over the cache (split-K flash-decode).
+ * Piece 3: decode attention over the cache (flash-decode on the tensor cores).
  * Replaces the attention half of flash_attn_with_kvcache's SDPA path,
  * modelcore/kernels/flash_attn.py:348-366 with _sdpa_attention (:203-244) and
  * _ragged_decode_mask (:246-264):
@@ -120,8 +120,14 @@ int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
  * over keys c with c <= L_b + t and (window < 0 or L_b + t - c <= window), L_b = cache_seqlens[b]
  * and G = Hq / Hkv (SDPA's enable_gqa mapping q head h -> kv head h / G).  The new tokens'
  * keys/values must already be in the cache (mcb_kv_append_rope with WRITE_KV).
- * Keys are streamed once per (row, kv head, split) by TMA into a shared-memory ring that the
- * G grouped query heads share; partial results of the splits are merged by a second kernel.
+ * A row group (one row's G grouped q heads of one kv head) shares every K/V tile, streamed by
+ * TMA through a shared-memory ring.  Two launch plans, same results up to fp32 summation order:
+ *  - persistent: all row groups' key tiles form one sequence that a resident grid divides
+ *    evenly on the device, from cache_seqlens (no host knowledge of the lengths); row groups
+ *    cut between CTAs are merged by the last CTA to finish them.  Chosen for rows that can hold
+ *    more than 2048 keys (min(Tmax, window + T)).
+ *  - split: one CTA per row group and key split, partials merged by a second kernel when split.
+ *    Chosen for shorter rows, where the persistent plan's fixed costs do not pay off.
  * ------------------------------------------------------------------------------------------- */
 typedef struct {
   const void* q;              /* (B,T,Hq,D) bf16                                            */
@@ -133,13 +139,29 @@ typedef struct {
   int32_t B, T, Hq, Hkv, D, Tmax;
   int32_t window;             /* left window; < 0 = full context                            */
   float softmax_scale;        /* 1/sqrt(D) in modelcore (SDPA default)                      */
-  int32_t num_splits;         /* 0 = choose from the shape                                  */
-  void* workspace;            /* device scratch of mcb_decode_attn_workspace_size() bytes   */
+  int32_t num_ctas;           /* 0: choose the plan; > 0: persistent grid of that many CTAs
+                                 (rounded down to whole groups of Hkv); < 0: split plan with
+                                 -num_ctas key splits per row group                         */
+  void* workspace;            /* partials: mcb_decode_attn_workspace_size() bytes, no
+                                 initialisation needed                                      */
   size_t workspace_bytes;
+  int32_t* counters;          /* mcb_decode_attn_counter_count() int32 arrival counters, one
+                                 per row group: zero before the first call, and every
+                                 completed call leaves the ones it used at zero again, so one
+                                 array serves every call of a stream (of any shape that fits)*/
+  size_t counter_count;
 } mcb_attn_args;
 
-/* Bytes of workspace mcb_decode_attn needs for this shape (0 when no split is used). */
+/* Bytes of workspace mcb_decode_attn needs for its partial results (0: none): persistent plan,
+ * two slots per CTA, ctas * 2 * rows * (D + 1) * 4; split plan with s > 1 splits,
+ * B * T * Hq * s * (D + 1) * 4; in two 256-byte-rounded parts (rows = 8 or 16).  It does not
+ * depend on the row lengths.  Calls that can overlap on the GPU need separate workspaces and
+ * counter arrays. */
 size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
+
+/* int32 arrival counters mcb_decode_attn needs: one per row group,
+ * B * ceil(T * Hq / Hkv / rows) * Hkv, for the persistent plan; 0 for the split plan. */
+size_t mcb_decode_attn_counter_count(const mcb_attn_args* args);
 
 int mcb_decode_attn(const mcb_attn_args* args, void* stream);
 
@@ -150,19 +172,21 @@ int mcb_decode_attn(const mcb_attn_args* args, void* stream);
  * carved all of HBM into its own pools up front, or a foreign-language binding with no device
  * allocator at hand -- and cannot produce the workspace mcb_decode_attn asks for; a cudaMalloc
  * of their own inside a decode step would also synchronise the device.  This entry point keeps
- * the split partials in a static device array compiled into the library instead:
+ * the partials and arrival counters in a static device array compiled into the library instead:
  * MCB_NOALLOC_SCRATCH_BYTES (8 MiB) per GPU, held by every GPU that loads the library until the
- * process exits.  args->workspace and args->workspace_bytes are ignored; a shape whose split
- * plan needs more scratch than that (mcb_decode_attn_workspace_size() > the limit) is rejected
- * with MCB_ERR_WORKSPACE before anything is enqueued -- lower num_splits, or use mcb_decode_attn.
+ * process exits.  args->workspace, workspace_bytes, counters and counter_count are ignored; a
+ * call whose partials and counters need more than that (workspace_size + 4 * counter_count,
+ * rounded to 256 bytes, > the limit) is rejected with MCB_ERR_WORKSPACE before anything is
+ * enqueued -- lower num_ctas, or use mcb_decode_attn.
  * Nothing is allocated: no cudaMalloc, no cudaFree, no allocating library call.
  *
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with
  * that device current, which may load the library's kernels); make that first call before any
  * stream capture on the device.  Every call on a device shares the one array, so calls whose
  * kernels can overlap on the GPU (other streams, other host threads) race on it: serialise them
- * on one stream.  No part of the array needs to start at zero: every partial a call reads is
- * written earlier in the same call. */
+ * on one stream.  Of the array only the arrival counters must start at zero, and each call
+ * clears the ones it uses first (cudaMemsetAsync on the caller's stream, no allocation); every
+ * partial a call reads is written earlier in the same call. */
 #define MCB_NOALLOC_SCRATCH_BYTES (8u << 20)
 int mcb_decode_attn_noalloc(const mcb_attn_args* args, void* stream);
 

@@ -35,7 +35,7 @@ DEVICE_ERRORS = {
     3: "pipeline wait timed out",
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "mcb_kv_copy_rows",
     "mcb_kv_advance",
     "mcb_decode_attn_workspace_size",
+    "mcb_decode_attn_counter_count",
     "mcb_decode_attn",
     "mcb_decode_attn_noalloc",
     "mcb_device_error",
@@ -94,8 +95,9 @@ class AttnArgs(ctypes.Structure):
         ("Hkv", ctypes.c_int32), ("D", ctypes.c_int32), ("Tmax", ctypes.c_int32),
         ("window", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
-        ("num_splits", ctypes.c_int32),
+        ("num_ctas", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("counters", ctypes.c_void_p), ("counter_count", ctypes.c_size_t),
     ]
 
 
@@ -125,6 +127,8 @@ def _declare(lib):
     lib.mcb_kv_advance.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
     lib.mcb_decode_attn_workspace_size.restype = ctypes.c_size_t
     lib.mcb_decode_attn_workspace_size.argtypes = [P(AttnArgs)]
+    lib.mcb_decode_attn_counter_count.restype = ctypes.c_size_t
+    lib.mcb_decode_attn_counter_count.argtypes = [P(AttnArgs)]
     lib.mcb_decode_attn.restype = ctypes.c_int
     lib.mcb_decode_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]
     lib.mcb_decode_attn_noalloc.restype = ctypes.c_int

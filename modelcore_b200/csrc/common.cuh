@@ -97,6 +97,41 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Like mbar_wait, but also gives up at once when another warp of the CTA has already timed out
+// (*abort != 0), and raises *abort itself on a timeout: after the first timeout every wait of
+// the CTA returns immediately, so the CTA drains in bounded time.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*abort) return false;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(kErrWaitTimeout);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// atomicAdd with acquire-release semantics at GPU scope: releases the stores the calling CTA
+// ordered before it (through a barrier) and acquires those of earlier releasers.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15; 0 is
+// __syncthreads).
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // TMA: 4-D tiled bulk tensor load global -> shared, completion signalled on an mbarrier as a
 // transaction count.  No multicast: every CTA fetches its own tiles.  `policy` is an L2 cache

@@ -1,27 +1,37 @@
-// Piece 3: decode attention over the KV cache -- split-K flash-decode with GQA grouping, a
+// Piece 3: decode attention over the KV cache -- a persistent flash-decode with GQA grouping, a
 // per-row sliding window and per-row (right-ragged) positions.
 //
 // Semantics (modelcore/kernels/flash_attn.py:246-264 and :348-366): query token t of row b sits
 // at q_pos = L_b + t (L_b = cache_seqlens[b]) and sees key c iff c <= q_pos and
 // (window < 0 or q_pos - c <= window); softmax scale 1/sqrt(D); q head h reads kv head h / G.
 //
-// Work decomposition.  One CTA per (row b, kv head, query block, split).  A query block is up to
-// 8*NQT flattened query rows r = t*G + g of one kv head (for decode, T = 1: the G grouped heads).
-// The CTA's key range [lo, hi] (the union over its rows) is cut into TK-key tiles; split s takes
-// tiles [s*tps, (s+1)*tps).  A producer warp streams K and V tiles with TMA (4-D tensor maps over
-// the (B, Tmax, Hkv, D) slot, 128-byte swizzled panels of 64 columns, no multicast) into a
-// STAGES-deep shared-memory ring; four consumer warps each take KPW keys of every tile.
+// Work decomposition: a flat tile space, balanced on the device.  An *entry* is (row b, query
+// block qb): up to ROWS = 8*NQT flattened query rows r = t*G + g per kv head (for decode, T = 1,
+// the G grouped q heads), which share every K/V tile of that head, so each K/V byte is fetched
+// once for all of them.  An entry's key range -- the union of its rows' visible ranges -- is cut
+// into TK-key tiles; all entries' tiles, in entry order, form one sequence of S tiles.  The grid
+// is NG groups of Hkv CTAs: CTA c serves kv head c % Hkv over the tiles
+// [g*S/NG, (g+1)*S/NG) of group g = c / Hkv.  The Hkv CTAs of a group read the same positions
+// of all kv heads together (whole contiguous (position, head, dim) blocks for DRAM), and every
+// CTA computes S itself from cache_seqlens (no host sync, so a CUDA graph stays valid as rows
+// grow): the work is balanced to within one tile whatever the batch, lengths or windows.  A row
+// group (entry, kv head) that a CTA holds entirely is written as bf16 output.  One cut by a group
+// boundary leaves a partial (O/l, log2-sum-exp) in each contributing CTA's slot 0 (its first
+// entry) or slot 1 (its last); each contributor then bumps the row group's arrival counter, and
+// the contributor that arrives last merges all the partials into the output and resets the
+// counter to zero -- no CTA ever waits for another, and no second kernel is launched.
 //
-// Per consumer warp the contraction runs on the tensor cores with keys on the M side (the K tile
-// is the A operand straight from shared memory) and the query rows on the N side:
+// Per CTA a producer warp streams the K and V tiles of its whole tile range with TMA (4-D tensor
+// maps over the (B, Tmax, Hkv, D) slot, 128-byte swizzled panels of 64 columns, no multicast) into
+// a STAGES-deep shared-memory ring, never draining it between row groups; four consumer warps
+// each take KPW keys of every tile.  Per consumer warp the contraction runs on the tensor cores
+// with keys on the M side (the K tile is the A operand straight from shared memory) and the
+// query rows on the N side:
 //   S^T(16 keys x 8 rows)  = K(16 x D) . Q^T(D x 8)        mma.m16n8k16, Q^T fragments in registers
 //   O^T(D x 8 rows)       += V^T(D x 16 keys) . P^T(16 x 8)  V^T via ldmatrix.trans, P^T from the S^T
 //                                                            accumulators via movmatrix.trans
-// so each grouped query head costs one of 8 accumulator columns (G = 4 fills half of them) and
-// the K/V tile is read from shared memory once for all of them.  Online softmax runs in fp32
-// per warp; the four warps are merged through shared memory at the end.  With one split the CTA
-// writes the bf16 output; otherwise it writes (O / l, log2-sum-exp) partials that
-// decode_attn_combine_kernel merges.
+// Online softmax in fp32 per warp; the four warps merge through a separate shared buffer after
+// each row group (named barrier over the consumer warps only, so the producer keeps streaming).
 #pragma once
 
 #include <math_constants.h>
@@ -35,11 +45,15 @@ struct AttnParams {
   long long qs[3];
   const int32_t* cache_seqlens;
   uint16_t* out;
-  float* part_o;    // [((b*T + t)*Hq + h)*nsplit + s][D]
-  float* part_lse;  // [((b*T + t)*Hq + h)*nsplit + s]
+  float* part_o;    // [(cta*2 + slot)*ROWS + n][D]
+  float* part_lse;  // [(cta*2 + slot)*ROWS + n]
+  int* counters;     // [entry * Hkv + kv head] arrivals; zero on entry, left zero on exit
   int B, T, Hq, Hkv, G, Tmax, window;
   float scale_log2;  // softmax_scale * log2(e)
-  int nsplit, tiles_per_split, nqb;
+  int nqb;           // query blocks per row
+  int n_entries;     // B * nqb
+  int grid;          // persistent CTAs = ngroups * Hkv
+  int ngroups;       // CTA groups; CTA c serves kv head c % Hkv of group c / Hkv
 };
 
 constexpr int kAttnConsumerWarps = 4;
@@ -47,8 +61,8 @@ constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
 
 template <int D, int NQT, int KPW, int STAGES>
 struct AttnConfig {
-  static constexpr int kRows = 8 * NQT;                      // query rows per CTA
-  static constexpr int TK = KPW * kAttnConsumerWarps;        // keys per stage
+  static constexpr int kRows = 8 * NQT;                      // query rows per row group
+  static constexpr int TK = KPW * kAttnConsumerWarps;        // keys per tile
   static constexpr int PANEL = D < 64 ? D : 64;              // columns per swizzled panel
   static constexpr int NPANEL = D / PANEL;
   static constexpr int ROW_BYTES = PANEL * 2;                // 32, 64 or 128
@@ -58,16 +72,17 @@ struct AttnConfig {
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
-  static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
-  static constexpr int BODY_BYTES = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
-  // barriers (full + empty per stage) then per-warp row statistics
-  static constexpr int BAR_OFFSET = BODY_BYTES;
+  static constexpr int MERGE_OFFSET = RING_BYTES;
+  static constexpr int MERGE_BYTES = 2 * kAttnConsumerWarps * kRows * OPITCH * 4;  // two copies
+  static constexpr int BAR_OFFSET = MERGE_OFFSET + MERGE_BYTES;
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
-  static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
-  static constexpr int SMEM_BYTES = STAT_OFFSET + STAT_BYTES + 1024;  // + alignment slack
+  static constexpr int STAT_BYTES = 2 * 2 * kAttnConsumerWarps * kRows * 4;  // (m, l) x two copies
+  static constexpr int CTL_OFFSET = STAT_OFFSET + STAT_BYTES;  // abort flag, start state, last flag
+  static constexpr int CTL_BYTES = 64;
+  static constexpr int SMEM_BYTES = CTL_OFFSET + CTL_BYTES + 1024;  // + alignment slack
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
-  static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
+  static_assert(RING_BYTES % 1024 == 0, "ring alignment");
 };
 
 // Byte offset of the 16-byte chunk `chunk` (0 .. ROW_BYTES/16) of key row `key` in a panel,
@@ -79,124 +94,228 @@ __device__ __forceinline__ uint32_t swz(int key, int chunk) {
   return off ^ (((off >> 7) & SWZ_MASK) << 4);
 }
 
+// One (row b, query block qb) entry: its query rows, visible key range and tile count.
+struct Entry {
+  int b, r0, r1, L, lo, hi, kb, n;
+};
+
+template <int ROWS, int TK>
+__device__ __forceinline__ Entry make_entry(const AttnParams& p, int e, int L) {
+  Entry x;
+  x.b = e / p.nqb;
+  const int qb = e - x.b * p.nqb;
+  x.r0 = qb * ROWS;
+  x.r1 = min(x.r0 + ROWS, p.T * p.G);
+  const int t_first = x.r0 / p.G;
+  const int t_last = (x.r1 - 1) / p.G;
+  x.L = L;
+  x.hi = min(max(L + t_last, 0), p.Tmax - 1);  // out-of-range L is reported by the scan
+  x.lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
+  x.kb = (min(x.lo, x.hi) / TK) * TK;
+  x.n = (x.hi - x.kb) / TK + 1;
+  return x;
+}
+
+__device__ __forceinline__ long long range_begin(long long c, long long total, int grid) {
+  return c * total / grid;
+}
+
+// The group whose range [range_begin(g), range_begin(g + 1)) holds tile t.
+__device__ __forceinline__ int tile_owner(long long t, long long total, int ngroups) {
+  return static_cast<int>(((t + 1) * ngroups - 1) / total);
+}
+
+// Walk position through the tile space.
+struct Walk {
+  int e, kvh, local;
+  long long t;
+  Entry ent;
+};
+
+template <int ROWS, int TK>
+__device__ __forceinline__ void walk_next_group(const AttnParams& p, Walk& w) {
+  w.local = 0;
+  if (++w.e < p.n_entries) w.ent = make_entry<ROWS, TK>(p, w.e, p.cache_seqlens[w.e / p.nqb]);
+}
+
+// Warp-cooperative start of a CTA: the total tile count S and the entry holding the first tile
+// of the CTA's group.  Writes {S, e, kvh, local} to ctl[1..4] (smem).
+template <int ROWS, int TK>
+__device__ void locate_start(const AttnParams& p, int* ctl) {
+  const int lane = threadIdx.x & 31;
+  const int grp = blockIdx.x / p.Hkv;
+  long long total = 0;
+#pragma unroll 4
+  for (int base = 0; base < p.n_entries; base += 32) {
+    const int e = base + lane;
+    if (e < p.n_entries) {
+      const int L = p.cache_seqlens[e / p.nqb];
+      const Entry x = make_entry<ROWS, TK>(p, e, L);
+      if (L < 0 || L + (x.r1 - 1) / p.G >= p.Tmax) record_error(kErrPositionBeyondCache);
+      total += x.n;
+    }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) total += __shfl_xor_sync(0xffffffffu, total, m);
+  const long long begin = range_begin(grp, total, p.ngroups);
+  const long long end = range_begin(grp + 1, total, p.ngroups);
+  int e_found = -1, local = 0;
+  if (begin < end) {
+    long long running = 0;
+    for (int base = 0; base < p.n_entries; base += 32) {
+      const int e = base + lane;
+      long long v = 0;
+      if (e < p.n_entries) v = make_entry<ROWS, TK>(p, e, p.cache_seqlens[e / p.nqb]).n;
+      long long incl = v;
+#pragma unroll
+      for (int m = 1; m < 32; m <<= 1) {
+        const long long o = __shfl_up_sync(0xffffffffu, incl, m);
+        if (lane >= m) incl += o;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, running + incl > begin);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        const long long excl = running + __shfl_sync(0xffffffffu, incl - v, src);
+        e_found = base + src;
+        local = static_cast<int>(begin - excl);
+        break;
+      }
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  if (lane == 0) {
+    const int kvh = blockIdx.x % p.Hkv;
+    ctl[1] = static_cast<int>(total);
+    ctl[2] = e_found;
+    ctl[3] = kvh;
+    ctl[4] = local;
+  }
+}
+
+// Q^T fragments (the B operand of S^T = K Q^T) of a row group: row n = j*8 + lane/4, columns
+// d = kk*16 + 2*(lane%4) + {0,1} and + 8; zeros for padding rows.
+template <int D, int NQT>
+__device__ __forceinline__ void load_q_frags(const AttnParams& p, const Entry& ent, int kvh,
+                                             uint32_t (&qf)[NQT][D / 16][2]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < NQT; ++j) {
+    const int r = ent.r0 + j * 8 + (lane >> 2);
+    const uint16_t* qrow = nullptr;
+    if (r < ent.r1) {
+      const int t = r / p.G, h = kvh * p.G + r % p.G;
+      qrow = p.q + ent.b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+    }
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int d0 = kk * 16 + 2 * (lane & 3);
+      qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+      qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+    }
+  }
+}
+
 template <int D, int NQT, int KPW, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads)
     decode_attn_kernel(const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const AttnParams p) {
   using C = AttnConfig<D, NQT, KPW, STAGES>;
+  constexpr int ROWS = C::kRows;
+  constexpr int TK = C::TK;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  float* merge = reinterpret_cast<float*>(smem + C::MERGE_OFFSET);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFFSET);
   uint64_t* empty_bar = full_bar + STAGES;
   float* stat_m = reinterpret_cast<float*>(smem + C::STAT_OFFSET);
-  float* stat_l = stat_m + kAttnConsumerWarps * C::kRows;
-  float* stat_f = stat_l + kAttnConsumerWarps * C::kRows;
+  int* ctl = reinterpret_cast<int*>(smem + C::CTL_OFFSET);  // [0] abort, [1..4] start, [5..6] last
+  volatile int* abort_flag = ctl;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // ---- which (b, kv head, query block, split) ----
-  int x = blockIdx.x;
-  const int split = x % p.nsplit;
-  x /= p.nsplit;
-  const int qb = x % p.nqb;
-  x /= p.nqb;
-  const int kvh = x % p.Hkv;
-  const int b = x / p.Hkv;
-
-  const int rows_total = p.T * p.G;
-  const int r0 = qb * C::kRows;
-  const int r1 = min(r0 + C::kRows, rows_total);
-  const int t_first = r0 / p.G;
-  const int t_last = (r1 - 1) / p.G;
-  const int L = p.cache_seqlens[b];
-  int hi = L + t_last;
-  if (hi >= p.Tmax || L < 0) {
-    if (threadIdx.x == 0) record_error(kErrPositionBeyondCache);
-    hi = min(max(hi, 0), p.Tmax - 1);
-  }
-  const int lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
-  const int kb = (min(lo, hi) / C::TK) * C::TK;
-  const int ntiles = (hi - kb) / C::TK + 1;
-  const int tile0 = split * p.tiles_per_split;
-  const int my_tiles = max(0, min(ntiles - tile0, p.tiles_per_split));
-
-  if (my_tiles == 0) {  // an empty split: its partial carries no weight
-    if (threadIdx.x < C::kRows) {
-      const int r = r0 + threadIdx.x;
-      if (r < r1) {
-        const int t = r / p.G, h = kvh * p.G + r % p.G;
-        p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] =
-            -CUDART_INF_F;
-      }
-    }
-    return;
-  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kAttnConsumerWarps);
     }
+    ctl[0] = 0;
     fence_mbarrier_init();
   }
+  if (warp == 0) locate_start<ROWS, TK>(p, ctl);
   __syncthreads();
 
+  const long long total = ctl[1];
+  if (ctl[2] < 0) return;  // no tiles for this CTA
+  const int grp = blockIdx.x / p.Hkv;
+  const long long t_end = range_begin(grp + 1, total, p.ngroups);
+  Walk w;
+  w.e = ctl[2];
+  w.kvh = ctl[3];
+  w.local = ctl[4];
+  w.t = range_begin(grp, total, p.ngroups);
+  w.ent = make_entry<ROWS, TK>(p, w.e, p.cache_seqlens[w.e / p.nqb]);
+
   if (warp == kAttnConsumerWarps) {
-    // ---------------- producer warp ----------------
+    // ---------------- producer warp: one lane streams every tile of the CTA's range ----------------
     if (lane == 0) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       const uint64_t policy = l2_policy_evict_first();
-      for (int i = 0; i < my_tiles; ++i) {
-        const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-        const int key0 = kb + (tile0 + i) * C::TK;
-        uint8_t* kdst = smem + s * C::STAGE_BYTES;
-        uint8_t* vdst = kdst + C::TILE_BYTES;
+      uint32_t g = 0;
+      while (w.t < t_end) {
+        const int seg = static_cast<int>(min(static_cast<long long>(w.ent.n - w.local), t_end - w.t));
+        for (int i = 0; i < seg; ++i, ++g) {
+          const int s = g % STAGES;
+          if (g >= STAGES && !mbar_wait_or_abort(&empty_bar[s], ((g / STAGES) - 1) & 1, abort_flag))
+            return;
+          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          const int key0 = w.ent.kb + (w.local + i) * TK;
+          uint8_t* kdst = smem + s * C::STAGE_BYTES;
+          uint8_t* vdst = kdst + C::TILE_BYTES;
 #pragma unroll
-        for (int pn = 0; pn < C::NPANEL; ++pn) {
-          tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
-                      policy);
-          tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
-                      policy);
+          for (int pn = 0; pn < C::NPANEL; ++pn) {
+            tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, w.kvh, key0,
+                        w.ent.b, policy);
+            tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, w.kvh, key0,
+                        w.ent.b, policy);
+          }
         }
+        w.t += seg;
+        w.local += seg;
+        if (w.local == w.ent.n) walk_next_group<ROWS, TK>(p, w);
       }
     }
+    return;
   }
 
-  // Per-thread softmax state for rows n = j*8 + 2*(lane%4) + e.
-  float m_run[NQT][2], l_run[NQT][2];
-  float o_acc[NQT][D / 16][4];
-  int row_hi[NQT][2], row_lo[NQT][2];
+  // ---------------- consumer warps ----------------
+  constexpr int NCH = KPW / 16;  // 16-key chunks per warp per tile
+  uint32_t g = 0;
+  bool first_segment = true;
+  int seg_index = 0;
+  uint32_t qf[NQT][D / 16][2];
+  load_q_frags<D, NQT>(p, w.ent, w.kvh, qf);
+  while (w.t < t_end) {
+    const Entry& ent = w.ent;
+    const int seg = static_cast<int>(min(static_cast<long long>(ent.n - w.local), t_end - w.t));
+    const bool complete = (w.local == 0 && seg == ent.n);
+    const int slot = first_segment ? 0 : 1;
+    const int nvalid = ent.r1 - ent.r0;
 
-  if (warp < kAttnConsumerWarps) {
-    // ---------------- consumer warps ----------------
-    // Q^T fragments (B operand): row n = j*8 + lane/4, columns d = kk*16 + 2*(lane%4) + {0,1}, +8.
-    uint32_t qf[NQT][D / 16][2];
+    float m_run[NQT][2], l_run[NQT][2];
+    float o_acc[NQT][D / 16][4];
+    int row_hi[NQT][2], row_lo[NQT][2];
 #pragma unroll
     for (int j = 0; j < NQT; ++j) {
-      const int r = r0 + j * 8 + (lane >> 2);
-      const uint16_t* qrow = nullptr;
-      if (r < r1) {
-        const int t = r / p.G, h = kvh * p.G + r % p.G;
-        qrow = p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
-      }
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int d0 = kk * 16 + 2 * (lane & 3);
-        qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
-        qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
-      }
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int rr = r0 + j * 8 + 2 * (lane & 3) + e;
+        const int rr = ent.r0 + j * 8 + 2 * (lane & 3) + e;
         m_run[j][e] = -CUDART_INF_F;
         l_run[j][e] = 0.f;
-        if (rr < r1) {
-          const int qpos = L + rr / p.G;
+        if (rr < ent.r1) {
+          const int qpos = ent.L + rr / p.G;
           row_hi[j][e] = qpos;
           row_lo[j][e] = p.window >= 0 ? qpos - p.window : 0;
         } else {
@@ -210,107 +329,125 @@ __global__ void __launch_bounds__(kAttnThreads)
         for (int c = 0; c < 4; ++c) o_acc[j][db][c] = 0.f;
     }
 
-    constexpr int NCH = KPW / 16;  // 16-key chunks per warp per stage
-    for (int i = 0; i < my_tiles; ++i) {
-      const int s = i % STAGES;
-      if (!mbar_wait(&full_bar[s], (i / STAGES) & 1)) break;
-      const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
-      const uint32_t vbase = kbase + C::TILE_BYTES;
-      const int tile_key0 = kb + (tile0 + i) * C::TK;
+    for (int i = 0; i < seg; ++i, ++g) {
+      const int s = g % STAGES;
+      const bool ready = mbar_wait_or_abort(&full_bar[s], (g / STAGES) & 1, abort_flag);
+      if (ready) {
+        const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t vbase = kbase + C::TILE_BYTES;
+        const int tile_key0 = ent.kb + (w.local + i) * TK;
 
-      float sc[NCH][NQT][4];
+        float sc[NCH][NQT][4];
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
+        for (int ch = 0; ch < NCH; ++ch) {
 #pragma unroll
-        for (int j = 0; j < NQT; ++j)
+          for (int j = 0; j < NQT; ++j)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) sc[ch][j][c] = 0.f;
-        const int krow = warp * KPW + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            for (int c = 0; c < 4; ++c) sc[ch][j][c] = 0.f;
+          const int krow = warp * KPW + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int col = kk * 16 + (lane >> 4) * 8;  // first column of this lane's 8-wide chunk
-          const uint32_t addr = kbase + (col / C::PANEL) * C::PANEL_BYTES +
-                                swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(addr, a0, a1, a2, a3);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int col = kk * 16 + (lane >> 4) * 8;
+            const uint32_t addr = kbase + (col / C::PANEL) * C::PANEL_BYTES +
+                                  swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(addr, a0, a1, a2, a3);
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) mma_16816(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
-        }
-      }
-
-      // Mask, then the online-softmax update over this warp's NCH*16 keys.
-#pragma unroll
-      for (int j = 0; j < NQT; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float mx = -CUDART_INF_F;
-#pragma unroll
-          for (int ch = 0; ch < NCH; ++ch) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const int key = tile_key0 + warp * KPW + ch * 16 + (lane >> 2) + hh * 8;
-              float& v = sc[ch][j][e + 2 * hh];
-              if (key > row_hi[j][e] || key < row_lo[j][e]) v = -CUDART_INF_F;
-              mx = fmaxf(mx, v);
-            }
-          }
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          const float m_new = fmaxf(m_run[j][e], mx);
-          float alpha = 1.f;
-          float msub = 0.f;
-          if (m_new != -CUDART_INF_F) {
-            alpha = fast_exp2((m_run[j][e] - m_new) * p.scale_log2);
-            msub = m_new * p.scale_log2;
-          }
-          m_run[j][e] = m_new;
-          float lsum = 0.f;
-#pragma unroll
-          for (int ch = 0; ch < NCH; ++ch) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              float& v = sc[ch][j][e + 2 * hh];
-              v = fast_exp2(fmaf(v, p.scale_log2, -msub));  // exp2(-inf) = 0 for masked keys
-              lsum += v;
-            }
-          }
-          l_run[j][e] = fmaf(l_run[j][e], alpha, lsum);
-#pragma unroll
-          for (int db = 0; db < D / 16; ++db) {
-            o_acc[j][db][e] *= alpha;
-            o_acc[j][db][e + 2] *= alpha;
+            for (int j = 0; j < NQT; ++j)
+              mma_16816(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
           }
         }
-      }
 
-      // O^T += V^T . P^T
-#pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        uint32_t pb[NQT][2];
+        // Mask, then the online-softmax update over this warp's NCH*16 keys.
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
-          pb[j][0] = movmatrix_trans(pack_bf16x2(sc[ch][j][0], sc[ch][j][1]));
-          pb[j][1] = movmatrix_trans(pack_bf16x2(sc[ch][j][2], sc[ch][j][3]));
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float mx = -CUDART_INF_F;
+#pragma unroll
+            for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const int key = tile_key0 + warp * KPW + ch * 16 + (lane >> 2) + hh * 8;
+                float& v = sc[ch][j][e + 2 * hh];
+                if (key > row_hi[j][e] || key < row_lo[j][e]) v = -CUDART_INF_F;
+                mx = fmaxf(mx, v);
+              }
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float m_new = fmaxf(m_run[j][e], mx);
+            float alpha = 1.f;
+            float msub = 0.f;
+            if (m_new != -CUDART_INF_F) {
+              alpha = fast_exp2((m_run[j][e] - m_new) * p.scale_log2);
+              msub = m_new * p.scale_log2;
+            }
+            m_run[j][e] = m_new;
+            float lsum = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                float& v = sc[ch][j][e + 2 * hh];
+                v = fast_exp2(fmaf(v, p.scale_log2, -msub));  // exp2(-inf) = 0 for masked keys
+                lsum += v;
+              }
+            }
+            l_run[j][e] = fmaf(l_run[j][e], alpha, lsum);
+#pragma unroll
+            for (int db = 0; db < D / 16; ++db) {
+              o_acc[j][db][e] *= alpha;
+              o_acc[j][db][e + 2] *= alpha;
+            }
+          }
         }
-        const int m = lane >> 3;
-        const int vrow = warp * KPW + ch * 16 + (lane & 7) + (m >> 1) * 8;
+
+        // O^T += V^T . P^T
 #pragma unroll
-        for (int db = 0; db < D / 16; ++db) {
-          const int col = db * 16 + (m & 1) * 8;
-          const uint32_t addr = vbase + (col / C::PANEL) * C::PANEL_BYTES +
-                                swz<C::ROW_BYTES, C::SWZ_MASK>(vrow, (col % C::PANEL) / 8);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_trans(addr, a0, a1, a2, a3);
+        for (int ch = 0; ch < NCH; ++ch) {
+          uint32_t pb[NQT][2];
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) mma_16816(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+          for (int j = 0; j < NQT; ++j) {
+            pb[j][0] = movmatrix_trans(pack_bf16x2(sc[ch][j][0], sc[ch][j][1]));
+            pb[j][1] = movmatrix_trans(pack_bf16x2(sc[ch][j][2], sc[ch][j][3]));
+          }
+          const int m = lane >> 3;
+          const int vrow = warp * KPW + ch * 16 + (lane & 7) + (m >> 1) * 8;
+#pragma unroll
+          for (int db = 0; db < D / 16; ++db) {
+            const int col = db * 16 + (m & 1) * 8;
+            const uint32_t addr = vbase + (col / C::PANEL) * C::PANEL_BYTES +
+                                  swz<C::ROW_BYTES, C::SWZ_MASK>(vrow, (col % C::PANEL) / 8);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_trans(addr, a0, a1, a2, a3);
+#pragma unroll
+            for (int j = 0; j < NQT; ++j)
+              mma_16816(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
 
-    // Full per-row sums of this warp.
+    // The next row group's Q fragments load while this one merges.
+    Walk wn = w;
+    wn.t += seg;
+    wn.local += seg;
+    if (wn.local == wn.ent.n) walk_next_group<ROWS, TK>(p, wn);
+    uint32_t qf_next[NQT][D / 16][2];
+    if (wn.t < t_end) load_q_frags<D, NQT>(p, wn.ent, wn.kvh, qf_next);
+
+    // ---- merge the four warps' partial softmax states of this row group ----
+    // The merge buffer, the statistics and the "last contributor" flag alternate between two
+    // copies by row-group parity, so one barrier per row group suffices: a warp can only write
+    // a copy again after the next row group's barrier, which every warp reaches after its reads.
+    const int par = seg_index & 1;
+    float* mbuf = merge + par * (kAttnConsumerWarps * ROWS * C::OPITCH);
+    float* st_m = stat_m + par * (2 * kAttnConsumerWarps * ROWS);
+    float* st_l = st_m + kAttnConsumerWarps * ROWS;
 #pragma unroll
     for (int j = 0; j < NQT; ++j)
 #pragma unroll
@@ -319,114 +456,136 @@ __global__ void __launch_bounds__(kAttnThreads)
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 8);
         v += __shfl_xor_sync(0xffffffffu, v, 16);
-        l_run[j][e] = v;
-      }
-  }
-
-  __syncthreads();  // the ring is drained: reuse it as the merge buffer
-
-  float* merge = reinterpret_cast<float*>(smem);
-  if (warp < kAttnConsumerWarps) {
-#pragma unroll
-    for (int j = 0; j < NQT; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
         const int n = j * 8 + 2 * (lane & 3) + e;
+        if (n >= nvalid) continue;
         if (lane < 4) {
-          stat_m[warp * C::kRows + n] = m_run[j][e];
-          stat_l[warp * C::kRows + n] = l_run[j][e];
+          st_m[warp * ROWS + n] = m_run[j][e];
+          st_l[warp * ROWS + n] = v;
         }
+        float* row = mbuf + (warp * ROWS + n) * C::OPITCH;
 #pragma unroll
         for (int db = 0; db < D / 16; ++db) {
           const int d = db * 16 + (lane >> 2);
-          float* row = merge + (warp * C::kRows + n) * C::OPITCH;
           row[d] = o_acc[j][db][e];
           row[d + 8] = o_acc[j][db][e + 2];
         }
       }
-    }
-  }
-  __syncthreads();
+    named_barrier(1, kAttnConsumerWarps * 32);
 
-  // Per row: the CTA max, each warp's weight and the total.
-  if (threadIdx.x < C::kRows) {
-    const int n = threadIdx.x;
-    float mmax = -CUDART_INF_F;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) mmax = fmaxf(mmax, stat_m[w * C::kRows + n]);
-    float ltot = 0.f;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) {
-      const float mw = stat_m[w * C::kRows + n];
-      const float f = (mw == -CUDART_INF_F) ? 0.f : fast_exp2((mw - mmax) * p.scale_log2);
-      stat_f[w * C::kRows + n] = f;
-      ltot = fmaf(stat_l[w * C::kRows + n], f, ltot);
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += kAttnConsumerWarps * 32) {
+      const int n = idx / D;
+      const int d = idx - n * D;
+      float mmax = -CUDART_INF_F;
+#pragma unroll
+      for (int ww = 0; ww < kAttnConsumerWarps; ++ww) mmax = fmaxf(mmax, st_m[ww * ROWS + n]);
+      float ltot = 0.f, o = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kAttnConsumerWarps; ++ww) {
+        const float mw = st_m[ww * ROWS + n];
+        const float f = (mw == -CUDART_INF_F) ? 0.f : fast_exp2((mw - mmax) * p.scale_log2);
+        ltot = fmaf(st_l[ww * ROWS + n], f, ltot);
+        o = fmaf(mbuf[(ww * ROWS + n) * C::OPITCH + d], f, o);
+      }
+      o = ltot > 0.f ? o / ltot : 0.f;
+      if (complete) {
+        const int r = ent.r0 + n;
+        const int t = r / p.G, h = w.kvh * p.G + r % p.G;
+        p.out[((static_cast<long long>(ent.b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);
+      } else {
+        const long long prow = (static_cast<long long>(blockIdx.x) * 2 + slot) * ROWS + n;
+        p.part_o[prow * D + d] = o;
+        if (d == 0) p.part_lse[prow] = ltot > 0.f ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+      }
     }
-    const float inv = ltot > 0.f ? 1.f / ltot : 0.f;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) stat_f[w * C::kRows + n] *= inv;
-    const int r = r0 + n;
-    if (p.nsplit > 1 && r < r1) {
-      const int t = r / p.G, h = kvh * p.G + r % p.G;
-      p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] =
-          (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+    if (!complete) {
+      // Publish this partial (the barrier orders every thread's stores before thread 0's release
+      // of the arrival counter); the contributor that arrives last merges every partial of the
+      // row group, its own included, into the output and resets the counter.
+      named_barrier(1, kAttnConsumerWarps * 32);
+      const long long start_e = w.t - w.local;  // tile index of the entry's first tile
+      const int g_first = tile_owner(start_e, total, p.ngroups);
+      const int g_last = tile_owner(start_e + ent.n - 1, total, p.ngroups);
+      const bool first_in_slot1 = start_e != range_begin(g_first, total, p.ngroups);
+      if (threadIdx.x == 0) {
+        int ncontrib = 0;
+        for (int gg = g_first; gg <= g_last; ++gg)
+          ncontrib += range_begin(gg, total, p.ngroups) < range_begin(gg + 1, total, p.ngroups);
+        int* counter = p.counters + static_cast<long long>(w.e) * p.Hkv + w.kvh;
+        const int prev = atom_add_acq_rel_gpu(counter, 1);
+        const bool last = prev == ncontrib - 1;
+        if (last) *counter = 0;  // every contributor has arrived: ready for the next call
+        ctl[5 + par] = last;
+      }
+      named_barrier(1, kAttnConsumerWarps * 32);
+      if (ctl[5 + par]) {
+        // Warp `warp` merges rows warp, warp + 4, ...: lanes load the contributors'
+        // log-sum-exps in parallel (32 at a time), then stream the weighted partial rows.
+        constexpr int PER_LANE = (D + 31) / 32;
+        const int ncand = g_last - g_first + 1;
+        for (int n = warp; n < nvalid; n += kAttnConsumerWarps) {
+          auto row_of = [&](int k) {
+            const int gg = g_first + k;
+            const int sl = (k == 0 && first_in_slot1) ? 1 : 0;
+            return (static_cast<long long>(gg * p.Hkv + w.kvh) * 2 + sl) * ROWS + n;
+          };
+          auto has_tiles = [&](int k) {
+            return range_begin(g_first + k, total, p.ngroups) <
+                   range_begin(g_first + k + 1, total, p.ngroups);
+          };
+          float mmax = -CUDART_INF_F;
+          for (int k = lane; k < ncand; k += 32)
+            if (has_tiles(k)) mmax = fmaxf(mmax, __ldcg(p.part_lse + row_of(k)));
+#pragma unroll
+          for (int m = 16; m >= 1; m >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, m));
+          float acc[PER_LANE];
+#pragma unroll
+          for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
+          float wsum = 0.f;
+          for (int k0 = 0; k0 < ncand; k0 += 32) {
+            float wk = 0.f;
+            if (k0 + lane < ncand && has_tiles(k0 + lane)) {
+              const float ls = __ldcg(p.part_lse + row_of(k0 + lane));
+              wk = (ls == -CUDART_INF_F) ? 0.f : fast_exp2(ls - mmax);
+            }
+            float ws = wk;
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, m);
+            wsum += ws;
+            const int cnt = min(32, ncand - k0);
+#pragma unroll 4
+            for (int j = 0; j < cnt; ++j) {
+              const float wgt = __shfl_sync(0xffffffffu, wk, j);
+              if (wgt == 0.f) continue;
+              const float* po = p.part_o + row_of(k0 + j) * D;
+#pragma unroll
+              for (int u = 0; u < PER_LANE; ++u) {
+                const int d = lane + 32 * u;
+                if (d < D) acc[u] = fmaf(wgt, __ldcg(po + d), acc[u]);
+              }
+            }
+          }
+          const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+          const int r = ent.r0 + n;
+          const int t = r / p.G, h = w.kvh * p.G + r % p.G;
+          uint16_t* dst = p.out + ((static_cast<long long>(ent.b) * p.T + t) * p.Hq + h) * D;
+#pragma unroll
+          for (int u = 0; u < PER_LANE; ++u) {
+            const int d = lane + 32 * u;
+            if (d < D) dst[d] = float_to_bf16_bits(acc[u] * inv);
+          }
+        }
+      }
     }
-  }
-  __syncthreads();
-
-  for (int idx = threadIdx.x; idx < C::kRows * D; idx += kAttnThreads) {
-    const int n = idx / D;
-    const int d = idx - n * D;
-    const int r = r0 + n;
-    if (r >= r1) continue;
-    float o = 0.f;
+    first_segment = false;
+    ++seg_index;
+    w = wn;
 #pragma unroll
-    for (int w = 0; w < kAttnConsumerWarps; ++w)
-      o = fmaf(merge[(w * C::kRows + n) * C::OPITCH + d], stat_f[w * C::kRows + n], o);
-    const int t = r / p.G, h = kvh * p.G + r % p.G;
-    const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;
-    if (p.nsplit == 1) {
-      p.out[row * D + d] = float_to_bf16_bits(o);
-    } else {
-      p.part_o[(row * p.nsplit + split) * D + d] = o;
-    }
-  }
-}
-
-// Merges the split partials of every (b, t, h) row: one warp per row.
-template <int D>
-__global__ void __launch_bounds__(128) decode_attn_combine_kernel(const AttnParams p) {
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
-  const long long nrows = static_cast<long long>(p.B) * p.T * p.Hq;
-  if (row >= nrows) return;
-  const float* lse = p.part_lse + row * p.nsplit;
-  float mmax = -CUDART_INF_F;
-  for (int s = lane; s < p.nsplit; s += 32) mmax = fmaxf(mmax, lse[s]);
+    for (int j = 0; j < NQT; ++j)
 #pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, m));
-  float wsum = 0.f;
-  for (int s = lane; s < p.nsplit; s += 32)
-    wsum += (lse[s] == -CUDART_INF_F) ? 0.f : fast_exp2(lse[s] - mmax);
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, m);
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  constexpr int PER_LANE = (D + 31) / 32;
-  float acc[PER_LANE];
-#pragma unroll
-  for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
-  const float* po = p.part_o + row * p.nsplit * D;
-  for (int s = 0; s < p.nsplit; ++s) {
-    const float ls = lse[s];
-    if (ls == -CUDART_INF_F) continue;
-    const float w = fast_exp2(ls - mmax) * inv;
-#pragma unroll
-    for (int u = 0; u < PER_LANE; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) acc[u] = fmaf(w, po[s * D + d], acc[u]);
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < PER_LANE; ++u) {
-    const int d = lane + 32 * u;
-    if (d < D) p.out[row * D + d] = float_to_bf16_bits(acc[u]);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        qf[j][kk][0] = qf_next[j][kk][0];
+        qf[j][kk][1] = qf_next[j][kk][1];
+      }
   }
 }
 

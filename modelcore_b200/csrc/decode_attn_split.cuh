@@ -1,0 +1,411 @@
+// Piece 3, short-row variant: decode attention with one CTA per (row, kv head, query block, key
+// split) -- no persistent loop, no tile-space scan, no cross-CTA publishing.  The host picks it
+// when a row can hold at most a few thousand keys (min(Tmax, window + T) <= 32 tiles of 64): there
+// the persistent kernel's fixed costs (the start-up scan over every row's length and the merges
+// of rows cut between CTAs) are not amortised, and short independent CTAs in waves stream better.
+//
+// Semantics are those of decode_attn.cuh.  Per CTA: a producer warp streams its K/V tiles by TMA
+// into a STAGES-deep ring; four consumer warps each take 16 keys of every 64-key tile; the same
+// tensor-core contraction with keys on the M side (S^T = K Q^T, O^T += V^T P^T via
+// ldmatrix.trans / movmatrix.trans); the warps merge through shared memory.  With one split per
+// row the CTA writes the bf16 output; with several it writes (O/l, log2-sum-exp) partials that
+// decode_attn_split_combine_kernel merges, one warp per output row.
+#pragma once
+
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "decode_attn.cuh"
+
+namespace mcb {
+
+struct SplitAttnParams {
+  const uint16_t* q;
+  long long qs[3];
+  const int32_t* cache_seqlens;
+  uint16_t* out;
+  float* part_o;    // [((b*T + t)*Hq + h)*nsplit + s][D]
+  float* part_lse;  // [((b*T + t)*Hq + h)*nsplit + s]
+  int B, T, Hq, Hkv, G, Tmax, window;
+  float scale_log2;  // softmax_scale * log2(e)
+  int nsplit, tiles_per_split, nqb;
+};
+
+
+template <int D, int NQT, int KPW, int STAGES>
+struct SplitAttnConfig {
+  static constexpr int kRows = 8 * NQT;                      // query rows per CTA
+  static constexpr int TK = KPW * kAttnConsumerWarps;        // keys per stage
+  static constexpr int PANEL = D < 64 ? D : 64;              // columns per swizzled panel
+  static constexpr int NPANEL = D / PANEL;
+  static constexpr int ROW_BYTES = PANEL * 2;                // 32, 64 or 128
+  static constexpr int SWZ_MASK = ROW_BYTES == 128 ? 7 : (ROW_BYTES == 64 ? 3 : 1);
+  static constexpr int PANEL_BYTES = TK * ROW_BYTES;
+  static constexpr int TILE_BYTES = NPANEL * PANEL_BYTES;    // one K (or V) tile
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
+  static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
+  static constexpr int BODY_BYTES = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
+  // barriers (full + empty per stage) then per-warp row statistics
+  static constexpr int BAR_OFFSET = BODY_BYTES;
+  static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
+  static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
+  static constexpr int SMEM_BYTES = STAT_OFFSET + STAT_BYTES + 1024;  // + alignment slack
+  static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
+  static_assert(KPW % 16 == 0, "keys per warp");
+  static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
+};
+
+template <int D, int NQT, int KPW, int STAGES>
+__global__ void __launch_bounds__(kAttnThreads)
+    decode_attn_split_kernel(const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const SplitAttnParams p) {
+  using C = SplitAttnConfig<D, NQT, KPW, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFFSET);
+  uint64_t* empty_bar = full_bar + STAGES;
+  float* stat_m = reinterpret_cast<float*>(smem + C::STAT_OFFSET);
+  float* stat_l = stat_m + kAttnConsumerWarps * C::kRows;
+  float* stat_f = stat_l + kAttnConsumerWarps * C::kRows;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- which (b, kv head, query block, split) ----
+  int x = blockIdx.x;
+  const int split = x % p.nsplit;
+  x /= p.nsplit;
+  const int qb = x % p.nqb;
+  x /= p.nqb;
+  const int kvh = x % p.Hkv;
+  const int b = x / p.Hkv;
+
+  const int rows_total = p.T * p.G;
+  const int r0 = qb * C::kRows;
+  const int r1 = min(r0 + C::kRows, rows_total);
+  const int t_first = r0 / p.G;
+  const int t_last = (r1 - 1) / p.G;
+  const int L = p.cache_seqlens[b];
+  int hi = L + t_last;
+  if (hi >= p.Tmax || L < 0) {
+    if (threadIdx.x == 0) record_error(kErrPositionBeyondCache);
+    hi = min(max(hi, 0), p.Tmax - 1);
+  }
+  const int lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
+  const int kb = (min(lo, hi) / C::TK) * C::TK;
+  const int ntiles = (hi - kb) / C::TK + 1;
+  const int tile0 = split * p.tiles_per_split;
+  const int my_tiles = max(0, min(ntiles - tile0, p.tiles_per_split));
+
+  if (my_tiles == 0) {  // an empty split: its partial carries no weight
+    if (threadIdx.x < C::kRows) {
+      const int r = r0 + threadIdx.x;
+      if (r < r1) {
+        const int t = r / p.G, h = kvh * p.G + r % p.G;
+        p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] =
+            -CUDART_INF_F;
+      }
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kAttnConsumerWarps);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kAttnConsumerWarps) {
+    // ---------------- producer warp ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const uint64_t policy = l2_policy_evict_first();
+      for (int i = 0; i < my_tiles; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+        const int key0 = kb + (tile0 + i) * C::TK;
+        uint8_t* kdst = smem + s * C::STAGE_BYTES;
+        uint8_t* vdst = kdst + C::TILE_BYTES;
+#pragma unroll
+        for (int pn = 0; pn < C::NPANEL; ++pn) {
+          tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
+                      policy);
+          tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
+                      policy);
+        }
+      }
+    }
+  }
+
+  // Per-thread softmax state for rows n = j*8 + 2*(lane%4) + e.
+  float m_run[NQT][2], l_run[NQT][2];
+  float o_acc[NQT][D / 16][4];
+  int row_hi[NQT][2], row_lo[NQT][2];
+
+  if (warp < kAttnConsumerWarps) {
+    // ---------------- consumer warps ----------------
+    // Q^T fragments (B operand): row n = j*8 + lane/4, columns d = kk*16 + 2*(lane%4) + {0,1}, +8.
+    uint32_t qf[NQT][D / 16][2];
+#pragma unroll
+    for (int j = 0; j < NQT; ++j) {
+      const int r = r0 + j * 8 + (lane >> 2);
+      const uint16_t* qrow = nullptr;
+      if (r < r1) {
+        const int t = r / p.G, h = kvh * p.G + r % p.G;
+        qrow = p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+      }
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int d0 = kk * 16 + 2 * (lane & 3);
+        qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+        qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int rr = r0 + j * 8 + 2 * (lane & 3) + e;
+        m_run[j][e] = -CUDART_INF_F;
+        l_run[j][e] = 0.f;
+        if (rr < r1) {
+          const int qpos = L + rr / p.G;
+          row_hi[j][e] = qpos;
+          row_lo[j][e] = p.window >= 0 ? qpos - p.window : 0;
+        } else {
+          row_hi[j][e] = -1;  // padding row: every key masked
+          row_lo[j][e] = 0;
+        }
+      }
+#pragma unroll
+      for (int db = 0; db < D / 16; ++db)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o_acc[j][db][c] = 0.f;
+    }
+
+    constexpr int NCH = KPW / 16;  // 16-key chunks per warp per stage
+    for (int i = 0; i < my_tiles; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(&full_bar[s], (i / STAGES) & 1)) break;
+      const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
+      const uint32_t vbase = kbase + C::TILE_BYTES;
+      const int tile_key0 = kb + (tile0 + i) * C::TK;
+
+      float sc[NCH][NQT][4];
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+        for (int j = 0; j < NQT; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sc[ch][j][c] = 0.f;
+        const int krow = warp * KPW + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int col = kk * 16 + (lane >> 4) * 8;  // first column of this lane's 8-wide chunk
+          const uint32_t addr = kbase + (col / C::PANEL) * C::PANEL_BYTES +
+                                swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(addr, a0, a1, a2, a3);
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) mma_16816(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
+        }
+      }
+
+      // Mask, then the online-softmax update over this warp's NCH*16 keys.
+#pragma unroll
+      for (int j = 0; j < NQT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float mx = -CUDART_INF_F;
+#pragma unroll
+          for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int key = tile_key0 + warp * KPW + ch * 16 + (lane >> 2) + hh * 8;
+              float& v = sc[ch][j][e + 2 * hh];
+              if (key > row_hi[j][e] || key < row_lo[j][e]) v = -CUDART_INF_F;
+              mx = fmaxf(mx, v);
+            }
+          }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float m_new = fmaxf(m_run[j][e], mx);
+          float alpha = 1.f;
+          float msub = 0.f;
+          if (m_new != -CUDART_INF_F) {
+            alpha = fast_exp2((m_run[j][e] - m_new) * p.scale_log2);
+            msub = m_new * p.scale_log2;
+          }
+          m_run[j][e] = m_new;
+          float lsum = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              float& v = sc[ch][j][e + 2 * hh];
+              v = fast_exp2(fmaf(v, p.scale_log2, -msub));  // exp2(-inf) = 0 for masked keys
+              lsum += v;
+            }
+          }
+          l_run[j][e] = fmaf(l_run[j][e], alpha, lsum);
+#pragma unroll
+          for (int db = 0; db < D / 16; ++db) {
+            o_acc[j][db][e] *= alpha;
+            o_acc[j][db][e + 2] *= alpha;
+          }
+        }
+      }
+
+      // O^T += V^T . P^T
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        uint32_t pb[NQT][2];
+#pragma unroll
+        for (int j = 0; j < NQT; ++j) {
+          pb[j][0] = movmatrix_trans(pack_bf16x2(sc[ch][j][0], sc[ch][j][1]));
+          pb[j][1] = movmatrix_trans(pack_bf16x2(sc[ch][j][2], sc[ch][j][3]));
+        }
+        const int m = lane >> 3;
+        const int vrow = warp * KPW + ch * 16 + (lane & 7) + (m >> 1) * 8;
+#pragma unroll
+        for (int db = 0; db < D / 16; ++db) {
+          const int col = db * 16 + (m & 1) * 8;
+          const uint32_t addr = vbase + (col / C::PANEL) * C::PANEL_BYTES +
+                                swz<C::ROW_BYTES, C::SWZ_MASK>(vrow, (col % C::PANEL) / 8);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(addr, a0, a1, a2, a3);
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) mma_16816(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+
+    // Full per-row sums of this warp.
+#pragma unroll
+    for (int j = 0; j < NQT; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = l_run[j][e];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        l_run[j][e] = v;
+      }
+  }
+
+  __syncthreads();  // the ring is drained: reuse it as the merge buffer
+
+  float* merge = reinterpret_cast<float*>(smem);
+  if (warp < kAttnConsumerWarps) {
+#pragma unroll
+    for (int j = 0; j < NQT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = j * 8 + 2 * (lane & 3) + e;
+        if (lane < 4) {
+          stat_m[warp * C::kRows + n] = m_run[j][e];
+          stat_l[warp * C::kRows + n] = l_run[j][e];
+        }
+#pragma unroll
+        for (int db = 0; db < D / 16; ++db) {
+          const int d = db * 16 + (lane >> 2);
+          float* row = merge + (warp * C::kRows + n) * C::OPITCH;
+          row[d] = o_acc[j][db][e];
+          row[d + 8] = o_acc[j][db][e + 2];
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // Per row: the CTA max, each warp's weight and the total.
+  if (threadIdx.x < C::kRows) {
+    const int n = threadIdx.x;
+    float mmax = -CUDART_INF_F;
+    for (int w = 0; w < kAttnConsumerWarps; ++w) mmax = fmaxf(mmax, stat_m[w * C::kRows + n]);
+    float ltot = 0.f;
+    for (int w = 0; w < kAttnConsumerWarps; ++w) {
+      const float mw = stat_m[w * C::kRows + n];
+      const float f = (mw == -CUDART_INF_F) ? 0.f : fast_exp2((mw - mmax) * p.scale_log2);
+      stat_f[w * C::kRows + n] = f;
+      ltot = fmaf(stat_l[w * C::kRows + n], f, ltot);
+    }
+    const float inv = ltot > 0.f ? 1.f / ltot : 0.f;
+    for (int w = 0; w < kAttnConsumerWarps; ++w) stat_f[w * C::kRows + n] *= inv;
+    const int r = r0 + n;
+    if (p.nsplit > 1 && r < r1) {
+      const int t = r / p.G, h = kvh * p.G + r % p.G;
+      p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] =
+          (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+    }
+  }
+  __syncthreads();
+
+  for (int idx = threadIdx.x; idx < C::kRows * D; idx += kAttnThreads) {
+    const int n = idx / D;
+    const int d = idx - n * D;
+    const int r = r0 + n;
+    if (r >= r1) continue;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w)
+      o = fmaf(merge[(w * C::kRows + n) * C::OPITCH + d], stat_f[w * C::kRows + n], o);
+    const int t = r / p.G, h = kvh * p.G + r % p.G;
+    const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;
+    if (p.nsplit == 1) {
+      p.out[row * D + d] = float_to_bf16_bits(o);
+    } else {
+      p.part_o[(row * p.nsplit + split) * D + d] = o;
+    }
+  }
+}
+
+// Merges the split partials of every (b, t, h) row: one warp per row.
+template <int D>
+__global__ void __launch_bounds__(128) decode_attn_split_combine_kernel(const SplitAttnParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const long long nrows = static_cast<long long>(p.B) * p.T * p.Hq;
+  if (row >= nrows) return;
+  const float* lse = p.part_lse + row * p.nsplit;
+  float mmax = -CUDART_INF_F;
+  for (int s = lane; s < p.nsplit; s += 32) mmax = fmaxf(mmax, lse[s]);
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, m));
+  float wsum = 0.f;
+  for (int s = lane; s < p.nsplit; s += 32)
+    wsum += (lse[s] == -CUDART_INF_F) ? 0.f : fast_exp2(lse[s] - mmax);
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, m);
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  constexpr int PER_LANE = (D + 31) / 32;
+  float acc[PER_LANE];
+#pragma unroll
+  for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
+  const float* po = p.part_o + row * p.nsplit * D;
+  for (int s = 0; s < p.nsplit; ++s) {
+    const float ls = lse[s];
+    if (ls == -CUDART_INF_F) continue;
+    const float w = fast_exp2(ls - mmax) * inv;
+#pragma unroll
+    for (int u = 0; u < PER_LANE; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) acc[u] = fmaf(w, po[s * D + d], acc[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < PER_LANE; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) p.out[row * D + d] = float_to_bf16_bits(acc[u]);
+  }
+}
+
+}  // namespace mcb

@@ -12,6 +12,7 @@
 #include "../../include/mcb200.h"
 #include "common.cuh"
 #include "decode_attn.cuh"
+#include "decode_attn_split.cuh"
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
 
@@ -81,14 +82,119 @@ cudaError_t ensure_smem(K kernel, int bytes, std::atomic<uint64_t>& done) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Decode attention planning.
-struct AttnPlan {
-  int D, nqt, tk, rows, nqb, nsplit, tps;
-  size_t part_o_bytes, part_lse_bytes, ws_bytes;
+// Decode attention planning.  Two kernels share the semantics: the persistent one
+// (decode_attn.cuh: a balanced partition of every row's key tiles over a resident grid) and the
+// split one (decode_attn_split.cuh: one CTA per row group and key split).  With num_ctas == 0 the
+// host picks by how many key tiles a row can hold: up to kSplitMaxTiles the split kernel (short
+// rows: the persistent kernel's start-up scan and cross-CTA merges are not amortised), beyond it
+// the persistent one.  num_ctas > 0 forces a persistent grid of that size, num_ctas < 0 forces
+// the split kernel with -num_ctas key splits per row group.
+constexpr int kKPW = 16;             // keys per consumer warp per tile (tile = 64 keys)
+constexpr long long kSplitMaxTiles = 33;  // 2048 keys + one tile of alignment slack
+
+enum AttnMode { kModePersistent = 0, kModeSplit = 1 };
+
+template <int D, int NQT>
+struct AttnVariant {
+  // Ring depth per head_dim (persistent): 144-256 KB of tiles in flight per SM at this occupancy.
+  static constexpr int STAGES = D <= 32 ? 8 : (D == 64 ? 3 : (D == 128 ? 4 : 2));
+  using Cfg = mcb::AttnConfig<D, NQT, kKPW, STAGES>;
+  static constexpr auto kernel = mcb::decode_attn_kernel<D, NQT, kKPW, STAGES>;
+  // Split kernel: 3-4 stages, 2-3 CTAs per SM.
+  static constexpr int SPLIT_STAGES = D >= 128 ? 3 : 4;
+  using SplitCfg = mcb::SplitAttnConfig<D, NQT, kKPW, SPLIT_STAGES>;
+  static constexpr auto split_kernel = mcb::decode_attn_split_kernel<D, NQT, kKPW, SPLIT_STAGES>;
+
+  // Raises the persistent kernel's shared-memory limit on the current device (once) and returns
+  // how many of its CTAs stay resident per SM.
+  static int ctas_per_sm(int* out) {
+    static std::atomic<uint64_t> done{0};
+    static std::mutex mu;
+    static int cache[64] = {0};
+    cudaError_t e = ensure_smem(kernel, Cfg::SMEM_BYTES, done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn)");
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+      *out = cache[dev];
+      return MCB_OK;
+    }
+    int n = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, mcb::kAttnThreads, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (n <= 0) return fail(MCB_ERR_UNSUPPORTED, "decode_attn<%d,%d> cannot be resident on an SM", D, NQT);
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    *out = n;
+    return MCB_OK;
+  }
+
+  static int launch(int grid, const CUtensorMap& km, const CUtensorMap& vm, const mcb::AttnParams& prm,
+                    cudaStream_t st) {
+    int dummy = 0;
+    int rc = ctas_per_sm(&dummy);  // also sets the shared-memory limit
+    if (rc != MCB_OK) return rc;
+    kernel<<<grid, mcb::kAttnThreads, Cfg::SMEM_BYTES, st>>>(km, vm, prm);
+    g_launches++;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
+    return MCB_OK;
+  }
+
+  static int launch_split(long long grid, const CUtensorMap& km, const CUtensorMap& vm,
+                          const mcb::SplitAttnParams& prm, cudaStream_t st) {
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = ensure_smem(split_kernel, SplitCfg::SMEM_BYTES, done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn_split)");
+    split_kernel<<<static_cast<unsigned>(grid), mcb::kAttnThreads, SplitCfg::SMEM_BYTES, st>>>(km, vm, prm);
+    g_launches++;
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
+    if (prm.nsplit > 1) {
+      const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
+      mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
+      g_launches++;
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split_combine launch");
+    }
+    return MCB_OK;
+  }
 };
 
-constexpr int kKPW = 16;
+#define MCB_DISPATCH_D(D_, NQT_, CALL)                                   \
+  switch (D_) {                                                          \
+    case 16: return (NQT_) == 1 ? AttnVariant<16, 1>::CALL : AttnVariant<16, 2>::CALL;   \
+    case 32: return (NQT_) == 1 ? AttnVariant<32, 1>::CALL : AttnVariant<32, 2>::CALL;   \
+    case 64: return (NQT_) == 1 ? AttnVariant<64, 1>::CALL : AttnVariant<64, 2>::CALL;   \
+    case 128: return (NQT_) == 1 ? AttnVariant<128, 1>::CALL : AttnVariant<128, 2>::CALL; \
+    case 256: return AttnVariant<256, 1>::CALL;                          \
+  }                                                                      \
+  return fail(MCB_ERR_UNSUPPORTED, "head_dim %d", D_);
 
+int variant_ctas_per_sm(int D, int nqt, int* out) { MCB_DISPATCH_D(D, nqt, ctas_per_sm(out)) }
+
+int variant_launch(int D, int nqt, int grid, const CUtensorMap& km, const CUtensorMap& vm,
+                   const mcb::AttnParams& p, cudaStream_t st) {
+  MCB_DISPATCH_D(D, nqt, launch(grid, km, vm, p, st))
+}
+
+int variant_launch_split(int D, int nqt, long long grid, const CUtensorMap& km, const CUtensorMap& vm,
+                         const mcb::SplitAttnParams& p, cudaStream_t st) {
+  MCB_DISPATCH_D(D, nqt, launch_split(grid, km, vm, p, st))
+}
+
+struct AttnPlan {
+  int D, nqt, rows, tk, nqb, mode;
+  int grid;         // persistent CTAs (persistent mode)
+  int nsplit, tps;  // key splits per row group and tiles per split (split mode)
+  size_t part_o_bytes, part_lse_bytes, ws_bytes, counter_count;
+};
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Validates the shape and plans the launch.  Without a usable device (a CPU-only process asking
+// for the workspace size) an automatic persistent grid assumes one CTA per SM of a B200.
 int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_decode_attn: args is NULL");
   if (a->B < 0 || a->T < 0 || a->Hq <= 0 || a->Hkv <= 0 || a->D <= 0 || a->Tmax <= 0)
@@ -103,34 +209,62 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
                 a->D);
   const int G = a->Hq / a->Hkv;
   pl->D = a->D;
-  const int rows_total = a->T * G;
+  const long long rows_total = static_cast<long long>(a->T) * G;
   pl->nqt = (rows_total <= 8 || a->D == 256) ? 1 : 2;
   pl->rows = 8 * pl->nqt;
   pl->tk = kKPW * mcb::kAttnConsumerWarps;
-  pl->nqb = rows_total > 0 ? (rows_total + pl->rows - 1) / pl->rows : 0;
+  pl->nqb = rows_total > 0 ? static_cast<int>((rows_total + pl->rows - 1) / pl->rows) : 0;
   const long long cap_keys =
       a->window >= 0 ? std::min<long long>(a->Tmax, static_cast<long long>(a->window) + a->T)
                      : a->Tmax;
-  const int max_tiles = static_cast<int>((cap_keys + pl->tk - 1) / pl->tk) + 1;
-  long long base = static_cast<long long>(a->B) * a->Hkv * pl->nqb;
-  int nsplit;
-  if (a->num_splits > 0) {
-    nsplit = std::min(a->num_splits, max_tiles);
-  } else {
-    const long long target = 4ll * device_sm_count();
-    nsplit = base > 0 ? static_cast<int>((target + base - 1) / base) : 1;
-    nsplit = std::max(1, std::min(nsplit, std::max(1, max_tiles / 4)));
-  }
-  pl->tps = (max_tiles + nsplit - 1) / nsplit;
-  pl->nsplit = (max_tiles + pl->tps - 1) / pl->tps;
-  if (base * pl->nsplit > 0x7fffffffll)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: grid too large");
+  const long long max_tiles = (cap_keys + pl->tk - 1) / pl->tk + 1;
+  const long long base = static_cast<long long>(a->B) * a->Hkv * pl->nqb;
+  if (base * max_tiles > 0x7fffffffll)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: more than 2^31 key tiles");
+  pl->mode = (a->num_ctas < 0 || (a->num_ctas == 0 && max_tiles <= kSplitMaxTiles)) ? kModeSplit
+                                                                                  : kModePersistent;
   const size_t rows_out = static_cast<size_t>(a->B) * a->T * a->Hq;
-  if (pl->nsplit > 1) {
-    pl->part_o_bytes = (rows_out * pl->nsplit * a->D * 4 + 255) & ~size_t(255);
-    pl->part_lse_bytes = (rows_out * pl->nsplit * 4 + 255) & ~size_t(255);
+  if (pl->mode == kModeSplit) {
+    int nsplit;
+    if (a->num_ctas < 0) {
+      nsplit = static_cast<int>(std::min<long long>(-static_cast<long long>(a->num_ctas), max_tiles));
+    } else {
+      const long long target = 4ll * device_sm_count();
+      nsplit = base > 0 ? static_cast<int>(std::min<long long>((target + base - 1) / base, max_tiles)) : 1;
+      nsplit = std::max(1, std::min<int>(nsplit, std::max<long long>(1, max_tiles / 4)));
+    }
+    pl->tps = static_cast<int>((max_tiles + nsplit - 1) / nsplit);
+    pl->nsplit = static_cast<int>((max_tiles + pl->tps - 1) / pl->tps);
+    if (base * pl->nsplit > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: grid too large");
+    pl->grid = 0;
+    if (pl->nsplit > 1) {
+      pl->part_o_bytes = round256(rows_out * pl->nsplit * a->D * 4);
+      pl->part_lse_bytes = round256(rows_out * pl->nsplit * 4);
+    } else {
+      pl->part_o_bytes = pl->part_lse_bytes = 0;
+    }
+    pl->counter_count = 0;
   } else {
-    pl->part_o_bytes = pl->part_lse_bytes = 0;
+    if (a->num_ctas > 0) {
+      pl->grid = a->num_ctas;
+    } else {
+      int per_sm = 1;
+      int dev = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess) {
+        const int rc = variant_ctas_per_sm(a->D, pl->nqt, &per_sm);
+        if (rc != MCB_OK) return rc;
+      } else {
+        cudaGetLastError();
+      }
+      pl->grid = device_sm_count() * per_sm;
+    }
+    // whole groups of Hkv CTAs (one per kv head), at least one group
+    pl->grid = std::max(a->Hkv, pl->grid / a->Hkv * a->Hkv);
+    pl->nsplit = pl->tps = 0;
+    const size_t slots = static_cast<size_t>(pl->grid) * 2 * pl->rows;
+    pl->part_o_bytes = round256(slots * a->D * 4);
+    pl->part_lse_bytes = round256(slots * 4);
+    pl->counter_count = static_cast<size_t>(base);
   }
   pl->ws_bytes = pl->part_o_bytes + pl->part_lse_bytes;
   return MCB_OK;
@@ -156,28 +290,71 @@ int encode_cache_map(CUtensorMap* map, const void* base, int D, int Hkv, int Tma
   return MCB_OK;
 }
 
-template <int D, int NQT>
-int launch_attn_variant(const AttnPlan& pl, const CUtensorMap& km, const CUtensorMap& vm,
-                        const mcb::AttnParams& prm, cudaStream_t st) {
-  constexpr int STAGES = D >= 128 ? 3 : 4;
-  using Cfg = mcb::AttnConfig<D, NQT, kKPW, STAGES>;
-  static std::atomic<uint64_t> done{0};
-  auto kern = mcb::decode_attn_kernel<D, NQT, kKPW, STAGES>;
-  cudaError_t e = ensure_smem(kern, Cfg::SMEM_BYTES, done);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn)");
-  const long long grid = static_cast<long long>(prm.B) * prm.Hkv * pl.nqb * pl.nsplit;
-  kern<<<static_cast<unsigned>(grid), mcb::kAttnThreads, Cfg::SMEM_BYTES, st>>>(km, vm, prm);
-  g_launches++;
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
-  if (pl.nsplit > 1) {
-    const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
-    mcb::decode_attn_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
-    g_launches++;
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "decode_attn_combine launch");
-  }
+int check_attn_pointers(const mcb_attn_args* a, const char* who) {
+  if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->out == nullptr ||
+      a->cache_seqlens == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "%s: NULL pointer argument", who);
+  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || !aligned(a->q, 16) ||
+      !aligned(a->out, 16))
+    return fail(MCB_ERR_ALIGNMENT, "%s: q, out and cache pointers must be 16-byte aligned", who);
+  for (int i = 0; i < 3; ++i)
+    if (a->q_stride[i] < 0 || (a->q_stride[i] % 8) != 0)
+      return fail(MCB_ERR_ALIGNMENT, "%s: q strides must be non-negative multiples of 8 elements", who);
   return MCB_OK;
+}
+
+// Encodes the tensor maps, fills the kernel parameters with the workspace `ws` (and, for the
+// persistent kernel, the arrival counters) and launches.
+int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* counters, cudaStream_t st) {
+  CUtensorMap km, vm;
+  int rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  if (rc != MCB_OK) return rc;
+  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  if (rc != MCB_OK) return rc;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  if (pl.mode == kModeSplit) {
+    mcb::SplitAttnParams p;
+    p.q = static_cast<const uint16_t*>(a->q);
+    for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
+    p.cache_seqlens = a->cache_seqlens;
+    p.out = static_cast<uint16_t*>(a->out);
+    p.part_o = pl.nsplit > 1 ? reinterpret_cast<float*>(w) : nullptr;
+    p.part_lse = pl.nsplit > 1 ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
+    p.B = a->B;
+    p.T = a->T;
+    p.Hq = a->Hq;
+    p.Hkv = a->Hkv;
+    p.G = a->Hq / a->Hkv;
+    p.Tmax = a->Tmax;
+    p.window = a->window;
+    p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+    p.nsplit = pl.nsplit;
+    p.tiles_per_split = pl.tps;
+    p.nqb = pl.nqb;
+    const long long grid = static_cast<long long>(a->B) * a->Hkv * pl.nqb * pl.nsplit;
+    return variant_launch_split(a->D, pl.nqt, grid, km, vm, p, st);
+  }
+  mcb::AttnParams p;
+  p.q = static_cast<const uint16_t*>(a->q);
+  for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
+  p.cache_seqlens = a->cache_seqlens;
+  p.out = static_cast<uint16_t*>(a->out);
+  p.part_o = reinterpret_cast<float*>(w);
+  p.part_lse = reinterpret_cast<float*>(w + pl.part_o_bytes);
+  p.counters = counters;
+  p.B = a->B;
+  p.T = a->T;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.G = a->Hq / a->Hkv;
+  p.Tmax = a->Tmax;
+  p.window = a->window;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.nqb = pl.nqb;
+  p.n_entries = a->B * pl.nqb;
+  p.grid = pl.grid;
+  p.ngroups = pl.grid / a->Hkv;
+  return variant_launch(a->D, pl.nqt, pl.grid, km, vm, p, st);
 }
 
 }  // namespace
@@ -332,58 +509,28 @@ size_t mcb_decode_attn_workspace_size(const mcb_attn_args* a) {
   return pl.ws_bytes;
 }
 
+size_t mcb_decode_attn_counter_count(const mcb_attn_args* a) {
+  AttnPlan pl;
+  if (plan_attn(a, &pl) != MCB_OK) return 0;
+  return pl.counter_count;
+}
+
 int mcb_decode_attn(const mcb_attn_args* a, void* stream) {
   AttnPlan pl;
   int rc = plan_attn(a, &pl);
   if (rc != MCB_OK) return rc;
-  if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->out == nullptr ||
-      a->cache_seqlens == nullptr)
-    return fail(MCB_ERR_INVALID_ARG, "mcb_decode_attn: NULL pointer argument");
-  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || !aligned(a->q, 16) ||
-      !aligned(a->out, 16))
-    return fail(MCB_ERR_ALIGNMENT, "mcb_decode_attn: q, out and cache pointers must be 16-byte aligned");
-  for (int i = 0; i < 3; ++i)
-    if (a->q_stride[i] < 0 || (a->q_stride[i] % 8) != 0)
-      return fail(MCB_ERR_ALIGNMENT, "mcb_decode_attn: q strides must be non-negative multiples of 8 elements");
-  if (pl.ws_bytes > 0 && (a->workspace == nullptr || a->workspace_bytes < pl.ws_bytes || !aligned(a->workspace, 256)))
+  rc = check_attn_pointers(a, "mcb_decode_attn");
+  if (rc != MCB_OK) return rc;
+  if (pl.ws_bytes > 0 &&
+      (a->workspace == nullptr || a->workspace_bytes < pl.ws_bytes || !aligned(a->workspace, 256)))
     return fail(MCB_ERR_WORKSPACE, "mcb_decode_attn: needs %zu bytes of 256-byte aligned workspace, got %zu",
                 pl.ws_bytes, a->workspace ? a->workspace_bytes : size_t(0));
+  if (pl.counter_count > 0 &&
+      (a->counters == nullptr || a->counter_count < pl.counter_count || !aligned(a->counters, 4)))
+    return fail(MCB_ERR_WORKSPACE, "mcb_decode_attn: needs %zu zero-initialised int32 counters, got %zu",
+                pl.counter_count, a->counters ? a->counter_count : size_t(0));
   if (a->B == 0 || a->T == 0) return MCB_OK;
-
-  CUtensorMap km, vm;
-  rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
-  if (rc != MCB_OK) return rc;
-  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
-  if (rc != MCB_OK) return rc;
-
-  mcb::AttnParams p;
-  p.q = static_cast<const uint16_t*>(a->q);
-  for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
-  p.cache_seqlens = a->cache_seqlens;
-  p.out = static_cast<uint16_t*>(a->out);
-  p.part_o = pl.nsplit > 1 ? static_cast<float*>(a->workspace) : nullptr;
-  p.part_lse = pl.nsplit > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) + pl.part_o_bytes)
-                             : nullptr;
-  p.B = a->B;
-  p.T = a->T;
-  p.Hq = a->Hq;
-  p.Hkv = a->Hkv;
-  p.G = a->Hq / a->Hkv;
-  p.Tmax = a->Tmax;
-  p.window = a->window;
-  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
-  p.nsplit = pl.nsplit;
-  p.tiles_per_split = pl.tps;
-  p.nqb = pl.nqb;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (a->D) {
-    case 16: return pl.nqt == 1 ? launch_attn_variant<16, 1>(pl, km, vm, p, st) : launch_attn_variant<16, 2>(pl, km, vm, p, st);
-    case 32: return pl.nqt == 1 ? launch_attn_variant<32, 1>(pl, km, vm, p, st) : launch_attn_variant<32, 2>(pl, km, vm, p, st);
-    case 64: return pl.nqt == 1 ? launch_attn_variant<64, 1>(pl, km, vm, p, st) : launch_attn_variant<64, 2>(pl, km, vm, p, st);
-    case 128: return pl.nqt == 1 ? launch_attn_variant<128, 1>(pl, km, vm, p, st) : launch_attn_variant<128, 2>(pl, km, vm, p, st);
-    case 256: return launch_attn_variant<256, 1>(pl, km, vm, p, st);
-  }
-  return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: head_dim %d", a->D);
+  return run_attn(a, pl, a->workspace, a->counters, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -424,65 +571,27 @@ int mcb_decode_attn_noalloc(const mcb_attn_args* a, void* stream) {
   AttnPlan pl;
   int rc = plan_attn(a, &pl);
   if (rc != MCB_OK) return rc;
-  if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->out == nullptr ||
-      a->cache_seqlens == nullptr)
-    return fail(MCB_ERR_INVALID_ARG, "mcb_decode_attn_noalloc: NULL pointer argument");
-  if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || !aligned(a->q, 16) ||
-      !aligned(a->out, 16))
-    return fail(MCB_ERR_ALIGNMENT,
-                "mcb_decode_attn_noalloc: q, out and cache pointers must be 16-byte aligned");
-  for (int i = 0; i < 3; ++i)
-    if (a->q_stride[i] < 0 || (a->q_stride[i] % 8) != 0)
-      return fail(MCB_ERR_ALIGNMENT,
-                  "mcb_decode_attn_noalloc: q strides must be non-negative multiples of 8 elements");
-  if (pl.ws_bytes > MCB_NOALLOC_SCRATCH_BYTES)
+  rc = check_attn_pointers(a, "mcb_decode_attn_noalloc");
+  if (rc != MCB_OK) return rc;
+  const size_t counter_bytes = round256(pl.counter_count * 4);
+  if (pl.ws_bytes + counter_bytes > MCB_NOALLOC_SCRATCH_BYTES)
     return fail(MCB_ERR_WORKSPACE,
-                "mcb_decode_attn_noalloc: this shape's %d-way split needs %zu bytes of scratch, more "
-                "than the %u-byte static scratch; pass a smaller num_splits or use mcb_decode_attn "
-                "with a workspace",
-                pl.nsplit, pl.ws_bytes, MCB_NOALLOC_SCRATCH_BYTES);
+                "mcb_decode_attn_noalloc: %d persistent CTAs and %zu row groups need %zu bytes of "
+                "scratch, more than the %u-byte static scratch; pass a smaller num_ctas or use "
+                "mcb_decode_attn with a workspace",
+                pl.grid, pl.counter_count, pl.ws_bytes + counter_bytes, MCB_NOALLOC_SCRATCH_BYTES);
   if (a->B == 0 || a->T == 0) return MCB_OK;
   void* scratch = nullptr;
-  if (pl.ws_bytes > 0) {
-    rc = noalloc_scratch_ptr(&scratch);
-    if (rc != MCB_OK) return rc;
-  }
-
-  CUtensorMap km, vm;
-  rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  rc = noalloc_scratch_ptr(&scratch);
   if (rc != MCB_OK) return rc;
-  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
-  if (rc != MCB_OK) return rc;
-
-  mcb::AttnParams p;
-  p.q = static_cast<const uint16_t*>(a->q);
-  for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
-  p.cache_seqlens = a->cache_seqlens;
-  p.out = static_cast<uint16_t*>(a->out);
-  p.part_o = pl.nsplit > 1 ? static_cast<float*>(scratch) : nullptr;
-  p.part_lse = pl.nsplit > 1
-                   ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + pl.part_o_bytes)
-                   : nullptr;
-  p.B = a->B;
-  p.T = a->T;
-  p.Hq = a->Hq;
-  p.Hkv = a->Hkv;
-  p.G = a->Hq / a->Hkv;
-  p.Tmax = a->Tmax;
-  p.window = a->window;
-  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
-  p.nsplit = pl.nsplit;
-  p.tiles_per_split = pl.tps;
-  p.nqb = pl.nqb;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (a->D) {
-    case 16: return pl.nqt == 1 ? launch_attn_variant<16, 1>(pl, km, vm, p, st) : launch_attn_variant<16, 2>(pl, km, vm, p, st);
-    case 32: return pl.nqt == 1 ? launch_attn_variant<32, 1>(pl, km, vm, p, st) : launch_attn_variant<32, 2>(pl, km, vm, p, st);
-    case 64: return pl.nqt == 1 ? launch_attn_variant<64, 1>(pl, km, vm, p, st) : launch_attn_variant<64, 2>(pl, km, vm, p, st);
-    case 128: return pl.nqt == 1 ? launch_attn_variant<128, 1>(pl, km, vm, p, st) : launch_attn_variant<128, 2>(pl, km, vm, p, st);
-    case 256: return launch_attn_variant<256, 1>(pl, km, vm, p, st);
+  // The arrival counters (after the partials) must start at zero; the scratch keeps whatever the
+  // last call left there.
+  int32_t* counters = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + pl.ws_bytes);
+  if (counter_bytes > 0) {
+    cudaError_t e = cudaMemsetAsync(counters, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "mcb_decode_attn_noalloc: clearing the counters");
   }
-  return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn_noalloc: head_dim %d", a->D);
+  return run_attn(a, pl, scratch, counters, static_cast<cudaStream_t>(stream));
 }
 
 int mcb_device_error(int32_t* code, void* stream) {

@@ -2,8 +2,9 @@
 
 Each wrapper checks device, dtype, shape and layout on the host (no device sync), passes raw
 pointers and the current CUDA stream to libmcb200 and returns.  All of them are safe inside
-CUDA-graph capture: they only enqueue kernels, and the one allocation (the split-K workspace)
-comes from torch's caching allocator.  None has a CPU path: non-CUDA or non-bf16 tensors raise.
+CUDA-graph capture: they only enqueue kernels; the attention workspace is a cached per-device
+buffer (allocated the first time, outside capture when the first call is eager).  None has a
+CPU path: non-CUDA or non-bf16 tensors raise.
 """
 import ctypes
 import math
@@ -172,7 +173,7 @@ def kv_advance(cache_seqlens, n):
                                         cache_seqlens.numel(), int(n), _stream(cache_seqlens)))
 
 
-def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out):
+def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out):
     _need("q", q, 4)
     B, T, Hq, D = q.shape
     Hkv = k_cache.shape[2] if k_cache.dim() == 4 else -1
@@ -192,46 +193,93 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_sp
     args.B, args.T, args.Hq, args.Hkv, args.D, args.Tmax = B, T, Hq, Hkv, D, k_cache.shape[1]
     args.window = -1 if window is None or window < 0 else int(window)
     args.softmax_scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
-    args.num_splits = int(num_splits)
+    args.num_ctas = int(num_ctas)
     return args
 
 
-def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_splits=0):
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_splits, None)
+def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0):
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None)
     return int(_native.load().mcb_decode_attn_workspace_size(ctypes.byref(args)))
 
 
+_WORKSPACES = {}  # device index -> partial-result buffers (grown on demand)
+_COUNTERS = {}    # device index -> zero-initialised arrival-counter arrays (grown on demand)
+
+
+def _grow(cache, device, n, dtype, zero):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    bufs = cache.setdefault(idx, [])
+    if not bufs or bufs[-1].numel() < n:
+        make = torch.zeros if zero else torch.empty
+        bufs.append(make(max(n, 1 << 16), dtype=dtype, device=device))  # older ones stay alive:
+    return bufs[-1]                                                     # a CUDA graph may hold them
+
+
+def attn_workspace(device, nbytes):
+    """The per-device partials buffer decode_attn uses when none is passed."""
+    return _grow(_WORKSPACES, device, nbytes, torch.uint8, zero=False)
+
+
+def attn_counters(device, count):
+    """The per-device arrival counters decode_attn uses when none are passed: allocated
+    zero-filled; every completed call leaves the counters it used at zero again, so one array
+    serves every call on the device, CUDA-graph replays included.  Calls that can overlap on the
+    GPU must pass their own workspace and counters."""
+    return _grow(_COUNTERS, device, count, torch.int32, zero=True)
+
+
+def reset_counters():
+    """Zero the cached counter arrays again (after a call that reported a device error)."""
+    for bufs in _COUNTERS.values():
+        for b in bufs:
+            b.zero_()
+
+
 def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
-                num_splits=0, out=None, workspace=None):
+                num_ctas=0, out=None, workspace=None, counters=None):
     """softmax(q . K^T * scale) . V over each row's visible keys of one cache slot.
 
     q: (B, T, Hq, D) bf16; k_cache/v_cache: (B, T_max, Hkv, D) bf16 slot; query t of row b sits at
     cache_seqlens[b] + t and sees keys c <= that position within `window` (< 0: all).  The new
-    tokens must already be in the cache.  Returns out (B, T, Hq, D) bf16."""
+    tokens must already be in the cache.  num_ctas: 0 picks the launch plan; > 0 a persistent grid
+    of that many CTAs dividing all key tiles; < 0 one CTA per row group and key split, -num_ctas
+    splits (every plan gives the same result up to fp32 summation order).  workspace: uint8
+    partials buffer; counters: int32 arrival counters, zero before their first use (defaults:
+    the cached per-device ones).  Returns out (B, T, Hq, D) bf16."""
     if out is None:
         out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
     else:
         _need("out", out, 4)
         if out.shape != q.shape or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous tensor shaped like q")
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out)
     lib = _native.load()
     need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
+    ncount = int(lib.mcb_decode_attn_counter_count(ctypes.byref(args)))
     if need:
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        if workspace is None:
+            workspace = attn_workspace(q.device, need)
+        elif workspace.numel() < need:
+            raise RuntimeError(f"workspace of {workspace.numel()} bytes, {need} needed")
         args.workspace = workspace.data_ptr()
         args.workspace_bytes = workspace.numel()
+    if ncount:
+        if counters is None:
+            counters = attn_counters(q.device, ncount)
+        elif counters.dtype != torch.int32 or counters.numel() < ncount:
+            raise RuntimeError(f"counters must be >= {ncount} zero-initialised int32")
+        args.counters = counters.data_ptr()
+        args.counter_count = counters.numel()
     check(lib.mcb_decode_attn(ctypes.byref(args), _stream(q)))
     return out
 
 
 def decode_attn_noalloc(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
-                        num_splits=0, out=None):
+                        num_ctas=0, out=None):
     """decode_attn through mcb_decode_attn_noalloc: for callers that cannot allocate device
     memory (a host whose HBM is all carved into its own pools, or a binding without a device
-    allocator).  The split partials go to the library's static 8 MiB per-GPU scratch instead of a
-    workspace; shapes whose split plan needs more raise McbError(MCB_ERR_WORKSPACE).  Calls that
+    allocator).  The partials go to the library's static 8 MiB per-GPU scratch instead of a
+    workspace; a grid whose partials need more raise McbError(MCB_ERR_WORKSPACE).  Calls that
     can overlap on the GPU share that scratch and race: keep them on one stream.  `out` must be
     given by such a caller; when it is None this wrapper allocates it (torch), for tests."""
     if out is None:
@@ -240,7 +288,7 @@ def decode_attn_noalloc(q, k_cache, v_cache, cache_seqlens, *, window=-1, softma
         _need("out", out, 4)
         if out.shape != q.shape or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous tensor shaped like q")
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_splits, out)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out)
     check(_native.load().mcb_decode_attn_noalloc(ctypes.byref(args), _stream(q)))
     return out
 

@@ -22,7 +22,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 1
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
@@ -122,26 +122,34 @@ def test_attention_rejects_unsupported_shapes_without_a_device():
     assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
 
 
-def test_attention_workspace_grows_with_forced_splits():
+def test_attention_workspace_is_per_persistent_cta_not_per_length():
     lib = _native.load()
-    one = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=1, Tmax=1024)))
-    four = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=4, Tmax=1024)))
-    # splits are capped by the key tiles a row can span: Tmax 64 -> at most 2
-    capped = lib.mcb_decode_attn_workspace_size(ctypes.byref(_attn(num_splits=4, Tmax=64)))
-    assert capped == 16 * 2 * 128 * 4 + 256
-    assert one == 0
-    # (B*T*Hq rows) x splits x (D + 1) fp32, each part rounded up to 256 bytes
-    rows = 2 * 1 * 8
-    assert four == ((rows * 4 * 128 * 4 + 255) // 256 * 256) + ((rows * 4 * 4 + 255) // 256 * 256)
+    r256 = lambda x: (x + 255) // 256 * 256
+    # rows = 8 (T=1, G=4), D=128: per CTA two partial slots of 8 rows x (128 + 1) fp32; the grid
+    # is whole groups of Hkv (= 2) CTAs, at least one group
+    for asked, ctas in ((1, 2), (4, 4), (5, 4), (300, 300)):
+        want = r256(ctas * 2 * 8 * 128 * 4) + r256(ctas * 2 * 8 * 4)
+        for tmax in (64, 4096):
+            a = _attn(num_ctas=asked, Tmax=tmax)
+            assert lib.mcb_decode_attn_workspace_size(ctypes.byref(a)) == want
+            assert lib.mcb_decode_attn_counter_count(ctypes.byref(a)) == 2 * 1 * 2  # B x blocks x Hkv
+    # 16 rows per group when T * G > 8: T=3, G=4 -> 12 rows -> one query block
+    a = _attn(num_ctas=2, T=3)
+    assert lib.mcb_decode_attn_workspace_size(ctypes.byref(a)) == r256(2 * 2 * 16 * 128 * 4) + r256(2 * 2 * 16 * 4)
+    # T=5, G=4 -> 20 rows -> two query blocks of 16
+    assert lib.mcb_decode_attn_counter_count(ctypes.byref(_attn(num_ctas=2, T=5))) == 2 * 2 * 2
 
 
 def test_attention_checks_the_workspace_before_launching():
     lib = _native.load()
-    a = _attn(num_splits=4, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000,
+    a = _attn(num_ctas=4, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000,
               cache_seqlens=0x5000)
     a.q_stride[:] = (8 * 128, 8 * 128, 128)
     st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
     assert st == _native.MCB_ERR_WORKSPACE and "workspace" in msg
+    a.workspace, a.workspace_bytes = 0x100000, 1 << 20  # enough partials, no counters
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_WORKSPACE and "counters" in msg
     a.q_stride[:] = (8 * 128, 8 * 128, 100)
     st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
     assert st == _native.MCB_ERR_ALIGNMENT

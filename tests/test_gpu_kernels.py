@@ -215,13 +215,13 @@ def _attn_case_to_device(z):
             torch.from_numpy(z["seqlens"]).to(torch.int32).cuda(), int(z["window"]))
 
 
-@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("splits", [0, 1, 3, 37, -1, -3])
 @pytest.mark.parametrize("name", golden_files("kv_attn_"))
 def test_attention_matches_the_reference_golden_outputs(mcb, name, splits):
     _, ops = mcb
     z = load_golden(name)
     q, kc, vc, seqlens, window = _attn_case_to_device(z)
-    y = ops.decode_attn(q, kc, vc, seqlens, window=window, num_splits=splits)
+    y = ops.decode_attn(q, kc, vc, seqlens, window=window, num_ctas=splits)
     torch.cuda.synchronize()
     no_device_error(ops)
     err = (y.float().cpu().numpy() - z["y"]).__abs__().max()
@@ -269,8 +269,8 @@ def test_attention_matches_the_oracle_on_random_ragged_rows(mcb, case):
     lens[0] = 0
     ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
     args = (dev_bf16(q), dev_bf16(kc), dev_bf16(vc), torch.from_numpy(lens).to(torch.int32).cuda())
-    for splits in (0, 1, 2, 5):
-        y = ops.decode_attn(*args, window=window, num_splits=splits)
+    for splits in (0, 1, 2, 5, 300, -1, -2, -7):
+        y = ops.decode_attn(*args, window=window, num_ctas=splits)
         err = np.abs(y.float().cpu().numpy() - ref).max()
         assert err <= ATTN_TOL, (splits, err)
     no_device_error(ops)
@@ -282,7 +282,7 @@ def test_stale_kv_beyond_a_rows_content_is_unreachable(mcb):
     rng = np.random.default_rng(11)
     B, Hq, Hkv, D, Tmax = 4, 16, 4, 128, 512
     lens, q, kc, vc = _random_case(rng, B, 1, Hq, Hkv, D, Tmax, lens=[4, 170, 311, 9])
-    args = dict(window=-1, num_splits=2)
+    args = dict(window=-1, num_ctas=2)
     dq, dk, dv = dev_bf16(q), dev_bf16(kc), dev_bf16(vc)
     sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
     clean = ops.decode_attn(dq, dk, dv, sl, **args)
@@ -293,7 +293,9 @@ def test_stale_kv_beyond_a_rows_content_is_unreachable(mcb):
 
 
 def test_batched_rows_equal_each_row_alone(mcb):
-    """A ragged batch computes each row exactly as that row alone (same split plan)."""
+    """A ragged batch computes each row as that row alone (test_kernels.py:465-472).  The tile
+    partition spans the whole batch, so a row alone is cut at other tile boundaries: the results
+    agree up to fp32 summation order (a bf16 ulp or two), and both match the oracle."""
     _, ops = mcb
     rng = np.random.default_rng(5)
     B, Hq, Hkv, D, Tmax = 5, 32, 8, 128, 2000
@@ -301,12 +303,15 @@ def test_batched_rows_equal_each_row_alone(mcb):
     dq, dk, dv = dev_bf16(q), dev_bf16(kc), dev_bf16(vc)
     sl = torch.from_numpy(lens).to(torch.int32).cuda()
     for window in (-1, 300):
-        batched = ops.decode_attn(dq, dk, dv, sl, window=window, num_splits=4)
-        for b in range(B):
-            alone = ops.decode_attn(dq[b:b + 1].contiguous(), dk[b:b + 1].contiguous(),
-                                    dv[b:b + 1].contiguous(), sl[b:b + 1].contiguous(),
-                                    window=window, num_splits=4)
-            assert torch.equal(batched[b:b + 1], alone)
+        ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
+        for ctas in (0, 4, -3):
+            batched = ops.decode_attn(dq, dk, dv, sl, window=window, num_ctas=ctas)
+            assert np.abs(batched.float().cpu().numpy() - ref).max() <= ATTN_TOL
+            for b in range(B):
+                alone = ops.decode_attn(dq[b:b + 1].contiguous(), dk[b:b + 1].contiguous(),
+                                        dv[b:b + 1].contiguous(), sl[b:b + 1].contiguous(),
+                                        window=window, num_ctas=ctas)
+                assert (batched[b:b + 1].float() - alone.float()).abs().max().item() <= 2e-3
 
 
 def test_sliding_window_is_measured_from_each_rows_own_position(mcb):

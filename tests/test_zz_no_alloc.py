@@ -30,28 +30,31 @@ def _inputs(seed, B, Hq, Hkv, D, Tmax):
     return q, kc, vc, torch.from_numpy(lens).to(torch.int32).cuda()
 
 
-def _call_noalloc(q, kc, vc, sl, out, window, num_splits):
+def _call_noalloc(q, kc, vc, sl, out, window, num_ctas):
     """One call of the new entry point through the C ABI (ctypes, raw pointers, current stream)."""
-    args = ops._attn_args(q, kc, vc, sl, window, None, num_splits, out)
+    args = ops._attn_args(q, kc, vc, sl, window, None, num_ctas, out)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     return _native.load().mcb_decode_attn_noalloc(ctypes.byref(args), stream)
 
 
 SHAPES = [
-    # B, Hq, Hkv, D, Tmax, window, num_splits (0 = automatic)
+    # B, Hq, Hkv, D, Tmax, window, num_ctas (0: automatic plan, persistent for these rows;
+    # > 0 persistent grid; < 0 split plan with that many key splits)
     (8, 32, 8, 128, 8192, -1, 0),
-    (4, 12, 12, 64, 3000, 100, 3),
+    (4, 12, 12, 64, 3000, 100, 24),
+    (4, 12, 12, 64, 1000, -1, -3),
 ]
 
 
-@pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto-split", "mha-d64-window-3-split"])
+@pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto", "mha-d64-window-24-ctas",
+                                               "mha-d64-3-splits"])
 def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape):
     B, Hq, Hkv, D, Tmax, window, splits = shape
     for call, seed in enumerate((11, 12)):
         q, kc, vc, sl = _inputs(seed, B, Hq, Hkv, D, Tmax)
-        need = ops.decode_attn_workspace_bytes(q, kc, vc, sl, window=window, num_splits=splits)
-        assert 0 < need <= _native.NOALLOC_SCRATCH_BYTES  # the split path, i.e. the scratch, is used
-        expected = ops.decode_attn(q, kc, vc, sl, window=window, num_splits=splits)
+        need = ops.decode_attn_workspace_bytes(q, kc, vc, sl, window=window, num_ctas=splits)
+        assert 0 < need <= _native.NOALLOC_SCRATCH_BYTES  # partials live in the scratch
+        expected = ops.decode_attn(q, kc, vc, sl, window=window, num_ctas=splits)
         out = torch.full_like(q, float("nan"))
         torch.cuda.synchronize()
         free_before = torch.cuda.mem_get_info()[0]
@@ -65,17 +68,17 @@ def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape)
         assert ops.device_error()[0] == 0
 
 
-def test_noalloc_rejects_a_split_plan_larger_than_its_scratch():
+def test_noalloc_rejects_a_grid_whose_partials_exceed_its_scratch():
     B, Hq, Hkv, D, Tmax = 64, 32, 8, 128, 4096
     q, kc, vc, sl = _inputs(3, B, Hq, Hkv, D, Tmax)
-    assert ops.decode_attn_workspace_bytes(q, kc, vc, sl, num_splits=16) > _native.NOALLOC_SCRATCH_BYTES
+    assert ops.decode_attn_workspace_bytes(q, kc, vc, sl, num_ctas=4096) > _native.NOALLOC_SCRATCH_BYTES
     out = torch.zeros_like(q)
-    st = _call_noalloc(q, kc, vc, sl, out, -1, 16)
+    st = _call_noalloc(q, kc, vc, sl, out, -1, 4096)
     assert st == _native.MCB_ERR_WORKSPACE
     assert "static scratch" in _native.last_error()
     torch.cuda.synchronize()
     assert out.abs().sum().item() == 0  # nothing was enqueued
-    # with fewer splits the same shape fits and matches
-    out2 = ops.decode_attn_noalloc(q, kc, vc, sl, num_splits=2)
-    ref = ops.decode_attn(q, kc, vc, sl, num_splits=2)
+    # with fewer CTAs the same shape fits and matches
+    out2 = ops.decode_attn_noalloc(q, kc, vc, sl, num_ctas=64)
+    ref = ops.decode_attn(q, kc, vc, sl, num_ctas=64)
     assert (out2.float() - ref.float()).abs().max().item() <= ATTN_TOL

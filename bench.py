@@ -44,6 +44,9 @@ PROMPT_LEN = 512
 DECODE_LEN = 512
 CPU_SAMPLE_ROWS = 8
 FALLBACK_HBM_GBS = 6650.0
+# From the ncu capture of the split decode-attention kernel on config 2 (profiles/decode_attn_cfg2.md):
+NCU_READ_BYTES_PER_TILE_D64 = 16402   # 113.37 MB read / 6,912 fetched tiles
+NCU_WRITE_BYTES_CFG2 = 3_600_000       # mean of the two captured launches
 METRIC = "decode tokens/sec + KV-read HBM GB/s (% of peak) at 1/2/4/8 B200"
 
 
@@ -220,8 +223,16 @@ def _attention_roofline(dec, peak, reps=4):
     us = e0.elapsed_time(e1) * 1e3 / (reps * S)
     del g
     gbs = bytes_per_launch / (us * 1e-6) / 1e9
+    # DRAM traffic per launch from the ncu capture of this kernel on this model (profiles/
+    # decode_attn_cfg2.md): 16,402 bytes read per fetched 64-key tile of one kv head (K and V)
+    # plus ~3.6 MB written, scaled to the tiles this launch fetches.
+    tiles = int(sum((L + 1 + 63) // 64 for L in lens)) * H
+    traffic = tiles * NCU_READ_BYTES_PER_TILE_D64 + NCU_WRITE_BYTES_CFG2
+    ncount = ops.decode_attn_counter_count(q, cache.k_cache[0], cache.v_cache[0], cache.cache_seqlens)
+    kernel = ("mcb::decode_attn_split_kernel<64,1,16,4>" if ncount == 0 else
+              "mcb::decode_attn_kernel<64,1,16,3>")
     return {"bytes_per_launch": bytes_per_launch, "us_per_launch": us, "achieved_gbs": gbs,
-            "frac": gbs / peak, "mean_context": keys / B}
+            "frac": gbs / peak, "mean_context": keys / B, "traffic": traffic, "kernel": kernel}
 
 
 def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
@@ -439,7 +450,9 @@ def run_b200(args):
                     "mean_context": round(roof["mean_context"], 1)},
         "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1),
                      "peak": peak, "unit": "GB/s", "frac": round(roof["frac"], 4),
-                     "traffic": None, "kernel": "mcb::decode_attn_kernel<64,1,16,4>",
+                     "traffic": roof["traffic"], "kernel": roof["kernel"],
+                     "traffic_source": "ncu capture of this kernel on this model at context 516 "
+                                       "(profiles/decode_attn_cfg2.md), scaled by fetched 64-key tiles",
                      "algorithmic_bytes_per_launch": roof["bytes_per_launch"],
                      "us_per_launch": round(roof["us_per_launch"], 2),
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},

@@ -197,6 +197,12 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ct
     return args
 
 
+def decode_attn_counter_count(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0):
+    """Arrival counters the launch plan needs (0: the split plan, which uses none)."""
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None)
+    return int(_native.load().mcb_decode_attn_counter_count(ctypes.byref(args)))
+
+
 def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0):
     args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None)
     return int(_native.load().mcb_decode_attn_workspace_size(ctypes.byref(args)))

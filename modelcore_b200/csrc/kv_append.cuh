@@ -12,11 +12,15 @@
 //   norm   (F.rms_norm, modelcore/components/norm.py:43-44): fp32 sum of squares, then
 //            z = bf16(y * rsqrt(sum/D + eps)),  eps = fp32 machine epsilon when None
 //   scale  (modelcore/components/attention.py:149-150): out = bf16(z * 1.2f)
-// The fp32 sum of squares has a fixed order: lane l adds y1^2 then y2^2 for its pairs
-// i = l, l+32, ... in increasing i, then the 32 lane sums are combined by an xor butterfly over
-// lane masks 16, 8, 4, 2, 1.  The CPU oracle restates exactly that order, so kernel and oracle
-// agree bit for bit; against torch's own reduction order the result can differ by one bf16 ulp
-// in rare elements (reduction order only).
+// Two kernels, one arithmetic.  For D a power of two in [16, 256] (every head size modelcore
+// configs use) kv_append_rope_vec_kernel gives each vector L = D/16 lanes that move 16-byte
+// chunks: lane i owns the pairs 8i .. 8i+7, and the fp32 sum of squares adds, per lane, y1^2 then
+// y2^2 for its pairs in increasing order, then combines the L lane sums by an xor butterfly over
+// masks L/2, .., 1.  For other D kv_append_rope_kernel uses one warp per vector: lane l adds
+// y1^2 then y2^2 for its pairs i = l, l+32, ... in increasing i, then a butterfly over masks
+// 16 .. 1.  The CPU oracle restates both orders, so kernel and oracle agree bit for bit; against
+// torch's own reduction order the result can differ by one bf16 ulp in rare elements (reduction
+// order only).
 #pragma once
 
 #include "common.cuh"
@@ -132,6 +136,114 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
       dst[i] = float_to_bf16_bits(__fmul_rn(z1, p.scale));
       dst[i + half] = float_to_bf16_bits(__fmul_rn(z2, p.scale));
     }
+  }
+}
+
+// 8 bf16 (one 16-byte chunk) <-> 8 floats
+__device__ __forceinline__ void unpack8(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  return v;
+}
+
+// Vectorised variant: L = D/16 lanes per vector, 16-byte loads and stores, 32/L vectors per warp.
+// Requires 16-byte aligned rows (checked on the host).
+template <int D>
+__global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
+    kv_append_rope_vec_kernel(const AppendParams p) {
+  constexpr int L = D / 16;        // lanes per vector
+  constexpr int VPW = 32 / L;      // vectors per warp
+  constexpr int HALF = D / 2;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % L;        // chunk index within the half
+  const long long w = (static_cast<long long>(blockIdx.x) * kAppendWarpsPerBlock + (threadIdx.x >> 5)) * VPW +
+                      lane / L;
+  const bool active = w < p.total_vectors;
+  const long long wv = active ? w : 0;
+  const int per_bt = p.nq + 2 * p.nk;
+  const int j = static_cast<int>(wv % per_bt);
+  const long long bt = wv / per_bt;
+  const int t = static_cast<int>(bt % p.T);
+  const int b = static_cast<int>(bt / p.T);
+  const int pos = p.cache_seqlens[b] + t;
+
+  const bool is_v = j >= p.nq + p.nk;
+  const bool is_q = j < p.nq;
+  const int h = is_q ? j : (is_v ? j - p.nq - p.nk : j - p.nq);
+  const uint16_t* src = is_q ? p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2]
+                             : (is_v ? p.v + b * p.vs[0] + t * p.vs[1] + h * p.vs[2]
+                                     : p.k + b * p.ks[0] + t * p.ks[1] + h * p.ks[2]);
+  bool ok = active;
+  uint16_t* dst = nullptr;
+  if (is_q) {
+    dst = p.q_out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D;
+  } else {
+    if (pos < 0 || pos >= p.Tmax) {
+      if (active && sub == 0) record_error(kErrPositionBeyondCache);
+      ok = false;
+    } else {
+      dst = (is_v ? p.v_cache : p.k_cache) + ((static_cast<long long>(b) * p.Tmax + pos) * p.Hkv + h) * D;
+    }
+  }
+  const bool rotate = is_q || (!is_v && p.rotate_k);
+  if (ok && rotate && (pos < 0 || pos >= p.rot_len)) {
+    if (sub == 0) record_error(kErrPositionBeyondRotary);
+    ok = false;
+  }
+
+  const uint4 x1v = ok ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
+  const uint4 x2v = ok ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
+  if (!rotate) {  // value heads and raw key inserts: a copy
+    if (ok) {
+      *reinterpret_cast<uint4*>(dst + 8 * sub) = x1v;
+      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = x2v;
+    }
+    // lanes of a rotating vector in this warp still take part in the butterfly below
+  }
+  float y1[8], y2[8];
+  float acc = 0.f;
+  if (rotate && ok) {
+    float x1[8], x2[8], c[8], sn[8];
+    unpack8(x1v, x1);
+    unpack8(x2v, x2);
+    const long long trow = static_cast<long long>(pos) * HALF + 8 * sub;
+    unpack8(*reinterpret_cast<const uint4*>(p.cos + trow), c);
+    unpack8(*reinterpret_cast<const uint4*>(p.sin + trow), sn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = round_bf16(__fmul_rn(x1[i], c[i]));
+      const float bb = round_bf16(__fmul_rn(x2[i], sn[i]));
+      const float cc = round_bf16(__fmul_rn(x1[i], -sn[i]));
+      const float dd = round_bf16(__fmul_rn(x2[i], c[i]));
+      y1[i] = round_bf16(__fadd_rn(a, bb));
+      y2[i] = round_bf16(__fadd_rn(cc, dd));
+      acc = __fadd_rn(acc, __fmul_rn(y1[i], y1[i]));
+      acc = __fadd_rn(acc, __fmul_rn(y2[i], y2[i]));
+    }
+  }
+#pragma unroll
+  for (int m = L / 2; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  if (rotate && ok) {
+    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(D)), p.eps));
+    float o1[8], o2[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o1[i] = __fmul_rn(round_bf16(__fmul_rn(y1[i], r)), p.scale);
+      o2[i] = __fmul_rn(round_bf16(__fmul_rn(y2[i], r)), p.scale);
+    }
+    *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
+    *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
   }
 }
 

@@ -428,10 +428,37 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   p.rotate_k = rk;
   p.total_vectors = static_cast<long long>(a->B) * a->T * (p.nq + 2 * p.nk);
   if (p.total_vectors == 0) return MCB_OK;
+  // 16-byte chunks when every row the kernel touches starts on a 16-byte boundary.
+  bool vec = (a->D == 16 || a->D == 32 || a->D == 64 || a->D == 128 || a->D == 256);
+  auto rows16 = [](const void* ptr, const int64_t* st) {
+    return aligned(ptr, 16) && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0;
+  };
+  if (rq) vec = vec && rows16(a->q, a->q_stride) && aligned(a->q_out, 16);
+  if (wkv) vec = vec && rows16(a->k, a->k_stride) && rows16(a->v, a->v_stride) &&
+                 aligned(a->k_cache, 16) && aligned(a->v_cache, 16);
+  if (rq || rk) vec = vec && aligned(a->cos, 16) && aligned(a->sin, 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vec) {
+    const long long vpw = 32 / (a->D / 16);
+    const long long warps = (p.total_vectors + vpw - 1) / vpw;
+    const long long blocks = (warps + mcb::kAppendWarpsPerBlock - 1) / mcb::kAppendWarpsPerBlock;
+    if (blocks > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: grid too large");
+    const dim3 grid(static_cast<unsigned>(blocks)), block(mcb::kAppendWarpsPerBlock * 32);
+    switch (a->D) {
+      case 16: mcb::kv_append_rope_vec_kernel<16><<<grid, block, 0, st>>>(p); break;
+      case 32: mcb::kv_append_rope_vec_kernel<32><<<grid, block, 0, st>>>(p); break;
+      case 64: mcb::kv_append_rope_vec_kernel<64><<<grid, block, 0, st>>>(p); break;
+      case 128: mcb::kv_append_rope_vec_kernel<128><<<grid, block, 0, st>>>(p); break;
+      default: mcb::kv_append_rope_vec_kernel<256><<<grid, block, 0, st>>>(p); break;
+    }
+    g_launches++;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "kv_append_rope launch");
+    return MCB_OK;
+  }
   const long long blocks = (p.total_vectors + mcb::kAppendWarpsPerBlock - 1) / mcb::kAppendWarpsPerBlock;
   if (blocks > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: grid too large");
-  mcb::kv_append_rope_kernel<<<static_cast<unsigned>(blocks), mcb::kAppendWarpsPerBlock * 32, 0,
-                               static_cast<cudaStream_t>(stream)>>>(p);
+  mcb::kv_append_rope_kernel<<<static_cast<unsigned>(blocks), mcb::kAppendWarpsPerBlock * 32, 0, st>>>(p);
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kv_append_rope launch");

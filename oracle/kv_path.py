@@ -11,10 +11,10 @@ round-to-nearest-even.  Parity is pinned by tests/test_oracle_golden.py against 
 that tests/golden/make_golden.py produced by running the reference itself.
 
 The one place where bit-exactness against torch is not defined is the fp32 sum of squares
-inside rms_norm: torch's reduction order is an implementation detail.  `rms_norm_scale` fixes an
-order (the one the CUDA kernel uses: per-lane partial sums over pairs (i, i + D/2), i = lane +
-32*u, then an xor butterfly over 32 lanes), so the kernel matches this oracle bit for bit and the
-reference to within one bf16 ulp on rare elements.
+inside rms_norm: torch's reduction order is an implementation detail.  `rms_norm_scale` fixes the
+order the CUDA kernels use (per-lane partial sums over pairs (i, i + D/2), then an xor butterfly;
+see `sum_squares_kernel_order`), so the kernels match this oracle bit for bit and the reference to
+within one bf16 ulp on rare elements.
 """
 import numpy as np
 
@@ -73,22 +73,33 @@ def rope(x_bits, cos_bits, sin_bits):
 # RMSNorm + scale: modelcore/components/norm.py:43-44 (F.rms_norm, eps=None -> the fp32 machine
 # epsilon for bf16 input) and modelcore/components/attention.py:149-150 (x 1.2)
 def sum_squares_kernel_order(y):
-    """fp32 sum of y^2 over the last axis in the CUDA kernel's fixed order (see module doc)."""
+    """fp32 sum of y^2 over the last axis in the CUDA kernels' fixed order.
+
+    D a power of two in [16, 256] (the vectorised kernel): L = D/16 lanes; lane i adds y1^2 then
+    y2^2 for its pairs 8i .. 8i+7 (pair p = (y[p], y[p + D/2])) in increasing order; the L lane
+    sums combine by an xor butterfly over masks L/2 .. 1.  Other D (one warp per vector): lane l
+    adds y1^2 then y2^2 for its pairs l, l+32, ..; the 32 lane sums combine over masks 16 .. 1."""
     y = np.asarray(y, dtype=np.float32)
     D = y.shape[-1]
     half = D // 2
     lead = y.shape[:-1]
-    acc = np.zeros(lead + (32,), dtype=np.float32)
-    for u in range(4):
-        for lane in range(32):
-            i = lane + 32 * u
-            if i < half:
-                a = y[..., i]
-                b = y[..., i + half]
-                acc[..., lane] = acc[..., lane] + a * a
-                acc[..., lane] = acc[..., lane] + b * b
-    for m in (16, 8, 4, 2, 1):
-        acc = acc + acc[..., np.arange(32) ^ m]
+    if D in (16, 32, 64, 128, 256):
+        lanes = D // 16
+        pairs = [[8 * i + j for j in range(8)] for i in range(lanes)]
+        masks = [m for m in (8, 4, 2, 1) if m < lanes]
+    else:
+        lanes = 32
+        pairs = [[lane + 32 * u for u in range(4) if lane + 32 * u < half] for lane in range(32)]
+        masks = [16, 8, 4, 2, 1]
+    acc = np.zeros(lead + (lanes,), dtype=np.float32)
+    for lane in range(lanes):
+        for i in pairs[lane]:
+            a = y[..., i]
+            b = y[..., i + half]
+            acc[..., lane] = acc[..., lane] + a * a
+            acc[..., lane] = acc[..., lane] + b * b
+    for m in masks:
+        acc = acc + acc[..., np.arange(lanes) ^ m]
     return acc[..., 0]
 
 

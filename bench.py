@@ -170,11 +170,12 @@ def _barrier(world):
     torch.cuda.synchronize()
 
 
-def _build_decoder(rank, world, steps_needed):
+def _build_decoder(rank, world, steps_needed, fuse_step=True):
     import torch
     import modelcore_b200
     from modelcore_b200 import workloads
     mgr = modelcore_b200.ModelManager()
+    mgr.fuse_step = fuse_step
     model = mgr.create_model(workloads.quickstart_config(), device=torch.device("cuda"), seed=0)
     model = model.to(torch.bfloat16).eval()
     from modelcore_b200.sharding import contiguous_rows
@@ -438,7 +439,7 @@ def run_b200(args):
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
     steps_needed = 1 + args.warmup + args.steps + args.e2e_steps + 2
-    mgr, model, dec = _build_decoder(rank, world, steps_needed)
+    mgr, model, dec = _build_decoder(rank, world, steps_needed, fuse_step=args.step == "fused")
     cache = dec.kv_cache
     B = cache.batch_size
 
@@ -515,6 +516,10 @@ def run_b200(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded uniform token ids, random-init weights)",
         "config": _config(world),
+        "decode_step": {"fused": "packed QKV and gate|up GEMMs; residual add + norm and silu * up "
+                                 "on libmcb200",
+                        "plain": "modelcore's op-by-op forward around the libmcb200 append and "
+                                 "attention"}[args.step],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
                     "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
                     "attention_kernel_gbs": round(roof["achieved_gbs"], 1),
@@ -547,6 +552,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--step", choices=("fused", "plain"), default="fused",
+                    help="decode step around attention: fused (default) or modelcore's op-by-op")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")

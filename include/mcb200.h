@@ -191,6 +191,41 @@ int mcb_decode_attn(const mcb_attn_args* args, void* stream);
 int mcb_decode_attn_noalloc(const mcb_attn_args* args, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * The decode step either side of attention (one launch each, any number of rows):
+ *
+ * mcb_add_rms_norm: x_out = x + delta; h_out = rms_norm(x_out) (delta NULL: h_out = rms_norm(x)).
+ * Replaces the residual add of Block.forward followed by the next norm() call,
+ * modelcore/components/block.py:57-59 with RMSNorm.forward, modelcore/components/norm.py:43-44.
+ * The add rounds once to bf16; the norm accumulates in fp32 and rounds once (eps as for
+ * mcb_append_args).  x_out may alias x.  C a multiple of 8, at most 4096; rows 16-byte aligned.
+ *
+ * mcb_gated_silu: out = silu(gate) * up, silu in fp32 rounded to bf16, product rounded to bf16.
+ * Replaces GatedMLP.forward's act(gate_proj(x)) * up_proj(x) for activation "silu",
+ * modelcore/components/mlp.py:89-90.  H a multiple of 8; rows 16-byte aligned.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* x;              /* (rows, C) bf16 residual stream                             */
+  const void* delta;          /* (rows, C) bf16 to add, or NULL                             */
+  void* x_out;                /* (rows, C) bf16 x + delta (NULL when delta is NULL)         */
+  void* h_out;                /* (rows, C) bf16 rms_norm(x + delta)                         */
+  int64_t x_stride, delta_stride, x_out_stride, h_stride;  /* row strides, elements          */
+  int32_t rows, C;
+  float eps;
+} mcb_add_norm_args;
+
+int mcb_add_rms_norm(const mcb_add_norm_args* args, void* stream);
+
+typedef struct {
+  const void* gate;           /* (rows, H) bf16                                             */
+  const void* up;             /* (rows, H) bf16                                             */
+  void* out;                  /* (rows, H) bf16                                             */
+  int64_t gate_stride, up_stride, out_stride;  /* row strides, elements                     */
+  int32_t rows, H;
+} mcb_gated_silu_args;
+
+int mcb_gated_silu(const mcb_gated_silu_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
  * overflow) or a timed-out pipeline wait sets a device error word and skips the access.
  * mcb_device_error synchronises `stream`, returns the word in *code and clears it.

@@ -51,6 +51,8 @@ EXPORTED_SYMBOLS = (
     "mcb_decode_attn_counter_count",
     "mcb_decode_attn",
     "mcb_decode_attn_noalloc",
+    "mcb_add_rms_norm",
+    "mcb_gated_silu",
     "mcb_device_error",
     "mcb_launch_count",
 )
@@ -101,6 +103,24 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+class AddNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("delta", ctypes.c_void_p), ("x_out", ctypes.c_void_p),
+        ("h_out", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64), ("delta_stride", ctypes.c_int64),
+        ("x_out_stride", ctypes.c_int64), ("h_stride", ctypes.c_int64),
+        ("rows", ctypes.c_int32), ("C", ctypes.c_int32), ("eps", ctypes.c_float),
+    ]
+
+
+class GatedSiluArgs(ctypes.Structure):
+    _fields_ = [
+        ("gate", ctypes.c_void_p), ("up", ctypes.c_void_p), ("out", ctypes.c_void_p),
+        ("gate_stride", ctypes.c_int64), ("up_stride", ctypes.c_int64), ("out_stride", ctypes.c_int64),
+        ("rows", ctypes.c_int32), ("H", ctypes.c_int32),
+    ]
+
+
 class McbError(RuntimeError):
     """A C-ABI call returned a non-zero mcb_status."""
 
@@ -133,6 +153,10 @@ def _declare(lib):
     lib.mcb_decode_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]
     lib.mcb_decode_attn_noalloc.restype = ctypes.c_int
     lib.mcb_decode_attn_noalloc.argtypes = [P(AttnArgs), ctypes.c_void_p]
+    lib.mcb_add_rms_norm.restype = ctypes.c_int
+    lib.mcb_add_rms_norm.argtypes = [P(AddNormArgs), ctypes.c_void_p]
+    lib.mcb_gated_silu.restype = ctypes.c_int
+    lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
     lib.mcb_device_error.restype = ctypes.c_int
     lib.mcb_device_error.argtypes = [P(ctypes.c_int32), ctypes.c_void_p]
     lib.mcb_launch_count.restype = ctypes.c_uint64

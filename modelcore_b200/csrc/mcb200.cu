@@ -15,6 +15,7 @@
 #include "decode_attn_split.cuh"
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
+#include "step_fused.cuh"
 
 namespace {
 
@@ -516,6 +517,74 @@ int mcb_kv_copy_rows(const mcb_copy_args* a, void* stream) {
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kv_copy_rows launch");
+  return MCB_OK;
+}
+
+int mcb_add_rms_norm(const mcb_add_norm_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_add_rms_norm: args is NULL");
+  if (a->rows < 0 || a->C <= 0 || a->C % 8 != 0 || a->C > 4096)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_add_rms_norm: C=%d must be a positive multiple of 8, at most 4096",
+                a->C);
+  if (a->x == nullptr || a->h_out == nullptr || (a->delta != nullptr && a->x_out == nullptr))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_add_rms_norm: NULL pointer argument");
+  const bool ok16 = aligned(a->x, 16) && aligned(a->h_out, 16) && a->x_stride % 8 == 0 &&
+                    a->h_stride % 8 == 0 &&
+                    (a->delta == nullptr ||
+                     (aligned(a->delta, 16) && aligned(a->x_out, 16) && a->delta_stride % 8 == 0 &&
+                      a->x_out_stride % 8 == 0));
+  if (!ok16) return fail(MCB_ERR_ALIGNMENT, "mcb_add_rms_norm: rows must start on 16-byte boundaries");
+  if (a->rows == 0) return MCB_OK;
+  mcb::AddNormParams p;
+  p.x = static_cast<const uint16_t*>(a->x);
+  p.delta = static_cast<const uint16_t*>(a->delta);
+  p.x_out = a->delta ? static_cast<uint16_t*>(a->x_out) : nullptr;
+  p.h_out = static_cast<uint16_t*>(a->h_out);
+  p.xs = a->x_stride;
+  p.ds = a->delta_stride;
+  p.xos = a->x_out_stride;
+  p.hs = a->h_stride;
+  p.rows = a->rows;
+  p.C = a->C;
+  p.eps = a->eps;
+  const int chunks = a->C / 8;
+  const dim3 grid((a->rows + 3) / 4), block(128);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (chunks <= 32) mcb::add_rms_norm_kernel<1><<<grid, block, 0, st>>>(p);
+  else if (chunks <= 64) mcb::add_rms_norm_kernel<2><<<grid, block, 0, st>>>(p);
+  else if (chunks <= 128) mcb::add_rms_norm_kernel<4><<<grid, block, 0, st>>>(p);
+  else if (chunks <= 256) mcb::add_rms_norm_kernel<8><<<grid, block, 0, st>>>(p);
+  else mcb::add_rms_norm_kernel<16><<<grid, block, 0, st>>>(p);
+  g_launches++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "add_rms_norm launch");
+  return MCB_OK;
+}
+
+int mcb_gated_silu(const mcb_gated_silu_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_gated_silu: args is NULL");
+  if (a->rows < 0 || a->H <= 0 || a->H % 8 != 0)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_gated_silu: H=%d must be a positive multiple of 8", a->H);
+  if (a->gate == nullptr || a->up == nullptr || a->out == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_gated_silu: NULL pointer argument");
+  if (!aligned(a->gate, 16) || !aligned(a->up, 16) || !aligned(a->out, 16) || a->gate_stride % 8 ||
+      a->up_stride % 8 || a->out_stride % 8)
+    return fail(MCB_ERR_ALIGNMENT, "mcb_gated_silu: rows must start on 16-byte boundaries");
+  if (a->rows == 0) return MCB_OK;
+  mcb::GatedActParams p;
+  p.gate = static_cast<const uint16_t*>(a->gate);
+  p.up = static_cast<const uint16_t*>(a->up);
+  p.out = static_cast<uint16_t*>(a->out);
+  p.gs = a->gate_stride;
+  p.us = a->up_stride;
+  p.os = a->out_stride;
+  p.rows = a->rows;
+  p.H = a->H;
+  const long long total = static_cast<long long>(a->rows) * (a->H / 8);
+  mcb::gated_silu_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(p);
+  g_launches++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gated_silu launch");
   return MCB_OK;
 }
 

@@ -18,11 +18,12 @@ import types
 
 import torch
 
-from . import ops
+from . import ops, step
 from .cache import KVCache
 from .flash_attn import flash_attn_with_kvcache
 
 _ORIGINAL_FORWARD = "_mcb_original_forward"
+_FUSE_QKV = "_mcb_fuse_qkv"
 
 
 def _fusable(attn, x):
@@ -50,15 +51,23 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
     if kv_cache is None or not isinstance(kv_cache, KVCache):
         return getattr(self, _ORIGINAL_FORWARD)(x, idx, kv_cache, kv_bus, doc_args)
     B, T, C = x.size()
-    q = self.c_q(x).view(B, T, self.n_head, self.head_dim)
+    fused = _fusable(self, x)
+    qkv = None
+    if fused and self.produces_kv and getattr(self, _FUSE_QKV, False):
+        qkv = step.qkv_projection(self, x)  # q, k, v as views of one GEMM's output
+    if qkv is not None:
+        q, k, v = qkv
+    else:
+        q = self.c_q(x).view(B, T, self.n_head, self.head_dim)
     k_cache, v_cache = kv_cache.get_slot_cache(self.kv_slot)
     seqlens = kv_cache.cache_seqlens
-    if _fusable(self, x):
+    if fused:
         rope = self.rope
         kv_cache.check_room(T, rope.cos.size(1))
         if self.produces_kv:
-            k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
-            v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
+            if qkv is None:
+                k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
+                v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
             v = self._hook("values", v, x, idx)
             q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
                                    rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
@@ -91,25 +100,36 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
     return self.c_proj(y)
 
 
-def install(model):
+def install(model, fuse_step=True):
     """Binds attention_forward to every modelcore Attention module of `model`; returns the
-    number of modules changed.  Idempotent."""
+    number of modules changed.  With fuse_step, producer layers project q, k, v with one GEMM
+    and, where the model's structure qualifies, the body runs modelcore_b200.step.stack_forward
+    (residual add + norm and the gated MLP fused); fuse_step=False keeps modelcore's op-by-op
+    forward around the libmcb200 attention.  Idempotent; a second call only changes fuse_step."""
     from modelcore.components.attention import Attention
     n = 0
     for m in model.modules():
-        if isinstance(m, Attention) and not hasattr(m, _ORIGINAL_FORWARD):
-            object.__setattr__(m, _ORIGINAL_FORWARD, m.forward)
-            object.__setattr__(m, "forward", types.MethodType(attention_forward, m))
-            n += 1
+        if isinstance(m, Attention):
+            if not hasattr(m, _ORIGINAL_FORWARD):
+                object.__setattr__(m, _ORIGINAL_FORWARD, m.forward)
+                object.__setattr__(m, "forward", types.MethodType(attention_forward, m))
+                n += 1
+            object.__setattr__(m, _FUSE_QKV, bool(fuse_step))
+    if fuse_step:
+        step.install(model)
+    else:
+        step.uninstall(model)
     return n
 
 
 def uninstall(model):
     from modelcore.components.attention import Attention
+    step.uninstall(model)
     for m in model.modules():
         if isinstance(m, Attention) and hasattr(m, _ORIGINAL_FORWARD):
             object.__setattr__(m, "forward", getattr(m, _ORIGINAL_FORWARD))
             object.__delattr__(m, _ORIGINAL_FORWARD)
+            object.__delattr__(m, _FUSE_QKV)
 
 
 def _manager_base():
@@ -118,14 +138,16 @@ def _manager_base():
 
 
 class _ManagerMixin:
+    fuse_step = True  # install(model, fuse_step) for the models this manager returns
+
     def create_model(self, *args, **kwargs):
         model = super().create_model(*args, **kwargs)
-        install(model)
+        install(model, fuse_step=self.fuse_step)
         return model
 
     def load_model(self, *args, **kwargs):
         model = super().load_model(*args, **kwargs)
-        install(model)
+        install(model, fuse_step=self.fuse_step)
         return model
 
     def new_kv_cache(self, model, *, batch_size, seq_len, device=None):

@@ -12,7 +12,7 @@ import math
 import torch
 
 from . import _native
-from ._native import AppendArgs, AttnArgs, CopyArgs, check
+from ._native import AddNormArgs, AppendArgs, AttnArgs, CopyArgs, GatedSiluArgs, check
 
 
 def _stream(t):
@@ -296,6 +296,60 @@ def decode_attn_noalloc(q, k_cache, v_cache, cache_seqlens, *, window=-1, softma
             raise RuntimeError("out must be a contiguous tensor shaped like q")
     args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out)
     check(_native.load().mcb_decode_attn_noalloc(ctypes.byref(args), _stream(q)))
+    return out
+
+
+def _rows2d(name, t):
+    _need(name, t, 2)
+    if t.stride(1) != 1:
+        raise RuntimeError(f"{name} must have unit stride on its last dim")
+    return t.stride(0)
+
+
+def add_rms_norm(x, delta=None, *, eps=None, x_out=None, h_out=None):
+    """x' = x + delta (bf16), h = rms_norm(x') (bf16): Block's residual add fused with the next
+    norm (modelcore/components/block.py:57-59, norm.py:43-44).  x, delta: (rows, C) bf16.
+    Returns (x', h); with delta None returns (x, rms_norm(x)).  x_out may be x (in place)."""
+    rows, C = x.shape
+    args = AddNormArgs()
+    args.x = x.data_ptr()
+    args.x_stride = _rows2d("x", x)
+    if h_out is None:
+        h_out = torch.empty((rows, C), dtype=torch.bfloat16, device=x.device)
+    args.h_out = h_out.data_ptr()
+    args.h_stride = _rows2d("h_out", h_out)
+    if delta is not None:
+        if tuple(delta.shape) != (rows, C):
+            raise RuntimeError(f"delta must be ({rows}, {C}), got {tuple(delta.shape)}")
+        args.delta = delta.data_ptr()
+        args.delta_stride = _rows2d("delta", delta)
+        if x_out is None:
+            x_out = torch.empty((rows, C), dtype=torch.bfloat16, device=x.device)
+        args.x_out = x_out.data_ptr()
+        args.x_out_stride = _rows2d("x_out", x_out)
+    else:
+        x_out = x
+    args.rows, args.C = rows, C
+    args.eps = rms_norm_eps(eps)
+    check(_native.load().mcb_add_rms_norm(ctypes.byref(args), _stream(x)))
+    return x_out, h_out
+
+
+def gated_silu(gate, up, out=None):
+    """silu(gate) * up in bf16 (GatedMLP with activation "silu", modelcore/components/mlp.py:89-90);
+    gate, up: (rows, H) bf16, e.g. the two halves of one fused gate|up projection."""
+    rows, H = gate.shape
+    if tuple(up.shape) != (rows, H):
+        raise RuntimeError("gate and up must have equal shapes")
+    if out is None:
+        out = torch.empty((rows, H), dtype=torch.bfloat16, device=gate.device)
+    args = GatedSiluArgs()
+    args.gate, args.up, args.out = gate.data_ptr(), up.data_ptr(), out.data_ptr()
+    args.gate_stride = _rows2d("gate", gate)
+    args.up_stride = _rows2d("up", up)
+    args.out_stride = _rows2d("out", out)
+    args.rows, args.H = rows, H
+    check(_native.load().mcb_gated_silu(ctypes.byref(args), _stream(gate)))
     return out
 
 

@@ -133,6 +133,42 @@ def rope_tables_at(cos_bits, sin_bits, cache_seqlens, T):
 
 
 # ---------------------------------------------------------------------------------------------
+# The decode step either side of attention
+def add_rms_norm(x_bits, delta_bits=None, eps=None):
+    """Block's residual add then norm (modelcore/components/block.py:57-59, norm.py:43-44):
+    x' = bf16(x + delta), h = bf16(x' * rsqrt(sum(x'^2)/C + eps)) with the fp32 sum in the
+    kernel's order (lane l: its 8-element chunks l, l+32, .., element by element; then an xor
+    butterfly over 32 lanes).  Returns (x' bits, h bits)."""
+    x = bf16_to_f32(x_bits)
+    if delta_bits is not None:
+        x = round_bf16((x + bf16_to_f32(delta_bits)).astype(np.float32))
+    C = x.shape[-1]
+    lead = x.shape[:-1]
+    acc = np.zeros(lead + (32,), dtype=np.float32)
+    for lane in range(32):
+        for c in range(lane, C // 8, 32):
+            for i in range(8):
+                v = x[..., 8 * c + i]
+                acc[..., lane] = acc[..., lane] + v * v
+    for m in (16, 8, 4, 2, 1):
+        acc = acc + acc[..., np.arange(32) ^ m]
+    e = F32(np.finfo(np.float32).eps if eps is None else eps)
+    v = ((acc[..., 0] / F32(C)).astype(np.float32) + e).astype(np.float32)
+    r = (np.longdouble(1.0) / np.sqrt(v.astype(np.longdouble))).astype(np.float32)
+    return f32_to_bf16(x), f32_to_bf16((x * r[..., None]).astype(np.float32))
+
+
+def gated_silu(gate_bits, up_bits):
+    """GatedMLP's silu(gate) * up (modelcore/components/mlp.py:89-90): silu in fp32 as
+    g / (1 + exp(-g)) rounded to bf16, the product rounded to bf16.  numpy's exp may differ from
+    the device's expf by an fp32 ulp, which can move a bf16 rounding (tests allow one bf16 ulp)."""
+    g = bf16_to_f32(gate_bits)
+    u = bf16_to_f32(up_bits)
+    s = round_bf16((g / (F32(1.0) + np.exp(-g))).astype(np.float32))
+    return f32_to_bf16((s * u).astype(np.float32))
+
+
+# ---------------------------------------------------------------------------------------------
 # The insert of flash_attn_with_kvcache: modelcore/kernels/flash_attn.py:337-346
 def kv_insert(k_cache, v_cache, k, v, cache_seqlens):
     """In place: row b's new tokens land at [cache_seqlens[b], cache_seqlens[b] + T)."""

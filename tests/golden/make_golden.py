@@ -18,6 +18,10 @@ Fixtures:
                             (modelcore/kernels/flash_attn.py:306-366), ragged and uniform rows,
                             windows -1 / 8, T_new 1 / 3, MHA and GQA
   prefill.npz               KVCache.prefill broadcast and prefill_row (modelcore/cache.py:75-119)
+  step_fused.npz            Block's residual add + RMSNorm(eps=None) in bf16 (modelcore/components/
+                            block.py:57-59, norm.py:43-44) for C in 40 / 768 / 2048 / 4096, and
+                            GatedMLP's act(gate) * up with activation "silu" in bf16
+                            (modelcore/components/mlp.py:89-90)
   decode_cfg1.npz           the README quickstart model (fp32, seed 0), prompts (2, 16) from seed 1,
                             64 greedy steps through Decoder: the token streams, for the plain
                             random init and for the awake init of
@@ -159,6 +163,29 @@ def make_prefill(out_dir):
              rows_seqlens=rows.cache_seqlens.numpy())
 
 
+def make_step_fused(out_dir):
+    import torch
+    from modelcore.components.mlp import GatedMLP
+    from modelcore.components.norm import RMSNorm
+
+    out = {}
+    norm = RMSNorm(eps=None)
+    g = torch.Generator().manual_seed(zlib.crc32(b"step_fused"))
+    for C in (40, 768, 2048, 4096):
+        rows = 37
+        x = (torch.randn(rows, C, generator=g) * 3).to(torch.bfloat16)
+        d = (torch.randn(rows, C, generator=g) * 0.5).to(torch.bfloat16)
+        x1 = x + d
+        out[f"x_C{C}"], out[f"delta_C{C}"] = bits(x), bits(d)
+        out[f"sum_C{C}"], out[f"norm_C{C}"] = bits(x1), bits(norm(x1))
+        out[f"norm_only_C{C}"] = bits(norm(x))
+    mlp = GatedMLP(n_embd=64, activation="silu", hidden_dim=2048)
+    gate = (torch.randn(16, 2048, generator=g) * 6).to(torch.bfloat16)
+    up = torch.randn(16, 2048, generator=g).to(torch.bfloat16)
+    out["gate"], out["up"], out["gated"] = bits(gate), bits(up), bits(mlp.act(gate) * up)
+    np.savez_compressed(os.path.join(out_dir, "step_fused.npz"), **out)
+
+
 def quickstart_config():
     from modelcore import ComponentSpec, ModelConfig
     head_dim = 64
@@ -227,6 +254,7 @@ def main():
     make_rope_norm(args.out)
     make_kv_attn(args.out)
     make_prefill(args.out)
+    make_step_fused(args.out)
     if not args.skip_decode:
         make_decode_cfg1(args.out)
     print("wrote fixtures to", args.out)

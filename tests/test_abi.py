@@ -10,7 +10,7 @@ import pytest
 
 from conftest import REPO
 from modelcore_b200 import _native
-from modelcore_b200._native import AppendArgs, AttnArgs, CopyArgs
+from modelcore_b200._native import AddNormArgs, AppendArgs, AttnArgs, CopyArgs, GatedSiluArgs
 
 HEADER = os.path.join(REPO, "include", "mcb200.h")
 
@@ -50,7 +50,8 @@ def _c_layout(struct, fields):
 
 
 @pytest.mark.parametrize("cls,cname", [(AppendArgs, "mcb_append_args"), (CopyArgs, "mcb_copy_args"),
-                                       (AttnArgs, "mcb_attn_args")])
+                                       (AttnArgs, "mcb_attn_args"), (AddNormArgs, "mcb_add_norm_args"),
+                                       (GatedSiluArgs, "mcb_gated_silu_args")])
 def test_ctypes_structures_match_the_c_layout(cls, cname):
     fields = [f for f, _ in cls._fields_]
     c = _c_layout(cname, fields)
@@ -159,3 +160,26 @@ def test_advance_rejects_null():
     lib = _native.load()
     st, _ = _err(lib.mcb_kv_advance(None, 4, 1, None))
     assert st == _native.MCB_ERR_INVALID_ARG
+
+
+def test_step_kernels_validate_on_the_host():
+    """Shape and alignment errors are reported before any launch (no device needed)."""
+    lib = _native.load()
+    MCB_ERR_UNSUPPORTED, MCB_ERR_ALIGNMENT = _native.MCB_ERR_UNSUPPORTED, _native.MCB_ERR_ALIGNMENT
+    MCB_ERR_INVALID_ARG = _native.MCB_ERR_INVALID_ARG
+    a = AddNormArgs()
+    a.x, a.h_out, a.rows, a.C = 16, 32, 4, 12
+    assert lib.mcb_add_rms_norm(ctypes.byref(a), None) == MCB_ERR_UNSUPPORTED
+    a.C = 4104
+    assert lib.mcb_add_rms_norm(ctypes.byref(a), None) == MCB_ERR_UNSUPPORTED
+    a.C, a.x = 64, 18
+    assert lib.mcb_add_rms_norm(ctypes.byref(a), None) == MCB_ERR_ALIGNMENT
+    a.x, a.delta = 16, 48          # delta without x_out
+    assert lib.mcb_add_rms_norm(ctypes.byref(a), None) == MCB_ERR_INVALID_ARG
+    g = GatedSiluArgs()
+    g.gate, g.up, g.out, g.rows, g.H = 16, 32, 48, 2, 20
+    assert lib.mcb_gated_silu(ctypes.byref(g), None) == MCB_ERR_UNSUPPORTED
+    g.H, g.gate_stride, g.up_stride, g.out_stride = 16, 20, 16, 16
+    assert lib.mcb_gated_silu(ctypes.byref(g), None) == MCB_ERR_ALIGNMENT
+    g.gate_stride, g.rows = 16, 0
+    assert lib.mcb_gated_silu(ctypes.byref(g), None) == 0   # nothing to do, nothing launched

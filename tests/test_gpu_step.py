@@ -1,0 +1,272 @@
+"""GPU parity of the decode-step kernels either side of attention, called through the C ABI
+(modelcore_b200.ops): the residual add fused with the next RMSNorm, and GatedMLP's silu(gate) * up.
+
+Bars: the add and silu * up are bit-exact against torch's own CUDA ops (one bf16 rounding per op,
+the same fp32 formulas); the norm is bit-exact against the CPU oracle, which restates the kernel's
+fp32 summation order, and within one bf16 ulp of torch's F.rms_norm and of the reference's golden
+vectors."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import load_golden
+from oracle import kv_path as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from modelcore_b200 import ops
+    return ops
+
+
+def dev_bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def host_bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def ulps(a, b):
+    return np.abs(a.astype(np.int32) - b.astype(np.int32))
+
+
+@pytest.mark.parametrize("C", [40, 768, 2048, 4096])
+def test_add_rms_norm_against_the_reference_golden_vectors(ops, C):
+    z = load_golden("step_fused.npz")
+    x, d = dev_bf16(z[f"x_C{C}"]), dev_bf16(z[f"delta_C{C}"])
+    s, h = ops.add_rms_norm(x, d)
+    torch.cuda.synchronize()
+    assert np.array_equal(host_bits(s), z[f"sum_C{C}"])
+    assert ulps(host_bits(h), z[f"norm_C{C}"]).max() <= 1
+    assert np.array_equal(host_bits(h), O.add_rms_norm(z[f"x_C{C}"], z[f"delta_C{C}"])[1])
+    _, h0 = ops.add_rms_norm(x)
+    assert np.array_equal(host_bits(h0), O.add_rms_norm(z[f"x_C{C}"])[1])
+    assert ulps(host_bits(h0), z[f"norm_only_C{C}"]).max() <= 1
+
+
+@pytest.mark.parametrize("rows,C", [(1, 8), (3, 264), (64, 768), (129, 2048), (1000, 1536),
+                                    (7, 4096)])
+def test_add_rms_norm_is_bit_exact_against_the_oracle(ops, rows, C):
+    g = torch.Generator(device="cuda").manual_seed(rows * 7919 + C)
+    x = (torch.randn(rows, C, device="cuda", generator=g) * 4).to(torch.bfloat16)
+    d = torch.randn(rows, C, device="cuda", generator=g).to(torch.bfloat16)
+    s, h = ops.add_rms_norm(x, d)
+    torch.cuda.synchronize()
+    os_, oh = O.add_rms_norm(host_bits(x), host_bits(d))
+    assert np.array_equal(host_bits(s), os_)
+    assert np.array_equal(host_bits(h), oh)
+    # against torch's CUDA ops: the add exactly, the norm within one ulp on rare elements
+    s_t = x + d
+    assert torch.equal(s, s_t)
+    diff = ulps(host_bits(h), host_bits(F.rms_norm(s_t, (C,))))
+    assert diff.max() <= 1
+    assert (diff != 0).mean() <= 5e-3
+
+
+def test_add_rms_norm_in_place_with_strided_rows(ops):
+    """x_out may alias x (the residual stream updated in place); rows may be strided views."""
+    rows, C = 33, 768
+    g = torch.Generator(device="cuda").manual_seed(5)
+    wide = (torch.randn(rows, 2 * C, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    x = wide[:, C:]
+    d = torch.randn(rows, 3 * C, device="cuda", generator=g).to(torch.bfloat16)[:, :C]
+    want_s, want_h = O.add_rms_norm(host_bits(x), host_bits(d), eps=1e-5)
+    left = wide[:, :C].clone()
+    h = torch.empty(rows, 2 * C, device="cuda", dtype=torch.bfloat16)[:, :C]
+    s, h = ops.add_rms_norm(x, d, eps=1e-5, x_out=x, h_out=h)
+    torch.cuda.synchronize()
+    assert s.data_ptr() == x.data_ptr()
+    assert np.array_equal(host_bits(x), want_s)
+    assert np.array_equal(host_bits(h), want_h)
+    assert torch.equal(wide[:, :C], left)
+
+
+@pytest.mark.parametrize("rows,H", [(16, 2048), (1, 8), (64, 5632), (333, 2048)])
+def test_gated_silu_is_bit_exact_against_torch(ops, rows, H):
+    g = torch.Generator(device="cuda").manual_seed(rows + H)
+    gu = (torch.randn(rows, 2 * H, device="cuda", generator=g) * 5).to(torch.bfloat16)
+    gate, up = gu[:, :H], gu[:, H:]      # the two halves of one fused gate|up projection
+    out = ops.gated_silu(gate, up)
+    torch.cuda.synchronize()
+    assert torch.equal(out, F.silu(gate) * up)
+    assert ulps(host_bits(out), O.gated_silu(host_bits(gate), host_bits(up))).max() <= 1
+
+
+def test_gated_silu_against_the_reference_golden_vectors(ops):
+    z = load_golden("step_fused.npz")
+    out = ops.gated_silu(dev_bf16(z["gate"]), dev_bf16(z["up"]))
+    torch.cuda.synchronize()
+    assert ulps(host_bits(out), z["gated"]).max() <= 1
+
+
+def test_step_kernels_reject_unsupported_shapes(ops):
+    from modelcore_b200._native import McbError
+    x = torch.zeros(4, 12, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(McbError, match="multiple of 8"):
+        ops.add_rms_norm(x)
+    with pytest.raises(McbError, match="at most 4096"):
+        ops.add_rms_norm(torch.zeros(2, 4104, device="cuda", dtype=torch.bfloat16))
+    y = torch.zeros(4, 24, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(McbError, match="16-byte"):
+        ops.add_rms_norm(y[:, 1:17])
+    with pytest.raises(McbError, match="multiple of 8"):
+        ops.gated_silu(x, x)
+
+
+# ---------------------------------------------------------------------------------------------
+# the fused decode step through modelcore's API (bf16 weights: the fused path's precondition)
+LOGIT_TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def env():
+    from conftest import have_modelcore
+    if not have_modelcore():
+        raise RuntimeError("modelcore (the reference package) is not importable: install it into "
+                           "baseline/_ref to run the end-to-end tests")
+    import modelcore
+    import modelcore_b200
+    return modelcore, modelcore_b200
+
+
+def _models(env, config):
+    """The reference model, the fused B200 model and the op-by-op B200 model, all with the same
+    awake bf16 weights on the GPU, plus an fp32 copy of the reference for the error yardstick."""
+    import copy
+    modelcore, mcb = env
+    from modelcore_b200 import step, workloads
+    mgr = modelcore.ModelManager()
+    cpu = workloads.awaken(mgr.create_model(config, device=torch.device("cpu"), seed=0)).eval()
+    ref = copy.deepcopy(cpu).to("cuda", torch.bfloat16)
+    fused = copy.deepcopy(cpu).to("cuda", torch.bfloat16)
+    plain = copy.deepcopy(cpu).to("cuda", torch.bfloat16)
+    mcb.install(fused, fuse_step=True)
+    mcb.install(plain, fuse_step=False)
+    assert step.installed(fused) and not step.installed(plain)
+    m32 = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
+    ref32 = m32.create_model(config, device=torch.device("cpu"), seed=0)
+    ref32.load_state_dict({k: v.float().cpu() for k, v in ref.state_dict().items()})
+    return (mgr, ref), (mcb.ModelManager(), fused), (mcb.ModelManager(), plain), (m32, ref32.to("cuda").eval())
+
+
+@torch.inference_mode()
+def _forced(mgr, model, prompts, columns):
+    dec = mgr.new_decoder(model, prompts, max_tokens=columns.shape[1])
+    out = []
+    for i in range(columns.shape[1]):
+        out.append(dec.logits.float().clone())
+        dec.step(columns[:, i].tolist())
+    out.append(dec.logits.float().clone())
+    return torch.stack(out, 1)
+
+
+def _configs():
+    from modelcore_b200 import workloads
+    return {
+        "quickstart": lambda: workloads.quickstart_config(n_layer=4),
+        "gqa_window": lambda: workloads.gqa_window_config(n_layer=4, window=16),
+        "kv_share": lambda: workloads.gqa_window_config(n_layer=4, kv_share=True, window=16),
+    }
+
+
+@pytest.mark.parametrize("name", ["quickstart", "gqa_window", "kv_share"])
+def test_fused_step_decode_is_as_accurate_as_the_reference(env, name):
+    """Right-ragged prompts, fixed token columns (teacher forcing): the fused step's logits are
+    within LOGIT_TOL of the fp32 reference and no further from it than the reference's own bf16
+    forward (x1.25 + 1e-3); the op-by-op B200 path is the same bar's control."""
+    from modelcore.tests.test_generate import RAGGED_PROMPTS
+    (rm, ref), (fm, fused), (pm, plain), (m32, ref32) = _models(env, _configs()[name]())
+    steps = 12
+    cols = torch.tensor([[(s * 7 + i * 3) % 100 + 1 for s in range(steps)]
+                         for i in range(len(RAGGED_PROMPTS))])
+    l32 = _forced(m32, ref32, RAGGED_PROMPTS, cols)
+    l_ref = _forced(rm, ref, RAGGED_PROMPTS, cols)
+    l_fused = _forced(fm, fused, RAGGED_PROMPTS, cols)
+    l_plain = _forced(pm, plain, RAGGED_PROMPTS, cols)
+    e_ref = (l_ref - l32).abs().max().item()
+    e_fused = (l_fused - l32).abs().max().item()
+    e_plain = (l_plain - l32).abs().max().item()
+    print(f"{name}: max|logits - fp32|: reference bf16 {e_ref:.3e}, fused {e_fused:.3e}, "
+          f"op-by-op {e_plain:.3e}")
+    assert e_fused <= LOGIT_TOL
+    assert e_fused <= 1.25 * e_ref + 1e-3
+
+
+def test_fused_step_launches_and_graph_replay(env):
+    """One decode step of the fused 4-layer quickstart launches the libmcb200 kernels it should
+    (per layer: append, attention, two add+norm, silu*up; plus the first norm and the advance),
+    and the CUDA-graph decoder reproduces the eager fused decoder bit for bit."""
+    modelcore, mcb = env
+    from modelcore_b200 import ops, workloads
+    mgr = mcb.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
+                                              device=torch.device("cuda"), seed=0))
+    model = model.to(torch.bfloat16).eval()
+    prompts = workloads.prompts(3, 20, seed=1).tolist()
+    prompts[2] = prompts[2][:9]
+    eager = mgr.new_decoder(model, prompts, max_tokens=16)
+    graph = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+    cols = [[1, 2, 3]] + [[(s * 5 + i) % 1000 for i in range(3)] for s in range(1, 7)]
+    with torch.inference_mode():
+        n0 = ops.launch_count()
+        eager.step(cols[0])
+        per_step = ops.launch_count() - n0
+        attn_launches = per_step - (1 + 4 * 4 + 1)   # first norm, 4 per layer, the advance
+        assert attn_launches in (4, 8), per_step     # one or two (split + combine) per layer
+        graph.step(cols[0])                           # eager: the graph decoder's first step
+        for col in cols[1:]:                          # capture, then replays
+            assert torch.equal(eager.step(col), graph.step(col))
+
+
+def test_packed_weights_follow_the_parameters(env):
+    """The packed [Wq; Wk; Wv] and [Wg; Wu] are the Parameters' own storage: the state dict keeps
+    its keys and shapes, load_state_dict lands in the packed buffer, and replacing the storage
+    (model.to) re-packs on the next forward."""
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    mgr = mcb.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=2),
+                                              device=torch.device("cuda"), seed=0))
+    model = model.to(torch.bfloat16).eval()
+    keys = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    prompts = workloads.prompts(2, 8, seed=3).tolist()
+
+    def logits():
+        with torch.inference_mode():
+            return mgr.new_decoder(model, prompts, max_tokens=4).step([5, 6]).float().clone()
+
+    first = logits()
+    attn = model.body.blocks[0].mixer
+    wq, wk = attn.c_q.weight, attn.c_k.weight
+    assert wk.data_ptr() == wq.data_ptr() + wq.numel() * wq.element_size()
+    assert {k: tuple(v.shape) for k, v in model.state_dict().items()} == keys
+    # new weights through load_state_dict: the fused forward sees them
+    sd = {k: v.clone() for k, v in model.state_dict().items()}
+    with torch.no_grad():
+        for k in sd:
+            if k.endswith(("c_k.weight", "gate_proj.weight")):
+                sd[k].mul_(-1.5)
+    model.load_state_dict(sd)
+    changed = logits()
+    control = copy_with_plain_forward(env, model)
+    assert (changed - first).abs().max().item() > 0
+    assert (changed - control).abs().max().item() <= LOGIT_TOL
+    # storage replaced: re-packed on the next forward
+    model.to(torch.float32).to(torch.bfloat16)
+    again = logits()
+    assert torch.equal(again, changed)
+
+
+def copy_with_plain_forward(env, model):
+    import copy
+    _, mcb = env
+    other = copy.deepcopy(model)
+    mcb.install(other, fuse_step=False)
+    with torch.inference_mode():
+        from modelcore_b200 import workloads
+        prompts = workloads.prompts(2, 8, seed=3).tolist()
+        return mcb.ModelManager().new_decoder(other, prompts, max_tokens=4).step([5, 6]).float().clone()

@@ -102,3 +102,26 @@ def test_decode_golden_streams_are_well_formed():
     for v in ("random", "awake"):
         assert z[f"{v}_tokens"].shape == (2, 64)
         assert (z[f"{v}_tokens"] >= 0).all() and (z[f"{v}_tokens"] < 32768).all()
+
+
+@pytest.mark.parametrize("C", [40, 768, 2048, 4096])
+def test_add_rms_norm_matches_the_reference_block(C):
+    """Block's residual add is one bf16 rounding and matches exactly; RMSNorm's fp32 sum order is
+    torch's detail, so the oracle (the CUDA kernel's order) may move a rare element by one ulp."""
+    z = load_golden("step_fused.npz")
+    s, h = O.add_rms_norm(z[f"x_C{C}"], z[f"delta_C{C}"])
+    assert np.array_equal(s, z[f"sum_C{C}"])
+    for got, want in ((h, z[f"norm_C{C}"]), (O.add_rms_norm(z[f"x_C{C}"])[1], z[f"norm_only_C{C}"])):
+        diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        assert diff.max() <= 1
+        assert (diff != 0).mean() <= 2e-3
+
+
+def test_gated_silu_matches_the_reference_mlp():
+    """silu(gate) * up in bf16: torch's CPU exp and numpy's may differ by an fp32 ulp, which can
+    move a bf16 rounding of silu; everything else is one rounding per op."""
+    z = load_golden("step_fused.npz")
+    got = O.gated_silu(z["gate"], z["up"])
+    diff = np.abs(got.astype(np.int32) - z["gated"].astype(np.int32))
+    assert diff.max() <= 1
+    assert (diff != 0).mean() <= 1e-3

@@ -225,12 +225,47 @@ typedef struct {
 
 int mcb_gated_silu(const mcb_gated_silu_args* args, void* stream);
 
+/* mcb_embed_rms_norm: x_out = rms_norm(table[ids[r]]); h_out = rms_norm(x_out) (h_out optional).
+ * Replaces TokenEmbedding.forward without smear (wte lookup + norm,
+ * modelcore/components/embedding.py:71-75) followed by the first Block's norm (block.py:57).
+ * An id outside [0, V) sets device error 4 and writes zeros (torch raises a device assert).
+ * Same C and alignment rules as mcb_add_rms_norm; ids is int64. */
+typedef struct {
+  const int64_t* ids;         /* (rows,) token ids                                          */
+  const void* table;          /* (V, C) bf16 embedding table                                */
+  void* x_out;                /* (rows, C) bf16                                             */
+  void* h_out;                /* (rows, C) bf16, or NULL                                    */
+  int64_t table_stride, x_stride, h_stride;  /* row strides, elements                       */
+  int64_t V;
+  int32_t rows, C;
+  float eps;
+} mcb_embed_args;
+
+int mcb_embed_rms_norm(const mcb_embed_args* args, void* stream);
+
+/* mcb_softcap_argmax: out[r, j] = cap * tanh(float(logits[r, j]) * (1 / cap)) for j < V (cap <= 0:
+ * no cap; the reciprocal rounded to fp32, as torch's CUDA division by a Python number computes it), argmax[r] = the first index of the row's maximum (NaN counts as the maximum).  Replaces
+ * LMHead.forward's crop, .float() and softcap (modelcore/components/unembedding.py:52-56) and the
+ * greedy branch of sample_next_token (modelcore/generate.py:23-24).  out or argmax may be NULL.
+ * logits rows may be padded (logits_stride >= V).  argmax_stride lets the ids feed a (B, 1)
+ * token column directly. */
+typedef struct {
+  const void* logits;         /* (rows, >= V) bf16                                          */
+  float* out;                 /* (rows, V) fp32, or NULL                                    */
+  int64_t* argmax;            /* (rows,) int64 at argmax_stride, or NULL                    */
+  int64_t logits_stride, out_stride, argmax_stride;
+  int32_t rows, V;
+  float softcap;
+} mcb_softcap_args;
+
+int mcb_softcap_argmax(const mcb_softcap_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
  * overflow) or a timed-out pipeline wait sets a device error word and skips the access.
  * mcb_device_error synchronises `stream`, returns the word in *code and clears it.
  * Codes: 0 none, 1 position beyond Tmax, 2 position beyond the rotary table, 3 pipeline wait
- * timed out.
+ * timed out, 4 token id outside the embedding table.
  * ------------------------------------------------------------------------------------------- */
 int mcb_device_error(int32_t* code, void* stream);
 

@@ -33,6 +33,7 @@ DEVICE_ERRORS = {
     1: "position beyond the cache length (Tmax)",
     2: "position beyond the rotary table",
     3: "pipeline wait timed out",
+    4: "token id outside the embedding table",
 }
 
 ABI_VERSION = 2
@@ -53,6 +54,8 @@ EXPORTED_SYMBOLS = (
     "mcb_decode_attn_noalloc",
     "mcb_add_rms_norm",
     "mcb_gated_silu",
+    "mcb_embed_rms_norm",
+    "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
 )
@@ -121,6 +124,24 @@ class GatedSiluArgs(ctypes.Structure):
     ]
 
 
+class EmbedArgs(ctypes.Structure):
+    _fields_ = [
+        ("ids", ctypes.c_void_p), ("table", ctypes.c_void_p), ("x_out", ctypes.c_void_p),
+        ("h_out", ctypes.c_void_p),
+        ("table_stride", ctypes.c_int64), ("x_stride", ctypes.c_int64), ("h_stride", ctypes.c_int64),
+        ("V", ctypes.c_int64), ("rows", ctypes.c_int32), ("C", ctypes.c_int32), ("eps", ctypes.c_float),
+    ]
+
+
+class SoftcapArgs(ctypes.Structure):
+    _fields_ = [
+        ("logits", ctypes.c_void_p), ("out", ctypes.c_void_p), ("argmax", ctypes.c_void_p),
+        ("logits_stride", ctypes.c_int64), ("out_stride", ctypes.c_int64),
+        ("argmax_stride", ctypes.c_int64),
+        ("rows", ctypes.c_int32), ("V", ctypes.c_int32), ("softcap", ctypes.c_float),
+    ]
+
+
 class McbError(RuntimeError):
     """A C-ABI call returned a non-zero mcb_status."""
 
@@ -157,6 +178,10 @@ def _declare(lib):
     lib.mcb_add_rms_norm.argtypes = [P(AddNormArgs), ctypes.c_void_p]
     lib.mcb_gated_silu.restype = ctypes.c_int
     lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
+    lib.mcb_embed_rms_norm.restype = ctypes.c_int
+    lib.mcb_embed_rms_norm.argtypes = [P(EmbedArgs), ctypes.c_void_p]
+    lib.mcb_softcap_argmax.restype = ctypes.c_int
+    lib.mcb_softcap_argmax.argtypes = [P(SoftcapArgs), ctypes.c_void_p]
     lib.mcb_device_error.restype = ctypes.c_int
     lib.mcb_device_error.argtypes = [P(ctypes.c_int32), ctypes.c_void_p]
     lib.mcb_launch_count.restype = ctypes.c_uint64

@@ -17,6 +17,7 @@ enum DeviceError : int {
   kErrPositionBeyondCache = 1,
   kErrPositionBeyondRotary = 2,
   kErrWaitTimeout = 3,
+  kErrTokenOutOfRange = 4,
 };
 // Defined once here: the library is a single translation unit (mcb200.cu).
 __device__ int g_device_error = 0;

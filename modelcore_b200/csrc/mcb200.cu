@@ -8,6 +8,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "../../include/mcb200.h"
 #include "common.cuh"
@@ -360,6 +361,20 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
 
 }  // namespace
 
+// One warp per row, 4 rows per 128-thread block; CPL = 16-byte chunks per lane, the smallest of
+// 1, 2, 4, 8, 16 that covers C.
+template <class F>
+static void launch_row_norm(int C, int rows, cudaStream_t st, F&& launch) {
+  const int chunks = C / 8;
+  const dim3 grid((rows + 3) / 4), block(128);
+  if (chunks <= 32) launch(std::integral_constant<int, 1>{}, grid, block, st);
+  else if (chunks <= 64) launch(std::integral_constant<int, 2>{}, grid, block, st);
+  else if (chunks <= 128) launch(std::integral_constant<int, 4>{}, grid, block, st);
+  else if (chunks <= 256) launch(std::integral_constant<int, 8>{}, grid, block, st);
+  else launch(std::integral_constant<int, 16>{}, grid, block, st);
+  g_launches++;
+}
+
 extern "C" {
 
 int mcb_abi_version(void) { return MCB_ABI_VERSION; }
@@ -546,17 +561,74 @@ int mcb_add_rms_norm(const mcb_add_norm_args* a, void* stream) {
   p.rows = a->rows;
   p.C = a->C;
   p.eps = a->eps;
-  const int chunks = a->C / 8;
-  const dim3 grid((a->rows + 3) / 4), block(128);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (chunks <= 32) mcb::add_rms_norm_kernel<1><<<grid, block, 0, st>>>(p);
-  else if (chunks <= 64) mcb::add_rms_norm_kernel<2><<<grid, block, 0, st>>>(p);
-  else if (chunks <= 128) mcb::add_rms_norm_kernel<4><<<grid, block, 0, st>>>(p);
-  else if (chunks <= 256) mcb::add_rms_norm_kernel<8><<<grid, block, 0, st>>>(p);
-  else mcb::add_rms_norm_kernel<16><<<grid, block, 0, st>>>(p);
-  g_launches++;
+  launch_row_norm(a->C, a->rows, static_cast<cudaStream_t>(stream), [&](auto cpl, dim3 g, dim3 b,
+                                                                        cudaStream_t st) {
+    mcb::add_rms_norm_kernel<decltype(cpl)::value><<<g, b, 0, st>>>(p);
+  });
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "add_rms_norm launch");
+  return MCB_OK;
+}
+
+int mcb_embed_rms_norm(const mcb_embed_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_embed_rms_norm: args is NULL");
+  if (a->rows < 0 || a->C <= 0 || a->C % 8 != 0 || a->C > 4096)
+    return fail(MCB_ERR_UNSUPPORTED,
+                "mcb_embed_rms_norm: C=%d must be a positive multiple of 8, at most 4096", a->C);
+  if (a->V <= 0) return fail(MCB_ERR_INVALID_ARG, "mcb_embed_rms_norm: V=%lld", (long long)a->V);
+  if (a->ids == nullptr || a->table == nullptr || a->x_out == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_embed_rms_norm: NULL pointer argument");
+  if (!aligned(a->table, 16) || !aligned(a->x_out, 16) || a->table_stride % 8 || a->x_stride % 8 ||
+      (a->h_out != nullptr && (!aligned(a->h_out, 16) || a->h_stride % 8)))
+    return fail(MCB_ERR_ALIGNMENT, "mcb_embed_rms_norm: rows must start on 16-byte boundaries");
+  if (a->rows == 0) return MCB_OK;
+  mcb::EmbedNormParams p;
+  p.ids = a->ids;
+  p.table = static_cast<const uint16_t*>(a->table);
+  p.x_out = static_cast<uint16_t*>(a->x_out);
+  p.h_out = static_cast<uint16_t*>(a->h_out);
+  p.ts = a->table_stride;
+  p.xs = a->x_stride;
+  p.hs = a->h_stride;
+  p.V = a->V;
+  p.rows = a->rows;
+  p.C = a->C;
+  p.eps = a->eps;
+  launch_row_norm(a->C, a->rows, static_cast<cudaStream_t>(stream), [&](auto cpl, dim3 g, dim3 b,
+                                                                        cudaStream_t st) {
+    mcb::embed_rms_norm_kernel<decltype(cpl)::value><<<g, b, 0, st>>>(p);
+  });
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "embed_rms_norm launch");
+  return MCB_OK;
+}
+
+int mcb_softcap_argmax(const mcb_softcap_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_softcap_argmax: args is NULL");
+  if (a->rows < 0 || a->V <= 0 || a->logits_stride < a->V ||
+      (a->out != nullptr && a->out_stride < a->V))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_softcap_argmax: rows=%d V=%d logits_stride=%lld", a->rows,
+                a->V, (long long)a->logits_stride);
+  if (a->logits == nullptr || (a->out == nullptr && a->argmax == nullptr))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_softcap_argmax: NULL logits, or neither out nor argmax");
+  if (a->rows == 0) return MCB_OK;
+  mcb::SoftcapParams p;
+  p.logits = static_cast<const uint16_t*>(a->logits);
+  p.out = a->out;
+  p.argmax = a->argmax;
+  p.ls = a->logits_stride;
+  p.os = a->out_stride;
+  p.as = a->argmax_stride;
+  p.rows = a->rows;
+  p.V = a->V;
+  p.cap = a->softcap;
+  p.inv_cap = a->softcap > 0.f ? 1.0f / a->softcap : 0.f;
+  p.vec = a->V % 8 == 0 && aligned(a->logits, 16) && a->logits_stride % 8 == 0 &&
+          (a->out == nullptr || (aligned(a->out, 16) && a->out_stride % 4 == 0));
+  mcb::softcap_argmax_kernel<<<a->rows, 512, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  g_launches++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "softcap_argmax launch");
   return MCB_OK;
 }
 

@@ -1,16 +1,23 @@
-// The decode step either side of attention: the residual add fused with the next RMSNorm, and
-// GatedMLP's act(gate) * up, for one (rows, C) bf16 activation block per launch.
+// The decode step around attention, one (rows, C) bf16 activation block per launch:
 //
-//   add_rms_norm:  x' = bf16(x + delta)                    (Block: x = x + mixer(..) / ffn(..),
-//                  h  = bf16(x' * rsqrt(mean(x'^2) + eps))  modelcore/components/block.py:57-59,
+//   add_rms_norm:    x' = bf16(x + delta)                   (Block: x = x + mixer(..) / ffn(..),
+//                    h  = bf16(x' * rsqrt(mean(x'^2) + eps)) modelcore/components/block.py:57-59,
 //                                                            then norm, modelcore/components/norm.py:43-44)
-//   gated_silu:    out = bf16(bf16(silu(gate)) * up)        (GatedMLP.forward, modelcore/components/mlp.py:89-90)
+//   embed_rms_norm:  x = norm(wte[id]), h = norm(x)          (TokenEmbedding.forward,
+//                                                            modelcore/components/embedding.py:71-75,
+//                                                            then the first block's norm)
+//   gated_silu:      out = bf16(bf16(silu(gate)) * up)       (GatedMLP.forward, modelcore/components/mlp.py:89-90)
+//   softcap_argmax:  y = cap * tanh(float(x) / cap), argmax  (LMHead.forward's epilogue,
+//                                                            modelcore/components/unembedding.py:52-56,
+//                                                            and greedy sample_next_token)
 //
-// Rounding follows torch's bf16 ops: the add is computed in fp32 and rounded once; rms_norm
-// accumulates the sum of squares in fp32, in this kernel's fixed order (lane l adds the squares of
+// Rounding follows torch's ops: the add is computed in fp32 and rounded once; rms_norm
+// accumulates the sum of squares in fp32, in this file's fixed order (lane l adds the squares of
 // its 16-byte chunks c = l, l+32, .. in order, element by element, then an xor butterfly over
 // masks 16 .. 1), and rounds once; silu is computed in fp32 as g / (1 + exp(-g)) and rounded, the
-// product in fp32 and rounded.  The CPU oracle restates the same order.
+// product in fp32 and rounded; the softcap multiplies by the fp32 reciprocal of the cap (as torch's
+// CUDA division by a Python number does), then tanhf, then an fp32 multiply.  The
+// CPU oracle restates the same order.
 #pragma once
 
 #include "common.cuh"
@@ -27,71 +34,141 @@ struct AddNormParams {
   float eps;
 };
 
-// One warp per row; C a multiple of 8 with C <= 256 * CPL (CPL 16-byte chunks per lane); rows
-// 16-byte aligned.
+// A row of C bf16 values held by one warp as v[u][0..7] = elements 8c .. 8c+7 of chunk
+// c = lane + 32u (CPL 16-byte chunks per lane).
+template <int CPL>
+__device__ __forceinline__ void load_row_chunks(const uint16_t* row, int lane, int nchunk,
+                                                float (&v)[CPL][8]) {
+#pragma unroll
+  for (int u = 0; u < CPL; ++u) {
+    const int c = lane + 32 * u;
+    if (c < nchunk) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + 8 * c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[u][2 * i] = __uint_as_float(ws[i] << 16);
+        v[u][2 * i + 1] = __uint_as_float(ws[i] & 0xffff0000u);
+      }
+    }
+  }
+}
+
+template <int CPL>
+__device__ __forceinline__ void store_row_chunks(uint16_t* row, int lane, int nchunk,
+                                                 const float (&v)[CPL][8]) {
+#pragma unroll
+  for (int u = 0; u < CPL; ++u) {
+    const int c = lane + 32 * u;
+    if (c < nchunk) {
+      uint4 o;
+      o.x = pack_bf16x2(v[u][0], v[u][1]);
+      o.y = pack_bf16x2(v[u][2], v[u][3]);
+      o.z = pack_bf16x2(v[u][4], v[u][5]);
+      o.w = pack_bf16x2(v[u][6], v[u][7]);
+      *reinterpret_cast<uint4*>(row + 8 * c) = o;
+    }
+  }
+}
+
+// rsqrt(mean(v^2) + eps) of the warp's row: each lane sums the squares of its chunks in order
+// (u ascending, element by element), then an xor butterfly 16 .. 1 adds the lanes' sums.
+template <int CPL>
+__device__ __forceinline__ float row_rms_rsqrt(const float (&v)[CPL][8], int lane, int nchunk,
+                                               int C, float eps) {
+  float acc = 0.f;
+#pragma unroll
+  for (int u = 0; u < CPL; ++u) {
+    if (lane + 32 * u < nchunk) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[u][i], v[u][i]));
+    }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  return __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(C)), eps));
+}
+
+// v <- bf16(v * r)
+template <int CPL>
+__device__ __forceinline__ void scale_round(float (&v)[CPL][8], float r) {
+#pragma unroll
+  for (int u = 0; u < CPL; ++u)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[u][i] = round_bf16(__fmul_rn(v[u][i], r));
+}
+
+// One warp per row; C a multiple of 8 with C <= 256 * CPL; rows 16-byte aligned.
 template <int CPL>
 __global__ void __launch_bounds__(128) add_rms_norm_kernel(const AddNormParams p) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   const int nchunk = p.C / 8;
-  const uint16_t* xr = p.x + static_cast<long long>(row) * p.xs;
-  const uint16_t* dr = p.delta ? p.delta + static_cast<long long>(row) * p.ds : nullptr;
-  uint16_t* xo = p.x_out ? p.x_out + static_cast<long long>(row) * p.xos : nullptr;
-  uint16_t* ho = p.h_out + static_cast<long long>(row) * p.hs;
-  constexpr int MAXC = CPL;
-  float v[MAXC][8];
-  float acc = 0.f;
+  float v[CPL][8];
+  load_row_chunks<CPL>(p.x + static_cast<long long>(row) * p.xs, lane, nchunk, v);
+  if (p.delta) {
+    const uint16_t* dr = p.delta + static_cast<long long>(row) * p.ds;
 #pragma unroll
-  for (int u = 0; u < MAXC; ++u) {
-    const int c = lane + 32 * u;
-    if (c < nchunk) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(xr + 8 * c);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-      uint32_t dw[4] = {0, 0, 0, 0};
-      if (dr) {
-        const uint4 dv = *reinterpret_cast<const uint4*>(dr + 8 * c);
-        dw[0] = dv.x; dw[1] = dv.y; dw[2] = dv.z; dw[3] = dv.w;
-      }
+    for (int u = 0; u < CPL; ++u) {
+      const int c = lane + 32 * u;
+      if (c < nchunk) {
+        const uint4 w = *reinterpret_cast<const uint4*>(dr + 8 * c);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float a0 = __uint_as_float(xw[i] << 16), a1 = __uint_as_float(xw[i] & 0xffff0000u);
-        if (dr) {
-          a0 = round_bf16(__fadd_rn(a0, __uint_as_float(dw[i] << 16)));
-          a1 = round_bf16(__fadd_rn(a1, __uint_as_float(dw[i] & 0xffff0000u)));
+        for (int i = 0; i < 4; ++i) {
+          v[u][2 * i] = round_bf16(__fadd_rn(v[u][2 * i], __uint_as_float(ws[i] << 16)));
+          v[u][2 * i + 1] =
+              round_bf16(__fadd_rn(v[u][2 * i + 1], __uint_as_float(ws[i] & 0xffff0000u)));
         }
-        v[u][2 * i] = a0;
-        v[u][2 * i + 1] = a1;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[u][i], v[u][i]));
-      if (xo) {
-        uint4 o;
-        o.x = pack_bf16x2(v[u][0], v[u][1]);
-        o.y = pack_bf16x2(v[u][2], v[u][3]);
-        o.z = pack_bf16x2(v[u][4], v[u][5]);
-        o.w = pack_bf16x2(v[u][6], v[u][7]);
-        *reinterpret_cast<uint4*>(xo + 8 * c) = o;
       }
     }
+    store_row_chunks<CPL>(p.x_out + static_cast<long long>(row) * p.xos, lane, nchunk, v);
   }
+  const float r = row_rms_rsqrt<CPL>(v, lane, nchunk, p.C, p.eps);
+  scale_round<CPL>(v, r);
+  store_row_chunks<CPL>(p.h_out + static_cast<long long>(row) * p.hs, lane, nchunk, v);
+}
+
+struct EmbedNormParams {
+  const int64_t* ids;
+  const uint16_t* table;  // (V, C) bf16
+  uint16_t* x_out;        // norm(table[id])
+  uint16_t* h_out;        // norm(x_out), or null
+  long long ts, xs, hs;   // row strides (elements)
+  long long V;
+  int rows, C;
+  float eps;
+};
+
+// TokenEmbedding (wte lookup + norm) and the first block's norm in one pass: one warp per row.
+// An id outside [0, V) records kErrTokenOutOfRange and writes zeros.
+template <int CPL>
+__global__ void __launch_bounds__(128) embed_rms_norm_kernel(const EmbedNormParams p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int nchunk = p.C / 8;
+  const long long id = p.ids[row];
+  float v[CPL][8];
+  uint16_t* xo = p.x_out + static_cast<long long>(row) * p.xs;
+  uint16_t* ho = p.h_out ? p.h_out + static_cast<long long>(row) * p.hs : nullptr;
+  if (id < 0 || id >= p.V) {
+    if (lane == 0) record_error(kErrTokenOutOfRange);
 #pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.C)), p.eps));
+    for (int u = 0; u < CPL; ++u)
 #pragma unroll
-  for (int u = 0; u < MAXC; ++u) {
-    const int c = lane + 32 * u;
-    if (c < nchunk) {
-      float o[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[u][i], r);
-      uint4 ov;
-      ov.x = pack_bf16x2(o[0], o[1]);
-      ov.y = pack_bf16x2(o[2], o[3]);
-      ov.z = pack_bf16x2(o[4], o[5]);
-      ov.w = pack_bf16x2(o[6], o[7]);
-      *reinterpret_cast<uint4*>(ho + 8 * c) = ov;
-    }
+      for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+    store_row_chunks<CPL>(xo, lane, nchunk, v);
+    if (ho) store_row_chunks<CPL>(ho, lane, nchunk, v);
+    return;
+  }
+  load_row_chunks<CPL>(p.table + id * p.ts, lane, nchunk, v);
+  scale_round<CPL>(v, row_rms_rsqrt<CPL>(v, lane, nchunk, p.C, p.eps));
+  store_row_chunks<CPL>(xo, lane, nchunk, v);
+  if (ho) {
+    scale_round<CPL>(v, row_rms_rsqrt<CPL>(v, lane, nchunk, p.C, p.eps));
+    store_row_chunks<CPL>(ho, lane, nchunk, v);
   }
 }
 
@@ -127,6 +204,94 @@ __global__ void __launch_bounds__(256) gated_silu_kernel(const GatedActParams p)
     ow[k] = pack_bf16x2(o[0], o[1]);
   }
   *reinterpret_cast<uint4*>(p.out + row * p.os + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+struct SoftcapParams {
+  const uint16_t* logits;  // (rows, V) bf16, row stride ls
+  float* out;              // (rows, V) fp32, row stride os, or null
+  int64_t* argmax;         // (rows,) int64 at stride as, or null
+  long long ls, os, as;
+  int rows, V;
+  float cap;               // > 0: cap * tanh(x * inv_cap); otherwise x
+  float inv_cap;           // 1 / cap in fp32
+  int vec;                 // rows 16-byte aligned and V % 8 == 0: 16-byte loads, 32-byte stores
+};
+
+// torch evaluates `logits / cap` with a Python-number cap as logits * (1 / cap) on CUDA (the
+// reciprocal rounded to fp32 once), then tanh, then `cap * t`.
+__device__ __forceinline__ float softcap_value(float x, float cap, float inv_cap) {
+  return cap > 0.f ? __fmul_rn(cap, tanhf(__fmul_rn(x, inv_cap))) : x;
+}
+
+// (a, ia) beats (b, ib) under torch.argmax's order: NaN above everything, then the larger value,
+// then the smaller index.
+__device__ __forceinline__ bool argmax_better(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na != nb) return na;
+  if (!na && a != b) return a > b;
+  return ia < ib;
+}
+
+// LMHead's epilogue, modelcore/components/unembedding.py:52-56 (crop to V, .float(), softcap),
+// fused with the greedy pick of sample_next_token(temperature=0), modelcore/generate.py:23-24.
+// One CTA per row.
+__global__ void __launch_bounds__(512) softcap_argmax_kernel(const SoftcapParams p) {
+  const int row = blockIdx.x;
+  const uint16_t* in = p.logits + static_cast<long long>(row) * p.ls;
+  float* out = p.out ? p.out + static_cast<long long>(row) * p.os : nullptr;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  if (p.vec) {
+    const int nchunk = p.V / 8;
+    for (int c = threadIdx.x; c < nchunk; c += blockDim.x) {
+      const uint4 w = *reinterpret_cast<const uint4*>(in + 8 * c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        y[2 * i] = softcap_value(__uint_as_float(ws[i] << 16), p.cap, p.inv_cap);
+        y[2 * i + 1] = softcap_value(__uint_as_float(ws[i] & 0xffff0000u), p.cap, p.inv_cap);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (argmax_better(y[i], 8 * c + i, best, bi)) { best = y[i]; bi = 8 * c + i; }
+      if (out) {
+        float4* o = reinterpret_cast<float4*>(out + 8 * c);
+        o[0] = make_float4(y[0], y[1], y[2], y[3]);
+        o[1] = make_float4(y[4], y[5], y[6], y[7]);
+      }
+    }
+  } else {
+    for (int j = threadIdx.x; j < p.V; j += blockDim.x) {
+      const float y = softcap_value(bf16_bits_to_float(in[j]), p.cap, p.inv_cap);
+      if (argmax_better(y, j, best, bi)) { best = y; bi = j; }
+      if (out) out[j] = y;
+    }
+  }
+  if (!p.argmax) return;
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+    if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
+  }
+  __shared__ float sb[16];
+  __shared__ int si[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sb[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, m);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+      if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) p.argmax[static_cast<long long>(row) * p.as] = bi;
+  }
 }
 
 }  // namespace mcb

@@ -225,12 +225,18 @@ class GraphDecoder:
         with torch.inference_mode():
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
+            fused_pick = (greedy and step.decode_installed(self.model)
+                          and step._model_call_ok(self.model, self._ids, cache))
             with torch.cuda.graph(g, stream=side):
-                logits = self.model.forward(self._ids, kv_cache=cache)[:, -1, :]
                 nxt = None
-                if greedy:
-                    nxt = torch.argmax(logits, dim=-1, keepdim=True)
-                    self._ids.copy_(nxt)
+                if fused_pick:   # the LM-head epilogue writes the greedy ids into _ids
+                    logits = step.decode_forward(self.model, self._ids, cache,
+                                                 argmax_out=self._ids)[:, -1, :]
+                else:
+                    logits = self.model.forward(self._ids, kv_cache=cache)[:, -1, :]
+                    if greedy:
+                        nxt = torch.argmax(logits, dim=-1, keepdim=True)
+                        self._ids.copy_(nxt)
             torch.cuda.current_stream().wait_stream(side)
         self.launches_per_step = ops.launch_count() - launches
         cache.restore_host_state(snap)

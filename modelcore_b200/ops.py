@@ -12,7 +12,8 @@ import math
 import torch
 
 from . import _native
-from ._native import AddNormArgs, AppendArgs, AttnArgs, CopyArgs, GatedSiluArgs, check
+from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
+                      SoftcapArgs, check)
 
 
 def _stream(t):
@@ -333,6 +334,65 @@ def add_rms_norm(x, delta=None, *, eps=None, x_out=None, h_out=None):
     args.eps = rms_norm_eps(eps)
     check(_native.load().mcb_add_rms_norm(ctypes.byref(args), _stream(x)))
     return x_out, h_out
+
+
+def embed_rms_norm(ids, table, *, eps=None, second_norm=True, x_out=None, h_out=None):
+    """TokenEmbedding without smear (wte lookup + norm, modelcore/components/embedding.py:71-75)
+    and, with second_norm, the first block's norm of its output, in one launch.  ids: int64 of
+    any shape; table: (V, C) bf16.  Returns (x, h) shaped ids.shape + (C,) (h None without
+    second_norm).  An id outside [0, V) sets device error 4 and yields zeros."""
+    if ids.dtype != torch.int64 or not ids.is_cuda:
+        raise RuntimeError("ids must be an int64 CUDA tensor")
+    V, C = table.shape
+    flat = ids.reshape(-1)
+    if not flat.is_contiguous():
+        flat = flat.contiguous()
+    rows = flat.numel()
+    if x_out is None:
+        x_out = torch.empty((rows, C), dtype=torch.bfloat16, device=ids.device)
+    if second_norm and h_out is None:
+        h_out = torch.empty((rows, C), dtype=torch.bfloat16, device=ids.device)
+    args = EmbedArgs()
+    args.ids = flat.data_ptr()
+    args.table, args.table_stride = table.data_ptr(), _rows2d("table", table)
+    args.x_out, args.x_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
+    if second_norm:
+        args.h_out, args.h_stride = h_out.data_ptr(), _rows2d("h_out", h_out)
+    args.V, args.rows, args.C = V, rows, C
+    args.eps = rms_norm_eps(eps)
+    check(_native.load().mcb_embed_rms_norm(ctypes.byref(args), _stream(table)))
+    shape = tuple(ids.shape) + (C,)
+    return x_out.view(shape), (h_out.view(shape) if second_norm else None)
+
+
+def softcap_argmax(logits, vocab_size, softcap, *, out=None, want_logits=True, argmax_out=None):
+    """LMHead's epilogue (modelcore/components/unembedding.py:52-56): crop the (..., V_padded)
+    bf16 logits to vocab_size, .float(), and cap * tanh(x / cap) (softcap None: no cap); with
+    argmax_out (an int64 tensor holding one id per row), also the greedy pick of
+    sample_next_token(temperature=0) (modelcore/generate.py:23-24).  Returns the fp32 logits
+    shaped (..., vocab_size), or None when want_logits is False."""
+    _need("logits", logits)
+    lead = tuple(logits.shape[:-1])
+    lg = logits.reshape(-1, logits.shape[-1])
+    if lg.stride(-1) != 1:
+        raise RuntimeError("logits must have unit stride on the vocab dim")
+    rows = lg.shape[0]
+    args = SoftcapArgs()
+    args.logits, args.logits_stride = lg.data_ptr(), lg.stride(0)
+    if want_logits:
+        if out is None:
+            out = torch.empty(lead + (vocab_size,), dtype=torch.float32, device=logits.device)
+        o2 = out.view(rows, vocab_size)
+        args.out, args.out_stride = o2.data_ptr(), o2.stride(0)
+    if argmax_out is not None:
+        if argmax_out.dtype != torch.int64 or argmax_out.numel() != rows:
+            raise RuntimeError(f"argmax_out must hold {rows} int64 ids")
+        args.argmax = argmax_out.data_ptr()
+        args.argmax_stride = argmax_out.reshape(-1).stride(0)
+    args.rows, args.V = rows, vocab_size
+    args.softcap = float(softcap) if softcap is not None else 0.0
+    check(_native.load().mcb_softcap_argmax(ctypes.byref(args), _stream(logits)))
+    return out if want_logits else None
 
 
 def gated_silu(gate, up, out=None):

@@ -36,6 +36,13 @@ the next forward; in-place writes (load_state_dict's copy_) land in the packed b
 Applies to a StackComposer body without features whose blocks are all featureless Blocks with
 modelcore's RMSNorm, an Attention mixer without features and a GatedMLP "silu" ffn, with bf16
 weights, under a modelcore_b200 KVCache; any other model or call runs the reference forward.
+
+When the embedding is a TokenEmbedding without smear and the output an LMHead, all norms sharing
+one eps, `model_forward` replaces Model.forward at decode too: one launch gathers the token rows
+and gives both the embedding's norm and the first block's (mcb_embed_rms_norm), the last block's
+fused add + norm is the LM head's norm, and one launch after the LM-head GEMM does the vocab crop,
+.float() and softcap (mcb_softcap_argmax) -- with the greedy pick in the same pass when a
+caller asks for it (GraphDecoder.greedy_steps).
 """
 import types
 
@@ -46,6 +53,7 @@ from . import ops
 from .cache import KVCache
 
 _ORIGINAL_FORWARD = "_mcb_original_stack_forward"
+_ORIGINAL_MODEL_FORWARD = "_mcb_original_model_forward"
 _PACKED = "_mcb_packed"
 
 
@@ -144,36 +152,102 @@ def _call_ok(body, x, kv_cache):
     return True
 
 
+def body_forward(body, x2, h, idx, kv_cache, B, T):
+    """The blocks on the (rows, C) residual x2 and its normed h = norm(x2); returns the final
+    residual and its norm (rows, C), the residual in a new buffer."""
+    C = x2.size(1)
+    rows = B * T
+    resid = torch.empty((rows, C), dtype=x2.dtype, device=x2.device)
+    src = x2
+    for block in body.blocks:
+        y = block.mixer(h.view(B, T, C), idx, kv_cache, None, None)
+        ops.add_rms_norm(src, y.view(rows, C), eps=block.norm.eps, x_out=resid, h_out=h)
+        src = resid
+        f = gated_mlp(block.ffn, h)
+        ops.add_rms_norm(resid, f, eps=block.norm.eps, x_out=resid, h_out=h)
+    return resid, h
+
+
 def stack_forward(self, x, idx, kv_cache, doc_args=None):
     """StackComposer.forward (modelcore/composers/stack.py:35-42) for the structure in the module
     docstring, with the residual add and the next norm fused and the projections packed."""
     if not _call_ok(self, x, kv_cache):
         return getattr(self, _ORIGINAL_FORWARD)(x, idx, kv_cache, doc_args)
     B, T, C = x.shape
-    rows = B * T
-    norm = self.blocks[0].norm
-    x2 = x.reshape(rows, C)
-    resid = torch.empty((rows, C), dtype=x.dtype, device=x.device)
-    h = torch.empty_like(resid)
-    ops.add_rms_norm(x2, eps=norm.eps, h_out=h)
-    src = x2
-    for block in self.blocks:
-        y = block.mixer(h.view(B, T, C), idx, kv_cache, None, doc_args)
-        ops.add_rms_norm(src, y.view(rows, C), eps=block.norm.eps, x_out=resid, h_out=h)
-        src = resid
-        f = gated_mlp(block.ffn, h)
-        ops.add_rms_norm(resid, f, eps=block.norm.eps, x_out=resid, h_out=h)
+    x2 = x.reshape(B * T, C)
+    h = torch.empty_like(x2)
+    ops.add_rms_norm(x2, eps=self.blocks[0].norm.eps, h_out=h)
+    resid, _ = body_forward(self, x2, h, idx, kv_cache, B, T)
     return resid.view(B, T, C)
 
 
-def install(model):
-    """Binds stack_forward to the model's body when its structure qualifies; returns True if it
-    did.  Idempotent."""
-    body = getattr(model, "body", None)
-    if body is None or hasattr(body, _ORIGINAL_FORWARD) or not _structure_ok(body):
+# ---------------------------------------------------------------------------------------------
+# The whole decode forward: embedding and LM head fused too
+def _head_structure_ok(model):
+    from modelcore.components.embedding import TokenEmbedding
+    from modelcore.components.norm import RMSNorm
+    from modelcore.components.unembedding import LMHead
+    emb, un = getattr(model, "embedding", None), getattr(model, "unembedding", None)
+    if type(emb) is not TokenEmbedding or emb.smear is not None or type(emb.norm) is not RMSNorm:
         return False
-    object.__setattr__(body, _ORIGINAL_FORWARD, body.forward)
-    object.__setattr__(body, "forward", types.MethodType(stack_forward, body))
+    if type(un) is not LMHead or type(un.norm) is not RMSNorm:
+        return False
+    eps = {emb.norm.eps, un.norm.eps} | {b.norm.eps for b in model.body.blocks}
+    return len(eps) == 1
+
+
+def _model_call_ok(model, idx, kv_cache):
+    emb, un = model.embedding, model.unembedding
+    if not (isinstance(kv_cache, KVCache) and idx.dtype == torch.int64 and idx.is_cuda
+            and idx.dim() == 2 and emb.runtime.compute_dtype == torch.bfloat16
+            and emb.wte.weight.dtype == torch.bfloat16
+            and un.lm_head.weight.dtype == torch.bfloat16):
+        return False
+    C = emb.wte.weight.size(1)
+    probe = torch.empty((0, C), dtype=torch.bfloat16, device=idx.device)
+    return _call_ok(model.body, probe, kv_cache)
+
+
+def decode_forward(model, idx, kv_cache, argmax_out=None, want_logits=True):
+    """Model.forward (modelcore/model.py:93-101) with kv_cache and without targets, for a model
+    whose body qualifies for stack_forward and whose embedding (TokenEmbedding without smear) and
+    LM head (LMHead) share one RMSNorm eps: mcb_embed_rms_norm gives the embedding and the first
+    block's normed input in one launch; the last block's fused add + norm is the LM head's norm;
+    mcb_softcap_argmax does the crop, .float() and softcap after the projection and, with
+    argmax_out, the greedy pick.  Returns the fp32 logits (B, T, vocab_size) (None when
+    want_logits is False)."""
+    B, T = idx.shape
+    emb, un = model.embedding, model.unembedding
+    x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
+    C = x.size(-1)
+    _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
+    kv_cache.advance(T)
+    logits = F.linear(h, un.lm_head.weight)
+    out = ops.softcap_argmax(logits, un.vocab_size, un.softcap, argmax_out=argmax_out,
+                             want_logits=want_logits)
+    return out.view(B, T, un.vocab_size) if want_logits else None
+
+
+def model_forward(self, idx, targets=None, kv_cache=None, loss_reduction='mean', doc_args=None):
+    if targets is not None or not _model_call_ok(self, idx, kv_cache):
+        return getattr(self, _ORIGINAL_MODEL_FORWARD)(idx, targets, kv_cache, loss_reduction,
+                                                      doc_args)
+    return decode_forward(self, idx, kv_cache)
+
+
+def install(model):
+    """Binds stack_forward to the model's body when its structure qualifies, and model_forward to
+    the model when its embedding and LM head qualify too; returns True if the body was bound.
+    Idempotent."""
+    body = getattr(model, "body", None)
+    if body is None or not _structure_ok(body):
+        return False
+    if not hasattr(body, _ORIGINAL_FORWARD):
+        object.__setattr__(body, _ORIGINAL_FORWARD, body.forward)
+        object.__setattr__(body, "forward", types.MethodType(stack_forward, body))
+    if not hasattr(model, _ORIGINAL_MODEL_FORWARD) and _head_structure_ok(model):
+        object.__setattr__(model, _ORIGINAL_MODEL_FORWARD, model.forward)
+        object.__setattr__(model, "forward", types.MethodType(model_forward, model))
     return True
 
 
@@ -182,8 +256,16 @@ def uninstall(model):
     if body is not None and hasattr(body, _ORIGINAL_FORWARD):
         object.__setattr__(body, "forward", getattr(body, _ORIGINAL_FORWARD))
         object.__delattr__(body, _ORIGINAL_FORWARD)
+    if hasattr(model, _ORIGINAL_MODEL_FORWARD):
+        object.__setattr__(model, "forward", getattr(model, _ORIGINAL_MODEL_FORWARD))
+        object.__delattr__(model, _ORIGINAL_MODEL_FORWARD)
 
 
 def installed(model):
     body = getattr(model, "body", None)
     return body is not None and hasattr(body, _ORIGINAL_FORWARD)
+
+
+def decode_installed(model):
+    """True when model_forward (the whole fused decode forward) is bound."""
+    return hasattr(model, _ORIGINAL_MODEL_FORWARD)

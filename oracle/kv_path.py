@@ -134,17 +134,12 @@ def rope_tables_at(cos_bits, sin_bits, cache_seqlens, T):
 
 # ---------------------------------------------------------------------------------------------
 # The decode step either side of attention
-def add_rms_norm(x_bits, delta_bits=None, eps=None):
-    """Block's residual add then norm (modelcore/components/block.py:57-59, norm.py:43-44):
-    x' = bf16(x + delta), h = bf16(x' * rsqrt(sum(x'^2)/C + eps)) with the fp32 sum in the
-    kernel's order (lane l: its 8-element chunks l, l+32, .., element by element; then an xor
-    butterfly over 32 lanes).  Returns (x' bits, h bits)."""
-    x = bf16_to_f32(x_bits)
-    if delta_bits is not None:
-        x = round_bf16((x + bf16_to_f32(delta_bits)).astype(np.float32))
+def _row_rms_norm(x, eps):
+    """bf16-representable fp32 rows x (..., C) -> bf16(x * rsqrt(sum(x^2)/C + eps)) as fp32, the sum
+    in the step kernels' order: lane l adds its 8-element chunks l, l+32, .. element by element,
+    then an xor butterfly over the 32 lanes."""
     C = x.shape[-1]
-    lead = x.shape[:-1]
-    acc = np.zeros(lead + (32,), dtype=np.float32)
+    acc = np.zeros(x.shape[:-1] + (32,), dtype=np.float32)
     for lane in range(32):
         for c in range(lane, C // 8, 32):
             for i in range(8):
@@ -155,7 +150,44 @@ def add_rms_norm(x_bits, delta_bits=None, eps=None):
     e = F32(np.finfo(np.float32).eps if eps is None else eps)
     v = ((acc[..., 0] / F32(C)).astype(np.float32) + e).astype(np.float32)
     r = (np.longdouble(1.0) / np.sqrt(v.astype(np.longdouble))).astype(np.float32)
-    return f32_to_bf16(x), f32_to_bf16((x * r[..., None]).astype(np.float32))
+    return round_bf16((x * r[..., None]).astype(np.float32))
+
+
+def add_rms_norm(x_bits, delta_bits=None, eps=None):
+    """Block's residual add then norm (modelcore/components/block.py:57-59, norm.py:43-44):
+    x' = bf16(x + delta), h = bf16(x' * rsqrt(sum(x'^2)/C + eps)), the fp32 sum in the kernel's
+    order (_row_rms_norm).  Returns (x' bits, h bits)."""
+    x = bf16_to_f32(x_bits)
+    if delta_bits is not None:
+        x = round_bf16((x + bf16_to_f32(delta_bits)).astype(np.float32))
+    return f32_to_bf16(x), f32_to_bf16(_row_rms_norm(x, eps))
+
+
+def embed_rms_norm(ids, table_bits, eps=None):
+    """TokenEmbedding without smear (modelcore/components/embedding.py:71-75: wte lookup, norm)
+    and the first block's norm of its output (block.py:57).  Returns (x bits, h bits)."""
+    x = _row_rms_norm(bf16_to_f32(table_bits[np.asarray(ids)]), eps)
+    return f32_to_bf16(x), f32_to_bf16(_row_rms_norm(x, eps))
+
+
+def softcap_logits(logits_bits, vocab_size, softcap):
+    """LMHead.forward's epilogue (modelcore/components/unembedding.py:52-56): crop the padded
+    bf16 logits to vocab_size, .float(), softcap * tanh(x / softcap) in fp32, with the division
+    as torch performs it on CUDA for a Python-number divisor: x * fp32(1 / softcap).  On the CPU
+    torch divides exactly and uses its own vectorised tanh; numpy's float32 tanh differs from
+    both by an ulp or two on some elements (tests bound it)."""
+    x = bf16_to_f32(logits_bits[..., :vocab_size])
+    if softcap is None:
+        return x
+    c = F32(softcap)
+    inv = (F32(1.0) / c).astype(np.float32)
+    return (c * np.tanh((x * inv).astype(np.float32)).astype(np.float32)).astype(np.float32)
+
+
+def greedy_pick(logits):
+    """sample_next_token(temperature=0) (modelcore/generate.py:23-24): the first index of each
+    row's maximum."""
+    return np.argmax(logits, axis=-1)
 
 
 def gated_silu(gate_bits, up_bits):

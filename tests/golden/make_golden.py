@@ -21,7 +21,9 @@ Fixtures:
   step_fused.npz            Block's residual add + RMSNorm(eps=None) in bf16 (modelcore/components/
                             block.py:57-59, norm.py:43-44) for C in 40 / 768 / 2048 / 4096, and
                             GatedMLP's act(gate) * up with activation "silu" in bf16
-                            (modelcore/components/mlp.py:89-90)
+                            (modelcore/components/mlp.py:89-90); TokenEmbedding without smear
+                            then the first norm (embedding.py:71-75); LMHead with softcap 15 and
+                            without (unembedding.py:50-56): its bf16 logits and fp32 outputs
   decode_cfg1.npz           the README quickstart model (fp32, seed 0), prompts (2, 16) from seed 1,
                             64 greedy steps through Decoder: the token streams, for the plain
                             random init and for the awake init of
@@ -183,6 +185,31 @@ def make_step_fused(out_dir):
     gate = (torch.randn(16, 2048, generator=g) * 6).to(torch.bfloat16)
     up = torch.randn(16, 2048, generator=g).to(torch.bfloat16)
     out["gate"], out["up"], out["gated"] = bits(gate), bits(up), bits(mlp.act(gate) * up)
+    # TokenEmbedding (no smear) + the first block's norm
+    from modelcore.components.embedding import TokenEmbedding
+    from modelcore.components.unembedding import LMHead
+    from modelcore.runtime import Runtime
+    emb = TokenEmbedding(padded_vocab_size=1024, n_embd=768, norm=norm, smear=False,
+                         runtime=Runtime(compute_dtype=torch.bfloat16))
+    emb.init_weights()
+    ids = torch.randint(0, 1024, (3, 7), generator=g)
+    ids[0, 0], ids[2, 6] = 0, 1023
+    with torch.no_grad():
+        xe = emb(ids)
+    out["wte"], out["ids"], out["embed_x"], out["embed_h"] = (bits(emb.wte.weight), ids.numpy(),
+                                                              bits(xe), bits(norm(xe)))
+    # LMHead: norm, projection, crop, .float(), softcap
+    head = LMHead(n_embd=64, vocab_size=1000, padded_vocab_size=1024, norm=norm, softcap=15)
+    with torch.no_grad():
+        head.lm_head.weight.copy_(torch.randn(1024, 64, generator=g) * 3)
+    head = head.to(torch.bfloat16)
+    xh = torch.randn(9, 64, generator=g).to(torch.bfloat16)
+    out["head_x"] = bits(xh)
+    with torch.no_grad():
+        out["head_logits_bf16"] = bits(head.lm_head(head.norm(xh)))
+        out["head_out"] = head(xh).numpy()
+        head.softcap = None
+        out["head_out_nocap"] = head(xh).numpy()
     np.savez_compressed(os.path.join(out_dir, "step_fused.npz"), **out)
 
 

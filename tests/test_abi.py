@@ -10,7 +10,8 @@ import pytest
 
 from conftest import REPO
 from modelcore_b200 import _native
-from modelcore_b200._native import AddNormArgs, AppendArgs, AttnArgs, CopyArgs, GatedSiluArgs
+from modelcore_b200._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs,
+                                    GatedSiluArgs, SoftcapArgs)
 
 HEADER = os.path.join(REPO, "include", "mcb200.h")
 
@@ -51,7 +52,8 @@ def _c_layout(struct, fields):
 
 @pytest.mark.parametrize("cls,cname", [(AppendArgs, "mcb_append_args"), (CopyArgs, "mcb_copy_args"),
                                        (AttnArgs, "mcb_attn_args"), (AddNormArgs, "mcb_add_norm_args"),
-                                       (GatedSiluArgs, "mcb_gated_silu_args")])
+                                       (GatedSiluArgs, "mcb_gated_silu_args"), (EmbedArgs, "mcb_embed_args"),
+                                       (SoftcapArgs, "mcb_softcap_args")])
 def test_ctypes_structures_match_the_c_layout(cls, cname):
     fields = [f for f, _ in cls._fields_]
     c = _c_layout(cname, fields)
@@ -183,3 +185,20 @@ def test_step_kernels_validate_on_the_host():
     assert lib.mcb_gated_silu(ctypes.byref(g), None) == MCB_ERR_ALIGNMENT
     g.gate_stride, g.rows = 16, 0
     assert lib.mcb_gated_silu(ctypes.byref(g), None) == 0   # nothing to do, nothing launched
+
+
+def test_embedding_and_lm_head_epilogue_validate_on_the_host():
+    lib = _native.load()
+    e = EmbedArgs()
+    e.ids, e.table, e.x_out, e.rows, e.C, e.V = 16, 32, 48, 2, 20, 100
+    assert lib.mcb_embed_rms_norm(ctypes.byref(e), None) == _native.MCB_ERR_UNSUPPORTED
+    e.C, e.V = 64, 0
+    assert lib.mcb_embed_rms_norm(ctypes.byref(e), None) == _native.MCB_ERR_INVALID_ARG
+    e.V, e.table_stride, e.x_stride = 100, 68, 64
+    assert lib.mcb_embed_rms_norm(ctypes.byref(e), None) == _native.MCB_ERR_ALIGNMENT
+    s = SoftcapArgs()
+    s.logits, s.rows, s.V, s.logits_stride = 16, 2, 1000, 999
+    s.argmax = 64
+    assert lib.mcb_softcap_argmax(ctypes.byref(s), None) == _native.MCB_ERR_INVALID_ARG
+    s.logits_stride, s.argmax = 1024, None
+    assert lib.mcb_softcap_argmax(ctypes.byref(s), None) == _native.MCB_ERR_INVALID_ARG

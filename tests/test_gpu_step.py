@@ -117,6 +117,74 @@ def test_step_kernels_reject_unsupported_shapes(ops):
         ops.gated_silu(x, x)
 
 
+def test_embed_rms_norm_against_the_reference_and_the_oracle(ops):
+    z = load_golden("step_fused.npz")
+    ids = torch.from_numpy(z["ids"]).cuda()
+    x, h = ops.embed_rms_norm(ids, dev_bf16(z["wte"]))
+    torch.cuda.synchronize()
+    ox, oh = O.embed_rms_norm(z["ids"], z["wte"])
+    assert np.array_equal(host_bits(x), ox) and np.array_equal(host_bits(h), oh)
+    assert ulps(host_bits(x), z["embed_x"]).max() <= 1
+    assert ulps(host_bits(h), z["embed_h"]).max() <= 1
+
+
+def test_embed_rms_norm_against_torch_and_out_of_range_ids(ops):
+    g = torch.Generator(device="cuda").manual_seed(11)
+    table = (torch.randn(5000, 2048, device="cuda", generator=g) * 0.8).to(torch.bfloat16)
+    ids = torch.randint(0, 5000, (64, 1), device="cuda", generator=g)
+    x, h = ops.embed_rms_norm(ids, table)
+    x_t = F.rms_norm(table[ids], (2048,))
+    assert (ulps(host_bits(x), host_bits(x_t)) != 0).mean() <= 5e-3
+    assert ulps(host_bits(h), host_bits(F.rms_norm(x, (2048,)))).max() <= 1
+    assert ops.device_error()[0] == 0
+    bad = ids.clone()
+    bad[3, 0] = 5000
+    bad[7, 0] = -1
+    xb, hb = ops.embed_rms_norm(bad, table)
+    code, what = ops.device_error()
+    assert code == 4, what
+    assert not xb[3].any() and not hb[7].any()
+    assert torch.equal(xb[5], x[5])
+
+
+def _softcap_torch(lg, V, cap):
+    f = lg[..., :V].float()
+    return f if cap is None else cap * torch.tanh(f / cap)
+
+
+@pytest.mark.parametrize("rows,Vp,V,cap", [(64, 32768, 32768, 15.0), (9, 1024, 1000, 15.0),
+                                           (5, 1024, 1001, 30.0), (3, 512, 512, None)])
+def test_softcap_argmax_is_bit_exact_against_torch(ops, rows, Vp, V, cap):
+    """LMHead's crop + .float() + softcap as torch computes it on the GPU, and torch.argmax."""
+    g = torch.Generator(device="cuda").manual_seed(rows + V)
+    lg = (torch.randn(rows, Vp, device="cuda", generator=g) * 20).to(torch.bfloat16)
+    lg[0, 17] = lg[0, 900 % V] = 200.0    # a tie at the maximum: the first index wins
+    ids = torch.empty(rows, dtype=torch.int64, device="cuda")
+    out = ops.softcap_argmax(lg, V, cap, argmax_out=ids)
+    want = _softcap_torch(lg, V, cap)
+    assert out.shape == (rows, V)
+    assert torch.equal(out, want)
+    assert torch.equal(ids, torch.argmax(want, dim=-1))
+    assert ids[0].item() == 17
+    only = torch.zeros(rows, 1, dtype=torch.int64, device="cuda")
+    assert ops.softcap_argmax(lg, V, cap, want_logits=False, argmax_out=only) is None
+    assert torch.equal(only[:, 0], ids)
+
+
+def test_softcap_argmax_against_the_reference_lm_head(ops):
+    z = load_golden("step_fused.npz")
+    lg = dev_bf16(z["head_logits_bf16"])
+    ids = torch.empty(lg.shape[0], dtype=torch.int64, device="cuda")
+    out = ops.softcap_argmax(lg, 1000, 15, argmax_out=ids).cpu().numpy()
+    f32 = lambda a: a.view(np.int32).astype(np.int64)
+    assert np.abs(f32(out) - f32(z["head_out"])).max() <= 4
+    assert np.array_equal(ids.cpu().numpy(), np.argmax(z["head_out"], axis=-1))
+    # numpy's float32 tanh against the device's tanhf: a few ulps
+    assert np.abs(f32(out) - f32(O.softcap_logits(z["head_logits_bf16"], 1000, 15))).max() <= 4
+    nocap = ops.softcap_argmax(lg, 1000, None).cpu().numpy()
+    assert np.array_equal(nocap, z["head_out_nocap"])
+
+
 # ---------------------------------------------------------------------------------------------
 # the fused decode step through modelcore's API (bf16 weights: the fused path's precondition)
 LOGIT_TOL = 2e-2
@@ -147,6 +215,7 @@ def _models(env, config):
     mcb.install(fused, fuse_step=True)
     mcb.install(plain, fuse_step=False)
     assert step.installed(fused) and not step.installed(plain)
+    assert step.decode_installed(fused) and not step.decode_installed(plain)
     m32 = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
     ref32 = m32.create_model(config, device=torch.device("cpu"), seed=0)
     ref32.load_state_dict({k: v.float().cpu() for k, v in ref.state_dict().items()})
@@ -215,11 +284,24 @@ def test_fused_step_launches_and_graph_replay(env):
         n0 = ops.launch_count()
         eager.step(cols[0])
         per_step = ops.launch_count() - n0
-        attn_launches = per_step - (1 + 4 * 4 + 1)   # first norm, 4 per layer, the advance
+        # embedding + first norm, 4 per layer, the advance, the LM-head epilogue
+        attn_launches = per_step - (1 + 4 * 4 + 1 + 1)
         assert attn_launches in (4, 8), per_step     # one or two (split + combine) per layer
         graph.step(cols[0])                           # eager: the graph decoder's first step
         for col in cols[1:]:                          # capture, then replays
             assert torch.equal(eager.step(col), graph.step(col))
+        # the device-resident greedy loop (greedy pick fused into the LM-head epilogue) equals
+        # the host-driven loop over torch.argmax
+        g2 = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+        e2 = mgr.new_decoder(model, prompts, max_tokens=16)
+        dev_tokens = g2.greedy_steps(12).cpu()
+        host = []
+        for _ in range(12):
+            nxt = torch.argmax(e2.logits, dim=-1)
+            host.append(nxt.cpu())
+            e2.step(nxt.tolist())
+        assert torch.equal(dev_tokens, torch.stack(host, 1))
+        assert torch.equal(g2.logits, e2.logits)
 
 
 def test_packed_weights_follow_the_parameters(env):

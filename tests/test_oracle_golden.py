@@ -125,3 +125,26 @@ def test_gated_silu_matches_the_reference_mlp():
     diff = np.abs(got.astype(np.int32) - z["gated"].astype(np.int32))
     assert diff.max() <= 1
     assert (diff != 0).mean() <= 1e-3
+
+
+def test_embed_rms_norm_matches_the_reference_token_embedding():
+    z = load_golden("step_fused.npz")
+    x, h = O.embed_rms_norm(z["ids"], z["wte"])
+    assert np.array_equal(x, z["embed_x"])
+    assert np.array_equal(h, z["embed_h"])
+
+
+def _f32_ulps(a, b):
+    return np.abs(a.view(np.int32).astype(np.int64) - b.view(np.int32).astype(np.int64))
+
+
+def test_softcap_and_greedy_pick_match_the_reference_lm_head():
+    """The crop and .float() are exact; the softcap differs from the reference's CPU evaluation by
+    at most a few fp32 ulps (exact division and torch's vectorised tanh on the CPU, the reciprocal
+    multiply of torch's CUDA path and numpy's tanh here); the greedy pick agrees."""
+    z = load_golden("step_fused.npz")
+    assert np.array_equal(O.softcap_logits(z["head_logits_bf16"], 1000, None), z["head_out_nocap"])
+    y = O.softcap_logits(z["head_logits_bf16"], 1000, 15)
+    assert y.shape == z["head_out"].shape
+    assert _f32_ulps(y, z["head_out"]).max() <= 4
+    assert np.array_equal(O.greedy_pick(y), np.argmax(z["head_out"], axis=-1))

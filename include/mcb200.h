@@ -128,6 +128,8 @@ int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
  *    more than 2048 keys (min(Tmax, window + T)).
  *  - split: one CTA per row group and key split, partials merged by a second kernel when split.
  *    Chosen for shorter rows, where the persistent plan's fixed costs do not pay off.
+ *  - prefill (num_ctas == 0, T >= 64, D 64 or 128): 128-query x 128-key tiles on the tcgen05
+ *    tensor cores with TMEM accumulators (mcb_prefill_attn below); no workspace or counters.
  * ------------------------------------------------------------------------------------------- */
 typedef struct {
   const void* q;              /* (B,T,Hq,D) bf16                                            */
@@ -164,6 +166,14 @@ size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
 size_t mcb_decode_attn_counter_count(const mcb_attn_args* args);
 
 int mcb_decode_attn(const mcb_attn_args* args, void* stream);
+
+/* The prefill plan on its own, for any T >= 1: the attention of flash_attn_with_kvcache with
+ * T_new new tokens per row (modelcore/kernels/flash_attn.py:348-366 through _sdpa_attention,
+ * :203-244, whose dense causal mask :214-215 is the ragged mask with every L_b = 0).  One CTA
+ * per (row, q head, 128-query tile): S = Q K^T and O += P V as tcgen05.mma into TMEM, online
+ * softmax in fp32 between them, K/V tiles of 128 keys by TMA.  head_dim 64 or 128; q strides
+ * multiples of 8 elements; num_ctas, workspace and counters are ignored. */
+int mcb_prefill_attn(const mcb_attn_args* args, void* stream);
 
 /* mcb_decode_attn for callers that cannot allocate device memory.  No counterpart in the
  * reference: modelcore allocates through torch and has no such caller.

@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "mcb_add_rms_norm",
     "mcb_gated_silu",
     "mcb_embed_rms_norm",
+    "mcb_prefill_attn",
     "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
@@ -178,6 +179,8 @@ def _declare(lib):
     lib.mcb_add_rms_norm.argtypes = [P(AddNormArgs), ctypes.c_void_p]
     lib.mcb_gated_silu.restype = ctypes.c_int
     lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
+    lib.mcb_prefill_attn.restype = ctypes.c_int
+    lib.mcb_prefill_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]
     lib.mcb_embed_rms_norm.restype = ctypes.c_int
     lib.mcb_embed_rms_norm.argtypes = [P(EmbedArgs), ctypes.c_void_p]
     lib.mcb_softcap_argmax.restype = ctypes.c_int

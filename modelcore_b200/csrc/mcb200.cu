@@ -16,6 +16,7 @@
 #include "decode_attn_split.cuh"
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
+#include "prefill_attn.cuh"
 #include "step_fused.cuh"
 
 namespace {
@@ -94,7 +95,28 @@ cudaError_t ensure_smem(K kernel, int bytes, std::atomic<uint64_t>& done) {
 constexpr int kKPW = 16;             // keys per consumer warp per tile (tile = 64 keys)
 constexpr long long kSplitMaxTiles = 33;  // 2048 keys + one tile of alignment slack
 
-enum AttnMode { kModePersistent = 0, kModeSplit = 1 };
+enum AttnMode { kModePersistent = 0, kModeSplit = 1, kModePrefill = 2 };
+
+// With num_ctas == 0, T_new >= kPrefillMinT and head_dim 64 or 128, the tensor-core prefill
+// kernel (prefill_attn.cuh) runs instead: 128-query tiles on tcgen05, no workspace.
+constexpr int kPrefillMinT = 64;
+
+template <int D>
+struct PrefillVariant {
+  using Cfg = mcb::PrefillConfig<D>;
+  static constexpr auto kernel = mcb::prefill_attn_kernel<D>;
+  static int launch(long long grid, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                    const mcb::PrefillParams& prm, cudaStream_t st) {
+    static std::atomic<uint64_t> done{0};
+    cudaError_t e = ensure_smem(kernel, Cfg::kSmem, done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_attn)");
+    kernel<<<static_cast<unsigned>(grid), mcb::kPfThreads, Cfg::kSmem, st>>>(qm, km, vm, prm);
+    g_launches++;
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "prefill_attn launch");
+    return MCB_OK;
+  }
+};
 
 template <int D, int NQT>
 struct AttnVariant {
@@ -211,6 +233,17 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
                 a->D);
   const int G = a->Hq / a->Hkv;
   pl->D = a->D;
+  if (a->num_ctas == 0 && a->T >= kPrefillMinT && (a->D == 64 || a->D == 128)) {
+    pl->mode = kModePrefill;
+    pl->nqt = pl->rows = pl->nqb = 0;
+    pl->tk = mcb::kPfTile;
+    pl->grid = pl->nsplit = pl->tps = 0;
+    pl->part_o_bytes = pl->part_lse_bytes = pl->ws_bytes = pl->counter_count = 0;
+    const long long qtiles = (a->T + mcb::kPfTile - 1) / mcb::kPfTile;
+    if (qtiles * a->B * a->Hq > 0x7fffffffll)
+      return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: prefill grid too large");
+    return MCB_OK;
+  }
   const long long rows_total = static_cast<long long>(a->T) * G;
   pl->nqt = (rows_total <= 8 || a->D == 256) ? 1 : 2;
   pl->rows = 8 * pl->nqt;
@@ -305,9 +338,53 @@ int check_attn_pointers(const mcb_attn_args* a, const char* who) {
   return MCB_OK;
 }
 
+// q as a 4-D tensor map {D, Hq, T, B} with its own strides; 128-query boxes of 64-column panels.
+int encode_q_map(CUtensorMap* map, const mcb_attn_args* a) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a->D), static_cast<cuuint64_t>(a->Hq),
+                        static_cast<cuuint64_t>(a->T), static_cast<cuuint64_t>(a->B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a->q_stride[2]) * 2,
+                           static_cast<cuuint64_t>(a->q_stride[1]) * 2,
+                           static_cast<cuuint64_t>(a->q_stride[0]) * 2};
+  cuuint32_t box[4] = {64u, 1u, static_cast<cuuint32_t>(mcb::kPfTile), 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a->q), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled(q) failed (CUresult %d)", (int)r);
+  return MCB_OK;
+}
+
+int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
+  CUtensorMap qm, km, vm;
+  int rc = encode_q_map(&qm, a);
+  if (rc != MCB_OK) return rc;
+  rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, mcb::kPfTile);
+  if (rc != MCB_OK) return rc;
+  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, mcb::kPfTile);
+  if (rc != MCB_OK) return rc;
+  mcb::PrefillParams p;
+  p.out = static_cast<uint16_t*>(a->out);
+  p.cache_seqlens = a->cache_seqlens;
+  p.B = a->B;
+  p.T = a->T;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.G = a->Hq / a->Hkv;
+  p.Tmax = a->Tmax;
+  p.window = a->window;
+  p.n_qpairs = (a->T + 2 * mcb::kPfTile - 1) / (2 * mcb::kPfTile);
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  const long long grid = static_cast<long long>(p.n_qpairs) * a->B * a->Hq;
+  if (a->D == 64) return PrefillVariant<64>::launch(grid, qm, km, vm, p, st);
+  return PrefillVariant<128>::launch(grid, qm, km, vm, p, st);
+}
+
 // Encodes the tensor maps, fills the kernel parameters with the workspace `ws` (and, for the
 // persistent kernel, the arrival counters) and launches.
 int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* counters, cudaStream_t st) {
+  if (pl.mode == kModePrefill) return run_prefill(a, st);
   CUtensorMap km, vm;
   int rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
   if (rc != MCB_OK) return rc;
@@ -681,6 +758,20 @@ size_t mcb_decode_attn_counter_count(const mcb_attn_args* a) {
   AttnPlan pl;
   if (plan_attn(a, &pl) != MCB_OK) return 0;
   return pl.counter_count;
+}
+
+int mcb_prefill_attn(const mcb_attn_args* a, void* stream) {
+  AttnPlan pl;
+  int rc = plan_attn(a, &pl);  // shape validation
+  if (rc != MCB_OK) return rc;
+  if (a->D != 64 && a->D != 128)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_prefill_attn: head_dim %d not supported (64/128)", a->D);
+  if ((static_cast<long long>(a->T) + mcb::kPfTile - 1) / mcb::kPfTile * a->B * a->Hq > 0x7fffffffll)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_prefill_attn: grid too large");
+  rc = check_attn_pointers(a, "mcb_prefill_attn");
+  if (rc != MCB_OK) return rc;
+  if (a->B == 0 || a->T == 0) return MCB_OK;
+  return run_prefill(a, static_cast<cudaStream_t>(stream));
 }
 
 int mcb_decode_attn(const mcb_attn_args* a, void* stream) {

@@ -1,0 +1,445 @@
+// Prefill attention through the cache on the 5th-generation tensor cores (tcgen05, TMEM, TMA).
+//
+// The attention of flash_attn_with_kvcache with T_new > 1 (modelcore/kernels/flash_attn.py:348-366,
+// _sdpa_attention :203-244 with _ragged_decode_mask :246-264): query t of row b sits at position
+// L_b + t and sees cache keys c <= L_b + t within the window.  The new tokens' K/V are already in
+// the cache (the append ran first), so a prompt's prefill is dense causal attention over its own
+// keys plus whatever prefix the row already held.
+//
+// One CTA takes two 128-query tiles (Q0, Q1: 256 consecutive queries) of one q head of one row
+// and walks 128-key tiles, each K/V tile serving both query tiles:
+//
+//   warp 0       TMA producer: Q0 and Q1 once, then K_j and V_j into a two-stage ring
+//   warp 1       allocates all 512 TMEM columns; lane 0 issues the MMAs, ping-ponging the tiles:
+//                  S0_j = Q0 K_j^T, S1_j = Q1 K_j^T      kind::f16, M=128 N=128 K=D, A and B
+//                                                        from shared memory, fp32 into TMEM
+//                  O0 += P0_j V_j, O1 += P1_j V_j        M=128 N=D K=128, A = P from TMEM (P is
+//                                                        written over S as bf16), B = V MN-major
+//                in the order S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | ... so the
+//                tensor core computes one tile's S while the other tile's softmax runs
+//   warps 4-7    softmax of Q0, warps 8-11 softmax of Q1: one thread per query row (TMEM lane =
+//                row): S from TMEM, mask only on tiles that cross the diagonal, the window edge or
+//                the end of the rows; online max with a lazy rescale (the running max moves, and
+//                O and the row sum are rescaled, only when a row's max grows by more than 2^8);
+//                P = exp2(S * scale * log2 e - max) written back into TMEM as bf16; at the end
+//                O / sum as bf16 to the output
+//
+// Tensor-core MMAs issued by one thread execute in order, so S_{j+1} may overwrite the columns
+// that held P_j once PV_j was issued before it, and a completed S_{j+1} implies a completed PV_j
+// (the softmax warps rescale O only then).
+//
+// TMEM: S0 columns [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).  Every wait is
+// bounded (2 s); a timeout raises the CTA's abort flag, every later wait returns at once, the MMA
+// issuer waits (bounded) for its committed MMAs, and TMEM is freed before the CTA exits.
+#pragma once
+
+#include "common.cuh"
+
+namespace mcb {
+
+constexpr int kPfTile = 128;          // queries per query tile and keys per key tile
+constexpr int kPfThreads = 384;       // 12 warps
+constexpr uint32_t kPfTmemCols = 512;
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 helpers
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc], bf16 in, fp32 accumulate.
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A is M rows (TMEM lanes) x K bf16, two per column.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on `bar` when every tcgen05 operation this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 128 consecutive 32-bit TMEM columns of this warp's 32 lanes (lane i: row lane_base + i),
+// waited for inside the same asm so no use of the values can move above the wait.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%129];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95}, [%130];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%131];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr + 0u), "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u)
+      : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes (lane i: row lane_base + i),
+// waited for inside the same asm so no use of the values can move above the wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr + 0u)
+      : "memory");
+}
+
+// Stores 64 consecutive 32-bit TMEM columns of this warp's 32 lanes and waits for them.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33};\n\t"
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%1], {%34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      :
+      : "r"(taddr + 0u), "r"(taddr + 32u), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
+      : "memory");
+}
+
+// Stores 32 consecutive 32-bit TMEM columns of this warp's 32 lanes and waits for them.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      :
+      : "r"(taddr + 0u), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1"), 128B swizzle.  Addresses and offsets
+// are in bytes; the descriptor keeps them >> 4.
+//   K-major tile (rows of 64 bf16 = 128 B, 8-row atoms of 1024 B stacked): LBO 16 B (unused),
+//   SBO 1024 B.  MN-major tile (64 N-values per 128 B row, one row per K index): LBO = stride
+//   between 64-wide N panels, SBO = stride between 8-row K groups (1024 B).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3fffu) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) |  // version 1
+         (2ull << 61);                                                          // SWIZZLE_128B
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, M x N, A K-major, B K-major
+// (b_mn_major = 0) or MN-major (1).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+struct PrefillParams {
+  uint16_t* out;              // (B, T, Hq, D) bf16 contiguous
+  const int* cache_seqlens;   // (B,) positions before the new tokens
+  int B, T, Hq, Hkv, G, Tmax, window;
+  int n_qpairs;               // ceil(T / 256)
+  float scale_log2;           // softmax_scale * log2(e)
+};
+
+template <int D>
+struct PrefillConfig {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kTileBytes = kPanels * kPfTile * 128;  // one Q / K / V tile
+  static constexpr int kQOff = 0;                             // Q0, Q1
+  static constexpr int kKOff = kQOff + 2 * kTileBytes;        // K ring, 2 stages
+  static constexpr int kVOff = kKOff + 2 * kTileBytes;        // V ring, 2 stages
+  static constexpr int kBarOff = kVOff + 2 * kTileBytes;
+  static constexpr int kBytes = kBarOff + 256;
+  // at least 116 KB so two CTAs never share an SM: each holds all 512 TMEM columns
+  static constexpr int kSmem = (kBytes + 1024 > 118784 ? kBytes + 1024 : 118784);
+};
+
+// The first key tile a query tile needs and how many tiles (from k_first) it spans.
+struct QTileRange {
+  int qbase, j_begin, j_end;  // key tiles [j_begin, j_end) of the CTA's walk
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
+                        const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  using Cfg = PrefillConfig<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2] per query tile
+  uint64_t* p_full = bars + 9;    // [2] per query tile, 128 arrivals
+  uint64_t* o_done = bars + 11;
+  uint64_t* drained = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 14);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = p.B * p.Hq;
+  const int qp = p.n_qpairs - 1 - static_cast<int>(blockIdx.x / bh);  // longest pairs first
+  const int b = static_cast<int>(blockIdx.x % bh) / p.Hq;
+  const int h = static_cast<int>(blockIdx.x % bh) % p.Hq;
+  const int hk = h / p.G;
+  const int L = p.cache_seqlens[b];
+  const int q0 = qp * 2 * kPfTile;
+  const int pos_last = L + min(q0 + 2 * kPfTile, p.T) - 1;
+  const bool in_range = L >= 0 && pos_last < p.Tmax;
+  const int k_first =
+      (p.window >= 0 ? max(0, L + q0 - p.window) : 0) / kPfTile * kPfTile;
+  QTileRange rng[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qb = q0 + t * kPfTile;
+    rng[t].qbase = qb;
+    if (!in_range || qb >= p.T) {
+      rng[t].j_begin = rng[t].j_end = 0;
+    } else {
+      const int first = (p.window >= 0 ? max(0, L + qb - p.window) : 0) / kPfTile * kPfTile;
+      rng[t].j_begin = (first - k_first) / kPfTile;
+      rng[t].j_end = (L + min(qb + kPfTile, p.T) - 1 - k_first) / kPfTile + 1;
+    }
+  }
+  const int nkv = max(rng[0].j_end, rng[1].j_end);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 13; ++i) mbar_init(bars + i, (i == 9 || i == 10) ? 128 : 1);
+    *abort_flag = 0;
+    if (!in_range) record_error(kErrPositionBeyondCache);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kPfTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t base = smem_u32(smem);
+
+  if (warp == 0 && lane == 0 && nkv > 0) {
+    // ---------------- TMA producer ----------------
+    const uint64_t pol = l2_policy_evict_first();
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    mbar_arrive_expect_tx(q_full, 2 * Cfg::kTileBytes);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int pn = 0; pn < Cfg::kPanels; ++pn)
+        tma_load_4d(smem + Cfg::kQOff + t * Cfg::kTileBytes + pn * kPfTile * 128, &qmap, q_full,
+                    pn * 64, h, q0 + t * kPfTile, b, pol);
+    int issued = 0;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (j >= 2 && !mbar_wait_or_abort(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag)) break;
+      const int k0 = k_first + j * kPfTile;
+      mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
+#pragma unroll
+      for (int pn = 0; pn < Cfg::kPanels; ++pn)
+        tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &kmap,
+                    &k_full[st], pn * 64, hk, k0, b, pol);
+      mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
+#pragma unroll
+      for (int pn = 0; pn < Cfg::kPanels; ++pn)
+        tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &vmap,
+                    &v_full[st], pn * 64, hk, k0, b, pol);
+      issued = j + 1;
+    }
+    // on an abort, wait (bounded) for the copies still in flight before the CTA can exit
+    if (*abort_flag) {
+      for (int j = max(0, issued - 2); j < issued; ++j) {
+        mbar_wait(&k_full[j & 1], (j >> 1) & 1);
+        mbar_wait(&v_full[j & 1], (j >> 1) & 1);
+      }
+      mbar_wait(q_full, 0);
+    }
+  } else if (warp == 1 && lane == 0 && nkv > 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc_s = umma_idesc_bf16(128, kPfTile, 0);
+    constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 1);
+    bool ok = mbar_wait_or_abort(q_full, 0, abort_flag);
+    int k_waited = -1, v_waited = -1;
+    int pv_count[2] = {0, 0};
+    auto active = [&](int t, int j) { return j >= rng[t].j_begin && j < rng[t].j_end; };
+    auto issue_s = [&](int t, int j) -> bool {
+      if (k_waited < j) {
+        if (!mbar_wait_or_abort(&k_full[j & 1], (j >> 1) & 1, abort_flag)) return false;
+        k_waited = j;
+      }
+      tc_fence_after();
+      const uint32_t q_base = base + Cfg::kQOff + t * Cfg::kTileBytes;
+      const uint32_t k_base = base + Cfg::kKOff + (j & 1) * Cfg::kTileBytes;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * (kPfTile * 128) + (kk & 3) * 32;
+        umma_ss(tmem + t * kPfTile, smem_desc_sw128(q_base + off, 16, 1024),
+                smem_desc_sw128(k_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[t]);
+      return true;
+    };
+    auto issue_pv = [&](int t, int j) -> bool {
+      if (!mbar_wait_or_abort(&p_full[t], pv_count[t] & 1, abort_flag)) return false;
+      if (v_waited < j) {
+        if (!mbar_wait_or_abort(&v_full[j & 1], (j >> 1) & 1, abort_flag)) return false;
+        v_waited = j;
+      }
+      tc_fence_after();
+      const uint32_t v_base = base + Cfg::kVOff + (j & 1) * Cfg::kTileBytes;
+#pragma unroll
+      for (int kk = 0; kk < kPfTile / 16; ++kk)
+        umma_ts(tmem + 256 + t * D, tmem + t * kPfTile + kk * 8,
+                smem_desc_sw128(v_base + kk * 16 * 128, kPfTile * 128, 1024), idesc_o,
+                (pv_count[t] > 0 || kk > 0) ? 1u : 0u);
+      ++pv_count[t];
+      return true;
+    };
+    if (ok && active(0, 0)) ok = issue_s(0, 0);
+    if (ok && active(1, 0)) ok = issue_s(1, 0);
+    for (int j = 0; ok && j < nkv; ++j) {
+      if (ok && active(0, j)) ok = issue_pv(0, j);
+      if (ok && active(0, j + 1)) ok = issue_s(0, j + 1);
+      if (ok && active(1, j)) ok = issue_pv(1, j);
+      if (ok) umma_commit(&kv_empty[j & 1]);
+      if (ok && active(1, j + 1)) ok = issue_s(1, j + 1);
+    }
+    if (ok) umma_commit(o_done);
+    // every MMA this thread issued has completed before TMEM can be freed
+    umma_commit(drained);
+    mbar_wait(drained, 0);
+  } else if (warp >= 4) {
+    // ---------------- softmax: warps 4-7 query tile 0, warps 8-11 query tile 1 ----------------
+    const int t = (warp - 4) >> 2;
+    const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
+    const int row = quarter * 32 + lane;          // query row within the tile
+    const int qbase = rng[t].qbase;
+    const int q = qbase + row;
+    const bool valid = q < p.T;
+    const int pos = L + q;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + t * kPfTile;
+    const uint32_t o_addr = tmem + lane_off + 256 + t * D;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    int cnt = 0;
+    for (int j = rng[t].j_begin; j < rng[t].j_end; ++j, ++cnt) {
+      // waits are made warp-uniform: the tcgen05.ld/st below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[t], cnt & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = k_first + j * kPfTile;
+      uint32_t sr[128];
+      tmem_ld128(s_addr, sr);
+      float mx = -INFINITY;
+      const bool full = k0 + kPfTile - 1 <= L + qbase &&
+                        (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
+                        qbase + kPfTile <= p.T;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const float s = __uint_as_float(sr[i]) * p.scale_log2;
+          sr[i] = __float_as_uint(s);
+          mx = fmaxf(mx, s);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const int key = k0 + i;
+          const bool vis = valid && key <= pos && (p.window < 0 || pos - key <= p.window);
+          const float s = vis ? __uint_as_float(sr[i]) * p.scale_log2 : -INFINITY;
+          sr[i] = __float_as_uint(s);
+          mx = fmaxf(mx, s);
+        }
+      }
+      // lazy rescale: move the running max only when it grows by more than 2^8
+      float alpha = 1.f;
+      if (mx > m_used + 8.f) {
+        alpha = fast_exp2(m_used - mx);  // 0 when m_used is -inf
+        m_used = mx;
+        l *= alpha;
+      }
+      const float m_exp = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float e0 = fast_exp2(__uint_as_float(sr[2 * i]) - m_exp);
+        const float e1 = fast_exp2(__uint_as_float(sr[2 * i + 1]) - m_exp);
+        sum += e0 + e1;
+        pk[i] = pack_bf16x2(e0, e1);
+      }
+      l += sum;
+      tmem_st64(s_addr, pk);  // P over the first 64 columns of S
+      if (cnt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    // epilogue: O / l -> bf16 -> out[b, q, h, :]
+    if (ok && cnt > 0 && __all_sync(0xffffffffu, mbar_wait_or_abort(o_done, 0, abort_flag))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint16_t* dst = p.out + ((static_cast<long long>(b) * p.T + q) * p.Hq + h) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        if (valid) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + 8 * u) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kPfTmemCols);
+  }
+}
+
+}  // namespace mcb

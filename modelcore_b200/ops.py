@@ -281,6 +281,21 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     return out
 
 
+def prefill_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None, out=None):
+    """decode_attn's semantics on the tensor-core prefill kernel (mcb_prefill_attn), for any T:
+    128-query tiles, S = Q K^T and O += P V as tcgen05 MMAs with TMEM accumulators.  head_dim 64
+    or 128.  decode_attn picks this plan itself for T >= 64 with num_ctas=0."""
+    if out is None:
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    else:
+        _need("out", out, 4)
+        if out.shape != q.shape or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous tensor shaped like q")
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, 0, out)
+    check(_native.load().mcb_prefill_attn(ctypes.byref(args), _stream(q)))
+    return out
+
+
 def decode_attn_noalloc(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
                         num_ctas=0, out=None):
     """decode_attn through mcb_decode_attn_noalloc: for callers that cannot allocate device

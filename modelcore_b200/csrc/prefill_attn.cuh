@@ -17,8 +17,8 @@
 //                                                        written over S as bf16), B = V MN-major
 //                in the order S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | ... so the
 //                tensor core computes one tile's S while the other tile's softmax runs
-//   warps 4-7    softmax of Q0, warps 8-11 softmax of Q1: one thread per query row (TMEM lane =
-//                row): S from TMEM, mask only on tiles that cross the diagonal, the window edge or
+//   warps 2-5    softmax of Q0, warps 6-9 softmax of Q1: one thread per query row (TMEM lane =
+//                row; warp w reaches lanes 32 (w % 4) .. +31, so each group of four covers all 128): S from TMEM, mask only on tiles that cross the diagonal, the window edge or
 //                the end of the rows; online max with a lazy rescale (the running max moves, and
 //                O and the row sum are rescaled, only when a row's max grows by more than 2^8);
 //                P = exp2(S * scale * log2 e - max) written back into TMEM as bf16; at the end
@@ -38,7 +38,7 @@
 namespace mcb {
 
 constexpr int kPfTile = 128;          // queries per query tile and keys per key tile
-constexpr int kPfThreads = 384;       // 12 warps
+constexpr int kPfThreads = 320;       // 10 warps
 constexpr uint32_t kPfTmemCols = 512;
 
 // ---------------------------------------------------------------------------------------------
@@ -129,6 +129,63 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       :
       : "r"(taddr + 0u), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+// Stores 16 consecutive 32-bit TMEM columns of this warp's 32 lanes (no wait: the registers are
+// read at issue; tmem_st_wait() orders the stores before a fence).
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+      :
+      : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Packed fp32 pairs (sm_100): one instruction for two lanes' worth of FMA / add.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two floats to packed bf16x2 (lo in the low half), round-to-nearest-even, one instruction.
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// 2^x on the FMA pipe, for x <= 8 (and 0 below -125): x = n + f with n = round(x) by the
+// 1.5 * 2^23 rounding constant, f in [-1/2, 1/2], 2^f by a cubic fitted here (least squares on
+// Chebyshev nodes, reweighted toward equal-ripple relative error: 7.5e-5 at most, far below
+// bf16's 2^-8), and n added to the exponent field.  One in four of a tile's exponentials takes
+// this path so the MUFU unit, which the two query tiles' softmax warps share, is not the limit.
+__device__ __forceinline__ float exp2_poly3(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  float q = fmaf(0.0551716648f, f, 0.242611125f);
+  q = fmaf(q, f, 0.693260968f);
+  q = fmaf(q, f, 0.999928057f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(q) + (n << 23));
+  return x < -125.f ? 0.f : r;
 }
 
 // Shared-memory matrix descriptor (tcgen05 "version 1"), 128B swizzle.  Addresses and offsets
@@ -332,9 +389,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // every MMA this thread issued has completed before TMEM can be freed
     umma_commit(drained);
     mbar_wait(drained, 0);
-  } else if (warp >= 4) {
-    // ---------------- softmax: warps 4-7 query tile 0, warps 8-11 query tile 1 ----------------
-    const int t = (warp - 4) >> 2;
+  } else if (warp >= 2) {
+    // ---------------- softmax: warps 2-5 query tile 0, warps 6-9 query tile 1 ----------------
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;          // query row within the tile
     const int qbase = rng[t].qbase;
@@ -356,28 +413,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_fence_after();
       const int k0 = k_first + j * kPfTile;
       uint32_t sr[128];
-      tmem_ld128(s_addr, sr);
+      tmem_ld128(s_addr, sr);  // one round trip: TMEM load latency dominates a chunked read
+      // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
       float mx = -INFINITY;
       const bool full = k0 + kPfTile - 1 <= L + qbase &&
                         (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
                         qbase + kPfTile <= p.T;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const float s = __uint_as_float(sr[i]) * p.scale_log2;
-          sr[i] = __float_as_uint(s);
-          mx = fmaxf(mx, s);
-        }
-      } else {
+      if (!full) {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
           const int key = k0 + i;
           const bool vis = valid && key <= pos && (p.window < 0 || pos - key <= p.window);
-          const float s = vis ? __uint_as_float(sr[i]) * p.scale_log2 : -INFINITY;
-          sr[i] = __float_as_uint(s);
-          mx = fmaxf(mx, s);
+          if (!vis) sr[i] = __float_as_uint(-INFINITY);
         }
       }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmax3(mx, __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]));
+      mx *= p.scale_log2;
       // lazy rescale: move the running max only when it grows by more than 2^8
       float alpha = 1.f;
       if (mx > m_used + 8.f) {
@@ -385,18 +437,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         m_used = mx;
         l *= alpha;
       }
-      const float m_exp = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
-      uint32_t pk[64];
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      const float sc = p.scale_log2;
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float e0 = fast_exp2(__uint_as_float(sr[2 * i]) - m_exp);
-        const float e1 = fast_exp2(__uint_as_float(sr[2 * i + 1]) - m_exp);
-        sum += e0 + e1;
-        pk[i] = pack_bf16x2(e0, e1);
+      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns of packed bf16 P over S
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {  // 4 keys: three exponentials on MUFU, one on the FMA pipe
+          const int k = 32 * c + 4 * i;
+          float x0, x1, x2, x3;
+          ffma2(x0, x1, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), sc, sc, neg_m, neg_m);
+          ffma2(x2, x3, __uint_as_float(sr[k + 2]), __uint_as_float(sr[k + 3]), sc, sc, neg_m, neg_m);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2);
+          const float e3 = exp2_poly3(x3);
+          fadd2(sum0, sum1, sum0, sum1, e0, e1);
+          fadd2(sum0, sum1, sum0, sum1, e2, e3);
+          pk[2 * i] = pack_bf16x2_rn(e0, e1);
+          pk[2 * i + 1] = pack_bf16x2_rn(e2, e3);
+        }
+        tmem_st16_nowait(s_addr + 16 * c, pk);
       }
+      const float sum = sum0 + sum1;
       l += sum;
-      tmem_st64(s_addr, pk);  // P over the first 64 columns of S
+      tmem_st_wait();
       if (cnt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {

@@ -152,6 +152,17 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
+// (d0, d1) = (a0, a1) * b + c with b, c packed pairs (a pair of equal scalars here).
+__device__ __forceinline__ void ffma2_bc(float& d0, float& d1, float a0, float a1, uint64_t b,
+                                         uint64_t c) {
+  asm("{\n\t.reg .b64 ra, rd;\n\tmov.b64 ra, {%2, %3};\n\t"
+      "fma.rn.f32x2 rd, ra, %4, %5;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "l"(b), "l"(c));
+}
+__device__ __forceinline__ uint64_t pair_f32(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
 __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
   asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
       "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
@@ -438,25 +449,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         l *= alpha;
       }
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-      const float sc = p.scale_log2;
+      const uint64_t sc2 = pair_f32(p.scale_log2, p.scale_log2), nm2 = pair_f32(neg_m, neg_m);
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns of packed bf16 P over S
-        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {  // 4 keys: three exponentials on MUFU, one on the FMA pipe
           const int k = 32 * c + 4 * i;
           float x0, x1, x2, x3;
-          ffma2(x0, x1, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), sc, sc, neg_m, neg_m);
-          ffma2(x2, x3, __uint_as_float(sr[k + 2]), __uint_as_float(sr[k + 3]), sc, sc, neg_m, neg_m);
+          ffma2_bc(x0, x1, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), sc2, nm2);
+          ffma2_bc(x2, x3, __uint_as_float(sr[k + 2]), __uint_as_float(sr[k + 3]), sc2, nm2);
           const float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2);
           const float e3 = exp2_poly3(x3);
-          fadd2(sum0, sum1, sum0, sum1, e0, e1);
-          fadd2(sum0, sum1, sum0, sum1, e2, e3);
-          pk[2 * i] = pack_bf16x2_rn(e0, e1);
-          pk[2 * i + 1] = pack_bf16x2_rn(e2, e3);
+          sum0 += e0 + e2;
+          sum1 += e1 + e3;
+          // the packed P words reuse the registers of scores already consumed
+          sr[32 * c + 2 * i] = pack_bf16x2_rn(e0, e1);
+          sr[32 * c + 2 * i + 1] = pack_bf16x2_rn(e2, e3);
         }
-        tmem_st16_nowait(s_addr + 16 * c, pk);
+        tmem_st16_nowait(s_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
       }
       const float sum = sum0 + sum1;
       l += sum;

@@ -60,6 +60,15 @@ def _ensure_modelcore():
         import modelcore  # noqa: F401
 
 
+def _bf16_peak():
+    """Dense bf16 TFLOP/s measured on this pool (burst: a kernel timed alone), else fallback."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def _peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -354,6 +363,50 @@ def _copy_and_append(peak):
     return out
 
 
+def _prefill(tflops_peak):
+    """The tensor-core prefill attention (tcgen05) against the measured dense bf16 peak.
+
+    config 3's longest prompt (8,192 tokens, 16 q / 4 kv heads of 128, full window and window
+    1024) and config 2's prefill (64 prompts x 512 tokens, 12 / 12 heads of 64), each as one
+    mcb_decode_attn call over an empty cache (the automatic prefill plan).  Algorithmic FLOPs =
+    4 * D * Hq * (visible keys summed over queries): QK^T and PV, causal.  L2 flushed before
+    each timed launch."""
+    import torch
+    from modelcore_b200 import ops
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    rows = []
+    for name, B, T, Hq, Hkv, D, window in (("config 3 prompt, 8192 tokens", 1, 8192, 16, 4, 128, -1),
+                                            ("config 3 prompt, 8192 tokens, window 1024", 1, 8192, 16, 4, 128, 1024),
+                                            ("config 2 prefill, 64 prompts x 512 tokens", 64, 512, 12, 12, 64, -1)):
+        g = torch.Generator(device="cuda").manual_seed(2)
+        q = torch.randn(B, T, Hq, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        kc = torch.randn(B, T, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        vc = torch.randn(B, T, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        sl = torch.zeros(B, dtype=torch.int32, device="cuda")
+        out = torch.empty_like(q)
+        keys = sum(min(t + 1, window + 1) if window >= 0 else t + 1 for t in range(T))
+        flops = 4 * D * Hq * B * keys
+        ts = []
+        for i in range(6):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ops.decode_attn(q, kc, vc, sl, window=window, out=out)
+            b.record(stream)
+            torch.cuda.synchronize()
+            if i:
+                ts.append(a.elapsed_time(b) * 1e3)
+        us = statistics.median(ts)
+        rows.append({"workload": name, "kernel": "mcb::prefill_attn_kernel<%d>" % D, "us": round(us, 1),
+                     "tflops": round(flops / us / 1e6, 1),
+                     "frac": round(flops / us / 1e6 / tflops_peak, 3)})
+        del q, kc, vc, out
+    del flush
+    torch.cuda.empty_cache()
+    return rows
+
+
 def _cpu_reference_decode(rows, steps, warmup, threads=None):
     """The reference itself (modelcore's Decoder over its KVCache and SDPA path, fp32 on the host
     cores) on `rows` of the same prompts; returns (tokens/s, seconds per step, cores)."""
@@ -420,6 +473,14 @@ def _config(n):
             "seq_len": PROMPT_LEN + DECODE_LEN, "prompt_len": PROMPT_LEN,
             "parallelism": f"batch-sharded replicas x{n}",
             "l2": "inputs larger than L2: 1.2-2.4 GB of KV + 0.2 GB of weights per step per GPU"}
+
+
+def run_prefill_only(args):
+    """--prefill-only: the prefill-attention measurements alone (used for small ncu captures)."""
+    import torch
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    _ensure_modelcore()
+    print(json.dumps({"prefill_attention": _prefill(_bf16_peak())}), flush=True)
 
 
 def run_sweep_only(args):
@@ -497,9 +558,10 @@ def run_b200(args):
     if world == 1 and not args.no_sweep:
         sweep = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
                                windows=tuple(args.sweep_windows))
-    copies = None
+    copies = prefill = None
     if world == 1 and not args.no_sweep:
         copies = _copy_and_append(peak)
+        prefill = _prefill(_bf16_peak())
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
@@ -541,6 +603,7 @@ def run_b200(args):
         "cpu_baseline": cpu,
         "kv_read_sweep": sweep,
         "kv_copies": copies,
+        "prefill_attention": prefill,
     }
     print(json.dumps(line), flush=True)
 
@@ -557,6 +620,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the prefill-attention measurements")
     ap.add_argument("--sweep-batches", type=int, nargs="+", default=[1, 8, 64, 256, 512])
     ap.add_argument("--sweep-windows", type=int, nargs="+", default=[-1, 4096])
     args = ap.parse_args()
@@ -566,6 +631,8 @@ def main():
         run_reference(args)
     elif args.sweep_only:
         run_sweep_only(args)
+    elif args.prefill_only:
+        run_prefill_only(args)
     else:
         run_b200(args)
         import torch.distributed as dist

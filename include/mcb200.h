@@ -270,6 +270,24 @@ typedef struct {
 
 int mcb_softcap_argmax(const mcb_softcap_args* args, void* stream);
 
+/* mcb_sample: one token per row from fp32 logits, sample_next_token (modelcore/generate.py:19-34)
+ * for temperature > 0: with 1 <= top_k <= 1024 (and top_k < V) the top_k largest logits (ties by
+ * ascending index), divided by the temperature, softmax, one draw; otherwise softmax over the
+ * whole row, one draw.  The draw is the inverse CDF at u = uniforms[r] in [0, 1) (candidates in
+ * descending-logit order, or index order for the whole row), so it is a deterministic function of
+ * (logits, u) with the reference's distribution over u.  temperature == 0 is the greedy pick:
+ * call with top_k = 1 (any temperature > 0) or use mcb_softcap_argmax. */
+typedef struct {
+  const float* logits;        /* (rows, >= V) fp32                                          */
+  const float* uniforms;      /* (rows,) in [0, 1)                                          */
+  int64_t* out;               /* (rows,) int64 at out_stride                                */
+  int64_t logits_stride, out_stride;
+  int32_t rows, V, top_k;
+  float temperature;          /* > 0                                                        */
+} mcb_sample_args;
+
+int mcb_sample(const mcb_sample_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
  * overflow) or a timed-out pipeline wait sets a device error word and skips the access.

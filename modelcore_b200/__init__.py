@@ -7,6 +7,7 @@ Public surface (mirrors modelcore's names for this path):
   ModelManager              modelcore.ModelManager with the decode path installed (needs modelcore)
   install / uninstall       bind / unbind the B200 attention forward on a built modelcore model
   GraphDecoder              modelcore's Decoder stepping through a captured CUDA graph
+  sample_next_token         modelcore.generate.sample_next_token on one libmcb200 kernel
   ops                       the torch-facing wrappers of the C ABI (include/mcb200.h)
 
 The kernels live in libmcb200.so next to this file (build: `python -m modelcore_b200.build`).
@@ -16,9 +17,10 @@ here has a CPU or pure-Python fallback.
 from . import _native, ops
 from .cache import KVCache
 from .flash_attn import flash_attn, flash_attn_with_kvcache
+from .sampling import sample_next_token
 
 __all__ = ["KVCache", "flash_attn", "flash_attn_with_kvcache", "ModelManager", "install",
-           "uninstall", "GraphDecoder", "ops"]
+           "uninstall", "GraphDecoder", "sample_next_token", "ops"]
 
 
 def __getattr__(name):

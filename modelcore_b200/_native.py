@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "mcb_gated_silu",
     "mcb_embed_rms_norm",
     "mcb_prefill_attn",
+    "mcb_sample",
     "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
@@ -143,6 +144,15 @@ class SoftcapArgs(ctypes.Structure):
     ]
 
 
+class SampleArgs(ctypes.Structure):
+    _fields_ = [
+        ("logits", ctypes.c_void_p), ("uniforms", ctypes.c_void_p), ("out", ctypes.c_void_p),
+        ("logits_stride", ctypes.c_int64), ("out_stride", ctypes.c_int64),
+        ("rows", ctypes.c_int32), ("V", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("temperature", ctypes.c_float),
+    ]
+
+
 class McbError(RuntimeError):
     """A C-ABI call returned a non-zero mcb_status."""
 
@@ -179,6 +189,8 @@ def _declare(lib):
     lib.mcb_add_rms_norm.argtypes = [P(AddNormArgs), ctypes.c_void_p]
     lib.mcb_gated_silu.restype = ctypes.c_int
     lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
+    lib.mcb_sample.restype = ctypes.c_int
+    lib.mcb_sample.argtypes = [P(SampleArgs), ctypes.c_void_p]
     lib.mcb_prefill_attn.restype = ctypes.c_int
     lib.mcb_prefill_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]
     lib.mcb_embed_rms_norm.restype = ctypes.c_int

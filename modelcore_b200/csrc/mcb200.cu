@@ -17,6 +17,7 @@
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
 #include "prefill_attn.cuh"
+#include "sample.cuh"
 #include "step_fused.cuh"
 
 namespace {
@@ -438,12 +439,15 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
 
 }  // namespace
 
-// One warp per row, 4 rows per 128-thread block; CPL = 16-byte chunks per lane, the smallest of
-// 1, 2, 4, 8, 16 that covers C.
+// One warp per row; CPL = 16-byte chunks per lane, the smallest of 1, 2, 4, 8, 16 that covers C.
+// A decode step has few rows (one per sequence): one row per 32-thread block spreads them over
+// as many SMs as possible (these launches are latency-bound); prefill-sized row counts use
+// 4 rows per block.
 template <class F>
 static void launch_row_norm(int C, int rows, cudaStream_t st, F&& launch) {
   const int chunks = C / 8;
-  const dim3 grid((rows + 3) / 4), block(128);
+  const int per_block = rows <= 1024 ? 1 : 4;
+  const dim3 grid((rows + per_block - 1) / per_block), block(32 * per_block);
   if (chunks <= 32) launch(std::integral_constant<int, 1>{}, grid, block, st);
   else if (chunks <= 64) launch(std::integral_constant<int, 2>{}, grid, block, st);
   else if (chunks <= 128) launch(std::integral_constant<int, 4>{}, grid, block, st);
@@ -706,6 +710,35 @@ int mcb_softcap_argmax(const mcb_softcap_args* a, void* stream) {
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "softcap_argmax launch");
+  return MCB_OK;
+}
+
+int mcb_sample(const mcb_sample_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_sample: args is NULL");
+  if (a->rows < 0 || a->V <= 0 || a->logits_stride < a->V)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_sample: rows=%d V=%d logits_stride=%lld", a->rows, a->V,
+                (long long)a->logits_stride);
+  if (!(a->temperature > 0.f))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_sample: temperature must be > 0 (greedy: top_k = 1)");
+  if (a->top_k > mcb::kSampleMaxK && a->top_k < a->V)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_sample: top_k %d above %d", a->top_k, mcb::kSampleMaxK);
+  if (a->logits == nullptr || a->uniforms == nullptr || a->out == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_sample: NULL pointer argument");
+  if (a->rows == 0) return MCB_OK;
+  mcb::SampleParams p;
+  p.logits = a->logits;
+  p.uniforms = a->uniforms;
+  p.out = a->out;
+  p.ls = a->logits_stride;
+  p.os = a->out_stride;
+  p.rows = a->rows;
+  p.V = a->V;
+  p.top_k = a->top_k;
+  p.inv_temperature = 1.0f / a->temperature;
+  mcb::sample_kernel<<<a->rows, mcb::kSampleThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  g_launches++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sample launch");
   return MCB_OK;
 }
 

@@ -98,11 +98,12 @@ __device__ __forceinline__ void scale_round(float (&v)[CPL][8], float r) {
     for (int i = 0; i < 8; ++i) v[u][i] = round_bf16(__fmul_rn(v[u][i], r));
 }
 
-// One warp per row; C a multiple of 8 with C <= 256 * CPL; rows 16-byte aligned.
+// One warp per row (any number of warps per block); C a multiple of 8 with C <= 256 * CPL; rows
+// 16-byte aligned.
 template <int CPL>
 __global__ void __launch_bounds__(128) add_rms_norm_kernel(const AddNormParams p) {
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   const int nchunk = p.C / 8;
   float v[CPL][8];
@@ -146,7 +147,7 @@ struct EmbedNormParams {
 template <int CPL>
 __global__ void __launch_bounds__(128) embed_rms_norm_kernel(const EmbedNormParams p) {
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   const int nchunk = p.C / 8;
   const long long id = p.ids[row];

@@ -243,6 +243,62 @@ class GraphDecoder:
         cache.state.update(state_snap)
         return g, logits, nxt
 
+    def _capture_sampling(self, temperature, top_k, generator):
+        cache = self.kv_cache
+        snap = cache.host_state()
+        state_snap = dict(cache.state)
+        g = torch.cuda.CUDAGraph()
+        if generator is not None:
+            g.register_generator_state(generator)
+        B = cache.batch_size
+        with torch.inference_mode():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=side):
+                if step.decode_installed(self.model) and step._model_call_ok(self.model, self._ids, cache):
+                    logits = step.decode_forward(self.model, self._ids, cache)[:, -1, :]
+                else:
+                    logits = self.model.forward(self._ids, kv_cache=cache)[:, -1, :].float()
+                u = torch.rand(B, generator=generator, dtype=torch.float32, device=self._ids.device)
+                ops.sample(logits, u, temperature=temperature, top_k=top_k, out=self._ids)
+            torch.cuda.current_stream().wait_stream(side)
+        cache.restore_host_state(snap)
+        cache.state.update(state_snap)
+        return g, logits
+
+    @torch.inference_mode()
+    def sample_steps(self, n, *, temperature=1.0, top_k=None, generator=None, first_tokens=None,
+                     out=None):
+        """n device-resident sampled steps: step i feeds token t_i and draws t_{i+1} from its
+        logits with sample_next_token's distribution (modelcore/generate.py:19-34: top_k,
+        temperature; one mcb_sample launch on uniforms from `generator`, a CUDA torch.Generator or
+        the default one); t_0 = first_tokens (default: drawn from the current logits).  Returns
+        out (B, n) int64 holding t_0 .. t_{n-1}; .logits afterwards are those of the last step."""
+        from .sampling import sample_next_token
+        B = self.kv_cache.batch_size
+        if first_tokens is None:
+            first_tokens = sample_next_token(self._logits, generator, temperature, top_k)
+        self._ids.copy_(first_tokens.view(-1, 1))
+        if out is None:
+            out = torch.empty((B, n), dtype=torch.long, device=self._ids.device)
+        key = (float(temperature), top_k, id(generator))
+        graphs = self.__dict__.setdefault("_sample_graphs", {})
+        for i in range(n):
+            out[:, i] = self._ids[:, 0]
+            self._room(1)
+            if key not in graphs and self._eager_steps == 0:
+                logits = self._eager(self._ids.clone())
+                self._ids.copy_(sample_next_token(logits, generator, temperature, top_k))
+                self._logits = logits
+                continue
+            if key not in graphs:
+                graphs[key] = self._capture_sampling(temperature, top_k, generator)
+            graph, logits = graphs[key]
+            graph.replay()
+            self._replayed()
+            self._logits = logits
+        return out
+
     def _eager(self, ids):
         logits = self.model.forward(ids, kv_cache=self.kv_cache)[:, -1, :]
         self._eager_steps += 1

@@ -13,7 +13,7 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      SoftcapArgs, check)
+                      SampleArgs, SoftcapArgs, check)
 
 
 def _stream(t):
@@ -408,6 +408,38 @@ def softcap_argmax(logits, vocab_size, softcap, *, out=None, want_logits=True, a
     args.softcap = float(softcap) if softcap is not None else 0.0
     check(_native.load().mcb_softcap_argmax(ctypes.byref(args), _stream(logits)))
     return out if want_logits else None
+
+
+def sample(logits, uniforms, *, temperature=1.0, top_k=None, out=None):
+    """One token per row of fp32 logits (B, V): sample_next_token (modelcore/generate.py:19-34)
+    for temperature > 0 with the draw at the given uniforms (B,) in [0, 1) -- the inverse CDF over
+    the top_k candidates in descending-logit order (ties by index), or over the whole row in index
+    order.  temperature == 0 is the greedy pick (top_k = 1).  Returns out (B, 1) int64."""
+    _need("logits", logits, 2, dtype=torch.float32)
+    rows, V = logits.shape
+    if logits.stride(1) != 1:
+        raise RuntimeError("logits must have unit stride on the vocab dim")
+    if uniforms.dtype != torch.float32 or uniforms.numel() != rows or not uniforms.is_cuda:
+        raise RuntimeError(f"uniforms must be {rows} float32 values on the GPU")
+    if out is None:
+        out = torch.empty((rows, 1), dtype=torch.int64, device=logits.device)
+    args = SampleArgs()
+    args.logits, args.logits_stride = logits.data_ptr(), logits.stride(0)
+    u = uniforms.reshape(-1)
+    if not u.is_contiguous():
+        u = u.contiguous()
+    args.uniforms = u.data_ptr()
+    args.out, args.out_stride = out.data_ptr(), out.reshape(-1).stride(0)
+    args.rows, args.V = rows, V
+    if temperature == 0:
+        args.top_k, args.temperature = 1, 1.0
+    else:
+        if temperature < 0:
+            raise RuntimeError("temperature must be non-negative")
+        args.top_k = int(top_k) if top_k is not None and top_k > 0 else 0
+        args.temperature = float(temperature)
+    check(_native.load().mcb_sample(ctypes.byref(args), _stream(logits)))
+    return out
 
 
 def gated_silu(gate, up, out=None):

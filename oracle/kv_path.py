@@ -294,3 +294,34 @@ def kv_read_bytes(cache_seqlens, T, Hkv, D, window, itemsize=2):
         hi = L + T - 1
         total += (hi - lo + 1)
     return total * 2 * Hkv * D * itemsize
+
+
+# ---------------------------------------------------------------------------------------------
+# Sampling: sample_next_token, modelcore/generate.py:19-34
+def sample_candidates(logits, temperature, top_k):
+    """The reference's candidates and their probabilities for one row of fp32 logits: with
+    1 <= top_k < V the top_k largest (torch.topk, generate.py:26-27; ties here by ascending
+    index) in descending order, else the whole row in index order; probabilities
+    softmax(x / T) (generate.py:28-29, 32-33) with x / T as x * fp32(1 / T), in float64."""
+    x = np.asarray(logits, dtype=np.float32)
+    V = x.shape[-1]
+    if top_k is not None and 1 <= top_k < V:
+        order = np.lexsort((np.arange(V), -x.astype(np.float64)))[:top_k]
+    else:
+        order = np.arange(V)
+    inv = (F32(1.0) / F32(temperature)).astype(np.float32)
+    xs = (x[order] * inv).astype(np.float32).astype(np.float64)
+    w = np.exp(xs - xs.max())
+    return order, w / w.sum()
+
+
+def sample_token(logits, u, temperature, top_k):
+    """The draw at uniform u: the first candidate whose inclusive cumulative probability exceeds
+    u (the inverse CDF; torch.multinomial, generate.py:30 and :34, draws from the same
+    distribution with its own generator).  Returns (index, distance of u to the nearest CDF
+    boundary) -- the second lets tests skip draws that fp32 rounding can move."""
+    order, p = sample_candidates(logits, temperature, top_k)
+    c = np.cumsum(p)
+    i = int(np.searchsorted(c, u, side="right"))
+    i = min(i, len(order) - 1)
+    return int(order[i]), float(np.min(np.abs(c - u)))

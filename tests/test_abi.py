@@ -11,7 +11,7 @@ import pytest
 from conftest import REPO
 from modelcore_b200 import _native
 from modelcore_b200._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs,
-                                    GatedSiluArgs, SoftcapArgs)
+                                    GatedSiluArgs, SampleArgs, SoftcapArgs)
 
 HEADER = os.path.join(REPO, "include", "mcb200.h")
 
@@ -53,7 +53,7 @@ def _c_layout(struct, fields):
 @pytest.mark.parametrize("cls,cname", [(AppendArgs, "mcb_append_args"), (CopyArgs, "mcb_copy_args"),
                                        (AttnArgs, "mcb_attn_args"), (AddNormArgs, "mcb_add_norm_args"),
                                        (GatedSiluArgs, "mcb_gated_silu_args"), (EmbedArgs, "mcb_embed_args"),
-                                       (SoftcapArgs, "mcb_softcap_args")])
+                                       (SoftcapArgs, "mcb_softcap_args"), (SampleArgs, "mcb_sample_args")])
 def test_ctypes_structures_match_the_c_layout(cls, cname):
     fields = [f for f, _ in cls._fields_]
     c = _c_layout(cname, fields)
@@ -202,3 +202,16 @@ def test_embedding_and_lm_head_epilogue_validate_on_the_host():
     assert lib.mcb_softcap_argmax(ctypes.byref(s), None) == _native.MCB_ERR_INVALID_ARG
     s.logits_stride, s.argmax = 1024, None
     assert lib.mcb_softcap_argmax(ctypes.byref(s), None) == _native.MCB_ERR_INVALID_ARG
+
+
+def test_sampler_validates_on_the_host():
+    lib = _native.load()
+    a = SampleArgs()
+    a.logits, a.uniforms, a.out, a.rows, a.V, a.logits_stride = 16, 32, 48, 2, 1000, 1000
+    a.temperature = 0.0
+    assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_INVALID_ARG
+    a.temperature = 1.0
+    a.V, a.logits_stride, a.top_k = 5000, 5000, 2000
+    assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_UNSUPPORTED
+    a.top_k, a.rows = 50, 0
+    assert lib.mcb_sample(ctypes.byref(a), None) == 0

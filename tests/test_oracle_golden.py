@@ -148,3 +148,27 @@ def test_softcap_and_greedy_pick_match_the_reference_lm_head():
     assert y.shape == z["head_out"].shape
     assert _f32_ulps(y, z["head_out"]).max() <= 4
     assert np.array_equal(O.greedy_pick(y), np.argmax(z["head_out"], axis=-1))
+
+
+@pytest.mark.parametrize("top_k,T", [(50, 1.0), (7, 0.6), (None, 1.3)])
+def test_sampling_candidates_match_the_reference_topk_softmax(top_k, T):
+    """The oracle's candidates and probabilities against the reference's own torch ops
+    (sample_next_token, modelcore/generate.py:25-33: topk, / temperature, softmax) on the CPU."""
+    import torch
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(3)
+    logits = torch.randn(4, 3000, generator=g) * 4
+    for r in range(4):
+        order, p = O.sample_candidates(logits[r].numpy(), T, top_k)
+        if top_k:
+            vals, idx = torch.topk(logits[r], top_k)
+            probs = F.softmax(vals / T, dim=-1)
+            assert np.array_equal(order, idx.numpy())
+        else:
+            probs = F.softmax(logits[r] / T, dim=-1)
+        assert np.allclose(p, probs.double().numpy(), rtol=1e-5, atol=1e-9)
+    # ties at the cut keep the smallest indices
+    x = np.zeros(100, dtype=np.float32)
+    x[[3, 50, 77]] = 1.0
+    order, _ = O.sample_candidates(x, 1.0, 5)
+    assert order.tolist() == [3, 50, 77, 0, 1]

@@ -288,6 +288,26 @@ typedef struct {
 
 int mcb_sample(const mcb_sample_args* args, void* stream);
 
+/* mcb_linear: Y = X W^T (F.linear without bias, modelcore/components/linear.py:14) for the decode
+ * step's few rows: X (R, K), W (N, K) as nn.Linear stores it, Y (R, N), bf16, fp32 accumulation,
+ * one rounding.  R <= 256, K a multiple of 64, x and w rows 16-byte aligned.  The weight tiles stream by
+ * TMA into tcgen05 MMAs (128 output features per CTA, fp32 accumulators in TMEM); split > 1 cuts
+ * K across a cluster of that many CTAs whose partial tiles are summed through distributed shared
+ * memory (0: chosen from N and K).  With pdl != 0 the kernel is launched with programmatic
+ * stream serialization: its weight loads start while the previous kernel in the stream finishes,
+ * and it reads X only after that kernel completed (griddepcontrol.wait). */
+typedef struct {
+  const void* x;              /* (R, K) bf16                                                */
+  const void* w;              /* (N, K) bf16                                                */
+  void* y;                    /* (R, N) bf16                                                */
+  int64_t x_stride, w_stride, y_stride;  /* row strides, elements                           */
+  int32_t R, N, K;
+  int32_t split;
+  int32_t pdl;
+} mcb_linear_args;
+
+int mcb_linear(const mcb_linear_args* args, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table
  * overflow) or a timed-out pipeline wait sets a device error word and skips the access.

@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "mcb_embed_rms_norm",
     "mcb_prefill_attn",
     "mcb_sample",
+    "mcb_linear",
     "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
@@ -153,6 +154,15 @@ class SampleArgs(ctypes.Structure):
     ]
 
 
+class LinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64), ("w_stride", ctypes.c_int64), ("y_stride", ctypes.c_int64),
+        ("R", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32),
+        ("split", ctypes.c_int32), ("pdl", ctypes.c_int32),
+    ]
+
+
 class McbError(RuntimeError):
     """A C-ABI call returned a non-zero mcb_status."""
 
@@ -189,6 +199,8 @@ def _declare(lib):
     lib.mcb_add_rms_norm.argtypes = [P(AddNormArgs), ctypes.c_void_p]
     lib.mcb_gated_silu.restype = ctypes.c_int
     lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
+    lib.mcb_linear.restype = ctypes.c_int
+    lib.mcb_linear.argtypes = [P(LinearArgs), ctypes.c_void_p]
     lib.mcb_sample.restype = ctypes.c_int
     lib.mcb_sample.argtypes = [P(SampleArgs), ctypes.c_void_p]
     lib.mcb_prefill_attn.restype = ctypes.c_int

@@ -17,6 +17,7 @@
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
 #include "prefill_attn.cuh"
+#include "decode_gemm.cuh"
 #include "sample.cuh"
 #include "step_fused.cuh"
 
@@ -456,6 +457,61 @@ static void launch_row_norm(int C, int rows, cudaStream_t st, F&& launch) {
   g_launches++;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode projections (decode_gemm.cuh)
+int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long long cols,
+                    long long stride, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), 1, 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride) * 2, static_cast<cuuint64_t>(stride) * 2 * rows,
+                           static_cast<cuuint64_t>(stride) * 2 * rows};
+  cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(box_rows), 1u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled(rows) failed (CUresult %d)", (int)r);
+  return MCB_OK;
+}
+
+template <int RN, int STAGES>
+int launch_linear(const CUtensorMap& wm, const CUtensorMap& xm, const mcb::LinearParams& prm,
+                  int tiles, bool pdl, cudaStream_t st) {
+  using Cfg = mcb::LinearConfig<RN, STAGES>;
+  static std::atomic<uint64_t> done{0};
+  auto kernel = mcb::linear_kernel<RN, STAGES>;
+  cudaError_t e = ensure_smem(kernel, Cfg::kSmem, done);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * prm.split));
+  cfg.blockDim = dim3(mcb::kLinThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (prm.split > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = static_cast<unsigned>(prm.split);
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, kernel, wm, xm, prm);
+  g_launches++;
+  if (e != cudaSuccess) return cuda_fail(e, "linear launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "linear launch");
+  return MCB_OK;
+}
+
 extern "C" {
 
 int mcb_abi_version(void) { return MCB_ABI_VERSION; }
@@ -740,6 +796,57 @@ int mcb_sample(const mcb_sample_args* a, void* stream) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sample launch");
   return MCB_OK;
+}
+
+int mcb_linear(const mcb_linear_args* a, void* stream) {
+  if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: args is NULL");
+  if (a->R < 0 || a->N <= 0 || a->K <= 0)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: R=%d N=%d K=%d", a->R, a->N, a->K);
+  if (a->R > 256 || a->K % 64 != 0)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most 256), K=%d (a multiple of 64)", a->R,
+                a->K);
+  if (a->x == nullptr || a->w == nullptr || a->y == nullptr)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: NULL pointer argument");
+  if (a->x_stride < a->K || a->w_stride < a->K || a->y_stride < a->N)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: row strides shorter than the rows");
+  if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->y, 2) || a->x_stride % 8 ||
+      a->w_stride % 8)
+    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x and w rows must start on 16-byte boundaries");
+  if (a->split < 0 || a->split > 8)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d (0..8)", a->split);
+  if (a->R == 0) return MCB_OK;
+  const int tiles = (a->N + mcb::kLinTile - 1) / mcb::kLinTile;
+  const int steps = a->K / 64;
+  int split = a->split;
+  if (split == 0) {
+    split = 1;
+    for (int s = 8; s >= 2; --s)
+      if (steps % s == 0 && tiles * s <= device_sm_count()) { split = s; break; }
+  } else if (steps % split != 0) {
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d does not divide %d K panels", split, steps);
+  }
+  CUtensorMap wm, xm;
+  const int RN = a->R <= 32 ? 32 : (a->R <= 64 ? 64 : (a->R <= 128 ? 128 : 256));
+  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, mcb::kLinTile);
+  if (rc != MCB_OK) return rc;
+  rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, RN);
+  if (rc != MCB_OK) return rc;
+  mcb::LinearParams p;
+  p.y = static_cast<uint16_t*>(a->y);
+  p.ys = a->y_stride;
+  p.R = a->R;
+  p.N = a->N;
+  p.K = a->K;
+  p.split = split;
+  p.steps_per_cta = steps / split;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool pdl = a->pdl != 0;
+  switch (RN) {
+    case 32: return launch_linear<32, 8>(wm, xm, p, tiles, pdl, st);
+    case 64: return launch_linear<64, 8>(wm, xm, p, tiles, pdl, st);
+    case 128: return launch_linear<128, 6>(wm, xm, p, tiles, pdl, st);
+    default: return launch_linear<256, 4>(wm, xm, p, tiles, pdl, st);
+  }
 }
 
 int mcb_gated_silu(const mcb_gated_silu_args* a, void* stream) {

@@ -403,9 +403,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp >= 2) {
     // ---------------- softmax: warps 2-5 query tile 0, warps 6-9 query tile 1 ----------------
     const int t = (warp - 2) >> 2;
+    // scalars, not rng[t]: a runtime index would put the array in local memory
+    const int qbase = t ? rng[1].qbase : rng[0].qbase;
+    const int j_begin = t ? rng[1].j_begin : rng[0].j_begin;
+    const int j_end = t ? rng[1].j_end : rng[0].j_end;
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;          // query row within the tile
-    const int qbase = rng[t].qbase;
     const int q = qbase + row;
     const bool valid = q < p.T;
     const int pos = L + q;
@@ -415,7 +418,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     int cnt = 0;
-    for (int j = rng[t].j_begin; j < rng[t].j_end; ++j, ++cnt) {
+    for (int j = j_begin; j < j_end; ++j, ++cnt) {
       // waits are made warp-uniform: the tcgen05.ld/st below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[t], cnt & 1, abort_flag))) {
         ok = false;

@@ -13,7 +13,7 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      SampleArgs, SoftcapArgs, check)
+                      LinearArgs, SampleArgs, SoftcapArgs, check)
 
 
 def _stream(t):
@@ -439,6 +439,30 @@ def sample(logits, uniforms, *, temperature=1.0, top_k=None, out=None):
         args.top_k = int(top_k) if top_k is not None and top_k > 0 else 0
         args.temperature = float(temperature)
     check(_native.load().mcb_sample(ctypes.byref(args), _stream(logits)))
+    return out
+
+
+LINEAR_MAX_ROWS = 256
+
+
+def linear(x, weight, *, out=None, split=0, pdl=False):
+    """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
+    rows: x (R, K) with R <= 256, weight (N, K), bf16, fp32 accumulation on tcgen05.  split: K cut
+    across a cluster of that many CTAs (0: chosen).  pdl: launch with programmatic stream
+    serialization (the weight stream overlaps the previous kernel).  Returns out (R, N)."""
+    R, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise RuntimeError(f"weight must be (N, {K}), got {tuple(weight.shape)}")
+    if out is None:
+        out = torch.empty((R, N), dtype=torch.bfloat16, device=x.device)
+    args = LinearArgs()
+    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
+    args.w, args.w_stride = weight.data_ptr(), _rows2d("weight", weight)
+    args.y, args.y_stride = out.data_ptr(), _rows2d("out", out)
+    args.R, args.N, args.K = R, N, K
+    args.split, args.pdl = split, int(bool(pdl))
+    check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))
     return out
 
 

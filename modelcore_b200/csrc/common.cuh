@@ -134,6 +134,17 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization may
+// start before the kernel ahead of it in the stream has finished; pdl_wait() returns once that
+// kernel has completed and its memory is visible, and must precede every read of its outputs.
+// pdl_launch_dependents() lets the next kernel (if launched that way) start early.  Both are
+// no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
 // TMA: 4-D tiled bulk tensor load global -> shared, completion signalled on an mbarrier as a
 // transaction count.  No multicast: every CTA fetches its own tiles.  `policy` is an L2 cache
 // policy from createpolicy.

@@ -127,11 +127,18 @@ __global__ void __launch_bounds__(kAttnThreads)
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       const uint64_t policy = l2_policy_evict_first();
+      bool waited = false;
       for (int i = 0; i < my_tiles; ++i) {
         const int s = i % STAGES;
         if (i >= STAGES && !mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
         const int key0 = kb + (tile0 + i) * C::TK;
+        // keys below L are from earlier steps; a tile reaching L holds this step's new keys,
+        // written by the append kernel this launch may have overlapped (PDL)
+        if (!waited && key0 + C::TK > L) {
+          pdl_wait();
+          waited = true;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
         uint8_t* kdst = smem + s * C::STAGE_BYTES;
         uint8_t* vdst = kdst + C::TILE_BYTES;
 #pragma unroll
@@ -152,6 +159,7 @@ __global__ void __launch_bounds__(kAttnThreads)
 
   if (warp < kAttnConsumerWarps) {
     // ---------------- consumer warps ----------------
+    pdl_wait();  // q comes from the append kernel ahead of this one
     // Q^T fragments (B operand): row n = j*8 + lane/4, columns d = kk*16 + 2*(lane%4) + {0,1}, +8.
     uint32_t qf[NQT][D / 16][2];
 #pragma unroll

@@ -13,9 +13,10 @@
 //     overlaps the tail of the kernel before; every CTA calls griddepcontrol.launch_dependents at
 //     once so the kernel after can do the same;
 //   * split-K across a thread-block cluster of `split` CTAs (N = 768 projections have only six
-//     128-feature tiles): each CTA reduces its K range into TMEM, the partial tiles are summed by
-//     the cluster's rank 0 through distributed shared memory (fixed order rank 0, 1, ..), which
-//     writes Y -- no workspace, no atomics;
+//     128-feature tiles): each CTA reduces its K range into TMEM and parks the partial tile in its
+//     shared memory; rank q then sums its share of the tile's columns over every rank through
+//     distributed shared memory (fixed order rank 0, 1, ..) and writes those rows of Y -- no
+//     workspace, no atomics;
 //   * epilogue: 4 warps, thread = output feature (TMEM lane), bf16 rounding once.
 //
 // Every mbarrier wait is bounded; a timeout raises the CTA's abort flag, the MMA issuer waits
@@ -31,10 +32,6 @@ namespace mcb {
 constexpr int kLinTile = 128;    // output features per CTA (MMA M)
 constexpr int kLinThreads = 192;
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -54,8 +51,7 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+               : "r"(addr));
   return v;
 }
 
@@ -65,6 +61,7 @@ struct LinearParams {
   int R, N, K;
   int steps_per_cta;   // 64-column K panels per CTA (K / 64 / split)
   int split;           // CTAs of a cluster sharing one output tile
+  int vec_out;         // y 16-byte aligned, ys and N multiples of 8: 16-byte stores
 };
 
 template <int RN, int STAGES>
@@ -75,7 +72,8 @@ struct LinearConfig {
   static constexpr int kBarOff = STAGES * kStageBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static constexpr uint32_t kTmemCols = RN <= 32 ? 32 : (RN <= 64 ? 64 : (RN <= 128 ? 128 : 256));
-  static_assert(kLinTile * RN * 4 <= kBarOff, "split-K partial tile must fit in the ring");
+  // split-K partials (padded rows) plus the staged bf16 rows of one rank (at most RN / 2 rows)
+  static_assert(kLinTile * (RN + 4) * 4 + (RN / 2) * kLinTile * 2 <= kBarOff, "epilogue must fit in the ring");
 };
 
 template <int RN, int STAGES>
@@ -173,8 +171,14 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
   bool have = false;
   if (epi) have = __all_sync(0xffffffffu, mbar_wait_or_abort(acc_full, 0, abort_flag));
-  // the ring is free once the accumulator is complete: partial tiles go there, [feat][RN] fp32
+  // The ring is free once the accumulator is complete.  Split-K partial tiles go there as
+  // [feature][row] fp32 with a padded row (RN + 4 floats: conflict-free float4 access by
+  // consecutive features); the bf16 output rows a CTA writes are staged as [row][128 features]
+  // and copied out 16 bytes a thread.
+  constexpr int PSTR = RN + 4;
   float* part = reinterpret_cast<float*>(smem);
+  uint16_t* staged;
+  int r0 = 0, r1 = RN;
   if (split > 1) {
     if (epi && have) {
       tc_fence_after();
@@ -184,41 +188,75 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         tmem_ld32(tmem + lane_off + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(part + feat * RN + c * 32 + i) =
+          *reinterpret_cast<float4*>(part + feat * PSTR + c * 32 + i) =
               make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
                           __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
       }
     }
     cluster_sync();  // every partial tile written and visible to the cluster
-    if (rank == 0 && epi && have) {
-      const int n = n0 + feat;
-#pragma unroll 1
-      for (int c = 0; c < RN; c += 4) {
-        float4 a = *reinterpret_cast<const float4*>(part + feat * RN + c);
-        for (int r = 1; r < split; ++r) {
-          const float4 b = ld_dsmem_f4(map_to_rank(part + feat * RN + c, r));
-          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-        }
-        const float vals[4] = {a.x, a.y, a.z, a.w};
+    // rank q sums rows [q * per, (q + 1) * per) of the tile over all ranks, in rank order, 8 rows
+    // at a time with every rank's loads in flight together
+    const int per = ((RN + split - 1) / split + 7) & ~7;
+    r0 = static_cast<int>(rank) * per;
+    r1 = r0 + per < RN ? r0 + per : RN;
+    staged = reinterpret_cast<uint16_t*>(smem + kLinTile * PSTR * 4);
+    if (epi) {
+      for (int c = r0; c < r1; c += 8) {
+        float4 v[8][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (c + i < p.R && n < p.N)
-            p.y[static_cast<long long>(c + i) * p.ys + n] = float_to_bf16_bits(vals[i]);
+        for (int q = 0; q < 8; ++q) {
+          if (q < split) {
+            const uint32_t a = map_to_rank(part + feat * PSTR + c, static_cast<uint32_t>(q));
+            v[q][0] = ld_dsmem_f4(a);
+            v[q][1] = ld_dsmem_f4(a + 16);
+          }
+        }
+        float acc[8] = {v[0][0].x, v[0][0].y, v[0][0].z, v[0][0].w,
+                        v[0][1].x, v[0][1].y, v[0][1].z, v[0][1].w};
+#pragma unroll
+        for (int q = 1; q < 8; ++q) {
+          if (q < split) {
+            acc[0] += v[q][0].x; acc[1] += v[q][0].y; acc[2] += v[q][0].z; acc[3] += v[q][0].w;
+            acc[4] += v[q][1].x; acc[5] += v[q][1].y; acc[6] += v[q][1].z; acc[7] += v[q][1].w;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (c + i < r1) staged[(c + i - r0) * kLinTile + feat] = float_to_bf16_bits(acc[i]);
       }
     }
-    cluster_sync();  // rank 0 has read every partial before any CTA of the cluster exits
-  } else if (epi && have) {
-    tc_fence_after();
-    const int n = n0 + feat;
+    cluster_sync();  // every rank has read the partials it needs before any CTA exits
+  } else {
+    staged = reinterpret_cast<uint16_t*>(smem);
+    if (epi && have) {
+      tc_fence_after();
 #pragma unroll
-    for (int c = 0; c < RN / 32; ++c) {
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_off + c * 32, v);
-      if (n < p.N) {
+      for (int c = 0; c < RN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + c * 32, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < p.R)
-            p.y[static_cast<long long>(c * 32 + i) * p.ys + n] = float_to_bf16_bits(__uint_as_float(v[i]));
+        for (int i = 0; i < 32; ++i) staged[(c * 32 + i) * kLinTile + feat] = float_to_bf16_bits(__uint_as_float(v[i]));
+      }
+    }
+  }
+  if (epi) {
+    named_barrier(1, 128);  // the staged rows are complete
+    const int rows = (r1 < p.R ? r1 : p.R) - r0;
+    if (have && rows > 0) {
+      const int t = threadIdx.x - 64;
+      if (p.vec_out) {  // 16 bytes = 8 features a thread, a row of 128 features is 16 chunks
+        for (int idx = t; idx < rows * 16; idx += 128) {
+          const int r = idx >> 4, ch = idx & 15;
+          const int n = n0 + ch * 8;
+          if (n < p.N)
+            *reinterpret_cast<uint4*>(p.y + static_cast<long long>(r0 + r) * p.ys + n) =
+                *reinterpret_cast<const uint4*>(staged + r * kLinTile + ch * 8);
+        }
+      } else {
+        for (int idx = t; idx < rows * kLinTile; idx += 128) {
+          const int r = idx >> 7, f = idx & 127;
+          if (n0 + f < p.N) p.y[static_cast<long long>(r0 + r) * p.ys + n0 + f] = staged[r * kLinTile + f];
+        }
       }
     }
   }

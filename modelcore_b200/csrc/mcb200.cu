@@ -173,8 +173,21 @@ struct AttnVariant {
     static std::atomic<uint64_t> done{0};
     cudaError_t e = ensure_smem(split_kernel, SplitCfg::SMEM_BYTES, done);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn_split)");
-    split_kernel<<<static_cast<unsigned>(grid), mcb::kAttnThreads, SplitCfg::SMEM_BYTES, st>>>(km, vm, prm);
+    // programmatic stream serialization: the K/V tiles of earlier steps stream in while the
+    // append kernel ahead finishes (the kernel waits for it before q and the new keys)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(mcb::kAttnThreads);
+    cfg.dynamicSmemBytes = SplitCfg::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, split_kernel, km, vm, prm);
     g_launches++;
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     if (prm.nsplit > 1) {
@@ -839,6 +852,7 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   p.K = a->K;
   p.split = split;
   p.steps_per_cta = steps / split;
+  p.vec_out = aligned(a->y, 16) && a->y_stride % 8 == 0 && a->N % 8 == 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
   switch (RN) {

@@ -50,7 +50,8 @@ constexpr int kAppendWarpsPerBlock = 4;
 
 __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
     kv_append_rope_kernel(const AppendParams p) {
-  pdl_launch_dependents();  // the attention after it waits for completion before reading
+  pdl_launch_dependents();  // the kernel after it waits for completion before reading
+  pdl_wait();               // q, k, v come from the projection ahead
   const int lane = threadIdx.x & 31;
   const long long w = static_cast<long long>(blockIdx.x) * kAppendWarpsPerBlock + (threadIdx.x >> 5);
   if (w >= p.total_vectors) return;
@@ -163,7 +164,8 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
 template <int D>
 __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
     kv_append_rope_vec_kernel(const AppendParams p) {
-  pdl_launch_dependents();  // the attention after it waits for completion before reading
+  pdl_launch_dependents();  // the kernel after it waits for completion before reading
+  pdl_wait();               // q, k, v come from the projection ahead
   constexpr int L = D / 16;        // lanes per vector
   constexpr int VPW = 32 / L;      // vectors per warp
   constexpr int HALF = D / 2;

@@ -86,6 +86,25 @@ cudaError_t ensure_smem(K kernel, int bytes, std::atomic<uint64_t>& done) {
   return e;
 }
 
+// Launches `kernel` with programmatic stream serialization: it may start while the kernel ahead
+// in the stream finishes (every kernel of this library calls pdl_wait() before reading anything
+// another kernel wrote).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ------------------------------------------------------------------------------------------
 // Decode attention planning.  Two kernels share the semantics: the persistent one
 // (decode_attn.cuh: a balanced partition of every row's key tiles over a resident grid) and the
@@ -610,23 +629,25 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
     const long long blocks = (warps + mcb::kAppendWarpsPerBlock - 1) / mcb::kAppendWarpsPerBlock;
     if (blocks > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: grid too large");
     const dim3 grid(static_cast<unsigned>(blocks)), block(mcb::kAppendWarpsPerBlock * 32);
+    cudaError_t e;
     switch (a->D) {
-      case 16: mcb::kv_append_rope_vec_kernel<16><<<grid, block, 0, st>>>(p); break;
-      case 32: mcb::kv_append_rope_vec_kernel<32><<<grid, block, 0, st>>>(p); break;
-      case 64: mcb::kv_append_rope_vec_kernel<64><<<grid, block, 0, st>>>(p); break;
-      case 128: mcb::kv_append_rope_vec_kernel<128><<<grid, block, 0, st>>>(p); break;
-      default: mcb::kv_append_rope_vec_kernel<256><<<grid, block, 0, st>>>(p); break;
+      case 16: e = launch_pdl(mcb::kv_append_rope_vec_kernel<16>, grid, block, 0, st, p); break;
+      case 32: e = launch_pdl(mcb::kv_append_rope_vec_kernel<32>, grid, block, 0, st, p); break;
+      case 64: e = launch_pdl(mcb::kv_append_rope_vec_kernel<64>, grid, block, 0, st, p); break;
+      case 128: e = launch_pdl(mcb::kv_append_rope_vec_kernel<128>, grid, block, 0, st, p); break;
+      default: e = launch_pdl(mcb::kv_append_rope_vec_kernel<256>, grid, block, 0, st, p); break;
     }
     g_launches++;
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "kv_append_rope launch");
     return MCB_OK;
   }
   const long long blocks = (p.total_vectors + mcb::kAppendWarpsPerBlock - 1) / mcb::kAppendWarpsPerBlock;
   if (blocks > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: grid too large");
-  mcb::kv_append_rope_kernel<<<static_cast<unsigned>(blocks), mcb::kAppendWarpsPerBlock * 32, 0, st>>>(p);
+  cudaError_t e = launch_pdl(mcb::kv_append_rope_kernel, dim3(static_cast<unsigned>(blocks)),
+                             dim3(mcb::kAppendWarpsPerBlock * 32), 0, st, p);
   g_launches++;
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kv_append_rope launch");
   return MCB_OK;
 }
@@ -713,7 +734,7 @@ int mcb_add_rms_norm(const mcb_add_norm_args* a, void* stream) {
   p.eps = a->eps;
   launch_row_norm(a->C, a->rows, static_cast<cudaStream_t>(stream), [&](auto cpl, dim3 g, dim3 b,
                                                                         cudaStream_t st) {
-    mcb::add_rms_norm_kernel<decltype(cpl)::value><<<g, b, 0, st>>>(p);
+    launch_pdl(mcb::add_rms_norm_kernel<decltype(cpl)::value>, g, b, 0, st, p);
   });
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "add_rms_norm launch");
@@ -746,7 +767,7 @@ int mcb_embed_rms_norm(const mcb_embed_args* a, void* stream) {
   p.eps = a->eps;
   launch_row_norm(a->C, a->rows, static_cast<cudaStream_t>(stream), [&](auto cpl, dim3 g, dim3 b,
                                                                         cudaStream_t st) {
-    mcb::embed_rms_norm_kernel<decltype(cpl)::value><<<g, b, 0, st>>>(p);
+    launch_pdl(mcb::embed_rms_norm_kernel<decltype(cpl)::value>, g, b, 0, st, p);
   });
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "embed_rms_norm launch");
@@ -775,7 +796,7 @@ int mcb_softcap_argmax(const mcb_softcap_args* a, void* stream) {
   p.inv_cap = a->softcap > 0.f ? 1.0f / a->softcap : 0.f;
   p.vec = a->V % 8 == 0 && aligned(a->logits, 16) && a->logits_stride % 8 == 0 &&
           (a->out == nullptr || (aligned(a->out, 16) && a->out_stride % 4 == 0));
-  mcb::softcap_argmax_kernel<<<a->rows, 512, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  launch_pdl(mcb::softcap_argmax_kernel, dim3(a->rows), dim3(512), 0, static_cast<cudaStream_t>(stream), p);
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "softcap_argmax launch");
@@ -804,7 +825,7 @@ int mcb_sample(const mcb_sample_args* a, void* stream) {
   p.V = a->V;
   p.top_k = a->top_k;
   p.inv_temperature = 1.0f / a->temperature;
-  mcb::sample_kernel<<<a->rows, mcb::kSampleThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  launch_pdl(mcb::sample_kernel, dim3(a->rows), dim3(mcb::kSampleThreads), 0, static_cast<cudaStream_t>(stream), p);
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sample launch");
@@ -830,16 +851,19 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   if (a->R == 0) return MCB_OK;
   const int tiles = (a->N + mcb::kLinTile - 1) / mcb::kLinTile;
   const int steps = a->K / 64;
+  const int RN = a->R <= 32 ? 32 : (a->R <= 64 ? 64 : (a->R <= 128 ? 128 : 256));
+  const int stages = RN <= 64 ? 8 : (RN == 128 ? 6 : 4);
   int split = a->split;
   if (split == 0) {
+    // the fewest CTAs per output tile whose weight slices fit the ring: every W load is issued
+    // before griddepcontrol.wait, i.e. under the kernel ahead
     split = 1;
-    for (int s = 8; s >= 2; --s)
-      if (steps % s == 0 && tiles * s <= device_sm_count()) { split = s; break; }
+    while (split < 8 && (steps % split != 0 || steps / split > stages)) ++split;
+    if (steps % split != 0) split = 1;
   } else if (steps % split != 0) {
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d does not divide %d K panels", split, steps);
   }
   CUtensorMap wm, xm;
-  const int RN = a->R <= 32 ? 32 : (a->R <= 64 ? 64 : (a->R <= 128 ? 128 : 256));
   int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, mcb::kLinTile);
   if (rc != MCB_OK) return rc;
   rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, RN);
@@ -883,8 +907,8 @@ int mcb_gated_silu(const mcb_gated_silu_args* a, void* stream) {
   p.rows = a->rows;
   p.H = a->H;
   const long long total = static_cast<long long>(a->rows) * (a->H / 8);
-  mcb::gated_silu_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0,
-                          static_cast<cudaStream_t>(stream)>>>(p);
+  launch_pdl(mcb::gated_silu_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), p);
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gated_silu launch");
@@ -895,7 +919,7 @@ int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream) {
   if (cache_seqlens == nullptr || B < 0)
     return fail(MCB_ERR_INVALID_ARG, "mcb_kv_advance: bad arguments");
   if (B == 0) return MCB_OK;
-  mcb::kv_advance_kernel<<<(B + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(cache_seqlens, B, n);
+  launch_pdl(mcb::kv_advance_kernel, dim3((B + 255) / 256), dim3(256), 0, static_cast<cudaStream_t>(stream), cache_seqlens, B, n);
   g_launches++;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kv_advance launch");

@@ -72,6 +72,8 @@ __device__ __forceinline__ T block_exclusive_scan(T v, T* scratch, T* total) {
 }
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
+  pdl_launch_dependents();
+  pdl_wait();  // logits come from the kernel ahead (programmatic dependent launch)
   __shared__ uint32_t hist[256];
   __shared__ float cand_v[kSampleMaxK];
   __shared__ int cand_i[kSampleMaxK];

@@ -97,6 +97,8 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
                                         window_size=(self.window, 0))
     y = self._hook("output", y, x)
     y = y.contiguous().view(B, T, -1)
+    if getattr(self, _FUSE_QKV, False) and self.c_proj.weight.dtype == y.dtype:
+        return step.project(y.view(B * T, -1), self.c_proj.weight).view(B, T, -1)
     return self.c_proj(y)
 
 

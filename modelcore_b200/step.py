@@ -93,6 +93,22 @@ def packed_weight(owner, key, linears):
     return view
 
 
+# With USE_MCB_LINEAR the decode step's projections run on libmcb200's tcgen05 kernel
+# (mcb_linear: weight tiles streamed under programmatic dependent launch, split-K over a cluster)
+# for up to 256 rows.  Off by default: at 64 rows it measures 6-8 us a projection against
+# cuBLAS's 3-4 us in the same CUDA graph (config 2: 84.4k vs 99.0k tokens/s), so F.linear
+# (cuBLAS) stays the projection path; the kernel is kept, tested, for the fusions it allows.
+USE_MCB_LINEAR = False
+
+
+def project(x2d, weight):
+    """F.linear(x2d, weight) without bias for a (rows, K) activation block."""
+    if (USE_MCB_LINEAR and x2d.size(0) <= ops.LINEAR_MAX_ROWS and x2d.size(1) % 64 == 0
+            and x2d.is_contiguous()):
+        return ops.linear(x2d, weight, pdl=True)
+    return F.linear(x2d, weight)
+
+
 def qkv_projection(attn, x):
     """c_q, c_k, c_v of a producer Attention as one GEMM: returns (q, k, v) views shaped
     (B, T, H, D) into the (B, T, (Hq + 2 Hkv) D) product, or None when the weights are not in
@@ -101,7 +117,7 @@ def qkv_projection(attn, x):
         return None
     B, T, _ = x.shape
     w = packed_weight(attn, "qkv", (attn.c_q, attn.c_k, attn.c_v))
-    qkv = F.linear(x, w)
+    qkv = project(x.reshape(B * T, x.size(-1)), w).view(B, T, -1)
     nq = attn.n_head * attn.head_dim
     nk = attn.n_kv_head * attn.head_dim
     q = qkv[..., :nq].view(B, T, attn.n_head, attn.head_dim)
@@ -114,9 +130,9 @@ def gated_mlp(ffn, h):
     """GatedMLP.forward (modelcore/components/mlp.py:89-90) for activation "silu" on (rows, C):
     one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj."""
     w = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
-    gu = F.linear(h, w)
+    gu = project(h, w)
     H = ffn.hidden_dim
-    return F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
+    return project(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
 
 
 def _structure_ok(body):

@@ -284,8 +284,11 @@ def test_fused_step_launches_and_graph_replay(env):
         n0 = ops.launch_count()
         eager.step(cols[0])
         per_step = ops.launch_count() - n0
-        # embedding + first norm, 4 per layer, the advance, the LM-head epilogue
-        attn_launches = per_step - (1 + 4 * 4 + 1 + 1)
+        # embedding + first norm, 4 per layer (+ 4 projections on mcb_linear), the advance,
+        # the LM-head epilogue
+        from modelcore_b200 import step
+        per_layer = 4 + (4 if step.USE_MCB_LINEAR else 0)
+        attn_launches = per_step - (1 + 4 * per_layer + 1 + 1)
         assert attn_launches in (4, 8), per_step     # one or two (split + combine) per layer
         graph.step(cols[0])                           # eager: the graph decoder's first step
         for col in cols[1:]:                          # capture, then replays

@@ -355,3 +355,25 @@ def copy_with_plain_forward(env, model):
         from modelcore_b200 import workloads
         prompts = workloads.prompts(2, 8, seed=3).tolist()
         return mcb.ModelManager().new_decoder(other, prompts, max_tokens=4).step([5, 6]).float().clone()
+
+
+def test_fused_step_on_mcb_linear_projections_is_as_accurate(env):
+    """The same bar with the decode projections on libmcb200's tcgen05 kernel (mcb_linear under
+    programmatic dependent launch) instead of cuBLAS."""
+    from modelcore.tests.test_generate import RAGGED_PROMPTS
+    from modelcore_b200 import step
+    (rm, ref), (fm, fused), _, (m32, ref32) = _models(env, _configs()["quickstart"]())
+    cols = torch.tensor([[(s * 7 + i * 3) % 100 + 1 for s in range(8)]
+                         for i in range(len(RAGGED_PROMPTS))])
+    saved = step.USE_MCB_LINEAR
+    step.USE_MCB_LINEAR = True
+    try:
+        l_fused = _forced(fm, fused, RAGGED_PROMPTS, cols)
+    finally:
+        step.USE_MCB_LINEAR = saved
+    l32 = _forced(m32, ref32, RAGGED_PROMPTS, cols)
+    l_ref = _forced(rm, ref, RAGGED_PROMPTS, cols)
+    e_ref = (l_ref - l32).abs().max().item()
+    e_fused = (l_fused - l32).abs().max().item()
+    assert e_fused <= LOGIT_TOL
+    assert e_fused <= 1.25 * e_ref + 1e-3

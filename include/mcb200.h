@@ -125,9 +125,11 @@ int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
  *  - persistent: all row groups' key tiles form one sequence that a resident grid divides
  *    evenly on the device, from cache_seqlens (no host knowledge of the lengths); row groups
  *    cut between CTAs are merged by the last CTA to finish them.  Chosen for rows that can hold
- *    more than 2048 keys (min(Tmax, window + T)).
- *  - split: one CTA per row group and key split, partials merged by a second kernel when split.
- *    Chosen for shorter rows, where the persistent plan's fixed costs do not pay off.
+ *    more than 2048 keys (min(Tmax, window + T)) when there are more than 128 row groups.
+ *  - split: one CTA per row group and key split.  Up to 8 splits of a row group form a
+ *    thread-block cluster and merge through distributed shared memory; more splits write
+ *    partials that a second kernel merges.  Chosen for shorter rows, where the persistent plan's
+ *    fixed costs do not pay off, and for long rows of at most 128 row groups (2-16 splits).
  *  - prefill (num_ctas == 0, T >= 64, D 64 or 128): 128-query x 128-key tiles on the tcgen05
  *    tensor cores with TMEM accumulators (mcb_prefill_attn below); no workspace or counters.
  * ------------------------------------------------------------------------------------------- */
@@ -155,8 +157,8 @@ typedef struct {
 } mcb_attn_args;
 
 /* Bytes of workspace mcb_decode_attn needs for its partial results (0: none): persistent plan,
- * two slots per CTA, ctas * 2 * rows * (D + 1) * 4; split plan with s > 1 splits,
- * B * T * Hq * s * (D + 1) * 4; in two 256-byte-rounded parts (rows = 8 or 16).  It does not
+ * two slots per CTA, ctas * 2 * rows * (D + 1) * 4; split plan with s > 8 splits,
+ * B * T * Hq * s * (D + 1) * 4 (2 to 8 splits merge in a cluster and need none); in two 256-byte-rounded parts (rows = 8 or 16).  It does not
  * depend on the row lengths.  Calls that can overlap on the GPU need separate workspaces and
  * counter arrays. */
 size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);

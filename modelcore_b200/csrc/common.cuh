@@ -145,6 +145,37 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Thread-block clusters and distributed shared memory
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Cluster-wide barrier, not .aligned: lanes of the producer and MMA warps may arrive apart.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+
+// ---------------------------------------------------------------------------------------------
 // TMA: 4-D tiled bulk tensor load global -> shared, completion signalled on an mbarrier as a
 // transaction count.  No multicast: every CTA fetches its own tiles.  `policy` is an L2 cache
 // policy from createpolicy.

@@ -29,6 +29,7 @@ struct SplitAttnParams {
   int B, T, Hq, Hkv, G, Tmax, window;
   float scale_log2;  // softmax_scale * log2(e)
   int nsplit, tiles_per_split, nqb;
+  int cluster;       // the nsplit (<= 8) CTAs of a row group form a cluster and merge in DSMEM
 };
 
 
@@ -46,7 +47,12 @@ struct SplitAttnConfig {
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
   static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
-  static constexpr int BODY_BYTES = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
+  // cluster merge: this CTA's merged partial [kRows][D], its per-row log2-sum-exp and the
+  // per-row weights of up to 8 ranks, after the per-warp merge buffer
+  static constexpr int CL_OFFSET = (MERGE_BYTES + 15) & ~15;
+  static constexpr int CL_BYTES = kRows * D * 4 + kRows * 4 + kRows * 8 * 4;
+  static constexpr int BODY_BYTES =
+      RING_BYTES > CL_OFFSET + CL_BYTES ? RING_BYTES : CL_OFFSET + CL_BYTES;
   // barriers (full + empty per stage) then per-warp row statistics
   static constexpr int BAR_OFFSET = BODY_BYTES;
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
@@ -100,7 +106,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int tile0 = split * p.tiles_per_split;
   const int my_tiles = max(0, min(ntiles - tile0, p.tiles_per_split));
 
-  if (my_tiles == 0) {  // an empty split: its partial carries no weight
+  if (my_tiles == 0 && !p.cluster) {  // an empty split: its partial carries no weight
     if (threadIdx.x < C::kRows) {
       const int r = r0 + threadIdx.x;
       if (r < r1) {
@@ -349,10 +355,12 @@ __global__ void __launch_bounds__(kAttnThreads)
     const float inv = ltot > 0.f ? 1.f / ltot : 0.f;
     for (int w = 0; w < kAttnConsumerWarps; ++w) stat_f[w * C::kRows + n] *= inv;
     const int r = r0 + n;
-    if (p.nsplit > 1 && r < r1) {
+    const float lse = (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+    if (p.cluster) {
+      reinterpret_cast<float*>(smem + C::CL_OFFSET)[C::kRows * D + n] = lse;
+    } else if (p.nsplit > 1 && r < r1) {
       const int t = r / p.G, h = kvh * p.G + r % p.G;
-      p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] =
-          (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+      p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] = lse;
     }
   }
   __syncthreads();
@@ -370,10 +378,55 @@ __global__ void __launch_bounds__(kAttnThreads)
     const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;
     if (p.nsplit == 1) {
       p.out[row * D + d] = float_to_bf16_bits(o);
+    } else if (p.cluster) {
+      reinterpret_cast<float*>(smem + C::CL_OFFSET)[n * D + d] = o;
     } else {
       p.part_o[(row * p.nsplit + split) * D + d] = o;
     }
   }
+  if (!p.cluster) return;
+
+  // ---- cluster merge: rank q (= split) writes rows n = q, q + nsplit, .. of the row group ----
+  float* cpart = reinterpret_cast<float*>(smem + C::CL_OFFSET);
+  float* clse = cpart + C::kRows * D;
+  float* cw = clse + C::kRows;  // [kRows][8]
+  cluster_sync();  // every rank's partial and lse are written
+  const int ns = p.nsplit;
+  if (threadIdx.x < C::kRows && static_cast<int>(threadIdx.x) % ns == split) {
+    const int n = threadIdx.x;
+    float l[8];
+    float mmax = -CUDART_INF_F;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      l[q] = q < ns ? ld_dsmem_f32(map_to_rank(clse + n, static_cast<uint32_t>(q))) : -CUDART_INF_F;
+      mmax = fmaxf(mmax, l[q]);
+    }
+    float wsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      l[q] = (l[q] == -CUDART_INF_F) ? 0.f : fast_exp2(l[q] - mmax);
+      wsum += l[q];
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cw[n * 8 + q] = l[q] * inv;
+  }
+  __syncthreads();
+  const int my_rows = (C::kRows - split + ns - 1) / ns;
+  for (int idx = threadIdx.x; idx < my_rows * D; idx += kAttnThreads) {
+    const int n = split + (idx / D) * ns;
+    const int d = idx % D;
+    const int r = r0 + n;
+    float o = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < ns) o = fmaf(cw[n * 8 + q], ld_dsmem_f32(map_to_rank(cpart + n * D + d, static_cast<uint32_t>(q))), o);
+    if (r < r1) {
+      const int t = r / p.G, h = kvh * p.G + r % p.G;
+      p.out[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);
+    }
+  }
+  cluster_sync();  // no rank exits while another still reads its shared memory
 }
 
 // Merges the split partials of every (b, t, h) row: one warp per row.

@@ -199,17 +199,24 @@ struct AttnVariant {
     cfg.blockDim = dim3(mcb::kAttnThreads);
     cfg.dynamicSmemBytes = SplitCfg::SMEM_BYTES;
     cfg.stream = st;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr.val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = &attr;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.numAttrs = 1;
+    if (prm.cluster) {
+      attrs[1].id = cudaLaunchAttributeClusterDimension;
+      attrs[1].val.clusterDim.x = static_cast<unsigned>(prm.nsplit);
+      attrs[1].val.clusterDim.y = 1;
+      attrs[1].val.clusterDim.z = 1;
+      cfg.numAttrs = 2;
+    }
+    cfg.attrs = attrs;
     e = cudaLaunchKernelEx(&cfg, split_kernel, km, vm, prm);
     g_launches++;
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
-    if (prm.nsplit > 1) {
+    if (prm.nsplit > 1 && !prm.cluster) {
       const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
       mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
       g_launches++;
@@ -244,6 +251,7 @@ int variant_launch_split(int D, int nqt, long long grid, const CUtensorMap& km, 
 
 struct AttnPlan {
   int D, nqt, rows, tk, nqb, mode;
+  bool cluster = false;  // split plan merged inside a cluster
   int grid;         // persistent CTAs (persistent mode)
   int nsplit, tps;  // key splits per row group and tiles per split (split mode)
   size_t part_o_bytes, part_lse_bytes, ws_bytes, counter_count;
@@ -290,13 +298,21 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
   const long long base = static_cast<long long>(a->B) * a->Hkv * pl->nqb;
   if (base * max_tiles > 0x7fffffffll)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: more than 2^31 key tiles");
-  pl->mode = (a->num_ctas < 0 || (a->num_ctas == 0 && max_tiles <= kSplitMaxTiles)) ? kModeSplit
-                                                                                  : kModePersistent;
+  // Long rows of few row groups (config 5 at batch 1 and 8): a fixed split count beats the
+  // persistent partition, whose start-up scan and cross-CTA merge are not amortised over so few
+  // groups (measured on B200 at 4,096-key windows and 32k-key rows).
+  const bool few_long = a->num_ctas == 0 && max_tiles > kSplitMaxTiles && base <= 128;
+  pl->mode = (a->num_ctas < 0 || few_long || (a->num_ctas == 0 && max_tiles <= kSplitMaxTiles))
+                 ? kModeSplit
+                 : kModePersistent;
   const size_t rows_out = static_cast<size_t>(a->B) * a->T * a->Hq;
   if (pl->mode == kModeSplit) {
     int nsplit;
     if (a->num_ctas < 0) {
       nsplit = static_cast<int>(std::min<long long>(-static_cast<long long>(a->num_ctas), max_tiles));
+    } else if (few_long) {
+      nsplit = base <= 16 ? static_cast<int>(std::max<long long>(2, std::min<long long>(16, max_tiles / 8)))
+                          : static_cast<int>(std::max<long long>(2, std::min<long long>(4, max_tiles / 16)));
     } else {
       const long long target = 4ll * device_sm_count();
       nsplit = base > 0 ? static_cast<int>(std::min<long long>((target + base - 1) / base, max_tiles)) : 1;
@@ -306,7 +322,10 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
     pl->nsplit = static_cast<int>((max_tiles + pl->tps - 1) / pl->tps);
     if (base * pl->nsplit > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: grid too large");
     pl->grid = 0;
-    if (pl->nsplit > 1) {
+    // up to 8 splits of a row group form a thread-block cluster and merge through distributed
+    // shared memory: no partials in global memory and no combine kernel
+    pl->cluster = pl->nsplit >= 2 && pl->nsplit <= 8;
+    if (pl->nsplit > 1 && !pl->cluster) {
       pl->part_o_bytes = round256(rows_out * pl->nsplit * a->D * 4);
       pl->part_lse_bytes = round256(rows_out * pl->nsplit * 4);
     } else {
@@ -431,8 +450,9 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     for (int i = 0; i < 3; ++i) p.qs[i] = a->q_stride[i];
     p.cache_seqlens = a->cache_seqlens;
     p.out = static_cast<uint16_t*>(a->out);
-    p.part_o = pl.nsplit > 1 ? reinterpret_cast<float*>(w) : nullptr;
-    p.part_lse = pl.nsplit > 1 ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
+    p.part_o = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w) : nullptr;
+    p.part_lse = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
+    p.cluster = pl.cluster ? 1 : 0;
     p.B = a->B;
     p.T = a->T;
     p.Hq = a->Hq;

@@ -215,7 +215,7 @@ def _attn_case_to_device(z):
             torch.from_numpy(z["seqlens"]).to(torch.int32).cuda(), int(z["window"]))
 
 
-@pytest.mark.parametrize("splits", [0, 1, 3, 37, -1, -3])
+@pytest.mark.parametrize("splits", [0, 1, 3, 37, -1, -3, -12])
 @pytest.mark.parametrize("name", golden_files("kv_attn_"))
 def test_attention_matches_the_reference_golden_outputs(mcb, name, splits):
     _, ops = mcb
@@ -269,7 +269,7 @@ def test_attention_matches_the_oracle_on_random_ragged_rows(mcb, case):
     lens[0] = 0
     ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
     args = (dev_bf16(q), dev_bf16(kc), dev_bf16(vc), torch.from_numpy(lens).to(torch.int32).cuda())
-    for splits in (0, 1, 2, 5, 300, -1, -2, -7):
+    for splits in (0, 1, 2, 5, 300, -1, -2, -7, -8, -12):  # -2..-8: cluster merge; -12: combine kernel
         y = ops.decode_attn(*args, window=window, num_ctas=splits)
         err = np.abs(y.float().cpu().numpy() - ref).max()
         assert err <= ATTN_TOL, (splits, err)

@@ -38,16 +38,18 @@ def _call_noalloc(q, kc, vc, sl, out, window, num_ctas):
 
 
 SHAPES = [
-    # B, Hq, Hkv, D, Tmax, window, num_ctas (0: automatic plan, persistent for these rows;
-    # > 0 persistent grid; < 0 split plan with that many key splits)
-    (8, 32, 8, 128, 8192, -1, 0),
+    # B, Hq, Hkv, D, Tmax, window, num_ctas (0: automatic plan, persistent for these rows --
+    # long, and more than 128 row groups;
+    # > 0 persistent grid; < 0 split plan with that many key splits -- more than 8, so its
+    # partials go through memory: up to 8 splits merge inside a cluster and need none)
+    (32, 32, 8, 128, 8192, -1, 0),
     (4, 12, 12, 64, 3000, 100, 24),
-    (4, 12, 12, 64, 1000, -1, -3),
+    (4, 12, 12, 64, 1000, -1, -12),
 ]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto", "mha-d64-window-24-ctas",
-                                               "mha-d64-3-splits"])
+                                               "mha-d64-12-splits"])
 def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape):
     B, Hq, Hkv, D, Tmax, window, splits = shape
     for call, seed in enumerate((11, 12)):
@@ -82,3 +84,15 @@ def test_noalloc_rejects_a_grid_whose_partials_exceed_its_scratch():
     out2 = ops.decode_attn_noalloc(q, kc, vc, sl, num_ctas=64)
     ref = ops.decode_attn(q, kc, vc, sl, num_ctas=64)
     assert (out2.float() - ref.float()).abs().max().item() <= ATTN_TOL
+
+
+def test_cluster_merged_splits_need_no_scratch():
+    """Up to 8 key splits of a row group merge through distributed shared memory: the plan needs
+    no partials at all, so the no-alloc entry point serves it without touching the scratch."""
+    q, kc, vc, sl = _inputs(3, 4, 12, 12, 64, 1000)
+    assert ops.decode_attn_workspace_bytes(q, kc, vc, sl, num_ctas=-3) == 0
+    out = torch.empty_like(q)
+    assert _call_noalloc(q, kc, vc, sl, out, -1, -3) == _native.MCB_OK
+    expected = ops.decode_attn(q, kc, vc, sl, num_ctas=-12)
+    torch.cuda.synchronize()
+    assert (out.float() - expected.float()).abs().max().item() <= ATTN_TOL

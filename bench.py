@@ -14,7 +14,7 @@ hot path; the sampled tokens are gathered with NCCL at the end of the timed regi
 
 value      64*N*K / max-over-ranks(device time of K CUDA-graph replays), tokens/s; the graph
            feeds each step's greedy token to the next on the device.
-e2e        the same through the public step() call: per step a pinned host->device copy of the
+e2e        the same through the public step_greedy() call: per step a pinned host->device copy of the
            token column, the replayed step, and the device->host read of the greedy tokens.
 roofline   the decode-attention kernel: algorithmic KV bytes (exact keys per row and layer,
            2*Hkv*D*2 bytes each) / its mean launch time, timed with CUDA events on its stream
@@ -537,18 +537,19 @@ def run_b200(args):
     kv_bytes_step = float(((ctx_before + ctx_after) / 2 + 1).sum()) * cache.n_slots * 2 * \
         cache.n_kv_head * cache.head_dim * 2
 
-    # e2e: the public step() with host token columns in pinned memory, tokens read back per step
+    # e2e: the public GraphDecoder.step_greedy() -- host token column in through pinned memory,
+    # the forward, the greedy pick, the next tokens back in pinned memory and read on the host,
+    # every step
     with torch.inference_mode():
-        host_tok = torch.argmax(dec.logits, dim=-1).cpu().pin_memory()
-        for _ in range(2):  # the first step() captures its graph: keep that out of the timing
-            host_tok = torch.argmax(dec.step(host_tok), dim=-1).to("cpu")
+        host_tok = torch.argmax(dec.logits, dim=-1).cpu()
+        for _ in range(2):  # the first call captures its graph: keep that out of the timing
+            host_tok = dec.step_greedy(host_tok).clone()
         _barrier(world)
         t0 = time.perf_counter()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(args.e2e_steps):
-            logits = dec.step(host_tok)
-            host_tok = torch.argmax(logits, dim=-1).to("cpu")
+            host_tok = dec.step_greedy(host_tok)
         f1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0

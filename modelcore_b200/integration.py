@@ -190,7 +190,10 @@ class GraphDecoder:
     cache must not be reallocated while it lives.
 
     greedy_steps(n) additionally keeps the argmax on the device: each replay feeds its own
-    greedy token to the next step (no host round trip), returning the (B, n) tokens."""
+    greedy token to the next step (no host round trip), returning the (B, n) tokens.
+    step_greedy(tokens) is step() plus the greedy pick for a caller that drives every step from
+    the host: the pinned-memory copy in, the forward, the pick and the pinned-memory copy out are
+    one graph, and the call returns the next tokens on the host."""
 
     def __init__(self, model, manager, tokens, *, num_samples=1, max_tokens=None, device=None):
         from modelcore.generate import Decoder
@@ -209,6 +212,10 @@ class GraphDecoder:
         self._ids = torch.zeros((B, 1), dtype=torch.long, device=dev)
         self._ids_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
         self._static_logits = None
+        self._rt_graph = None
+        self._next = torch.zeros((B, 1), dtype=torch.long, device=dev)
+        self._next_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
+        self._rt_done = torch.cuda.Event()
         self.launches_per_step = None  # libmcb200 kernels recorded in one captured step
 
     @property
@@ -300,6 +307,52 @@ class GraphDecoder:
             self._replayed()
             self._logits = logits
         return out
+
+    def _capture_roundtrip(self):
+        cache = self.kv_cache
+        snap = cache.host_state()
+        state_snap = dict(cache.state)
+        g = torch.cuda.CUDAGraph()
+        with torch.inference_mode():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            fused_pick = step.decode_installed(self.model) and step._model_call_ok(self.model, self._ids, cache)
+            with torch.cuda.graph(g, stream=side):
+                self._ids.copy_(self._ids_host, non_blocking=True)
+                if fused_pick:
+                    logits = step.decode_forward(self.model, self._ids, cache,
+                                                 argmax_out=self._next)[:, -1, :]
+                else:
+                    logits = self.model.forward(self._ids, kv_cache=cache)[:, -1, :]
+                    self._next.copy_(torch.argmax(logits, dim=-1, keepdim=True))
+                self._next_host.copy_(self._next, non_blocking=True)
+            torch.cuda.current_stream().wait_stream(side)
+        cache.restore_host_state(snap)
+        cache.state.update(state_snap)
+        return g, logits
+
+    @torch.inference_mode()
+    def step_greedy(self, token_column):
+        """step(token_column), then the greedy pick of the new logits (sample_next_token with
+        temperature 0, modelcore/generate.py:23-24): returns the (B,) next tokens as a host int64
+        tensor (a view of pinned memory, valid until the next call).  The host-to-device copy of
+        the column, the decode forward with the pick fused into the LM-head epilogue and the
+        device-to-host copy of the tokens replay as one CUDA graph."""
+        self._room(1)
+        self._ids_host.copy_(torch.as_tensor(token_column, dtype=torch.long).view(-1, 1))
+        if self._rt_graph is None and self._eager_steps == 0:
+            self._ids.copy_(self._ids_host, non_blocking=True)
+            self._logits = self._eager(self._ids.clone())
+            self._next_host.copy_(torch.argmax(self._logits, dim=-1, keepdim=True).cpu())
+            return self._next_host.view(-1)
+        if self._rt_graph is None:
+            self._rt_graph, self._rt_logits = self._capture_roundtrip()
+        self._rt_graph.replay()
+        self._replayed()
+        self._rt_done.record()
+        self._rt_done.synchronize()
+        self._logits = self._rt_logits
+        return self._next_host.view(-1)
 
     def _eager(self, ids):
         logits = self.model.forward(ids, kv_cache=self.kv_cache)[:, -1, :]

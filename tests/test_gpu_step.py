@@ -305,6 +305,16 @@ def test_fused_step_launches_and_graph_replay(env):
             e2.step(nxt.tolist())
         assert torch.equal(dev_tokens, torch.stack(host, 1))
         assert torch.equal(g2.logits, e2.logits)
+        # step_greedy: host column in, host greedy tokens out, one graph per step
+        g3 = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+        e3 = mgr.new_decoder(model, prompts, max_tokens=16)
+        tok = torch.argmax(e3.logits, dim=-1).cpu()
+        for _ in range(8):
+            nxt = g3.step_greedy(tok).clone()
+            want = torch.argmax(e3.step(tok.tolist()), dim=-1).cpu()
+            assert torch.equal(nxt, want)
+            assert torch.equal(g3.logits, e3.logits)
+            tok = nxt
 
 
 def test_packed_weights_follow_the_parameters(env):

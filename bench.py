@@ -192,9 +192,27 @@ def _build_decoder(rank, world, steps_needed, fuse_step=True):
     begin, end = contiguous_rows(ROWS_PER_GPU * world, world, rank)
     mine = all_prompts[begin:end].tolist()
     with torch.inference_mode():
+        # one warm-up prefill (kernel modules, cuBLAS heuristics), then the timed one
+        mgr.new_decoder(model, mine[:2], max_tokens=8, cuda_graph=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
         dec = mgr.new_decoder(model, mine, max_tokens=DECODE_LEN, cuda_graph=True)
+        torch.cuda.synchronize()
+        dec.prefill_ms = (time.perf_counter() - t0) * 1e3
     assert steps_needed <= DECODE_LEN, "more decode steps than the configured 512"
     return mgr, model, dec
+
+
+def _per_prompt_prefill_ms(mgr, model, prompts):
+    """The same prefill the reference's Decoder does (every prompt alone at batch 1, then
+    prefill_row), on the B200 kernels: wall time in ms."""
+    import torch
+    with torch.inference_mode():
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        mgr.new_decoder(model, prompts, max_tokens=DECODE_LEN, cuda_graph=True, batched_prefill=False)
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e3
 
 
 def _attention_roofline(dec, peak, reps=4):
@@ -562,9 +580,16 @@ def run_b200(args):
         sweep = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
                                windows=tuple(args.sweep_windows))
     copies = prefill = None
+    prompt_prefill = {"workload": f"{B} prompts x {PROMPT_LEN} tokens per GPU, one forward "
+                                  "(GraphDecoder batched ragged prefill)",
+                      "batched_ms": round(dec.prefill_ms, 2)}
     if world == 1 and not args.no_sweep:
         copies = _copy_and_append(peak)
         prefill = _prefill(_bf16_peak())
+        from modelcore_b200 import workloads
+        mine = workloads.prompts(ROWS_PER_GPU, PROMPT_LEN, seed=1).tolist()
+        prompt_prefill["per_prompt_ms"] = round(_per_prompt_prefill_ms(mgr, model, mine), 2)
+        prompt_prefill["per_prompt"] = "modelcore's Decoder order: each prompt at batch 1, then prefill_row"
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
@@ -609,6 +634,7 @@ def run_b200(args):
         "kv_read_sweep": sweep,
         "kv_copies": copies,
         "prefill_attention": prefill,
+        "prompt_prefill": prompt_prefill,
     }
     print(json.dumps(line), flush=True)
 

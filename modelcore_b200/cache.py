@@ -123,6 +123,17 @@ class KVCache:
         lens = self._host_lens
         self._pos_uniform = int(lens[0]) if bool((lens == lens[0]).all()) else None
 
+    def set_row_lengths(self, lengths):
+        """Sets every row's length (device and host mirror): after a batched ragged prefill that
+        advanced all rows by the padded prompt length, each row keeps only its own prompt.
+        Positions past a row's length hold stale keys the attention never reads."""
+        lens = np.asarray(lengths, dtype=np.int64)
+        assert lens.shape == (self.batch_size,), "one length per row"
+        assert int(lens.max(initial=0)) <= self.max_seq_len, "length beyond the cache"
+        self.cache_seqlens.copy_(torch.from_numpy(lens.astype(np.int32)), non_blocking=False)
+        self._host_lens[:] = lens
+        self._pos_uniform = int(lens[0]) if lens.size and bool((lens == lens[0]).all()) else None
+
     # -- host-side helpers ---------------------------------------------------------------------
     def host_lens(self):
         """Row lengths as this cache's methods have set them (no device read)."""

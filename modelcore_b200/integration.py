@@ -164,12 +164,13 @@ class _ManagerMixin:
                        **spec)
 
     def new_decoder(self, model, tokens, *, num_samples=1, max_tokens=None, device=None,
-                    cuda_graph=False):
+                    cuda_graph=False, batched_prefill=True):
         """modelcore's Decoder (modelcore/generate.py:37-94) over the B200 cache; with
-        cuda_graph=True, a GraphDecoder."""
+        cuda_graph=True, a GraphDecoder (whose multi-prompt prefill is one batched forward unless
+        batched_prefill=False)."""
         if cuda_graph:
             return GraphDecoder(model, self, tokens, num_samples=num_samples, max_tokens=max_tokens,
-                                device=device)
+                                device=device, batched_prefill=batched_prefill)
         from modelcore.generate import Decoder
         return Decoder(model, self, tokens, num_samples=num_samples, max_tokens=max_tokens,
                        device=device)
@@ -195,15 +196,24 @@ class GraphDecoder:
     the host: the pinned-memory copy in, the forward, the pick and the pinned-memory copy out are
     one graph, and the call returns the next tokens on the host."""
 
-    def __init__(self, model, manager, tokens, *, num_samples=1, max_tokens=None, device=None):
-        from modelcore.generate import Decoder
-        self._dec = Decoder(model, manager, tokens, num_samples=num_samples, max_tokens=max_tokens,
-                            device=device)
+    def __init__(self, model, manager, tokens, *, num_samples=1, max_tokens=None, device=None,
+                 batched_prefill=True):
         self.model = model
-        self.kv_cache = self._dec.kv_cache
+        prompts = None if isinstance(tokens[0], int) else [list(p) for p in tokens]
+        dev = torch.device(device) if device is not None else model.get_device()
+        done = None
+        if (batched_prefill and prompts is not None and len(prompts) > 1
+                and step.decode_installed(model) and dev.type == "cuda"):
+            done = self._batched_prefill(manager, prompts, num_samples, max_tokens, dev)
+        if done is not None:
+            self.kv_cache, self._logits = done
+        else:
+            from modelcore.generate import Decoder
+            dec = Decoder(model, manager, tokens, num_samples=num_samples, max_tokens=max_tokens,
+                          device=device)
+            self.kv_cache, self._logits = dec.kv_cache, dec.logits
         if not isinstance(self.kv_cache, KVCache):
             raise RuntimeError("GraphDecoder needs the modelcore_b200 KVCache (a CUDA model)")
-        self._logits = self._dec.logits
         self._graph = None
         self._greedy_graph = None
         self._eager_steps = 0
@@ -217,6 +227,42 @@ class GraphDecoder:
         self._next_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
         self._rt_done = torch.cuda.Event()
         self.launches_per_step = None  # libmcb200 kernels recorded in one captured step
+
+    @torch.inference_mode()
+    def _batched_prefill(self, manager, prompts, num_samples, max_tokens, dev):
+        """Decoder's multi-prompt prefill (modelcore/generate.py:64-79: every prompt prefilled
+        alone at batch 1, then prefill_row into its right-ragged row) as one forward: the prompts
+        right-padded into a (P, max_len) batch, one pass through the model (the tensor-core
+        prefill attention, the projections at M = P x max_len), the LM head only at each prompt's
+        last token, then every row cut back to its own length.  A row's padding positions hold
+        keys no later query reads (each decode step overwrites the next one).  num_samples > 1
+        copies each prompt's row into its samples' rows."""
+        model = self.model
+        P, S = len(prompts), num_samples
+        lens = [len(p) for p in prompts]
+        width = max(lens)
+        kv_len = (width + max_tokens) if max_tokens is not None else model.config.sequence_len
+        cache = manager.new_kv_cache(model, batch_size=P * S, seq_len=kv_len, device=dev)
+        ids = torch.zeros((P, width), dtype=torch.long)
+        for i, p in enumerate(prompts):
+            ids[i, :len(p)] = torch.tensor(p, dtype=torch.long)
+        ids = ids.to(dev)
+        last = torch.tensor([n - 1 for n in lens], dtype=torch.long, device=dev)
+        target = cache if S == 1 else manager.new_kv_cache(model, batch_size=P, seq_len=width,
+                                                             device=dev)
+        if not step._model_call_ok(model, ids, target):
+            return None  # not the fused decode forward's model: modelcore's prefill runs
+        target.check_room(width)
+        logits = step.decode_forward(model, ids, target, last_positions=last)[:, 0, :]
+        target.set_row_lengths(lens)
+        if S > 1:
+            for i, n in enumerate(lens):
+                ops.kv_copy_rows(cache.k_cache, cache.v_cache, target.k_cache, target.v_cache,
+                                 src_row=i, dst_row_begin=i * S, dst_row_count=S, n_pos=n,
+                                 dst_seqlens=cache.cache_seqlens)
+            cache.set_row_lengths([n for n in lens for _ in range(S)])
+            logits = logits.repeat_interleave(S, dim=0)
+        return cache, logits
 
     @property
     def logits(self):

@@ -224,20 +224,25 @@ def _model_call_ok(model, idx, kv_cache):
     return _call_ok(model.body, probe, kv_cache)
 
 
-def decode_forward(model, idx, kv_cache, argmax_out=None, want_logits=True):
+def decode_forward(model, idx, kv_cache, argmax_out=None, want_logits=True, last_positions=None):
     """Model.forward (modelcore/model.py:93-101) with kv_cache and without targets, for a model
     whose body qualifies for stack_forward and whose embedding (TokenEmbedding without smear) and
     LM head (LMHead) share one RMSNorm eps: mcb_embed_rms_norm gives the embedding and the first
     block's normed input in one launch; the last block's fused add + norm is the LM head's norm;
     mcb_softcap_argmax does the crop, .float() and softcap after the projection and, with
     argmax_out, the greedy pick.  Returns the fp32 logits (B, T, vocab_size) (None when
-    want_logits is False)."""
+    want_logits is False).  With last_positions (B,) the LM head runs only on row b's position
+    last_positions[b] and the logits are (B, 1, vocab_size): a batched prefill needs the next-token
+    logits of each prompt's last token, not the (B, T, vocab) block."""
     B, T = idx.shape
     emb, un = model.embedding, model.unembedding
     x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
     C = x.size(-1)
     _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
     kv_cache.advance(T)
+    if last_positions is not None:
+        h = h.view(B, T, C)[torch.arange(B, device=h.device), last_positions]
+        T = 1
     logits = F.linear(h, un.lm_head.weight)
     out = ops.softcap_argmax(logits, un.vocab_size, un.softcap, argmax_out=argmax_out,
                              want_logits=want_logits)

@@ -387,3 +387,30 @@ def test_fused_step_on_mcb_linear_projections_is_as_accurate(env):
     e_fused = (l_fused - l32).abs().max().item()
     assert e_fused <= LOGIT_TOL
     assert e_fused <= 1.25 * e_ref + 1e-3
+
+
+@pytest.mark.parametrize("samples", [1, 3])
+def test_batched_prefill_matches_per_prompt_prefill(env, samples):
+    """GraphDecoder's one-forward ragged prefill against modelcore's per-prompt prefill
+    (Decoder, batch-1 forwards + prefill_row): same row lengths, logits within LOGIT_TOL, and the
+    first decode steps' logits too (the caches hold the same keys up to GEMM summation order)."""
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    mgr = mcb.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
+                                              device=torch.device("cuda"), seed=0))
+    model = model.to(torch.bfloat16).eval()
+    prompts = workloads.prompts(5, 150, seed=4).tolist()
+    for i, n in enumerate((150, 3, 77, 128, 1)):
+        prompts[i] = prompts[i][:n]
+    with torch.inference_mode():
+        fast = mgr.new_decoder(model, prompts, num_samples=samples, max_tokens=8, cuda_graph=True)
+        slow = mgr.new_decoder(model, prompts, num_samples=samples, max_tokens=8, cuda_graph=True,
+                               batched_prefill=False)
+        assert fast.kv_cache.cache_seqlens.tolist() == slow.kv_cache.cache_seqlens.tolist()
+        assert fast.kv_cache.host_lens().tolist() == slow.kv_cache.cache_seqlens.tolist()
+        assert (fast.logits - slow.logits).abs().max().item() <= LOGIT_TOL
+        for s in range(4):
+            col = [(s * 13 + r) % 500 for r in range(5 * samples)]
+            a, b = fast.step(col), slow.step(col)
+            assert (a - b).abs().max().item() <= LOGIT_TOL, s

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 2
+#define MCB_ABI_VERSION 3
 
 typedef enum {
   MCB_OK = 0,
@@ -81,6 +81,8 @@ typedef struct {
   float eps;                  /* rms_norm epsilon as fp32 (torch: fp32 machine eps when None) */
   float scale;                /* 1.2f in modelcore                                          */
   uint32_t flags;             /* MCB_APPEND_* bits                                          */
+  int32_t ring;               /* 0: position p at index p; 1: the slot is a ring of Tmax
+                                 positions, position p at index p % Tmax                    */
 } mcb_append_args;
 
 int mcb_kv_append_rope(const mcb_append_args* args, void* stream);
@@ -154,6 +156,9 @@ typedef struct {
                                  completed call leaves the ones it used at zero again, so one
                                  array serves every call of a stream (of any shape that fits)*/
   size_t counter_count;
+  int32_t ring;               /* 1: the slot is a ring of Tmax positions (p at p % Tmax);
+                                 needs window >= 0, window + T <= Tmax and Tmax a multiple of
+                                 128, so every visible key is resident and no key tile wraps */
 } mcb_attn_args;
 
 /* Bytes of workspace mcb_decode_attn needs for its partial results (0: none): persistent plan,

@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -78,6 +78,7 @@ class AppendArgs(ctypes.Structure):
         ("rot_len", ctypes.c_int32),
         ("eps", ctypes.c_float), ("scale", ctypes.c_float),
         ("flags", ctypes.c_uint32),
+        ("ring", ctypes.c_int32),
     ]
 
 
@@ -106,6 +107,7 @@ class AttnArgs(ctypes.Structure):
         ("num_ctas", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("counters", ctypes.c_void_p), ("counter_count", ctypes.c_size_t),
+        ("ring", ctypes.c_int32),
     ]
 
 

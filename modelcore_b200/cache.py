@@ -30,7 +30,15 @@ def _aligned_zeros(shape, device):
 
 
 class KVCache:
-    def __init__(self, batch_size, n_kv_head, seq_len, head_dim, num_kv_slots, device, dtype):
+    """modelcore.cache.KVCache on the B200 layout.  ring_slots / ring_capacity: optional window
+    rings -- slots read only by sliding-window layers keep ring_capacity positions (a multiple of
+    128, below seq_len), position p at index p % ring_capacity, instead of seq_len; step_limit is
+    then the most tokens one forward may append (ring_capacity minus the largest window of those
+    layers), so every key a query can see is still resident.  The full-length slots stay in
+    k_cache / v_cache, the rings in k_ring / v_ring; get_slot_cache and slot_ring resolve a slot."""
+
+    def __init__(self, batch_size, n_kv_head, seq_len, head_dim, num_kv_slots, device, dtype,
+                 ring_slots=(), ring_capacity=0, ring_window=None):
         _native.load()
         device = torch.device(device)
         if device.type != "cuda":
@@ -44,9 +52,21 @@ class KVCache:
         self.n_slots = num_kv_slots
         self.n_kv_head = n_kv_head
         self.head_dim = head_dim
-        shape = (num_kv_slots, batch_size, seq_len, n_kv_head, head_dim)
-        self.k_cache = _aligned_zeros(shape, device)
-        self.v_cache = _aligned_zeros(shape, device)
+        ring = sorted(set(int(x) for x in ring_slots)) if 0 < ring_capacity < seq_len else []
+        if ring:
+            assert ring_capacity % 128 == 0, "ring capacity must be a multiple of 128 positions"
+            assert ring_window is not None and 0 <= ring_window < ring_capacity, \
+                "a window ring needs the largest window of its layers, below the capacity"
+        full = [x for x in range(num_kv_slots) if x not in ring]
+        self._slots = {x: (False, i) for i, x in enumerate(full)}
+        self._slots.update({x: (True, i) for i, x in enumerate(ring)})
+        self.ring_capacity = ring_capacity if ring else 0
+        self.step_limit = ring_capacity - ring_window if ring else None
+        self.k_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device)
+        self.v_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device)
+        rshape = (len(ring), batch_size, self.ring_capacity, n_kv_head, head_dim)
+        self.k_ring = _aligned_zeros(rshape, device)
+        self.v_ring = _aligned_zeros(rshape, device)
         self.cache_seqlens = torch.zeros(batch_size, dtype=torch.int32, device=device)
         self._pos_uniform = 0
         self._host_lens = np.zeros(batch_size, dtype=np.int64)
@@ -70,7 +90,44 @@ class KVCache:
         return self._pos_uniform
 
     def get_slot_cache(self, slot):
-        return self.k_cache[slot], self.v_cache[slot]
+        is_ring, i = self._slots[slot]
+        if is_ring:
+            return self.k_ring[i], self.v_ring[i]
+        return self.k_cache[i], self.v_cache[i]
+
+    def slot_ring(self, slot):
+        """True when `slot` is a window ring (position p at index p % ring_capacity)."""
+        return self._slots[slot][0]
+
+    def cache_bytes(self):
+        """Device bytes of the K and V storage."""
+        return 2 * (self.k_cache.numel() + self.k_ring.numel()) * 2
+
+    def _copy_slots_from(self, other, dst_row_begin, dst_row_count, n_pos, src_row=0):
+        """Positions [0, n_pos) of other's row src_row into rows [dst_row_begin, +count), every
+        slot, ring or not; cache_seqlens of those rows set to n_pos."""
+        same_layout = (not self.ring_capacity and not other.ring_capacity)
+        if same_layout:
+            ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=src_row,
+                             dst_row_begin=dst_row_begin, dst_row_count=dst_row_count, n_pos=n_pos,
+                             dst_seqlens=self.cache_seqlens)
+            return
+        for slot in range(self.n_slots):
+            d_ring, di = self._slots[slot]
+            s_ring, si = other._slots[slot]
+            dk, dv = (self.k_ring, self.v_ring) if d_ring else (self.k_cache, self.v_cache)
+            sk, sv = (other.k_ring, other.v_ring) if s_ring else (other.k_cache, other.v_cache)
+            n = n_pos
+            if d_ring:
+                assert s_ring and other.ring_capacity == self.ring_capacity or n_pos <= self.ring_capacity, \
+                    "a window ring takes a longer prompt only from a ring of the same capacity"
+                n = min(n_pos, self.ring_capacity)  # a ring holds positions p at p % capacity
+            else:
+                assert not s_ring, "a full-length slot cannot be filled from a window ring"
+            ops.kv_copy_rows(dk[di:di + 1], dv[di:di + 1], sk[si:si + 1], sv[si:si + 1],
+                             src_row=src_row, dst_row_begin=dst_row_begin,
+                             dst_row_count=dst_row_count, n_pos=n, dst_seqlens=None)
+        self.cache_seqlens[dst_row_begin:dst_row_begin + dst_row_count] = n_pos
 
     def advance(self, num_tokens):
         """cache_seqlens += num_tokens on the device, and the host mirrors with it
@@ -88,9 +145,7 @@ class KVCache:
         assert self.max_seq_len >= other.max_seq_len
         other_pos = other.get_pos()
         if self.n_slots:
-            ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=0,
-                             dst_row_begin=0, dst_row_count=self.batch_size, n_pos=other_pos,
-                             dst_seqlens=self.cache_seqlens)
+            self._copy_slots_from(other, 0, self.batch_size, other_pos)
         else:
             self.cache_seqlens.fill_(other_pos)
         self._pos_uniform = other_pos
@@ -108,9 +163,7 @@ class KVCache:
         other_pos = other.get_pos()
         assert other_pos <= self.max_seq_len, f"prompt of {other_pos} tokens exceeds cache length {self.max_seq_len}"
         if self.n_slots:
-            ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=0,
-                             dst_row_begin=row, dst_row_count=1, n_pos=other_pos,
-                             dst_seqlens=self.cache_seqlens)
+            self._copy_slots_from(other, row, 1, other_pos)
         else:
             self.cache_seqlens[row] = other_pos
         for key, value in other.state.items():

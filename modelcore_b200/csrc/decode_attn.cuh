@@ -49,6 +49,7 @@ struct AttnParams {
   float* part_lse;  // [(cta*2 + slot)*ROWS + n]
   int* counters;     // [entry * Hkv + kv head] arrivals; zero on entry, left zero on exit
   int B, T, Hq, Hkv, G, Tmax, window;
+  int ring;  // the slot is a ring of Tmax positions (key c at index c % Tmax)
   float scale_log2;  // softmax_scale * log2(e)
   int nqb;           // query blocks per row
   int n_entries;     // B * nqb
@@ -109,7 +110,7 @@ __device__ __forceinline__ Entry make_entry(const AttnParams& p, int e, int L) {
   const int t_first = x.r0 / p.G;
   const int t_last = (x.r1 - 1) / p.G;
   x.L = L;
-  x.hi = min(max(L + t_last, 0), p.Tmax - 1);  // out-of-range L is reported by the scan
+  x.hi = p.ring ? max(L + t_last, 0) : min(max(L + t_last, 0), p.Tmax - 1);  // bad L: the scan reports
   x.lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
   x.kb = (min(x.lo, x.hi) / TK) * TK;
   x.n = (x.hi - x.kb) / TK + 1;
@@ -151,7 +152,7 @@ __device__ void locate_start(const AttnParams& p, int* ctl) {
     if (e < p.n_entries) {
       const int L = p.cache_seqlens[e / p.nqb];
       const Entry x = make_entry<ROWS, TK>(p, e, L);
-      if (L < 0 || L + (x.r1 - 1) / p.G >= p.Tmax) record_error(kErrPositionBeyondCache);
+      if (L < 0 || (!p.ring && L + (x.r1 - 1) / p.G >= p.Tmax)) record_error(kErrPositionBeyondCache);
       total += x.n;
     }
   }
@@ -272,13 +273,14 @@ __global__ void __launch_bounds__(kAttnThreads)
             return;
           mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
           const int key0 = w.ent.kb + (w.local + i) * TK;
+          const int slot0 = p.ring ? key0 % p.Tmax : key0;  // a ring slot: Tmax % TK == 0
           uint8_t* kdst = smem + s * C::STAGE_BYTES;
           uint8_t* vdst = kdst + C::TILE_BYTES;
 #pragma unroll
           for (int pn = 0; pn < C::NPANEL; ++pn) {
-            tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, w.kvh, key0,
+            tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, w.kvh, slot0,
                         w.ent.b, policy);
-            tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, w.kvh, key0,
+            tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, w.kvh, slot0,
                         w.ent.b, policy);
           }
         }

@@ -30,6 +30,7 @@ struct SplitAttnParams {
   float scale_log2;  // softmax_scale * log2(e)
   int nsplit, tiles_per_split, nqb;
   int cluster;       // the nsplit (<= 8) CTAs of a row group form a cluster and merge in DSMEM
+  int ring;          // the slot is a ring of Tmax positions (key c at index c % Tmax)
 };
 
 
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int t_last = (r1 - 1) / p.G;
   const int L = p.cache_seqlens[b];
   int hi = L + t_last;
-  if (hi >= p.Tmax || L < 0) {
+  if ((!p.ring && hi >= p.Tmax) || L < 0) {
     if (threadIdx.x == 0) record_error(kErrPositionBeyondCache);
     hi = min(max(hi, 0), p.Tmax - 1);
   }
@@ -145,13 +146,14 @@ __global__ void __launch_bounds__(kAttnThreads)
           waited = true;
         }
         mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+        const int slot0 = p.ring ? key0 % p.Tmax : key0;  // a ring slot: Tmax % TK == 0
         uint8_t* kdst = smem + s * C::STAGE_BYTES;
         uint8_t* vdst = kdst + C::TILE_BYTES;
 #pragma unroll
         for (int pn = 0; pn < C::NPANEL; ++pn) {
-          tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
+          tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
                       policy);
-          tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, key0, b,
+          tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
                       policy);
         }
       }

@@ -44,6 +44,7 @@ struct AppendParams {
   int nk;     // key vectors per (b, t): Hkv when writing kv, else 0
   bool rotate_k;
   long long total_vectors;
+  int ring;   // the slot is a ring of Tmax positions: position p at index p % Tmax
 };
 
 constexpr int kAppendWarpsPerBlock = 4;
@@ -66,12 +67,13 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
   // Value heads: a plain copy into the cache.
   if (j >= p.nq + p.nk) {
     const int h = j - p.nq - p.nk;
-    if (pos < 0 || pos >= p.Tmax) {
+    if (pos < 0 || (!p.ring && pos >= p.Tmax)) {
       if (lane == 0) record_error(kErrPositionBeyondCache);
       return;
     }
     const uint16_t* src = p.v + b * p.vs[0] + t * p.vs[1] + h * p.vs[2];
-    uint16_t* dst = p.v_cache + ((static_cast<long long>(b) * p.Tmax + pos) * p.Hkv + h) * p.D;
+    const int idx = p.ring ? pos % p.Tmax : pos;
+    uint16_t* dst = p.v_cache + ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + h) * p.D;
     for (int d = lane; d < p.D; d += 32) dst[d] = src[d];
     return;
   }
@@ -84,11 +86,11 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
   if (is_q) {
     dst = p.q_out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.D;
   } else {
-    if (pos < 0 || pos >= p.Tmax) {
+    if (pos < 0 || (!p.ring && pos >= p.Tmax)) {
       if (lane == 0) record_error(kErrPositionBeyondCache);
       return;
     }
-    dst = p.k_cache + ((static_cast<long long>(b) * p.Tmax + pos) * p.Hkv + h) * p.D;
+    dst = p.k_cache + ((static_cast<long long>(b) * p.Tmax + (p.ring ? pos % p.Tmax : pos)) * p.Hkv + h) * p.D;
   }
 
   if (!is_q && !p.rotate_k) {  // raw key insert
@@ -193,11 +195,12 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
   if (is_q) {
     dst = p.q_out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D;
   } else {
-    if (pos < 0 || pos >= p.Tmax) {
+    if (pos < 0 || (!p.ring && pos >= p.Tmax)) {
       if (active && sub == 0) record_error(kErrPositionBeyondCache);
       ok = false;
     } else {
-      dst = (is_v ? p.v_cache : p.k_cache) + ((static_cast<long long>(b) * p.Tmax + pos) * p.Hkv + h) * D;
+      dst = (is_v ? p.v_cache : p.k_cache) +
+            ((static_cast<long long>(b) * p.Tmax + (p.ring ? pos % p.Tmax : pos)) * p.Hkv + h) * D;
     }
   }
   const bool rotate = is_q || (!is_v && p.rotate_k);

@@ -273,6 +273,11 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
   if (a->D != 16 && a->D != 32 && a->D != 64 && a->D != 128 && a->D != 256)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: head_dim %d not supported (16/32/64/128/256)",
                 a->D);
+  if (a->ring && (a->window < 0 || static_cast<long long>(a->window) + a->T > a->Tmax ||
+                  a->Tmax % 128 != 0))
+    return fail(MCB_ERR_INVALID_ARG,
+                "mcb_decode_attn: a ring slot needs window >= 0, window + T <= Tmax and Tmax a "
+                "multiple of 128 (window=%d T=%d Tmax=%d)", a->window, a->T, a->Tmax);
   const int G = a->Hq / a->Hkv;
   pl->D = a->D;
   if (a->num_ctas == 0 && a->T >= kPrefillMinT && (a->D == 64 || a->D == 128)) {
@@ -428,6 +433,7 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
   p.Tmax = a->Tmax;
   p.window = a->window;
   p.n_qpairs = (a->T + 2 * mcb::kPfTile - 1) / (2 * mcb::kPfTile);
+  p.ring = a->ring != 0;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   const long long grid = static_cast<long long>(p.n_qpairs) * a->B * a->Hq;
   if (a->D == 64) return PrefillVariant<64>::launch(grid, qm, km, vm, p, st);
@@ -453,6 +459,7 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.part_o = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w) : nullptr;
     p.part_lse = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
     p.cluster = pl.cluster ? 1 : 0;
+    p.ring = a->ring != 0;
     p.B = a->B;
     p.T = a->T;
     p.Hq = a->Hq;
@@ -485,6 +492,7 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   p.nqb = pl.nqb;
   p.n_entries = a->B * pl.nqb;
+  p.ring = a->ring != 0;
   p.grid = pl.grid;
   p.ngroups = pl.grid / a->Hkv;
   return variant_launch(a->D, pl.nqt, pl.grid, km, vm, p, st);
@@ -631,6 +639,7 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   p.nq = rq ? a->Hq : 0;
   p.nk = wkv ? a->Hkv : 0;
   p.rotate_k = rk;
+  p.ring = a->ring != 0;
   p.total_vectors = static_cast<long long>(a->B) * a->T * (p.nq + 2 * p.nk);
   if (p.total_vectors == 0) return MCB_OK;
   // 16-byte chunks when every row the kernel touches starts on a 16-byte boundary.

@@ -224,6 +224,7 @@ struct PrefillParams {
   int B, T, Hq, Hkv, G, Tmax, window;
   int n_qpairs;               // ceil(T / 256)
   float scale_log2;           // softmax_scale * log2(e)
+  int ring;                   // the slot is a ring of Tmax positions (key c at index c % Tmax)
 };
 
 template <int D>
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int L = p.cache_seqlens[b];
   const int q0 = qp * 2 * kPfTile;
   const int pos_last = L + min(q0 + 2 * kPfTile, p.T) - 1;
-  const bool in_range = L >= 0 && pos_last < p.Tmax;
+  const bool in_range = L >= 0 && (p.ring || pos_last < p.Tmax);
   const int k_first =
       (p.window >= 0 ? max(0, L + q0 - p.window) : 0) / kPfTile * kPfTile;
   QTileRange rng[2];
@@ -326,16 +327,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int st = j & 1;
       if (j >= 2 && !mbar_wait_or_abort(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag)) break;
       const int k0 = k_first + j * kPfTile;
+      const int slot0 = p.ring ? k0 % p.Tmax : k0;  // a ring slot: Tmax % 128 == 0
       mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
 #pragma unroll
       for (int pn = 0; pn < Cfg::kPanels; ++pn)
         tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &kmap,
-                    &k_full[st], pn * 64, hk, k0, b, pol);
+                    &k_full[st], pn * 64, hk, slot0, b, pol);
       mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
 #pragma unroll
       for (int pn = 0; pn < Cfg::kPanels; ++pn)
         tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &vmap,
-                    &v_full[st], pn * 64, hk, k0, b, pol);
+                    &v_full[st], pn * 64, hk, slot0, b, pol);
       issued = j + 1;
     }
     // on an abort, wait (bounded) for the copies still in flight before the CTA can exit

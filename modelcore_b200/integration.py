@@ -60,7 +60,11 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
     else:
         q = self.c_q(x).view(B, T, self.n_head, self.head_dim)
     k_cache, v_cache = kv_cache.get_slot_cache(self.kv_slot)
+    ring = kv_cache.slot_ring(self.kv_slot)
     seqlens = kv_cache.cache_seqlens
+    if ring and not fused:
+        raise RuntimeError("a window-ring KV cache needs modelcore's RotaryEmbedding + RMSNorm "
+                           "attention (the fused append); build the cache without rings")
     if fused:
         rope = self.rope
         kv_cache.check_room(T, rope.cos.size(1))
@@ -71,12 +75,12 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
             v = self._hook("values", v, x, idx)
             q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
                                    rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
-                                   scale=1.2)
+                                   scale=1.2, ring=ring)
         else:
             q = ops.kv_append_rope(q, None, None, None, None, seqlens, rope.cos, rope.sin,
                                    rotate_q=True, rotate_k=False, write_kv=False,
                                    eps=self.norm.eps, scale=1.2)
-        y = ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window)
+        y = ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window, ring=ring)
     else:
         kv_cache.check_room(T)
         if self.produces_kv:
@@ -139,8 +143,35 @@ def _manager_base():
     return RefManager
 
 
+RING_CHUNK = 512  # tokens one forward may append to a window ring (longer inputs are chunked)
+
+
+def ring_config(model, seq_len):
+    """The window rings new_kv_cache builds with ring_window on: the slots whose every layer has
+    a sliding window, one capacity for all of them (the largest window plus RING_CHUNK, rounded up
+    to 128 positions), or none when that is not below seq_len.  Returns (slots, capacity, window)."""
+    windows = {}
+    for i, spec in enumerate(model.layer_specs()):
+        if not hasattr(spec, "window") or not hasattr(spec, "kv_slot"):
+            continue  # not an attention layer
+        slot = i if spec.kv_slot is None else spec.kv_slot
+        windows.setdefault(slot, []).append(spec.window)
+    ring = sorted(s for s, ws in windows.items() if all(w is not None and w >= 0 for w in ws))
+    if not ring:
+        return (), 0, None
+    wmax = max(max(windows[s]) for s in ring)
+    cap = (wmax + RING_CHUNK + 127) // 128 * 128
+    if cap >= seq_len:
+        return (), 0, None
+    return tuple(ring), cap, wmax
+
+
 class _ManagerMixin:
     fuse_step = True  # install(model, fuse_step) for the models this manager returns
+    # new_kv_cache keeps the slots of sliding-window layers as window rings (see ring_config):
+    # cache memory in proportion to the window instead of the sequence length.  Off by default:
+    # it needs the fused decode forward (chunked prefill) and is a layout modelcore does not have.
+    ring_window = False
 
     def create_model(self, *args, **kwargs):
         model = super().create_model(*args, **kwargs)
@@ -160,8 +191,11 @@ class _ManagerMixin:
         if device.type != "cuda":
             return super().new_kv_cache(model, batch_size=batch_size, seq_len=seq_len, device=device)
         spec = kv_cache_spec(model.layer_specs())
+        ring_slots, cap, wmax = ring_config(model, seq_len) if self.ring_window else ((), 0, None)
+        if ring_slots and not step.decode_installed(model):
+            raise RuntimeError("window rings need the fused decode forward (install with fuse_step)")
         return KVCache(batch_size=batch_size, seq_len=seq_len, device=device, dtype=torch.bfloat16,
-                       **spec)
+                       ring_slots=ring_slots, ring_capacity=cap, ring_window=wmax, **spec)
 
     def new_decoder(self, model, tokens, *, num_samples=1, max_tokens=None, device=None,
                     cuda_graph=False, batched_prefill=True):
@@ -257,9 +291,7 @@ class GraphDecoder:
         target.set_row_lengths(lens)
         if S > 1:
             for i, n in enumerate(lens):
-                ops.kv_copy_rows(cache.k_cache, cache.v_cache, target.k_cache, target.v_cache,
-                                 src_row=i, dst_row_begin=i * S, dst_row_count=S, n_pos=n,
-                                 dst_seqlens=cache.cache_seqlens)
+                cache._copy_slots_from(target, i * S, S, n, src_row=i)
             cache.set_row_lengths([n for n in lens for _ in range(S)])
             logits = logits.repeat_interleave(S, dim=0)
         return cache, logits

@@ -62,7 +62,7 @@ def rms_norm_eps(eps):
 
 
 def kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, rotate_q=True,
-                   rotate_k=True, write_kv=True, eps=None, scale=1.2, q_out=None):
+                   rotate_k=True, write_kv=True, eps=None, scale=1.2, q_out=None, ring=False):
     """Fused rope + QK-norm + scale for q (and k), and the insert of k, v at each row's position.
 
     q: (B, T, Hq, D) bf16 or None; k, v: (B, T, Hkv, D) bf16 or None; k_cache/v_cache: one slot
@@ -127,6 +127,7 @@ def kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, rotate
     args.eps = rms_norm_eps(eps)
     args.scale = scale
     args.flags = flags
+    args.ring = int(bool(ring))
     check(_native.load().mcb_kv_append_rope(ctypes.byref(args), _stream(ref)))
     return q_out
 
@@ -174,7 +175,7 @@ def kv_advance(cache_seqlens, n):
                                         cache_seqlens.numel(), int(n), _stream(cache_seqlens)))
 
 
-def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out):
+def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring=False):
     _need("q", q, 4)
     B, T, Hq, D = q.shape
     Hkv = k_cache.shape[2] if k_cache.dim() == 4 else -1
@@ -195,17 +196,20 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ct
     args.window = -1 if window is None or window < 0 else int(window)
     args.softmax_scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
     args.num_ctas = int(num_ctas)
+    args.ring = int(bool(ring))
     return args
 
 
-def decode_attn_counter_count(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0):
+def decode_attn_counter_count(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0,
+                              ring=False):
     """Arrival counters the launch plan needs (0: the split plan, which uses none)."""
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None, ring)
     return int(_native.load().mcb_decode_attn_counter_count(ctypes.byref(args)))
 
 
-def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0):
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None)
+def decode_attn_workspace_bytes(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0,
+                                ring=False):
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None, ring)
     return int(_native.load().mcb_decode_attn_workspace_size(ctypes.byref(args)))
 
 
@@ -243,7 +247,7 @@ def reset_counters():
 
 
 def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
-                num_ctas=0, out=None, workspace=None, counters=None):
+                num_ctas=0, out=None, workspace=None, counters=None, ring=False):
     """softmax(q . K^T * scale) . V over each row's visible keys of one cache slot.
 
     q: (B, T, Hq, D) bf16; k_cache/v_cache: (B, T_max, Hkv, D) bf16 slot; query t of row b sits at
@@ -252,14 +256,16 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     of that many CTAs dividing all key tiles; < 0 one CTA per row group and key split, -num_ctas
     splits (every plan gives the same result up to fp32 summation order).  workspace: uint8
     partials buffer; counters: int32 arrival counters, zero before their first use (defaults:
-    the cached per-device ones).  Returns out (B, T, Hq, D) bf16."""
+    the cached per-device ones).  ring: the slot is a ring of T_max positions (key c at index
+    c % T_max; needs window >= 0 and window + T <= T_max, T_max a multiple of 128).  Returns out
+    (B, T, Hq, D) bf16."""
     if out is None:
         out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
     else:
         _need("out", out, 4)
         if out.shape != q.shape or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous tensor shaped like q")
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring)
     lib = _native.load()
     need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
     ncount = int(lib.mcb_decode_attn_counter_count(ctypes.byref(args)))
@@ -281,7 +287,8 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     return out
 
 
-def prefill_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None, out=None):
+def prefill_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None, out=None,
+                 ring=False):
     """decode_attn's semantics on the tensor-core prefill kernel (mcb_prefill_attn), for any T:
     128-query tiles, S = Q K^T and O += P V as tcgen05 MMAs with TMEM accumulators.  head_dim 64
     or 128.  decode_attn picks this plan itself for T >= 64 with num_ctas=0."""
@@ -291,7 +298,7 @@ def prefill_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale
         _need("out", out, 4)
         if out.shape != q.shape or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous tensor shaped like q")
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, 0, out)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, 0, out, ring)
     check(_native.load().mcb_prefill_attn(ctypes.byref(args), _stream(q)))
     return out
 

@@ -224,6 +224,24 @@ def _model_call_ok(model, idx, kv_cache):
     return _call_ok(model.body, probe, kv_cache)
 
 
+def _hidden(model, idx, kv_cache):
+    """Embedding, every block and the cache advance: the (B*T, C) final normed hidden states."""
+    B, T = idx.shape
+    emb = model.embedding
+    x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
+    C = x.size(-1)
+    _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
+    kv_cache.advance(T)
+    return h
+
+
+def _lm_head(model, h, argmax_out=None, want_logits=True):
+    un = model.unembedding
+    logits = F.linear(h, un.lm_head.weight)
+    return ops.softcap_argmax(logits, un.vocab_size, un.softcap, argmax_out=argmax_out,
+                              want_logits=want_logits)
+
+
 def decode_forward(model, idx, kv_cache, argmax_out=None, want_logits=True, last_positions=None):
     """Model.forward (modelcore/model.py:93-101) with kv_cache and without targets, for a model
     whose body qualifies for stack_forward and whose embedding (TokenEmbedding without smear) and
@@ -233,20 +251,36 @@ def decode_forward(model, idx, kv_cache, argmax_out=None, want_logits=True, last
     argmax_out, the greedy pick.  Returns the fp32 logits (B, T, vocab_size) (None when
     want_logits is False).  With last_positions (B,) the LM head runs only on row b's position
     last_positions[b] and the logits are (B, 1, vocab_size): a batched prefill needs the next-token
-    logits of each prompt's last token, not the (B, T, vocab) block."""
+    logits of each prompt's last token, not the (B, T, vocab) block.
+
+    A cache with window rings takes at most kv_cache.step_limit new tokens a forward (every key a
+    query can see must still be in its ring): longer inputs run as consecutive chunks, which is
+    the same computation -- each chunk's queries read the earlier chunks' keys from the cache."""
     B, T = idx.shape
-    emb, un = model.embedding, model.unembedding
-    x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
-    C = x.size(-1)
-    _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
-    kv_cache.advance(T)
+    vocab = model.unembedding.vocab_size
+    limit = getattr(kv_cache, "step_limit", None)
+    if limit is not None and T > limit:
+        assert argmax_out is None, "the greedy pick is for single-step forwards"
+        if last_positions is None:
+            return torch.cat([decode_forward(model, idx[:, a:a + limit], kv_cache)
+                              for a in range(0, T, limit)], dim=1)
+        h_last = None
+        for a in range(0, T, limit):
+            chunk = idx[:, a:a + limit]
+            h = _hidden(model, chunk, kv_cache).view(B, chunk.size(1), -1)
+            if h_last is None:
+                h_last = torch.empty((B, h.size(-1)), dtype=h.dtype, device=h.device)
+            rel = (last_positions - a).clamp(0, chunk.size(1) - 1)
+            take = (last_positions >= a) & (last_positions < a + chunk.size(1))
+            picked = h[torch.arange(B, device=h.device), rel]
+            h_last = torch.where(take[:, None], picked, h_last)
+        return _lm_head(model, h_last).view(B, 1, vocab)
+    h = _hidden(model, idx, kv_cache)
     if last_positions is not None:
-        h = h.view(B, T, C)[torch.arange(B, device=h.device), last_positions]
+        h = h.view(B, T, -1)[torch.arange(B, device=h.device), last_positions]
         T = 1
-    logits = F.linear(h, un.lm_head.weight)
-    out = ops.softcap_argmax(logits, un.vocab_size, un.softcap, argmax_out=argmax_out,
-                             want_logits=want_logits)
-    return out.view(B, T, un.vocab_size) if want_logits else None
+    out = _lm_head(model, h, argmax_out, want_logits)
+    return out.view(B, T, vocab) if want_logits else None
 
 
 def model_forward(self, idx, targets=None, kv_cache=None, loss_reduction='mean', doc_args=None):

@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 2
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 3
 
 
 def test_every_declared_symbol_is_exported():
@@ -215,3 +215,15 @@ def test_sampler_validates_on_the_host():
     assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_UNSUPPORTED
     a.top_k, a.rows = 50, 0
     assert lib.mcb_sample(ctypes.byref(a), None) == 0
+
+
+def test_ring_slots_are_validated_on_the_host():
+    """A ring slot must hold every visible key: window >= 0, window + T <= Tmax, Tmax a multiple
+    of 128 (so no 64- or 128-key tile wraps)."""
+    lib = _native.load()
+    for kw in (dict(window=-1, Tmax=1024), dict(window=1000, T=30, Tmax=1024),
+               dict(window=100, Tmax=1000)):
+        a = _attn(**kw)
+        a.ring = 1
+        st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+        assert st == _native.MCB_ERR_INVALID_ARG and "ring" in msg

@@ -46,7 +46,7 @@ CPU_SAMPLE_ROWS = 8
 FALLBACK_HBM_GBS = 6650.0
 # From the ncu capture of the split decode-attention kernel on config 2 (profiles/decode_attn_cfg2.md):
 NCU_READ_BYTES_PER_TILE_D64 = 16402   # 113.37 MB read / 6,912 fetched tiles
-NCU_WRITE_BYTES_CFG2 = 3_600_000       # mean of the two captured launches
+NCU_WRITE_BYTES_CFG2 = 3_500_000       # mean of the two captured launches
 METRIC = "decode tokens/sec + KV-read HBM GB/s (% of peak) at 1/2/4/8 B200"
 
 
@@ -257,7 +257,8 @@ def _attention_roofline(dec, peak, reps=4):
     tiles = int(sum((L + 1 + 63) // 64 for L in lens)) * H
     traffic = tiles * NCU_READ_BYTES_PER_TILE_D64 + NCU_WRITE_BYTES_CFG2
     ncount = ops.decode_attn_counter_count(q, cache.k_cache[0], cache.v_cache[0], cache.cache_seqlens)
-    kernel = ("mcb::decode_attn_split_kernel<64,1,16,4>" if ncount == 0 else
+    # config 2's 768 split CTAs run the 2-stage copy (all resident in one wave)
+    kernel = ("mcb::decode_attn_split_kernel<64,1,16,2>" if ncount == 0 else
               "mcb::decode_attn_kernel<64,1,16,3>")
     return {"bytes_per_launch": bytes_per_launch, "us_per_launch": us, "achieved_gbs": gbs,
             "frac": gbs / peak, "mean_context": keys / B, "traffic": traffic, "kernel": kernel}

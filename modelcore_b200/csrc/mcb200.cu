@@ -145,10 +145,44 @@ struct AttnVariant {
   static constexpr int STAGES = D <= 32 ? 8 : (D == 64 ? 3 : (D == 128 ? 4 : 2));
   using Cfg = mcb::AttnConfig<D, NQT, kKPW, STAGES>;
   static constexpr auto kernel = mcb::decode_attn_kernel<D, NQT, kKPW, STAGES>;
-  // Split kernel: 3-4 stages, 2-3 CTAs per SM.
+  // Split kernel: 3-4 stages, 2-3 CTAs per SM; and a 2-stage copy with about twice the CTAs
+  // per SM, used when it makes the whole grid resident at once while the deep one would need a
+  // second, partly empty wave (config 2: 768 CTAs, 3 vs 6 per SM -> 0.85 vs 0.91 of the copy
+  // bandwidth at 819 keys a row).
   static constexpr int SPLIT_STAGES = D >= 128 ? 3 : 4;
   using SplitCfg = mcb::SplitAttnConfig<D, NQT, kKPW, SPLIT_STAGES>;
   static constexpr auto split_kernel = mcb::decode_attn_split_kernel<D, NQT, kKPW, SPLIT_STAGES>;
+  using SplitCfgLo = mcb::SplitAttnConfig<D, NQT, kKPW, 2>;
+  static constexpr auto split_kernel_lo = mcb::decode_attn_split_kernel<D, NQT, kKPW, 2>;
+
+  // Resident split CTAs on the whole device for the deep (lo = false) or 2-stage kernel; also
+  // raises the kernel's shared-memory limit.  Cached per device.
+  static int split_slots(bool lo, long long* out) {
+    static std::atomic<uint64_t> done_hi{0}, done_lo{0};
+    static std::mutex mu;
+    static long long cache[2][64] = {{0}};
+    cudaError_t e = lo ? ensure_smem(split_kernel_lo, SplitCfgLo::SMEM_BYTES, done_lo)
+                       : ensure_smem(split_kernel, SplitCfg::SMEM_BYTES, done_hi);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn_split)");
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && cache[lo][dev] > 0) {
+      *out = cache[lo][dev];
+      return MCB_OK;
+    }
+    int n = 0;
+    e = lo ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_kernel_lo, mcb::kAttnThreads,
+                                                           SplitCfgLo::SMEM_BYTES)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_kernel, mcb::kAttnThreads,
+                                                           SplitCfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    const long long slots = static_cast<long long>(n) * device_sm_count();
+    if (dev >= 0 && dev < 64) cache[lo][dev] = slots;
+    *out = slots;
+    return MCB_OK;
+  }
 
   // Raises the persistent kernel's shared-memory limit on the current device (once) and returns
   // how many of its CTAs stay resident per SM.
@@ -189,15 +223,19 @@ struct AttnVariant {
 
   static int launch_split(long long grid, const CUtensorMap& km, const CUtensorMap& vm,
                           const mcb::SplitAttnParams& prm, cudaStream_t st) {
-    static std::atomic<uint64_t> done{0};
-    cudaError_t e = ensure_smem(split_kernel, SplitCfg::SMEM_BYTES, done);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn_split)");
+    long long hi_slots = 0, lo_slots = 0;
+    int rc = split_slots(false, &hi_slots);
+    if (rc != MCB_OK) return rc;
+    rc = split_slots(true, &lo_slots);
+    if (rc != MCB_OK) return rc;
+    const bool lo = grid > hi_slots && grid <= lo_slots;
+    cudaError_t e;
     // programmatic stream serialization: the K/V tiles of earlier steps stream in while the
     // append kernel ahead finishes (the kernel waits for it before q and the new keys)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(mcb::kAttnThreads);
-    cfg.dynamicSmemBytes = SplitCfg::SMEM_BYTES;
+    cfg.dynamicSmemBytes = lo ? SplitCfgLo::SMEM_BYTES : SplitCfg::SMEM_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -211,7 +249,8 @@ struct AttnVariant {
       cfg.numAttrs = 2;
     }
     cfg.attrs = attrs;
-    e = cudaLaunchKernelEx(&cfg, split_kernel, km, vm, prm);
+    e = lo ? cudaLaunchKernelEx(&cfg, split_kernel_lo, km, vm, prm)
+           : cudaLaunchKernelEx(&cfg, split_kernel, km, vm, prm);
     g_launches++;
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();

@@ -367,3 +367,23 @@ def test_attention_at_config5_size(mcb, window):
     y2 = ops.decode_attn(q, kc, vc * 2, sl, window=window)
     assert torch.equal(y2.float(), 2 * y.float())
     no_device_error(ops)
+
+
+def test_attention_at_config2_size_single_wave_kernel(mcb):
+    """Config 2's step shape (64 rows x 12 kv heads of 64: 768 split CTAs) runs the 2-stage split
+    kernel whose grid is resident in one wave; it matches the fp32 reference and the persistent
+    plan."""
+    _, ops = mcb
+    B, Hq, Hkv, D, Tmax = 64, 12, 12, 64, 1024
+    g = torch.Generator(device="cuda").manual_seed(21)
+    kc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(B, 1, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
+    lens = torch.randint(500, 1000, (B,), device="cuda", generator=g, dtype=torch.int32)
+    y = ops.decode_attn(q, kc, vc, lens)
+    y_p = ops.decode_attn(q, kc, vc, lens, num_ctas=296)
+    torch.cuda.synchronize()
+    no_device_error(ops)
+    ref = _torch_fp32_reference(q, kc, vc, lens.tolist(), -1)
+    assert (y.float() - ref).abs().max().item() <= ATTN_TOL
+    assert (y.float() - y_p.float()).abs().max().item() <= 2e-3

@@ -23,7 +23,7 @@ LOGIT_TOL = 2e-2
 def env():
     if not have_modelcore():
         raise RuntimeError("modelcore (the reference package) is not importable: install it into "
-                           "baseline/_ref (see DESIGN.md) to run the end-to-end parity tests")
+                           "baseline/_ref (__graft_entry__.build() does) to run the end-to-end parity tests")
     import modelcore
     import modelcore_b200
     return modelcore, modelcore_b200

@@ -864,9 +864,33 @@ int mcb_softcap_argmax(const mcb_softcap_args* a, void* stream) {
   p.inv_cap = a->softcap > 0.f ? 1.0f / a->softcap : 0.f;
   p.vec = a->V % 8 == 0 && aligned(a->logits, 16) && a->logits_stride % 8 == 0 &&
           (a->out == nullptr || (aligned(a->out, 16) && a->out_stride % 4 == 0));
-  launch_pdl(mcb::softcap_argmax_kernel, dim3(a->rows), dim3(512), 0, static_cast<cudaStream_t>(stream), p);
+  // Split a row over a cluster when the rows alone leave SMs idle: up to 8 CTAs a row, each with
+  // at least one chunk (or element) per thread.
+  const int units = p.vec ? p.V / 8 : p.V;
+  int cs = 1;
+  if (a->rows < 2 * device_sm_count()) {
+    cs = (units + mcb::kSoftcapThreads - 1) / mcb::kSoftcapThreads;
+    cs = cs < 1 ? 1 : (cs > 8 ? 8 : cs);
+  }
+  if (static_cast<long long>(a->rows) * cs > 0x7fffffffll)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_softcap_argmax: %d rows is too many", a->rows);
+  p.cs = cs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a->rows * cs));
+  cfg.blockDim = dim3(mcb::kSoftcapThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;
+  attrs[1].val.clusterDim.x = static_cast<unsigned>(cs);
+  attrs[1].val.clusterDim.y = 1;
+  attrs[1].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = cs > 1 ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, mcb::softcap_argmax_kernel, p);
   g_launches++;
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "softcap_argmax launch");
   return MCB_OK;
 }

@@ -222,7 +222,10 @@ struct SoftcapParams {
   float cap;               // > 0: cap * tanh(x * inv_cap); otherwise x
   float inv_cap;           // 1 / cap in fp32
   int vec;                 // rows 16-byte aligned and V % 8 == 0: 16-byte loads, 32-byte stores
+  int cs;                  // CTAs per row: one thread-block cluster of cs CTAs (1: no cluster)
 };
+
+constexpr int kSoftcapThreads = 256;
 
 // torch evaluates `logits / cap` with a Python-number cap as logits * (1 / cap) on CUDA (the
 // reciprocal rounded to fp32 once), then tanh, then `cap * t`.
@@ -239,20 +242,36 @@ __device__ __forceinline__ bool argmax_better(float a, int ia, float b, int ib) 
   return ia < ib;
 }
 
+__device__ __forceinline__ void argmax_warp(float& best, int& bi) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+    if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
+  }
+}
+
 // LMHead's epilogue, modelcore/components/unembedding.py:52-56 (crop to V, .float(), softcap),
 // fused with the greedy pick of sample_next_token(temperature=0), modelcore/generate.py:23-24.
-// One CTA per row.
-__global__ void __launch_bounds__(512) softcap_argmax_kernel(const SoftcapParams p) {
+// A row is split over the cs CTAs of one cluster (cs consecutive blocks of the grid), each taking
+// a contiguous range of 16-byte chunks (or elements); the per-CTA picks meet in rank 0 through
+// distributed shared memory.  The pick does not depend on the split: argmax_better is a total
+// order on (value, index).
+__global__ void __launch_bounds__(kSoftcapThreads) softcap_argmax_kernel(const SoftcapParams p) {
   pdl_launch_dependents();
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
-  const int row = blockIdx.x;
+  const int row = blockIdx.x / p.cs;
+  const int part = blockIdx.x % p.cs;
   const uint16_t* in = p.logits + static_cast<long long>(row) * p.ls;
   float* out = p.out ? p.out + static_cast<long long>(row) * p.os : nullptr;
   float best = -INFINITY;
   int bi = 0x7fffffff;
+  const int units = p.vec ? p.V / 8 : p.V;
+  const int per = (units + p.cs - 1) / p.cs;
+  const int u0 = part * per;
+  const int u1 = min(units, u0 + per);
   if (p.vec) {
-    const int nchunk = p.V / 8;
-    for (int c = threadIdx.x; c < nchunk; c += blockDim.x) {
+    for (int c = u0 + threadIdx.x; c < u1; c += kSoftcapThreads) {
       const uint4 w = *reinterpret_cast<const uint4*>(in + 8 * c);
       const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
       float y[8];
@@ -271,36 +290,44 @@ __global__ void __launch_bounds__(512) softcap_argmax_kernel(const SoftcapParams
       }
     }
   } else {
-    for (int j = threadIdx.x; j < p.V; j += blockDim.x) {
+    for (int j = u0 + threadIdx.x; j < u1; j += kSoftcapThreads) {
       const float y = softcap_value(bf16_bits_to_float(in[j]), p.cap, p.inv_cap);
       if (argmax_better(y, j, best, bi)) { best = y; bi = j; }
       if (out) out[j] = y;
     }
   }
-  if (!p.argmax) return;
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, m);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-    if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
-  }
-  __shared__ float sb[16];
-  __shared__ int si[16];
+  if (!p.argmax) return;  // uniform over the grid: no CTA of a cluster waits below
+  argmax_warp(best, bi);
+  constexpr int kWarps = kSoftcapThreads / 32;
+  __shared__ float sb[kWarps];
+  __shared__ int si[kWarps];
+  __shared__ float cb;  // this CTA's pick, read by rank 0 of the cluster
+  __shared__ int ci;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) { sb[warp] = best; si[warp] = bi; }
   __syncthreads();
   if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    best = lane < nw ? sb[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, m);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-      if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
+    best = lane < kWarps ? sb[lane] : -INFINITY;
+    bi = lane < kWarps ? si[lane] : 0x7fffffff;
+    argmax_warp(best, bi);
+    if (lane == 0) { cb = best; ci = bi; }
+  }
+  if (p.cs == 1) {
+    if (threadIdx.x == 0) p.argmax[static_cast<long long>(row) * p.as] = ci;
+    return;
+  }
+  cluster_sync();  // every CTA's pick is in its shared memory
+  if (part == 0 && warp == 0) {
+    best = -INFINITY;
+    bi = 0x7fffffff;
+    if (lane < p.cs) {
+      best = ld_dsmem_f32(map_to_rank(&cb, lane));
+      bi = __float_as_int(ld_dsmem_f32(map_to_rank(&ci, lane)));
     }
+    argmax_warp(best, bi);
     if (lane == 0) p.argmax[static_cast<long long>(row) * p.as] = bi;
   }
+  cluster_sync();  // rank 0 has read every CTA's shared memory before any of them exits
 }
 
 }  // namespace mcb

@@ -171,6 +171,30 @@ def test_softcap_argmax_is_bit_exact_against_torch(ops, rows, Vp, V, cap):
     assert torch.equal(only[:, 0], ids)
 
 
+@pytest.mark.parametrize("rows,V", [(1, 50257), (2, 32768), (300, 4096), (40, 7)])
+def test_softcap_argmax_rows_split_over_a_cluster(ops, rows, V):
+    """Rows split over up to 8 CTAs (fewer than 296 rows) or one CTA each: ties across the split
+    go to the first index, a NaN anywhere wins, an all -inf row picks index 0."""
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + V)
+    lg = (torch.randn(rows, V, device="cuda", generator=g) * 20).to(torch.bfloat16)
+    lg[0, V - 1] = lg[0, V // 3] = 300.0      # equal maxima in different CTAs of the row
+    if rows > 1:
+        lg[1, V - 2] = float("nan")
+        lg[1, 1] = 300.0
+    if rows > 2:
+        lg[rows - 1] = float("-inf")
+    ids = torch.empty(rows, dtype=torch.int64, device="cuda")
+    out = ops.softcap_argmax(lg, V, 15.0, argmax_out=ids)
+    want = _softcap_torch(lg, V, 15.0)
+    assert torch.equal(out.nan_to_num(7.0), want.nan_to_num(7.0))
+    assert torch.equal(ids, torch.argmax(want, dim=-1))
+    assert ids[0].item() == V // 3
+    if rows > 1:
+        assert ids[1].item() == V - 2
+    if rows > 2:
+        assert ids[rows - 1].item() == 0
+
+
 def test_softcap_argmax_against_the_reference_lm_head(ops):
     z = load_golden("step_fused.npz")
     lg = dev_bf16(z["head_logits_bf16"])

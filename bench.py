@@ -516,7 +516,7 @@ def run_b200(args):
     _ensure_modelcore()
     import modelcore_b200
     from modelcore_b200 import step as _step
-    _step.USE_MCB_LINEAR = args.linear == "mcb"
+    _step.USE_FUSED_PROJ = args.linear == "mcb"
     from modelcore_b200 import ops
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
@@ -611,8 +611,10 @@ def run_b200(args):
                                  "on libmcb200",
                         "plain": "modelcore's op-by-op forward around the libmcb200 append and "
                                  "attention"}[args.step],
-        "projections": {"mcb": "libmcb200 mcb_linear (tcgen05, weights prefetched under programmatic "
-                               "dependent launch)", "cublas": "torch F.linear (cuBLAS)"}[args.linear],
+        "projections": {"mcb": "libmcb200 mcb_linear (tcgen05, split-K over a cluster, weights "
+                               "prefetched under programmatic dependent launch, residual add + norm "
+                               "and silu * up fused into the operand load)",
+                        "cublas": "torch F.linear (cuBLAS)"}[args.linear],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
                     "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
                     "attention_kernel_gbs": round(roof["achieved_gbs"], 1),
@@ -650,7 +652,8 @@ def main():
     ap.add_argument("--step", choices=("fused", "plain"), default="fused",
                     help="decode step around attention: fused (default) or modelcore's op-by-op")
     ap.add_argument("--linear", choices=("mcb", "cublas"), default="cublas",
-                    help="decode projections: cuBLAS (default) or libmcb200's tcgen05 kernel")
+                    help="decode projections: cuBLAS with the add + norm and silu * up as "
+                         "libmcb200 kernels (default), or libmcb200's tcgen05 kernel with them fused in")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")

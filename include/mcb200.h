@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 3
+#define MCB_ABI_VERSION 4
 
 typedef enum {
   MCB_OK = 0,
@@ -295,20 +295,39 @@ typedef struct {
 
 int mcb_sample(const mcb_sample_args* args, void* stream);
 
-/* mcb_linear: Y = X W^T (F.linear without bias, modelcore/components/linear.py:14) for the decode
- * step's few rows: X (R, K), W (N, K) as nn.Linear stores it, Y (R, N), bf16, fp32 accumulation,
- * one rounding.  R <= 256, K a multiple of 64, x and w rows 16-byte aligned.  The weight tiles stream by
- * TMA into tcgen05 MMAs (128 output features per CTA, fp32 accumulators in TMEM); split > 1 cuts
- * K across a cluster of that many CTAs whose partial tiles are summed through distributed shared
- * memory (0: chosen from N and K).  With pdl != 0 the kernel is launched with programmatic
- * stream serialization: its weight loads start while the previous kernel in the stream finishes,
- * and it reads X only after that kernel completed (griddepcontrol.wait). */
+/* mcb_linear: Y = P(X) W^T (F.linear without bias, modelcore/components/linear.py:14) for the
+ * decode step's few rows, with the elementwise op in front of the projection fused into its
+ * operand load (`prologue`):
+ *   MCB_PROLOGUE_NONE        P(X) = x
+ *   MCB_PROLOGUE_ADD_NORM    x' = x + x2 (bf16), written to x_out; P = rms_norm(x') with eps, no
+ *                            weight (Block's residual add and next norm,
+ *                            modelcore/components/block.py:57-59, norm.py:43-44); x2 = NULL:
+ *                            P = rms_norm(x), x_out unused.  Same bits as mcb_add_rms_norm.
+ *   MCB_PROLOGUE_GATED_SILU  P = bf16(bf16(silu(x)) * x2), x the gate and x2 the up half
+ *                            (GatedMLP.forward, modelcore/components/mlp.py:89-90).  Same bits as
+ *                            mcb_gated_silu.
+ * X, x2, x_out (R, K), W (N, K) as nn.Linear stores it, Y (R, N), bf16, fp32 accumulation, one
+ * rounding.  R <= 128, K a multiple of 64, x / x2 / x_out / w rows 16-byte aligned; x_out must not
+ * overlap x or x2.  128 output features per CTA on tcgen05 MMAs (fp32 accumulators in TMEM), the
+ * CTA's weight panels issued by TMA before the operand; split > 1 cuts K across a cluster of
+ * that many CTAs (at most 16) whose partial tiles are summed through distributed shared memory in
+ * rank order (0: chosen from N and K).  With pdl != 0 the kernel is launched with programmatic
+ * stream serialization: its weight loads start while the previous kernel in the stream
+ * finishes; it reads the activations only after that kernel completed (griddepcontrol.wait). */
+#define MCB_PROLOGUE_NONE 0
+#define MCB_PROLOGUE_ADD_NORM 1
+#define MCB_PROLOGUE_GATED_SILU 2
+
 typedef struct {
-  const void* x;              /* (R, K) bf16                                                */
+  const void* x;              /* (R, K) bf16: X, the residual, or the gate                  */
+  const void* x2;             /* (R, K) bf16: delta (ADD_NORM, may be NULL), up (GATED_SILU) */
+  void* x_out;                /* (R, K) bf16: x + x2 (ADD_NORM with x2)                      */
   const void* w;              /* (N, K) bf16                                                */
   void* y;                    /* (R, N) bf16                                                */
-  int64_t x_stride, w_stride, y_stride;  /* row strides, elements                           */
+  int64_t x_stride, x2_stride, x_out_stride, w_stride, y_stride;  /* row strides, elements  */
   int32_t R, N, K;
+  int32_t prologue;           /* MCB_PROLOGUE_*                                             */
+  float eps;                  /* ADD_NORM                                                   */
   int32_t split;
   int32_t pdl;
 } mcb_linear_args;

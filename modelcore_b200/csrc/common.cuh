@@ -155,6 +155,28 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+// The two halves of cluster_sync, for a barrier whose wait can come later than its arrival.
+// Every thread of every CTA of the cluster executes each arrive and then its wait, in order.
+// The relaxed arrive orders no memory accesses: for a barrier that only says "has reached this
+// point" (mbarriers initialised -- fence.mbarrier_init publishes those --, or all incoming bulk
+// copies landed, which the mbarrier already observed).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory to shared memory of a CTA of the cluster (`dst`, `bar`: shared::cluster addresses from
+// map_to_rank); completion is counted as transaction bytes on that CTA's mbarrier `bar`.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes,
+                                                  uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
 // The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
   uint32_t out;

@@ -2,6 +2,7 @@
 // planning, TMA descriptor encoding and the kernel launches for the KV-cache decode path.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -17,7 +18,7 @@
 #include "kv_append.cuh"
 #include "kv_copy.cuh"
 #include "prefill_attn.cuh"
-#include "decode_gemm.cuh"
+#include "decode_proj.cuh"
 #include "sample.cuh"
 #include "step_fused.cuh"
 
@@ -557,7 +558,7 @@ static void launch_row_norm(int C, int rows, cudaStream_t st, F&& launch) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Decode projections (decode_gemm.cuh)
+// Decode projections (decode_proj.cuh)
 int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long long cols,
                     long long stride, int box_rows) {
   auto fn = encode_fn();
@@ -574,18 +575,37 @@ int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long lon
   return MCB_OK;
 }
 
-template <int RN, int STAGES>
-int launch_linear(const CUtensorMap& wm, const CUtensorMap& xm, const mcb::LinearParams& prm,
-                  int tiles, bool pdl, cudaStream_t st) {
-  using Cfg = mcb::LinearConfig<RN, STAGES>;
+// Panels a CTA may hold: the W panels (16 KB each), the activation panels (RN x 128 B) and the
+// cluster exchange buffers share the 227 KB of shared memory a CTA may use.
+int proj_max_panels(int RN) { return RN <= 64 ? 6 : 3; }
+constexpr int kMaxSmemOptin = 232448;
+
+template <int RN, int PRO>
+int launch_proj(const CUtensorMap& wm, const mcb::ProjParams& prm, int tiles, bool pdl, cudaStream_t st,
+                bool* cluster_unfit) {
+  const mcb::ProjSmem L = mcb::proj_smem(RN, prm.max_np, prm.split, prm.panels, PRO == mcb::kProAddNorm);
+  if (L.total > kMaxSmemOptin)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: %d bytes of shared memory (split %d, %d panels)", L.total,
+                prm.split, prm.max_np);
   static std::atomic<uint64_t> done{0};
-  auto kernel = mcb::linear_kernel<RN, STAGES>;
-  cudaError_t e = ensure_smem(kernel, Cfg::kSmem, done);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear)");
+  auto kernel = mcb::proj_kernel<RN, PRO>;
+  cudaError_t e = ensure_smem(kernel, kMaxSmemOptin, done);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(proj)");
+  static std::atomic<uint64_t> nonportable{0};
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(nonportable.load() & bit)) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(proj, non-portable clusters)");
+      nonportable.fetch_or(bit);
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(tiles * prm.split));
-  cfg.blockDim = dim3(mcb::kLinThreads);
-  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.blockDim = dim3(mcb::kProjThreads);
+  cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
   cudaLaunchAttribute attrs[2];
   int na = 0;
@@ -596,19 +616,47 @@ int launch_linear(const CUtensorMap& wm, const CUtensorMap& xm, const mcb::Linea
     attrs[na].val.clusterDim.z = 1;
     ++na;
   }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  if (prm.split > 8) {  // a cluster above the portable size must fit a GPC with this shared memory
+    int nclusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&nclusters, kernel, &cfg);
+    if (e != cudaSuccess || nclusters < 1) {
+      cudaGetLastError();
+      *cluster_unfit = true;
+      return MCB_OK;
+    }
+  }
   if (pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
-  cfg.attrs = attrs;
   cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kernel, wm, xm, prm);
+  e = cudaLaunchKernelEx(&cfg, kernel, wm, prm);
   g_launches++;
   if (e != cudaSuccess) return cuda_fail(e, "linear launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "linear launch");
   return MCB_OK;
+}
+
+template <int RN>
+int launch_proj_rn(int prologue, const CUtensorMap& wm, const mcb::ProjParams& prm, int tiles, bool pdl,
+                   cudaStream_t st, bool* unfit) {
+  switch (prologue) {
+    case MCB_PROLOGUE_ADD_NORM: return launch_proj<RN, mcb::kProAddNorm>(wm, prm, tiles, pdl, st, unfit);
+    case MCB_PROLOGUE_GATED_SILU: return launch_proj<RN, mcb::kProGatedSilu>(wm, prm, tiles, pdl, st, unfit);
+    default: return launch_proj<RN, mcb::kProNone>(wm, prm, tiles, pdl, st, unfit);
+  }
+}
+
+bool ranges_overlap(const void* a, long long a_stride, const void* b, long long b_stride, int rows, int cols) {
+  if (a == nullptr || b == nullptr || rows <= 0) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  const uintptr_t a1 = a0 + static_cast<uintptr_t>(((rows - 1) * a_stride + cols) * 2);
+  const uintptr_t b1 = b0 + static_cast<uintptr_t>(((rows - 1) * b_stride + cols) * 2);
+  return a0 < b1 && b0 < a1;
 }
 
 extern "C" {
@@ -928,54 +976,77 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: args is NULL");
   if (a->R < 0 || a->N <= 0 || a->K <= 0)
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: R=%d N=%d K=%d", a->R, a->N, a->K);
-  if (a->R > 256 || a->K % 64 != 0)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most 256), K=%d (a multiple of 64)", a->R,
+  if (a->prologue < MCB_PROLOGUE_NONE || a->prologue > MCB_PROLOGUE_GATED_SILU)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: prologue %d", a->prologue);
+  if (a->R > 128 || a->K % 64 != 0)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most 128), K=%d (a multiple of 64)", a->R,
                 a->K);
-  if (a->x == nullptr || a->w == nullptr || a->y == nullptr)
+  const bool norm = a->prologue == MCB_PROLOGUE_ADD_NORM, silu = a->prologue == MCB_PROLOGUE_GATED_SILU;
+  if (a->x == nullptr || a->w == nullptr || a->y == nullptr || (silu && a->x2 == nullptr) ||
+      (norm && a->x2 != nullptr && a->x_out == nullptr))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: NULL pointer argument");
-  if (a->x_stride < a->K || a->w_stride < a->K || a->y_stride < a->N)
+  if (a->x_stride < a->K || a->w_stride < a->K || a->y_stride < a->N ||
+      (a->x2 != nullptr && (norm || silu) && a->x2_stride < a->K) ||
+      (norm && a->x2 != nullptr && a->x_out_stride < a->K))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: row strides shorter than the rows");
-  if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->y, 2) || a->x_stride % 8 ||
-      a->w_stride % 8)
-    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x and w rows must start on 16-byte boundaries");
-  if (a->split < 0 || a->split > 8)
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d (0..8)", a->split);
-  if (a->R == 0) return MCB_OK;
-  const int tiles = (a->N + mcb::kLinTile - 1) / mcb::kLinTile;
-  const int steps = a->K / 64;
-  const int RN = a->R <= 32 ? 32 : (a->R <= 64 ? 64 : (a->R <= 128 ? 128 : 256));
-  const int stages = RN <= 64 ? 8 : (RN == 128 ? 6 : 4);
+  const bool use_x2 = (norm || silu) && a->x2 != nullptr, use_out = norm && a->x2 != nullptr;
+  if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->y, 2) || a->x_stride % 8 || a->w_stride % 8 ||
+      (use_x2 && (!aligned(a->x2, 16) || a->x2_stride % 8)) ||
+      (use_out && (!aligned(a->x_out, 16) || a->x_out_stride % 8)))
+    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x, x2, x_out and w rows must start on 16-byte boundaries");
+  if (use_out && (ranges_overlap(a->x_out, a->x_out_stride, a->x, a->x_stride, a->R, a->K) ||
+                  ranges_overlap(a->x_out, a->x_out_stride, a->x2, a->x2_stride, a->R, a->K)))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: x_out overlaps x or x2 (other CTAs still read them)");
+  const int panels = a->K / 64;
+  const int tiles = (a->N + mcb::kProjFeat - 1) / mcb::kProjFeat;
+  const int RN = a->R <= 64 ? 64 : 128;
+  const int maxp = proj_max_panels(RN);
+  const int smax = std::min(panels, mcb::kProjMaxSplit);
+  const int smin = (panels + maxp - 1) / maxp;
+  if (a->split < 0 || a->split > mcb::kProjMaxSplit)
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d (0..%d)", a->split, mcb::kProjMaxSplit);
+  if (smin > smax)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d needs more than %d CTAs of %d panels", a->K,
+                mcb::kProjMaxSplit, maxp);
   int split = a->split;
   if (split == 0) {
-    // the fewest CTAs per output tile whose weight slices fit the ring: every W load is issued
-    // before griddepcontrol.wait, i.e. under the kernel ahead
-    split = 1;
-    while (split < 8 && (steps % split != 0 || steps / split > stages)) ++split;
-    if (steps % split != 0) split = 1;
-  } else if (steps % split != 0) {
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d does not divide %d K panels", split, steps);
+    // about one CTA per SM: the fewest K panels per CTA that the SM count allows
+    const int want = (device_sm_count() + tiles - 1) / tiles;
+    split = std::max(smin, std::min(want, smax));
+  } else if (split > smax || split < smin) {
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d outside %d..%d for K=%d", split, smin, smax, a->K);
   }
-  CUtensorMap wm, xm;
-  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, mcb::kLinTile);
+  if (a->R == 0) return MCB_OK;
+  CUtensorMap wm;
+  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, mcb::kProjFeat);
   if (rc != MCB_OK) return rc;
-  rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, RN);
-  if (rc != MCB_OK) return rc;
-  mcb::LinearParams p;
+  mcb::ProjParams p;
+  p.a = static_cast<const uint16_t*>(a->x);
+  p.b = use_x2 ? static_cast<const uint16_t*>(a->x2) : nullptr;
+  p.a_out = use_out ? static_cast<uint16_t*>(a->x_out) : nullptr;
   p.y = static_cast<uint16_t*>(a->y);
+  p.as = a->x_stride;
+  p.bs = use_x2 ? a->x2_stride : 0;
+  p.aos = use_out ? a->x_out_stride : 0;
   p.ys = a->y_stride;
   p.R = a->R;
   p.N = a->N;
   p.K = a->K;
-  p.split = split;
-  p.steps_per_cta = steps / split;
+  p.panels = panels;
   p.vec_out = aligned(a->y, 16) && a->y_stride % 8 == 0 && a->N % 8 == 0;
+  p.eps = a->eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
-  switch (RN) {
-    case 32: return launch_linear<32, 8>(wm, xm, p, tiles, pdl, st);
-    case 64: return launch_linear<64, 8>(wm, xm, p, tiles, pdl, st);
-    case 128: return launch_linear<128, 6>(wm, xm, p, tiles, pdl, st);
-    default: return launch_linear<256, 4>(wm, xm, p, tiles, pdl, st);
+  while (true) {
+    p.split = split;
+    p.max_np = (panels + split - 1) / split;
+    bool unfit = false;
+    rc = RN == 64 ? launch_proj_rn<64>(a->prologue, wm, p, tiles, pdl, st, &unfit)
+                  : launch_proj_rn<128>(a->prologue, wm, p, tiles, pdl, st, &unfit);
+    if (rc != MCB_OK || !unfit) return rc;
+    if (split <= 8 || smin > 8)  // cannot shrink to a portable cluster
+      return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: no cluster of %d CTAs fits this device", split);
+    split = std::max(smin, 8);
   }
 }
 

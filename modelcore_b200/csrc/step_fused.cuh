@@ -12,9 +12,9 @@
 //                                                            and greedy sample_next_token)
 //
 // Rounding follows torch's ops: the add is computed in fp32 and rounded once; rms_norm
-// accumulates the sum of squares in fp32, in this file's fixed order (lane l adds the squares of
-// its 16-byte chunks c = l, l+32, .. in order, element by element, then an xor butterfly over
-// masks 16 .. 1), and rounds once; silu is computed in fp32 as g / (1 + exp(-g)) and rounded, the
+// accumulates the sum of squares in fp32 in one fixed order (row_rms_rsqrt: within 8-element
+// chunks, a pairwise tree over the 8 chunks of each 64-column panel, then the panels in order),
+// and rounds once; silu is computed in fp32 as g / (1 + exp(-g)) and rounded, the
 // product in fp32 and rounded; the softcap multiplies by the fp32 reciprocal of the cap (as torch's
 // CUDA division by a Python number does), then tanhf, then an fp32 multiply.  The
 // CPU oracle restates the same order.
@@ -71,21 +71,35 @@ __device__ __forceinline__ void store_row_chunks(uint16_t* row, int lane, int nc
   }
 }
 
-// rsqrt(mean(v^2) + eps) of the warp's row: each lane sums the squares of its chunks in order
-// (u ascending, element by element), then an xor butterfly 16 .. 1 adds the lanes' sums.
+// rsqrt(mean(v^2) + eps) of the warp's row.  The fp32 sum of squares has one fixed order, shared
+// with mcb_linear's fused norm (decode_proj.cuh), which holds a row as 64-column panels spread
+// over the CTAs of a cluster: squares added element by element within each 8-element chunk
+// (chunk c = lane + 32u), a pairwise tree over the 8 chunks of each 64-column panel (lanes 8g ..
+// 8g + 7: xor shuffles 1, 2, 4), then the panels in order, from 0.
 template <int CPL>
 __device__ __forceinline__ float row_rms_rsqrt(const float (&v)[CPL][8], int lane, int nchunk,
                                                int C, float eps) {
-  float acc = 0.f;
+  float s[CPL];
 #pragma unroll
   for (int u = 0; u < CPL; ++u) {
+    s[u] = 0.f;
     if (lane + 32 * u < nchunk) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[u][i], v[u][i]));
+      for (int i = 0; i < 8; ++i) s[u] = __fadd_rn(s[u], __fmul_rn(v[u][i], v[u][i]));
     }
+    s[u] = __fadd_rn(s[u], __shfl_xor_sync(0xffffffffu, s[u], 1));
+    s[u] = __fadd_rn(s[u], __shfl_xor_sync(0xffffffffu, s[u], 2));
+    s[u] = __fadd_rn(s[u], __shfl_xor_sync(0xffffffffu, s[u], 4));
   }
+  const int npanel = (nchunk + 7) / 8;
+  float acc = 0.f;
 #pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  for (int u = 0; u < CPL; ++u)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float t = __shfl_sync(0xffffffffu, s[u], 8 * g);  // panel 4u + g
+      if (4 * u + g < npanel) acc = __fadd_rn(acc, t);
+    }
   return __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(C)), eps));
 }
 

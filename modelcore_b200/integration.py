@@ -37,6 +37,28 @@ def _fusable(attn, x):
             and attn.head_dim % 2 == 0 and attn.head_dim <= 256)
 
 
+def attend(self, q, k, v, kv_cache):
+    """The fused KV-cache branch of Attention.forward (modelcore/components/attention.py:144-178)
+    from projected (B, T, H, D) q, k, v (k and v None for a consumer layer, produces_kv=False):
+    one kernel does rope + RMSNorm + x1.2 for q and k and writes k, v into the layer's slot at each
+    row's position, then the decode attention over the slot.  Returns y (B, T, Hq, D)."""
+    T = q.size(1)
+    k_cache, v_cache = kv_cache.get_slot_cache(self.kv_slot)
+    ring = kv_cache.slot_ring(self.kv_slot)
+    seqlens = kv_cache.cache_seqlens
+    rope = self.rope
+    kv_cache.check_room(T, rope.cos.size(1))
+    if self.produces_kv:
+        q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
+                               rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
+                               scale=1.2, ring=ring)
+    else:
+        q = ops.kv_append_rope(q, None, None, None, None, seqlens, rope.cos, rope.sin,
+                               rotate_q=True, rotate_k=False, write_kv=False,
+                               eps=self.norm.eps, scale=1.2)
+    return ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window, ring=ring)
+
+
 def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
     """modelcore Attention.forward (modelcore/components/attention.py:135-184) with the KV-cache
     branch on libmcb200.  Same projections, hooks (`values` after c_v, `output` before c_proj),
@@ -66,21 +88,14 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
         raise RuntimeError("a window-ring KV cache needs modelcore's RotaryEmbedding + RMSNorm "
                            "attention (the fused append); build the cache without rings")
     if fused:
-        rope = self.rope
-        kv_cache.check_room(T, rope.cos.size(1))
         if self.produces_kv:
             if qkv is None:
                 k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
                 v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
             v = self._hook("values", v, x, idx)
-            q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
-                                   rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
-                                   scale=1.2, ring=ring)
         else:
-            q = ops.kv_append_rope(q, None, None, None, None, seqlens, rope.cos, rope.sin,
-                                   rotate_q=True, rotate_k=False, write_kv=False,
-                                   eps=self.norm.eps, scale=1.2)
-        y = ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window, ring=ring)
+            k = v = None
+        y = attend(self, q, k, v, kv_cache)
     else:
         kv_cache.check_room(T)
         if self.produces_kv:
@@ -101,8 +116,6 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
                                         window_size=(self.window, 0))
     y = self._hook("output", y, x)
     y = y.contiguous().view(B, T, -1)
-    if getattr(self, _FUSE_QKV, False) and self.c_proj.weight.dtype == y.dtype:
-        return step.project(y.view(B * T, -1), self.c_proj.weight).view(B, T, -1)
     return self.c_proj(y)
 
 

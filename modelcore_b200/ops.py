@@ -13,7 +13,8 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      LinearArgs, SampleArgs, SoftcapArgs, check)
+                      LinearArgs, PROLOGUE_ADD_NORM, PROLOGUE_GATED_SILU, PROLOGUE_NONE,
+                      SampleArgs, SoftcapArgs, check)
 
 
 def _stream(t):
@@ -449,28 +450,69 @@ def sample(logits, uniforms, *, temperature=1.0, top_k=None, out=None):
     return out
 
 
-LINEAR_MAX_ROWS = 256
+LINEAR_MAX_ROWS = 128
 
 
-def linear(x, weight, *, out=None, split=0, pdl=False):
-    """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
-    rows: x (R, K) with R <= 256, weight (N, K), bf16, fp32 accumulation on tcgen05.  split: K cut
-    across a cluster of that many CTAs (0: chosen).  pdl: launch with programmatic stream
-    serialization (the weight stream overlaps the previous kernel).  Returns out (R, N)."""
-    R, K = x.shape
+def _linear_call(args, x, weight, out, R, K, split, pdl):
     N = weight.shape[0]
     if weight.shape[1] != K:
         raise RuntimeError(f"weight must be (N, {K}), got {tuple(weight.shape)}")
     if out is None:
         out = torch.empty((R, N), dtype=torch.bfloat16, device=x.device)
-    args = LinearArgs()
-    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
     args.w, args.w_stride = weight.data_ptr(), _rows2d("weight", weight)
     args.y, args.y_stride = out.data_ptr(), _rows2d("out", out)
     args.R, args.N, args.K = R, N, K
     args.split, args.pdl = split, int(bool(pdl))
     check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))
     return out
+
+
+def linear(x, weight, *, out=None, split=0, pdl=False):
+    """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
+    rows: x (R, K) with R <= 128 and K a multiple of 64, weight (N, K), bf16, fp32 accumulation on
+    tcgen05.  split: K cut across a cluster of that many CTAs (0: chosen).  pdl: launch with
+    programmatic stream serialization (the weight stream overlaps the previous kernel).  Returns
+    out (R, N)."""
+    R, K = x.shape
+    args = LinearArgs()
+    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
+    args.prologue = PROLOGUE_NONE
+    return _linear_call(args, x, weight, out, R, K, split, pdl)
+
+
+def add_norm_linear(x, delta, weight, *, eps=None, x_out=None, out=None, split=0, pdl=False):
+    """Block's residual add and the next norm fused in front of a projection
+    (modelcore/components/block.py:57-59, norm.py:43-44, linear.py:14): x' = bf16(x + delta),
+    h = rms_norm(x', eps), returns (x', h @ weight^T); delta None: h = rms_norm(x), returns
+    (x, h @ weight^T).  h has the bits of add_rms_norm's; x_out must not overlap x or delta."""
+    R, K = x.shape
+    args = LinearArgs()
+    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
+    args.prologue = PROLOGUE_ADD_NORM
+    args.eps = rms_norm_eps(eps)
+    if delta is not None:
+        if tuple(delta.shape) != (R, K):
+            raise RuntimeError("x and delta must have equal shapes")
+        if x_out is None:
+            x_out = torch.empty_like(x)
+        args.x2, args.x2_stride = delta.data_ptr(), _rows2d("delta", delta)
+        args.x_out, args.x_out_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
+    y = _linear_call(args, x, weight, out, R, K, split, pdl)
+    return (x_out if delta is not None else x), y
+
+
+def silu_linear(gate, up, weight, *, out=None, split=0, pdl=False):
+    """GatedMLP's act(gate) * up (activation "silu", modelcore/components/mlp.py:89-90) fused in
+    front of down_proj: returns (bf16(bf16(silu(gate)) * up)) @ weight^T, the product's bits those
+    of gated_silu."""
+    R, K = gate.shape
+    if tuple(up.shape) != (R, K):
+        raise RuntimeError("gate and up must have equal shapes")
+    args = LinearArgs()
+    args.x, args.x_stride = gate.data_ptr(), _rows2d("gate", gate)
+    args.x2, args.x2_stride = up.data_ptr(), _rows2d("up", up)
+    args.prologue = PROLOGUE_GATED_SILU
+    return _linear_call(args, gate, weight, out, R, K, split, pdl)
 
 
 def gated_silu(gate, up, out=None):

@@ -93,20 +93,13 @@ def packed_weight(owner, key, linears):
     return view
 
 
-# With USE_MCB_LINEAR the decode step's projections run on libmcb200's tcgen05 kernel
-# (mcb_linear: weight tiles streamed under programmatic dependent launch, split-K over a cluster)
-# for up to 256 rows.  Off by default: at 64 rows it measures 6-8 us a projection against
-# cuBLAS's 3-4 us in the same CUDA graph (config 2: 84.4k vs 99.0k tokens/s), so F.linear
-# (cuBLAS) stays the projection path; the kernel is kept, tested, for the fusions it allows.
-USE_MCB_LINEAR = False
-
-
-def project(x2d, weight):
-    """F.linear(x2d, weight) without bias for a (rows, K) activation block."""
-    if (USE_MCB_LINEAR and x2d.size(0) <= ops.LINEAR_MAX_ROWS and x2d.size(1) % 64 == 0
-            and x2d.is_contiguous()):
-        return ops.linear(x2d, weight, pdl=True)
-    return F.linear(x2d, weight)
+# With USE_FUSED_PROJ a decode step of at most ops.LINEAR_MAX_ROWS rows runs its projections on
+# libmcb200's mcb_linear, with the elementwise op in front of each fused into the projection's
+# operand load (body_forward_proj: 6 launches a layer instead of 9).  Off by default: at 64 rows
+# the split-K cluster kernel measures 6.9-7.7 us a projection in a CUDA graph against cuBLAS's
+# 3.3-5.4 us, more than the 7 us a layer the fused add + norm and silu save (config 2: 58k vs
+# 101k tokens/s with the first version); prefill-sized blocks always use cuBLAS (F.linear).
+USE_FUSED_PROJ = False
 
 
 def qkv_projection(attn, x):
@@ -117,7 +110,7 @@ def qkv_projection(attn, x):
         return None
     B, T, _ = x.shape
     w = packed_weight(attn, "qkv", (attn.c_q, attn.c_k, attn.c_v))
-    qkv = project(x.reshape(B * T, x.size(-1)), w).view(B, T, -1)
+    qkv = F.linear(x.reshape(B * T, x.size(-1)), w).view(B, T, -1)
     nq = attn.n_head * attn.head_dim
     nk = attn.n_kv_head * attn.head_dim
     q = qkv[..., :nq].view(B, T, attn.n_head, attn.head_dim)
@@ -130,9 +123,9 @@ def gated_mlp(ffn, h):
     """GatedMLP.forward (modelcore/components/mlp.py:89-90) for activation "silu" on (rows, C):
     one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj."""
     w = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
-    gu = project(h, w)
+    gu = F.linear(h, w)
     H = ffn.hidden_dim
-    return project(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
+    return F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
 
 
 def _structure_ok(body):
@@ -184,6 +177,73 @@ def body_forward(body, x2, h, idx, kv_cache, B, T):
     return resid, h
 
 
+def _proj_ok(body, rows, x):
+    """The fused-projection body applies: at most LINEAR_MAX_ROWS rows, every block's attention
+    on the fused append (modelcore's RMSNorm QK-norm and RotaryEmbedding), every projection's K a
+    multiple of 64."""
+    from .integration import _fusable
+    if not USE_FUSED_PROJ or not 0 < rows <= ops.LINEAR_MAX_ROWS or x.size(-1) % 64:
+        return False
+    for b in body.blocks:
+        a = b.mixer
+        if not _fusable(a, x) or (a.n_head * a.head_dim) % 64 or b.ffn.hidden_dim % 64:
+            return False
+        if a.c_q.weight.dtype != x.dtype:
+            return False
+    return True
+
+
+def body_forward_proj(body, x2, kv_cache, B, T):
+    """body_forward for a decode step's few rows with every projection on mcb_linear:
+
+        per block:  x, qkv = x + delta, norm(x + delta) @ [Wq; Wk; Wv]^T   (block 0: norm(x))
+                    append + attention                                      (integration.attend)
+                    o = attn @ Wo^T
+                    x, gu = x + o, norm(x + o) @ [Wg; Wu]^T
+                    delta = (silu(gu[:, :H]) * gu[:, H:]) @ Wd^T
+        then x + delta and its norm (mcb_add_rms_norm).
+
+    6 launches a layer, each projection launched with programmatic dependent launch so its
+    weight stream overlaps the kernel ahead.  The residual alternates between two buffers: a
+    fused add writes x + delta while other CTAs of the same launch still read x.  The operand
+    bits equal body_forward's (h and silu * up are bit-exact); the products differ from cuBLAS's
+    in fp32 summation order only.  Returns the final residual and its norm (rows, C)."""
+    from .integration import attend
+    rows, C = x2.shape
+    bufs = (torch.empty_like(x2), torch.empty_like(x2))
+    nxt = 0
+    src, delta = x2, None
+    for block in body.blocks:
+        attn, ffn, eps = block.mixer, block.ffn, block.norm.eps
+        if attn.produces_kv:
+            w = packed_weight(attn, "qkv", (attn.c_q, attn.c_k, attn.c_v))
+        else:
+            w = attn.c_q.weight
+        if delta is None:
+            _, qkv = ops.add_norm_linear(src, None, w, eps=eps, pdl=True)
+        else:
+            src, qkv = ops.add_norm_linear(src, delta, w, eps=eps, x_out=bufs[nxt], pdl=True)
+            nxt ^= 1
+        hd = attn.head_dim
+        nq = attn.n_head * hd
+        q = qkv[:, :nq].view(B, T, attn.n_head, hd)
+        k = v = None
+        if attn.produces_kv:
+            nk = attn.n_kv_head * hd
+            k = qkv[:, nq:nq + nk].view(B, T, attn.n_kv_head, hd)
+            v = qkv[:, nq + nk:].view(B, T, attn.n_kv_head, hd)
+        y = attend(attn, q, k, v, kv_cache)
+        o = ops.linear(y.view(rows, nq), attn.c_proj.weight, pdl=True)
+        wgu = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
+        src, gu = ops.add_norm_linear(src, o, wgu, eps=eps, x_out=bufs[nxt], pdl=True)
+        nxt ^= 1
+        H = ffn.hidden_dim
+        delta = ops.silu_linear(gu[:, :H], gu[:, H:], ffn.down_proj.weight, pdl=True)
+    h = torch.empty_like(x2)
+    resid, _ = ops.add_rms_norm(src, delta, eps=body.blocks[-1].norm.eps, x_out=bufs[nxt], h_out=h)
+    return resid, h
+
+
 def stack_forward(self, x, idx, kv_cache, doc_args=None):
     """StackComposer.forward (modelcore/composers/stack.py:35-42) for the structure in the module
     docstring, with the residual add and the next norm fused and the projections packed."""
@@ -191,6 +251,8 @@ def stack_forward(self, x, idx, kv_cache, doc_args=None):
         return getattr(self, _ORIGINAL_FORWARD)(x, idx, kv_cache, doc_args)
     B, T, C = x.shape
     x2 = x.reshape(B * T, C)
+    if _proj_ok(self, B * T, x):
+        return body_forward_proj(self, x2, kv_cache, B, T)[0].view(B, T, C)
     h = torch.empty_like(x2)
     ops.add_rms_norm(x2, eps=self.blocks[0].norm.eps, h_out=h)
     resid, _ = body_forward(self, x2, h, idx, kv_cache, B, T)
@@ -228,9 +290,14 @@ def _hidden(model, idx, kv_cache):
     """Embedding, every block and the cache advance: the (B*T, C) final normed hidden states."""
     B, T = idx.shape
     emb = model.embedding
-    x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
-    C = x.size(-1)
-    _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
+    C = emb.wte.weight.size(1)
+    probe = emb.wte.weight[:0]
+    if _proj_ok(model.body, B * T, probe):
+        x, _ = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps, second_norm=False)
+        _, h = body_forward_proj(model.body, x.view(B * T, C), kv_cache, B, T)
+    else:
+        x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
+        _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
     kv_cache.advance(T)
     return h
 

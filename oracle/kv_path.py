@@ -136,19 +136,25 @@ def rope_tables_at(cos_bits, sin_bits, cache_seqlens, T):
 # The decode step either side of attention
 def _row_rms_norm(x, eps):
     """bf16-representable fp32 rows x (..., C) -> bf16(x * rsqrt(sum(x^2)/C + eps)) as fp32, the sum
-    in the step kernels' order: lane l adds its 8-element chunks l, l+32, .. element by element,
-    then an xor butterfly over the 32 lanes."""
+    in the step kernels' order (step_fused.cuh row_rms_rsqrt, decode_proj.cuh's fused norm): the
+    squares added element by element within each 8-element chunk, a pairwise tree over the 8
+    chunks of each 64-column panel ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)) (absent chunks of a short
+    last panel count 0), then the panels in order."""
     C = x.shape[-1]
-    acc = np.zeros(x.shape[:-1] + (32,), dtype=np.float32)
-    for lane in range(32):
-        for c in range(lane, C // 8, 32):
-            for i in range(8):
-                v = x[..., 8 * c + i]
-                acc[..., lane] = acc[..., lane] + v * v
-    for m in (16, 8, 4, 2, 1):
-        acc = acc + acc[..., np.arange(32) ^ m]
+    nchunk = C // 8
+    npanel = (nchunk + 7) // 8
+    s = np.zeros(x.shape[:-1] + (npanel * 8,), dtype=np.float32)
+    for c in range(nchunk):
+        for i in range(8):
+            v = x[..., 8 * c + i]
+            s[..., c] = s[..., c] + v * v
+    for m in (1, 2, 4):
+        s = s + s[..., np.arange(npanel * 8) ^ m]
+    acc = np.zeros(x.shape[:-1], dtype=np.float32)
+    for p in range(npanel):
+        acc = acc + s[..., 8 * p]
     e = F32(np.finfo(np.float32).eps if eps is None else eps)
-    v = ((acc[..., 0] / F32(C)).astype(np.float32) + e).astype(np.float32)
+    v = ((acc / F32(C)).astype(np.float32) + e).astype(np.float32)
     r = (np.longdouble(1.0) / np.sqrt(v.astype(np.longdouble))).astype(np.float32)
     return round_bf16((x * r[..., None]).astype(np.float32))
 

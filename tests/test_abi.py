@@ -11,7 +11,7 @@ import pytest
 from conftest import REPO
 from modelcore_b200 import _native
 from modelcore_b200._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs,
-                                    GatedSiluArgs, SampleArgs, SoftcapArgs)
+                                    GatedSiluArgs, LinearArgs, SampleArgs, SoftcapArgs)
 
 HEADER = os.path.join(REPO, "include", "mcb200.h")
 
@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 3
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_every_declared_symbol_is_exported():
@@ -53,7 +53,8 @@ def _c_layout(struct, fields):
 @pytest.mark.parametrize("cls,cname", [(AppendArgs, "mcb_append_args"), (CopyArgs, "mcb_copy_args"),
                                        (AttnArgs, "mcb_attn_args"), (AddNormArgs, "mcb_add_norm_args"),
                                        (GatedSiluArgs, "mcb_gated_silu_args"), (EmbedArgs, "mcb_embed_args"),
-                                       (SoftcapArgs, "mcb_softcap_args"), (SampleArgs, "mcb_sample_args")])
+                                       (SoftcapArgs, "mcb_softcap_args"), (SampleArgs, "mcb_sample_args"),
+                                       (LinearArgs, "mcb_linear_args")])
 def test_ctypes_structures_match_the_c_layout(cls, cname):
     fields = [f for f, _ in cls._fields_]
     c = _c_layout(cname, fields)
@@ -227,3 +228,42 @@ def test_ring_slots_are_validated_on_the_host():
         a.ring = 1
         st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
         assert st == _native.MCB_ERR_INVALID_ARG and "ring" in msg
+
+
+def test_linear_rejects_bad_arguments_on_the_host():
+    """Every case fails in the host checks, before any launch (the pointers are never read)."""
+    lib = _native.load()
+    base = 1 << 20
+
+    def args(**kw):
+        a = LinearArgs()
+        a.x, a.w, a.y = base, base + (1 << 16), base + (2 << 16)
+        a.x_stride = a.w_stride = a.y_stride = 768
+        a.R, a.N, a.K = 64, 768, 768
+        a.prologue = _native.PROLOGUE_NONE
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=3)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "prologue" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=96, x_stride=96, w_stride=96)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "multiple of 64" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(R=129)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "at most 128" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(split=17)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "split" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(split=13)), None))  # 12 panels
+    assert st == _native.MCB_ERR_INVALID_ARG and "split 13" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=_native.PROLOGUE_GATED_SILU)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(x=base + 8)), None))
+    assert st == _native.MCB_ERR_ALIGNMENT
+    # the fused residual must not overlap what other CTAs still read
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=_native.PROLOGUE_ADD_NORM, x2=base + (3 << 20),
+                                                    x2_stride=768, x_out=base + 64 * 768,
+                                                    x_out_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "overlaps" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=64 * 8 * 17, x_stride=64 * 8 * 17,
+                                                    w_stride=64 * 8 * 17)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED

@@ -289,12 +289,15 @@ def test_fused_step_decode_is_as_accurate_as_the_reference(env, name):
     assert e_fused <= 1.25 * e_ref + 1e-3
 
 
-def test_fused_step_launches_and_graph_replay(env):
+@pytest.mark.parametrize("fused_proj", [False, True])
+def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
     """One decode step of the fused 4-layer quickstart launches the libmcb200 kernels it should
-    (per layer: append, attention, two add+norm, silu*up; plus the first norm and the advance),
+    (per layer: the three fused projections, c_proj, append, attention; plus the embedding, the
+    last add + norm, the advance and the LM-head epilogue),
     and the CUDA-graph decoder reproduces the eager fused decoder bit for bit."""
     modelcore, mcb = env
-    from modelcore_b200 import ops, workloads
+    from modelcore_b200 import ops, step, workloads
+    monkeypatch.setattr(step, "USE_FUSED_PROJ", fused_proj)
     mgr = mcb.ModelManager()
     model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
                                               device=torch.device("cuda"), seed=0))
@@ -308,11 +311,14 @@ def test_fused_step_launches_and_graph_replay(env):
         n0 = ops.launch_count()
         eager.step(cols[0])
         per_step = ops.launch_count() - n0
-        # embedding + first norm, 4 per layer (+ 4 projections on mcb_linear), the advance,
-        # the LM-head epilogue
-        from modelcore_b200 import step
-        per_layer = 4 + (4 if step.USE_MCB_LINEAR else 0)
-        attn_launches = per_step - (1 + 4 * per_layer + 1 + 1)
+        if fused_proj:
+            # the embedding; per layer q|k|v (with add + norm), append, c_proj, gate|up (with
+            # add + norm), down (with silu * up); the last add + norm, the advance, the LM-head
+            # epilogue
+            attn_launches = per_step - (1 + 4 * 5 + 1 + 1 + 1)
+        else:
+            # embedding + first norm, 4 per layer, the advance, the LM-head epilogue
+            attn_launches = per_step - (1 + 4 * 4 + 1 + 1)
         assert attn_launches in (4, 8), per_step     # one or two (split + combine) per layer
         graph.step(cols[0])                           # eager: the graph decoder's first step
         for col in cols[1:]:                          # capture, then replays
@@ -392,19 +398,20 @@ def copy_with_plain_forward(env, model):
 
 
 def test_fused_step_on_mcb_linear_projections_is_as_accurate(env):
-    """The same bar with the decode projections on libmcb200's tcgen05 kernel (mcb_linear under
-    programmatic dependent launch) instead of cuBLAS."""
+    """The same bar with the decode projections on libmcb200's tcgen05 kernel with the residual
+    add + norm and silu * up fused into them (USE_FUSED_PROJ, body_forward_proj) instead of
+    cuBLAS and separate kernels."""
     from modelcore.tests.test_generate import RAGGED_PROMPTS
     from modelcore_b200 import step
     (rm, ref), (fm, fused), _, (m32, ref32) = _models(env, _configs()["quickstart"]())
     cols = torch.tensor([[(s * 7 + i * 3) % 100 + 1 for s in range(8)]
                          for i in range(len(RAGGED_PROMPTS))])
-    saved = step.USE_MCB_LINEAR
-    step.USE_MCB_LINEAR = True
+    saved = step.USE_FUSED_PROJ
+    step.USE_FUSED_PROJ = True
     try:
         l_fused = _forced(fm, fused, RAGGED_PROMPTS, cols)
     finally:
-        step.USE_MCB_LINEAR = saved
+        step.USE_FUSED_PROJ = saved
     l32 = _forced(m32, ref32, RAGGED_PROMPTS, cols)
     l_ref = _forced(rm, ref, RAGGED_PROMPTS, cols)
     e_ref = (l_ref - l32).abs().max().item()

@@ -611,9 +611,9 @@ def run_b200(args):
                                  "on libmcb200",
                         "plain": "modelcore's op-by-op forward around the libmcb200 append and "
                                  "attention"}[args.step],
-        "projections": {"mcb": "libmcb200 mcb_linear (tcgen05, split-K over a cluster, weights "
-                               "prefetched under programmatic dependent launch, residual add + norm "
-                               "and silu * up fused into the operand load)",
+        "projections": {"mcb": "libmcb200 mcb_linear (one CTA per 16-32 output features, mma.sync, "
+                               "weights prefetched under programmatic dependent launch, norms and "
+                               "residual adds fused in); down_proj on cuBLAS",
                         "cublas": "torch F.linear (cuBLAS)"}[args.linear],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
                     "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
@@ -652,8 +652,8 @@ def main():
     ap.add_argument("--step", choices=("fused", "plain"), default="fused",
                     help="decode step around attention: fused (default) or modelcore's op-by-op")
     ap.add_argument("--linear", choices=("mcb", "cublas"), default="cublas",
-                    help="decode projections: cuBLAS with the add + norm and silu * up as "
-                         "libmcb200 kernels (default), or libmcb200's tcgen05 kernel with them fused in")
+                    help="decode projections: cuBLAS with the add + norm as a libmcb200 kernel "
+                         "(default), or libmcb200's mcb_linear with the norms and adds fused in")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")

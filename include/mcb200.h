@@ -295,40 +295,35 @@ typedef struct {
 
 int mcb_sample(const mcb_sample_args* args, void* stream);
 
-/* mcb_linear: Y = P(X) W^T (F.linear without bias, modelcore/components/linear.py:14) for the
- * decode step's few rows, with the elementwise op in front of the projection fused into its
- * operand load (`prologue`):
- *   MCB_PROLOGUE_NONE        P(X) = x
- *   MCB_PROLOGUE_ADD_NORM    x' = x + x2 (bf16), written to x_out; P = rms_norm(x') with eps, no
- *                            weight (Block's residual add and next norm,
- *                            modelcore/components/block.py:57-59, norm.py:43-44); x2 = NULL:
- *                            P = rms_norm(x), x_out unused.  Same bits as mcb_add_rms_norm.
- *   MCB_PROLOGUE_GATED_SILU  P = bf16(bf16(silu(x)) * x2), x the gate and x2 the up half
- *                            (GatedMLP.forward, modelcore/components/mlp.py:89-90).  Same bits as
- *                            mcb_gated_silu.
- * X, x2, x_out (R, K), W (N, K) as nn.Linear stores it, Y (R, N), bf16, fp32 accumulation, one
- * rounding.  R <= 128, K a multiple of 64, x / x2 / x_out / w rows 16-byte aligned; x_out must not
- * overlap x or x2.  128 output features per CTA on tcgen05 MMAs (fp32 accumulators in TMEM), the
- * CTA's weight panels issued by TMA before the operand; split > 1 cuts K across a cluster of
- * that many CTAs (at most 16) whose partial tiles are summed through distributed shared memory in
- * rank order (0: chosen from N and K).  With pdl != 0 the kernel is launched with programmatic
- * stream serialization: its weight loads start while the previous kernel in the stream
- * finishes; it reads the activations only after that kernel completed (griddepcontrol.wait). */
-#define MCB_PROLOGUE_NONE 0
-#define MCB_PROLOGUE_ADD_NORM 1
-#define MCB_PROLOGUE_GATED_SILU 2
+/* mcb_linear: Y = X W^T (F.linear without bias, modelcore/components/linear.py:14) for the
+ * decode step's few rows, with the Block's elementwise ops around the projection fused in:
+ *   flags & MCB_LINEAR_NORM   Y = rms_norm(X, eps) W^T, the norm without weight
+ *                             (modelcore/components/norm.py:43-44) -- the bits of
+ *                             mcb_add_rms_norm's h; K <= 1024;
+ *   ... and delta != NULL     X' = bf16(X + delta) is written to x_out first and normed
+ *                             (the residual add of the previous block's MLP; K <= 768);
+ *   res != NULL               Y = bf16(res + bf16(X W^T)): the residual add after c_proj
+ *                             (modelcore/components/block.py:58); res may be Y (in place).
+ * X, delta, x_out (R, K), W (N, K) as nn.Linear stores it, Y and res (R, N), bf16, fp32
+ * accumulation.  R <= 64, K a multiple of 64, x / delta / x_out / w rows 16-byte aligned; Y, res
+ * and x_out must not overlap X or delta.  Every CTA takes 16 or 32 output features and all of K:
+ * its W slice and the activation panels arrive by TMA, warp-level tensor-core MMAs (mma.sync)
+ * split K over the CTA's warps.  With pdl != 0 the kernel is launched with programmatic stream
+ * serialization: the W slice is requested while the previous kernel in the stream finishes; the
+ * activations are read only after that kernel completed. */
+#define MCB_LINEAR_NORM 1
 
 typedef struct {
-  const void* x;              /* (R, K) bf16: X, the residual, or the gate                  */
-  const void* x2;             /* (R, K) bf16: delta (ADD_NORM, may be NULL), up (GATED_SILU) */
-  void* x_out;                /* (R, K) bf16: x + x2 (ADD_NORM with x2)                      */
+  const void* x;              /* (R, K) bf16                                                */
   const void* w;              /* (N, K) bf16                                                */
   void* y;                    /* (R, N) bf16                                                */
-  int64_t x_stride, x2_stride, x_out_stride, w_stride, y_stride;  /* row strides, elements  */
+  const void* res;            /* (R, N) bf16 residual, or NULL                              */
+  const void* delta;          /* (R, K) bf16 added to x before the norm, or NULL            */
+  void* x_out;                /* (R, K) bf16: x + delta (with delta)                        */
+  int64_t x_stride, w_stride, y_stride, res_stride, delta_stride, x_out_stride;  /* elements */
   int32_t R, N, K;
-  int32_t prologue;           /* MCB_PROLOGUE_*                                             */
-  float eps;                  /* ADD_NORM                                                   */
-  int32_t split;
+  int32_t flags;              /* MCB_LINEAR_NORM                                            */
+  float eps;                  /* the norm's eps                                             */
   int32_t pdl;
 } mcb_linear_args;
 

@@ -156,18 +156,18 @@ class SampleArgs(ctypes.Structure):
     ]
 
 
-PROLOGUE_NONE, PROLOGUE_ADD_NORM, PROLOGUE_GATED_SILU = 0, 1, 2
+LINEAR_NORM = 1
 
 
 class LinearArgs(ctypes.Structure):
     _fields_ = [
-        ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("x_out", ctypes.c_void_p),
-        ("w", ctypes.c_void_p), ("y", ctypes.c_void_p),
-        ("x_stride", ctypes.c_int64), ("x2_stride", ctypes.c_int64),
-        ("x_out_stride", ctypes.c_int64), ("w_stride", ctypes.c_int64), ("y_stride", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("res", ctypes.c_void_p), ("delta", ctypes.c_void_p), ("x_out", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64), ("w_stride", ctypes.c_int64), ("y_stride", ctypes.c_int64),
+        ("res_stride", ctypes.c_int64), ("delta_stride", ctypes.c_int64),
+        ("x_out_stride", ctypes.c_int64),
         ("R", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32),
-        ("prologue", ctypes.c_int32), ("eps", ctypes.c_float),
-        ("split", ctypes.c_int32), ("pdl", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("eps", ctypes.c_float), ("pdl", ctypes.c_int32),
     ]
 
 

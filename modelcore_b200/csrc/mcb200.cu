@@ -575,87 +575,46 @@ int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long lon
   return MCB_OK;
 }
 
-// Panels a CTA may hold: the W panels (16 KB each), the activation panels (RN x 128 B) and the
-// cluster exchange buffers share the 227 KB of shared memory a CTA may use.
-int proj_max_panels(int RN) { return RN <= 64 ? 6 : 3; }
 constexpr int kMaxSmemOptin = 232448;
 
-template <int RN, int PRO>
-int launch_proj(const CUtensorMap& wm, const mcb::ProjParams& prm, int tiles, bool pdl, cudaStream_t st,
-                bool* cluster_unfit) {
-  const mcb::ProjSmem L = mcb::proj_smem(RN, prm.max_np, prm.split, prm.panels, PRO == mcb::kProAddNorm);
-  if (L.total > kMaxSmemOptin)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: %d bytes of shared memory (split %d, %d panels)", L.total,
-                prm.split, prm.max_np);
+template <int F, bool NORM, bool ADD>
+int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& dm, const mcb::ProjParams& prm,
+                bool pdl, cudaStream_t st) {
   static std::atomic<uint64_t> done{0};
-  auto kernel = mcb::proj_kernel<RN, PRO>;
+  auto kernel = mcb::proj_kernel<F, NORM, ADD>;
   cudaError_t e = ensure_smem(kernel, kMaxSmemOptin, done);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(proj)");
-  static std::atomic<uint64_t> nonportable{0};
-  {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(nonportable.load() & bit)) {
-      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(proj, non-portable clusters)");
-      nonportable.fetch_or(bit);
-    }
-  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * prm.split));
+  cfg.gridDim = dim3(static_cast<unsigned>((prm.N + F - 1) / F));
   cfg.blockDim = dim3(mcb::kProjThreads);
-  cfg.dynamicSmemBytes = L.total;
+  cfg.dynamicSmemBytes = mcb::proj_smem_bytes(F, prm.panels, ADD);
   cfg.stream = st;
-  cudaLaunchAttribute attrs[2];
-  int na = 0;
-  if (prm.split > 1) {
-    attrs[na].id = cudaLaunchAttributeClusterDimension;
-    attrs[na].val.clusterDim.x = static_cast<unsigned>(prm.split);
-    attrs[na].val.clusterDim.y = 1;
-    attrs[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  cfg.attrs = attrs;
-  cfg.numAttrs = na;
-  if (prm.split > 8) {  // a cluster above the portable size must fit a GPC with this shared memory
-    int nclusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&nclusters, kernel, &cfg);
-    if (e != cudaSuccess || nclusters < 1) {
-      cudaGetLastError();
-      *cluster_unfit = true;
-      return MCB_OK;
-    }
-  }
-  if (pdl) {
-    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  cfg.numAttrs = na;
-  e = cudaLaunchKernelEx(&cfg, kernel, wm, prm);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kernel, wm, xm, dm, prm);
   g_launches++;
-  if (e != cudaSuccess) return cuda_fail(e, "linear launch");
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "linear launch");
   return MCB_OK;
 }
 
-template <int RN>
-int launch_proj_rn(int prologue, const CUtensorMap& wm, const mcb::ProjParams& prm, int tiles, bool pdl,
-                   cudaStream_t st, bool* unfit) {
-  switch (prologue) {
-    case MCB_PROLOGUE_ADD_NORM: return launch_proj<RN, mcb::kProAddNorm>(wm, prm, tiles, pdl, st, unfit);
-    case MCB_PROLOGUE_GATED_SILU: return launch_proj<RN, mcb::kProGatedSilu>(wm, prm, tiles, pdl, st, unfit);
-    default: return launch_proj<RN, mcb::kProNone>(wm, prm, tiles, pdl, st, unfit);
-  }
+template <int F>
+int launch_proj_f(bool norm, bool add, const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& dm,
+                  const mcb::ProjParams& prm, bool pdl, cudaStream_t st) {
+  if (add) return launch_proj<F, true, true>(wm, xm, dm, prm, pdl, st);
+  if (norm) return launch_proj<F, true, false>(wm, xm, dm, prm, pdl, st);
+  return launch_proj<F, false, false>(wm, xm, dm, prm, pdl, st);
 }
 
-bool ranges_overlap(const void* a, long long a_stride, const void* b, long long b_stride, int rows, int cols) {
+bool ranges_overlap(const void* a, long long a_stride, int a_cols, const void* b, long long b_stride,
+                    int b_cols, int rows) {
   if (a == nullptr || b == nullptr || rows <= 0) return false;
   const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
-  const uintptr_t a1 = a0 + static_cast<uintptr_t>(((rows - 1) * a_stride + cols) * 2);
-  const uintptr_t b1 = b0 + static_cast<uintptr_t>(((rows - 1) * b_stride + cols) * 2);
+  const uintptr_t a1 = a0 + static_cast<uintptr_t>(((rows - 1) * a_stride + a_cols) * 2);
+  const uintptr_t b1 = b0 + static_cast<uintptr_t>(((rows - 1) * b_stride + b_cols) * 2);
   return a0 < b1 && b0 < a1;
 }
 
@@ -976,78 +935,71 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: args is NULL");
   if (a->R < 0 || a->N <= 0 || a->K <= 0)
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: R=%d N=%d K=%d", a->R, a->N, a->K);
-  if (a->prologue < MCB_PROLOGUE_NONE || a->prologue > MCB_PROLOGUE_GATED_SILU)
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: prologue %d", a->prologue);
-  if (a->R > 128 || a->K % 64 != 0)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most 128), K=%d (a multiple of 64)", a->R,
-                a->K);
-  const bool norm = a->prologue == MCB_PROLOGUE_ADD_NORM, silu = a->prologue == MCB_PROLOGUE_GATED_SILU;
-  if (a->x == nullptr || a->w == nullptr || a->y == nullptr || (silu && a->x2 == nullptr) ||
-      (norm && a->x2 != nullptr && a->x_out == nullptr))
+  if (a->flags & ~MCB_LINEAR_NORM) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: flags %d", a->flags);
+  const bool norm = (a->flags & MCB_LINEAR_NORM) != 0;
+  const bool add = a->delta != nullptr;
+  if (add && !norm) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: delta needs MCB_LINEAR_NORM");
+  if (a->R > mcb::kProjRows || a->K % 64 != 0 || (norm && a->K > 32 * 8 * mcb::kProjNormCpl))
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most %d), K=%d (a multiple of 64%s)", a->R,
+                mcb::kProjRows, a->K, norm ? ", at most 1024 with the norm" : "");
+  if (a->x == nullptr || a->w == nullptr || a->y == nullptr || (add && a->x_out == nullptr))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: NULL pointer argument");
   if (a->x_stride < a->K || a->w_stride < a->K || a->y_stride < a->N ||
-      (a->x2 != nullptr && (norm || silu) && a->x2_stride < a->K) ||
-      (norm && a->x2 != nullptr && a->x_out_stride < a->K))
+      (a->res != nullptr && a->res_stride < a->N) ||
+      (add && (a->delta_stride < a->K || a->x_out_stride < a->K)))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: row strides shorter than the rows");
-  const bool use_x2 = (norm || silu) && a->x2 != nullptr, use_out = norm && a->x2 != nullptr;
   if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->y, 2) || a->x_stride % 8 || a->w_stride % 8 ||
-      (use_x2 && (!aligned(a->x2, 16) || a->x2_stride % 8)) ||
-      (use_out && (!aligned(a->x_out, 16) || a->x_out_stride % 8)))
-    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x, x2, x_out and w rows must start on 16-byte boundaries");
-  if (use_out && (ranges_overlap(a->x_out, a->x_out_stride, a->x, a->x_stride, a->R, a->K) ||
-                  ranges_overlap(a->x_out, a->x_out_stride, a->x2, a->x2_stride, a->R, a->K)))
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: x_out overlaps x or x2 (other CTAs still read them)");
+      (a->res != nullptr && !aligned(a->res, 2)) ||
+      (add && (!aligned(a->delta, 16) || !aligned(a->x_out, 16) || a->delta_stride % 8 || a->x_out_stride % 8)))
+    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x, delta, x_out and w rows must start on 16-byte boundaries");
+  // every CTA reads all of x (and delta) while others write y and x_out
+  if (ranges_overlap(a->y, a->y_stride, a->N, a->x, a->x_stride, a->K, a->R) ||
+      ranges_overlap(a->res, a->res_stride, a->N, a->x, a->x_stride, a->K, a->R) ||
+      (add && (ranges_overlap(a->x_out, a->x_out_stride, a->K, a->x, a->x_stride, a->K, a->R) ||
+               ranges_overlap(a->x_out, a->x_out_stride, a->K, a->delta, a->delta_stride, a->K, a->R) ||
+               ranges_overlap(a->y, a->y_stride, a->N, a->delta, a->delta_stride, a->K, a->R) ||
+               ranges_overlap(a->y, a->y_stride, a->N, a->x_out, a->x_out_stride, a->K, a->R))))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: y, res and x_out must not overlap x or delta");
+  if (a->res != nullptr && a->res != a->y &&
+      ranges_overlap(a->y, a->y_stride, a->N, a->res, a->res_stride, a->N, a->R))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: res must be y itself or not overlap it");
   const int panels = a->K / 64;
-  const int tiles = (a->N + mcb::kProjFeat - 1) / mcb::kProjFeat;
-  const int RN = a->R <= 64 ? 64 : 128;
-  const int maxp = proj_max_panels(RN);
-  const int smax = std::min(panels, mcb::kProjMaxSplit);
-  const int smin = (panels + maxp - 1) / maxp;
-  if (a->split < 0 || a->split > mcb::kProjMaxSplit)
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d (0..%d)", a->split, mcb::kProjMaxSplit);
-  if (smin > smax)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d needs more than %d CTAs of %d panels", a->K,
-                mcb::kProjMaxSplit, maxp);
-  int split = a->split;
-  if (split == 0) {
-    // about one CTA per SM: the fewest K panels per CTA that the SM count allows
-    const int want = (device_sm_count() + tiles - 1) / tiles;
-    split = std::max(smin, std::min(want, smax));
-  } else if (split > smax || split < smin) {
-    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: split %d outside %d..%d for K=%d", split, smin, smax, a->K);
-  }
+  // the narrower feature slice while it keeps the grid within about one CTA per SM (always with
+  // delta: its panels leave no room for a wider weight slice)
+  const int F = add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32;
+  if (mcb::proj_smem_bytes(F, panels, add) > kMaxSmemOptin)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d does not fit the shared memory (%d features a CTA%s)",
+                a->K, F, add ? ", with delta" : "");
   if (a->R == 0) return MCB_OK;
-  CUtensorMap wm;
-  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, mcb::kProjFeat);
+  CUtensorMap wm, xm, dm;
+  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, F);
   if (rc != MCB_OK) return rc;
+  rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, mcb::kProjRows);
+  if (rc != MCB_OK) return rc;
+  if (add) {
+    rc = encode_rows_map(&dm, a->delta, a->R, a->K, a->delta_stride, mcb::kProjRows);
+    if (rc != MCB_OK) return rc;
+  } else {
+    dm = xm;
+  }
   mcb::ProjParams p;
-  p.a = static_cast<const uint16_t*>(a->x);
-  p.b = use_x2 ? static_cast<const uint16_t*>(a->x2) : nullptr;
-  p.a_out = use_out ? static_cast<uint16_t*>(a->x_out) : nullptr;
+  p.res = static_cast<const uint16_t*>(a->res);
   p.y = static_cast<uint16_t*>(a->y);
-  p.as = a->x_stride;
-  p.bs = use_x2 ? a->x2_stride : 0;
-  p.aos = use_out ? a->x_out_stride : 0;
+  p.x_out = add ? static_cast<uint16_t*>(a->x_out) : nullptr;
+  p.ress = a->res_stride;
   p.ys = a->y_stride;
+  p.xos = add ? a->x_out_stride : 0;
   p.R = a->R;
   p.N = a->N;
   p.K = a->K;
   p.panels = panels;
-  p.vec_out = aligned(a->y, 16) && a->y_stride % 8 == 0 && a->N % 8 == 0;
+  p.vec_out = aligned(a->y, 16) && a->y_stride % 8 == 0 && a->N % 8 == 0 &&
+              (a->res == nullptr || (aligned(a->res, 16) && a->res_stride % 8 == 0));
   p.eps = a->eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
-  while (true) {
-    p.split = split;
-    p.max_np = (panels + split - 1) / split;
-    bool unfit = false;
-    rc = RN == 64 ? launch_proj_rn<64>(a->prologue, wm, p, tiles, pdl, st, &unfit)
-                  : launch_proj_rn<128>(a->prologue, wm, p, tiles, pdl, st, &unfit);
-    if (rc != MCB_OK || !unfit) return rc;
-    if (split <= 8 || smin > 8)  // cannot shrink to a portable cluster
-      return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: no cluster of %d CTAs fits this device", split);
-    split = std::max(smin, 8);
-  }
+  return F == 16 ? launch_proj_f<16>(norm, add, wm, xm, dm, p, pdl, st)
+                 : launch_proj_f<32>(norm, add, wm, xm, dm, p, pdl, st);
 }
 
 int mcb_gated_silu(const mcb_gated_silu_args* a, void* stream) {

@@ -13,8 +13,7 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      LinearArgs, PROLOGUE_ADD_NORM, PROLOGUE_GATED_SILU, PROLOGUE_NONE,
-                      SampleArgs, SoftcapArgs, check)
+                      LINEAR_NORM, LinearArgs, SampleArgs, SoftcapArgs, check)
 
 
 def _stream(t):
@@ -450,69 +449,51 @@ def sample(logits, uniforms, *, temperature=1.0, top_k=None, out=None):
     return out
 
 
-LINEAR_MAX_ROWS = 128
+LINEAR_MAX_ROWS = 64
 
 
-def _linear_call(args, x, weight, out, R, K, split, pdl):
+def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None, eps=None,
+           pdl=False):
+    """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
+    rows -- x (R, K) with R <= 64 and K a multiple of 64, weight (N, K), bf16, fp32 accumulation
+    -- with the Block's elementwise ops around it fused in:
+
+      norm=True   rms_norm(x, eps) @ weight^T (modelcore/components/norm.py:43-44; the bits of
+                  add_rms_norm's h), K <= 1024;
+      delta       (with norm) x' = x + delta is written to x_out (allocated when None) and
+                  normed: the residual add of the previous block's MLP, K <= 768;
+      res         res + (x @ weight^T), each rounded to bf16 (the residual add after c_proj,
+                  modelcore/components/block.py:58); out may be res (in place).
+
+    pdl: launch with programmatic stream serialization (the weight slice streams in while the
+    previous kernel finishes).  Returns out (R, N), or (x_out, out) with delta."""
+    R, K = x.shape
     N = weight.shape[0]
     if weight.shape[1] != K:
         raise RuntimeError(f"weight must be (N, {K}), got {tuple(weight.shape)}")
     if out is None:
         out = torch.empty((R, N), dtype=torch.bfloat16, device=x.device)
+    args = LinearArgs()
+    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
     args.w, args.w_stride = weight.data_ptr(), _rows2d("weight", weight)
     args.y, args.y_stride = out.data_ptr(), _rows2d("out", out)
-    args.R, args.N, args.K = R, N, K
-    args.split, args.pdl = split, int(bool(pdl))
-    check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))
-    return out
-
-
-def linear(x, weight, *, out=None, split=0, pdl=False):
-    """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
-    rows: x (R, K) with R <= 128 and K a multiple of 64, weight (N, K), bf16, fp32 accumulation on
-    tcgen05.  split: K cut across a cluster of that many CTAs (0: chosen).  pdl: launch with
-    programmatic stream serialization (the weight stream overlaps the previous kernel).  Returns
-    out (R, N)."""
-    R, K = x.shape
-    args = LinearArgs()
-    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
-    args.prologue = PROLOGUE_NONE
-    return _linear_call(args, x, weight, out, R, K, split, pdl)
-
-
-def add_norm_linear(x, delta, weight, *, eps=None, x_out=None, out=None, split=0, pdl=False):
-    """Block's residual add and the next norm fused in front of a projection
-    (modelcore/components/block.py:57-59, norm.py:43-44, linear.py:14): x' = bf16(x + delta),
-    h = rms_norm(x', eps), returns (x', h @ weight^T); delta None: h = rms_norm(x), returns
-    (x, h @ weight^T).  h has the bits of add_rms_norm's; x_out must not overlap x or delta."""
-    R, K = x.shape
-    args = LinearArgs()
-    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
-    args.prologue = PROLOGUE_ADD_NORM
-    args.eps = rms_norm_eps(eps)
+    if res is not None:
+        if tuple(res.shape) != (R, N):
+            raise RuntimeError(f"res must be ({R}, {N}), got {tuple(res.shape)}")
+        args.res, args.res_stride = res.data_ptr(), _rows2d("res", res)
     if delta is not None:
         if tuple(delta.shape) != (R, K):
-            raise RuntimeError("x and delta must have equal shapes")
+            raise RuntimeError(f"delta must be ({R}, {K}), got {tuple(delta.shape)}")
         if x_out is None:
-            x_out = torch.empty_like(x)
-        args.x2, args.x2_stride = delta.data_ptr(), _rows2d("delta", delta)
+            x_out = torch.empty((R, K), dtype=torch.bfloat16, device=x.device)
+        args.delta, args.delta_stride = delta.data_ptr(), _rows2d("delta", delta)
         args.x_out, args.x_out_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
-    y = _linear_call(args, x, weight, out, R, K, split, pdl)
-    return (x_out if delta is not None else x), y
-
-
-def silu_linear(gate, up, weight, *, out=None, split=0, pdl=False):
-    """GatedMLP's act(gate) * up (activation "silu", modelcore/components/mlp.py:89-90) fused in
-    front of down_proj: returns (bf16(bf16(silu(gate)) * up)) @ weight^T, the product's bits those
-    of gated_silu."""
-    R, K = gate.shape
-    if tuple(up.shape) != (R, K):
-        raise RuntimeError("gate and up must have equal shapes")
-    args = LinearArgs()
-    args.x, args.x_stride = gate.data_ptr(), _rows2d("gate", gate)
-    args.x2, args.x2_stride = up.data_ptr(), _rows2d("up", up)
-    args.prologue = PROLOGUE_GATED_SILU
-    return _linear_call(args, gate, weight, out, R, K, split, pdl)
+    args.R, args.N, args.K = R, N, K
+    args.flags = LINEAR_NORM if norm else 0
+    args.eps = rms_norm_eps(eps)
+    args.pdl = int(bool(pdl))
+    check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))
+    return (x_out, out) if delta is not None else out
 
 
 def gated_silu(gate, up, out=None):

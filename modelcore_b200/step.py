@@ -93,12 +93,13 @@ def packed_weight(owner, key, linears):
     return view
 
 
-# With USE_FUSED_PROJ a decode step of at most ops.LINEAR_MAX_ROWS rows runs its projections on
-# libmcb200's mcb_linear, with the elementwise op in front of each fused into the projection's
-# operand load (body_forward_proj: 6 launches a layer instead of 9).  Off by default: at 64 rows
-# the split-K cluster kernel measures 6.9-7.7 us a projection in a CUDA graph against cuBLAS's
-# 3.3-5.4 us, more than the 7 us a layer the fused add + norm and silu save (config 2: 58k vs
-# 101k tokens/s with the first version); prefill-sized blocks always use cuBLAS (F.linear).
+# With USE_FUSED_PROJ a decode step of at most 64 rows runs its q|k|v, c_proj and gate|up
+# projections on libmcb200's mcb_linear with the Block's norms fused in front of q|k|v and gate|up
+# and the residual adds fused around them (body_forward_proj: 7 launches a layer instead of 9);
+# down_proj (K = the MLP width) and prefill-sized blocks of rows use cuBLAS (F.linear).  Off by
+# default: the plain projection matches cuBLAS at 64 rows (3.1-3.5 us in a CUDA graph), but the
+# fused norm costs about 7 us inside it -- 64 rows' dependent reduction chains on 8 warps --
+# against 2.6 us for the stand-alone kernel (config 2: 81k vs 102k tokens/s).
 USE_FUSED_PROJ = False
 
 
@@ -178,41 +179,46 @@ def body_forward(body, x2, h, idx, kv_cache, B, T):
 
 
 def _proj_ok(body, rows, x):
-    """The fused-projection body applies: at most LINEAR_MAX_ROWS rows, every block's attention
-    on the fused append (modelcore's RMSNorm QK-norm and RotaryEmbedding), every projection's K a
-    multiple of 64."""
+    """The fused-projection body applies: at most 64 rows, every block's attention on the fused
+    append (modelcore's RMSNorm QK-norm and RotaryEmbedding), n_embd a multiple of 64 and at most
+    768 (the normed projections hold all n_embd columns of the rows -- and of the residual delta
+    -- in shared memory)."""
     from .integration import _fusable
-    if not USE_FUSED_PROJ or not 0 < rows <= ops.LINEAR_MAX_ROWS or x.size(-1) % 64:
+    C = x.size(-1)
+    if not USE_FUSED_PROJ or not 0 < rows <= ops.LINEAR_MAX_ROWS or C % 64 or C > 768:
         return False
     for b in body.blocks:
         a = b.mixer
-        if not _fusable(a, x) or (a.n_head * a.head_dim) % 64 or b.ffn.hidden_dim % 64:
+        if not _fusable(a, x) or (a.n_head * a.head_dim) % 64:
             return False
         if a.c_q.weight.dtype != x.dtype:
             return False
     return True
 
 
-def body_forward_proj(body, x2, kv_cache, B, T):
-    """body_forward for a decode step's few rows with every projection on mcb_linear:
+def body_forward_proj(body, x2, kv_cache, B, T, inplace=False, want_h=True):
+    """body_forward for a decode step's few rows with the projections around attention on
+    mcb_linear:
 
-        per block:  x, qkv = x + delta, norm(x + delta) @ [Wq; Wk; Wv]^T   (block 0: norm(x))
-                    append + attention                                      (integration.attend)
-                    o = attn @ Wo^T
-                    x, gu = x + o, norm(x + o) @ [Wg; Wu]^T
-                    delta = (silu(gu[:, :H]) * gu[:, H:]) @ Wd^T
+        per block:  x, qkv = x + delta, norm(x + delta) @ [Wq; Wk; Wv]^T   (block 0: norm(x);
+                                                   the add and the norm inside the projection)
+                    append + attention              (integration.attend)
+                    x = x + attn @ Wo^T             (the add in the projection's epilogue)
+                    gu = norm(x) @ [Wg; Wu]^T
+                    a = silu(gu[:, :H]) * gu[:, H:]  (mcb_gated_silu)
+                    delta = a @ Wd^T                 (cuBLAS: K = H is the MLP width)
         then x + delta and its norm (mcb_add_rms_norm).
 
-    6 launches a layer, each projection launched with programmatic dependent launch so its
-    weight stream overlaps the kernel ahead.  The residual alternates between two buffers: a
-    fused add writes x + delta while other CTAs of the same launch still read x.  The operand
-    bits equal body_forward's (h and silu * up are bit-exact); the products differ from cuBLAS's
-    in fp32 summation order only.  Returns the final residual and its norm (rows, C)."""
+    7 launches a layer; the libmcb200 projections are launched with programmatic dependent
+    launch, so each one's weight slice streams in while the kernel ahead finishes.  The fused add
+    writes x + delta to the other of two buffers (other CTAs still read x).  The operand bits
+    equal body_forward's (the norm and the adds are the same roundings); the products differ from
+    cuBLAS's in fp32 summation order only.  Returns the final residual and its norm (rows, C)
+    (None without want_h); x2 itself is not written unless inplace."""
     from .integration import attend
     rows, C = x2.shape
-    bufs = (torch.empty_like(x2), torch.empty_like(x2))
-    nxt = 0
-    src, delta = x2, None
+    bufs = (x2 if inplace else torch.empty_like(x2), torch.empty_like(x2))
+    x, cur, delta = x2, -1, None
     for block in body.blocks:
         attn, ffn, eps = block.mixer, block.ffn, block.norm.eps
         if attn.produces_kv:
@@ -220,10 +226,15 @@ def body_forward_proj(body, x2, kv_cache, B, T):
         else:
             w = attn.c_q.weight
         if delta is None:
-            _, qkv = ops.add_norm_linear(src, None, w, eps=eps, pdl=True)
+            if not inplace and cur < 0:   # the c_proj add below writes x: work on a copy
+                bufs[0].copy_(x2)
+                x, cur = bufs[0], 0
+            qkv = ops.linear(x, w, norm=True, eps=eps, pdl=True)
         else:
-            src, qkv = ops.add_norm_linear(src, delta, w, eps=eps, x_out=bufs[nxt], pdl=True)
-            nxt ^= 1
+            cur = 1 - cur
+            x, qkv = ops.linear(x, w, norm=True, delta=delta, x_out=bufs[cur], eps=eps, pdl=True)
+        if cur < 0:
+            cur = 0                       # inplace: bufs[0] is x2
         hd = attn.head_dim
         nq = attn.n_head * hd
         q = qkv[:, :nq].view(B, T, attn.n_head, hd)
@@ -233,15 +244,17 @@ def body_forward_proj(body, x2, kv_cache, B, T):
             k = qkv[:, nq:nq + nk].view(B, T, attn.n_kv_head, hd)
             v = qkv[:, nq + nk:].view(B, T, attn.n_kv_head, hd)
         y = attend(attn, q, k, v, kv_cache)
-        o = ops.linear(y.view(rows, nq), attn.c_proj.weight, pdl=True)
+        ops.linear(y.view(rows, nq), attn.c_proj.weight, out=x, res=x, pdl=True)
         wgu = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
-        src, gu = ops.add_norm_linear(src, o, wgu, eps=eps, x_out=bufs[nxt], pdl=True)
-        nxt ^= 1
+        gu = ops.linear(x, wgu, norm=True, eps=eps, pdl=True)
         H = ffn.hidden_dim
-        delta = ops.silu_linear(gu[:, :H], gu[:, H:], ffn.down_proj.weight, pdl=True)
+        delta = F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
+    out = bufs[1 - cur]
+    if not want_h:
+        return torch.add(x, delta, out=out), None
     h = torch.empty_like(x2)
-    resid, _ = ops.add_rms_norm(src, delta, eps=body.blocks[-1].norm.eps, x_out=bufs[nxt], h_out=h)
-    return resid, h
+    ops.add_rms_norm(x, delta, eps=body.blocks[-1].norm.eps, x_out=out, h_out=h)
+    return out, h
 
 
 def stack_forward(self, x, idx, kv_cache, doc_args=None):
@@ -252,7 +265,7 @@ def stack_forward(self, x, idx, kv_cache, doc_args=None):
     B, T, C = x.shape
     x2 = x.reshape(B * T, C)
     if _proj_ok(self, B * T, x):
-        return body_forward_proj(self, x2, kv_cache, B, T)[0].view(B, T, C)
+        return body_forward_proj(self, x2, kv_cache, B, T, want_h=False)[0].view(B, T, C)
     h = torch.empty_like(x2)
     ops.add_rms_norm(x2, eps=self.blocks[0].norm.eps, h_out=h)
     resid, _ = body_forward(self, x2, h, idx, kv_cache, B, T)
@@ -294,7 +307,7 @@ def _hidden(model, idx, kv_cache):
     probe = emb.wte.weight[:0]
     if _proj_ok(model.body, B * T, probe):
         x, _ = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps, second_norm=False)
-        _, h = body_forward_proj(model.body, x.view(B * T, C), kv_cache, B, T)
+        _, h = body_forward_proj(model.body, x.view(B * T, C), kv_cache, B, T, inplace=True)
     else:
         x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
         _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)

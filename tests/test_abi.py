@@ -237,33 +237,36 @@ def test_linear_rejects_bad_arguments_on_the_host():
 
     def args(**kw):
         a = LinearArgs()
-        a.x, a.w, a.y = base, base + (1 << 16), base + (2 << 16)
+        a.x, a.w, a.y = base, base + (1 << 20), base + (2 << 20)
         a.x_stride = a.w_stride = a.y_stride = 768
         a.R, a.N, a.K = 64, 768, 768
-        a.prologue = _native.PROLOGUE_NONE
         for k, v in kw.items():
             setattr(a, k, v)
         return a
 
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=3)), None))
-    assert st == _native.MCB_ERR_INVALID_ARG and "prologue" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=2)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "flags" in msg
     st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=96, x_stride=96, w_stride=96)), None))
     assert st == _native.MCB_ERR_UNSUPPORTED and "multiple of 64" in msg
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(R=129)), None))
-    assert st == _native.MCB_ERR_UNSUPPORTED and "at most 128" in msg
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(split=17)), None))
-    assert st == _native.MCB_ERR_INVALID_ARG and "split" in msg
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(split=13)), None))  # 12 panels
-    assert st == _native.MCB_ERR_INVALID_ARG and "split 13" in msg
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=_native.PROLOGUE_GATED_SILU)), None))
-    assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(R=65)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "at most 64" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(delta=base + (3 << 20), delta_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "delta needs" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=_native.LINEAR_NORM, delta=base + (3 << 20),
+                                                    delta_stride=768, x_out=base + 1024, x_out_stride=768)),
+                                  None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "overlap" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=_native.LINEAR_NORM, K=1088, x_stride=1088,
+                                                    w_stride=1088)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "1024" in msg
     st, msg = _err(lib.mcb_linear(ctypes.byref(args(x=base + 8)), None))
     assert st == _native.MCB_ERR_ALIGNMENT
-    # the fused residual must not overlap what other CTAs still read
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(prologue=_native.PROLOGUE_ADD_NORM, x2=base + (3 << 20),
-                                                    x2_stride=768, x_out=base + 64 * 768,
-                                                    x_out_stride=768)), None))
-    assert st == _native.MCB_ERR_INVALID_ARG and "overlaps" in msg
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=64 * 8 * 17, x_stride=64 * 8 * 17,
-                                                    w_stride=64 * 8 * 17)), None))
-    assert st == _native.MCB_ERR_UNSUPPORTED
+    # every CTA reads all of x: the output must not overlap it
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(y=base + 64 * 768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "overlap" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(res=base + (2 << 20) + 16, res_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "res" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=64 * 400, x_stride=64 * 400, w_stride=64 * 400,
+                                                    x=base, w=base + (8 << 20), y=base + (16 << 20))),
+                                  None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "shared memory" in msg

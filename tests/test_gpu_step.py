@@ -312,9 +312,9 @@ def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
         eager.step(cols[0])
         per_step = ops.launch_count() - n0
         if fused_proj:
-            # the embedding; per layer q|k|v (with add + norm), append, c_proj, gate|up (with
-            # add + norm), down (with silu * up); the last add + norm, the advance, the LM-head
-            # epilogue
+            # the embedding; per layer q|k|v (add + norm inside), append, c_proj (+ residual),
+            # gate|up (norm inside), silu * up (down_proj is cuBLAS); the final add + norm, the
+            # advance, the LM-head epilogue
             attn_launches = per_step - (1 + 4 * 5 + 1 + 1 + 1)
         else:
             # embedding + first norm, 4 per layer, the advance, the LM-head epilogue
@@ -397,21 +397,18 @@ def copy_with_plain_forward(env, model):
         return mcb.ModelManager().new_decoder(other, prompts, max_tokens=4).step([5, 6]).float().clone()
 
 
-def test_fused_step_on_mcb_linear_projections_is_as_accurate(env):
-    """The same bar with the decode projections on libmcb200's tcgen05 kernel with the residual
-    add + norm and silu * up fused into them (USE_FUSED_PROJ, body_forward_proj) instead of
-    cuBLAS and separate kernels."""
+@pytest.mark.parametrize("fused_proj", [False, True])
+def test_fused_step_projection_paths_are_as_accurate(env, fused_proj, monkeypatch):
+    """The same bar with the decode projections on libmcb200's tcgen05 kernel with the norms and
+    residual adds fused into them (USE_FUSED_PROJ, body_forward_proj), and on cuBLAS with the
+    norms and adds as their own kernels."""
     from modelcore.tests.test_generate import RAGGED_PROMPTS
     from modelcore_b200 import step
+    monkeypatch.setattr(step, "USE_FUSED_PROJ", fused_proj)
     (rm, ref), (fm, fused), _, (m32, ref32) = _models(env, _configs()["quickstart"]())
     cols = torch.tensor([[(s * 7 + i * 3) % 100 + 1 for s in range(8)]
                          for i in range(len(RAGGED_PROMPTS))])
-    saved = step.USE_FUSED_PROJ
-    step.USE_FUSED_PROJ = True
-    try:
-        l_fused = _forced(fm, fused, RAGGED_PROMPTS, cols)
-    finally:
-        step.USE_FUSED_PROJ = saved
+    l_fused = _forced(fm, fused, RAGGED_PROMPTS, cols)
     l32 = _forced(m32, ref32, RAGGED_PROMPTS, cols)
     l_ref = _forced(rm, ref, RAGGED_PROMPTS, cols)
     e_ref = (l_ref - l32).abs().max().item()

@@ -21,8 +21,9 @@ roofline   the decode-attention kernel: algorithmic KV bytes (exact keys per row
            over the 12 cache slots in rotation (1.6 GB, far above L2), against the measured HBM
            copy bandwidth in MEASURED_PEAKS.json.
 kv_read_sweep  measurement config 5 (32 q / 8 kv heads of 128, lengths U[1, 32768] from seed 5,
-           window -1 / 4096): one step = fused rope append + decode attention; L2 flushed before
-           every timed launch.
+           window -1 / 4096): one step = fused rope append + decode attention, timed on the device
+           in CUDA graphs of consecutive steps on rotating groups of cache rows (no launch finds
+           its keys in L2).
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
            sample of the same workload (rank 0, N = 1).
 """
@@ -265,12 +266,14 @@ def _attention_roofline(dec, peak, reps=4):
 
 
 def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
-    """Config 5: fused rope append + decode attention per step, cold L2 per launch."""
+    """Config 5: fused rope append + decode attention per step.  Each (batch, window) point is
+    timed on the device in a CUDA graph of consecutive steps, each on a different group of cache
+    rows (kc[g*B:(g+1)*B]) so that no launch finds its keys in L2 (the groups cycled through hold
+    more than the 126 MB L2 between two visits); attention alone and append + attention."""
     import numpy as np
     import torch
     from modelcore_b200 import ops
     Hq, Hkv, D, Tmax = 32, 8, 128, 32769
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     g = torch.Generator(device="cuda").manual_seed(5)
     rows = []
@@ -280,37 +283,62 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
     ang = torch.arange(Tmax + 1, device="cuda", dtype=torch.float32)[:, None] * \
         (100000.0 ** (-torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))[None]
     cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+
+    def graph_us(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.graph(gr, stream=side):
+            fn()
+        stream.wait_stream(side)
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(3):
+            gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del gr
+        return e0.elapsed_time(e1) * 1e3 / (3 * n)
+
     for B in batches:
         lens = np.random.default_rng(5).integers(1, 32769, size=B) - 1
         sl = torch.from_numpy(lens).to(torch.int32).cuda()
         q = torch.randn(B, 1, Hq, D, device="cuda", generator=g, dtype=torch.bfloat16)
         k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
         v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
-        kcb, vcb = kc[:B], vc[:B]
+        groups = max(1, min(16, max_b // B))
+        kcs = [kc[i * B:(i + 1) * B] for i in range(groups)]
+        vcs = [vc[i * B:(i + 1) * B] for i in range(groups)]
         for w in windows:
             keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
             nbytes = keys * 2 * Hkv * D * 2
-            t_att, t_step = [], []
             torch.cuda.nvtx.range_push(f"sweep_b{B}_w{w}")
-            for it in range(6):
-                flush.zero_()
-                a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-                a0.record(stream)
-                qr = ops.kv_append_rope(q, k, v, kcb, vcb, sl, cos, sin)
-                a1.record(stream)
-                ops.decode_attn(qr, kcb, vcb, sl, window=w)
-                a2.record(stream)
-                torch.cuda.synchronize()
-                if it:
-                    t_att.append(a1.elapsed_time(a2))
-                    t_step.append(a0.elapsed_time(a2))
+            qr = ops.kv_append_rope(q, k, v, kcs[0], vcs[0], sl, cos, sin)
+            out = torch.empty_like(qr)
+            n = 4 * groups
+
+            def attn_only():
+                for i in range(n):
+                    ops.decode_attn(qr, kcs[i % groups], vcs[i % groups], sl, window=w, out=out)
+
+            def step():
+                for i in range(n):
+                    qi = ops.kv_append_rope(q, k, v, kcs[i % groups], vcs[i % groups], sl, cos, sin,
+                                            q_out=qr)
+                    ops.decode_attn(qi, kcs[i % groups], vcs[i % groups], sl, window=w, out=out)
+
+            ta = graph_us(attn_only, n)
+            ts = graph_us(step, n)
             torch.cuda.nvtx.range_pop()
-            ta, ts = statistics.median(t_att), statistics.median(t_step)
-            gbs = nbytes / (ta * 1e-3) / 1e9
+            gbs = nbytes / (ta * 1e-6) / 1e9
             rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
-                         "attn_us": round(ta * 1e3, 1), "step_us": round(ts * 1e3, 1),
+                         "attn_us": round(ta, 1), "step_us": round(ts, 1),
                          "kv_gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
-    del kc, vc, flush
+    del kc, vc
     torch.cuda.empty_cache()
     return rows
 

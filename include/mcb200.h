@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 4
+#define MCB_ABI_VERSION 5
 
 typedef enum {
   MCB_OK = 0,
@@ -83,6 +83,15 @@ typedef struct {
   uint32_t flags;             /* MCB_APPEND_* bits                                          */
   int32_t ring;               /* 0: position p at index p; 1: the slot is a ring of Tmax
                                  positions, position p at index p % Tmax                    */
+  /* fp8 cache (k_scale != NULL): k_cache / v_cache hold float8 e4m3 bytes, one per element, and
+     each (row, position, kv head) vector its scale at k_scale / v_scale[(b * Hkv + h) *
+     scale_tmax + index] (fp32, scale_tmax >= Tmax and a multiple of 64): the vector of bf16
+     values x a bf16 cache would hold is stored as e4m3(x * (448 / amax)) rounded to nearest
+     even and saturated, with scale amax / 448 (amax = max |x|; 0 stores zeros and scale 0).
+     Needs D = 64 or 128 and 16-byte aligned rows. */
+  float* k_scale;
+  float* v_scale;
+  int32_t scale_tmax;
 } mcb_append_args;
 
 int mcb_kv_append_rope(const mcb_append_args* args, void* stream);
@@ -159,6 +168,12 @@ typedef struct {
   int32_t ring;               /* 1: the slot is a ring of Tmax positions (p at p % Tmax);
                                  needs window >= 0, window + T <= Tmax and Tmax a multiple of
                                  128, so every visible key is resident and no key tile wraps */
+  /* fp8 cache (k_scale != NULL): e4m3 k_cache / v_cache with per-vector scales as written by
+     mcb_kv_append_rope (layout (B, Hkv, scale_tmax) fp32, zero where never written); keys are
+     read as e4m3 * scale.  The split plan only (D = 64 or 128). */
+  const float* k_scale;
+  const float* v_scale;
+  int32_t scale_tmax;
 } mcb_attn_args;
 
 /* Bytes of workspace mcb_decode_attn needs for its partial results (0: none): persistent plan,

@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -79,6 +79,8 @@ class AppendArgs(ctypes.Structure):
         ("eps", ctypes.c_float), ("scale", ctypes.c_float),
         ("flags", ctypes.c_uint32),
         ("ring", ctypes.c_int32),
+        ("k_scale", ctypes.c_void_p), ("v_scale", ctypes.c_void_p),
+        ("scale_tmax", ctypes.c_int32),
     ]
 
 
@@ -108,6 +110,8 @@ class AttnArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("counters", ctypes.c_void_p), ("counter_count", ctypes.c_size_t),
         ("ring", ctypes.c_int32),
+        ("k_scale", ctypes.c_void_p), ("v_scale", ctypes.c_void_p),
+        ("scale_tmax", ctypes.c_int32),
     ]
 
 

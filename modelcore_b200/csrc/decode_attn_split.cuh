@@ -31,10 +31,15 @@ struct SplitAttnParams {
   int nsplit, tiles_per_split, nqb;
   int cluster;       // the nsplit (<= 8) CTAs of a row group form a cluster and merge in DSMEM
   int ring;          // the slot is a ring of Tmax positions (key c at index c % Tmax)
+  // fp8 cache (decode_attn_split_kernel<.., true>): e4m3 K/V with per-vector fp32 scales at
+  // [(b * Hkv + h) * scale_tmax + index]
+  const float* k_scale;
+  const float* v_scale;
+  int scale_tmax;
 };
 
 
-template <int D, int NQT, int KPW, int STAGES>
+template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
 struct SplitAttnConfig {
   static constexpr int kRows = 8 * NQT;                      // query rows per CTA
   static constexpr int TK = KPW * kAttnConsumerWarps;        // keys per stage
@@ -44,8 +49,17 @@ struct SplitAttnConfig {
   static constexpr int SWZ_MASK = ROW_BYTES == 128 ? 7 : (ROW_BYTES == 64 ? 3 : 1);
   static constexpr int PANEL_BYTES = TK * ROW_BYTES;
   static constexpr int TILE_BYTES = NPANEL * PANEL_BYTES;    // one K (or V) tile
-  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  // fp8: a stage holds the e4m3 K and V tiles (TK rows of D bytes, one swizzled panel) and the
+  // tile's K and V scales; each consumer warp converts its KPW rows to f16 in its own scratch,
+  // laid out as a bf16 tile of KPW rows (same panels, same swizzle)
+  static constexpr int F8_ROW = D;
+  static constexpr int F8_MASK = D == 128 ? 7 : 3;
+  static constexpr int F8_TILE = TK * D;
+  static constexpr int F8_SCALES = 2 * TK * 4;
+  static constexpr int STAGE_BYTES = FP8 ? ((2 * F8_TILE + F8_SCALES + 1023) & ~1023) : 2 * TILE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int SCR_PANEL = KPW * ROW_BYTES;          // one warp's scratch panel
+  static constexpr int SCR_WARP = FP8 ? 2 * NPANEL * SCR_PANEL : 0;  // K then V
   static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
   static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
   // cluster merge: this CTA's merged partial [kRows][D], its per-row log2-sum-exp and the
@@ -54,21 +68,53 @@ struct SplitAttnConfig {
   static constexpr int CL_BYTES = kRows * D * 4 + kRows * 4 + kRows * 8 * 4;
   static constexpr int BODY_BYTES =
       RING_BYTES > CL_OFFSET + CL_BYTES ? RING_BYTES : CL_OFFSET + CL_BYTES;
+  static constexpr int SCR_OFFSET = BODY_BYTES;
   // barriers (full + empty per stage) then per-warp row statistics
-  static constexpr int BAR_OFFSET = BODY_BYTES;
+  static constexpr int BAR_OFFSET = SCR_OFFSET + kAttnConsumerWarps * SCR_WARP;
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
   static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
   static constexpr int SMEM_BYTES = STAT_OFFSET + STAT_BYTES + 1024;  // + alignment slack
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
   static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
+  static_assert(!FP8 || D == 64 || D == 128, "fp8 cache: head_dim 64 or 128");
 };
 
-template <int D, int NQT, int KPW, int STAGES>
+// 4 e4m3 bytes (memory order) -> two f16x2 words (exact)
+__device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// c[0..3] += A(16x16, row) * B(16x8, col), f16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_16816_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// 1-D bulk copy global -> this CTA's shared memory (bytes a multiple of 16, both 16-byte
+// aligned), counted on the mbarrier as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
 __global__ void __launch_bounds__(kAttnThreads)
     decode_attn_split_kernel(const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const SplitAttnParams p) {
-  using C = SplitAttnConfig<D, NQT, KPW, STAGES>;
+  using C = SplitAttnConfig<D, NQT, KPW, STAGES, FP8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -145,16 +191,26 @@ __global__ void __launch_bounds__(kAttnThreads)
           pdl_wait();
           waited = true;
         }
-        mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
         const int slot0 = p.ring ? key0 % p.Tmax : key0;  // a ring slot: Tmax % TK == 0
         uint8_t* kdst = smem + s * C::STAGE_BYTES;
-        uint8_t* vdst = kdst + C::TILE_BYTES;
+        if constexpr (FP8) {
+          mbar_arrive_expect_tx(&full_bar[s], 2 * C::F8_TILE + C::F8_SCALES);
+          tma_load_4d(kdst, &kmap, &full_bar[s], 0, kvh, slot0, b, policy);
+          tma_load_4d(kdst + C::F8_TILE, &vmap, &full_bar[s], 0, kvh, slot0, b, policy);
+          // the tile's scales; scale_tmax >= Tmax rounded up to TK keeps them in bounds
+          const long long so = (static_cast<long long>(b) * p.Hkv + kvh) * p.scale_tmax + slot0;
+          bulk_load(kdst + 2 * C::F8_TILE, p.k_scale + so, C::TK * 4, &full_bar[s]);
+          bulk_load(kdst + 2 * C::F8_TILE + C::TK * 4, p.v_scale + so, C::TK * 4, &full_bar[s]);
+        } else {
+          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          uint8_t* vdst = kdst + C::TILE_BYTES;
 #pragma unroll
-        for (int pn = 0; pn < C::NPANEL; ++pn) {
-          tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
-                      policy);
-          tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
-                      policy);
+          for (int pn = 0; pn < C::NPANEL; ++pn) {
+            tma_load_4d(kdst + pn * C::PANEL_BYTES, &kmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
+                        policy);
+            tma_load_4d(vdst + pn * C::PANEL_BYTES, &vmap, &full_bar[s], pn * C::PANEL, kvh, slot0, b,
+                        policy);
+          }
         }
       }
     }
@@ -183,6 +239,12 @@ __global__ void __launch_bounds__(kAttnThreads)
         const int d0 = kk * 16 + 2 * (lane & 3);
         qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
         qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+        if (FP8) {  // the products run in f16 against the exactly converted e4m3 keys
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            qf[j][kk][u] = pack_f16x2(__uint_as_float(qf[j][kk][u] << 16),
+                                      __uint_as_float(qf[j][kk][u] & 0xffff0000u));
+        }
       }
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -205,12 +267,59 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
 
     constexpr int NCH = KPW / 16;  // 16-key chunks per warp per stage
+    // fp8: this warp's f16 scratch (K then V), its rows at 0 .. KPW-1
+    const uint32_t scr_k = smem_u32(smem + C::SCR_OFFSET + warp * C::SCR_WARP);
+    const uint32_t scr_v = scr_k + C::NPANEL * C::SCR_PANEL;
     for (int i = 0; i < my_tiles; ++i) {
       const int s = i % STAGES;
       if (!mbar_wait(&full_bar[s], (i / STAGES) & 1)) break;
-      const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
-      const uint32_t vbase = kbase + C::TILE_BYTES;
+      uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
+      uint32_t vbase = kbase + C::TILE_BYTES;
+      int row0 = warp * KPW;                  // this warp's first key row in the tile buffers
+      int panel_bytes = C::PANEL_BYTES;
       const int tile_key0 = kb + (tile0 + i) * C::TK;
+      float ks[NCH][2], vs[NCH][2];           // fp8: the scales of this lane's key rows
+      if constexpr (FP8) {
+        const uint32_t f8k = kbase, f8v = kbase + C::F8_TILE;
+        const float* scl = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + 2 * C::F8_TILE);
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int kr = warp * KPW + ch * 16 + (lane >> 2) + hh * 8;
+            ks[ch][hh] = scl[kr];
+            vs[ch][hh] = scl[C::TK + kr];
+          }
+        // e4m3 rows warp*KPW .. +KPW-1 of K and V -> f16 (exact), 16 bytes of e4m3 a step
+        constexpr int CPR = D / 16;  // 16-byte e4m3 chunks per row
+#pragma unroll
+        for (int idx = lane; idx < KPW * CPR; idx += 32) {
+          const int r = idx / CPR, c16 = idx % CPR;
+          const uint32_t soff = swz<C::F8_ROW, C::F8_MASK>(warp * KPW + r, c16);
+          const int col = c16 * 16;  // two 8-column f16 chunks, swizzled independently
+          const uint32_t pbase = (col / C::PANEL) * C::SCR_PANEL;
+          const uint32_t doff0 = pbase + swz<C::ROW_BYTES, C::SWZ_MASK>(r, (col % C::PANEL) / 8);
+          const uint32_t doff1 = pbase + swz<C::ROW_BYTES, C::SWZ_MASK>(r, (col % C::PANEL) / 8 + 1);
+#pragma unroll
+          for (int kv = 0; kv < 2; ++kv) {
+            const uint4 w = lds128((kv ? f8v : f8k) + soff);
+            uint32_t h[8];
+            e4m3x4_to_f16x4(w.x, h[0], h[1]);
+            e4m3x4_to_f16x4(w.y, h[2], h[3]);
+            e4m3x4_to_f16x4(w.z, h[4], h[5]);
+            e4m3x4_to_f16x4(w.w, h[6], h[7]);
+            const uint32_t dst = kv ? scr_v : scr_k;
+            sts128(dst + doff0, make_uint4(h[0], h[1], h[2], h[3]));
+            sts128(dst + doff1, make_uint4(h[4], h[5], h[6], h[7]));
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);  // the stage is converted: refill it
+        kbase = scr_k;
+        vbase = scr_v;
+        row0 = 0;
+        panel_bytes = C::SCR_PANEL;
+      }
 
       float sc[NCH][NQT][4];
 #pragma unroll
@@ -219,16 +328,30 @@ __global__ void __launch_bounds__(kAttnThreads)
         for (int j = 0; j < NQT; ++j)
 #pragma unroll
           for (int c = 0; c < 4; ++c) sc[ch][j][c] = 0.f;
-        const int krow = warp * KPW + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int krow = row0 + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int col = kk * 16 + (lane >> 4) * 8;  // first column of this lane's 8-wide chunk
-          const uint32_t addr = kbase + (col / C::PANEL) * C::PANEL_BYTES +
+          const uint32_t addr = kbase + (col / C::PANEL) * panel_bytes +
                                 swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
           uint32_t a0, a1, a2, a3;
           ldsm_x4(addr, a0, a1, a2, a3);
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) mma_16816(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
+          for (int j = 0; j < NQT; ++j) {
+            if (FP8)
+              mma_16816_f16(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
+            else
+              mma_16816(sc[ch][j], a0, a1, a2, a3, qf[j][kk][0], qf[j][kk][1]);
+          }
+        }
+        if (FP8) {  // logits of the stored keys times their scales
+#pragma unroll
+          for (int j = 0; j < NQT; ++j) {
+            sc[ch][j][0] *= ks[ch][0];
+            sc[ch][j][1] *= ks[ch][0];
+            sc[ch][j][2] *= ks[ch][1];
+            sc[ch][j][3] *= ks[ch][1];
+          }
         }
       }
 
@@ -284,24 +407,34 @@ __global__ void __launch_bounds__(kAttnThreads)
         uint32_t pb[NQT][2];
 #pragma unroll
         for (int j = 0; j < NQT; ++j) {
-          pb[j][0] = movmatrix_trans(pack_bf16x2(sc[ch][j][0], sc[ch][j][1]));
-          pb[j][1] = movmatrix_trans(pack_bf16x2(sc[ch][j][2], sc[ch][j][3]));
+          if (FP8) {  // the value scales ride on the probabilities (l sums them unscaled)
+            pb[j][0] = movmatrix_trans(pack_f16x2(sc[ch][j][0] * vs[ch][0], sc[ch][j][1] * vs[ch][0]));
+            pb[j][1] = movmatrix_trans(pack_f16x2(sc[ch][j][2] * vs[ch][1], sc[ch][j][3] * vs[ch][1]));
+          } else {
+            pb[j][0] = movmatrix_trans(pack_bf16x2(sc[ch][j][0], sc[ch][j][1]));
+            pb[j][1] = movmatrix_trans(pack_bf16x2(sc[ch][j][2], sc[ch][j][3]));
+          }
         }
         const int m = lane >> 3;
-        const int vrow = warp * KPW + ch * 16 + (lane & 7) + (m >> 1) * 8;
+        const int vrow = row0 + ch * 16 + (lane & 7) + (m >> 1) * 8;
 #pragma unroll
         for (int db = 0; db < D / 16; ++db) {
           const int col = db * 16 + (m & 1) * 8;
-          const uint32_t addr = vbase + (col / C::PANEL) * C::PANEL_BYTES +
+          const uint32_t addr = vbase + (col / C::PANEL) * panel_bytes +
                                 swz<C::ROW_BYTES, C::SWZ_MASK>(vrow, (col % C::PANEL) / 8);
           uint32_t a0, a1, a2, a3;
           ldsm_x4_trans(addr, a0, a1, a2, a3);
 #pragma unroll
-          for (int j = 0; j < NQT; ++j) mma_16816(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+          for (int j = 0; j < NQT; ++j) {
+            if (FP8)
+              mma_16816_f16(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+            else
+              mma_16816(o_acc[j][db], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+          }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
+      if (!FP8 && lane == 0) mbar_arrive(&empty_bar[s]);
     }
 
     // Full per-row sums of this warp.

@@ -45,6 +45,11 @@ struct AppendParams {
   bool rotate_k;
   long long total_vectors;
   int ring;   // the slot is a ring of Tmax positions: position p at index p % Tmax
+  // fp8 cache (kv_append_rope_vec_kernel<D, true>): k_cache / v_cache hold e4m3 bytes and every
+  // (row, position, head) vector has its scale at k_scale / v_scale[(b * Hkv + h) * scale_tmax + index]
+  float* k_scale;
+  float* v_scale;
+  int scale_tmax;
 };
 
 constexpr int kAppendWarpsPerBlock = 4;
@@ -161,9 +166,28 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return v;
 }
 
+// The e4m3 quantization of one cache vector (fp8 cache): amax = max |x| over the vector's D
+// values (x the bf16 values a bf16 cache would hold), scale = amax / 448 and x8 =
+// e4m3(x * (448 / amax)) rounded to nearest even and saturated to +-448 (both quotients correctly
+// rounded fp32; amax = 0 stores zeros with scale 0).  cvt packs its first source in the upper byte.
+__device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint2 e4m3x8(const float* x, float inv) {
+  uint32_t w[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    w[i] = static_cast<uint32_t>(e4m3x2(__fmul_rn(x[4 * i], inv), __fmul_rn(x[4 * i + 1], inv))) |
+           (static_cast<uint32_t>(e4m3x2(__fmul_rn(x[4 * i + 2], inv), __fmul_rn(x[4 * i + 3], inv))) << 16);
+  return make_uint2(w[0], w[1]);
+}
+
 // Vectorised variant: L = D/16 lanes per vector, 16-byte loads and stores, 32/L vectors per warp.
-// Requires 16-byte aligned rows (checked on the host).
-template <int D>
+// Requires 16-byte aligned rows (checked on the host).  FP8: the cache vectors are stored as
+// e4m3 with a per-vector scale (e4m3x8 above), 8-byte stores.
+template <int D, bool FP8>
 __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
     kv_append_rope_vec_kernel(const AppendParams p) {
   pdl_launch_dependents();  // the kernel after it waits for completion before reading
@@ -191,6 +215,8 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
                              : (is_v ? p.v + b * p.vs[0] + t * p.vs[1] + h * p.vs[2]
                                      : p.k + b * p.ks[0] + t * p.ks[1] + h * p.ks[2]);
   bool ok = active;
+  long long cache_off = 0;   // element offset of the cache vector
+  long long scale_off = 0;
   uint16_t* dst = nullptr;
   if (is_q) {
     dst = p.q_out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D;
@@ -199,8 +225,10 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
       if (active && sub == 0) record_error(kErrPositionBeyondCache);
       ok = false;
     } else {
-      dst = (is_v ? p.v_cache : p.k_cache) +
-            ((static_cast<long long>(b) * p.Tmax + (p.ring ? pos % p.Tmax : pos)) * p.Hkv + h) * D;
+      const int idx = p.ring ? pos % p.Tmax : pos;
+      cache_off = ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + h) * D;
+      scale_off = (static_cast<long long>(b) * p.Hkv + h) * p.scale_tmax + idx;
+      if (!FP8) dst = (is_v ? p.v_cache : p.k_cache) + cache_off;
     }
   }
   const bool rotate = is_q || (!is_v && p.rotate_k);
@@ -211,7 +239,7 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
 
   const uint4 x1v = ok ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
   const uint4 x2v = ok ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
-  if (!rotate) {  // value heads and raw key inserts: a copy
+  if (!FP8 && !rotate) {  // value heads and raw key inserts: a copy
     if (ok) {
       *reinterpret_cast<uint4*>(dst + 8 * sub) = x1v;
       *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = x2v;
@@ -241,16 +269,37 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
   }
 #pragma unroll
   for (int m = L / 2; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  float o1[8], o2[8];  // the bf16 values of the output vector, as floats
   if (rotate && ok) {
     const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(D)), p.eps));
-    float o1[8], o2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      o1[i] = __fmul_rn(round_bf16(__fmul_rn(y1[i], r)), p.scale);
-      o2[i] = __fmul_rn(round_bf16(__fmul_rn(y2[i], r)), p.scale);
+      o1[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y1[i], r)), p.scale));
+      o2[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y2[i], r)), p.scale));
     }
-    *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
-    *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
+    if (!FP8 || is_q) {  // q always goes out as bf16; fp8 cache vectors are stored below
+      *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
+      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
+    }
+  } else {
+    unpack8(x1v, o1);
+    unpack8(x2v, o2);
+  }
+  if constexpr (FP8) {
+    // every lane takes part in the amax butterfly; q vectors and idle lanes contribute nothing
+    float amax = 0.f;
+    if (ok && !is_q)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(o1[i]), fabsf(o2[i])));
+#pragma unroll
+    for (int m = L / 2; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    if (ok && !is_q) {
+      const float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
+      uint8_t* d8 = static_cast<uint8_t*>(static_cast<void*>(is_v ? p.v_cache : p.k_cache)) + cache_off;
+      *reinterpret_cast<uint2*>(d8 + 8 * sub) = e4m3x8(o1, inv);
+      *reinterpret_cast<uint2*>(d8 + HALF + 8 * sub) = e4m3x8(o2, inv);
+      if (sub == 0) (is_v ? p.v_scale : p.k_scale)[scale_off] = amax > 0.f ? __fdiv_rn(amax, 448.f) : 0.f;
+    }
   }
 }
 

@@ -289,6 +289,77 @@ int variant_launch_split(int D, int nqt, long long grid, const CUtensorMap& km, 
   MCB_DISPATCH_D(D, nqt, launch_split(grid, km, vm, p, st))
 }
 
+// The split kernel over an fp8 (e4m3) cache: half the bytes per tile, so a 4-stage ring holds as
+// many keys in flight as 2 bf16 stages; a 2-stage copy for single-wave grids as above.
+template <int D, int NQT>
+struct SplitF8Variant {
+  using Cfg = mcb::SplitAttnConfig<D, NQT, kKPW, 4, true>;
+  static constexpr auto kernel = mcb::decode_attn_split_kernel<D, NQT, kKPW, 4, true>;
+  using CfgLo = mcb::SplitAttnConfig<D, NQT, kKPW, 2, true>;
+  static constexpr auto kernel_lo = mcb::decode_attn_split_kernel<D, NQT, kKPW, 2, true>;
+
+  static int slots(bool lo, long long* out) {
+    static std::atomic<uint64_t> done_hi{0}, done_lo{0};
+    cudaError_t e = lo ? ensure_smem(kernel_lo, CfgLo::SMEM_BYTES, done_lo)
+                       : ensure_smem(kernel, Cfg::SMEM_BYTES, done_hi);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_attn_split fp8)");
+    int n = 0;
+    e = lo ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel_lo, mcb::kAttnThreads, CfgLo::SMEM_BYTES)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, mcb::kAttnThreads, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    *out = static_cast<long long>(n) * device_sm_count();
+    return MCB_OK;
+  }
+
+  static int launch(long long grid, const CUtensorMap& km, const CUtensorMap& vm, const mcb::SplitAttnParams& prm,
+                    cudaStream_t st) {
+    long long hi_slots = 0, lo_slots = 0;
+    int rc = slots(false, &hi_slots);
+    if (rc != MCB_OK) return rc;
+    rc = slots(true, &lo_slots);
+    if (rc != MCB_OK) return rc;
+    const bool lo = grid > hi_slots && grid <= lo_slots;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(mcb::kAttnThreads);
+    cfg.dynamicSmemBytes = lo ? CfgLo::SMEM_BYTES : Cfg::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+    if (prm.cluster) {
+      attrs[1].id = cudaLaunchAttributeClusterDimension;
+      attrs[1].val.clusterDim.x = static_cast<unsigned>(prm.nsplit);
+      attrs[1].val.clusterDim.y = 1;
+      attrs[1].val.clusterDim.z = 1;
+      cfg.numAttrs = 2;
+    }
+    cfg.attrs = attrs;
+    cudaError_t e = lo ? cudaLaunchKernelEx(&cfg, kernel_lo, km, vm, prm) : cudaLaunchKernelEx(&cfg, kernel, km, vm, prm);
+    g_launches++;
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split (fp8) launch");
+    if (prm.nsplit > 1 && !prm.cluster) {
+      const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
+      mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
+      g_launches++;
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split_combine launch");
+    }
+    return MCB_OK;
+  }
+};
+
+int variant_launch_split_f8(int D, int nqt, long long grid, const CUtensorMap& km, const CUtensorMap& vm,
+                            const mcb::SplitAttnParams& p, cudaStream_t st) {
+  if (D == 64) return nqt == 1 ? SplitF8Variant<64, 1>::launch(grid, km, vm, p, st)
+                               : SplitF8Variant<64, 2>::launch(grid, km, vm, p, st);
+  if (D == 128) return nqt == 1 ? SplitF8Variant<128, 1>::launch(grid, km, vm, p, st)
+                                : SplitF8Variant<128, 2>::launch(grid, km, vm, p, st);
+  return fail(MCB_ERR_UNSUPPORTED, "fp8 cache: head_dim %d (64 or 128)", D);
+}
+
 struct AttnPlan {
   int D, nqt, rows, tk, nqb, mode;
   bool cluster = false;  // split plan merged inside a cluster
@@ -318,9 +389,15 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
     return fail(MCB_ERR_INVALID_ARG,
                 "mcb_decode_attn: a ring slot needs window >= 0, window + T <= Tmax and Tmax a "
                 "multiple of 128 (window=%d T=%d Tmax=%d)", a->window, a->T, a->Tmax);
+  const bool fp8 = a->k_scale != nullptr;
+  if (fp8 && (a->v_scale == nullptr || (a->D != 64 && a->D != 128) || a->num_ctas > 0 ||
+              a->scale_tmax < a->Tmax || a->scale_tmax % 64 != 0))
+    return fail(MCB_ERR_UNSUPPORTED,
+                "mcb_decode_attn: an fp8 cache needs k_scale and v_scale, D = 64 or 128, the split "
+                "plan (num_ctas <= 0), and scale_tmax >= Tmax, a multiple of 64");
   const int G = a->Hq / a->Hkv;
   pl->D = a->D;
-  if (a->num_ctas == 0 && a->T >= kPrefillMinT && (a->D == 64 || a->D == 128)) {
+  if (!fp8 && a->num_ctas == 0 && a->T >= kPrefillMinT && (a->D == 64 || a->D == 128)) {
     pl->mode = kModePrefill;
     pl->nqt = pl->rows = pl->nqb = 0;
     pl->tk = mcb::kPfTile;
@@ -347,7 +424,7 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
   // persistent partition, whose start-up scan and cross-CTA merge are not amortised over so few
   // groups (measured on B200 at 4,096-key windows and 32k-key rows).
   const bool few_long = a->num_ctas == 0 && max_tiles > kSplitMaxTiles && base <= 128;
-  pl->mode = (a->num_ctas < 0 || few_long || (a->num_ctas == 0 && max_tiles <= kSplitMaxTiles))
+  pl->mode = (fp8 || a->num_ctas < 0 || few_long || (a->num_ctas == 0 && max_tiles <= kSplitMaxTiles))
                  ? kModeSplit
                  : kModePersistent;
   const size_t rows_out = static_cast<size_t>(a->B) * a->T * a->Hq;
@@ -423,10 +500,30 @@ int encode_cache_map(CUtensorMap* map, const void* base, int D, int Hkv, int Tma
   return MCB_OK;
 }
 
+// An e4m3 cache slot {D, Hkv, Tmax, B} (one byte per element): boxes of tk keys x one head x all D
+// bytes, 128-byte (D = 128) or 64-byte (D = 64) swizzled rows.
+int encode_cache_map_f8(CUtensorMap* map, const void* base, int D, int Hkv, int Tmax, int B, int tk) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Hkv),
+                        static_cast<cuuint64_t>(Tmax), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Hkv) * D,
+                           static_cast<cuuint64_t>(Tmax) * Hkv * D};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(D), 1u, static_cast<cuuint32_t>(tk), 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MCB_ERR_CUDA, "cuTensorMapEncodeTiled(fp8 cache) failed (CUresult %d)", (int)r);
+  return MCB_OK;
+}
+
 int check_attn_pointers(const mcb_attn_args* a, const char* who) {
   if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->out == nullptr ||
       a->cache_seqlens == nullptr)
     return fail(MCB_ERR_INVALID_ARG, "%s: NULL pointer argument", who);
+  if (a->k_scale != nullptr && (!aligned(a->k_scale, 256) || !aligned(a->v_scale, 256)))
+    return fail(MCB_ERR_ALIGNMENT, "%s: fp8 scale arrays must be 256-byte aligned", who);
   if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || !aligned(a->q, 16) ||
       !aligned(a->out, 16))
     return fail(MCB_ERR_ALIGNMENT, "%s: q, out and cache pointers must be 16-byte aligned", who);
@@ -484,10 +581,13 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
 // persistent kernel, the arrival counters) and launches.
 int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* counters, cudaStream_t st) {
   if (pl.mode == kModePrefill) return run_prefill(a, st);
+  const bool fp8 = a->k_scale != nullptr;
   CUtensorMap km, vm;
-  int rc = encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  int rc = fp8 ? encode_cache_map_f8(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk)
+               : encode_cache_map(&km, a->k_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
   if (rc != MCB_OK) return rc;
-  rc = encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
+  rc = fp8 ? encode_cache_map_f8(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk)
+           : encode_cache_map(&vm, a->v_cache, a->D, a->Hkv, a->Tmax, a->B, pl.tk);
   if (rc != MCB_OK) return rc;
   uint8_t* w = static_cast<uint8_t*>(ws);
   if (pl.mode == kModeSplit) {
@@ -511,8 +611,12 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.nsplit = pl.nsplit;
     p.tiles_per_split = pl.tps;
     p.nqb = pl.nqb;
+    p.k_scale = a->k_scale;
+    p.v_scale = a->v_scale;
+    p.scale_tmax = a->scale_tmax;
     const long long grid = static_cast<long long>(a->B) * a->Hkv * pl.nqb * pl.nsplit;
-    return variant_launch_split(a->D, pl.nqt, grid, km, vm, p, st);
+    return fp8 ? variant_launch_split_f8(a->D, pl.nqt, grid, km, vm, p, st)
+               : variant_launch_split(a->D, pl.nqt, grid, km, vm, p, st);
   }
   mcb::AttnParams p;
   p.q = static_cast<const uint16_t*>(a->q);
@@ -657,6 +761,13 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   for (int i = 0; i < 3; ++i)
     if ((rq && a->q_stride[i] < 0) || (wkv && (a->k_stride[i] < 0 || a->v_stride[i] < 0)))
       return fail(MCB_ERR_INVALID_ARG, "mcb_kv_append_rope: negative stride");
+  const bool fp8 = a->k_scale != nullptr;
+  if (fp8 && (a->v_scale == nullptr || !wkv || a->scale_tmax < a->Tmax || a->scale_tmax % 64 != 0))
+    return fail(MCB_ERR_INVALID_ARG,
+                "mcb_kv_append_rope: an fp8 cache needs WRITE_KV, k_scale and v_scale, and scale_tmax >= "
+                "Tmax, a multiple of 64");
+  if (fp8 && a->D != 64 && a->D != 128)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: an fp8 cache needs D = 64 or 128 (D=%d)", a->D);
 
   mcb::AppendParams p;
   p.q = static_cast<const uint16_t*>(a->q);
@@ -686,6 +797,9 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   p.nk = wkv ? a->Hkv : 0;
   p.rotate_k = rk;
   p.ring = a->ring != 0;
+  p.k_scale = a->k_scale;
+  p.v_scale = a->v_scale;
+  p.scale_tmax = a->scale_tmax;
   p.total_vectors = static_cast<long long>(a->B) * a->T * (p.nq + 2 * p.nk);
   if (p.total_vectors == 0) return MCB_OK;
   // 16-byte chunks when every row the kernel touches starts on a 16-byte boundary.
@@ -698,6 +812,8 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
                  aligned(a->k_cache, 16) && aligned(a->v_cache, 16);
   if (rq || rk) vec = vec && aligned(a->cos, 16) && aligned(a->sin, 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fp8 && !vec)
+    return fail(MCB_ERR_ALIGNMENT, "mcb_kv_append_rope: an fp8 cache needs 16-byte aligned rows");
   if (vec) {
     const long long vpw = 32 / (a->D / 16);
     const long long warps = (p.total_vectors + vpw - 1) / vpw;
@@ -706,11 +822,17 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
     const dim3 grid(static_cast<unsigned>(blocks)), block(mcb::kAppendWarpsPerBlock * 32);
     cudaError_t e;
     switch (a->D) {
-      case 16: e = launch_pdl(mcb::kv_append_rope_vec_kernel<16>, grid, block, 0, st, p); break;
-      case 32: e = launch_pdl(mcb::kv_append_rope_vec_kernel<32>, grid, block, 0, st, p); break;
-      case 64: e = launch_pdl(mcb::kv_append_rope_vec_kernel<64>, grid, block, 0, st, p); break;
-      case 128: e = launch_pdl(mcb::kv_append_rope_vec_kernel<128>, grid, block, 0, st, p); break;
-      default: e = launch_pdl(mcb::kv_append_rope_vec_kernel<256>, grid, block, 0, st, p); break;
+      case 16: e = launch_pdl(mcb::kv_append_rope_vec_kernel<16, false>, grid, block, 0, st, p); break;
+      case 32: e = launch_pdl(mcb::kv_append_rope_vec_kernel<32, false>, grid, block, 0, st, p); break;
+      case 64:
+        e = fp8 ? launch_pdl(mcb::kv_append_rope_vec_kernel<64, true>, grid, block, 0, st, p)
+                : launch_pdl(mcb::kv_append_rope_vec_kernel<64, false>, grid, block, 0, st, p);
+        break;
+      case 128:
+        e = fp8 ? launch_pdl(mcb::kv_append_rope_vec_kernel<128, true>, grid, block, 0, st, p)
+                : launch_pdl(mcb::kv_append_rope_vec_kernel<128, false>, grid, block, 0, st, p);
+        break;
+      default: e = launch_pdl(mcb::kv_append_rope_vec_kernel<256, false>, grid, block, 0, st, p); break;
     }
     g_launches++;
     if (e == cudaSuccess) e = cudaGetLastError();

@@ -37,8 +37,35 @@ def _bthd_strides(name, t):
     return (t.stride(0), t.stride(1), t.stride(2))
 
 
+FP8 = torch.float8_e4m3fn
+
+
+def fp8_scale_tmax(Tmax):
+    """Positions per (row, kv head) in an fp8 cache's scale arrays: T_max rounded up to 64 (a key
+    tile's scales are read as one 256-byte block)."""
+    return (int(Tmax) + 63) // 64 * 64
+
+
+def fp8_scales(B, Hkv, Tmax, device, n_slots=None):
+    """Zeroed per-vector scales for an fp8 (e4m3) cache slot: (B, Hkv, fp8_scale_tmax(Tmax))
+    fp32, or (n_slots, B, Hkv, ...) for a whole cache."""
+    shape = (B, Hkv, fp8_scale_tmax(Tmax))
+    if n_slots is not None:
+        shape = (n_slots,) + shape
+    return torch.zeros(shape, dtype=torch.float32, device=device)
+
+
+def _check_fp8_scales(name, sc, k_cache):
+    B, Tmax, Hkv, _ = k_cache.shape
+    _need(name, sc, 3, torch.float32)
+    if tuple(sc.shape) != (B, Hkv, fp8_scale_tmax(Tmax)) or not sc.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous ({B}, {Hkv}, {fp8_scale_tmax(Tmax)}) float32 tensor")
+    if sc.data_ptr() % 256:
+        raise RuntimeError(f"{name} must be 256-byte aligned")
+
+
 def _check_slot_cache(name, c, B, Hkv, D):
-    _need(name, c, 4)
+    _need(name, c, 4, c.dtype if isinstance(c, torch.Tensor) and c.dtype == FP8 else torch.bfloat16)
     if not c.is_contiguous():
         raise RuntimeError(f"{name} must be a contiguous (B, T_max, H_kv, D) cache slot")
     if c.size(0) != B or c.size(2) != Hkv or c.size(3) != D:
@@ -62,13 +89,18 @@ def rms_norm_eps(eps):
 
 
 def kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, rotate_q=True,
-                   rotate_k=True, write_kv=True, eps=None, scale=1.2, q_out=None, ring=False):
+                   rotate_k=True, write_kv=True, eps=None, scale=1.2, q_out=None, ring=False,
+                   k_scale=None, v_scale=None):
     """Fused rope + QK-norm + scale for q (and k), and the insert of k, v at each row's position.
 
     q: (B, T, Hq, D) bf16 or None; k, v: (B, T, Hkv, D) bf16 or None; k_cache/v_cache: one slot
     (B, T_max, Hkv, D); cos/sin: the rotary buffers (1, rot_len, 1, D/2) bf16 of
     modelcore.components.rotary.RotaryEmbedding.  Returns the rotated q (a new (B, T, Hq, D)
-    tensor, or q_out) when rotate_q, else None.  cache_seqlens is not advanced."""
+    tensor, or q_out) when rotate_q, else None.  cache_seqlens is not advanced.
+
+    An fp8 slot (k_cache/v_cache of dtype float8_e4m3fn, D 64 or 128) stores each new vector as
+    e4m3 with a per-vector scale in k_scale / v_scale (fp8_scales): the bf16 vector x a bf16
+    cache would hold, as e4m3(x * 448 / max|x|) and scale max|x| / 448."""
     flags = 0
     ref = q if rotate_q else k
     if ref is None:
@@ -111,6 +143,15 @@ def kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, rotate
         args.v_cache = v_cache.data_ptr()
         args.Hkv = Hkv
         args.Tmax = k_cache.size(1)
+        if (k_cache.dtype == FP8) != (v_cache.dtype == FP8):
+            raise RuntimeError("k_cache and v_cache must both be bf16 or both fp8")
+        if k_cache.dtype == FP8:
+            if k_scale is None or v_scale is None:
+                raise RuntimeError("an fp8 cache slot needs k_scale and v_scale")
+            _check_fp8_scales("k_scale", k_scale, k_cache)
+            _check_fp8_scales("v_scale", v_scale, k_cache)
+            args.k_scale, args.v_scale = k_scale.data_ptr(), v_scale.data_ptr()
+            args.scale_tmax = k_scale.size(2)
     elif rotate_k:
         raise RuntimeError("rotate_k requires write_kv")
     _check_seqlens(cache_seqlens, B, ref.device)
@@ -175,7 +216,8 @@ def kv_advance(cache_seqlens, n):
                                         cache_seqlens.numel(), int(n), _stream(cache_seqlens)))
 
 
-def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring=False):
+def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring=False,
+               k_scale=None, v_scale=None):
     _need("q", q, 4)
     B, T, Hq, D = q.shape
     Hkv = k_cache.shape[2] if k_cache.dim() == 4 else -1
@@ -197,6 +239,13 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ct
     args.softmax_scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
     args.num_ctas = int(num_ctas)
     args.ring = int(bool(ring))
+    if k_cache.dtype == FP8:
+        if v_cache.dtype != FP8 or k_scale is None or v_scale is None:
+            raise RuntimeError("an fp8 cache slot needs fp8 k_cache and v_cache, k_scale and v_scale")
+        _check_fp8_scales("k_scale", k_scale, k_cache)
+        _check_fp8_scales("v_scale", v_scale, k_cache)
+        args.k_scale, args.v_scale = k_scale.data_ptr(), v_scale.data_ptr()
+        args.scale_tmax = k_scale.size(2)
     return args
 
 
@@ -247,7 +296,8 @@ def reset_counters():
 
 
 def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None,
-                num_ctas=0, out=None, workspace=None, counters=None, ring=False):
+                num_ctas=0, out=None, workspace=None, counters=None, ring=False, k_scale=None,
+                v_scale=None):
     """softmax(q . K^T * scale) . V over each row's visible keys of one cache slot.
 
     q: (B, T, Hq, D) bf16; k_cache/v_cache: (B, T_max, Hkv, D) bf16 slot; query t of row b sits at
@@ -257,15 +307,17 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     splits (every plan gives the same result up to fp32 summation order).  workspace: uint8
     partials buffer; counters: int32 arrival counters, zero before their first use (defaults:
     the cached per-device ones).  ring: the slot is a ring of T_max positions (key c at index
-    c % T_max; needs window >= 0 and window + T <= T_max, T_max a multiple of 128).  Returns out
-    (B, T, Hq, D) bf16."""
+    c % T_max; needs window >= 0 and window + T <= T_max, T_max a multiple of 128).  An fp8 slot
+    (float8_e4m3fn, with the k_scale / v_scale kv_append_rope filled) is read as e4m3 * scale, on
+    the split plan.  Returns out (B, T, Hq, D) bf16."""
     if out is None:
         out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
     else:
         _need("out", out, 4)
         if out.shape != q.shape or not out.is_contiguous():
             raise RuntimeError("out must be a contiguous tensor shaped like q")
-    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring)
+    args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ctas, out, ring,
+                      k_scale, v_scale)
     lib = _native.load()
     need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
     ncount = int(lib.mcb_decode_attn_counter_count(ctypes.byref(args)))

@@ -231,6 +231,57 @@ def append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos_bits, sin_bits, *,
 
 
 # ---------------------------------------------------------------------------------------------
+# fp8 (e4m3) cache vectors: a cache format this build adds (the reference stores the compute
+# dtype).  Each (row, position, kv head) vector x -- the bf16 values a bf16 cache would hold -- is
+# stored as e4m3(x * fp32(448 / amax)) with scale fp32(amax / 448), amax = max |x|; amax = 0 gives
+# zeros and scale 0.  e4m3 ("fn": 1 sign, 4 exponent bits with bias 7, 3 mantissa bits, no
+# infinities, max finite 448, subnormal step 2^-9) rounded to nearest even and saturated to 448.
+def e4m3_bits(x):
+    """float32 values -> e4m3 bit patterns (uint8), round to nearest even, saturating at 448."""
+    x = np.asarray(x, dtype=np.float32).astype(np.float64)
+    neg = np.signbit(x)
+    a = np.minimum(np.abs(x), 448.0)
+    e = np.floor(np.log2(np.where(a > 0, a, 1.0)))
+    e = np.clip(e, -6, 8)
+    step = np.exp2(e - 3)                      # 3 mantissa bits; binade -6 also spans subnormals
+    q = np.minimum(np.round(a / step) * step, 448.0)   # np.round: half to even
+    qe = np.floor(np.log2(np.where(q > 0, q, 1.0)))
+    normal = q >= 2.0 ** -6
+    exp_field = np.where(normal, qe + 7, 0)
+    man = np.where(normal, q / np.exp2(qe) * 8 - 8, q / 2.0 ** -9)
+    bits = (exp_field.astype(np.int64) << 3) | np.round(man).astype(np.int64)
+    bits = np.where(q == 0, 0, bits) | (neg.astype(np.int64) << 7)
+    return bits.astype(np.uint8)
+
+
+def e4m3_value(bits):
+    """e4m3 bit patterns -> float32 values (exact; 0x7f / 0xff, the NaNs, are not produced)."""
+    b = np.asarray(bits, dtype=np.uint8).astype(np.int64)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    ef = (b >> 3) & 0xF
+    m = b & 7
+    v = np.where(ef == 0, m * 2.0 ** -9, (1 + m / 8.0) * np.exp2(ef - 7.0))
+    return (sign * v).astype(np.float32)
+
+
+def quantize_fp8(x_bits):
+    """bf16 vectors (..., D) -> (e4m3 bytes (..., D), fp32 scales (...)) as the fp8 cache's append
+    stores them."""
+    x = bf16_to_f32(x_bits)
+    amax = np.abs(x).max(axis=-1).astype(np.float32)
+    pos = amax > 0
+    inv = np.where(pos, F32(448.0) / np.where(pos, amax, F32(1.0)), F32(0.0)).astype(np.float32)
+    scale = np.where(pos, amax / F32(448.0), F32(0.0)).astype(np.float32)
+    y = (x * inv[..., None]).astype(np.float32)
+    return e4m3_bits(y), scale
+
+
+def dequantize_fp8(bytes_, scale):
+    """The values an fp8 cache vector stands for: e4m3 value x scale (float64)."""
+    return e4m3_value(bytes_).astype(np.float64) * np.asarray(scale, dtype=np.float64)[..., None]
+
+
+# ---------------------------------------------------------------------------------------------
 # KVCache.prefill / prefill_row: modelcore/cache.py:75-90, :92-119
 def prefill_broadcast(dst_k, dst_v, src_k, src_v, n_pos):
     """dst[:, :, :n_pos] = src[:, :, :n_pos] with src batch 1 broadcast (cache.py:84-85)."""

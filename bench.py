@@ -24,6 +24,8 @@ kv_read_sweep  measurement config 5 (32 q / 8 kv heads of 128, lengths U[1, 3276
            window -1 / 4096): one step = fused rope append + decode attention, timed on the device
            in CUDA graphs of consecutive steps on rotating groups of cache rows (no launch finds
            its keys in L2).
+kv_read_sweep_fp8  the same over an fp8 (e4m3) cache with per-vector scales (an opt-in cache
+           format: bytes = e4m3 keys and values + fp32 scales), with the speed-up over bf16.
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
            sample of the same workload (rank 0, N = 1).
 """
@@ -265,11 +267,13 @@ def _attention_roofline(dec, peak, reps=4):
             "frac": gbs / peak, "mean_context": keys / B, "traffic": traffic, "kernel": kernel}
 
 
-def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
+def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096), fp8=False):
     """Config 5: fused rope append + decode attention per step.  Each (batch, window) point is
     timed on the device in a CUDA graph of consecutive steps, each on a different group of cache
     rows (kc[g*B:(g+1)*B]) so that no launch finds its keys in L2 (the groups cycled through hold
-    more than the 126 MB L2 between two visits); attention alone and append + attention."""
+    more than the 126 MB L2 between two visits); attention alone and append + attention.
+    fp8: the same over an e4m3 cache with per-vector scales (bytes = e4m3 keys and values plus
+    their fp32 scales)."""
     import numpy as np
     import torch
     from modelcore_b200 import ops
@@ -278,8 +282,16 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
     g = torch.Generator(device="cuda").manual_seed(5)
     rows = []
     max_b = max(batches)
-    kc = torch.randn(max_b, Tmax, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
-    vc = torch.randn(max_b, Tmax, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    kc = torch.empty(max_b, Tmax, Hkv, D, device="cuda", dtype=ops.FP8 if fp8 else torch.bfloat16)
+    vc = torch.empty_like(kc)
+    for c in (kc, vc):
+        for r in range(0, max_b, 8):   # a few rows at a time (an fp32 draw of all would not fit)
+            c[r:r + 8] = torch.randn(c[r:r + 8].shape, device="cuda", generator=g).to(c.dtype)
+    kscl = vscl = None
+    if fp8:
+        kscl = torch.ones(max_b, Hkv, ops.fp8_scale_tmax(Tmax), device="cuda", dtype=torch.float32)
+        vscl = torch.ones_like(kscl)
+    per_key = 2 * Hkv * (D + 4) if fp8 else 2 * Hkv * D * 2
     ang = torch.arange(Tmax + 1, device="cuda", dtype=torch.float32)[:, None] * \
         (100000.0 ** (-torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))[None]
     cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
@@ -313,23 +325,27 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
         groups = max(1, min(16, max_b // B))
         kcs = [kc[i * B:(i + 1) * B] for i in range(groups)]
         vcs = [vc[i * B:(i + 1) * B] for i in range(groups)]
+        kss = [kscl[i * B:(i + 1) * B] if fp8 else None for i in range(groups)]
+        vss = [vscl[i * B:(i + 1) * B] if fp8 else None for i in range(groups)]
         for w in windows:
             keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
-            nbytes = keys * 2 * Hkv * D * 2
-            torch.cuda.nvtx.range_push(f"sweep_b{B}_w{w}")
-            qr = ops.kv_append_rope(q, k, v, kcs[0], vcs[0], sl, cos, sin)
+            nbytes = keys * per_key
+            torch.cuda.nvtx.range_push(f"sweep_b{B}_w{w}{'_fp8' if fp8 else ''}")
+            qr = ops.kv_append_rope(q, k, v, kcs[0], vcs[0], sl, cos, sin, k_scale=kss[0], v_scale=vss[0])
             out = torch.empty_like(qr)
             n = 4 * groups
 
             def attn_only():
                 for i in range(n):
-                    ops.decode_attn(qr, kcs[i % groups], vcs[i % groups], sl, window=w, out=out)
+                    j = i % groups
+                    ops.decode_attn(qr, kcs[j], vcs[j], sl, window=w, out=out, k_scale=kss[j], v_scale=vss[j])
 
             def step():
                 for i in range(n):
-                    qi = ops.kv_append_rope(q, k, v, kcs[i % groups], vcs[i % groups], sl, cos, sin,
-                                            q_out=qr)
-                    ops.decode_attn(qi, kcs[i % groups], vcs[i % groups], sl, window=w, out=out)
+                    j = i % groups
+                    qi = ops.kv_append_rope(q, k, v, kcs[j], vcs[j], sl, cos, sin, q_out=qr,
+                                            k_scale=kss[j], v_scale=vss[j])
+                    ops.decode_attn(qi, kcs[j], vcs[j], sl, window=w, out=out, k_scale=kss[j], v_scale=vss[j])
 
             ta = graph_us(attn_only, n)
             ts = graph_us(step, n)
@@ -338,9 +354,21 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096)):
             rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
                          "attn_us": round(ta, 1), "step_us": round(ts, 1),
                          "kv_gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
-    del kc, vc
+    del kc, vc, kscl, vscl
     torch.cuda.empty_cache()
     return rows
+
+
+def _with_speedup(rows8, rows16):
+    """The fp8 sweep rows with the attention speed-up over the bf16 cache at the same point."""
+    base = {(r["batch"], r["window"]): r["attn_us"] for r in rows16}
+    out = []
+    for r in rows8:
+        r = dict(r)
+        b = base.get((r["batch"], r["window"]))
+        r["speedup_vs_bf16"] = round(b / r["attn_us"], 2) if b else None
+        out.append(r)
+    return out
 
 
 def _copy_and_append(peak):
@@ -536,7 +564,9 @@ def run_sweep_only(args):
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     peak, _ = _peaks()
     rows = _kv_read_sweep(peak, batches=tuple(args.sweep_batches), windows=tuple(args.sweep_windows))
-    print(json.dumps({"kv_read_sweep": rows, "peak_gbs": peak}), flush=True)
+    rows8 = _kv_read_sweep(peak, batches=tuple(args.sweep_batches), windows=tuple(args.sweep_windows), fp8=True)
+    print(json.dumps({"kv_read_sweep": rows, "kv_read_sweep_fp8": _with_speedup(rows8, rows),
+                      "peak_gbs": peak}), flush=True)
 
 
 def run_b200(args):
@@ -604,10 +634,12 @@ def run_b200(args):
     e2e_value = B * world * args.e2e_steps / (e2e_ms * 1e-3)
 
     roof = _attention_roofline(dec, peak)
-    sweep = None
+    sweep = sweep8 = None
     if world == 1 and not args.no_sweep:
         sweep = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
                                windows=tuple(args.sweep_windows))
+        sweep8 = _with_speedup(_kv_read_sweep(peak, batches=tuple(args.sweep_batches),
+                                              windows=tuple(args.sweep_windows), fp8=True), sweep)
     copies = prefill = None
     prompt_prefill = {"workload": f"{B} prompts x {PROMPT_LEN} tokens per GPU, one forward "
                                   "(GraphDecoder batched ragged prefill)",
@@ -663,6 +695,7 @@ def run_b200(args):
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
         "kv_read_sweep": sweep,
+        "kv_read_sweep_fp8": sweep8,
         "kv_copies": copies,
         "prefill_attention": prefill,
         "prompt_prefill": prompt_prefill,

@@ -22,8 +22,8 @@ from . import _native, ops
 CACHE_ALIGN = 256
 
 
-def _aligned_zeros(shape, device):
-    t = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+def _aligned_zeros(shape, device, dtype=torch.bfloat16):
+    t = torch.zeros(shape, dtype=dtype, device=device)
     if t.numel() and t.data_ptr() % CACHE_ALIGN:
         raise RuntimeError(f"KV cache base {t.data_ptr():#x} is not {CACHE_ALIGN}-byte aligned")
     return t
@@ -35,10 +35,16 @@ class KVCache:
     128, below seq_len), position p at index p % ring_capacity, instead of seq_len; step_limit is
     then the most tokens one forward may append (ring_capacity minus the largest window of those
     layers), so every key a query can see is still resident.  The full-length slots stay in
-    k_cache / v_cache, the rings in k_ring / v_ring; get_slot_cache and slot_ring resolve a slot."""
+    k_cache / v_cache, the rings in k_ring / v_ring; get_slot_cache and slot_ring resolve a slot.
+
+    kv_format "fp8" (an extension; the reference stores the compute dtype) keeps every slot as
+    float8 e4m3 with one fp32 scale per (row, position, kv head) vector -- half the bytes a key
+    costs -- in k_scale / v_scale (n_slots, B, H_kv, T_max rounded up to 64) and k_ring_scale /
+    v_ring_scale; get_slot_scales resolves them (None, None for bf16).  The fused append
+    quantizes each new vector, the attention reads e4m3 x scale; head_dim 64 or 128."""
 
     def __init__(self, batch_size, n_kv_head, seq_len, head_dim, num_kv_slots, device, dtype,
-                 ring_slots=(), ring_capacity=0, ring_window=None):
+                 ring_slots=(), ring_capacity=0, ring_window=None, kv_format="bf16"):
         _native.load()
         device = torch.device(device)
         if device.type != "cuda":
@@ -47,6 +53,11 @@ class KVCache:
             raise RuntimeError(f"modelcore_b200.KVCache stores bf16, got {dtype}")
         if num_kv_slots and (head_dim % 8):
             raise RuntimeError(f"head_dim {head_dim} must be a multiple of 8 (16-byte cache rows)")
+        if kv_format not in ("bf16", "fp8"):
+            raise RuntimeError(f"kv_format must be 'bf16' or 'fp8', got {kv_format!r}")
+        if kv_format == "fp8" and num_kv_slots and head_dim not in (64, 128):
+            raise RuntimeError(f"an fp8 KV cache needs head_dim 64 or 128, got {head_dim}")
+        self.kv_format = kv_format
         self.batch_size = batch_size
         self.max_seq_len = seq_len
         self.n_slots = num_kv_slots
@@ -62,11 +73,19 @@ class KVCache:
         self._slots.update({x: (True, i) for i, x in enumerate(ring)})
         self.ring_capacity = ring_capacity if ring else 0
         self.step_limit = ring_capacity - ring_window if ring else None
-        self.k_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device)
-        self.v_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device)
+        store = ops.FP8 if kv_format == "fp8" else torch.bfloat16
+        self.k_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device, store)
+        self.v_cache = _aligned_zeros((len(full), batch_size, seq_len, n_kv_head, head_dim), device, store)
         rshape = (len(ring), batch_size, self.ring_capacity, n_kv_head, head_dim)
-        self.k_ring = _aligned_zeros(rshape, device)
-        self.v_ring = _aligned_zeros(rshape, device)
+        self.k_ring = _aligned_zeros(rshape, device, store)
+        self.v_ring = _aligned_zeros(rshape, device, store)
+        self.k_scale = self.v_scale = self.k_ring_scale = self.v_ring_scale = None
+        if kv_format == "fp8":
+            self.k_scale = ops.fp8_scales(batch_size, n_kv_head, seq_len, device, n_slots=len(full))
+            self.v_scale = torch.zeros_like(self.k_scale)
+            self.k_ring_scale = ops.fp8_scales(batch_size, n_kv_head, self.ring_capacity, device,
+                                               n_slots=len(ring))
+            self.v_ring_scale = torch.zeros_like(self.k_ring_scale)
         self.cache_seqlens = torch.zeros(batch_size, dtype=torch.int32, device=device)
         self._pos_uniform = 0
         self._host_lens = np.zeros(batch_size, dtype=np.int64)
@@ -99,18 +118,35 @@ class KVCache:
         """True when `slot` is a window ring (position p at index p % ring_capacity)."""
         return self._slots[slot][0]
 
+    def get_slot_scales(self, slot):
+        """The fp8 slot's (k_scale, v_scale), (B, H_kv, T_max rounded up to 64) each; (None, None)
+        for a bf16 cache."""
+        if self.kv_format != "fp8":
+            return None, None
+        is_ring, i = self._slots[slot]
+        if is_ring:
+            return self.k_ring_scale[i], self.v_ring_scale[i]
+        return self.k_scale[i], self.v_scale[i]
+
     def cache_bytes(self):
-        """Device bytes of the K and V storage."""
-        return 2 * (self.k_cache.numel() + self.k_ring.numel()) * 2
+        """Device bytes of the K and V storage (and the fp8 scales)."""
+        n = 2 * (self.k_cache.numel() + self.k_ring.numel()) * self.k_cache.element_size()
+        if self.kv_format == "fp8":
+            n += 2 * (self.k_scale.numel() + self.k_ring_scale.numel()) * 4
+        return n
 
     def _copy_slots_from(self, other, dst_row_begin, dst_row_count, n_pos, src_row=0):
         """Positions [0, n_pos) of other's row src_row into rows [dst_row_begin, +count), every
         slot, ring or not; cache_seqlens of those rows set to n_pos."""
+        assert self.kv_format == other.kv_format, "prefill between caches of different formats"
         same_layout = (not self.ring_capacity and not other.ring_capacity)
         if same_layout:
             ops.kv_copy_rows(self.k_cache, self.v_cache, other.k_cache, other.v_cache, src_row=src_row,
                              dst_row_begin=dst_row_begin, dst_row_count=dst_row_count, n_pos=n_pos,
                              dst_seqlens=self.cache_seqlens)
+            if self.kv_format == "fp8":
+                self._copy_scales(self.k_scale, self.v_scale, other.k_scale, other.v_scale, src_row,
+                                  dst_row_begin, dst_row_count, n_pos)
             return
         for slot in range(self.n_slots):
             d_ring, di = self._slots[slot]
@@ -127,7 +163,19 @@ class KVCache:
             ops.kv_copy_rows(dk[di:di + 1], dv[di:di + 1], sk[si:si + 1], sv[si:si + 1],
                              src_row=src_row, dst_row_begin=dst_row_begin,
                              dst_row_count=dst_row_count, n_pos=n, dst_seqlens=None)
+            if self.kv_format == "fp8":
+                dks, dvs = (self.k_ring_scale, self.v_ring_scale) if d_ring else (self.k_scale, self.v_scale)
+                sks, svs = (other.k_ring_scale, other.v_ring_scale) if s_ring else (other.k_scale, other.v_scale)
+                self._copy_scales(dks[di:di + 1], dvs[di:di + 1], sks[si:si + 1], svs[si:si + 1], src_row,
+                                  dst_row_begin, dst_row_count, n)
         self.cache_seqlens[dst_row_begin:dst_row_begin + dst_row_count] = n_pos
+
+    @staticmethod
+    def _copy_scales(dk, dv, sk, sv, src_row, dst_row_begin, dst_row_count, n_pos):
+        """The fp8 scales of positions [0, n_pos) of row src_row into the destination rows."""
+        rows = slice(dst_row_begin, dst_row_begin + dst_row_count)
+        dk[:, rows, :, :n_pos] = sk[:, src_row:src_row + 1, :, :n_pos]
+        dv[:, rows, :, :n_pos] = sv[:, src_row:src_row + 1, :, :n_pos]
 
     def advance(self, num_tokens):
         """cache_seqlens += num_tokens on the device, and the host mirrors with it

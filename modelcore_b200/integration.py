@@ -44,6 +44,7 @@ def attend(self, q, k, v, kv_cache):
     row's position, then the decode attention over the slot.  Returns y (B, T, Hq, D)."""
     T = q.size(1)
     k_cache, v_cache = kv_cache.get_slot_cache(self.kv_slot)
+    k_scale, v_scale = kv_cache.get_slot_scales(self.kv_slot)
     ring = kv_cache.slot_ring(self.kv_slot)
     seqlens = kv_cache.cache_seqlens
     rope = self.rope
@@ -51,12 +52,13 @@ def attend(self, q, k, v, kv_cache):
     if self.produces_kv:
         q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
                                rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,
-                               scale=1.2, ring=ring)
+                               scale=1.2, ring=ring, k_scale=k_scale, v_scale=v_scale)
     else:
         q = ops.kv_append_rope(q, None, None, None, None, seqlens, rope.cos, rope.sin,
                                rotate_q=True, rotate_k=False, write_kv=False,
                                eps=self.norm.eps, scale=1.2)
-    return ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window, ring=ring)
+    return ops.decode_attn(q, k_cache, v_cache, seqlens, window=self.window, ring=ring,
+                           k_scale=k_scale, v_scale=v_scale)
 
 
 def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
@@ -87,6 +89,9 @@ def attention_forward(self, x, idx, kv_cache, kv_bus=None, doc_args=None):
     if ring and not fused:
         raise RuntimeError("a window-ring KV cache needs modelcore's RotaryEmbedding + RMSNorm "
                            "attention (the fused append); build the cache without rings")
+    if getattr(kv_cache, "kv_format", "bf16") == "fp8" and not fused:
+        raise RuntimeError("an fp8 KV cache needs modelcore's RotaryEmbedding + RMSNorm attention "
+                           "(the fused append quantizes); build the cache as bf16")
     if fused:
         if self.produces_kv:
             if qkv is None:
@@ -185,6 +190,9 @@ class _ManagerMixin:
     # cache memory in proportion to the window instead of the sequence length.  Off by default:
     # it needs the fused decode forward (chunked prefill) and is a layout modelcore does not have.
     ring_window = False
+    # new_kv_cache's storage: "bf16" (modelcore's layout) or "fp8" (e4m3 with per-vector scales:
+    # half the cache memory; an extension with its own parity rules)
+    kv_format = "bf16"
 
     def create_model(self, *args, **kwargs):
         model = super().create_model(*args, **kwargs)
@@ -208,7 +216,8 @@ class _ManagerMixin:
         if ring_slots and not step.decode_installed(model):
             raise RuntimeError("window rings need the fused decode forward (install with fuse_step)")
         return KVCache(batch_size=batch_size, seq_len=seq_len, device=device, dtype=torch.bfloat16,
-                       ring_slots=ring_slots, ring_capacity=cap, ring_window=wmax, **spec)
+                       ring_slots=ring_slots, ring_capacity=cap, ring_window=wmax,
+                       kv_format=self.kv_format, **spec)
 
     def new_decoder(self, model, tokens, *, num_samples=1, max_tokens=None, device=None,
                     cuda_graph=False, batched_prefill=True):

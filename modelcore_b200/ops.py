@@ -185,6 +185,10 @@ def kv_copy_rows(dst_k, dst_v, src_k, src_v, *, src_row, dst_row_begin, dst_row_
     """Copies positions [0, n_pos) of source row src_row, every slot, into destination rows
     [dst_row_begin, dst_row_begin + dst_row_count); optionally sets dst_seqlens for those rows.
     Caches are full (n_slots, B, T_max, Hkv, D) tensors."""
+    if dst_k.dtype == FP8:  # e4m3 bytes move as pairs: the same kernel on a bf16 view
+        if not all(t.dtype == FP8 for t in (dst_v, src_k, src_v)):
+            raise RuntimeError("k and v caches must all be fp8 or all bf16")
+        dst_k, dst_v, src_k, src_v = (t.view(torch.bfloat16) for t in (dst_k, dst_v, src_k, src_v))
     for name, t in (("dst_k", dst_k), ("dst_v", dst_v), ("src_k", src_k), ("src_v", src_v)):
         _need(name, t, 5)
         if not t.is_contiguous():

@@ -172,3 +172,20 @@ def test_sampling_candidates_match_the_reference_topk_softmax(top_k, T):
     x[[3, 50, 77]] = 1.0
     order, _ = O.sample_candidates(x, 1.0, 5)
     assert order.tolist() == [3, 50, 77, 0, 1]
+
+
+def test_e4m3_rounding_matches_torch_float8():
+    """The oracle's e4m3 encoding (round to nearest even, saturating at 448; the fp8 cache's
+    format) agrees with torch's float8_e4m3fn conversion across normals, subnormals and ties,
+    and its known values: 448, 1, the smallest subnormal, ties to even, saturation."""
+    import torch
+    rng = np.random.default_rng(0)
+    y = (rng.standard_normal(200000) * np.exp2(rng.integers(-12, 9, 200000))).astype(np.float32)
+    y = np.clip(y, -448, 448)
+    want = torch.from_numpy(y).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(O.e4m3_bits(y), want)
+    x = np.array([448, -448, 1.0, 2 ** -9, 0.0, 500, 1.0625, 2 ** -10, 3 * 2 ** -10, 232], dtype=np.float32)
+    assert O.e4m3_bits(x).tolist() == [0x7E, 0xFE, 0x38, 0x01, 0x00, 0x7E, 0x38, 0x00, 0x02, 0x76]
+    assert np.array_equal(O.e4m3_value(O.e4m3_bits(y)), torch.from_numpy(want).view(torch.float8_e4m3fn).float().numpy())
+    b, s = O.quantize_fp8(O.f32_to_bf16(np.array([[0.5, -3.0, 1.25], [0.0, 0.0, 0.0]], dtype=np.float32)))
+    assert s.tolist() == [np.float32(3.0) / np.float32(448.0), 0.0] and b[0, 1] == 0xFE and not b[1].any()

@@ -15,7 +15,8 @@ hot path; the sampled tokens are gathered with NCCL at the end of the timed regi
 value      64*N*K / max-over-ranks(device time of K CUDA-graph replays), tokens/s; the graph
            feeds each step's greedy token to the next on the device.
 e2e        the same through the public step_greedy() call: per step a pinned host->device copy of the
-           token column, the replayed step, and the device->host read of the greedy tokens.
+           token column, the replayed step, and the device->host read of the greedy tokens; over
+           the same contexts as `value` (the rows are rewound to where the timed steps began).
 roofline   the decode-attention kernel: algorithmic KV bytes (exact keys per row and layer,
            2*Hkv*D*2 bytes each) / its mean launch time, timed with CUDA events on its stream
            over the 12 cache slots in rotation (1.6 GB, far above L2), against the measured HBM
@@ -578,7 +579,7 @@ def run_b200(args):
     from modelcore_b200 import ops
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
-    steps_needed = 1 + args.warmup + args.steps + args.e2e_steps + 2
+    steps_needed = 1 + args.warmup + max(args.steps, args.e2e_steps or 0) + 2
     mgr, model, dec = _build_decoder(rank, world, steps_needed, fuse_step=args.step == "fused")
     cache = dec.kv_cache
     B = cache.batch_size
@@ -616,8 +617,12 @@ def run_b200(args):
 
     # e2e: the public GraphDecoder.step_greedy() -- host token column in through pinned memory,
     # the forward, the greedy pick, the next tokens back in pinned memory and read on the host,
-    # every step
+    # every step -- over the same context range as the timed steps: the rows are rewound to
+    # where the timed region began (less the two untimed calls below); the positions decoded
+    # again are overwritten by the steps' own appends, and no kernel reads past a row's length
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
     with torch.inference_mode():
+        cache.set_row_lengths(ctx_before - 2)
         host_tok = torch.argmax(dec.logits, dim=-1).cpu()
         for _ in range(2):  # the first call captures its graph: keep that out of the timing
             host_tok = dec.step_greedy(host_tok).clone()
@@ -625,13 +630,13 @@ def run_b200(args):
         t0 = time.perf_counter()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
-        for _ in range(args.e2e_steps):
+        for _ in range(e2e_steps):
             host_tok = dec.step_greedy(host_tok)
         f1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
-    e2e_value = B * world * args.e2e_steps / (e2e_ms * 1e-3)
+    e2e_value = B * world * e2e_steps / (e2e_ms * 1e-3)
 
     roof = _attention_roofline(dec, peak)
     sweep = sweep8 = None
@@ -708,7 +713,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="steps of the end-to-end loop (default: --steps, over the same contexts)")
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--step", choices=("fused", "plain"), default="fused",
                     help="decode step around attention: fused (default) or modelcore's op-by-op")

@@ -24,9 +24,10 @@
 //     hundreds -- the per-instruction cost of tcgen05.mma with M = 128, N = 16 (measured about
 //     0.38 us per 64 columns of K) exceeds the whole product on mma.sync (about 2 clocks per
 //     m16n8k16 per SM, 0.4 us for 64 x 16 x 768);
-//   * norm: once all panels are resident each warp takes two rows at a time and computes their
-//     fp32 sums of squares in the fixed order mcb_add_rms_norm uses (step_fused.cuh
-//     row_rms_rsqrt: chunk, 8-chunk panel tree, panels in order), then rescales them in place;
+//   * norm: once all panels are resident the 8 warps take all 64 rows at once (four lanes a row)
+//     and compute their fp32 sums of squares in the fixed order mcb_add_rms_norm uses
+//     (step_fused.cuh row_rms_rsqrt: chunk, 8-chunk panel tree, panels in order), then rescale
+//     them in place;
 //   * epilogue: round once to bf16 (residual: add the residual row, round again, as torch's
 //     `x + y` does) and store 16 bytes a thread.
 //
@@ -42,7 +43,7 @@ namespace mcb {
 constexpr int kProjThreads = 256;
 constexpr int kProjWarps = kProjThreads / 32;
 constexpr int kProjRows = 64;        // rows of the activation block (R <= 64)
-constexpr int kProjNormCpl = 4;      // the norm: panels a lane group covers (K <= 4 * 4 * 64)
+constexpr int kProjNormCpl = 4;      // the norm takes K <= 4 * 4 * 64 (as mcb_add_rms_norm's limit)
 constexpr int kProjPanel = kProjRows * 128;  // one 64-column activation panel, bytes
 
 struct ProjParams {
@@ -127,87 +128,63 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   if constexpr (NORM) {
     for (int i = 0; i < panels; ++i) ok = ok && mbar_wait_or_abort(&full[i], 0, abort_flag);
     ok = __syncthreads_and(ok);
-    // One pass over the rows, two rows a warp at a time (independent dependency chains): lane
-    // (g, c) = (lane / 8, lane % 8) holds chunk c of panels g, g + 4, g + 8, g + 12.  X' = X +
-    // delta (add + norm; CTA 0 writes it out), each chunk's sum of squares element by element,
-    // the 8-chunk panel tree over the lanes of a group, then every panel's partial gathered to
-    // every lane and added in panel order -- row_rms_rsqrt's order -- and the row rescaled.
-    const int g = lane >> 3, c = lane & 7;
+    // All 64 rows in one pass: warp w takes rows 8w .. 8w+7, four lanes a row; lane `sub` holds
+    // chunks 2 sub and 2 sub + 1 of every 64-column panel.  The fp32 sum of squares keeps
+    // row_rms_rsqrt's order (step_fused.cuh): each chunk element by element, the panel's
+    // pairwise tree -- its first level in the lane, the next two over xor 1 and 2 among the four
+    // lanes -- and the panels in order, which every lane of the row adds identically.  Chunks
+    // {2 sub, 2 sub + 1} of two consecutive rows land in disjoint swizzled slots: no bank
+    // conflicts.  add + norm first writes X' = X + delta (CTA 0 also to x_out).
+    const int r = warp * 8 + (lane >> 2), sub = lane & 3;
     const uint32_t xs_addr = smem_u32(xsm), ds_addr = smem_u32(dsm);
-    for (int r0 = warp * 2; ok && r0 < kProjRows; r0 += kProjWarps * 2) {
-      uint32_t xw[2][kProjNormCpl][4];
-      float part[2][kProjNormCpl];
+    float acc = 0.f;
+    for (int pl = 0; pl < panels; ++pl) {
+      float part[2];
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int r = r0 + t;
+      for (int h = 0; h < 2; ++h) {
+        const int c = 2 * sub + h;
+        const uint32_t off = pl * kProjPanel + swz128(r, c);
+        uint4 xv = ok ? lds128(xs_addr + off) : make_uint4(0, 0, 0, 0);
+        uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        if (ADD && ok) {
+          const uint4 dv = lds128(ds_addr + off);
+          const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-        for (int j = 0; j < kProjNormCpl; ++j) {
-          const int pl = g + 4 * j;
-          part[t][j] = 0.f;
-          if (pl < panels) {
-            const uint32_t off = pl * kProjPanel + swz128(r, c);
-            const uint4 xv = lds128(xs_addr + off);
-            xw[t][j][0] = xv.x; xw[t][j][1] = xv.y; xw[t][j][2] = xv.z; xw[t][j][3] = xv.w;
-            if (ADD) {
-              const uint4 dv = lds128(ds_addr + off);
-              const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                xw[t][j][k] = pack_bf16x2(
-                    __fadd_rn(__uint_as_float(xw[t][j][k] << 16), __uint_as_float(dw[k] << 16)),
-                    __fadd_rn(__uint_as_float(xw[t][j][k] & 0xffff0000u), __uint_as_float(dw[k] & 0xffff0000u)));
-              if (blockIdx.x == 0 && r < p.R)
-                *reinterpret_cast<uint4*>(p.x_out + static_cast<long long>(r) * p.xos + pl * 64 + c * 8) =
-                    make_uint4(xw[t][j][0], xw[t][j][1], xw[t][j][2], xw[t][j][3]);
-            }
-            float sq = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float e0 = __uint_as_float(xw[t][j][k] << 16);
-              const float e1 = __uint_as_float(xw[t][j][k] & 0xffff0000u);
-              sq = __fadd_rn(sq, __fmul_rn(e0, e0));
-              sq = __fadd_rn(sq, __fmul_rn(e1, e1));
-            }
-            part[t][j] = sq;
-          }
+          for (int k = 0; k < 4; ++k)
+            xw[k] = pack_bf16x2(__fadd_rn(__uint_as_float(xw[k] << 16), __uint_as_float(dw[k] << 16)),
+                                __fadd_rn(__uint_as_float(xw[k] & 0xffff0000u), __uint_as_float(dw[k] & 0xffff0000u)));
+          xv = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+          sts128(xs_addr + off, xv);
+          if (blockIdx.x == 0 && r < p.R)
+            *reinterpret_cast<uint4*>(p.x_out + static_cast<long long>(r) * p.xos + pl * 64 + c * 8) = xv;
         }
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float e0 = __uint_as_float(xw[k] << 16), e1 = __uint_as_float(xw[k] & 0xffff0000u);
+          sq = __fadd_rn(sq, __fmul_rn(e0, e0));
+          sq = __fadd_rn(sq, __fmul_rn(e1, e1));
+        }
+        part[h] = sq;
       }
+      float t = __fadd_rn(part[0], part[1]);
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+      acc = __fadd_rn(acc, t);
+    }
+    const float sc = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.K)), p.eps));
+    for (int pl = 0; ok && pl < panels; ++pl) {  // h = bf16(X' * scale) in place
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t a = xs_addr + pl * kProjPanel + swz128(r, 2 * sub + h);
+        const uint4 v = lds128(a);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < kProjNormCpl; ++j) {
-          float v = part[t][j];
-          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-          part[t][j] = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-        }
-      float acc[2] = {0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < kProjNormCpl; ++j)
-#pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {  // panel 4j + gg, in order
-          const float p0 = __shfl_sync(0xffffffffu, part[0][j], gg * 8);
-          const float p1 = __shfl_sync(0xffffffffu, part[1][j], gg * 8);
-          if (4 * j + gg < panels) {
-            acc[0] = __fadd_rn(acc[0], p0);
-            acc[1] = __fadd_rn(acc[1], p1);
-          }
-        }
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const float sc = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc[t], static_cast<float>(p.K)), p.eps));
-#pragma unroll
-        for (int j = 0; j < kProjNormCpl; ++j) {
-          const int pl = g + 4 * j;
-          if (pl < panels) {
-            uint32_t o[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              o[k] = pack_bf16x2(__fmul_rn(__uint_as_float(xw[t][j][k] << 16), sc),
-                                 __fmul_rn(__uint_as_float(xw[t][j][k] & 0xffff0000u), sc));
-            sts128(xs_addr + pl * kProjPanel + swz128(r0 + t, c), make_uint4(o[0], o[1], o[2], o[3]));
-          }
-        }
+        for (int k = 0; k < 4; ++k)
+          o[k] = pack_bf16x2(__fmul_rn(__uint_as_float(w[k] << 16), sc),
+                             __fmul_rn(__uint_as_float(w[k] & 0xffff0000u), sc));
+        sts128(a, make_uint4(o[0], o[1], o[2], o[3]));
       }
     }
     __syncthreads();

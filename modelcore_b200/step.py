@@ -98,8 +98,9 @@ def packed_weight(owner, key, linears):
 # and the residual adds fused around them (body_forward_proj: 7 launches a layer instead of 9);
 # down_proj (K = the MLP width) and prefill-sized blocks of rows use cuBLAS (F.linear).  Off by
 # default: the plain projection matches cuBLAS at 64 rows (3.1-3.5 us in a CUDA graph), but the
-# fused norm costs about 7 us inside it -- 64 rows' dependent reduction chains on 8 warps --
-# against 2.6 us for the stand-alone kernel (config 2: 81k vs 102k tokens/s).
+# fused norm costs about 5 us inside it -- every panel must land before it starts, and the 64
+# rows' reductions share one CTA -- against 2.6 us for the stand-alone kernel (config 2: 87k vs
+# 100k tokens/s).
 USE_FUSED_PROJ = False
 
 

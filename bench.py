@@ -27,6 +27,9 @@ kv_read_sweep  measurement config 5 (32 q / 8 kv heads of 128, lengths U[1, 3276
            its keys in L2).
 kv_read_sweep_fp8  the same over an fp8 (e4m3) cache with per-vector scales (an opt-in cache
            format: bytes = e4m3 keys and values + fp32 scales), with the speed-up over bf16.
+gqa_decode measurement configs 3 and 4 (the 24 x 2048 GQA model with windows; config 4 with
+           cross-layer KV sharing, a broadcast prefill and top-k sampling): a bounded sample of
+           their decode steps through ModelManager, tokens/s and the KV bytes read per second.
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
            sample of the same workload (rank 0, N = 1).
 """
@@ -372,6 +375,72 @@ def _with_speedup(rows8, rows16):
     return out
 
 
+def _gqa_decode(config, steps=64):
+    """Configs 3 and 4 on one GPU, a bounded sample of their decode runs (the full runs are 1024
+    and 256 steps): the 24-block GQA model (16 q / 4 kv heads of 128, windows of 1024 on three
+    layers of four), bf16 random-init weights (seed 0), through ModelManager and the CUDA-graph
+    decoder.  Config 3: 128 prompts of U[1024, 8192] tokens (seed 2), prefilled one by one
+    (prefill_row), `steps` greedy steps.  Config 4: odd layers read the preceding even layer's
+    slot; one 4,096-token prompt (seed 3) prefilled once and broadcast to 256 rows, `steps`
+    steps sampled at temperature 1.0, top_k 50 (seed 4).  kv_gbs: the KV bytes the step's
+    attention reads (every layer, its visible keys) / the step time."""
+    import numpy as np
+    import torch
+    import modelcore_b200
+    from modelcore_b200 import workloads
+    mgr = modelcore_b200.ModelManager()
+    model = mgr.create_model(workloads.gqa_window_config(kv_share=(config == 4)), device=torch.device("cuda"),
+                             seed=0).to(torch.bfloat16).eval()
+    blocks = model.body.blocks
+    windows = [b.mixer.window for b in blocks]
+    Hkv, D = blocks[0].mixer.n_kv_head, blocks[0].mixer.head_dim
+    stream = torch.cuda.current_stream()
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        if config == 3:
+            lens = torch.randint(1024, 8193, (128,), generator=torch.Generator().manual_seed(2))
+            toks = workloads.prompts(128, 8192, seed=2)
+            prompts = [toks[i, :int(lens[i])].tolist() for i in range(128)]
+            dec = mgr.new_decoder(model, prompts, max_tokens=steps + 8, cuda_graph=True, batched_prefill=False)
+        else:
+            prompt = workloads.prompts(1, 4096, seed=3)[0].tolist()
+            dec = mgr.new_decoder(model, [prompt], num_samples=256, max_tokens=steps + 8, cuda_graph=True)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        gen = torch.Generator(device="cuda").manual_seed(4)
+
+        def run(n):
+            if config == 3:
+                dec.greedy_steps(n)
+            else:
+                dec.sample_steps(n, temperature=1.0, top_k=50, generator=gen)
+
+        run(3)  # eager step, graph capture, one replay
+        before = dec.kv_cache.host_lens().astype(np.int64)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    B = int(before.size)
+    keys = 0
+    for i in range(steps):
+        L = before + i  # the new token's position
+        for w in windows:
+            keys += int(np.minimum(L + 1, w + 1).sum()) if w >= 0 else int((L + 1).sum())
+    kv_bytes = keys * 2 * Hkv * D * 2
+    out = {"workload": f"config {config}: 24 x 2048 GQA (16/4 heads of 128, window 1024 on 3 of 4 layers"
+                       + (", odd layers sharing the even layer's slot" if config == 4 else "")
+                       + f"), {B} rows, {steps} of the run's decode steps",
+           "rows": B, "mean_context": round(float(before.mean()) + steps / 2, 1),
+           "tokens_per_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 3),
+           "kv_gbs": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "prefill_s": round(prefill_s, 2)}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def _copy_and_append(peak):
     """Piece 2 and piece 1 against the HBM copy roofline.
 
@@ -649,9 +718,11 @@ def run_b200(args):
     prompt_prefill = {"workload": f"{B} prompts x {PROMPT_LEN} tokens per GPU, one forward "
                                   "(GraphDecoder batched ragged prefill)",
                       "batched_ms": round(dec.prefill_ms, 2)}
+    gqa = None
     if world == 1 and not args.no_sweep:
         copies = _copy_and_append(peak)
         prefill = _prefill(_bf16_peak())
+        gqa = [_gqa_decode(3), _gqa_decode(4)]
         from modelcore_b200 import workloads
         mine = workloads.prompts(ROWS_PER_GPU, PROMPT_LEN, seed=1).tolist()
         prompt_prefill["per_prompt_ms"] = round(_per_prompt_prefill_ms(mgr, model, mine), 2)
@@ -701,6 +772,7 @@ def run_b200(args):
         "cpu_baseline": cpu,
         "kv_read_sweep": sweep,
         "kv_read_sweep_fp8": sweep8,
+        "gqa_decode": gqa,
         "kv_copies": copies,
         "prefill_attention": prefill,
         "prompt_prefill": prompt_prefill,
@@ -726,6 +798,8 @@ def main():
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the prefill-attention measurements")
+    ap.add_argument("--gqa-only", action="store_true",
+                    help="run only the config-3 / config-4 decode measurements")
     ap.add_argument("--sweep-batches", type=int, nargs="+", default=[1, 8, 64, 256, 512])
     ap.add_argument("--sweep-windows", type=int, nargs="+", default=[-1, 4096])
     args = ap.parse_args()
@@ -737,6 +811,11 @@ def main():
         run_sweep_only(args)
     elif args.prefill_only:
         run_prefill_only(args)
+    elif args.gqa_only:
+        import torch
+        _ensure_modelcore()
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        print(json.dumps({"gqa_decode": [_gqa_decode(3), _gqa_decode(4)]}), flush=True)
     else:
         run_b200(args)
         import torch.distributed as dist

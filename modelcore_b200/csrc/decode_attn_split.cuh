@@ -39,6 +39,10 @@ struct SplitAttnParams {
 };
 
 
+// The most key splits of a row group that merge inside one thread-block cluster (clusters above
+// the portable 8 need the non-portable size, which the host checks the device schedules).
+constexpr int kMaxClusterSplits = 16;
+
 template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
 struct SplitAttnConfig {
   static constexpr int kRows = 8 * NQT;                      // query rows per CTA
@@ -63,9 +67,9 @@ struct SplitAttnConfig {
   static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
   static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
   // cluster merge: this CTA's merged partial [kRows][D], its per-row log2-sum-exp and the
-  // per-row weights of up to 8 ranks, after the per-warp merge buffer
+  // per-row weights of up to kMaxClusterSplits ranks, after the per-warp merge buffer
   static constexpr int CL_OFFSET = (MERGE_BYTES + 15) & ~15;
-  static constexpr int CL_BYTES = kRows * D * 4 + kRows * 4 + kRows * 8 * 4;
+  static constexpr int CL_BYTES = kRows * D * 4 + kRows * 4 + kRows * kMaxClusterSplits * 4;
   static constexpr int BODY_BYTES =
       RING_BYTES > CL_OFFSET + CL_BYTES ? RING_BYTES : CL_OFFSET + CL_BYTES;
   static constexpr int SCR_OFFSET = BODY_BYTES;
@@ -150,8 +154,12 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
   const int kb = (min(lo, hi) / C::TK) * C::TK;
   const int ntiles = (hi - kb) / C::TK + 1;
-  const int tile0 = split * p.tiles_per_split;
-  const int my_tiles = max(0, min(ntiles - tile0, p.tiles_per_split));
+  // The host sizes the splits for the longest possible row (tiles_per_split); a shorter row is
+  // cut by its own length into nsplit parts of at least min(8, tiles_per_split) tiles, so that
+  // the splits of a long row all share its keys while a short row's keys stay in a few CTAs.
+  const int tps = max((ntiles + p.nsplit - 1) / p.nsplit, min(8, p.tiles_per_split));
+  const int tile0 = split * tps;
+  const int my_tiles = max(0, min(ntiles - tile0, tps));
 
   if (my_tiles == 0 && !p.cluster) {  // an empty split: its partial carries no weight
     if (threadIdx.x < C::kRows) {
@@ -524,27 +532,27 @@ __global__ void __launch_bounds__(kAttnThreads)
   // ---- cluster merge: rank q (= split) writes rows n = q, q + nsplit, .. of the row group ----
   float* cpart = reinterpret_cast<float*>(smem + C::CL_OFFSET);
   float* clse = cpart + C::kRows * D;
-  float* cw = clse + C::kRows;  // [kRows][8]
+  float* cw = clse + C::kRows;  // [kRows][kMaxClusterSplits]
   cluster_sync();  // every rank's partial and lse are written
   const int ns = p.nsplit;
   if (threadIdx.x < C::kRows && static_cast<int>(threadIdx.x) % ns == split) {
     const int n = threadIdx.x;
-    float l[8];
+    float l[kMaxClusterSplits];
     float mmax = -CUDART_INF_F;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < kMaxClusterSplits; ++q) {
       l[q] = q < ns ? ld_dsmem_f32(map_to_rank(clse + n, static_cast<uint32_t>(q))) : -CUDART_INF_F;
       mmax = fmaxf(mmax, l[q]);
     }
     float wsum = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < kMaxClusterSplits; ++q) {
       l[q] = (l[q] == -CUDART_INF_F) ? 0.f : fast_exp2(l[q] - mmax);
       wsum += l[q];
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) cw[n * 8 + q] = l[q] * inv;
+    for (int q = 0; q < kMaxClusterSplits; ++q) cw[n * kMaxClusterSplits + q] = l[q] * inv;
   }
   __syncthreads();
   const int my_rows = (C::kRows - split + ns - 1) / ns;
@@ -554,8 +562,8 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int r = r0 + n;
     float o = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
-      if (q < ns) o = fmaf(cw[n * 8 + q], ld_dsmem_f32(map_to_rank(cpart + n * D + d, static_cast<uint32_t>(q))), o);
+    for (int q = 0; q < kMaxClusterSplits; ++q)
+      if (q < ns) o = fmaf(cw[n * kMaxClusterSplits + q], ld_dsmem_f32(map_to_rank(cpart + n * D + d, static_cast<uint32_t>(q))), o);
     if (r < r1) {
       const int t = r / p.G, h = kvh * p.G + r % p.G;
       p.out[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);

@@ -88,6 +88,46 @@ cudaError_t ensure_smem(K kernel, int bytes, std::atomic<uint64_t>& done) {
   return e;
 }
 
+// Whether clusters of n CTAs of `kernel` (shared-memory limit already raised) can be resident on
+// the current device; a size above the portable 8 is allowed on the kernel first.
+template <typename K>
+bool cluster_fits(K kernel, int smem, int n) {
+  if (n > 8 && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n));
+  cfg.blockDim = dim3(mcb::kAttnThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(n);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return clusters > 0;
+}
+
+// Caches a per-device answer (0 = not yet known); `compute` runs once per device.
+template <typename F>
+int per_device(int (&cache)[64], std::mutex& mu, F compute) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) cache[dev] = compute();
+  return cache[dev];
+}
+
 // Launches `kernel` with programmatic stream serialization: it may start while the kernel ahead
 // in the stream finishes (every kernel of this library calls pdl_wait() before reading anything
 // another kernel wrote).
@@ -184,6 +224,21 @@ struct AttnVariant {
     if (dev >= 0 && dev < 64) cache[lo][dev] = slots;
     *out = slots;
     return MCB_OK;
+  }
+
+  // The most splits merged inside one cluster: kMaxClusterSplits where the device schedules
+  // clusters of that size of both split kernels, else the portable 8 (also without a device).
+  static int max_cluster() {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    const int n = per_device(cache, mu, [] {
+      long long s = 0;
+      const bool ok = split_slots(false, &s) == MCB_OK && split_slots(true, &s) == MCB_OK &&
+                      cluster_fits(split_kernel, SplitCfg::SMEM_BYTES, mcb::kMaxClusterSplits) &&
+                      cluster_fits(split_kernel_lo, SplitCfgLo::SMEM_BYTES, mcb::kMaxClusterSplits);
+      return ok ? mcb::kMaxClusterSplits : 8;
+    });
+    return n > 0 ? n : 8;
   }
 
   // Raises the persistent kernel's shared-memory limit on the current device (once) and returns
@@ -312,6 +367,19 @@ struct SplitF8Variant {
     return MCB_OK;
   }
 
+  static int max_cluster() {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    const int n = per_device(cache, mu, [] {
+      long long s = 0;
+      const bool ok = slots(false, &s) == MCB_OK && slots(true, &s) == MCB_OK &&
+                      cluster_fits(kernel, Cfg::SMEM_BYTES, mcb::kMaxClusterSplits) &&
+                      cluster_fits(kernel_lo, CfgLo::SMEM_BYTES, mcb::kMaxClusterSplits);
+      return ok ? mcb::kMaxClusterSplits : 8;
+    });
+    return n > 0 ? n : 8;
+  }
+
   static int launch(long long grid, const CUtensorMap& km, const CUtensorMap& vm, const mcb::SplitAttnParams& prm,
                     cudaStream_t st) {
     long long hi_slots = 0, lo_slots = 0;
@@ -359,6 +427,15 @@ int variant_launch_split_f8(int D, int nqt, long long grid, const CUtensorMap& k
   if (D == 128) return nqt == 1 ? SplitF8Variant<128, 1>::launch(grid, km, vm, p, st)
                                 : SplitF8Variant<128, 2>::launch(grid, km, vm, p, st);
   return fail(MCB_ERR_UNSUPPORTED, "fp8 cache: head_dim %d (64 or 128)", D);
+}
+
+// The most key splits of one row group merged inside a cluster for this kernel family.
+int variant_max_cluster(int D, int nqt, bool fp8) {
+  if (fp8) {
+    if (D == 64) return nqt == 1 ? SplitF8Variant<64, 1>::max_cluster() : SplitF8Variant<64, 2>::max_cluster();
+    return nqt == 1 ? SplitF8Variant<128, 1>::max_cluster() : SplitF8Variant<128, 2>::max_cluster();
+  }
+  MCB_DISPATCH_D(D, nqt, max_cluster())
 }
 
 struct AttnPlan {
@@ -437,23 +514,40 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
       nsplit = base <= 16 ? static_cast<int>(std::max<long long>(2, std::min<long long>(16, max_tiles / 8)))
                           : static_cast<int>(std::max<long long>(2, std::min<long long>(4, max_tiles / 16)));
     } else {
-      const long long target = 4ll * device_sm_count();
-      nsplit = base > 0 ? static_cast<int>(std::min<long long>((target + base - 1) / base, max_tiles)) : 1;
-      nsplit = std::max(1, std::min<int>(nsplit, std::max<long long>(1, max_tiles / 4)));
-      // an fp8 cache has no persistent plan: rows of thousands of keys in many groups are cut
-      // into CTAs of at most kSplitMaxTiles - 1 tiles so that uneven row lengths still balance
-      // over the waves (measured: config 5 at batch 64, full context, 943 -> 611 us; windows of
-      // 4,096 keys run faster uncut)
-      if (fp8 && max_tiles > 4 * (kSplitMaxTiles - 1))
-        nsplit = std::max<int>(nsplit, static_cast<int>((max_tiles + kSplitMaxTiles - 2) / (kSplitMaxTiles - 1)));
+      // A split costs a CTA start, a pipeline fill and a cluster merge, and the CTAs of a grid
+      // start and drain together, so an extra split only pays while the row groups alone leave
+      // the GPU short of streaming CTAs.  Measured on B200 (head_dim 64 and 128, rows of 256 to
+      // 2,000 keys, 8 to 768 row groups): splitting loses once 128 groups (bf16; 384 for fp8,
+      // whose CTAs are bound by the e4m3 conversion, not by HBM) fill the machine, rows under 12
+      // tiles are never worth cutting, and cluster sizes 3 and 6 schedule badly on full grids --
+      // so the split count is a power of two, at most 8, each split at least 2 tiles.
+      const long long fill = fp8 ? 384 : 128;
+      long long want = base > 0 ? std::min<long long>({8, fill / base, max_tiles / 2}) : 1;
+      nsplit = 1;
+      if (max_tiles >= 12)
+        while (nsplit * 2 <= want) nsplit *= 2;
     }
+    // an fp8 cache has no persistent plan and its CTAs are bound by the e4m3 conversion: rows of
+    // thousands of keys are cut into CTAs of at most kSplitMaxTiles - 1 tiles, so that uneven
+    // row lengths still balance over the waves, and into at least two CTAs per SM (measured on
+    // config 5, full context: batch 64 943 -> 611 us, batch 8 167 -> 99 us, batch 1 39 -> 33 us;
+    // windows of 4,096 keys run faster uncut)
+    if (fp8 && a->num_ctas == 0 && max_tiles > 4 * (kSplitMaxTiles - 1) && base > 0)
+      nsplit = static_cast<int>(std::max<long long>(
+          {nsplit, (max_tiles + kSplitMaxTiles - 2) / (kSplitMaxTiles - 1),
+           std::min<long long>(max_tiles, (2ll * device_sm_count() + base - 1) / base)}));
     pl->tps = static_cast<int>((max_tiles + nsplit - 1) / nsplit);
     pl->nsplit = static_cast<int>((max_tiles + pl->tps - 1) / pl->tps);
     if (base * pl->nsplit > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: grid too large");
     pl->grid = 0;
     // up to 8 splits of a row group form a thread-block cluster and merge through distributed
-    // shared memory: no partials in global memory and no combine kernel
-    pl->cluster = pl->nsplit >= 2 && pl->nsplit <= 8;
+    // shared memory: no partials in global memory and no combine kernel.  Up to 16 where the
+    // device schedules clusters of 16 and the grid is at most two CTAs per SM (measured on B200:
+    // batch 1 at 22k keys, 16 splits, 25.0 -> 21.0 us; on grids of 768 CTAs and more the
+    // clusters of 16 schedule worse than the partials and combine kernel)
+    pl->cluster = pl->nsplit >= 2 &&
+                  (pl->nsplit <= 8 || (base * pl->nsplit <= 2ll * device_sm_count() &&
+                                       pl->nsplit <= variant_max_cluster(a->D, pl->nqt, fp8)));
     if (pl->nsplit > 1 && !pl->cluster) {
       pl->part_o_bytes = round256(rows_out * pl->nsplit * a->D * 4);
       pl->part_lse_bytes = round256(rows_out * pl->nsplit * 4);

@@ -215,7 +215,7 @@ def _attn_case_to_device(z):
             torch.from_numpy(z["seqlens"]).to(torch.int32).cuda(), int(z["window"]))
 
 
-@pytest.mark.parametrize("splits", [0, 1, 3, 37, -1, -3, -12])
+@pytest.mark.parametrize("splits", [0, 1, 3, 37, -1, -3, -12, -20])
 @pytest.mark.parametrize("name", golden_files("kv_attn_"))
 def test_attention_matches_the_reference_golden_outputs(mcb, name, splits):
     _, ops = mcb
@@ -257,6 +257,8 @@ CASES = [
     (4, 1, 12, 12, 64, 700, 100), (5, 1, 32, 8, 128, 1500, -1), (5, 1, 32, 8, 128, 1500, 257),
     (3, 2, 16, 4, 128, 400, 64), (2, 1, 8, 1, 128, 300, -1), (2, 1, 4, 1, 256, 330, 40),
     (3, 5, 4, 2, 64, 90, 0), (2, 1, 16, 16, 128, 66, 1), (6, 3, 6, 3, 64, 129, -1),
+    # few row groups of long rows: 9-16 splits merge in one (non-portable) cluster
+    (1, 1, 32, 8, 128, 2048, -1), (2, 1, 16, 4, 128, 1100, 600),
 ]
 
 
@@ -269,7 +271,8 @@ def test_attention_matches_the_oracle_on_random_ragged_rows(mcb, case):
     lens[0] = 0
     ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
     args = (dev_bf16(q), dev_bf16(kc), dev_bf16(vc), torch.from_numpy(lens).to(torch.int32).cuda())
-    for splits in (0, 1, 2, 5, 300, -1, -2, -7, -8, -12):  # -2..-8: cluster merge; -12: combine kernel
+    # -2..-16: cluster merge (above 8 in a non-portable cluster); -20: partials + combine kernel
+    for splits in (0, 1, 2, 5, 300, -1, -2, -7, -8, -12, -16, -20):
         y = ops.decode_attn(*args, window=window, num_ctas=splits)
         err = np.abs(y.float().cpu().numpy() - ref).max()
         assert err <= ATTN_TOL, (splits, err)

@@ -31,7 +31,7 @@ def _ring_of(lin, lens, T, cap):
 
 
 CASES = [  # B, T, Hq, Hkv, D, lengths, window, cap, plans
-    (3, 1, 8, 2, 128, [5, 900, 3000], 300, 512, (0, -1, -3, -12, 37)),
+    (3, 1, 8, 2, 128, [5, 900, 3000], 300, 512, (0, -1, -3, -12, -20, 37)),
     (2, 3, 12, 12, 64, [700, 1600], 400, 512, (0, -2, 5)),
     (2, 130, 4, 1, 128, [0, 1000], 256, 512, (0, -1)),   # T >= 64: the tensor-core prefill plan
     (64, 1, 16, 4, 128, list(range(1000, 1640, 10)), 1024, 1152, (0, 148)),

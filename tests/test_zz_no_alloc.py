@@ -40,16 +40,16 @@ def _call_noalloc(q, kc, vc, sl, out, window, num_ctas):
 SHAPES = [
     # B, Hq, Hkv, D, Tmax, window, num_ctas (0: automatic plan, persistent for these rows --
     # long, and more than 128 row groups;
-    # > 0 persistent grid; < 0 split plan with that many key splits -- more than 8, so its
-    # partials go through memory: up to 8 splits merge inside a cluster and need none)
+    # > 0 persistent grid; < 0 split plan with that many key splits -- more than 16, so its
+    # partials go through memory: up to 16 splits merge inside a cluster and need none)
     (32, 32, 8, 128, 8192, -1, 0),
     (4, 12, 12, 64, 3000, 100, 24),
-    (4, 12, 12, 64, 1000, -1, -12),
+    (4, 12, 12, 64, 1000, -1, -20),
 ]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto", "mha-d64-window-24-ctas",
-                                               "mha-d64-12-splits"])
+                                               "mha-d64-17-splits"])
 def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape):
     B, Hq, Hkv, D, Tmax, window, splits = shape
     for call, seed in enumerate((11, 12)):

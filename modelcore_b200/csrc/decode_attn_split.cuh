@@ -8,8 +8,9 @@
 // into a STAGES-deep ring; four consumer warps each take 16 keys of every 64-key tile; the same
 // tensor-core contraction with keys on the M side (S^T = K Q^T, O^T += V^T P^T via
 // ldmatrix.trans / movmatrix.trans); the warps merge through shared memory.  With one split per
-// row the CTA writes the bf16 output; with several it writes (O/l, log2-sum-exp) partials that
-// decode_attn_split_combine_kernel merges, one warp per output row.
+// row the CTA writes the bf16 output; the splits of a row group merge inside a thread-block
+// cluster through distributed shared memory, or -- too many splits for a cluster -- write
+// (O/l, log2-sum-exp) partials, and the split that finishes last merges them (split_publish).
 #pragma once
 
 #include <math_constants.h>
@@ -29,7 +30,8 @@ struct SplitAttnParams {
   int B, T, Hq, Hkv, G, Tmax, window;
   float scale_log2;  // softmax_scale * log2(e)
   int nsplit, tiles_per_split, nqb;
-  int cluster;       // the nsplit (<= 8) CTAs of a row group form a cluster and merge in DSMEM
+  int cluster;       // the nsplit (<= 16) CTAs of a row group form a cluster and merge in DSMEM
+  int* counters;     // otherwise (nsplit > 1): [row group] arrivals; zero on entry and on exit
   int ring;          // the slot is a ring of Tmax positions (key c at index c % Tmax)
   // fp8 cache (decode_attn_split_kernel<.., true>): e4m3 K/V with per-vector fp32 scales at
   // [(b * Hkv + h) * scale_tmax + index]
@@ -77,7 +79,8 @@ struct SplitAttnConfig {
   static constexpr int BAR_OFFSET = SCR_OFFSET + kAttnConsumerWarps * SCR_WARP;
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
   static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
-  static constexpr int SMEM_BYTES = STAT_OFFSET + STAT_BYTES + 1024;  // + alignment slack
+  static constexpr int CTL_OFFSET = STAT_OFFSET + STAT_BYTES;  // the "last arrival" flag
+  static constexpr int SMEM_BYTES = CTL_OFFSET + 16 + 1024;    // + alignment slack
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
   static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
@@ -112,6 +115,71 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// Merges the nsplit partials of output row `row` (one warp): weights from the partials'
+// log2-sum-exps, then the weighted sum of their O rows.  Reads through L2 (the partials were
+// written by other CTAs of this launch).
+template <int D>
+__device__ __forceinline__ void merge_split_row(const SplitAttnParams& p, long long row, int lane) {
+  const float* lse = p.part_lse + row * p.nsplit;
+  float mmax = -CUDART_INF_F;
+  for (int s = lane; s < p.nsplit; s += 32) mmax = fmaxf(mmax, __ldcg(lse + s));
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, m));
+  float wsum = 0.f;
+  for (int s = lane; s < p.nsplit; s += 32) {
+    const float ls = __ldcg(lse + s);
+    wsum += (ls == -CUDART_INF_F) ? 0.f : fast_exp2(ls - mmax);
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, m);
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  constexpr int PER_LANE = (D + 31) / 32;
+  float acc[PER_LANE];
+#pragma unroll
+  for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
+  const float* po = p.part_o + row * p.nsplit * D;
+  for (int s = 0; s < p.nsplit; ++s) {
+    const float ls = __ldcg(lse + s);
+    if (ls == -CUDART_INF_F) continue;
+    const float w = fast_exp2(ls - mmax) * inv;
+#pragma unroll
+    for (int u = 0; u < PER_LANE; ++u) {
+      const int d = lane + 32 * u;
+      if (d < D) acc[u] = fmaf(w, __ldcg(po + s * D + d), acc[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < PER_LANE; ++u) {
+    const int d = lane + 32 * u;
+    if (d < D) p.out[row * D + d] = float_to_bf16_bits(acc[u]);
+  }
+}
+
+// A split CTA of the partials plan has written its partial rows r0 .. r1-1: it bumps the row
+// group's arrival counter (the barrier orders every thread's stores before thread 0's release),
+// and the CTA that arrives last merges all the group's partials into the output and resets the
+// counter.  No CTA waits for another and no second kernel runs.
+template <int D>
+__device__ __forceinline__ void split_publish(const SplitAttnParams& p, int group, int b, int kvh,
+                                              int r0, int r1, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* counter = p.counters + group;
+    const int prev = atom_add_acq_rel_gpu(counter, 1);
+    const int last = prev == p.nsplit - 1;
+    if (last) *counter = 0;  // every split has arrived: ready for the next call
+    *flag = last;
+  }
+  __syncthreads();
+  if (!*flag) return;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int r = r0 + warp; r < r1; r += kAttnThreads / 32) {
+    const int t = r / p.G, h = kvh * p.G + r % p.G;
+    merge_split_row<D>(p, (static_cast<long long>(b) * p.T + t) * p.Hq + h, lane);
+  }
 }
 
 template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
@@ -170,6 +238,8 @@ __global__ void __launch_bounds__(kAttnThreads)
             -CUDART_INF_F;
       }
     }
+    split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
+                     reinterpret_cast<int*>(smem + C::CTL_OFFSET));
     return;
   }
 
@@ -527,7 +597,12 @@ __global__ void __launch_bounds__(kAttnThreads)
       p.part_o[(row * p.nsplit + split) * D + d] = o;
     }
   }
-  if (!p.cluster) return;
+  if (!p.cluster) {
+    if (p.nsplit > 1)
+      split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
+                       reinterpret_cast<int*>(smem + C::CTL_OFFSET));
+    return;
+  }
 
   // ---- cluster merge: rank q (= split) writes rows n = q, q + nsplit, .. of the row group ----
   float* cpart = reinterpret_cast<float*>(smem + C::CL_OFFSET);
@@ -570,46 +645,6 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   }
   cluster_sync();  // no rank exits while another still reads its shared memory
-}
-
-// Merges the split partials of every (b, t, h) row: one warp per row.
-template <int D>
-__global__ void __launch_bounds__(128) decode_attn_split_combine_kernel(const SplitAttnParams p) {
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
-  const long long nrows = static_cast<long long>(p.B) * p.T * p.Hq;
-  if (row >= nrows) return;
-  const float* lse = p.part_lse + row * p.nsplit;
-  float mmax = -CUDART_INF_F;
-  for (int s = lane; s < p.nsplit; s += 32) mmax = fmaxf(mmax, lse[s]);
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, m));
-  float wsum = 0.f;
-  for (int s = lane; s < p.nsplit; s += 32)
-    wsum += (lse[s] == -CUDART_INF_F) ? 0.f : fast_exp2(lse[s] - mmax);
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, m);
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  constexpr int PER_LANE = (D + 31) / 32;
-  float acc[PER_LANE];
-#pragma unroll
-  for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
-  const float* po = p.part_o + row * p.nsplit * D;
-  for (int s = 0; s < p.nsplit; ++s) {
-    const float ls = lse[s];
-    if (ls == -CUDART_INF_F) continue;
-    const float w = fast_exp2(ls - mmax) * inv;
-#pragma unroll
-    for (int u = 0; u < PER_LANE; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) acc[u] = fmaf(w, po[s * D + d], acc[u]);
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < PER_LANE; ++u) {
-    const int d = lane + 32 * u;
-    if (d < D) p.out[row * D + d] = float_to_bf16_bits(acc[u]);
-  }
 }
 
 }  // namespace mcb

@@ -312,13 +312,6 @@ struct AttnVariant {
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
-    if (prm.nsplit > 1 && !prm.cluster) {
-      const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
-      mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
-      g_launches++;
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split_combine launch");
-    }
     return MCB_OK;
   }
 };
@@ -409,13 +402,6 @@ struct SplitF8Variant {
     g_launches++;
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split (fp8) launch");
-    if (prm.nsplit > 1 && !prm.cluster) {
-      const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
-      mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
-      g_launches++;
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split_combine launch");
-    }
     return MCB_OK;
   }
 };
@@ -541,20 +527,22 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
     if (base * pl->nsplit > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: grid too large");
     pl->grid = 0;
     // up to 8 splits of a row group form a thread-block cluster and merge through distributed
-    // shared memory: no partials in global memory and no combine kernel.  Up to 16 where the
+    // shared memory: no partials in global memory.  Up to 16 where the
     // device schedules clusters of 16 and the grid is at most two CTAs per SM (measured on B200:
     // batch 1 at 22k keys, 16 splits, 25.0 -> 21.0 us; on grids of 768 CTAs and more the
-    // clusters of 16 schedule worse than the partials and combine kernel)
+    // clusters of 16 schedule worse than partials merged by the last split to finish)
     pl->cluster = pl->nsplit >= 2 &&
                   (pl->nsplit <= 8 || (base * pl->nsplit <= 2ll * device_sm_count() &&
                                        pl->nsplit <= variant_max_cluster(a->D, pl->nqt, fp8)));
     if (pl->nsplit > 1 && !pl->cluster) {
+      // partials in the workspace; the last split of a row group to finish merges them
       pl->part_o_bytes = round256(rows_out * pl->nsplit * a->D * 4);
       pl->part_lse_bytes = round256(rows_out * pl->nsplit * 4);
+      pl->counter_count = static_cast<size_t>(base);
     } else {
       pl->part_o_bytes = pl->part_lse_bytes = 0;
+      pl->counter_count = 0;
     }
-    pl->counter_count = 0;
   } else {
     if (a->num_ctas > 0) {
       pl->grid = a->num_ctas;
@@ -700,6 +688,7 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.part_o = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w) : nullptr;
     p.part_lse = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
     p.cluster = pl.cluster ? 1 : 0;
+    p.counters = pl.counter_count > 0 ? counters : nullptr;
     p.ring = a->ring != 0;
     p.B = a->B;
     p.T = a->T;

@@ -255,7 +255,8 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ct
 
 def decode_attn_counter_count(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0,
                               ring=False):
-    """Arrival counters the launch plan needs (0: the split plan, which uses none)."""
+    """Arrival counters the launch plan needs (one per row group for the persistent plan and for
+    a split plan whose partials go through memory; 0 for a split plan merged in a cluster)."""
     args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None, ring)
     return int(_native.load().mcb_decode_attn_counter_count(ctypes.byref(args)))
 

@@ -144,6 +144,17 @@ def test_attention_workspace_is_per_persistent_cta_not_per_length():
     assert lib.mcb_decode_attn_counter_count(ctypes.byref(_attn(num_ctas=2, T=5))) == 2 * 2 * 2
 
 
+def test_split_plan_counters_only_for_partials_through_memory():
+    """A split plan merged inside a cluster (here, without a device, up to 8 splits) needs no
+    workspace and no counters; more splits publish partials and count arrivals per row group."""
+    lib = _native.load()
+    for splits, partials in ((4, False), (8, False), (12, True), (40, True)):
+        a = _attn(num_ctas=-splits, Tmax=4096)
+        ws = lib.mcb_decode_attn_workspace_size(ctypes.byref(a))
+        cnt = lib.mcb_decode_attn_counter_count(ctypes.byref(a))
+        assert (ws > 0) == partials and cnt == (2 * 1 * 2 if partials else 0), (splits, ws, cnt)
+
+
 def test_attention_checks_the_workspace_before_launching():
     lib = _native.load()
     a = _attn(num_ctas=4, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000,

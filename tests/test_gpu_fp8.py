@@ -93,7 +93,7 @@ def fp8_cache(g, B, Tmax, Hkv, D, scale=1.0):
 CASES = [  # B, T, Hq, Hkv, D, Tmax, max_len, window, ring, num_ctas
     (4, 1, 8, 2, 128, 1024, 1000, -1, False, 0),       # short rows: split, one wave
     (2, 1, 32, 8, 128, 8192, 8000, -1, False, 0),      # long rows of few groups: cluster of 16
-    (2, 1, 32, 8, 128, 8192, 8000, 1000, False, -20),  # 18 splits: workspace + combine kernel
+    (2, 1, 32, 8, 128, 8192, 8000, 1000, False, -20),  # 18 splits: partials, last split merges
     (3, 4, 12, 12, 64, 512, 500, 100, False, 0),       # D 64, several tokens, a window
     (1, 70, 8, 2, 128, 512, 400, -1, False, 0),        # a 70-token chunk (no fp8 tcgen05 path)
     (3, 2, 16, 4, 128, 384, 1500, 200, True, 0),       # ring slot: positions beyond T_max

@@ -271,7 +271,8 @@ def test_attention_matches_the_oracle_on_random_ragged_rows(mcb, case):
     lens[0] = 0
     ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
     args = (dev_bf16(q), dev_bf16(kc), dev_bf16(vc), torch.from_numpy(lens).to(torch.int32).cuda())
-    # -2..-16: cluster merge (above 8 in a non-portable cluster); -20: partials + combine kernel
+    # -2..-16: cluster merge (above 8 in a non-portable cluster); -20: partials, merged by the
+    # split that finishes last
     for splits in (0, 1, 2, 5, 300, -1, -2, -7, -8, -12, -16, -20):
         y = ops.decode_attn(*args, window=window, num_ctas=splits)
         err = np.abs(y.float().cpu().numpy() - ref).max()

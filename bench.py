@@ -418,9 +418,11 @@ def _gqa_decode(config, steps=64):
         run(3)  # eager step, graph capture, one replay
         before = dec.kv_cache.host_lens().astype(np.int64)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(f"gqa_decode_cfg{config}")
         e0.record(stream)
         run(steps)
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     B = int(before.size)
@@ -800,6 +802,8 @@ def main():
                     help="run only the prefill-attention measurements")
     ap.add_argument("--gqa-only", action="store_true",
                     help="run only the config-3 / config-4 decode measurements")
+    ap.add_argument("--gqa-configs", type=int, nargs="+", choices=(3, 4), default=[3, 4],
+                    help="with --gqa-only: which of configs 3 and 4 to run")
     ap.add_argument("--sweep-batches", type=int, nargs="+", default=[1, 8, 64, 256, 512])
     ap.add_argument("--sweep-windows", type=int, nargs="+", default=[-1, 4096])
     args = ap.parse_args()
@@ -815,7 +819,7 @@ def main():
         import torch
         _ensure_modelcore()
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        print(json.dumps({"gqa_decode": [_gqa_decode(3), _gqa_decode(4)]}), flush=True)
+        print(json.dumps({"gqa_decode": [_gqa_decode(c) for c in args.gqa_configs]}), flush=True)
     else:
         run_b200(args)
         import torch.distributed as dist

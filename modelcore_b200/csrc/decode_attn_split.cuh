@@ -10,7 +10,8 @@
 // ldmatrix.trans / movmatrix.trans); the warps merge through shared memory.  With one split per
 // row the CTA writes the bf16 output; the splits of a row group merge inside a thread-block
 // cluster through distributed shared memory, or -- too many splits for a cluster -- write
-// (O/l, log2-sum-exp) partials, and the split that finishes last merges them (split_publish).
+// (O/l, log2-sum-exp) partials that the split that finishes last merges (split_publish; small
+// grids) or decode_attn_split_combine_kernel merges after the launch (large grids).
 #pragma once
 
 #include <math_constants.h>
@@ -30,8 +31,10 @@ struct SplitAttnParams {
   int B, T, Hq, Hkv, G, Tmax, window;
   float scale_log2;  // softmax_scale * log2(e)
   int nsplit, tiles_per_split, nqb;
+  int row_cuts;      // cut each row by its own length (small grids) instead of tiles_per_split
   int cluster;       // the nsplit (<= 16) CTAs of a row group form a cluster and merge in DSMEM
-  int* counters;     // otherwise (nsplit > 1): [row group] arrivals; zero on entry and on exit
+  int* counters;     // otherwise, on small grids: [row group] arrivals, zero on entry and on exit
+                     // (null: decode_attn_split_combine_kernel merges the partials afterwards)
   int ring;          // the slot is a ring of Tmax positions (key c at index c % Tmax)
   // fp8 cache (decode_attn_split_kernel<.., true>): e4m3 K/V with per-vector fp32 scales at
   // [(b * Hkv + h) * scale_tmax + index]
@@ -140,14 +143,26 @@ __device__ __forceinline__ void merge_split_row(const SplitAttnParams& p, long l
 #pragma unroll
   for (int u = 0; u < PER_LANE; ++u) acc[u] = 0.f;
   const float* po = p.part_o + row * p.nsplit * D;
-  for (int s = 0; s < p.nsplit; ++s) {
-    const float ls = __ldcg(lse + s);
-    if (ls == -CUDART_INF_F) continue;
-    const float w = fast_exp2(ls - mmax) * inv;
+  // 32 splits at a time: lane j holds split s0 + j's weight; the partial rows of four splits are
+  // requested together (no branch between them), so their L2 round trips overlap
+  for (int s0 = 0; s0 < p.nsplit; s0 += 32) {
+    const int sl = s0 + lane;
+    const float ls = sl < p.nsplit ? __ldcg(lse + sl) : -CUDART_INF_F;
+    const float wk = (ls == -CUDART_INF_F) ? 0.f : fast_exp2(ls - mmax) * inv;
+    const int cnt = min(32, p.nsplit - s0);
+#pragma unroll 4
+    for (int j = 0; j < cnt; ++j) {
+      const float w = __shfl_sync(0xffffffffu, wk, j);
+      const float* prow = po + static_cast<long long>(s0 + j) * D;
 #pragma unroll
-    for (int u = 0; u < PER_LANE; ++u) {
-      const int d = lane + 32 * u;
-      if (d < D) acc[u] = fmaf(w, __ldcg(po + s * D + d), acc[u]);
+      for (int u = 0; u < PER_LANE; ++u) {
+        const int d = lane + 32 * u;
+        if (d < D) {
+          // an empty split wrote only its log-sum-exp: its O row is unset memory, never used
+          const float x = __ldcg(prow + d);
+          acc[u] = w != 0.f ? fmaf(w, x, acc[u]) : acc[u];
+        }
+      }
     }
   }
 #pragma unroll
@@ -222,10 +237,13 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int lo = p.window >= 0 ? max(0, L + t_first - p.window) : 0;
   const int kb = (min(lo, hi) / C::TK) * C::TK;
   const int ntiles = (hi - kb) / C::TK + 1;
-  // The host sizes the splits for the longest possible row (tiles_per_split); a shorter row is
-  // cut by its own length into nsplit parts of at least min(8, tiles_per_split) tiles, so that
-  // the splits of a long row all share its keys while a short row's keys stay in a few CTAs.
-  const int tps = max((ntiles + p.nsplit - 1) / p.nsplit, min(8, p.tiles_per_split));
+  // The host sizes the splits for the longest possible row (tiles_per_split).  On small grids
+  // (row_cuts) a row is cut by its own length into nsplit parts of at least
+  // min(8, tiles_per_split) tiles, so that the splits of a long row all share its keys while a
+  // short row's keys stay in a few CTAs; on large grids the fixed size keeps the CTAs few and
+  // the waves balanced.
+  const int tps = p.row_cuts ? max((ntiles + p.nsplit - 1) / p.nsplit, min(8, p.tiles_per_split))
+                             : p.tiles_per_split;
   const int tile0 = split * tps;
   const int my_tiles = max(0, min(ntiles - tile0, tps));
 
@@ -238,8 +256,9 @@ __global__ void __launch_bounds__(kAttnThreads)
             -CUDART_INF_F;
       }
     }
-    split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
-                     reinterpret_cast<int*>(smem + C::CTL_OFFSET));
+    if (p.counters != nullptr)
+      split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
+                       reinterpret_cast<int*>(smem + C::CTL_OFFSET));
     return;
   }
 
@@ -598,7 +617,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   }
   if (!p.cluster) {
-    if (p.nsplit > 1)
+    if (p.nsplit > 1 && p.counters != nullptr)
       split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
                        reinterpret_cast<int*>(smem + C::CTL_OFFSET));
     return;
@@ -635,16 +654,31 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int n = split + (idx / D) * ns;
     const int d = idx % D;
     const int r = r0 + n;
+    // every rank's partial is requested before the first is used: the remote loads overlap
+    float part_q[kMaxClusterSplits];
+#pragma unroll
+    for (int q = 0; q < kMaxClusterSplits; ++q)
+      if (q < ns) part_q[q] = ld_dsmem_f32(map_to_rank(cpart + n * D + d, static_cast<uint32_t>(q)));
     float o = 0.f;
 #pragma unroll
     for (int q = 0; q < kMaxClusterSplits; ++q)
-      if (q < ns) o = fmaf(cw[n * kMaxClusterSplits + q], ld_dsmem_f32(map_to_rank(cpart + n * D + d, static_cast<uint32_t>(q))), o);
+      if (q < ns) o = fmaf(cw[n * kMaxClusterSplits + q], part_q[q], o);
     if (r < r1) {
       const int t = r / p.G, h = kvh * p.G + r % p.G;
       p.out[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);
     }
   }
   cluster_sync();  // no rank exits while another still reads its shared memory
+}
+
+// Merges the split partials of every (b, t, h) row after the split kernel: one warp per row (the
+// partials plan on large grids, where a merge inside the last CTA of each row group would hold
+// SM slots that the remaining waves need).
+template <int D>
+__global__ void __launch_bounds__(128) decode_attn_split_combine_kernel(const SplitAttnParams p) {
+  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  if (row >= static_cast<long long>(p.B) * p.T * p.Hq) return;
+  merge_split_row<D>(p, row, threadIdx.x & 31);
 }
 
 }  // namespace mcb

@@ -115,6 +115,18 @@ bool cluster_fits(K kernel, int smem, int n) {
   return clusters > 0;
 }
 
+// The combine kernel after a split launch whose partials no CTA merged (counters == null).
+template <int D>
+int launch_combine(const mcb::SplitAttnParams& prm, cudaStream_t st) {
+  if (prm.nsplit <= 1 || prm.cluster || prm.counters != nullptr) return MCB_OK;
+  const long long rows = static_cast<long long>(prm.B) * prm.T * prm.Hq;
+  mcb::decode_attn_split_combine_kernel<D><<<static_cast<unsigned>((rows + 3) / 4), 128, 0, st>>>(prm);
+  g_launches++;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split_combine launch");
+  return MCB_OK;
+}
+
 // Caches a per-device answer (0 = not yet known); `compute` runs once per device.
 template <typename F>
 int per_device(int (&cache)[64], std::mutex& mu, F compute) {
@@ -312,7 +324,7 @@ struct AttnVariant {
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
-    return MCB_OK;
+    return launch_combine<D>(prm, st);
   }
 };
 
@@ -402,7 +414,7 @@ struct SplitF8Variant {
     g_launches++;
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split (fp8) launch");
-    return MCB_OK;
+    return launch_combine<D>(prm, st);
   }
 };
 
@@ -429,6 +441,7 @@ struct AttnPlan {
   bool cluster = false;  // split plan merged inside a cluster
   int grid;         // persistent CTAs (persistent mode)
   int nsplit, tps;  // key splits per row group and tiles per split (split mode)
+  bool small_grid = false;  // split mode: at most about four CTAs per SM
   size_t part_o_bytes, part_lse_bytes, ws_bytes, counter_count;
 };
 
@@ -530,15 +543,20 @@ int plan_attn(const mcb_attn_args* a, AttnPlan* pl) {
     // shared memory: no partials in global memory.  Up to 16 where the
     // device schedules clusters of 16 and the grid is at most two CTAs per SM (measured on B200:
     // batch 1 at 22k keys, 16 splits, 25.0 -> 21.0 us; on grids of 768 CTAs and more the
-    // clusters of 16 schedule worse than partials merged by the last split to finish)
+    // clusters of 16 schedule worse than partials merged by a combine kernel)
     pl->cluster = pl->nsplit >= 2 &&
                   (pl->nsplit <= 8 || (base * pl->nsplit <= 2ll * device_sm_count() &&
                                        pl->nsplit <= variant_max_cluster(a->D, pl->nqt, fp8)));
+    pl->small_grid = base * pl->nsplit <= 4ll * device_sm_count();
     if (pl->nsplit > 1 && !pl->cluster) {
-      // partials in the workspace; the last split of a row group to finish merges them
+      // partials in the workspace.  On grids of at most about four CTAs per SM the last split of
+      // a row group to finish merges them (no second kernel: batch 1, fp8, 37 splits 30.8 ->
+      // 26.2 us); on larger grids a combine kernel after the launch does (config 5 fp8, batch 64,
+      // full rows, 17 splits: merges inside the grid held SM slots that its later waves needed,
+      // 636 -> 694-708 us)
       pl->part_o_bytes = round256(rows_out * pl->nsplit * a->D * 4);
       pl->part_lse_bytes = round256(rows_out * pl->nsplit * 4);
-      pl->counter_count = static_cast<size_t>(base);
+      pl->counter_count = pl->small_grid ? static_cast<size_t>(base) : 0;
     } else {
       pl->part_o_bytes = pl->part_lse_bytes = 0;
       pl->counter_count = 0;
@@ -700,6 +718,10 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
     p.nsplit = pl.nsplit;
     p.tiles_per_split = pl.tps;
+    // rows cut by their own lengths only on small grids (batch 1, 8,192 keys, 4 splits: 64 ->
+    // 20.7 us; on large grids the cuts multiply the CTAs: config 5 fp8 at batch 64, full rows,
+    // 17 splits, 636 vs 679 us)
+    p.row_cuts = pl.small_grid ? 1 : 0;
     p.nqb = pl.nqb;
     p.k_scale = a->k_scale;
     p.v_scale = a->v_scale;

@@ -255,8 +255,9 @@ def _attn_args(q, k_cache, v_cache, cache_seqlens, window, softmax_scale, num_ct
 
 def decode_attn_counter_count(q, k_cache, v_cache, cache_seqlens, *, window=-1, num_ctas=0,
                               ring=False):
-    """Arrival counters the launch plan needs (one per row group for the persistent plan and for
-    a split plan whose partials go through memory; 0 for a split plan merged in a cluster)."""
+    """Arrival counters the launch plan needs: one per row group for the persistent plan and for
+    a split plan on a small grid whose partials go through memory (its last split to finish
+    merges them); 0 for a split plan merged in a cluster or by the combine kernel."""
     args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, num_ctas, None, ring)
     return int(_native.load().mcb_decode_attn_counter_count(ctypes.byref(args)))
 

@@ -259,6 +259,9 @@ CASES = [
     (3, 5, 4, 2, 64, 90, 0), (2, 1, 16, 16, 128, 66, 1), (6, 3, 6, 3, 64, 129, -1),
     # few row groups of long rows: 9-16 splits merge in one (non-portable) cluster
     (1, 1, 32, 8, 128, 2048, -1), (2, 1, 16, 4, 128, 1100, 600),
+    # 320 row groups: 12-20 splits are a grid too large for clusters of 16 or for merges in the
+    # last CTA of each group -- the partials go to the combine kernel
+    (40, 1, 32, 8, 128, 1400, -1),
 ]
 
 
@@ -272,7 +275,7 @@ def test_attention_matches_the_oracle_on_random_ragged_rows(mcb, case):
     ref = O.decode_attention(O.bf16_to_f32(q), O.bf16_to_f32(kc), O.bf16_to_f32(vc), lens, window)
     args = (dev_bf16(q), dev_bf16(kc), dev_bf16(vc), torch.from_numpy(lens).to(torch.int32).cuda())
     # -2..-16: cluster merge (above 8 in a non-portable cluster); -20: partials, merged by the
-    # split that finishes last
+    # split that finishes last (small grids) or by the combine kernel (large grids)
     for splits in (0, 1, 2, 5, 300, -1, -2, -7, -8, -12, -16, -20):
         y = ops.decode_attn(*args, window=window, num_ctas=splits)
         err = np.abs(y.float().cpu().numpy() - ref).max()

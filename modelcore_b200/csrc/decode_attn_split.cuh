@@ -333,9 +333,13 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const int d0 = kk * 16 + 2 * (lane & 3);
+        // fp8: the key fragments come straight from the e4m3 rows, lane quad t holding head
+        // dimensions [t D/4, (t+1) D/4) (four per k-step); the query fragments follow the same
+        // order (a permutation of the summed dimension: the same dot product)
+        const int d0 = FP8 ? (lane & 3) * (D / 4) + 4 * kk : kk * 16 + 2 * (lane & 3);
+        const int d1 = FP8 ? d0 + 2 : d0 + 8;
         qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
-        qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+        qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d1) : 0u;
         if (FP8) {  // the products run in f16 against the exactly converted e4m3 keys
 #pragma unroll
           for (int u = 0; u < 2; ++u)
@@ -376,6 +380,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       int panel_bytes = C::PANEL_BYTES;
       const int tile_key0 = kb + (tile0 + i) * C::TK;
       float ks[NCH][2], vs[NCH][2];           // fp8: the scales of this lane's key rows
+      uint32_t kw[NCH][2][FP8 ? D / 16 : 1];  // fp8: this lane's e4m3 key words (see below)
       if constexpr (FP8) {
         const uint32_t f8k = kbase, f8v = kbase + C::F8_TILE;
         const float* scl = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + 2 * C::F8_TILE);
@@ -387,7 +392,23 @@ __global__ void __launch_bounds__(kAttnThreads)
             ks[ch][hh] = scl[kr];
             vs[ch][hh] = scl[C::TK + kr];
           }
-        // e4m3 rows warp*KPW .. +KPW-1 of K and V -> f16 (exact), 16 bytes of e4m3 a step
+        // this lane's e4m3 key bytes, rows g and g + 8 of each 16-key chunk, head dimensions
+        // [t D/4, (t+1) D/4): read before the stage is released, converted at the products
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int kr = warp * KPW + ch * 16 + (lane >> 2) + hh * 8;
+#pragma unroll
+            for (int c = 0; c < D / 64; ++c) {
+              const uint4 w = lds128(f8k + swz<C::F8_ROW, C::F8_MASK>(kr, (lane & 3) * (D / 64) + c));
+              kw[ch][hh][4 * c + 0] = w.x;
+              kw[ch][hh][4 * c + 1] = w.y;
+              kw[ch][hh][4 * c + 2] = w.z;
+              kw[ch][hh][4 * c + 3] = w.w;
+            }
+          }
+        // e4m3 rows warp*KPW .. +KPW-1 of V -> f16 (exact), 16 bytes of e4m3 a step
         constexpr int CPR = D / 16;  // 16-byte e4m3 chunks per row
 #pragma unroll
         for (int idx = lane; idx < KPW * CPR; idx += 32) {
@@ -397,21 +418,17 @@ __global__ void __launch_bounds__(kAttnThreads)
           const uint32_t pbase = (col / C::PANEL) * C::SCR_PANEL;
           const uint32_t doff0 = pbase + swz<C::ROW_BYTES, C::SWZ_MASK>(r, (col % C::PANEL) / 8);
           const uint32_t doff1 = pbase + swz<C::ROW_BYTES, C::SWZ_MASK>(r, (col % C::PANEL) / 8 + 1);
-#pragma unroll
-          for (int kv = 0; kv < 2; ++kv) {
-            const uint4 w = lds128((kv ? f8v : f8k) + soff);
-            uint32_t h[8];
-            e4m3x4_to_f16x4(w.x, h[0], h[1]);
-            e4m3x4_to_f16x4(w.y, h[2], h[3]);
-            e4m3x4_to_f16x4(w.z, h[4], h[5]);
-            e4m3x4_to_f16x4(w.w, h[6], h[7]);
-            const uint32_t dst = kv ? scr_v : scr_k;
-            sts128(dst + doff0, make_uint4(h[0], h[1], h[2], h[3]));
-            sts128(dst + doff1, make_uint4(h[4], h[5], h[6], h[7]));
-          }
+          const uint4 w = lds128(f8v + soff);
+          uint32_t h[8];
+          e4m3x4_to_f16x4(w.x, h[0], h[1]);
+          e4m3x4_to_f16x4(w.y, h[2], h[3]);
+          e4m3x4_to_f16x4(w.z, h[4], h[5]);
+          e4m3x4_to_f16x4(w.w, h[6], h[7]);
+          sts128(scr_v + doff0, make_uint4(h[0], h[1], h[2], h[3]));
+          sts128(scr_v + doff1, make_uint4(h[4], h[5], h[6], h[7]));
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);  // the stage is converted: refill it
+        if (lane == 0) mbar_arrive(&empty_bar[s]);  // keys read, values converted: refill it
         kbase = scr_k;
         vbase = scr_v;
         row0 = 0;
@@ -428,11 +445,16 @@ __global__ void __launch_bounds__(kAttnThreads)
         const int krow = row0 + ch * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const int col = kk * 16 + (lane >> 4) * 8;  // first column of this lane's 8-wide chunk
-          const uint32_t addr = kbase + (col / C::PANEL) * panel_bytes +
-                                swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(addr, a0, a1, a2, a3);
+          if constexpr (FP8) {  // bytes 4kk..4kk+3 of rows g and g + 8: (a0, a2) and (a1, a3)
+            e4m3x4_to_f16x4(kw[ch][0][kk], a0, a2);
+            e4m3x4_to_f16x4(kw[ch][1][kk], a1, a3);
+          } else {
+            const int col = kk * 16 + (lane >> 4) * 8;  // first column of this lane's 8-wide chunk
+            const uint32_t addr = kbase + (col / C::PANEL) * panel_bytes +
+                                  swz<C::ROW_BYTES, C::SWZ_MASK>(krow, (col % C::PANEL) / 8);
+            ldsm_x4(addr, a0, a1, a2, a3);
+          }
 #pragma unroll
           for (int j = 0; j < NQT; ++j) {
             if (FP8)

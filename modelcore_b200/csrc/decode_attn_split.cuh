@@ -59,8 +59,9 @@ struct SplitAttnConfig {
   static constexpr int PANEL_BYTES = TK * ROW_BYTES;
   static constexpr int TILE_BYTES = NPANEL * PANEL_BYTES;    // one K (or V) tile
   // fp8: a stage holds the e4m3 K and V tiles (TK rows of D bytes, one swizzled panel) and the
-  // tile's K and V scales; each consumer warp converts its KPW rows to f16 in its own scratch,
-  // laid out as a bf16 tile of KPW rows (same panels, same swizzle)
+  // tile's K and V scales; each consumer warp converts its KPW value rows to f16 in its own
+  // scratch, laid out as a bf16 tile of KPW rows (same panels, same swizzle); its keys go from
+  // the stage to registers
   static constexpr int F8_ROW = D;
   static constexpr int F8_MASK = D == 128 ? 7 : 3;
   static constexpr int F8_TILE = TK * D;
@@ -68,7 +69,7 @@ struct SplitAttnConfig {
   static constexpr int STAGE_BYTES = FP8 ? ((2 * F8_TILE + F8_SCALES + 1023) & ~1023) : 2 * TILE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int SCR_PANEL = KPW * ROW_BYTES;          // one warp's scratch panel
-  static constexpr int SCR_WARP = FP8 ? 2 * NPANEL * SCR_PANEL : 0;  // K then V
+  static constexpr int SCR_WARP = FP8 ? NPANEL * SCR_PANEL : 0;  // the warp's values in f16
   static constexpr int OPITCH = D + 4;                       // merge buffer row pitch (floats)
   static constexpr int MERGE_BYTES = kAttnConsumerWarps * kRows * OPITCH * 4;
   // cluster merge: this CTA's merged partial [kRows][D], its per-row log2-sum-exp and the
@@ -368,9 +369,8 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
 
     constexpr int NCH = KPW / 16;  // 16-key chunks per warp per stage
-    // fp8: this warp's f16 scratch (K then V), its rows at 0 .. KPW-1
-    const uint32_t scr_k = smem_u32(smem + C::SCR_OFFSET + warp * C::SCR_WARP);
-    const uint32_t scr_v = scr_k + C::NPANEL * C::SCR_PANEL;
+    // fp8: this warp's f16 scratch for its value rows, at rows 0 .. KPW-1
+    const uint32_t scr_v = smem_u32(smem + C::SCR_OFFSET + warp * C::SCR_WARP);
     for (int i = 0; i < my_tiles; ++i) {
       const int s = i % STAGES;
       if (!mbar_wait(&full_bar[s], (i / STAGES) & 1)) break;
@@ -429,7 +429,6 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);  // keys read, values converted: refill it
-        kbase = scr_k;
         vbase = scr_v;
         row0 = 0;
         panel_bytes = C::SCR_PANEL;

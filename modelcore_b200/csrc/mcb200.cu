@@ -351,13 +351,13 @@ int variant_launch_split(int D, int nqt, long long grid, const CUtensorMap& km, 
 }
 
 // The split kernel over an fp8 (e4m3) cache: half the bytes per tile, so a 4-stage ring holds as
-// many keys in flight as 2 bf16 stages; a 2-stage copy for single-wave grids as above.
+// many keys in flight as 2 bf16 stages (2 CTAs per SM); a 3-stage copy fits 3 per SM.
 template <int D, int NQT>
 struct SplitF8Variant {
   using Cfg = mcb::SplitAttnConfig<D, NQT, kKPW, 4, true>;
   static constexpr auto kernel = mcb::decode_attn_split_kernel<D, NQT, kKPW, 4, true>;
-  using CfgLo = mcb::SplitAttnConfig<D, NQT, kKPW, 2, true>;
-  static constexpr auto kernel_lo = mcb::decode_attn_split_kernel<D, NQT, kKPW, 2, true>;
+  using CfgLo = mcb::SplitAttnConfig<D, NQT, kKPW, 3, true>;
+  static constexpr auto kernel_lo = mcb::decode_attn_split_kernel<D, NQT, kKPW, 3, true>;
 
   static int slots(bool lo, long long* out) {
     static std::atomic<uint64_t> done_hi{0}, done_lo{0};
@@ -392,7 +392,11 @@ struct SplitF8Variant {
     if (rc != MCB_OK) return rc;
     rc = slots(true, &lo_slots);
     if (rc != MCB_OK) return rc;
-    const bool lo = grid > hi_slots && grid <= lo_slots;
+    // the 3-stage copy (3 CTAs per SM against 2): when it makes the grid resident at once, and on
+    // grids of many waves, whose consumer-bound CTAs gain from more warps per SM (config 5 at
+    // batch 64 / 256, full rows: 467 -> 430 us, 1,848 -> 1,724 us; batch 8, about 7 CTAs per SM,
+    // runs faster with the deeper ring: 78 vs 87 us)
+    const bool lo = grid > hi_slots && (grid <= lo_slots || grid >= 8ll * device_sm_count());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(mcb::kAttnThreads);

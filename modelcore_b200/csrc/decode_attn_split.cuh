@@ -412,7 +412,12 @@ __global__ void __launch_bounds__(kAttnThreads)
         constexpr int CPR = D / 16;  // 16-byte e4m3 chunks per row
 #pragma unroll
         for (int idx = lane; idx < KPW * CPR; idx += 32) {
-          const int r = idx / CPR, c16 = idx % CPR;
+          // D = 128: each quarter-warp takes half of two adjacent rows (chunks 0-3 of one and 4-7
+          // of the other), so its eight 16-byte reads and, in each of the two stores, its eight
+          // f16 chunks (two panels, swizzled by row) fall on distinct bank groups
+          const int u = idx & 15;
+          const int r = CPR == 8 ? (idx >> 4) * 2 + ((u >> 2) & 1) : idx / CPR;
+          const int c16 = CPR == 8 ? (u & 3) + 4 * (((u >> 2) ^ (u >> 3)) & 1) : idx % CPR;
           const uint32_t soff = swz<C::F8_ROW, C::F8_MASK>(warp * KPW + r, c16);
           const int col = c16 * 16;  // two 8-column f16 chunks, swizzled independently
           const uint32_t pbase = (col / C::PANEL) * C::SCR_PANEL;

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 5
+#define MCB_ABI_VERSION 6
 
 typedef enum {
   MCB_OK = 0,
@@ -174,6 +174,24 @@ typedef struct {
   const float* k_scale;
   const float* v_scale;
   int32_t scale_tmax;
+  /* fused append (fuse_append = 1; T = 1, a bf16 slot, D = 64 or 128, and a split plan --
+     mcb_decode_attn_fusable): q is the RAW query projection (B, 1, Hq, D); the kernel does what
+     mcb_kv_append_rope does for this step (rope at position cache_seqlens[b] from rot_cos /
+     rot_sin, rms_norm with norm_eps, x qk_scale, bit for bit) on the query and, with k_new /
+     v_new, on the new key, writes the key and value into k_cache / v_cache at that position,
+     and attends over the slot including them -- one launch instead of two.  k_new = v_new = NULL:
+     a layer that reads another layer's slot (only q is rotated).  cache_seqlens is not advanced. */
+  int32_t fuse_append;
+  const void* k_new;          /* (B, 1, Hkv, D) bf16 at k_new_stride (elements)               */
+  const void* v_new;
+  int64_t k_new_stride[3];
+  int64_t v_new_stride[3];
+  const void* rot_cos;        /* (rot_len, D/2) bf16 rotary tables, 16-byte aligned           */
+  const void* rot_sin;
+  int32_t rot_len;
+  int32_t rotate_k;           /* 1: the key is roped, normed and scaled like q; 0: raw insert */
+  float norm_eps;
+  float qk_scale;
 } mcb_attn_args;
 
 /* Bytes of workspace mcb_decode_attn needs for its partial results (0: none): persistent plan,
@@ -186,6 +204,13 @@ size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
 /* int32 arrival counters mcb_decode_attn needs: one per row group,
  * B * ceil(T * Hq / Hkv / rows) * Hkv, for the persistent plan; 0 for the split plan. */
 size_t mcb_decode_attn_counter_count(const mcb_attn_args* args);
+
+/* 1 when mcb_decode_attn can run this call with fuse_append = 1 (one new token a row, a bf16
+ * slot, D = 64 or 128, and the split plan: rows of at most 2,048 keys or few row groups), else
+ * 0 -- the caller then runs mcb_kv_append_rope and mcb_decode_attn.  Decided on the host from
+ * the shapes alone (no device read).  Not in the reference, whose append and attention are two
+ * calls (kernels/flash_attn.py:306-366). */
+int mcb_decode_attn_fusable(const mcb_attn_args* args);
 
 int mcb_decode_attn(const mcb_attn_args* args, void* stream);
 

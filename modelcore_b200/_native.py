@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "mcb_kv_advance",
     "mcb_decode_attn_workspace_size",
     "mcb_decode_attn_counter_count",
+    "mcb_decode_attn_fusable",
     "mcb_decode_attn",
     "mcb_decode_attn_noalloc",
     "mcb_add_rms_norm",
@@ -112,6 +113,12 @@ class AttnArgs(ctypes.Structure):
         ("ring", ctypes.c_int32),
         ("k_scale", ctypes.c_void_p), ("v_scale", ctypes.c_void_p),
         ("scale_tmax", ctypes.c_int32),
+        ("fuse_append", ctypes.c_int32),
+        ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p),
+        ("k_new_stride", _i64x3), ("v_new_stride", _i64x3),
+        ("rot_cos", ctypes.c_void_p), ("rot_sin", ctypes.c_void_p),
+        ("rot_len", ctypes.c_int32), ("rotate_k", ctypes.c_int32),
+        ("norm_eps", ctypes.c_float), ("qk_scale", ctypes.c_float),
     ]
 
 
@@ -202,6 +209,8 @@ def _declare(lib):
     lib.mcb_decode_attn_workspace_size.restype = ctypes.c_size_t
     lib.mcb_decode_attn_workspace_size.argtypes = [P(AttnArgs)]
     lib.mcb_decode_attn_counter_count.restype = ctypes.c_size_t
+    lib.mcb_decode_attn_fusable.restype = ctypes.c_int
+    lib.mcb_decode_attn_fusable.argtypes = [P(AttnArgs)]
     lib.mcb_decode_attn_counter_count.argtypes = [P(AttnArgs)]
     lib.mcb_decode_attn.restype = ctypes.c_int
     lib.mcb_decode_attn.argtypes = [P(AttnArgs), ctypes.c_void_p]

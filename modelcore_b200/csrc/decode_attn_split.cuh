@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "decode_attn.cuh"
+#include "kv_append.cuh"
 
 namespace mcb {
 
@@ -41,6 +42,20 @@ struct SplitAttnParams {
   const float* k_scale;
   const float* v_scale;
   int scale_tmax;
+  // fused append (bf16 cache, one new token a row): q is the raw query projection; each CTA
+  // ropes, norms and scales its query heads, and the CTA whose keys reach the row's position
+  // also writes the new key (roped, normed, scaled unless raw) and value into the slot and into
+  // its own copy of that tile -- kv_append_rope_vec_kernel's arithmetic, the same bits
+  int fuse;
+  const uint16_t* k_new;       // (B, 1, Hkv, D) raw key / value projections; null: q only
+  const uint16_t* v_new;
+  long long kns[3], vns[3];
+  uint16_t* kc_out;            // the slot (B, Tmax, Hkv, D) the new key and value go to
+  uint16_t* vc_out;
+  const uint16_t* rot_cos;     // rotary tables (rot_len, D/2) bf16
+  const uint16_t* rot_sin;
+  int rot_len, rotate_k;
+  float norm_eps, qk_scale;
 };
 
 
@@ -84,7 +99,10 @@ struct SplitAttnConfig {
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
   static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
   static constexpr int CTL_OFFSET = STAT_OFFSET + STAT_BYTES;  // the "last arrival" flag
-  static constexpr int SMEM_BYTES = CTL_OFFSET + 16 + 1024;    // + alignment slack
+  // fused append: the CTA's query rows [kRows][D] and the new key and value [2][D], bf16
+  static constexpr int FUSE_OFFSET = CTL_OFFSET + 16;
+  static constexpr int FUSE_BYTES = FP8 ? 0 : (kRows + 2) * D * 2;
+  static constexpr int SMEM_BYTES = FUSE_OFFSET + FUSE_BYTES + 1024;  // + alignment slack
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
   static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
@@ -198,8 +216,10 @@ __device__ __forceinline__ void split_publish(const SplitAttnParams& p, int grou
   }
 }
 
+// The 2-stage copy for head size <= 64 and 8-row groups exists to fit 6 CTAs per SM (config 2's
+// 768 CTAs in one wave): 160 threads x 64 registers each.
 template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
-__global__ void __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT == 1 && !FP8) ? 6 : 1)
     decode_attn_split_kernel(const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const SplitAttnParams p) {
   using C = SplitAttnConfig<D, NQT, KPW, STAGES, FP8>;
@@ -247,6 +267,10 @@ __global__ void __launch_bounds__(kAttnThreads)
                              : p.tiles_per_split;
   const int tile0 = split * tps;
   const int my_tiles = max(0, min(ntiles - tile0, tps));
+  // fused append: this CTA's tiles hold the row's new position (the single-token case)
+  const int tile_new = (L - kb) / C::TK;
+  const bool own_new = !FP8 && p.fuse && p.k_new != nullptr && L >= 0 && tile_new >= tile0 &&
+                       tile_new < tile0 + my_tiles;
 
   if (my_tiles == 0 && !p.cluster) {  // an empty split: its partial carries no weight
     if (threadIdx.x < C::kRows) {
@@ -285,7 +309,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         const int key0 = kb + (tile0 + i) * C::TK;
         // keys below L are from earlier steps; a tile reaching L holds this step's new keys,
         // written by the append kernel this launch may have overlapped (PDL)
-        if (!waited && key0 + C::TK > L) {
+        if (!waited && (p.fuse || key0 + C::TK > L)) {
           pdl_wait();
           waited = true;
         }
@@ -321,7 +345,50 @@ __global__ void __launch_bounds__(kAttnThreads)
 
   if (warp < kAttnConsumerWarps) {
     // ---------------- consumer warps ----------------
-    pdl_wait();  // q comes from the append kernel ahead of this one
+    pdl_wait();  // q comes from the append kernel ahead of this one (fused: the projection)
+    uint16_t* qbuf = reinterpret_cast<uint16_t*>(smem + C::FUSE_OFFSET);  // [kRows][D]
+    uint16_t* kvbuf = qbuf + C::kRows * D;                                 // [2][D]
+    if (!FP8 && p.fuse) {
+      if (warp == 0) {
+        // groups of D/16 lanes, one vector each: the query heads r0 .. r1-1, then (the CTA with
+        // the new position) the key and the value
+        constexpr int LG = D / 16, VPW = 32 / LG, HALF = D / 2;
+        const int nq = r1 - r0;
+        const int nvec = nq + (own_new ? 2 : 0);
+        const int sub = lane % LG;
+        const bool rot_ok = L >= 0 && L < p.rot_len;
+        for (int v0 = 0; v0 < nvec; v0 += VPW) {
+          const int vi = v0 + lane / LG;
+          const bool valid = vi < nvec;
+          const bool is_q = vi < nq, is_k = vi == nq;
+          const uint16_t* src = nullptr;
+          if (valid)
+            src = is_q ? p.q + b * p.qs[0] + (kvh * p.G + r0 + vi) * p.qs[2]
+                       : (is_k ? p.k_new + b * p.kns[0] + kvh * p.kns[2] : p.v_new + b * p.vns[0] + kvh * p.vns[2]);
+          const bool rotate = valid && (is_q || (is_k && p.rotate_k));
+          if (rotate && !rot_ok && sub == 0) record_error(kErrPositionBeyondRotary);
+          const uint4 x1v = valid ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
+          const uint4 x2v = valid ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
+          float o1[8], o2[8];
+          rope_norm_vec<D>(x1v, x2v, p.rot_cos, p.rot_sin, L, sub, rotate && rot_ok, p.norm_eps, p.qk_scale, o1,
+                           o2);
+          if (valid) {
+            const uint4 w1 = pack8(o1), w2 = pack8(o2);
+            uint16_t* dst = is_q ? qbuf + vi * D : kvbuf + (is_k ? 0 : D);
+            *reinterpret_cast<uint4*>(dst + 8 * sub) = w1;
+            *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = w2;
+            if (!is_q && (p.ring || L < p.Tmax)) {
+              const int idx = p.ring ? L % p.Tmax : L;
+              uint16_t* cdst = (is_k ? p.kc_out : p.vc_out) +
+                               ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + kvh) * D;
+              *reinterpret_cast<uint4*>(cdst + 8 * sub) = w1;
+              *reinterpret_cast<uint4*>(cdst + HALF + 8 * sub) = w2;
+            }
+          }
+        }
+      }
+      named_barrier(2, kAttnConsumerWarps * 32);  // the query rows and the new key are in place
+    }
     // Q^T fragments (B operand): row n = j*8 + lane/4, columns d = kk*16 + 2*(lane%4) + {0,1}, +8.
     uint32_t qf[NQT][D / 16][2];
 #pragma unroll
@@ -329,8 +396,12 @@ __global__ void __launch_bounds__(kAttnThreads)
       const int r = r0 + j * 8 + (lane >> 2);
       const uint16_t* qrow = nullptr;
       if (r < r1) {
-        const int t = r / p.G, h = kvh * p.G + r % p.G;
-        qrow = p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+        if (!FP8 && p.fuse) {
+          qrow = qbuf + (r - r0) * D;
+        } else {
+          const int t = r / p.G, h = kvh * p.G + r % p.G;
+          qrow = p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2];
+        }
       }
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
@@ -379,6 +450,23 @@ __global__ void __launch_bounds__(kAttnThreads)
       int row0 = warp * KPW;                  // this warp's first key row in the tile buffers
       int panel_bytes = C::PANEL_BYTES;
       const int tile_key0 = kb + (tile0 + i) * C::TK;
+      if constexpr (!FP8) {
+        // fused append: the tile arrived with the slot's old bytes at the new position; the warp
+        // that owns that row writes the new key and value over it before reading the tile
+        const int rr = L - tile_key0;
+        if (own_new && rr >= warp * KPW && rr < (warp + 1) * KPW) {
+          constexpr int NCHK = D / 8;  // 16-byte chunks per row
+          if (lane < 2 * NCHK) {
+            const int isv = lane >= NCHK ? 1 : 0;
+            const int col = (lane % NCHK) * 8;
+            const uint32_t dst = (isv ? vbase : kbase) + (col / C::PANEL) * C::PANEL_BYTES +
+                                 swz<C::ROW_BYTES, C::SWZ_MASK>(rr, (col % C::PANEL) / 8);
+            sts128(dst, lds128(smem_u32(kvbuf + isv * D + col)));
+          }
+          fence_proxy_async_shared();  // TMA refills this stage later
+          __syncwarp();
+        }
+      }
       float ks[NCH][2], vs[NCH][2];           // fp8: the scales of this lane's key rows
       uint32_t kw[NCH][2][FP8 ? D / 16 : 1];  // fp8: this lane's e4m3 key words (see below)
       if constexpr (FP8) {

@@ -184,6 +184,54 @@ __device__ __forceinline__ uint2 e4m3x8(const float* x, float inv) {
   return make_uint2(w[0], w[1]);
 }
 
+// One head vector's rope + rms_norm + scale, by a group of L = D/16 lanes (lane `sub` of the
+// group holds the pairs 8 sub .. 8 sub + 7 of the halves x1 = [0, D/2) and x2 = [D/2, D)): the
+// arithmetic of the append, shared by kv_append_rope_vec_kernel and the decode attention that
+// fuses the append, so both give the same bits.  Every lane of the warp calls it (the sum of
+// squares is an xor butterfly over the group's lanes); with rotate false o1 / o2 are x1 / x2 and
+// the lane adds nothing to its group's sum.
+template <int D>
+__device__ __forceinline__ void rope_norm_vec(const uint4& x1v, const uint4& x2v, const uint16_t* cos,
+                                              const uint16_t* sin, int pos, int sub, bool rotate, float eps,
+                                              float scale, float (&o1)[8], float (&o2)[8]) {
+  constexpr int L = D / 16;
+  constexpr int HALF = D / 2;
+  float y1[8], y2[8];
+  float acc = 0.f;
+  if (rotate) {
+    float x1[8], x2[8], c[8], sn[8];
+    unpack8(x1v, x1);
+    unpack8(x2v, x2);
+    const long long trow = static_cast<long long>(pos) * HALF + 8 * sub;
+    unpack8(*reinterpret_cast<const uint4*>(cos + trow), c);
+    unpack8(*reinterpret_cast<const uint4*>(sin + trow), sn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = round_bf16(__fmul_rn(x1[i], c[i]));
+      const float bb = round_bf16(__fmul_rn(x2[i], sn[i]));
+      const float cc = round_bf16(__fmul_rn(x1[i], -sn[i]));
+      const float dd = round_bf16(__fmul_rn(x2[i], c[i]));
+      y1[i] = round_bf16(__fadd_rn(a, bb));
+      y2[i] = round_bf16(__fadd_rn(cc, dd));
+      acc = __fadd_rn(acc, __fmul_rn(y1[i], y1[i]));
+      acc = __fadd_rn(acc, __fmul_rn(y2[i], y2[i]));
+    }
+  }
+#pragma unroll
+  for (int m = L / 2; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  if (rotate) {
+    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(D)), eps));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o1[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y1[i], r)), scale));
+      o2[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y2[i], r)), scale));
+    }
+  } else {
+    unpack8(x1v, o1);
+    unpack8(x2v, o2);
+  }
+}
+
 // Vectorised variant: L = D/16 lanes per vector, 16-byte loads and stores, 32/L vectors per warp.
 // Requires 16-byte aligned rows (checked on the host).  FP8: the cache vectors are stored as
 // e4m3 with a per-vector scale (e4m3x8 above), 8-byte stores.
@@ -246,44 +294,11 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
     }
     // lanes of a rotating vector in this warp still take part in the butterfly below
   }
-  float y1[8], y2[8];
-  float acc = 0.f;
-  if (rotate && ok) {
-    float x1[8], x2[8], c[8], sn[8];
-    unpack8(x1v, x1);
-    unpack8(x2v, x2);
-    const long long trow = static_cast<long long>(pos) * HALF + 8 * sub;
-    unpack8(*reinterpret_cast<const uint4*>(p.cos + trow), c);
-    unpack8(*reinterpret_cast<const uint4*>(p.sin + trow), sn);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = round_bf16(__fmul_rn(x1[i], c[i]));
-      const float bb = round_bf16(__fmul_rn(x2[i], sn[i]));
-      const float cc = round_bf16(__fmul_rn(x1[i], -sn[i]));
-      const float dd = round_bf16(__fmul_rn(x2[i], c[i]));
-      y1[i] = round_bf16(__fadd_rn(a, bb));
-      y2[i] = round_bf16(__fadd_rn(cc, dd));
-      acc = __fadd_rn(acc, __fmul_rn(y1[i], y1[i]));
-      acc = __fadd_rn(acc, __fmul_rn(y2[i], y2[i]));
-    }
-  }
-#pragma unroll
-  for (int m = L / 2; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
   float o1[8], o2[8];  // the bf16 values of the output vector, as floats
-  if (rotate && ok) {
-    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(D)), p.eps));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o1[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y1[i], r)), p.scale));
-      o2[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y2[i], r)), p.scale));
-    }
-    if (!FP8 || is_q) {  // q always goes out as bf16; fp8 cache vectors are stored below
-      *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
-      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
-    }
-  } else {
-    unpack8(x1v, o1);
-    unpack8(x2v, o2);
+  rope_norm_vec<D>(x1v, x2v, p.cos, p.sin, pos, sub, rotate && ok, p.eps, p.scale, o1, o2);
+  if (rotate && ok && (!FP8 || is_q)) {  // q always goes out as bf16; fp8 cache vectors below
+    *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
+    *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
   }
   if constexpr (FP8) {
     // every lane takes part in the amax butterfly; q vectors and idle lanes contribute nothing

@@ -641,7 +641,25 @@ int check_attn_pointers(const mcb_attn_args* a, const char* who) {
   for (int i = 0; i < 3; ++i)
     if (a->q_stride[i] < 0 || (a->q_stride[i] % 8) != 0)
       return fail(MCB_ERR_ALIGNMENT, "%s: q strides must be non-negative multiples of 8 elements", who);
+  if (a->fuse_append) {
+    if ((a->k_new == nullptr) != (a->v_new == nullptr) || a->rot_cos == nullptr || a->rot_sin == nullptr ||
+        a->rot_len <= 0)
+      return fail(MCB_ERR_INVALID_ARG, "%s: fused append needs rot_cos, rot_sin, rot_len > 0 and both or "
+                  "neither of k_new, v_new", who);
+    if (!aligned(a->rot_cos, 16) || !aligned(a->rot_sin, 16) ||
+        (a->k_new != nullptr && (!aligned(a->k_new, 16) || !aligned(a->v_new, 16))))
+      return fail(MCB_ERR_ALIGNMENT, "%s: fused append vectors and tables must be 16-byte aligned", who);
+    for (int i = 0; i < 3; ++i)
+      if (a->k_new != nullptr && (a->k_new_stride[i] < 0 || a->k_new_stride[i] % 8 || a->v_new_stride[i] < 0 ||
+                                  a->v_new_stride[i] % 8))
+        return fail(MCB_ERR_ALIGNMENT, "%s: k_new / v_new strides must be non-negative multiples of 8", who);
+  }
   return MCB_OK;
+}
+
+// Whether the planned call can fuse the append (the split kernel's bf16 path, one new token).
+bool plan_fusable(const mcb_attn_args* a, const AttnPlan& pl) {
+  return a->T == 1 && a->k_scale == nullptr && (a->D == 64 || a->D == 128) && pl.mode == kModeSplit;
 }
 
 // q as a 4-D tensor map {D, Hq, T, B} with its own strides; 128-query boxes of 64-column panels.
@@ -691,6 +709,9 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
 // Encodes the tensor maps, fills the kernel parameters with the workspace `ws` (and, for the
 // persistent kernel, the arrival counters) and launches.
 int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* counters, cudaStream_t st) {
+  if (a->fuse_append && !plan_fusable(a, pl))
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: the append fuses only for T = 1, a bf16 slot, D = 64 "
+                "or 128 and the split plan (mcb_decode_attn_fusable)");
   if (pl.mode == kModePrefill) return run_prefill(a, st);
   const bool fp8 = a->k_scale != nullptr;
   CUtensorMap km, vm;
@@ -711,6 +732,21 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.part_lse = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
     p.cluster = pl.cluster ? 1 : 0;
     p.counters = pl.counter_count > 0 ? counters : nullptr;
+    p.fuse = a->fuse_append ? 1 : 0;
+    p.k_new = static_cast<const uint16_t*>(a->k_new);
+    p.v_new = static_cast<const uint16_t*>(a->v_new);
+    for (int i = 0; i < 3; ++i) {
+      p.kns[i] = a->k_new_stride[i];
+      p.vns[i] = a->v_new_stride[i];
+    }
+    p.kc_out = static_cast<uint16_t*>(const_cast<void*>(a->k_cache));  // written with fuse_append
+    p.vc_out = static_cast<uint16_t*>(const_cast<void*>(a->v_cache));
+    p.rot_cos = static_cast<const uint16_t*>(a->rot_cos);
+    p.rot_sin = static_cast<const uint16_t*>(a->rot_sin);
+    p.rot_len = a->rot_len;
+    p.rotate_k = a->rotate_k;
+    p.norm_eps = a->norm_eps;
+    p.qk_scale = a->qk_scale;
     p.ring = a->ring != 0;
     p.B = a->B;
     p.T = a->T;
@@ -1289,6 +1325,12 @@ size_t mcb_decode_attn_counter_count(const mcb_attn_args* a) {
   AttnPlan pl;
   if (plan_attn(a, &pl) != MCB_OK) return 0;
   return pl.counter_count;
+}
+
+int mcb_decode_attn_fusable(const mcb_attn_args* a) {
+  AttnPlan pl;
+  if (plan_attn(a, &pl) != MCB_OK) return 0;
+  return plan_fusable(a, pl) ? 1 : 0;
 }
 
 int mcb_prefill_attn(const mcb_attn_args* a, void* stream) {

@@ -37,6 +37,11 @@ def _fusable(attn, x):
             and attn.head_dim % 2 == 0 and attn.head_dim <= 256)
 
 
+# The decode step's append and attention in one launch where the plan allows it (T = 1, a bf16
+# slot, the split plan; ops.append_attn), with the bits of the two launches.
+USE_FUSED_APPEND = True
+
+
 def attend(self, q, k, v, kv_cache):
     """The fused KV-cache branch of Attention.forward (modelcore/components/attention.py:144-178)
     from projected (B, T, H, D) q, k, v (k and v None for a consumer layer, produces_kv=False):
@@ -49,6 +54,11 @@ def attend(self, q, k, v, kv_cache):
     seqlens = kv_cache.cache_seqlens
     rope = self.rope
     kv_cache.check_room(T, rope.cos.size(1))
+    if USE_FUSED_APPEND:  # one launch where the plan allows it (ops.append_attn), else two
+        return ops.append_attn(q, k if self.produces_kv else None, v if self.produces_kv else None,
+                               k_cache, v_cache, seqlens, rope.cos, rope.sin, eps=self.norm.eps,
+                               scale=1.2, window=self.window, ring=ring, k_scale=k_scale,
+                               v_scale=v_scale)
     if self.produces_kv:
         q = ops.kv_append_rope(q, k, v, k_cache, v_cache, seqlens, rope.cos, rope.sin,
                                rotate_q=True, rotate_k=True, write_kv=True, eps=self.norm.eps,

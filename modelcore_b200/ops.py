@@ -345,6 +345,63 @@ def decode_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=
     return out
 
 
+def append_attn(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, eps=None, scale=1.2,
+                rotate_k=True, window=-1, ring=False, out=None, k_scale=None, v_scale=None):
+    """kv_append_rope followed by decode_attn -- one decode step of an attention layer from its
+    RAW projections q (B, T, Hq, D), k, v (B, T, Hkv, D; None for a layer that reads another
+    layer's slot) -- in ONE launch where the plan allows it (T = 1, a bf16 slot, D = 64 or 128,
+    the split plan: mcb_decode_attn_fusable), with the same bits as the two launches; otherwise
+    the two launches.  cache_seqlens is not advanced.  Returns the attention output."""
+    T, D = q.size(1), q.size(3)
+    fusable = k_cache.dtype == torch.bfloat16 and T == 1 and D in (64, 128)
+    if fusable:
+        if out is None:
+            out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+        args = _attn_args(q, k_cache, v_cache, cache_seqlens, window, None, 0, out, ring)
+        lib = _native.load()
+        fusable = bool(lib.mcb_decode_attn_fusable(ctypes.byref(args)))
+    if not fusable:
+        if k is not None:
+            q = kv_append_rope(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, rotate_q=True,
+                               rotate_k=rotate_k, write_kv=True, eps=eps, scale=scale, ring=ring,
+                               k_scale=k_scale, v_scale=v_scale)
+        else:
+            q = kv_append_rope(q, None, None, None, None, cache_seqlens, cos, sin, rotate_q=True,
+                               rotate_k=False, write_kv=False, eps=eps, scale=scale)
+        return decode_attn(q, k_cache, v_cache, cache_seqlens, window=window, ring=ring, out=out,
+                           k_scale=k_scale, v_scale=v_scale)
+    if not out.is_contiguous() or out.shape != q.shape:
+        raise RuntimeError("out must be a contiguous tensor shaped like q")
+    args.fuse_append = 1
+    if k is not None:
+        _need("k", k, 4)
+        _need("v", v, 4)
+        if k.shape != v.shape or k.shape[0] != q.shape[0] or k.shape[1] != 1 or k.shape[3] != D:
+            raise RuntimeError("k and v must be (B, 1, Hkv, D) like the slot")
+        args.k_new, args.v_new = k.data_ptr(), v.data_ptr()
+        args.k_new_stride[:] = _bthd_strides("k", k)
+        args.v_new_stride[:] = _bthd_strides("v", v)
+    for name, tab in (("cos", cos), ("sin", sin)):
+        _need(name, tab)
+        if not tab.is_contiguous() or tab.shape[-1] != D // 2:
+            raise RuntimeError(f"rotary {name} table must be contiguous with D/2={D // 2} columns")
+    args.rot_cos, args.rot_sin = cos.data_ptr(), sin.data_ptr()
+    args.rot_len = cos.numel() // (D // 2)
+    args.rotate_k = int(bool(rotate_k))
+    args.norm_eps = rms_norm_eps(eps)
+    args.qk_scale = scale
+    need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
+    ncount = int(lib.mcb_decode_attn_counter_count(ctypes.byref(args)))
+    if need:
+        ws = attn_workspace(q.device, need)
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    if ncount:
+        cnt = attn_counters(q.device, ncount)
+        args.counters, args.counter_count = cnt.data_ptr(), cnt.numel()
+    check(lib.mcb_decode_attn(ctypes.byref(args), _stream(q)))
+    return out
+
+
 def prefill_attn(q, k_cache, v_cache, cache_seqlens, *, window=-1, softmax_scale=None, out=None,
                  ring=False):
     """decode_attn's semantics on the tensor-core prefill kernel (mcb_prefill_attn), for any T:

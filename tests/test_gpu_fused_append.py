@@ -1,0 +1,133 @@
+"""GPU parity of the fused append (ops.append_attn / mcb_decode_attn with fuse_append): one launch
+that ropes, norms and scales the raw query and key of a decode step, writes the key and value into
+the slot and attends over it must give exactly what the two launches give (mcb_kv_append_rope,
+then mcb_decode_attn): the same cache bytes and the same attention output, bit for bit, on every
+split plan (one split, a cluster merge, partials), with windows, ring slots, GQA groups and
+layers that read another layer's slot."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from modelcore_b200 import ops
+    return ops
+
+
+def tables(rot_len, D):
+    ang = torch.arange(rot_len, dtype=torch.float32)[:, None] * \
+        (10000.0 ** (-torch.arange(0, D, 2, dtype=torch.float32) / D))[None]
+    return ang.cos().to(torch.bfloat16).cuda(), ang.sin().to(torch.bfloat16).cuda()
+
+
+CASES = [  # B, Hq, Hkv, D, Tmax, max_len, window, ring, produces_kv, num_ctas
+    (64, 12, 12, 64, 1024, 900, -1, False, True, 0),    # config 2's shape: one split per row group
+    (4, 32, 8, 128, 2048, 2000, -1, False, True, 0),    # few groups: splits merged in a cluster
+    (3, 16, 4, 128, 1024, 1000, 300, False, True, -12), # a window, 12 splits
+    (40, 32, 8, 128, 1400, 1390, -1, False, True, -20), # partials and the combine kernel
+    (2, 8, 2, 64, 512, 1500, 200, True, True, 0),       # a ring slot
+    (5, 16, 4, 128, 1024, 1000, -1, False, False, 0),   # a layer that reads another's slot
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "B{}Hq{}Hkv{}D{}w{}r{}kv{}n{}".format(
+    c[0], c[1], c[2], c[3], c[6], int(c[7]), int(c[8]), c[9]))
+def test_fused_append_equals_append_then_attention(ops, case):
+    B, Hq, Hkv, D, Tmax, max_len, window, ring, produces, nc = case
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + Hq + D)
+    qkv = (torch.randn(B, 1, Hq + 2 * Hkv, D, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    q, k, v = qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:]  # strided views, as packed
+    kc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    hi = max_len - 1
+    sl = torch.randint(hi // 2, hi + 1, (B,), device="cuda", generator=g, dtype=torch.int32)
+    cos, sin = tables(max(Tmax, max_len) + 8, D)
+    kc2, vc2 = kc.clone(), vc.clone()
+    # two launches
+    if produces:
+        qa = ops.kv_append_rope(q, k, v, kc, vc, sl, cos, sin, eps=1e-6, scale=1.2, ring=ring)
+    else:
+        qa = ops.kv_append_rope(q, None, None, None, None, sl, cos, sin, rotate_q=True, rotate_k=False,
+                                write_kv=False, eps=1e-6, scale=1.2)
+    want = ops.decode_attn(qa, kc, vc, sl, window=window, ring=ring, num_ctas=nc)
+    # one launch (num_ctas as above: the same split plan)
+    args = ops._attn_args(q, kc2, vc2, sl, window, None, nc, None, ring)
+    from modelcore_b200 import _native
+    assert _native.load().mcb_decode_attn_fusable(__import__("ctypes").byref(args)) == 1
+    got = fused(ops, q, k if produces else None, v if produces else None, kc2, vc2, sl, cos, sin,
+                window, ring, nc)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert torch.equal(kc2, kc) and torch.equal(vc2, vc)
+    assert torch.equal(got, want)
+
+
+def fused(ops, q, k, v, kc, vc, sl, cos, sin, window, ring, nc):
+    """ops.append_attn with an explicit split count (the tests pin the plan)."""
+    import ctypes
+    from modelcore_b200 import _native
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    args = ops._attn_args(q, kc, vc, sl, window, None, nc, out, ring)
+    args.fuse_append = 1
+    if k is not None:
+        args.k_new, args.v_new = k.data_ptr(), v.data_ptr()
+        args.k_new_stride[:] = ops._bthd_strides("k", k)
+        args.v_new_stride[:] = ops._bthd_strides("v", v)
+    D = q.size(3)
+    args.rot_cos, args.rot_sin = cos.data_ptr(), sin.data_ptr()
+    args.rot_len = cos.numel() // (D // 2)
+    args.rotate_k = 1
+    args.norm_eps = 1e-6
+    args.qk_scale = 1.2
+    lib = _native.load()
+    need = int(lib.mcb_decode_attn_workspace_size(ctypes.byref(args)))
+    ncount = int(lib.mcb_decode_attn_counter_count(ctypes.byref(args)))
+    if need:
+        ws = ops.attn_workspace(q.device, need)
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    if ncount:
+        cnt = ops.attn_counters(q.device, ncount)
+        args.counters, args.counter_count = cnt.data_ptr(), cnt.numel()
+    _native.check(lib.mcb_decode_attn(ctypes.byref(args), ops._stream(q)))
+    return out
+
+
+def test_append_attn_picks_the_fused_launch_and_falls_back(ops):
+    """ops.append_attn: one launch on a fusable plan, two (append + attention) otherwise -- the same
+    results either way."""
+    B, Hq, Hkv, D, Tmax = 8, 16, 4, 128, 8192
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, 1, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    sl = torch.randint(100, 8000, (B,), device="cuda", generator=g, dtype=torch.int32)
+    cos, sin = tables(Tmax + 8, D)
+    for window in (1000, -1):  # rows of 1,001 keys: split; 8k keys in 32 groups: split (few groups)
+        kc1, vc1, kc2, vc2 = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+        n0 = ops.launch_count()
+        got = ops.append_attn(q, k, v, kc1, vc1, sl, cos, sin, eps=1e-6, window=window)
+        launches = ops.launch_count() - n0
+        qa = ops.kv_append_rope(q, k, v, kc2, vc2, sl, cos, sin, eps=1e-6, scale=1.2)
+        want = ops.decode_attn(qa, kc2, vc2, sl, window=window)
+        torch.cuda.synchronize()
+        assert launches == 1
+        assert torch.equal(kc1, kc2) and torch.equal(got, want)
+    # a persistent plan (many groups of long rows) falls back to the two launches
+    B2 = 64
+    q2 = q.repeat(B2 // B, 1, 1, 1)
+    k2, v2 = k.repeat(B2 // B, 1, 1, 1), v.repeat(B2 // B, 1, 1, 1)
+    kc3 = kc.repeat(B2 // B, 1, 1, 1)
+    vc3 = vc.repeat(B2 // B, 1, 1, 1)
+    sl2 = sl.repeat(B2 // B)
+    kc4, vc4 = kc3.clone(), vc3.clone()
+    n0 = ops.launch_count()
+    got = ops.append_attn(q2, k2, v2, kc3, vc3, sl2, cos, sin, eps=1e-6)
+    assert ops.launch_count() - n0 == 2
+    qa = ops.kv_append_rope(q2, k2, v2, kc4, vc4, sl2, cos, sin, eps=1e-6, scale=1.2)
+    want = ops.decode_attn(qa, kc4, vc4, sl2)
+    torch.cuda.synchronize()
+    assert torch.equal(kc3, kc4) and torch.equal(got, want)

@@ -296,7 +296,7 @@ def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
     last add + norm, the advance and the LM-head epilogue),
     and the CUDA-graph decoder reproduces the eager fused decoder bit for bit."""
     modelcore, mcb = env
-    from modelcore_b200 import ops, step, workloads
+    from modelcore_b200 import integration, ops, step, workloads
     monkeypatch.setattr(step, "USE_FUSED_PROJ", fused_proj)
     mgr = mcb.ModelManager()
     model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
@@ -311,14 +311,18 @@ def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
         n0 = ops.launch_count()
         eager.step(cols[0])
         per_step = ops.launch_count() - n0
+        # the append runs inside the attention launch (integration.USE_FUSED_APPEND; these rows
+        # take the split plan) or as its own launch
+        append = 0 if integration.USE_FUSED_APPEND else 1
         if fused_proj:
             # the embedding; per layer q|k|v (add + norm inside), append, c_proj (+ residual),
             # gate|up (norm inside), silu * up (down_proj is cuBLAS); the final add + norm, the
             # advance, the LM-head epilogue
-            attn_launches = per_step - (1 + 4 * 5 + 1 + 1 + 1)
+            attn_launches = per_step - (1 + 4 * (4 + append) + 1 + 1 + 1)
         else:
-            # embedding + first norm, 4 per layer, the advance, the LM-head epilogue
-            attn_launches = per_step - (1 + 4 * 4 + 1 + 1)
+            # embedding + first norm, per layer two add + norms, silu * up and the append, the
+            # advance, the LM-head epilogue
+            attn_launches = per_step - (1 + 4 * (3 + append) + 1 + 1)
         assert attn_launches == 4, per_step           # one per layer
         graph.step(cols[0])                           # eager: the graph decoder's first step
         for col in cols[1:]:                          # capture, then replays

@@ -281,3 +281,25 @@ def test_linear_rejects_bad_arguments_on_the_host():
                                                     x=base, w=base + (8 << 20), y=base + (16 << 20))),
                                   None))
     assert st == _native.MCB_ERR_UNSUPPORTED and "shared memory" in msg
+
+
+def test_fused_append_is_offered_only_where_the_split_kernel_can_do_it():
+    """mcb_decode_attn_fusable decides from the shapes on the host: one new token a row, a bf16
+    slot, head size 64 or 128 and the split plan; a fused call outside that is rejected before any
+    launch (the pointers are never read)."""
+    lib = _native.load()
+    fusable = lambda **kw: lib.mcb_decode_attn_fusable(ctypes.byref(_attn(**kw)))
+    assert fusable() == 1                                     # 2 rows, 64-position slot: split
+    assert fusable(D=64, Hq=4, Hkv=4) == 1
+    assert fusable(T=2) == 0                                  # several new tokens
+    assert fusable(D=32) == 0
+    assert fusable(B=200, Tmax=65536) == 0                    # many groups of long rows: persistent
+    assert fusable(k_scale=1 << 20, v_scale=1 << 21, scale_tmax=64) == 0   # an fp8 slot
+    a = _attn(T=2, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000, cache_seqlens=0x5000,
+              fuse_append=1, rot_cos=0x6000, rot_sin=0x7000, rot_len=64)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "fuses only" in msg
+    a = _attn(q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000, cache_seqlens=0x5000,
+              fuse_append=1, rot_len=64)
+    st, msg = _err(lib.mcb_decode_attn(ctypes.byref(a), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "rot_cos" in msg

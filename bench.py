@@ -24,14 +24,24 @@ roofline   the decode-attention kernel: algorithmic KV bytes (exact keys per row
 kv_read_sweep  measurement config 5 (32 q / 8 kv heads of 128, lengths U[1, 32768] from seed 5,
            window -1 / 4096): one step = fused rope append + decode attention, timed on the device
            in CUDA graphs of consecutive steps on rotating groups of cache rows (no launch finds
-           its keys in L2).
+           its keys in L2).  On N GPUs each batch is partitioned over the ranks (B / N rows each,
+           balanced by length); time = max over ranks, bytes = sum.
 kv_read_sweep_fp8  the same over an fp8 (e4m3) cache with per-vector scales (an opt-in cache
-           format: bytes = e4m3 keys and values + fp32 scales), with the speed-up over bf16.
+           format: bytes = e4m3 keys and values + fp32 scales), with the speed-up over bf16 (N=1).
 gqa_decode measurement configs 3 and 4 (the 24 x 2048 GQA model with windows; config 4 with
            cross-layer KV sharing, a broadcast prefill and top-k sampling): a bounded sample of
-           their decode steps through ModelManager, tokens/s and the KV bytes read per second.
+           their decode steps through ModelManager, tokens/s and the KV bytes read per second; on
+           N GPUs config 3's 128 rows and config 4's 256 rows are sharded over the ranks (strong
+           scaling) and the timed region ends with the token gather.
+kv_copies  (N=1) the broadcast prefill copy, the per-step append and the append of whole prompts
+           (config 2's 64 x 512 tokens, config 3's 8,192) against the HBM copy roofline.
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
-           sample of the same workload (rank 0, N = 1).
+           sample of the same workload (rank 0, N = 1); cpu_baseline_config5 the reference's
+           flash_attn_with_kvcache on config 5 at batch 8.
+
+Output: rank 0 prints every measurement but the headline as its own JSON line
+{"bench_extra": name, "n_gpus": N, "data": ...}, then the headline line last (compact, with a
+summary of the extras: kv_read_sweep_frac, gqa_decode_tokens_per_s, prefill_append_frac).
 """
 import argparse
 import json
@@ -51,7 +61,7 @@ PROMPT_LEN = 512
 DECODE_LEN = 512
 CPU_SAMPLE_ROWS = 8
 FALLBACK_HBM_GBS = 6650.0
-# From the ncu capture of the split decode-attention kernel on config 2 (profiles/decode_attn_cfg2.md):
+# From an ncu capture of the split decode-attention kernel on config 2 (context 516):
 NCU_READ_BYTES_PER_TILE_D64 = 16402   # 113.37 MB read / 6,912 fetched tiles
 NCU_WRITE_BYTES_CFG2 = 3_500_000       # mean of the two captured launches
 METRIC = "decode tokens/sec + KV-read HBM GB/s (% of peak) at 1/2/4/8 B200"
@@ -226,7 +236,8 @@ def _attention_roofline(dec, peak, reps=4):
     """Mean device time of the decode-attention kernel on the bench's own cache (its current
     lengths): the 12 per-slot launches of one step are captured in a CUDA graph (so host launch
     cost is not timed) and replayed `reps` times between CUDA events on the replay stream; the
-    12 slots hold 1.6 GB, far above L2.  Algorithmic bytes = exact keys x 2 x Hkv x D x 2."""
+    12 slots hold 1.6 GB, far above L2.  Algorithmic bytes = exact keys x 2 x Hkv x D x 2.
+    `kernel` is the template instance the library reports for these launches."""
     import torch
     from modelcore_b200 import ops
     cache = dec.kv_cache
@@ -239,6 +250,7 @@ def _attention_roofline(dec, peak, reps=4):
     for s in range(S):  # warm (allocates the cached workspace outside the capture)
         ops.decode_attn(q, cache.k_cache[s], cache.v_cache[s], cache.cache_seqlens, out=out)
     torch.cuda.synchronize()
+    kernel = ops.last_attn_kernel()
     g = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -258,34 +270,60 @@ def _attention_roofline(dec, peak, reps=4):
     us = e0.elapsed_time(e1) * 1e3 / (reps * S)
     del g
     gbs = bytes_per_launch / (us * 1e-6) / 1e9
-    # DRAM traffic per launch from the ncu capture of this kernel on this model (profiles/
-    # decode_attn_cfg2.md): 16,402 bytes read per fetched 64-key tile of one kv head (K and V)
-    # plus ~3.6 MB written, scaled to the tiles this launch fetches.
+    # DRAM traffic per launch, scaled from an ncu capture of this kernel on this model (a shorter
+    # context): NCU_READ_BYTES_PER_TILE_D64 read per fetched 64-key tile of one kv head (K and V)
+    # plus NCU_WRITE_BYTES_CFG2 written (the outputs), times the tiles this launch fetches
     tiles = int(sum((L + 1 + 63) // 64 for L in lens)) * H
     traffic = tiles * NCU_READ_BYTES_PER_TILE_D64 + NCU_WRITE_BYTES_CFG2
-    ncount = ops.decode_attn_counter_count(q, cache.k_cache[0], cache.v_cache[0], cache.cache_seqlens)
-    # config 2's 768 split CTAs run the 2-stage copy (all resident in one wave)
-    kernel = ("mcb::decode_attn_split_kernel<64,1,16,2>" if ncount == 0 else
-              "mcb::decode_attn_kernel<64,1,16,3>")
     return {"bytes_per_launch": bytes_per_launch, "us_per_launch": us, "achieved_gbs": gbs,
-            "frac": gbs / peak, "mean_context": keys / B, "traffic": traffic, "kernel": kernel}
+            "frac": gbs / peak, "mean_context": keys / B, "traffic": traffic, "kernel": kernel,
+            "tiles": tiles}
 
 
-def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096), fp8=False):
+def _sum_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def _sweep_rows(B, rank, world):
+    """Config 5's B rows (lengths U[1, 32768] from seed 5, each row's position = length - 1) and
+    the ones this rank decodes: all of them on one GPU; with world > 1 an equal share balanced
+    by length (sharding.balanced_rows)."""
+    import numpy as np
+    from modelcore_b200.sharding import balanced_rows
+    lens = np.random.default_rng(5).integers(1, 32769, size=B) - 1
+    if world == 1:
+        return lens, lens
+    mine = balanced_rows(lens.tolist(), world, equal_counts=True)[rank]
+    return lens, lens[mine]
+
+
+def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096), fp8=False, rank=0,
+                   world=1):
     """Config 5: fused rope append + decode attention per step.  Each (batch, window) point is
     timed on the device in a CUDA graph of consecutive steps, each on a different group of cache
     rows (kc[g*B:(g+1)*B]) so that no launch finds its keys in L2 (the groups cycled through hold
     more than the 126 MB L2 between two visits); attention alone and append + attention.
     fp8: the same over an e4m3 cache with per-vector scales (bytes = e4m3 keys and values plus
-    their fp32 scales)."""
-    import numpy as np
+    their fp32 scales).
+    world > 1: the batch is partitioned over the ranks (each decodes B / world rows, an equal
+    share balanced by length; batches not divisible by world are skipped); a point's time is
+    the max over ranks, its bytes the sum, its fraction against world x the per-GPU peak."""
     import torch
     from modelcore_b200 import ops
     Hq, Hkv, D, Tmax = 32, 8, 128, 32769
     stream = torch.cuda.current_stream()
-    g = torch.Generator(device="cuda").manual_seed(5)
+    g = torch.Generator(device="cuda").manual_seed(5 + rank)
+    batches = [B for B in batches if B % world == 0]
     rows = []
-    max_b = max(batches)
+    if not batches:
+        return rows
+    max_b = max(batches) // world
     kc = torch.empty(max_b, Tmax, Hkv, D, device="cuda", dtype=ops.FP8 if fp8 else torch.bfloat16)
     vc = torch.empty_like(kc)
     for c in (kc, vc):
@@ -321,19 +359,20 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096), fp8=F
         return e0.elapsed_time(e1) * 1e3 / (3 * n)
 
     for B in batches:
-        lens = np.random.default_rng(5).integers(1, 32769, size=B) - 1
+        _, lens = _sweep_rows(B, rank, world)
+        b = int(lens.size)
         sl = torch.from_numpy(lens).to(torch.int32).cuda()
-        q = torch.randn(B, 1, Hq, D, device="cuda", generator=g, dtype=torch.bfloat16)
-        k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
-        v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
-        groups = max(1, min(16, max_b // B))
-        kcs = [kc[i * B:(i + 1) * B] for i in range(groups)]
-        vcs = [vc[i * B:(i + 1) * B] for i in range(groups)]
-        kss = [kscl[i * B:(i + 1) * B] if fp8 else None for i in range(groups)]
-        vss = [vscl[i * B:(i + 1) * B] if fp8 else None for i in range(groups)]
+        q = torch.randn(b, 1, Hq, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        k = torch.randn(b, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        v = torch.randn(b, 1, Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        groups = max(1, min(16, max_b // b))
+        kcs = [kc[i * b:(i + 1) * b] for i in range(groups)]
+        vcs = [vc[i * b:(i + 1) * b] for i in range(groups)]
+        kss = [kscl[i * b:(i + 1) * b] if fp8 else None for i in range(groups)]
+        vss = [vscl[i * b:(i + 1) * b] if fp8 else None for i in range(groups)]
         for w in windows:
             keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
-            nbytes = keys * per_key
+            nbytes = _sum_over_ranks(keys * per_key, world)
             torch.cuda.nvtx.range_push(f"sweep_b{B}_w{w}{'_fp8' if fp8 else ''}")
             qr = ops.kv_append_rope(q, k, v, kcs[0], vcs[0], sl, cos, sin, k_scale=kss[0], v_scale=vss[0])
             out = torch.empty_like(qr)
@@ -351,13 +390,17 @@ def _kv_read_sweep(peak, batches=(1, 8, 64, 256, 512), windows=(-1, 4096), fp8=F
                                             k_scale=kss[j], v_scale=vss[j])
                     ops.decode_attn(qi, kcs[j], vcs[j], sl, window=w, out=out, k_scale=kss[j], v_scale=vss[j])
 
-            ta = graph_us(attn_only, n)
-            ts = graph_us(step, n)
+            _barrier(world)
+            ta = _max_over_ranks(graph_us(attn_only, n), world)
+            ts = _max_over_ranks(graph_us(step, n), world)
             torch.cuda.nvtx.range_pop()
             gbs = nbytes / (ta * 1e-6) / 1e9
-            rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
-                         "attn_us": round(ta, 1), "step_us": round(ts, 1),
-                         "kv_gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
+            row = {"batch": B, "window": w, "mean_keys": round(nbytes / per_key / B, 1),
+                   "attn_us": round(ta, 1), "step_us": round(ts, 1),
+                   "kv_gbs": round(gbs, 1), "frac": round(gbs / (peak * world), 3)}
+            if world > 1:
+                row["rows_per_gpu"] = b
+            rows.append(row)
     del kc, vc, kscl, vscl
     torch.cuda.empty_cache()
     return rows
@@ -375,19 +418,26 @@ def _with_speedup(rows8, rows16):
     return out
 
 
-def _gqa_decode(config, steps=64):
-    """Configs 3 and 4 on one GPU, a bounded sample of their decode runs (the full runs are 1024
-    and 256 steps): the 24-block GQA model (16 q / 4 kv heads of 128, windows of 1024 on three
-    layers of four), bf16 random-init weights (seed 0), through ModelManager and the CUDA-graph
-    decoder.  Config 3: 128 prompts of U[1024, 8192] tokens (seed 2), prefilled one by one
-    (prefill_row), `steps` greedy steps.  Config 4: odd layers read the preceding even layer's
-    slot; one 4,096-token prompt (seed 3) prefilled once and broadcast to 256 rows, `steps`
-    steps sampled at temperature 1.0, top_k 50 (seed 4).  kv_gbs: the KV bytes the step's
-    attention reads (every layer, its visible keys) / the step time."""
+def _gqa_decode(config, peak, steps=64, rank=0, world=1):
+    """Configs 3 and 4, a bounded sample of their decode runs (the full runs are 1024 and 256
+    steps): the 24-block GQA model (16 q / 4 kv heads of 128, windows of 1024 on three layers of
+    four), bf16 random-init weights (seed 0), through ModelManager and the CUDA-graph decoder.
+    Config 3: 128 prompts of U[1024, 8192] tokens (seed 2), prefilled one by one (prefill_row),
+    `steps` greedy steps.  Config 4: odd layers read the preceding even layer's slot; one
+    4,096-token prompt (seed 3) prefilled once and broadcast to 256 rows, `steps` steps sampled at
+    temperature 1.0, top_k 50 (seed 4).
+    world > 1 (strong scaling, one process per GPU, full weights on every rank): config 3's 128
+    rows are partitioned by length (sharding.balanced_rows, an equal share per rank), config 4's
+    256 rows are split evenly and every rank prefills the prompt itself and broadcasts it into its
+    own rows.  The timed region ends with the gather of every rank's tokens (NCCL, the path's only
+    collective); the step time is the max over ranks.
+    kv_gbs: the KV bytes the steps' attention reads (every layer, its visible keys, all ranks) /
+    the step time."""
     import numpy as np
     import torch
     import modelcore_b200
     from modelcore_b200 import workloads
+    from modelcore_b200.sharding import balanced_rows, gather_tokens
     mgr = modelcore_b200.ModelManager()
     model = mgr.create_model(workloads.gqa_window_config(kv_share=(config == 4)), device=torch.device("cuda"),
                              seed=0).to(torch.bfloat16).eval()
@@ -395,50 +445,89 @@ def _gqa_decode(config, steps=64):
     windows = [b.mixer.window for b in blocks]
     Hkv, D = blocks[0].mixer.n_kv_head, blocks[0].mixer.head_dim
     stream = torch.cuda.current_stream()
+    n_rows = 128 if config == 3 else 256
     with torch.inference_mode():
         t0 = time.perf_counter()
         if config == 3:
             lens = torch.randint(1024, 8193, (128,), generator=torch.Generator().manual_seed(2))
             toks = workloads.prompts(128, 8192, seed=2)
-            prompts = [toks[i, :int(lens[i])].tolist() for i in range(128)]
+            mine = balanced_rows(lens.tolist(), world, equal_counts=True)[rank]
+            prompts = [toks[i, :int(lens[i])].tolist() for i in mine]
             dec = mgr.new_decoder(model, prompts, max_tokens=steps + 8, cuda_graph=True, batched_prefill=False)
         else:
             prompt = workloads.prompts(1, 4096, seed=3)[0].tolist()
-            dec = mgr.new_decoder(model, [prompt], num_samples=256, max_tokens=steps + 8, cuda_graph=True)
+            dec = mgr.new_decoder(model, [prompt], num_samples=n_rows // world, max_tokens=steps + 8,
+                                  cuda_graph=True)
         torch.cuda.synchronize()
-        prefill_s = time.perf_counter() - t0
-        gen = torch.Generator(device="cuda").manual_seed(4)
+        prefill_s = _max_over_ranks(time.perf_counter() - t0, world)
+        gen = torch.Generator(device="cuda").manual_seed(4 + rank)
 
         def run(n):
             if config == 3:
-                dec.greedy_steps(n)
-            else:
-                dec.sample_steps(n, temperature=1.0, top_k=50, generator=gen)
+                return dec.greedy_steps(n)
+            return dec.sample_steps(n, temperature=1.0, top_k=50, generator=gen)
 
         run(3)  # eager step, graph capture, one replay
         before = dec.kv_cache.host_lens().astype(np.int64)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _barrier(world)
         torch.cuda.nvtx.range_push(f"gqa_decode_cfg{config}")
         e0.record(stream)
-        run(steps)
+        toks_out = run(steps)
+        if world > 1:
+            gather_tokens(toks_out)
         e1.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
     B = int(before.size)
     keys = 0
     for i in range(steps):
         L = before + i  # the new token's position
         for w in windows:
             keys += int(np.minimum(L + 1, w + 1).sum()) if w >= 0 else int((L + 1).sum())
-    kv_bytes = keys * 2 * Hkv * D * 2
+    kv_bytes = _sum_over_ranks(keys * 2 * Hkv * D * 2, world)
+    ctx = _sum_over_ranks(float(before.sum()), world) / n_rows
+    kv_gbs = kv_bytes / (ms * 1e-3) / 1e9
     out = {"workload": f"config {config}: 24 x 2048 GQA (16/4 heads of 128, window 1024 on 3 of 4 layers"
                        + (", odd layers sharing the even layer's slot" if config == 4 else "")
-                       + f"), {B} rows, {steps} of the run's decode steps",
-           "rows": B, "mean_context": round(float(before.mean()) + steps / 2, 1),
-           "tokens_per_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 3),
-           "kv_gbs": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "prefill_s": round(prefill_s, 2)}
+                       + f"), {n_rows} rows" + (f" over {world} GPUs ({B} per GPU)" if world > 1 else "")
+                       + f", {steps} of the run's decode steps",
+           "rows": n_rows, "n_gpus": world, "mean_context": round(ctx + steps / 2, 1),
+           "tokens_per_s": round(n_rows * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 3),
+           "kv_gbs": round(kv_gbs, 1), "kv_frac_of_peak": round(kv_gbs / (peak * world), 3),
+           "prefill_s": round(prefill_s, 2)}
     del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def _prefill_append(peak, timed):
+    """Piece 1 at T_new = P -- the append of whole prompts -- against the HBM copy roofline:
+    config 2's prefill (64 rows x 512 tokens, 12 q / 12 kv heads of 64) and config 3's longest
+    prompt (one row of 8,192 tokens, 16 q / 4 kv heads of 128), one attention layer's
+    mcb_kv_append_rope each.  Algorithmic bytes: q, k, v read, the rotated q written, k' and v
+    written into the slot, and the rotary rows of the P positions (cos and sin) read once."""
+    import torch
+    from modelcore_b200 import ops
+    out = []
+    for name, B, T, Hq, Hkv, D in (("config 2 prefill: 64 rows x 512 tokens, 12/12 heads of 64", 64, 512, 12, 12, 64),
+                                   ("config 3 prompt: 1 row x 8192 tokens, 16/4 heads of 128", 1, 8192, 16, 4, 128)):
+        g = torch.Generator(device="cuda").manual_seed(7)
+        qkv = torch.randn(B, T, Hq + 2 * Hkv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+        q, k, v = qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:]  # views of one packed GEMM output
+        kc = torch.zeros(B, 1024 if T <= 512 else T + 1024, Hkv, D, device="cuda", dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        sl = torch.zeros(B, dtype=torch.int32, device="cuda")
+        ang = torch.arange(kc.size(1), device="cuda", dtype=torch.float32)[:, None] * \
+            (100000.0 ** (-torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))[None]
+        cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+        q_out = torch.empty(B, T, Hq, D, device="cuda", dtype=torch.bfloat16)
+        us = timed(lambda: ops.kv_append_rope(q, k, v, kc, vc, sl, cos, sin, q_out=q_out))
+        nbytes = B * T * D * 2 * ((Hq + 2 * Hkv) + Hq + 2 * Hkv) + T * D * 2
+        out.append({"workload": name, "bytes": nbytes, "us": round(us, 1),
+                    "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 3)})
+        del qkv, kc, vc, q_out
     torch.cuda.empty_cache()
     return out
 
@@ -450,7 +539,8 @@ def _copy_and_append(peak):
     heads of 128, into 256 rows of a 4,352-position cache): algorithmic bytes = the source read
     once + every destination row written.  kv_append: config 5's per-step fused rope append at
     batch 512 (32 q / 8 kv heads of 128): q, k, v read, q' and the cache rows written, the rotary
-    rows read.  Each timed with CUDA events around single launches, L2 flushed before each."""
+    rows read.  prefill_append: the append of whole prompts (_prefill_append).  Each timed with
+    CUDA events around single launches, L2 flushed before each, median of 5."""
     import torch
     import modelcore_b200
     from modelcore_b200 import ops
@@ -505,6 +595,8 @@ def _copy_and_append(peak):
     out["kv_append"] = {"workload": "config 5 step: batch 512, 32 q / 8 kv heads of 128",
                         "bytes": nbytes, "us": round(us, 2),
                         "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 3)}
+    del q, k, v, kc, vc, q_out
+    out["prefill_append"] = _prefill_append(peak, timed)
     del flush
     torch.cuda.empty_cache()
     return out
@@ -578,6 +670,49 @@ def _cpu_reference_decode(rows, steps, warmup, threads=None):
     return rows * steps / dt, dt / steps, threads
 
 
+def _cpu_reference_attention(B=8, windows=(-1, 4096), reps=2, threads=None):
+    """Config 5 on the host cores through the reference's own kernel call: modelcore's
+    flash_attn_with_kvcache on its SDPA path (modelcore/kernels/flash_attn.py:306-366), fp32,
+    B rows of 32 q / 8 kv heads of 128 with the GPU sweep's lengths (U[1, 32768] from seed 5),
+    one call = one decode step (the insert of one K/V per row + the attention over the cache).
+    Per point: the call time, keys/s, tokens/s and the same algorithmic KV bytes as the GPU
+    sweep (exact keys x 2 x Hkv x D x 2, i.e. the bf16 cache's bytes; the fp32 cache the CPU
+    reads holds twice as many)."""
+    import numpy as np
+    import torch
+    _ensure_modelcore()
+    from modelcore.kernels.flash_attn import flash_attn as fa
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    Hq, Hkv, D, Tmax = 32, 8, 128, 32769
+    lens = np.random.default_rng(5).integers(1, 32769, size=B) - 1
+    g = torch.Generator().manual_seed(5)
+    kc = torch.randn(B, Tmax, Hkv, D, generator=g)
+    vc = torch.randn(B, Tmax, Hkv, D, generator=g)
+    q = torch.randn(B, 1, Hq, D, generator=g)
+    k = torch.randn(B, 1, Hkv, D, generator=g)
+    v = torch.randn(B, 1, Hkv, D, generator=g)
+    sl = torch.from_numpy(lens).to(torch.int32)
+    rows = []
+    with torch.inference_mode():
+        for w in windows:
+            call = lambda: fa.flash_attn_with_kvcache(q, kc, vc, k=k, v=v, cache_seqlens=sl, causal=True,
+                                                     window_size=(w, 0))
+            call()
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                call()
+            dt = (time.perf_counter() - t0) / reps
+            keys = int(sum((L + 1) if w < 0 else min(L + 1, w + 1) for L in lens))
+            gbs = keys * 2 * Hkv * D * 2 / dt / 1e9
+            rows.append({"batch": B, "window": w, "mean_keys": round(keys / B, 1),
+                         "call_ms": round(dt * 1e3, 1), "keys_per_s": round(keys / dt),
+                         "tokens_per_s": round(B / dt, 2), "kv_gbs": round(gbs, 2)})
+    return {"value": rows, "unit": "per point", "cores": threads, "kind": "reference",
+            "sample": f"config 5 at batch {B} (of 1-512), {reps} timed calls per window after one "
+                      f"warm-up, modelcore flash_attn_with_kvcache SDPA path fp32 ({_cpu_model()})"}
+
+
 def _cpu_model():
     try:
         with open("/proc/cpuinfo") as fh:
@@ -590,15 +725,16 @@ def _cpu_model():
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only)."""
+    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only), on
+    the same 64 rows of config 2 the GPU decodes per rank (prefill untimed)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    rows = CPU_SAMPLE_ROWS
+    rows = ROWS_PER_GPU
     tps, sps, cores = _cpu_reference_decode(rows, args.steps, args.warmup)
-    sample = (f"{rows} of the 64 rows per GPU, 512-token prompts, {args.steps} timed greedy decode "
-              f"steps after {args.warmup} warm-up steps, modelcore SDPA path in fp32 on "
-              f"{cores} threads ({_cpu_model()})")
+    sample = (f"the 64 rows of one GPU, 512-token prompts (prefill untimed), {args.steps} timed "
+              f"greedy decode steps after {args.warmup} warm-up steps, modelcore Decoder + SDPA "
+              f"path in fp32 on {cores} threads ({_cpu_model()})")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tps, 2), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -606,7 +742,8 @@ def run_reference(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded uniform token ids)",
         "config": _config(args.gpus),
         "cpu_baseline": {"value": round(tps, 2), "unit": "tokens/s", "cores": cores,
-                         "kind": "reference", "sample": sample},
+                         "kind": "reference", "sample": sample,
+                         "per_row_tokens_per_s": round(tps / rows, 3)},
         "e2e": {"value": round(tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -641,13 +778,24 @@ def run_sweep_only(args):
                       "peak_gbs": peak}), flush=True)
 
 
+def _print_extras(extras, world):
+    """The measurements beside the headline, one JSON line each, printed before it (the headline
+    is the last line): {"bench_extra": name, "n_gpus": N, "data": ...}."""
+    for name, obj in extras.items():
+        if obj is not None:
+            print(json.dumps({"bench_extra": name, "n_gpus": world, "data": obj}), flush=True)
+
+
+def _sweep_summary(rows):
+    return {f"b{r['batch']}_w{r['window']}": r["frac"] for r in rows} if rows else None
+
+
 def run_b200(args):
     import torch
     _ensure_modelcore()
     import modelcore_b200
     from modelcore_b200 import step as _step
     _step.USE_FUSED_PROJ = args.linear == "mcb"
-    from modelcore_b200 import ops
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
     steps_needed = 1 + args.warmup + max(args.steps, args.e2e_steps or 0) + 2
@@ -708,37 +856,48 @@ def run_b200(args):
         wall = time.perf_counter() - t0
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
     e2e_value = B * world * e2e_steps / (e2e_ms * 1e-3)
-
+    launches_per_step = dec.launches_per_step  # libmcb200 kernels in one captured step
     roof = _attention_roofline(dec, peak)
-    sweep = sweep8 = None
-    if world == 1 and not args.no_sweep:
-        sweep = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
-                               windows=tuple(args.sweep_windows))
-        sweep8 = _with_speedup(_kv_read_sweep(peak, batches=tuple(args.sweep_batches),
-                                              windows=tuple(args.sweep_windows), fp8=True), sweep)
-    copies = prefill = None
     prompt_prefill = {"workload": f"{B} prompts x {PROMPT_LEN} tokens per GPU, one forward "
                                   "(GraphDecoder batched ragged prefill)",
                       "batched_ms": round(dec.prefill_ms, 2)}
-    gqa = None
     if world == 1 and not args.no_sweep:
-        copies = _copy_and_append(peak)
-        prefill = _prefill(_bf16_peak())
-        gqa = [_gqa_decode(3), _gqa_decode(4)]
         from modelcore_b200 import workloads
         mine = workloads.prompts(ROWS_PER_GPU, PROMPT_LEN, seed=1).tolist()
         prompt_prefill["per_prompt_ms"] = round(_per_prompt_prefill_ms(mgr, model, mine), 2)
         prompt_prefill["per_prompt"] = "modelcore's Decoder order: each prompt at batch 1, then prefill_row"
+    del dec, model, mgr, cache
+    torch.cuda.empty_cache()
+
+    # the other measurement configs: on one GPU all of them; on N GPUs the ones the path shards
+    # (config 3 and 4 rows, config 5 batches partitioned over the ranks, no collective but the
+    # token gather)
+    extras = {}
+    if not args.no_sweep:
+        extras["kv_read_sweep"] = _kv_read_sweep(peak, batches=tuple(args.sweep_batches),
+                                                 windows=tuple(args.sweep_windows), rank=rank, world=world)
+        extras["gqa_decode"] = [_gqa_decode(c, peak, rank=rank, world=world) for c in (3, 4)]
+        if world == 1:
+            extras["kv_read_sweep_fp8"] = _with_speedup(
+                _kv_read_sweep(peak, batches=tuple(args.sweep_batches), windows=tuple(args.sweep_windows),
+                               fp8=True), extras["kv_read_sweep"])
+            extras["kv_copies"] = _copy_and_append(peak)
+            extras["prefill_attention"] = _prefill(_bf16_peak())
+    extras["prompt_prefill"] = prompt_prefill
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
         cpu = {"value": round(tps, 2), "unit": "tokens/s", "cores": cores, "kind": "reference",
+               "per_row_tokens_per_s": round(tps / CPU_SAMPLE_ROWS, 3),
                "sample": f"{CPU_SAMPLE_ROWS} of the 64 rows, 512-token prompts, 5 timed greedy "
-                         f"steps, modelcore SDPA path fp32 ({_cpu_model()})"}
+                         f"steps, modelcore Decoder + SDPA path fp32 ({_cpu_model()}); the "
+                         f"--impl reference arm runs all 64 rows"}
+        extras["cpu_baseline_config5"] = _cpu_reference_attention()
 
     if rank != 0:
         return
-    launches_per_step = dec.launches_per_step  # libmcb200 kernels in one captured step
+    _print_extras(extras, world)
+    sweep, gqa, copies = extras.get("kv_read_sweep"), extras.get("gqa_decode"), extras.get("kv_copies")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -749,10 +908,7 @@ def run_b200(args):
                                  "on libmcb200",
                         "plain": "modelcore's op-by-op forward around the libmcb200 append and "
                                  "attention"}[args.step],
-        "projections": {"mcb": "libmcb200 mcb_linear (one CTA per 16-32 output features, mma.sync, "
-                               "weights prefetched under programmatic dependent launch, norms and "
-                               "residual adds fused in); down_proj on cuBLAS",
-                        "cublas": "torch F.linear (cuBLAS)"}[args.linear],
+        "projections": {"mcb": "libmcb200 mcb_linear", "cublas": "torch F.linear (cuBLAS)"}[args.linear],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
                     "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
                     "attention_kernel_gbs": round(roof["achieved_gbs"], 1),
@@ -761,8 +917,9 @@ def run_b200(args):
         "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1),
                      "peak": peak, "unit": "GB/s", "frac": round(roof["frac"], 4),
                      "traffic": roof["traffic"], "kernel": roof["kernel"],
-                     "traffic_source": "ncu capture of this kernel on this model at context 516 "
-                                       "(profiles/decode_attn_cfg2.md), scaled by fetched 64-key tiles",
+                     "traffic_source": "scaled constant: DRAM bytes per fetched 64-key tile from an "
+                                       "ncu capture of this kernel on this model, times the "
+                                       f"{roof['tiles']} tiles of this launch",
                      "algorithmic_bytes_per_launch": roof["bytes_per_launch"],
                      "us_per_launch": round(roof["us_per_launch"], 2),
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
@@ -772,12 +929,10 @@ def run_b200(args):
         "gpu_launches": int(launches_per_step * args.steps) if launches_per_step else None,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
-        "kv_read_sweep": sweep,
-        "kv_read_sweep_fp8": sweep8,
-        "gqa_decode": gqa,
-        "kv_copies": copies,
-        "prefill_attention": prefill,
-        "prompt_prefill": prompt_prefill,
+        "kv_read_sweep_frac": _sweep_summary(sweep),
+        "gqa_decode_tokens_per_s": {f"config {c}": r["tokens_per_s"] for c, r in zip((3, 4), gqa)} if gqa else None,
+        "prefill_append_frac": [r["frac"] for r in copies["prefill_append"]] if copies else None,
+        "extras_printed_above": [k for k, v in extras.items() if v is not None],
     }
     print(json.dumps(line), flush=True)
 
@@ -819,7 +974,8 @@ def main():
         import torch
         _ensure_modelcore()
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        print(json.dumps({"gqa_decode": [_gqa_decode(c) for c in args.gqa_configs]}), flush=True)
+        peak, _ = _peaks()
+        print(json.dumps({"gqa_decode": [_gqa_decode(c, peak) for c in args.gqa_configs]}), flush=True)
     else:
         run_b200(args)
         import torch.distributed as dist

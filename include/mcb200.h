@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 6
+#define MCB_ABI_VERSION 7
 
 typedef enum {
   MCB_OK = 0,
@@ -239,7 +239,11 @@ int mcb_prefill_attn(const mcb_attn_args* args, void* stream);
  *
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with
  * that device current, which may load the library's kernels); make that first call before any
- * stream capture on the device.  Every call on a device shares the one array, so calls whose
+ * stream capture on the device.  The address is kept per device ordinal for the life of the
+ * process and belongs to the device's primary context: after cudaDeviceReset on that device, or
+ * with a non-primary driver context current on it, the kept address is stale, so a process that
+ * resets a device or runs its own driver contexts must not call this entry point on that device
+ * afterwards.  Every call on a device shares the one array, so calls whose
  * kernels can overlap on the GPU (other streams, other host threads) race on it: serialise them
  * on one stream.  Of the array only the arrival counters must start at zero, and each call
  * clears the ones it uses first (cudaMemsetAsync on the caller's stream, no allocation); every
@@ -380,6 +384,12 @@ int mcb_device_error(int32_t* code, void* stream);
 
 /* Kernels this library has enqueued in this process (host-side count, for launch accounting). */
 uint64_t mcb_launch_count(void);
+
+/* The template instance of the attention kernel the calling thread enqueued last (e.g.
+ * "mcb::decode_attn_split_kernel<64,1,16,2>"; empty before the first), as the profiler names
+ * it: lets a benchmark report the kernel its timing is about.  No counterpart in the reference
+ * (modelcore has no native kernels).  Returns MCB_OK, or MCB_ERR_INVALID_ARG for an empty buffer. */
+int mcb_last_attn_kernel(char* buf, size_t len);
 
 #ifdef __cplusplus
 }

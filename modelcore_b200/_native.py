@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -62,6 +62,7 @@ EXPORTED_SYMBOLS = (
     "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
+    "mcb_last_attn_kernel",
 )
 
 _i64x3 = ctypes.c_int64 * 3
@@ -234,6 +235,8 @@ def _declare(lib):
     lib.mcb_device_error.argtypes = [P(ctypes.c_int32), ctypes.c_void_p]
     lib.mcb_launch_count.restype = ctypes.c_uint64
     lib.mcb_launch_count.argtypes = []
+    lib.mcb_last_attn_kernel.restype = ctypes.c_int
+    lib.mcb_last_attn_kernel.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
 
 
 def lib_path():

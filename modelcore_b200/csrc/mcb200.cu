@@ -27,6 +27,16 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
+// The attention kernel (template instance) this thread enqueued last: mcb_last_attn_kernel.
+thread_local char g_last_attn_kernel[96] = "";
+
+void note_attn_kernel(const char* name, int D, int nqt, int stages, bool fp8) {
+  if (nqt > 0)
+    snprintf(g_last_attn_kernel, sizeof(g_last_attn_kernel), "mcb::%s<%d,%d,16,%d%s>", name, D, nqt,
+             stages, fp8 ? ",true" : "");
+  else
+    snprintf(g_last_attn_kernel, sizeof(g_last_attn_kernel), "mcb::%s<%d>", name, D);
+}
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -187,6 +197,7 @@ struct PrefillVariant {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_attn)");
     kernel<<<static_cast<unsigned>(grid), mcb::kPfThreads, Cfg::kSmem, st>>>(qm, km, vm, prm);
     g_launches++;
+    note_attn_kernel("prefill_attn_kernel", D, 0, 0, false);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "prefill_attn launch");
     return MCB_OK;
@@ -285,6 +296,7 @@ struct AttnVariant {
     if (rc != MCB_OK) return rc;
     kernel<<<grid, mcb::kAttnThreads, Cfg::SMEM_BYTES, st>>>(km, vm, prm);
     g_launches++;
+    note_attn_kernel("decode_attn_kernel", D, NQT, STAGES, false);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn launch");
     return MCB_OK;
@@ -321,6 +333,7 @@ struct AttnVariant {
     e = lo ? cudaLaunchKernelEx(&cfg, split_kernel_lo, km, vm, prm)
            : cudaLaunchKernelEx(&cfg, split_kernel, km, vm, prm);
     g_launches++;
+    note_attn_kernel("decode_attn_split_kernel", D, NQT, lo ? 2 : SPLIT_STAGES, false);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split launch");
@@ -416,6 +429,7 @@ struct SplitF8Variant {
     cfg.attrs = attrs;
     cudaError_t e = lo ? cudaLaunchKernelEx(&cfg, kernel_lo, km, vm, prm) : cudaLaunchKernelEx(&cfg, kernel, km, vm, prm);
     g_launches++;
+    note_attn_kernel("decode_attn_split_kernel", D, NQT, lo ? 3 : 4, true);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_attn_split (fp8) launch");
     return launch_combine<D>(prm, st);
@@ -888,6 +902,12 @@ int mcb_last_error(char* buf, size_t len) {
 }
 
 uint64_t mcb_launch_count(void) { return g_launches.load(); }
+
+int mcb_last_attn_kernel(char* buf, size_t len) {
+  if (buf == nullptr || len == 0) return fail(MCB_ERR_INVALID_ARG, "mcb_last_attn_kernel: empty buffer");
+  snprintf(buf, len, "%s", g_last_attn_kernel);
+  return MCB_OK;
+}
 
 int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_kv_append_rope: args is NULL");
@@ -1406,12 +1426,19 @@ int mcb_decode_attn_noalloc(const mcb_attn_args* a, void* stream) {
   rc = check_attn_pointers(a, "mcb_decode_attn_noalloc");
   if (rc != MCB_OK) return rc;
   const size_t counter_bytes = round256(pl.counter_count * 4);
-  if (pl.ws_bytes + counter_bytes > MCB_NOALLOC_SCRATCH_BYTES)
+  if (pl.ws_bytes + counter_bytes > MCB_NOALLOC_SCRATCH_BYTES) {
+    if (pl.mode == kModePersistent)
+      return fail(MCB_ERR_WORKSPACE,
+                  "mcb_decode_attn_noalloc: %d persistent CTAs and %zu row groups need %zu bytes of "
+                  "scratch, more than the %u-byte static scratch; pass fewer CTAs (a smaller "
+                  "num_ctas > 0) or use mcb_decode_attn with a workspace",
+                  pl.grid, pl.counter_count, pl.ws_bytes + counter_bytes, MCB_NOALLOC_SCRATCH_BYTES);
     return fail(MCB_ERR_WORKSPACE,
-                "mcb_decode_attn_noalloc: %d persistent CTAs and %zu row groups need %zu bytes of "
-                "scratch, more than the %u-byte static scratch; pass a smaller num_ctas or use "
-                "mcb_decode_attn with a workspace",
-                pl.grid, pl.counter_count, pl.ws_bytes + counter_bytes, MCB_NOALLOC_SCRATCH_BYTES);
+                "mcb_decode_attn_noalloc: %d key splits of %lld row groups need %zu bytes of scratch, "
+                "more than the %u-byte static scratch; pass fewer splits (num_ctas < 0 of a smaller "
+                "magnitude) or use mcb_decode_attn with a workspace",
+                pl.nsplit, static_cast<long long>(a->B) * a->Hkv * pl.nqb, pl.ws_bytes + counter_bytes, MCB_NOALLOC_SCRATCH_BYTES);
+  }
   if (a->B == 0 || a->T == 0) return MCB_OK;
   void* scratch = nullptr;
   rc = noalloc_scratch_ptr(&scratch);

@@ -376,7 +376,8 @@ def append_attn(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, eps=None,
     if k is not None:
         _need("k", k, 4)
         _need("v", v, 4)
-        if k.shape != v.shape or k.shape[0] != q.shape[0] or k.shape[1] != 1 or k.shape[3] != D:
+        if (k.shape != v.shape or k.shape[0] != q.shape[0] or k.shape[1] != 1
+                or k.shape[2] != k_cache.shape[2] or k.shape[3] != D):
             raise RuntimeError("k and v must be (B, 1, Hkv, D) like the slot")
         args.k_new, args.v_new = k.data_ptr(), v.data_ptr()
         args.k_new_stride[:] = _bthd_strides("k", k)
@@ -641,3 +642,11 @@ def device_error(device=None):
 def launch_count():
     """Kernels libmcb200 has enqueued in this process."""
     return int(_native.load().mcb_launch_count())
+
+
+def last_attn_kernel():
+    """The attention kernel (template instance, as the profiler names it) this thread enqueued
+    last through libmcb200; '' before the first."""
+    buf = ctypes.create_string_buffer(96)
+    check(_native.load().mcb_last_attn_kernel(buf, len(buf)))
+    return buf.value.decode()

@@ -5,9 +5,11 @@ path shards with no collective on its hot path.  Each rank owns a subset of the 
 collective is a gather of the sampled token ids.
 
   contiguous_rows(n_rows, world, rank)  -> the rank's [begin, end) slice (equal-length rows)
-  balanced_rows(lengths, world)         -> per-rank row lists balancing the sum of context
+  balanced_rows(lengths, world, equal_counts=False)
+                                        -> per-rank row lists balancing the sum of context
                                            lengths (right-ragged prompts, e.g. lengths
-                                           U[1024, 8192]): longest first onto the least-loaded rank
+                                           U[1024, 8192]): longest first onto the least-loaded
+                                           rank; optionally the same row count on every rank
   gather_tokens(tokens, group=None)     -> every rank's (rows, steps) tokens concatenated in rank
                                            order (NCCL all_gather_into_tensor, or gloo all_gather)
 """
@@ -25,14 +27,22 @@ def contiguous_rows(n_rows, world, rank):
     return begin, begin + per + (1 if rank < extra else 0)
 
 
-def balanced_rows(lengths, world):
-    """Greedy longest-processing-time assignment; each rank's rows come back sorted ascending."""
+def balanced_rows(lengths, world, equal_counts=False):
+    """Greedy longest-processing-time assignment; each rank's rows come back sorted ascending.
+    equal_counts=True also gives every rank the same number of rows (len(lengths) must be a
+    multiple of world): a rank that holds its share leaves the pool.  Equal counts keep the
+    per-rank token tensors one shape, as the gather needs."""
+    n = len(lengths)
+    if equal_counts and n % world:
+        raise ValueError(f"{n} rows do not split into {world} equal shares")
+    cap = n // world if equal_counts else n
     heap = [(0, r) for r in range(world)]
     out = [[] for _ in range(world)]
-    for i in sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i)):
+    for i in sorted(range(n), key=lambda i: (-int(lengths[i]), i)):
         load, r = heapq.heappop(heap)
         out[r].append(i)
-        heapq.heappush(heap, (load + int(lengths[i]), r))
+        if len(out[r]) < cap:
+            heapq.heappush(heap, (load + int(lengths[i]), r))
     return [sorted(rows) for rows in out]
 
 

@@ -24,6 +24,14 @@ Fixtures:
                             (modelcore/components/mlp.py:89-90); TokenEmbedding without smear
                             then the first norm (embedding.py:71-75); LMHead with softcap 15 and
                             without (unembedding.py:50-56): its bf16 logits and fp32 outputs
+  v2_llama*.npz             modelcore's own real-weight goldens (modelcore/tests/goldens/v2_llama.pt,
+                            v2_llama_kvshare_win_gated_block.pt: awake weights, an input (2, 12) and
+                            the full-forward logits the v2 code produced), passed through modelcore's
+                            own v2 -> v3 upgrade (config.upgrade.upgrade_v2_to_v3 and
+                            convert.convert_state_v2_to_v3, the path test_v3_migration.py:43-52
+                            checks bit-exact): the v3 config as JSON, the v3 state (fp32) and the
+                            golden idx / logits.  The goldens ship in the reference's source tree
+                            only (not in its installed package): --ref-src names that tree
   decode_cfg1.npz           the README quickstart model (fp32, seed 0), prompts (2, 16) from seed 1,
                             64 greedy steps through Decoder: the token streams, for the plain
                             random init and for the awake init of
@@ -267,17 +275,58 @@ def make_decode_cfg1(out_dir, steps=64):
     np.savez_compressed(os.path.join(out_dir, "decode_cfg1.npz"), **out)
 
 
+V2_GOLDENS = ("v2_llama.pt", "v2_llama_kvshare_win_gated_block.pt")
+
+
+def make_v2_goldens(out_dir, ref_src):
+    """The reference's real-weight goldens in v3 form (see the module docstring).  The upgraded
+    model's own fp32 forward is checked against the golden logits (within 1e-5: the goldens are
+    bit-exact on the CPU that wrote them, fp32 BLAS order differs elsewhere) before anything is
+    written."""
+    import json
+    import torch
+    from modelcore import ModelConfig, ModelManager, Runtime
+    from modelcore.config.upgrade import upgrade_v2_to_v3
+    from modelcore.convert import convert_state_v2_to_v3
+
+    gdir = os.path.join(ref_src, "modelcore", "tests", "goldens")
+    for name in V2_GOLDENS:
+        golden = torch.load(os.path.join(gdir, name), map_location="cpu")
+        cfg = upgrade_v2_to_v3(golden["config"])
+        state = convert_state_v2_to_v3(golden["state"])
+        mgr = ModelManager(runtime=Runtime(compute_dtype=torch.float32))
+        model = mgr.create_model(ModelConfig.from_dict(cfg), device=torch.device("cpu"), seed=0)
+        model.load_state_dict(state)
+        with torch.no_grad():  # bit-exact on the CPU that wrote them; within fp32 BLAS noise here
+            err = (model.eval()(golden["idx"]) - golden["logits"]).abs().max().item()
+        assert err <= 1e-5, (name, err)
+        out = {"config_json": np.frombuffer(json.dumps(cfg).encode(), dtype=np.uint8),
+               "idx": golden["idx"].numpy(), "logits": golden["logits"].numpy(),
+               "state_keys": np.array(sorted(state))}
+        for i, key in enumerate(sorted(state)):
+            out[f"state_{i}"] = state[key].float().numpy()
+        np.savez_compressed(os.path.join(out_dir, name.replace(".pt", ".npz")), **out)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--ref", default=os.environ.get("MODELCORE_REF_PATH",
                                                     os.path.join(REPO, "baseline", "_ref")))
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--ref-src", default=os.environ.get("MODELCORE_REFERENCE_SRC",
+                                                        os.path.join(os.path.dirname(REPO), "reference")),
+                    help="the reference's source tree (its tests/goldens are not installed)")
     ap.add_argument("--skip-decode", action="store_true")
+    ap.add_argument("--only-v2", action="store_true", help="write only the v2_*.npz fixtures")
     args = ap.parse_args()
     os.environ.setdefault("MODELCORE_DTYPE", "float32")
     _import_reference(args.ref)
     import torch
     torch.manual_seed(0)
+    make_v2_goldens(args.out, args.ref_src)
+    if args.only_v2:
+        print("wrote fixtures to", args.out)
+        return
     make_rope_norm(args.out)
     make_kv_attn(args.out)
     make_prefill(args.out)

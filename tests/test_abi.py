@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 6
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 7
 
 
 def test_every_declared_symbol_is_exported():

@@ -131,3 +131,61 @@ def test_append_attn_picks_the_fused_launch_and_falls_back(ops):
     want = ops.decode_attn(qa, kc4, vc4, sl2)
     torch.cuda.synchronize()
     assert torch.equal(kc3, kc4) and torch.equal(got, want)
+
+
+ORACLE_CASES = [CASES[1], CASES[2], CASES[5]]  # cluster merge; window + 12 splits; a reading layer
+
+
+@pytest.mark.parametrize("case", ORACLE_CASES, ids=lambda c: "B{}Hq{}D{}w{}kv{}n{}".format(
+    c[0], c[1], c[3], c[6], int(c[8]), c[9]))
+def test_fused_append_matches_the_oracle(ops, case):
+    """The one-launch step against the CPU oracle (oracle/kv_path.py), not only against the
+    two-launch CUDA path: the cache bytes after the append are bit-exact (the new key roped,
+    normed and scaled; the value copied), the attention within the bf16 tolerance 2e-2 of a
+    float64 attention over the oracle's own q and cache."""
+    import numpy as np
+    from oracle import kv_path as O
+    B, Hq, Hkv, D, Tmax, max_len, window, ring, produces, nc = case
+    g = torch.Generator(device="cuda").manual_seed(B * 11 + Hq + D)
+    q = torch.randn(B, 1, Hq, D, device="cuda", generator=g).mul(2).to(torch.bfloat16)
+    k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).mul(2).to(torch.bfloat16)
+    v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Tmax, Hkv, D, device="cuda", generator=g).to(torch.bfloat16)
+    hi = max_len - 1
+    sl = torch.randint(hi // 2, hi + 1, (B,), device="cuda", generator=g, dtype=torch.int32)
+    cos, sin = tables(max(Tmax, max_len) + 8, D)
+
+    def bits(t):
+        return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    qb, kb, vb, kcb, vcb = bits(q), bits(k), bits(v), bits(kc), bits(vc)
+    lens = sl.cpu().numpy()
+    got = fused(ops, q, k if produces else None, v if produces else None, kc, vc, sl, cos, sin,
+                window, ring, nc)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    if produces:
+        q_ref = O.append_rope(qb, kb, vb, kcb, vcb, lens, bits(cos), bits(sin), eps=1e-6, scale=1.2)
+    else:
+        q_ref = O.append_rope(qb, None, None, None, None, lens, bits(cos), bits(sin), rotate_k=False,
+                              write_kv=False, eps=1e-6, scale=1.2)
+    assert np.array_equal(bits(kc), kcb) and np.array_equal(bits(vc), vcb)
+    y_ref = O.decode_attention(O.bf16_to_f32(q_ref), O.bf16_to_f32(kcb), O.bf16_to_f32(vcb), lens,
+                               window)
+    err = float(np.abs(got.float().cpu().numpy() - y_ref).max())
+    assert err <= 2e-2, f"fused step vs oracle: max-abs {err}"
+
+
+def test_fused_append_rejects_new_keys_with_the_wrong_head_count(ops):
+    """k / v of the fused path must carry the slot's Hkv heads; fewer would be read past their end
+    by the kernel, so the host rejects them (as the two-launch path does)."""
+    B, Hq, Hkv, D, Tmax = 2, 16, 4, 128, 256
+    q = torch.zeros(B, 1, Hq, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(B, 1, Hkv - 2, D, device="cuda", dtype=torch.bfloat16)
+    kc = torch.zeros(B, Tmax, Hkv, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    sl = torch.full((B,), 10, device="cuda", dtype=torch.int32)
+    cos, sin = tables(Tmax + 8, D)
+    with pytest.raises(RuntimeError, match="Hkv"):
+        ops.append_attn(q, k, k.clone(), kc, vc, sl, cos, sin, eps=1e-6)

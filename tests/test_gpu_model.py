@@ -121,6 +121,54 @@ def test_quickstart_awake_decode_is_as_accurate_as_the_reference(env):
     assert int((a_mine != a32).sum()) <= int((a_ref != a32).sum())
 
 
+LM_HEAD_GAIN = 30.0  # lm_head x30: median fp32 top-2 margin 0.13 instead of 0.005 (1e-3 init std)
+
+
+def test_awake_free_running_greedy_stream_against_the_reference_for_64_steps(env):
+    """The north-star stream check on a model whose attention reaches the logits: config 1's
+    architecture with modelcore's test wake-up and the lm_head scaled by LM_HEAD_GAIN (so top-2
+    margins mostly clear bf16 noise).  modelcore's bf16 SDPA path and the B200 path each decode
+    64 greedy steps from the same prompts, each feeding its own picks (free running).
+
+    The streams must be identical, except at a genuine near-tie: if a row's streams part, then at
+    the first step where they do (both contexts still identical there), the fp32 evaluation's
+    top-2 margin must be within the two bf16 paths' combined error at that step.  The first
+    divergence (step, row, margin) is printed either way."""
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    z = load_golden("decode_cfg1.npz")
+    prompts = z["prompts"].tolist()
+    ref_mgr, ref, mgr, mine = _pair(env, workloads.quickstart_config(), awake=True)
+    with torch.no_grad():
+        for m in (ref, mine):
+            m.unembedding.lm_head.weight.mul_(LM_HEAD_GAIN)
+    t_ref, _, _ = _greedy(ref_mgr, ref, prompts, 64)
+    t_mine, _, _ = _greedy(mgr, mine, prompts, 64)
+    differ = t_ref != t_mine
+    if not bool(differ.any()):
+        print("awake quickstart (lm_head x30): B200 and modelcore greedy streams identical for 64 steps")
+        return
+    m32 = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
+    ref32 = m32.create_model(workloads.quickstart_config(), device=torch.device("cpu"), seed=0)
+    ref32.load_state_dict({k: v.float().cpu() for k, v in ref.state_dict().items()})
+    ref32 = ref32.to("cuda").eval()
+    for r in range(differ.shape[0]):
+        if not bool(differ[r].any()):
+            print(f"row {r}: identical for 64 steps")
+            continue
+        s = int(differ[r].nonzero()[0])
+        cols = t_ref[:, :s]  # row r's context is identical on both paths up to step s
+        l32 = _forced(m32, ref32, prompts, cols)[:, s]
+        l_mine = _forced(mgr, mine, prompts, cols)[:, s]
+        l_ref = _forced(ref_mgr, ref, prompts, cols)[:, s]
+        top2 = torch.topk(l32[r], 2).values
+        margin = (top2[0] - top2[1]).item()
+        err = (l_mine[r] - l32[r]).abs().max().item() + (l_ref[r] - l32[r]).abs().max().item()
+        print(f"row {r}: first divergence at step {s}: fp32 top-2 margin {margin:.3e}, combined "
+              f"bf16 error {err:.3e}")
+        assert margin <= 2 * err, (r, s, margin, err)
+
+
 def _attention_flavors():
     from modelcore.tests.conftest import FLAVORS
     out = []

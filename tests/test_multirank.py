@@ -31,6 +31,13 @@ def test_balanced_rows_balance_ragged_context():
         assert sorted(i for p in parts for i in p) == list(range(128))
         loads = [sum(lengths[i] for i in p) for p in parts]
         assert max(loads) / (sum(lengths) / world) < 1.02
+        eq = balanced_rows(lengths, world, equal_counts=True)
+        assert sorted(i for p in eq for i in p) == list(range(128))
+        assert all(len(p) == 128 // world for p in eq)
+        loads = [sum(lengths[i] for i in p) for p in eq]
+        assert max(loads) / (sum(lengths) / world) < 1.03
+    with pytest.raises(ValueError):
+        balanced_rows(lengths[:7], 2, equal_counts=True)
 
 
 def _free_port():

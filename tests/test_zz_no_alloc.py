@@ -45,17 +45,22 @@ SHAPES = [
     (32, 32, 8, 128, 8192, -1, 0),
     (4, 12, 12, 64, 3000, 100, 24),
     (4, 12, 12, 64, 1000, -1, -20),
+    # two row groups of one long row cut into 19 splits: a small grid, so the split that arrives
+    # last merges the partials through the arrival counters, which each call clears first
+    (1, 16, 2, 128, 8192, -1, -20),
 ]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=["cfg5-like-auto", "mha-d64-window-24-ctas",
-                                               "mha-d64-17-splits"])
+                                               "mha-d64-17-splits", "gqa-d128-19-splits-counters"])
 def test_noalloc_matches_the_allocating_entry_point_on_two_calls_in_a_row(shape):
     B, Hq, Hkv, D, Tmax, window, splits = shape
     for call, seed in enumerate((11, 12)):
         q, kc, vc, sl = _inputs(seed, B, Hq, Hkv, D, Tmax)
         need = ops.decode_attn_workspace_bytes(q, kc, vc, sl, window=window, num_ctas=splits)
         assert 0 < need <= _native.NOALLOC_SCRATCH_BYTES  # partials live in the scratch
+        if shape == SHAPES[3]:
+            assert ops.decode_attn_counter_count(q, kc, vc, sl, window=window, num_ctas=splits) > 0
         expected = ops.decode_attn(q, kc, vc, sl, window=window, num_ctas=splits)
         out = torch.full_like(q, float("nan"))
         torch.cuda.synchronize()
@@ -77,7 +82,10 @@ def test_noalloc_rejects_a_grid_whose_partials_exceed_its_scratch():
     out = torch.zeros_like(q)
     st = _call_noalloc(q, kc, vc, sl, out, -1, 4096)
     assert st == _native.MCB_ERR_WORKSPACE
-    assert "static scratch" in _native.last_error()
+    assert "static scratch" in _native.last_error() and "persistent CTAs" in _native.last_error()
+    # a split plan whose partials do not fit: the message asks for fewer splits
+    assert _call_noalloc(q, kc, vc, sl, out, -1, -64) == _native.MCB_ERR_WORKSPACE
+    assert "key splits" in _native.last_error() and "fewer splits" in _native.last_error()
     torch.cuda.synchronize()
     assert out.abs().sum().item() == 0  # nothing was enqueued
     # with fewer CTAs the same shape fits and matches

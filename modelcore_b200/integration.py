@@ -292,6 +292,10 @@ class GraphDecoder:
         self._next = torch.zeros((B, 1), dtype=torch.long, device=dev)
         self._next_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
         self._rt_done = torch.cuda.Event()
+        # recorded after each step()'s copy out of _ids_host: the next step() waits on it before
+        # overwriting that pinned buffer (the copy reads it when the stream reaches it, not when
+        # it is enqueued)
+        self._h2d_done = torch.cuda.Event()
         self.launches_per_step = None  # libmcb200 kernels recorded in one captured step
 
     @torch.inference_mode()
@@ -482,8 +486,10 @@ class GraphDecoder:
         if isinstance(token_column, torch.Tensor) and token_column.is_cuda:
             self._ids.copy_(token_column.view(-1, 1))
         else:
+            self._h2d_done.synchronize()
             self._ids_host.copy_(torch.as_tensor(token_column, dtype=torch.long).view(-1, 1))
             self._ids.copy_(self._ids_host, non_blocking=True)
+            self._h2d_done.record()
         if self._graph is None and self._eager_steps == 0:
             self._logits = self._eager(self._ids.clone())
             return self._logits

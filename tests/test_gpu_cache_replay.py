@@ -12,8 +12,9 @@ append (mcb_kv_append_rope, with the rotary module's own tables and the same cac
 a shadow cache of the same shape, and the rotated q is kept beside modelcore's.
 
 Checked: values bit-exact; keys and queries bit-exact except where the fp32 sum of squares inside
-the norm lands on the other side of a bf16 rounding boundary in torch's CUDA reduction order
-(one ulp at most); the count of such elements is printed and bounded.
+the norm, summed in torch's CUDA reduction order, puts the normed value on the other side of a bf16
+rounding boundary: one ulp there, which the x1.2 that follows can round to two; the count of such
+elements is printed and bounded (measured on B200: 3.9e-6 of 321M key elements, at most 2 ulp).
 """
 import numpy as np
 import pytest
@@ -24,7 +25,7 @@ from conftest import have_modelcore
 pytestmark = pytest.mark.gpu
 
 ROWS, PROMPT, STEPS, TMAX = 64, 512, 32, 1024
-MAX_ULP_RATE = 1e-4  # measured against torch's CPU order: 6e-6
+MAX_ULP_RATE = 2e-5  # measured: 3.9e-6 against torch's CUDA order, 6e-6 against its CPU order
 
 
 def _ulp_diff(a, b):
@@ -111,7 +112,7 @@ def test_config2_cache_bytes_equal_modelcores_after_prefill_and_32_steps():
           f"{stats['q_elems']:,} query elements, {stats['q_diff']} differ "
           f"(rate {stats['q_diff'] / stats['q_elems']:.2e}, max {stats['q_max_ulp']} ulp); "
           f"values bit-exact")
-    assert int(dk.max()) <= 1 and stats["q_max_ulp"] <= 1
+    assert int(dk.max()) <= 2 and stats["q_max_ulp"] <= 2
     assert k_diff / k_elems <= MAX_ULP_RATE
     assert stats["q_diff"] / stats["q_elems"] <= MAX_ULP_RATE
     np.testing.assert_equal(cache.k_cache[:, :, filled:].abs().sum().item(), 0.0)

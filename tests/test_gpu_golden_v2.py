@@ -42,10 +42,14 @@ def _golden(name):
     return cfg, state, torch.from_numpy(z["idx"]), torch.from_numpy(z["logits"])
 
 
-def _model(modelcore, mgr, cfg, state):
+def _model(modelcore, mgr, cfg, state, weights):
+    """weights "fp32": modelcore's fp32 master weights cast per call (modelcore's own block
+    forward around the B200 attention); "bf16": the model cast to bf16 (the whole fused decode
+    forward of modelcore_b200.step on the B200 side)."""
     model = mgr.create_model(modelcore.ModelConfig.from_dict(cfg), device=torch.device("cpu"), seed=0)
     model.load_state_dict(state)
-    return model.to("cuda").eval()
+    model = model.to("cuda").eval()
+    return model.to(torch.bfloat16) if weights == "bf16" else model
 
 
 @torch.inference_mode()
@@ -61,14 +65,15 @@ def _forced(mgr, model, idx, prefix, **kw):
 
 @pytest.mark.parametrize("name", NAMES)
 @pytest.mark.parametrize("prefix", [1, 5])
-def test_decode_logits_match_the_reference_goldens(env, name, prefix):
+@pytest.mark.parametrize("weights", ["fp32", "bf16"])
+def test_decode_logits_match_the_reference_goldens(env, name, prefix, weights):
     modelcore, mcb = env
     cfg, state, idx, golden = _golden(name)
     want = golden[:, prefix - 1:]
     ref_mgr = modelcore.ModelManager()
-    l_ref, _ = _forced(ref_mgr, _model(modelcore, ref_mgr, cfg, state), idx, prefix)
+    l_ref, _ = _forced(ref_mgr, _model(modelcore, ref_mgr, cfg, state, weights), idx, prefix)
     mgr = mcb.ModelManager()
-    mine = _model(modelcore, mgr, cfg, state)
+    mine = _model(modelcore, mgr, cfg, state, weights)
     l_mine, dec = _forced(mgr, mine, idx, prefix)
     assert isinstance(dec.kv_cache, mcb.KVCache)
     l_graph, gdec = _forced(mgr, mine, idx, prefix, cuda_graph=True)
@@ -76,8 +81,10 @@ def test_decode_logits_match_the_reference_goldens(env, name, prefix):
     err_ref = (l_ref - want).abs().max().item()
     err_mine = (l_mine - want).abs().max().item()
     err_graph = (l_graph - want).abs().max().item()
-    print(f"{name} prefix {prefix}: max|B200 - golden| = {err_mine:.3e} (graph {err_graph:.3e}), "
-          f"max|modelcore bf16 - golden| = {err_ref:.3e}, |golden| <= {golden.abs().max().item():.2f}")
+    gap = (l_mine - l_ref).abs().max().item()
+    print(f"{name} prefix {prefix} {weights} weights: max|B200 - golden| = {err_mine:.3e} (graph "
+          f"{err_graph:.3e}), max|modelcore bf16 - golden| = {err_ref:.3e}, max|B200 - modelcore| = "
+          f"{gap:.3e}, |golden| <= {golden.abs().max().item():.2f}")
     assert err_mine <= LOGIT_TOL and err_graph <= LOGIT_TOL
     assert err_mine <= 1.25 * err_ref + 1e-3
     # greedy picks equal the golden's wherever the golden's own top-2 margin clears the error

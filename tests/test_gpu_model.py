@@ -164,8 +164,9 @@ def test_awake_free_running_greedy_stream_against_the_reference_for_64_steps(env
         top2 = torch.topk(l32[r], 2).values
         margin = (top2[0] - top2[1]).item()
         err = (l_mine[r] - l32[r]).abs().max().item() + (l_ref[r] - l32[r]).abs().max().item()
+        gap = (l_mine[r] - l_ref[r]).abs().max().item()
         print(f"row {r}: first divergence at step {s}: fp32 top-2 margin {margin:.3e}, combined "
-              f"bf16 error {err:.3e}")
+              f"bf16 error {err:.3e} (max |B200 - modelcore bf16| there {gap:.3e})")
         assert margin <= 2 * err, (r, s, margin, err)
 
 
@@ -238,6 +239,27 @@ def test_graph_decoder_reproduces_the_eager_decoder_bit_for_bit(env):
             host.append(nxt.cpu())
             e2.step(nxt.tolist())
         assert torch.equal(dev_tokens, torch.stack(host, 1))
+
+
+def test_graph_decoder_steps_fed_from_the_host_back_to_back(env):
+    """GraphDecoder.step(list) copies the column through a pinned host buffer with a
+    non-blocking copy; steps issued back to back, with nothing on the host waiting for the GPU in
+    between, must each see their own column (the buffer is not overwritten before its copy ran)."""
+    modelcore, mcb = env
+    from modelcore_b200 import workloads
+    mgr = mcb.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
+                                              device=torch.device("cuda"), seed=0)).eval()
+    prompts = workloads.prompts(64, 200, seed=1).tolist()
+    cols = [[(s * 131 + i * 7) % 30000 for i in range(64)] for s in range(12)]
+    with torch.inference_mode():
+        eager = mgr.new_decoder(model, prompts, max_tokens=16)
+        want = [eager.step(c).clone() for c in cols]
+        graph = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+        got = [graph.step(c).clone() for c in cols]  # no host read in between
+        torch.cuda.synchronize()
+    for s, (a, b) in enumerate(zip(want, got)):
+        assert torch.equal(a, b), s
 
 
 def test_config4_broadcast_and_kv_sharing_decode_matches_the_reference(env):

@@ -322,9 +322,10 @@ typedef struct {
 int mcb_softcap_argmax(const mcb_softcap_args* args, void* stream);
 
 /* mcb_sample: one token per row from fp32 logits, sample_next_token (modelcore/generate.py:19-34)
- * for temperature > 0: with 1 <= top_k <= 1024 (and top_k < V) the top_k largest logits (ties by
- * ascending index), divided by the temperature, softmax, one draw; otherwise softmax over the
- * whole row, one draw.  The draw is the inverse CDF at u = uniforms[r] in [0, 1) (candidates in
+ * for temperature > 0: with 1 <= top_k < V the top_k largest logits (ties by ascending index),
+ * divided by the temperature, softmax, one draw; otherwise softmax over the whole row, one draw.
+ * Above 1024 candidates the weights are fixed-point (2^-40 of the largest), which moves the
+ * distribution by at most k * 2^-41 of the total.  The draw is the inverse CDF at u = uniforms[r] in [0, 1) (candidates in
  * descending-logit order, or index order for the whole row), so it is a deterministic function of
  * (logits, u) with the reference's distribution over u.  temperature == 0 is the greedy pick:
  * call with top_k = 1 (any temperature > 0) or use mcb_softcap_argmax. */

@@ -369,11 +369,10 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
           if (rotate && !rot_ok && sub == 0) record_error(kErrPositionBeyondRotary);
           const uint4 x1v = valid ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
           const uint4 x2v = valid ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
-          float o1[8], o2[8];
-          rope_norm_vec<D>(x1v, x2v, p.rot_cos, p.rot_sin, L, sub, rotate && rot_ok, p.norm_eps, p.qk_scale, o1,
-                           o2);
+          uint4 w1, w2;
+          rope_norm_vec<D>(x1v, x2v, p.rot_cos, p.rot_sin, L, sub, rotate && rot_ok, p.norm_eps, p.qk_scale, w1,
+                           w2);
           if (valid) {
-            const uint4 w1 = pack8(o1), w2 = pack8(o2);
             uint16_t* dst = is_q ? qbuf + vi * D : kvbuf + (is_k ? 0 : D);
             *reinterpret_cast<uint4*>(dst + 8 * sub) = w1;
             *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = w2;

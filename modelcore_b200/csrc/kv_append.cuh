@@ -190,117 +190,198 @@ __device__ __forceinline__ uint2 e4m3x8(const float* x, float inv) {
 // fuses the append, so both give the same bits.  Every lane of the warp calls it (the sum of
 // squares is an xor butterfly over the group's lanes); with rotate false o1 / o2 are x1 / x2 and
 // the lane adds nothing to its group's sum.
+// Packed arithmetic for the vector path.  Every result is the bf16 (or fp32) value the scalar
+// recipe gives: a product of two bf16 values is exact in fp32, so fp32-multiply-then-round equals
+// mul.rn.bf16x2; a sum of two bf16 values is exact in fp32 whenever rounding to bf16 can depend
+// on its low bits (operand exponents within 15 of each other; farther apart the smaller one is
+// below a quarter ulp of the larger and both roundings return the larger), so
+// fp32-add-then-round equals add.rn.bf16x2; f32x2 multiplies round each lane as __fmul_rn does.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// (lo, hi) bf16 pair -> the two values as an fp32 pair (exact)
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) {
+  return static_cast<uint64_t>(w << 16) | (static_cast<uint64_t>(w & 0xffff0000u) << 32);
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// fp32 pair -> bf16 pair, each rounded to nearest even
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+  uint32_t d;
+  asm("{\n\t.reg .f32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}"
+      : "=r"(d)
+      : "l"(v));
+  return d;
+}
+
 template <int D>
-__device__ __forceinline__ void rope_norm_vec(const uint4& x1v, const uint4& x2v, const uint16_t* cos,
-                                              const uint16_t* sin, int pos, int sub, bool rotate, float eps,
-                                              float scale, float (&o1)[8], float (&o2)[8]) {
+__device__ __forceinline__ void rope_norm_vec_tab(const uint4& x1v, const uint4& x2v, const uint4& cv,
+                                                  const uint4& sv, bool rotate, float eps, float scale,
+                                                  uint4& w1, uint4& w2) {
   constexpr int L = D / 16;
-  constexpr int HALF = D / 2;
-  float y1[8], y2[8];
+  uint32_t y1[4], y2[4];
   float acc = 0.f;
   if (rotate) {
-    float x1[8], x2[8], c[8], sn[8];
-    unpack8(x1v, x1);
-    unpack8(x2v, x2);
-    const long long trow = static_cast<long long>(pos) * HALF + 8 * sub;
-    unpack8(*reinterpret_cast<const uint4*>(cos + trow), c);
-    unpack8(*reinterpret_cast<const uint4*>(sin + trow), sn);
+    const uint32_t X1[4] = {x1v.x, x1v.y, x1v.z, x1v.w}, X2[4] = {x2v.x, x2v.y, x2v.z, x2v.w};
+    const uint32_t C[4] = {cv.x, cv.y, cv.z, cv.w}, S[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = round_bf16(__fmul_rn(x1[i], c[i]));
-      const float bb = round_bf16(__fmul_rn(x2[i], sn[i]));
-      const float cc = round_bf16(__fmul_rn(x1[i], -sn[i]));
-      const float dd = round_bf16(__fmul_rn(x2[i], c[i]));
-      y1[i] = round_bf16(__fadd_rn(a, bb));
-      y2[i] = round_bf16(__fadd_rn(cc, dd));
-      acc = __fadd_rn(acc, __fmul_rn(y1[i], y1[i]));
-      acc = __fadd_rn(acc, __fmul_rn(y2[i], y2[i]));
+    for (int k = 0; k < 4; ++k) {  // elements 2k, 2k+1 of the lane's 8 pairs
+      y1[k] = badd2(bmul2(X1[k], C[k]), bmul2(X2[k], S[k]));
+      y2[k] = badd2(bmul2(X1[k], S[k] ^ 0x80008000u), bmul2(X2[k], C[k]));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // element order: y1[i]^2 then y2[i]^2, i increasing
+      const float a0 = __uint_as_float(y1[k] << 16), a1 = __uint_as_float(y1[k] & 0xffff0000u);
+      const float b0 = __uint_as_float(y2[k] << 16), b1 = __uint_as_float(y2[k] & 0xffff0000u);
+      acc = __fadd_rn(acc, __fmul_rn(a0, a0));
+      acc = __fadd_rn(acc, __fmul_rn(b0, b0));
+      acc = __fadd_rn(acc, __fmul_rn(a1, a1));
+      acc = __fadd_rn(acc, __fmul_rn(b1, b1));
     }
   }
 #pragma unroll
   for (int m = L / 2; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
   if (rotate) {
     const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(D)), eps));
+    const uint64_t rr = static_cast<uint64_t>(__float_as_uint(r)) * 0x100000001ull;
+    const uint64_t ss = static_cast<uint64_t>(__float_as_uint(scale)) * 0x100000001ull;
+    uint32_t o1[4], o2[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o1[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y1[i], r)), scale));
-      o2[i] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(y2[i], r)), scale));
+    for (int k = 0; k < 4; ++k) {
+      o1[k] = f2_to_bf2(fmul2(bf2_to_f2(f2_to_bf2(fmul2(bf2_to_f2(y1[k]), rr))), ss));
+      o2[k] = f2_to_bf2(fmul2(bf2_to_f2(f2_to_bf2(fmul2(bf2_to_f2(y2[k]), rr))), ss));
     }
+    w1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+    w2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
   } else {
-    unpack8(x1v, o1);
-    unpack8(x2v, o2);
+    w1 = x1v;
+    w2 = x2v;
   }
+}
+
+// The same with the lane's cos / sin chunks read from the tables at row `pos`.
+template <int D>
+__device__ __forceinline__ void rope_norm_vec(const uint4& x1v, const uint4& x2v, const uint16_t* cos,
+                                              const uint16_t* sin, int pos, int sub, bool rotate, float eps,
+                                              float scale, uint4& w1, uint4& w2) {
+  uint4 cv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
+  if (rotate) {
+    const long long trow = static_cast<long long>(pos) * (D / 2) + 8 * sub;
+    cv = *reinterpret_cast<const uint4*>(cos + trow);
+    sv = *reinterpret_cast<const uint4*>(sin + trow);
+  }
+  rope_norm_vec_tab<D>(x1v, x2v, cv, sv, rotate, eps, scale, w1, w2);
 }
 
 // Vectorised variant: L = D/16 lanes per vector, 16-byte loads and stores, 32/L vectors per warp.
 // Requires 16-byte aligned rows (checked on the host).  FP8: the cache vectors are stored as
 // e4m3 with a per-vector scale (e4m3x8 above), 8-byte stores.
-template <int D, bool FP8>
-__global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
-    kv_append_rope_vec_kernel(const AppendParams p) {
-  pdl_launch_dependents();  // the kernel after it waits for completion before reading
-  pdl_wait();               // q, k, v come from the projection ahead
-  constexpr int L = D / 16;        // lanes per vector
-  constexpr int VPW = 32 / L;      // vectors per warp
-  constexpr int HALF = D / 2;
-  const int lane = threadIdx.x & 31;
-  const int sub = lane % L;        // chunk index within the half
-  const long long w = (static_cast<long long>(blockIdx.x) * kAppendWarpsPerBlock + (threadIdx.x >> 5)) * VPW +
-                      lane / L;
-  const bool active = w < p.total_vectors;
-  const long long wv = active ? w : 0;
-  const int per_bt = p.nq + 2 * p.nk;
-  const int j = static_cast<int>(wv % per_bt);
-  const long long bt = wv / per_bt;
-  const int t = static_cast<int>(bt % p.T);
-  const int b = static_cast<int>(bt / p.T);
-  const int pos = p.cache_seqlens[b] + t;
+//
+// A grid-stride loop (the grid is four 256-thread CTAs per SM) over groups of vectors: each
+// iteration a warp loads a group's positions and 16-byte chunks, then the rotary table chunks at
+// those positions, computes and stores.  The arithmetic is packed (bf16x2 / f32x2, see
+// rope_norm_vec_tab): the kernel was bound by instruction issue, not by bytes in flight (config
+// 2's prefill append: 0.37 of the copy peak with scalar arithmetic and one vector group per
+// 128-thread CTA, 0.61 with packed arithmetic here; batching two or four groups per iteration for
+// more loads in flight measured slower, 0.58 and 0.55: more registers, fewer warps).
+constexpr int kAppendVecThreads = 256;
 
+struct AppendVecLoad {
+  int b, t, j, pos;
+  bool active, rotate, ok;
+  uint4 x1v, x2v, cv, sv;
+};
+
+template <int D>
+__device__ __forceinline__ void append_vec_load(const AppendParams& p, long long w, int sub, AppendVecLoad& r) {
+  constexpr int HALF = D / 2;
+  r.active = w < p.total_vectors;
+  const unsigned wv = r.active ? static_cast<unsigned>(w) : 0u;  // total_vectors < 2^31 (host)
+  const unsigned per_bt = static_cast<unsigned>(p.nq + 2 * p.nk);
+  r.j = static_cast<int>(wv % per_bt);
+  const unsigned bt = wv / per_bt;
+  r.t = static_cast<int>(bt % static_cast<unsigned>(p.T));
+  r.b = static_cast<int>(bt / static_cast<unsigned>(p.T));
+  const bool is_v = r.j >= p.nq + p.nk;
+  const bool is_q = r.j < p.nq;
+  const int h = is_q ? r.j : (is_v ? r.j - p.nq - p.nk : r.j - p.nq);
+  const uint16_t* src = is_q ? p.q + r.b * p.qs[0] + r.t * p.qs[1] + h * p.qs[2]
+                             : (is_v ? p.v + r.b * p.vs[0] + r.t * p.vs[1] + h * p.vs[2]
+                                     : p.k + r.b * p.ks[0] + r.t * p.ks[1] + h * p.ks[2]);
+  r.pos = p.cache_seqlens[r.b] + r.t;
+  r.x1v = *reinterpret_cast<const uint4*>(src + 8 * sub);
+  r.x2v = *reinterpret_cast<const uint4*>(src + HALF + 8 * sub);
+  r.rotate = is_q || (!is_v && p.rotate_k);
+}
+
+// The position checks, then the lane's rotary table chunks (rotating vectors only).
+template <int D>
+__device__ __forceinline__ void append_vec_tables(const AppendParams& p, int sub, AppendVecLoad& r) {
+  const bool is_q = r.j < p.nq;
+  r.ok = r.active;
+  if (!is_q && (r.pos < 0 || (!p.ring && r.pos >= p.Tmax))) {
+    if (r.active && sub == 0) record_error(kErrPositionBeyondCache);
+    r.ok = false;
+  }
+  if (r.ok && r.rotate && (r.pos < 0 || r.pos >= p.rot_len)) {
+    if (sub == 0) record_error(kErrPositionBeyondRotary);
+    r.ok = false;
+  }
+  r.cv = r.sv = make_uint4(0, 0, 0, 0);
+  if (r.ok && r.rotate) {
+    const long long trow = static_cast<long long>(r.pos) * (D / 2) + 8 * sub;
+    r.cv = *reinterpret_cast<const uint4*>(p.cos + trow);
+    r.sv = *reinterpret_cast<const uint4*>(p.sin + trow);
+  }
+}
+
+template <int D, bool FP8>
+__device__ __forceinline__ void append_vec_store(const AppendParams& p, const AppendVecLoad& v, int sub) {
+  constexpr int L = D / 16;
+  constexpr int HALF = D / 2;
+  const int b = v.b, t = v.t, j = v.j, pos = v.pos;
   const bool is_v = j >= p.nq + p.nk;
   const bool is_q = j < p.nq;
   const int h = is_q ? j : (is_v ? j - p.nq - p.nk : j - p.nq);
-  const uint16_t* src = is_q ? p.q + b * p.qs[0] + t * p.qs[1] + h * p.qs[2]
-                             : (is_v ? p.v + b * p.vs[0] + t * p.vs[1] + h * p.vs[2]
-                                     : p.k + b * p.ks[0] + t * p.ks[1] + h * p.ks[2]);
-  bool ok = active;
+  const bool ok = v.ok, rotate = v.rotate;
   long long cache_off = 0;   // element offset of the cache vector
   long long scale_off = 0;
   uint16_t* dst = nullptr;
   if (is_q) {
     dst = p.q_out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D;
-  } else {
-    if (pos < 0 || (!p.ring && pos >= p.Tmax)) {
-      if (active && sub == 0) record_error(kErrPositionBeyondCache);
-      ok = false;
-    } else {
-      const int idx = p.ring ? pos % p.Tmax : pos;
-      cache_off = ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + h) * D;
-      scale_off = (static_cast<long long>(b) * p.Hkv + h) * p.scale_tmax + idx;
-      if (!FP8) dst = (is_v ? p.v_cache : p.k_cache) + cache_off;
-    }
+  } else if (ok) {
+    const int idx = p.ring ? pos % p.Tmax : pos;
+    cache_off = ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + h) * D;
+    scale_off = (static_cast<long long>(b) * p.Hkv + h) * p.scale_tmax + idx;
+    if (!FP8) dst = (is_v ? p.v_cache : p.k_cache) + cache_off;
   }
-  const bool rotate = is_q || (!is_v && p.rotate_k);
-  if (ok && rotate && (pos < 0 || pos >= p.rot_len)) {
-    if (sub == 0) record_error(kErrPositionBeyondRotary);
-    ok = false;
-  }
-
-  const uint4 x1v = ok ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
-  const uint4 x2v = ok ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
   if (!FP8 && !rotate) {  // value heads and raw key inserts: a copy
     if (ok) {
-      *reinterpret_cast<uint4*>(dst + 8 * sub) = x1v;
-      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = x2v;
+      *reinterpret_cast<uint4*>(dst + 8 * sub) = v.x1v;
+      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = v.x2v;
     }
     // lanes of a rotating vector in this warp still take part in the butterfly below
   }
-  float o1[8], o2[8];  // the bf16 values of the output vector, as floats
-  rope_norm_vec<D>(x1v, x2v, p.cos, p.sin, pos, sub, rotate && ok, p.eps, p.scale, o1, o2);
+  uint4 w1, w2;  // the output vector's bf16 chunks
+  rope_norm_vec_tab<D>(v.x1v, v.x2v, v.cv, v.sv, rotate && ok, p.eps, p.scale, w1, w2);
   if (rotate && ok && (!FP8 || is_q)) {  // q always goes out as bf16; fp8 cache vectors below
-    *reinterpret_cast<uint4*>(dst + 8 * sub) = pack8(o1);
-    *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = pack8(o2);
+    *reinterpret_cast<uint4*>(dst + 8 * sub) = w1;
+    *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = w2;
   }
   if constexpr (FP8) {
+    float o1[8], o2[8];
+    unpack8(w1, o1);
+    unpack8(w2, o2);
     // every lane takes part in the amax butterfly; q vectors and idle lanes contribute nothing
     float amax = 0.f;
     if (ok && !is_q)
@@ -315,6 +396,26 @@ __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
       *reinterpret_cast<uint2*>(d8 + HALF + 8 * sub) = e4m3x8(o2, inv);
       if (sub == 0) (is_v ? p.v_scale : p.k_scale)[scale_off] = amax > 0.f ? __fdiv_rn(amax, 448.f) : 0.f;
     }
+  }
+}
+
+template <int D, bool FP8>
+__global__ void __launch_bounds__(kAppendVecThreads, 4)
+    kv_append_rope_vec_kernel(const AppendParams p) {
+  pdl_launch_dependents();  // the kernel after it waits for completion before reading
+  pdl_wait();               // q, k, v come from the projection ahead
+  constexpr int L = D / 16;        // lanes per vector
+  constexpr int VPW = 32 / L;      // vectors per warp
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % L;        // chunk index within the half
+  const long long warps = static_cast<long long>(gridDim.x) * (kAppendVecThreads / 32);
+  const long long stride = warps * VPW;  // vectors per sweep of the grid
+  const long long first = (static_cast<long long>(blockIdx.x) * (kAppendVecThreads / 32) + (threadIdx.x >> 5)) * VPW;
+  for (long long base = first; base < p.total_vectors; base += stride) {  // warp-uniform
+    AppendVecLoad v;
+    append_vec_load<D>(p, base + lane / L, sub, v);
+    append_vec_tables<D>(p, sub, v);
+    append_vec_store<D, FP8>(p, v, sub);
   }
 }
 

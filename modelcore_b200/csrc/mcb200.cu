@@ -182,6 +182,9 @@ constexpr long long kSplitMaxTiles = 33;  // 2048 keys + one tile of alignment s
 
 enum AttnMode { kModePersistent = 0, kModeSplit = 1, kModePrefill = 2 };
 
+// CTAs per SM of the grid-stride append kernel (256 threads of at most 64 registers each).
+constexpr int kAppendVecCtasPerSm = 4;
+
 // With num_ctas == 0, T_new >= kPrefillMinT and head_dim 64 or 128, the tensor-core prefill
 // kernel (prefill_attn.cuh) runs instead: 128-query tiles on tcgen05, no workspace.
 constexpr int kPrefillMinT = 64;
@@ -987,11 +990,17 @@ int mcb_kv_append_rope(const mcb_append_args* a, void* stream) {
   if (fp8 && !vec)
     return fail(MCB_ERR_ALIGNMENT, "mcb_kv_append_rope: an fp8 cache needs 16-byte aligned rows");
   if (vec) {
+    // a grid-stride kernel: at most kAppendVecCtasPerSm CTAs per SM, each warp looping over
+    // batches of vector groups with every load of a batch in flight before its arithmetic
+    if (p.total_vectors > 0x7fffffffll)
+      return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: %lld vectors in one call (at most 2^31 - 1)",
+                  p.total_vectors);
     const long long vpw = 32 / (a->D / 16);
     const long long warps = (p.total_vectors + vpw - 1) / vpw;
-    const long long blocks = (warps + mcb::kAppendWarpsPerBlock - 1) / mcb::kAppendWarpsPerBlock;
-    if (blocks > 0x7fffffffll) return fail(MCB_ERR_UNSUPPORTED, "mcb_kv_append_rope: grid too large");
-    const dim3 grid(static_cast<unsigned>(blocks)), block(mcb::kAppendWarpsPerBlock * 32);
+    const long long wpb = mcb::kAppendVecThreads / 32;
+    const long long blocks = std::min<long long>((warps + wpb - 1) / wpb,
+                                                 static_cast<long long>(kAppendVecCtasPerSm) * device_sm_count());
+    const dim3 grid(static_cast<unsigned>(blocks)), block(mcb::kAppendVecThreads);
     cudaError_t e;
     switch (a->D) {
       case 16: e = launch_pdl(mcb::kv_append_rope_vec_kernel<16, false>, grid, block, 0, st, p); break;
@@ -1203,8 +1212,6 @@ int mcb_sample(const mcb_sample_args* a, void* stream) {
                 (long long)a->logits_stride);
   if (!(a->temperature > 0.f))
     return fail(MCB_ERR_INVALID_ARG, "mcb_sample: temperature must be > 0 (greedy: top_k = 1)");
-  if (a->top_k > mcb::kSampleMaxK && a->top_k < a->V)
-    return fail(MCB_ERR_UNSUPPORTED, "mcb_sample: top_k %d above %d", a->top_k, mcb::kSampleMaxK);
   if (a->logits == nullptr || a->uniforms == nullptr || a->out == nullptr)
     return fail(MCB_ERR_INVALID_ARG, "mcb_sample: NULL pointer argument");
   if (a->rows == 0) return MCB_OK;

@@ -1,6 +1,6 @@
 // Sampling the next token from fp32 logits: sample_next_token, modelcore/generate.py:19-34.
 //
-//   top_k in [1, kSampleMaxK], < V:  the k largest logits (torch.topk), divided by the
+//   top_k in [1, V):                 the k largest logits (torch.topk), divided by the
 //                                    temperature, softmax, one multinomial draw
 //   otherwise:                       softmax over the whole row (logits / temperature), one draw
 //
@@ -14,8 +14,10 @@
 //
 // One 1024-thread CTA per row.  Top-k: a 4-pass radix select (8 bits a pass, MSB first) over the
 // order-preserving integer image of the logits finds the k-th largest value tau; the row's
-// elements above tau and the first (k - count above) elements equal to tau (by index) are
-// gathered, bitonic-sorted in shared memory, and scanned.  Each thread owns a contiguous chunk
+// elements above tau and the first (k - count above) elements equal to tau (by index) are the
+// candidates.  Up to kSampleMaxK of them are gathered, bitonic-sorted in shared memory, and
+// scanned; more are drawn from without sorting (sample_large_k: a radix descent over integer
+// weights).  Each thread owns a contiguous chunk
 // of the row, so "first by index" is a prefix count over threads.
 #pragma once
 
@@ -71,6 +73,137 @@ __device__ __forceinline__ T block_exclusive_scan(T v, T* scratch, T* total) {
   return excl;
 }
 
+// Inverse of float_key.
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Candidate weights of the large-k draw as fixed-point integers: round(expf(x / T - x0) * 2^40),
+// x0 the largest logit / T, so every weight is in [0, 2^40] and a row's total stays below 2^56.
+// Integer sums do not depend on their order, so the draw is deterministic however the threads
+// accumulate them.
+constexpr float kSampleFix = 1099511627776.0f;  // 2^40
+
+__device__ __forceinline__ unsigned long long sample_weight(float v, float inv_t, float x0) {
+  return __float2ull_rn(__fmul_rn(expf(__fmul_rn(v, inv_t) - x0), kSampleFix));
+}
+
+// top_k > kSampleMaxK (up to V - 1): the candidates are the elements above tau plus the first
+// `remaining` elements equal to tau (by index), as in the sorted path, but too many to sort in
+// shared memory.  The inverse-CDF draw over them in descending-logit order (ties by index) is
+// found without sorting: the target u * total is located by a 4-pass radix descent over the
+// candidates' order-preserving keys, MSB first, each pass a 256-bucket histogram of candidate
+// weights (walked from the largest bucket down, as the descending order walks them); the last
+// pass leaves the drawn key and the target's remainder within the candidates holding that key,
+// which share one weight, so the remainder divided by it is the rank of the drawn one among them
+// by index.
+__device__ __noinline__ void sample_large_k(const SampleParams& p, const float* lg, int row, int beg,
+                                            int end, uint32_t tau, int remaining, float u,
+                                            float* fscratch, int* iscratch, uint32_t* sel) {
+  __shared__ unsigned long long whist[256];
+  __shared__ unsigned long long wsum, wrem;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const float inv_t = p.inv_temperature;
+  // x0: the largest logit / T (the first candidate)
+  float mx = -INFINITY;
+  for (int i = beg; i < end; ++i) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) fscratch[tid >> 5] = mx;
+  __syncthreads();
+  mx = fscratch[0];
+  for (int w = 1; w < 32; ++w) mx = fmaxf(mx, fscratch[w]);
+  const float x0 = __fmul_rn(mx, inv_t);
+  // rank of this thread's first tie with tau among all ties (by index)
+  int n_eq = 0;
+  for (int i = beg; i < end; ++i) n_eq += float_key(lg[i]) == tau;
+  int tot_eq;
+  const int off_eq = block_exclusive_scan(n_eq, iscratch, &tot_eq);
+  // total candidate weight
+  unsigned long long t = 0;
+  {
+    int e = off_eq;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = float_key(lg[i]);
+      const bool cand = k > tau || (k == tau && e < remaining);
+      e += k == tau;
+      if (cand) t += sample_weight(lg[i], inv_t, x0);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (tid == 0) wsum = 0;
+  __syncthreads();
+  if (lane == 0) atomicAdd(&wsum, t);
+  __syncthreads();
+  const unsigned long long total = wsum;
+  unsigned long long rem = static_cast<unsigned long long>(static_cast<double>(u) * static_cast<double>(total));
+  if (rem >= total) rem = total - 1;
+  // radix descent to the drawn key
+  uint32_t pre = 0, msk = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (tid < 256) whist[tid] = 0;
+    __syncthreads();
+    int e = off_eq;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = float_key(lg[i]);
+      const bool cand = k > tau || (k == tau && e < remaining);
+      e += k == tau;
+      if (cand && (k & msk) == pre) atomicAdd(&whist[(k >> shift) & 0xffu], sample_weight(lg[i], inv_t, x0));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long acc = 0;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (acc + whist[b] > rem) break;
+        acc += whist[b];
+      }
+      sel[0] = pre | (static_cast<uint32_t>(b) << shift);
+      sel[1] = msk | (0xffu << shift);
+      wrem = rem - acc;
+    }
+    __syncthreads();
+    pre = sel[0];
+    msk = sel[1];
+    rem = wrem;
+    __syncthreads();
+  }
+  // the drawn key; its candidates share one weight: the rank among them (by index) follows
+  const uint32_t kappa = pre;
+  const unsigned long long wk = sample_weight(key_float(kappa), inv_t, x0);
+  long long j = wk > 0 ? static_cast<long long>(rem / wk) : 0;
+  int n_k = 0;
+  {
+    int e = off_eq;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = float_key(lg[i]);
+      const bool cand = k > tau || (k == tau && e < remaining);
+      e += k == tau;
+      n_k += cand && k == kappa;
+    }
+  }
+  int tot_k;
+  const int off_k = block_exclusive_scan(n_k, iscratch, &tot_k);
+  if (j >= tot_k) j = tot_k - 1;
+  if (off_k <= j && j < off_k + n_k) {
+    int c = off_k, e = off_eq;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = float_key(lg[i]);
+      const bool cand = k > tau || (k == tau && e < remaining);
+      e += k == tau;
+      if (cand && k == kappa) {
+        if (c == j) {
+          p.out[static_cast<long long>(row) * p.os] = i;
+          break;
+        }
+        ++c;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
   pdl_launch_dependents();
   pdl_wait();  // logits come from the kernel ahead (programmatic dependent launch)
@@ -88,7 +221,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const int beg = min(V, tid * chunk), end = min(V, beg + chunk);
   const float inv_t = p.inv_temperature;  // torch divides by a Python number as x * (1 / T)
   const float u = p.uniforms[row];
-  const bool topk = p.top_k >= 1 && p.top_k < V && p.top_k <= kSampleMaxK;
+  const bool topk = p.top_k >= 1 && p.top_k < V;
 
   if (!topk) {
     // ---- the whole row: softmax(logits / T) in index order ----
@@ -159,6 +292,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   }
   // tau = prefix (all 32 bits); `remaining` elements equal to tau complete the k
   const uint32_t tau = prefix;
+  if (p.top_k > kSampleMaxK) {
+    sample_large_k(p, lg, row, beg, end, tau, remaining, u, fscratch, iscratch, sel);
+    return;
+  }
   int n_gt = 0, n_eq = 0;
   for (int i = beg; i < end; ++i) {
     const uint32_t k = float_key(lg[i]);

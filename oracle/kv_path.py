@@ -376,7 +376,8 @@ def sample_token(logits, u, temperature, top_k):
     """The draw at uniform u: the first candidate whose inclusive cumulative probability exceeds
     u (the inverse CDF; torch.multinomial, generate.py:30 and :34, draws from the same
     distribution with its own generator).  Returns (index, distance of u to the nearest CDF
-    boundary) -- the second lets tests skip draws that fp32 rounding can move."""
+    boundary) -- the second lets tests skip draws that fp32 rounding can move (and, above 1024
+    candidates, the kernel's fixed-point weights: at most top_k * 2^-41 of the total)."""
     order, p = sample_candidates(logits, temperature, top_k)
     c = np.cumsum(p)
     i = int(np.searchsorted(c, u, side="right"))

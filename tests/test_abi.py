@@ -223,10 +223,10 @@ def test_sampler_validates_on_the_host():
     a.temperature = 0.0
     assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_INVALID_ARG
     a.temperature = 1.0
-    a.V, a.logits_stride, a.top_k = 5000, 5000, 2000
-    assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_UNSUPPORTED
-    a.top_k, a.rows = 50, 0
+    a.V, a.logits_stride, a.top_k, a.rows = 5000, 5000, 2000, 0  # any top_k < V is accepted
     assert lib.mcb_sample(ctypes.byref(a), None) == 0
+    a.top_k, a.logits = 50, None
+    assert lib.mcb_sample(ctypes.byref(a), None) == _native.MCB_ERR_INVALID_ARG
 
 
 def test_ring_slots_are_validated_on_the_host():

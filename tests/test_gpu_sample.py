@@ -2,7 +2,8 @@
 modelcore_b200.sample_next_token) against the CPU oracle and the reference's distribution.
 
 Bars: for a given uniform the drawn token equals the oracle's inverse-CDF draw (except draws
-within 1e-5 of a CDF boundary, where fp32 and float64 sums may disagree); greedy (temperature 0)
+within 2e-6 of a CDF boundary, where fp32 or fixed-point sums and float64 sums may disagree),
+for top_k up to V - 1 (above 1024 candidates the kernel draws without sorting); greedy (temperature 0)
 equals torch.argmax; over many uniforms the token frequencies match the reference's
 softmax(topk(logits) / T) within 5 standard errors."""
 import numpy as np
@@ -22,7 +23,9 @@ def ops():
 
 
 @pytest.mark.parametrize("top_k,T,V", [(50, 1.0, 32768), (1, 1.0, 32768), (1024, 0.7, 32768),
-                                       (None, 1.0, 32768), (13, 2.0, 1000), (None, 0.5, 1001)])
+                                       (None, 1.0, 32768), (13, 2.0, 1000), (None, 0.5, 1001),
+                                       (1025, 1.0, 32768), (2000, 1.0, 32768), (30000, 0.8, 32768),
+                                       (999, 1.0, 1000)])
 def test_draws_equal_the_oracle_for_given_uniforms(ops, top_k, T, V):
     g = torch.Generator(device="cuda").manual_seed(V + (top_k or 0))
     B = 64
@@ -48,12 +51,13 @@ def test_greedy_is_torch_argmax(ops):
     assert torch.equal(ids[:, 0], torch.argmax(logits, dim=-1))
 
 
-@pytest.mark.parametrize("top_k,T", [(50, 1.0), (None, 1.0), (8, 0.5)])
-def test_frequencies_match_the_reference_distribution(ops, top_k, T):
+@pytest.mark.parametrize("top_k,T,V", [(50, 1.0, 200), (None, 1.0, 200), (8, 0.5, 200),
+                                       (1500, 1.0, 2000)])
+def test_frequencies_match_the_reference_distribution(ops, top_k, T, V):
     import modelcore_b200
-    V, rows, reps = 200, 4096, 16
+    rows, reps = 4096, 16
     g = torch.Generator(device="cuda").manual_seed(7)
-    row = torch.randn(V, device="cuda", generator=g) * 2
+    row = torch.randn(V, device="cuda", generator=g) * (2 if V <= 200 else 4)
     logits = row.expand(rows, V).contiguous()
     counts = torch.zeros(V, device="cuda")
     for _ in range(reps):
@@ -68,7 +72,13 @@ def test_frequencies_match_the_reference_distribution(ops, top_k, T):
         p = F.softmax(row / T, dim=-1)
     freq = counts / n
     se = torch.sqrt(p * (1 - p) / n) + 1e-12
-    assert bool(((freq - p).abs() <= 5 * se + 1e-6).all())
+    big = p * n >= 20  # the normal approximation holds: each within 5 standard errors
+    assert bool(((freq - p).abs() <= 5 * se + 1e-6)[big].all())
+    # the rare candidates together: their total count within 5 standard errors of its mean
+    small = (p > 0) & ~big
+    if bool(small.any()):
+        ps = float(p[small].sum())
+        assert abs(float(counts[small].sum()) - ps * n) <= 5 * (ps * n * (1 - ps)) ** 0.5 + 1
     if top_k:
         assert bool((counts[p == 0] == 0).all())
 

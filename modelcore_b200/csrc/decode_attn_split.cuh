@@ -63,6 +63,17 @@ struct SplitAttnParams {
 // the portable 8 need the non-portable size, which the host checks the device schedules).
 constexpr int kMaxClusterSplits = 16;
 
+// The receive rows a cluster merge by push needs: split q's partial of the owner's j-th row goes to
+// slot q * ceil(kRows / ns) + j, so up to max over ns of ns * ceil(kRows / ns) slots.
+__host__ __device__ constexpr int split_recv_rows(int rows) {
+  int best = 0;
+  for (int ns = 2; ns <= kMaxClusterSplits; ++ns) {
+    const int v = ns * ((rows + ns - 1) / ns);
+    best = v > best ? v : best;
+  }
+  return best;
+}
+
 template <int D, int NQT, int KPW, int STAGES, bool FP8 = false>
 struct SplitAttnConfig {
   static constexpr int kRows = 8 * NQT;                      // query rows per CTA
@@ -102,7 +113,19 @@ struct SplitAttnConfig {
   // fused append: the CTA's query rows [kRows][D] and the new key and value [2][D], bf16
   static constexpr int FUSE_OFFSET = CTL_OFFSET + 16;
   static constexpr int FUSE_BYTES = FP8 ? 0 : (kRows + 2) * D * 2;
-  static constexpr int SMEM_BYTES = FUSE_OFFSET + FUSE_BYTES + 1024;  // + alignment slack
+  // cluster merge by push (bf16 copies of 3-4 stages with 8-row groups, D <= 128, where the extra
+  // shared memory keeps the CTAs per SM): every split stores its partial rows and log-sum-exps
+  // straight into the owning rank's receive buffer -- its own region, never part of the ring,
+  // because a split that finishes early writes while its owner may still be streaming -- and
+  // one cluster barrier later the owner merges from its own shared memory.  The 2-stage copies
+  // (sized for residency) and the fp8 ones pull the partials through DSMEM loads instead.
+  static constexpr bool PUSH = !FP8 && STAGES >= 3 && NQT == 1 && D <= 128;
+  static constexpr int RECV_ROWS = split_recv_rows(kRows);
+  static constexpr int RECV_OFFSET = (FUSE_OFFSET + FUSE_BYTES + 15) & ~15;
+  static constexpr int RECV_BYTES = PUSH ? RECV_ROWS * (D + 1) * 4 : 0;  // [RECV_ROWS][D], then lse
+  static constexpr int SMEM_BYTES = RECV_OFFSET + RECV_BYTES + 1024;  // + alignment slack
+  // 16-byte vector accesses: the query rows (FUSE) and the receive buffer; 8-byte mbarriers
+  static_assert(FUSE_OFFSET % 16 == 0 && RECV_OFFSET % 16 == 0 && BAR_OFFSET % 8 == 0, "alignment");
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
   static_assert(PANEL_BYTES % 1024 == 0 || ROW_BYTES < 128, "panel alignment");
@@ -295,6 +318,9 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     fence_mbarrier_init();
   }
   __syncthreads();
+  // push merge, phase 1 of the cluster barrier: this CTA runs (its receive buffer exists); the
+  // matching wait comes before the first remote store, long after every CTA has arrived
+  if (C::PUSH && p.cluster) cluster_arrive_relaxed();
 
   if (warp == kAttnConsumerWarps) {
     // ---------------- producer warp ----------------
@@ -684,6 +710,10 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     }
   }
   __syncthreads();
+  float* recv_o = reinterpret_cast<float*>(smem + C::RECV_OFFSET);  // push merge: [RECV_ROWS][D]
+  float* recv_lse = recv_o + C::RECV_ROWS * D;                       // [RECV_ROWS]
+  const int rpo = (C::kRows + p.nsplit - 1) / p.nsplit;  // rows a rank owns (row n: rank n % nsplit)
+  if (C::PUSH && p.cluster) cluster_wait();  // phase 1 done: every rank's buffer may be written
 
   // Per row: the CTA max, each warp's weight and the total.
   if (threadIdx.x < C::kRows) {
@@ -702,7 +732,10 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     const int r = r0 + n;
     const float lse = (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
     if (p.cluster) {
-      reinterpret_cast<float*>(smem + C::CL_OFFSET)[C::kRows * D + n] = lse;
+      if constexpr (C::PUSH)
+        st_dsmem_f32(map_to_rank(recv_lse + split * rpo + n / p.nsplit, static_cast<uint32_t>(n % p.nsplit)), lse);
+      else
+        reinterpret_cast<float*>(smem + C::CL_OFFSET)[C::kRows * D + n] = lse;
     } else if (p.nsplit > 1 && r < r1) {
       const int t = r / p.G, h = kvh * p.G + r % p.G;
       p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] = lse;
@@ -724,7 +757,11 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     if (p.nsplit == 1) {
       p.out[row * D + d] = float_to_bf16_bits(o);
     } else if (p.cluster) {
-      reinterpret_cast<float*>(smem + C::CL_OFFSET)[n * D + d] = o;
+      if constexpr (C::PUSH)
+        st_dsmem_f32(map_to_rank(recv_o + (split * rpo + n / p.nsplit) * D + d,
+                                 static_cast<uint32_t>(n % p.nsplit)), o);
+      else
+        reinterpret_cast<float*>(smem + C::CL_OFFSET)[n * D + d] = o;
     } else {
       p.part_o[(row * p.nsplit + split) * D + d] = o;
     }
@@ -733,6 +770,44 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     if (p.nsplit > 1 && p.counters != nullptr)
       split_publish<D>(p, static_cast<int>(blockIdx.x) / p.nsplit, b, kvh, r0, r1,
                        reinterpret_cast<int*>(smem + C::CTL_OFFSET));
+    return;
+  }
+
+  if constexpr (C::PUSH) {
+    // ---- push merge: rank q (= split) owns rows n = q, q + nsplit, .. of the row group, whose
+    // partials every rank stored into q's receive buffer before the barrier (one barrier in all;
+    // no rank reads another's shared memory, so none has to wait for the others to finish) ----
+    cluster_sync();  // phase 2: every rank's stores are visible to their owners
+    const int ns = p.nsplit;
+    const int my_rows = (C::kRows - split + ns - 1) / ns;
+    for (int idx = threadIdx.x; idx < my_rows * D; idx += kAttnThreads) {
+      const int j = idx / D;
+      const int d = idx - j * D;
+      const int n = split + j * ns;
+      const int r = r0 + n;
+      float lq[kMaxClusterSplits];
+      float mmax = -CUDART_INF_F;
+#pragma unroll
+      for (int q = 0; q < kMaxClusterSplits; ++q) {
+        lq[q] = q < ns ? recv_lse[q * rpo + j] : -CUDART_INF_F;
+        mmax = fmaxf(mmax, lq[q]);
+      }
+      float wsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxClusterSplits; ++q) {
+        lq[q] = (lq[q] == -CUDART_INF_F) ? 0.f : fast_exp2(lq[q] - mmax);
+        wsum += lq[q];
+      }
+      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+      float o = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxClusterSplits; ++q)
+        if (q < ns) o = fmaf(lq[q] * inv, recv_o[(q * rpo + j) * D + d], o);
+      if (r < r1) {
+        const int t = r / p.G, h = kvh * p.G + r % p.G;
+        p.out[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);
+      }
+    }
     return;
   }
 

@@ -139,6 +139,12 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 // kernel has completed and its memory is visible, and must precede every read of its outputs.
 // pdl_launch_dependents() lets the next kernel (if launched that way) start early.  Both are
 // no-ops for kernels launched without the attribute.
+//
+// Every kernel here triggers only after its own pdl_wait() has returned (the first trigger of any
+// thread counts for its CTA, and the next grid starts once every CTA has triggered or exited).
+// So when a kernel starts, every kernel before the one directly ahead of it has completed: the
+// reads some kernels make before their wait -- weights (decode_proj), cache_seqlens and the key
+// tiles of earlier steps (decode attention) -- only have to avoid what that one kernel writes.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -296,6 +296,9 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
                        tile_new < tile0 + my_tiles;
 
   if (my_tiles == 0 && !p.cluster) {  // an empty split: its partial carries no weight
+    // the workspace and the counters may still be in use by the launch ahead (its last-arrival
+    // merges): wait for it before writing either
+    pdl_wait();
     if (threadIdx.x < C::kRows) {
       const int r = r0 + threadIdx.x;
       if (r < r1) {
@@ -333,9 +336,11 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
         const int s = i % STAGES;
         if (i >= STAGES && !mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1)) break;
         const int key0 = kb + (tile0 + i) * C::TK;
-        // keys below L are from earlier steps; a tile reaching L holds this step's new keys,
-        // written by the append kernel this launch may have overlapped (PDL)
-        if (!waited && (p.fuse || key0 + C::TK > L)) {
+        // keys below L are from earlier steps, written at least two launches back (complete: see
+        // pdl_launch_dependents in common.cuh); a tile reaching L holds this step's new key,
+        // written by the append kernel this launch may have overlapped (PDL) -- or, fused, by
+        // this launch itself, whose owner warp overwrites the stale bytes in shared memory
+        if (!waited && key0 + C::TK > L) {
           pdl_wait();
           waited = true;
         }
@@ -372,6 +377,8 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
   if (warp < kAttnConsumerWarps) {
     // ---------------- consumer warps ----------------
     pdl_wait();  // q comes from the append kernel ahead of this one (fused: the projection)
+    // the kernel after this one may start its prologue and its loads of earlier steps' keys
+    pdl_launch_dependents();
     uint16_t* qbuf = reinterpret_cast<uint16_t*>(smem + C::FUSE_OFFSET);  // [kRows][D]
     uint16_t* kvbuf = qbuf + C::kRows * D;                                 // [2][D]
     if (!FP8 && p.fuse) {

@@ -99,7 +99,6 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   uint64_t* w_full = full + panels;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(w_full + 1);
 
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i <= panels; ++i) mbar_init(full + i, 1);
@@ -115,6 +114,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   }
   __syncthreads();  // barriers initialised
   pdl_wait();       // the activations and the residual come from the kernels ahead
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int i = 0; i < panels; ++i) {
       mbar_arrive_expect_tx(&full[i], ADD ? 2 * kProjPanel : kProjPanel);

@@ -56,8 +56,8 @@ constexpr int kAppendWarpsPerBlock = 4;
 
 __global__ void __launch_bounds__(kAppendWarpsPerBlock * 32)
     kv_append_rope_kernel(const AppendParams p) {
-  pdl_launch_dependents();  // the kernel after it waits for completion before reading
   pdl_wait();               // q, k, v come from the projection ahead
+  pdl_launch_dependents();  // after the wait: see pdl_launch_dependents in common.cuh
   const int lane = threadIdx.x & 31;
   const long long w = static_cast<long long>(blockIdx.x) * kAppendWarpsPerBlock + (threadIdx.x >> 5);
   if (w >= p.total_vectors) return;
@@ -402,8 +402,8 @@ __device__ __forceinline__ void append_vec_store(const AppendParams& p, const Ap
 template <int D, bool FP8>
 __global__ void __launch_bounds__(kAppendVecThreads, 4)
     kv_append_rope_vec_kernel(const AppendParams p) {
-  pdl_launch_dependents();  // the kernel after it waits for completion before reading
   pdl_wait();               // q, k, v come from the projection ahead
+  pdl_launch_dependents();  // after the wait: see pdl_launch_dependents in common.cuh
   constexpr int L = D / 16;        // lanes per vector
   constexpr int VPW = 32 / L;      // vectors per warp
   const int lane = threadIdx.x & 31;

@@ -65,8 +65,9 @@ __global__ void __launch_bounds__(256) kv_copy_rows_kernel(const CopyParams p) {
   }
 }
 
+// No trigger: the kernel after an advance may read cache_seqlens before its own wait (decode
+// attention does), so it must not start until the advance has completed.
 __global__ void kv_advance_kernel(int32_t* seqlens, int B, int n) {
-  pdl_launch_dependents();
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < B) seqlens[i] += n;

@@ -718,7 +718,11 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
   p.n_qpairs = (a->T + 2 * mcb::kPfTile - 1) / (2 * mcb::kPfTile);
   p.ring = a->ring != 0;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
-  const long long grid = static_cast<long long>(p.n_qpairs) * a->B * a->Hq;
+  const long long items = static_cast<long long>(p.n_qpairs) * a->B * a->Hq;
+  if (items > INT32_MAX) return fail(MCB_ERR_UNSUPPORTED, "mcb_prefill_attn: %lld work items", items);
+  p.n_items = static_cast<int>(items);
+  // persistent: one CTA per SM (each holds all of its SM's TMEM), items strided over them
+  const long long grid = std::min<long long>(items, device_sm_count());
   if (a->D == 64) return PrefillVariant<64>::launch(grid, qm, km, vm, p, st);
   return PrefillVariant<128>::launch(grid, qm, km, vm, p, st);
 }

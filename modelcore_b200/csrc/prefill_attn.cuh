@@ -6,10 +6,13 @@
 // the cache (the append ran first), so a prompt's prefill is dense causal attention over its own
 // keys plus whatever prefix the row already held.
 //
-// One CTA takes two 128-query tiles (Q0, Q1: 256 consecutive queries) of one q head of one row
-// and walks 128-key tiles, each K/V tile serving both query tiles:
+// A work item is two 128-query tiles (Q0, Q1: 256 consecutive queries) of one q head of one row;
+// its CTA walks 128-key tiles, each K/V tile serving both query tiles.  The grid is persistent
+// (one CTA per SM, items strided over the CTAs, longest first), so TMEM allocation, barrier setup
+// and the pipeline fill are paid once per CTA and the next item's loads overlap this one's end:
 //
-//   warp 0       TMA producer: Q0 and Q1 once, then K_j and V_j into a two-stage ring
+//   warp 0       TMA producer: per item Q0 and Q1 (double-buffered for D = 64), then K_j and V_j
+//                into a two-stage ring that runs on across items
 //   warp 1       allocates all 512 TMEM columns; lane 0 issues the MMAs, ping-ponging the tiles:
 //                  S0_j = Q0 K_j^T, S1_j = Q1 K_j^T      kind::f16, M=128 N=128 K=D, A and B
 //                                                        from shared memory, fp32 into TMEM
@@ -199,6 +202,7 @@ struct PrefillParams {
   const int* cache_seqlens;   // (B,) positions before the new tokens
   int B, T, Hq, Hkv, G, Tmax, window;
   int n_qpairs;               // ceil(T / 256)
+  int n_items;                // n_qpairs * B * Hq work items: one (query-tile pair, row, q head) each
   float scale_log2;           // softmax_scale * log2(e)
   int ring;                   // the slot is a ring of Tmax positions (key c at index c % Tmax)
 };
@@ -207,9 +211,12 @@ template <int D>
 struct PrefillConfig {
   static constexpr int kPanels = D / 64;
   static constexpr int kTileBytes = kPanels * kPfTile * 128;  // one Q / K / V tile
-  static constexpr int kQOff = 0;                             // Q0, Q1
-  static constexpr int kKOff = kQOff + 2 * kTileBytes;        // K ring, 2 stages
-  static constexpr int kVOff = kKOff + 2 * kTileBytes;        // V ring, 2 stages
+  // Q (the pair Q0, Q1) is double-buffered where shared memory allows it (D = 64): the next
+  // item's queries land while this item's last MMAs still read the current ones
+  static constexpr int kQBufs = D <= 64 ? 2 : 1;
+  static constexpr int kQOff = 0;                                  // [kQBufs][Q0, Q1]
+  static constexpr int kKOff = kQOff + kQBufs * 2 * kTileBytes;    // K ring, 2 stages
+  static constexpr int kVOff = kKOff + 2 * kTileBytes;             // V ring, 2 stages
   static constexpr int kBarOff = kVOff + 2 * kTileBytes;
   static constexpr int kBytes = kBarOff + 256;
   // at least 116 KB so two CTAs never share an SM: each holds all 512 TMEM columns
@@ -218,61 +225,94 @@ struct PrefillConfig {
 
 // The first key tile a query tile needs and how many tiles (from k_first) it spans.
 struct QTileRange {
-  int qbase, j_begin, j_end;  // key tiles [j_begin, j_end) of the CTA's walk
+  int qbase, j_begin, j_end;  // key tiles [j_begin, j_end) of the item's walk
 };
 
+// Work item i: query-tile pair qp (longest pairs first, so the short tail items fill the gaps
+// at the end) of row b, q head h.
+struct PfItem {
+  int b, h, hk, L, q0, k_first, nkv;
+  bool in_range;
+  QTileRange rng[2];
+};
+
+__device__ __forceinline__ PfItem prefill_item(const PrefillParams& p, int i) {
+  PfItem it;
+  const int bh = p.B * p.Hq;
+  const int qp = p.n_qpairs - 1 - i / bh;
+  it.b = (i % bh) / p.Hq;
+  it.h = (i % bh) % p.Hq;
+  it.hk = it.h / p.G;
+  it.L = p.cache_seqlens[it.b];
+  it.q0 = qp * 2 * kPfTile;
+  const int pos_last = it.L + min(it.q0 + 2 * kPfTile, p.T) - 1;
+  it.in_range = it.L >= 0 && (p.ring || pos_last < p.Tmax);
+  it.k_first = (p.window >= 0 ? max(0, it.L + it.q0 - p.window) : 0) / kPfTile * kPfTile;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qb = it.q0 + t * kPfTile;
+    it.rng[t].qbase = qb;
+    if (!it.in_range || qb >= p.T) {
+      it.rng[t].j_begin = it.rng[t].j_end = 0;
+    } else {
+      const int first = (p.window >= 0 ? max(0, it.L + qb - p.window) : 0) / kPfTile * kPfTile;
+      it.rng[t].j_begin = (first - it.k_first) / kPfTile;
+      it.rng[t].j_end = (it.L + min(qb + kPfTile, p.T) - 1 - it.k_first) / kPfTile + 1;
+    }
+  }
+  it.nkv = max(it.rng[0].j_end, it.rng[1].j_end);
+  return it;
+}
+
+// The item CTA c takes in round r: items are sorted longest first and dealt in serpentine order
+// (even rounds left to right, odd rounds right to left), so a CTA that drew a long item in one
+// round draws a short one in the next; -1 past the last item.
+__device__ __forceinline__ int prefill_round_item(const PrefillParams& p, int r) {
+  const int i = r * static_cast<int>(gridDim.x) +
+                ((r & 1) ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x));
+  return i < p.n_items ? i : -1;
+}
+
+// Persistent: CTA c takes one item a round (prefill_round_item); TMEM, the barriers and the tensor maps are
+// set up once per CTA, the K/V ring and every barrier phase run on across items, so the next
+// item's loads and first MMAs overlap this item's epilogue.  Items with no key tile (nkv == 0)
+// are skipped by every role alike.  Per item the MMA issuer commits q_empty (the Q buffer may be
+// refilled) and o_done; every softmax thread waits for o_done, reads its O, and arrives on
+// epi_done, which the issuer waits for before the next item's o_done -- so no softmax group, not
+// even one with no query tile in an item (T <= 128), can find o_done two phases ahead.
+// 168 registers a thread: the 10 warps land three to a sub-partition on two of the four, whose
+// 16,384 registers each cap a thread at 170 (a higher cap fails to launch); a few bytes spill.
 template <int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   using Cfg = PrefillConfig<D>;
+  constexpr int QB = Cfg::kQBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2] per query tile
-  uint64_t* p_full = bars + 9;    // [2] per query tile, 128 arrivals
-  uint64_t* o_done = bars + 11;
-  uint64_t* drained = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 14);
+  uint64_t* q_full = bars + 0;    // [2] per Q buffer
+  uint64_t* q_empty = bars + 2;   // [2] per Q buffer
+  uint64_t* k_full = bars + 4;    // [2]
+  uint64_t* v_full = bars + 6;    // [2]
+  uint64_t* kv_empty = bars + 8;  // [2]
+  uint64_t* s_full = bars + 10;   // [2] per query tile
+  uint64_t* p_full = bars + 12;   // [2] per query tile, 128 arrivals
+  uint64_t* o_done = bars + 14;
+  uint64_t* epi_done = bars + 15;  // 256 arrivals: every softmax thread, once per item
+  uint64_t* drained = bars + 16;
+  constexpr int kNumBars = 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = p.B * p.Hq;
-  const int qp = p.n_qpairs - 1 - static_cast<int>(blockIdx.x / bh);  // longest pairs first
-  const int b = static_cast<int>(blockIdx.x % bh) / p.Hq;
-  const int h = static_cast<int>(blockIdx.x % bh) % p.Hq;
-  const int hk = h / p.G;
-  const int L = p.cache_seqlens[b];
-  const int q0 = qp * 2 * kPfTile;
-  const int pos_last = L + min(q0 + 2 * kPfTile, p.T) - 1;
-  const bool in_range = L >= 0 && (p.ring || pos_last < p.Tmax);
-  const int k_first =
-      (p.window >= 0 ? max(0, L + q0 - p.window) : 0) / kPfTile * kPfTile;
-  QTileRange rng[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int qb = q0 + t * kPfTile;
-    rng[t].qbase = qb;
-    if (!in_range || qb >= p.T) {
-      rng[t].j_begin = rng[t].j_end = 0;
-    } else {
-      const int first = (p.window >= 0 ? max(0, L + qb - p.window) : 0) / kPfTile * kPfTile;
-      rng[t].j_begin = (first - k_first) / kPfTile;
-      rng[t].j_end = (L + min(qb + kPfTile, p.T) - 1 - k_first) / kPfTile + 1;
-    }
-  }
-  const int nkv = max(rng[0].j_end, rng[1].j_end);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 13; ++i) mbar_init(bars + i, (i == 9 || i == 10) ? 128 : 1);
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(bars + i, (i == 12 || i == 13) ? 128 : (i == 15 ? 256 : 1));
     *abort_flag = 0;
-    if (!in_range) record_error(kErrPositionBeyondCache);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -285,208 +325,260 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t base = smem_u32(smem);
 
-  if (warp == 0 && lane == 0 && nkv > 0) {
+  if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     const uint64_t pol = l2_policy_evict_first();
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    mbar_arrive_expect_tx(q_full, 2 * Cfg::kTileBytes);
+    int g = 0;                  // K/V tiles issued (ring position)
+    int k = 0;                  // items started
+    int q_last[2] = {-1, -1};   // per Q buffer: the use (k / QB) of its last load
+    bool ok = true;
+    for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
+      const int i = prefill_round_item(p, r);
+      if (i < 0) continue;
+      const PfItem it = prefill_item(p, i);
+      if (!it.in_range) record_error(kErrPositionBeyondCache);
+      if (it.nkv == 0) continue;
+      const int qb = k % QB, qn = k / QB;
+      if (qn > 0 && !mbar_wait_or_abort(&q_empty[qb], (qn - 1) & 1, abort_flag)) break;
+      mbar_arrive_expect_tx(&q_full[qb], 2 * Cfg::kTileBytes);
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < 2; ++t)
 #pragma unroll
-      for (int pn = 0; pn < Cfg::kPanels; ++pn)
-        tma_load_4d(smem + Cfg::kQOff + t * Cfg::kTileBytes + pn * kPfTile * 128, &qmap, q_full,
-                    pn * 64, h, q0 + t * kPfTile, b, pol);
-    int issued = 0;
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      if (j >= 2 && !mbar_wait_or_abort(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag)) break;
-      const int k0 = k_first + j * kPfTile;
-      const int slot0 = p.ring ? k0 % p.Tmax : k0;  // a ring slot: Tmax % 128 == 0
-      mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
+        for (int pn = 0; pn < Cfg::kPanels; ++pn)
+          tma_load_4d(smem + Cfg::kQOff + (qb * 2 + t) * Cfg::kTileBytes + pn * kPfTile * 128, &qmap,
+                      &q_full[qb], pn * 64, it.h, it.q0 + t * kPfTile, it.b, pol);
+      q_last[qb] = qn;
+      for (int j = 0; j < it.nkv; ++j, ++g) {
+        const int st = g & 1;
+        if (g >= 2 && !mbar_wait_or_abort(&kv_empty[st], ((g >> 1) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int k0 = it.k_first + j * kPfTile;
+        const int slot0 = p.ring ? k0 % p.Tmax : k0;  // a ring slot: Tmax % 128 == 0
+        mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
 #pragma unroll
-      for (int pn = 0; pn < Cfg::kPanels; ++pn)
-        tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &kmap,
-                    &k_full[st], pn * 64, hk, slot0, b, pol);
-      mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
+        for (int pn = 0; pn < Cfg::kPanels; ++pn)
+          tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &kmap,
+                      &k_full[st], pn * 64, it.hk, slot0, it.b, pol);
+        mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
 #pragma unroll
-      for (int pn = 0; pn < Cfg::kPanels; ++pn)
-        tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &vmap,
-                    &v_full[st], pn * 64, hk, slot0, b, pol);
-      issued = j + 1;
+        for (int pn = 0; pn < Cfg::kPanels; ++pn)
+          tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + pn * kPfTile * 128, &vmap,
+                      &v_full[st], pn * 64, it.hk, slot0, it.b, pol);
+      }
+      ++k;
     }
     // on an abort, wait (bounded) for the copies still in flight before the CTA can exit
     if (*abort_flag) {
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        mbar_wait(&k_full[j & 1], (j >> 1) & 1);
-        mbar_wait(&v_full[j & 1], (j >> 1) & 1);
+      for (int gg = max(0, g - 2); gg < g; ++gg) {
+        mbar_wait(&k_full[gg & 1], (gg >> 1) & 1);
+        mbar_wait(&v_full[gg & 1], (gg >> 1) & 1);
       }
-      mbar_wait(q_full, 0);
+      for (int qb = 0; qb < QB; ++qb)
+        if (q_last[qb] >= 0) mbar_wait(&q_full[qb], q_last[qb] & 1);
     }
-  } else if (warp == 1 && lane == 0 && nkv > 0) {
+  } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc_s = umma_idesc_bf16(128, kPfTile, 0);
     constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 1);
-    bool ok = mbar_wait_or_abort(q_full, 0, abort_flag);
-    int k_waited = -1, v_waited = -1;
-    int pv_count[2] = {0, 0};
-    auto active = [&](int t, int j) { return j >= rng[t].j_begin && j < rng[t].j_end; };
-    auto issue_s = [&](int t, int j) -> bool {
-      if (k_waited < j) {
-        if (!mbar_wait_or_abort(&k_full[j & 1], (j >> 1) & 1, abort_flag)) return false;
-        k_waited = j;
-      }
-      tc_fence_after();
-      const uint32_t q_base = base + Cfg::kQOff + t * Cfg::kTileBytes;
-      const uint32_t k_base = base + Cfg::kKOff + (j & 1) * Cfg::kTileBytes;
+    int g = 0;                   // K/V tiles consumed by earlier items
+    int k = 0;                   // items done
+    int pv_total[2] = {0, 0};    // PV MMAs issued per query tile (p_full phases)
+    bool ok = true;
+    for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
+      const int i = prefill_round_item(p, r);
+      if (i < 0) continue;
+      const PfItem it = prefill_item(p, i);
+      if (it.nkv == 0) continue;
+      const int qb = k % QB;
+      ok = mbar_wait_or_abort(&q_full[qb], (k / QB) & 1, abort_flag);
+      int k_waited = -1, v_waited = -1;
+      int pv_item[2] = {0, 0};
+      // Q is free for the next load once this item's last S MMA has read it
+      const int s_total = (it.rng[0].j_end - it.rng[0].j_begin) + (it.rng[1].j_end - it.rng[1].j_begin);
+      int s_issued = 0;
+      auto active = [&](int t, int j) { return j >= it.rng[t].j_begin && j < it.rng[t].j_end; };
+      auto issue_s = [&](int t, int j) -> bool {
+        const int gj = g + j;
+        if (k_waited < j) {
+          if (!mbar_wait_or_abort(&k_full[gj & 1], (gj >> 1) & 1, abort_flag)) return false;
+          k_waited = j;
+        }
+        tc_fence_after();
+        const uint32_t q_base = base + Cfg::kQOff + (qb * 2 + t) * Cfg::kTileBytes;
+        const uint32_t k_base = base + Cfg::kKOff + (gj & 1) * Cfg::kTileBytes;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * (kPfTile * 128) + (kk & 3) * 32;
-        umma_ss(tmem + t * kPfTile, smem_desc_sw128(q_base + off, 16, 1024),
-                smem_desc_sw128(k_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-      }
-      umma_commit(&s_full[t]);
-      return true;
-    };
-    auto issue_pv = [&](int t, int j) -> bool {
-      if (!mbar_wait_or_abort(&p_full[t], pv_count[t] & 1, abort_flag)) return false;
-      if (v_waited < j) {
-        if (!mbar_wait_or_abort(&v_full[j & 1], (j >> 1) & 1, abort_flag)) return false;
-        v_waited = j;
-      }
-      tc_fence_after();
-      const uint32_t v_base = base + Cfg::kVOff + (j & 1) * Cfg::kTileBytes;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kPfTile * 128) + (kk & 3) * 32;
+          umma_ss(tmem + t * kPfTile, smem_desc_sw128(q_base + off, 16, 1024),
+                  smem_desc_sw128(k_base + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+        if (++s_issued == s_total) umma_commit(&q_empty[qb]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int gj = g + j;
+        if (!mbar_wait_or_abort(&p_full[t], pv_total[t] & 1, abort_flag)) return false;
+        if (v_waited < j) {
+          if (!mbar_wait_or_abort(&v_full[gj & 1], (gj >> 1) & 1, abort_flag)) return false;
+          v_waited = j;
+        }
+        tc_fence_after();
+        const uint32_t v_base = base + Cfg::kVOff + (gj & 1) * Cfg::kTileBytes;
 #pragma unroll
-      for (int kk = 0; kk < kPfTile / 16; ++kk)
-        umma_ts(tmem + 256 + t * D, tmem + t * kPfTile + kk * 8,
-                smem_desc_sw128(v_base + kk * 16 * 128, kPfTile * 128, 1024), idesc_o,
-                (pv_count[t] > 0 || kk > 0) ? 1u : 0u);
-      ++pv_count[t];
-      return true;
-    };
-    if (ok && active(0, 0)) ok = issue_s(0, 0);
-    if (ok && active(1, 0)) ok = issue_s(1, 0);
-    for (int j = 0; ok && j < nkv; ++j) {
-      if (ok && active(0, j)) ok = issue_pv(0, j);
-      if (ok && active(0, j + 1)) ok = issue_s(0, j + 1);
-      if (ok && active(1, j)) ok = issue_pv(1, j);
-      if (ok) umma_commit(&kv_empty[j & 1]);
-      if (ok && active(1, j + 1)) ok = issue_s(1, j + 1);
+        for (int kk = 0; kk < kPfTile / 16; ++kk)
+          umma_ts(tmem + 256 + t * D, tmem + t * kPfTile + kk * 8,
+                  smem_desc_sw128(v_base + kk * 16 * 128, kPfTile * 128, 1024), idesc_o,
+                  (pv_item[t] > 0 || kk > 0) ? 1u : 0u);
+        ++pv_item[t];
+        ++pv_total[t];
+        return true;
+      };
+      if (ok && active(0, 0)) ok = issue_s(0, 0);
+      if (ok && active(1, 0)) ok = issue_s(1, 0);
+      for (int j = 0; ok && j < it.nkv; ++j) {
+        if (ok && active(0, j)) ok = issue_pv(0, j);
+        if (ok && active(0, j + 1)) ok = issue_s(0, j + 1);
+        if (ok && active(1, j)) ok = issue_pv(1, j);
+        if (ok) umma_commit(&kv_empty[(g + j) & 1]);
+        if (ok && active(1, j + 1)) ok = issue_s(1, j + 1);
+      }
+      if (ok && k > 0) ok = mbar_wait_or_abort(epi_done, (k - 1) & 1, abort_flag);
+      if (ok) umma_commit(o_done);
+      g += it.nkv;
+      ++k;
     }
-    if (ok) umma_commit(o_done);
     // every MMA this thread issued has completed before TMEM can be freed
     umma_commit(drained);
     mbar_wait(drained, 0);
   } else if (warp >= 2) {
     // ---------------- softmax: warps 2-5 query tile 0, warps 6-9 query tile 1 ----------------
     const int t = (warp - 2) >> 2;
-    // scalars, not rng[t]: a runtime index would put the array in local memory
-    const int qbase = t ? rng[1].qbase : rng[0].qbase;
-    const int j_begin = t ? rng[1].j_begin : rng[0].j_begin;
-    const int j_end = t ? rng[1].j_end : rng[0].j_end;
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
     const int row = quarter * 32 + lane;          // query row within the tile
-    const int q = qbase + row;
-    const bool valid = q < p.T;
-    const int pos = L + q;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * kPfTile;
     const uint32_t o_addr = tmem + lane_off + 256 + t * D;
-    float m_used = -INFINITY, l = 0.f;
+    int k = 0;       // items done
+    int s_cnt = 0;   // S tiles of this query tile consumed (s_full phases)
     bool ok = true;
-    int cnt = 0;
-    for (int j = j_begin; j < j_end; ++j, ++cnt) {
-      // waits are made warp-uniform: the tcgen05.ld/st below are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[t], cnt & 1, abort_flag))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int k0 = k_first + j * kPfTile;
-      uint32_t sr[128];
-      tmem_ld128(s_addr, sr);  // one round trip: TMEM load latency dominates a chunked read
-      // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
-      float mx = -INFINITY;
-      const bool full = k0 + kPfTile - 1 <= L + qbase &&
-                        (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
-                        qbase + kPfTile <= p.T;
-      if (!full) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const int key = k0 + i;
-          const bool vis = valid && key <= pos && (p.window < 0 || pos - key <= p.window);
-          if (!vis) sr[i] = __float_as_uint(-INFINITY);
+    for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
+      const int i = prefill_round_item(p, r);
+      if (i < 0) continue;
+      const PfItem it = prefill_item(p, i);
+      if (it.nkv == 0) continue;
+      // scalars, not it.rng[t]: a runtime index would put the array in local memory
+      const int qbase = t ? it.rng[1].qbase : it.rng[0].qbase;
+      const int j_begin = t ? it.rng[1].j_begin : it.rng[0].j_begin;
+      const int j_end = t ? it.rng[1].j_end : it.rng[0].j_end;
+      const int L = it.L;
+      const int q = qbase + row;
+      const bool valid = q < p.T;
+      const int pos = L + q;
+      float m_used = -INFINITY, l = 0.f;
+      int cnt = 0;
+      for (int j = j_begin; j < j_end; ++j, ++cnt, ++s_cnt) {
+        // waits are made warp-uniform: the tcgen05.ld/st below are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&s_full[t], s_cnt & 1, abort_flag))) {
+          ok = false;
+          break;
         }
-      }
+        tc_fence_after();
+        const int k0 = it.k_first + j * kPfTile;
+        uint32_t sr[128];
+        tmem_ld128(s_addr, sr);  // one round trip: TMEM load latency dominates a chunked read
+        // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
+        float mx = -INFINITY;
+        const bool full = k0 + kPfTile - 1 <= L + qbase &&
+                          (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
+                          qbase + kPfTile <= p.T;
+        if (!full) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmax3(mx, __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]));
-      mx *= p.scale_log2;
-      // lazy rescale: move the running max only when it grows by more than 2^8
-      float alpha = 1.f;
-      if (mx > m_used + 8.f) {
-        alpha = fast_exp2(m_used - mx);  // 0 when m_used is -inf
-        m_used = mx;
-        l *= alpha;
-      }
-      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-      const uint64_t sc2 = pair_f32(p.scale_log2, p.scale_log2), nm2 = pair_f32(neg_m, neg_m);
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns of packed bf16 P over S
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {  // 4 keys: three exponentials on MUFU, one on the FMA pipe
-          const int k = 32 * c + 4 * i;
-          float x0, x1, x2, x3;
-          ffma2_bc(x0, x1, __uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), sc2, nm2);
-          ffma2_bc(x2, x3, __uint_as_float(sr[k + 2]), __uint_as_float(sr[k + 3]), sc2, nm2);
-          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2);
-          const float e3 = exp2_poly3(x3);
-          sum0 += e0 + e2;
-          sum1 += e1 + e3;
-          // the packed P words reuse the registers of scores already consumed
-          sr[32 * c + 2 * i] = pack_bf16x2_rn(e0, e1);
-          sr[32 * c + 2 * i + 1] = pack_bf16x2_rn(e2, e3);
+          for (int c = 0; c < 128; ++c) {
+            const int key = k0 + c;
+            const bool vis = valid && key <= pos && (p.window < 0 || pos - key <= p.window);
+            if (!vis) sr[c] = __float_as_uint(-INFINITY);
+          }
         }
-        tmem_st16_nowait(s_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx = fmax3(mx, __uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1]));
+        mx *= p.scale_log2;
+        // lazy rescale: move the running max only when it grows by more than 2^8
+        float alpha = 1.f;
+        if (mx > m_used + 8.f) {
+          alpha = fast_exp2(m_used - mx);  // 0 when m_used is -inf
+          m_used = mx;
+          l *= alpha;
+        }
+        const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+        const uint64_t sc2 = pair_f32(p.scale_log2, p.scale_log2), nm2 = pair_f32(neg_m, neg_m);
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns of packed bf16 P over S
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {  // 4 keys: three exponentials on MUFU, one on the FMA pipe
+            const int kx = 32 * c + 4 * u;
+            float x0, x1, x2, x3;
+            ffma2_bc(x0, x1, __uint_as_float(sr[kx]), __uint_as_float(sr[kx + 1]), sc2, nm2);
+            ffma2_bc(x2, x3, __uint_as_float(sr[kx + 2]), __uint_as_float(sr[kx + 3]), sc2, nm2);
+            const float e0 = fast_exp2(x0), e1 = fast_exp2(x1), e2 = fast_exp2(x2);
+            const float e3 = exp2_poly3(x3);
+            sum0 += e0 + e2;
+            sum1 += e1 + e3;
+            // the packed P words reuse the registers of scores already consumed
+            sr[32 * c + 2 * u] = pack_bf16x2_rn(e0, e1);
+            sr[32 * c + 2 * u + 1] = pack_bf16x2_rn(e2, e3);
+          }
+          tmem_st16_nowait(s_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
+        }
+        const float sum = sum0 + sum1;
+        l += sum;
+        tmem_st_wait();
+        if (cnt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+            for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * alpha);
+            tmem_st32(o_addr + c * 32, o);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
       }
-      const float sum = sum0 + sum1;
-      l += sum;
-      tmem_st_wait();
-      if (cnt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // epilogue: O / l -> bf16 -> out[b, q, h, :]; every item's o_done phase is observed
+      if (ok && !__all_sync(0xffffffffu, mbar_wait_or_abort(o_done, k & 1, abort_flag))) ok = false;
+      if (ok && cnt > 0) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint16_t* dst = p.out + ((static_cast<long long>(it.b) * p.T + q) * p.Hq + it.h) * D;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
+          if (valid) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c * 32, o);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-    }
-    // epilogue: O / l -> bf16 -> out[b, q, h, :]
-    if (ok && cnt > 0 && __all_sync(0xffffffffu, mbar_wait_or_abort(o_done, 0, abort_flag))) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* dst = p.out + ((static_cast<long long>(b) * p.T + q) * p.Hq + h) * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c * 32, o);
-        if (valid) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + c * 32 + 8 * u) = w;
+            for (int u = 0; u < 4; ++u) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + 8 * u) = w;
+            }
           }
         }
       }
+      // O is read: the issuer may let the next item's o_done phase complete
+      tc_fence_before();
+      mbar_arrive(epi_done);
+      ++k;
     }
   }
   tc_fence_before();

@@ -205,8 +205,8 @@ __device__ __noinline__ void sample_large_k(const SampleParams& p, const float* 
 }
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
-  pdl_launch_dependents();
   pdl_wait();  // logits come from the kernel ahead (programmatic dependent launch)
+  pdl_launch_dependents();
   __shared__ uint32_t hist[256];
   __shared__ float cand_v[kSampleMaxK];
   __shared__ int cand_i[kSampleMaxK];

@@ -116,8 +116,8 @@ __device__ __forceinline__ void scale_round(float (&v)[CPL][8], float r) {
 // 16-byte aligned.
 template <int CPL>
 __global__ void __launch_bounds__(128) add_rms_norm_kernel(const AddNormParams p) {
-  pdl_launch_dependents();
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -162,8 +162,8 @@ struct EmbedNormParams {
 // An id outside [0, V) records kErrTokenOutOfRange and writes zeros.
 template <int CPL>
 __global__ void __launch_bounds__(128) embed_rms_norm_kernel(const EmbedNormParams p) {
-  pdl_launch_dependents();
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -201,8 +201,8 @@ struct GatedActParams {
 
 // One thread per 8 elements (a 16-byte chunk); H a multiple of 8.
 __global__ void __launch_bounds__(256) gated_silu_kernel(const GatedActParams p) {
-  pdl_launch_dependents();
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
+  pdl_launch_dependents();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nchunk = p.H / 8;
   if (i >= static_cast<long long>(p.rows) * nchunk) return;
@@ -272,8 +272,8 @@ __device__ __forceinline__ void argmax_warp(float& best, int& bi) {
 // distributed shared memory.  The pick does not depend on the split: argmax_better is a total
 // order on (value, index).
 __global__ void __launch_bounds__(kSoftcapThreads) softcap_argmax_kernel(const SoftcapParams p) {
-  pdl_launch_dependents();
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
+  pdl_launch_dependents();
   const int row = blockIdx.x / p.cs;
   const int part = blockIdx.x % p.cs;
   const uint16_t* in = p.logits + static_cast<long long>(row) * p.ls;

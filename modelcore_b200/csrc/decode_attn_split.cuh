@@ -750,27 +750,35 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
   }
   __syncthreads();
 
-  for (int idx = threadIdx.x; idx < C::kRows * D; idx += kAttnThreads) {
-    const int n = idx / D;
-    const int d = idx - n * D;
+  // four consecutive head dimensions a thread: 16-byte shared-memory reads, and 16-byte stores
+  // to the owner rank (a quarter of the cluster-network transactions of scalar stores)
+  for (int idx = threadIdx.x; idx < C::kRows * (D / 4); idx += kAttnThreads) {
+    const int n = idx / (D / 4);
+    const int d = 4 * (idx - n * (D / 4));
     const int r = r0 + n;
     if (r >= r1) continue;
-    float o = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < kAttnConsumerWarps; ++w)
-      o = fmaf(merge[(w * C::kRows + n) * C::OPITCH + d], stat_f[w * C::kRows + n], o);
+    for (int w = 0; w < kAttnConsumerWarps; ++w) {
+      const float4 m4 = *reinterpret_cast<const float4*>(merge + (w * C::kRows + n) * C::OPITCH + d);
+      const float f = stat_f[w * C::kRows + n];
+      o.x = fmaf(m4.x, f, o.x);
+      o.y = fmaf(m4.y, f, o.y);
+      o.z = fmaf(m4.z, f, o.z);
+      o.w = fmaf(m4.w, f, o.w);
+    }
     const int t = r / p.G, h = kvh * p.G + r % p.G;
     const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;
     if (p.nsplit == 1) {
-      p.out[row * D + d] = float_to_bf16_bits(o);
+      *reinterpret_cast<uint2*>(p.out + row * D + d) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
     } else if (p.cluster) {
       if constexpr (C::PUSH)
-        st_dsmem_f32(map_to_rank(recv_o + (split * rpo + n / p.nsplit) * D + d,
-                                 static_cast<uint32_t>(n % p.nsplit)), o);
+        st_dsmem_f4(map_to_rank(recv_o + (split * rpo + n / p.nsplit) * D + d,
+                                static_cast<uint32_t>(n % p.nsplit)), o);
       else
-        reinterpret_cast<float*>(smem + C::CL_OFFSET)[n * D + d] = o;
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(smem + C::CL_OFFSET) + n * D + d) = o;
     } else {
-      p.part_o[(row * p.nsplit + split) * D + d] = o;
+      *reinterpret_cast<float4*>(p.part_o + (row * p.nsplit + split) * D + d) = o;
     }
   }
   if (!p.cluster) {
@@ -787,9 +795,9 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     cluster_sync();  // phase 2: every rank's stores are visible to their owners
     const int ns = p.nsplit;
     const int my_rows = (C::kRows - split + ns - 1) / ns;
-    for (int idx = threadIdx.x; idx < my_rows * D; idx += kAttnThreads) {
-      const int j = idx / D;
-      const int d = idx - j * D;
+    for (int idx = threadIdx.x; idx < my_rows * (D / 4); idx += kAttnThreads) {
+      const int j = idx / (D / 4);
+      const int d = 4 * (idx - j * (D / 4));  // four consecutive head dimensions a thread
       const int n = split + j * ns;
       const int r = r0 + n;
       float lq[kMaxClusterSplits];
@@ -806,13 +814,21 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
         wsum += lq[q];
       }
       const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-      float o = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int q = 0; q < kMaxClusterSplits; ++q)
-        if (q < ns) o = fmaf(lq[q] * inv, recv_o[(q * rpo + j) * D + d], o);
+        if (q < ns) {
+          const float wq = lq[q] * inv;
+          const float4 v = *reinterpret_cast<const float4*>(recv_o + (q * rpo + j) * D + d);
+          o.x = fmaf(wq, v.x, o.x);
+          o.y = fmaf(wq, v.y, o.y);
+          o.z = fmaf(wq, v.z, o.z);
+          o.w = fmaf(wq, v.w, o.w);
+        }
       if (r < r1) {
         const int t = r / p.G, h = kvh * p.G + r % p.G;
-        p.out[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d] = float_to_bf16_bits(o);
+        *reinterpret_cast<uint2*>(p.out + ((static_cast<long long>(b) * p.T + t) * p.Hq + h) * D + d) =
+            make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
       }
     }
     return;

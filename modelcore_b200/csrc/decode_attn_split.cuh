@@ -108,7 +108,7 @@ struct SplitAttnConfig {
   // barriers (full + empty per stage) then per-warp row statistics
   static constexpr int BAR_OFFSET = SCR_OFFSET + kAttnConsumerWarps * SCR_WARP;
   static constexpr int STAT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
-  static constexpr int STAT_BYTES = 3 * kAttnConsumerWarps * kRows * 4;
+  static constexpr int STAT_BYTES = 2 * kAttnConsumerWarps * kRows * 4;  // per-warp row max, sum
   static constexpr int CTL_OFFSET = STAT_OFFSET + STAT_BYTES;  // the "last arrival" flag
   // fused append: the CTA's query rows [kRows][D] and the new key and value [2][D], bf16
   static constexpr int FUSE_OFFSET = CTL_OFFSET + 16;
@@ -253,7 +253,6 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
   uint64_t* empty_bar = full_bar + STAGES;
   float* stat_m = reinterpret_cast<float*>(smem + C::STAT_OFFSET);
   float* stat_l = stat_m + kAttnConsumerWarps * C::kRows;
-  float* stat_f = stat_l + kAttnConsumerWarps * C::kRows;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -722,50 +721,51 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
   const int rpo = (C::kRows + p.nsplit - 1) / p.nsplit;  // rows a rank owns (row n: rank n % nsplit)
   if (C::PUSH && p.cluster) cluster_wait();  // phase 1 done: every rank's buffer may be written
 
-  // Per row: the CTA max, each warp's weight and the total.
-  if (threadIdx.x < C::kRows) {
-    const int n = threadIdx.x;
-    float mmax = -CUDART_INF_F;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) mmax = fmaxf(mmax, stat_m[w * C::kRows + n]);
-    float ltot = 0.f;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) {
-      const float mw = stat_m[w * C::kRows + n];
-      const float f = (mw == -CUDART_INF_F) ? 0.f : fast_exp2((mw - mmax) * p.scale_log2);
-      stat_f[w * C::kRows + n] = f;
-      ltot = fmaf(stat_l[w * C::kRows + n], f, ltot);
-    }
-    const float inv = ltot > 0.f ? 1.f / ltot : 0.f;
-    for (int w = 0; w < kAttnConsumerWarps; ++w) stat_f[w * C::kRows + n] *= inv;
-    const int r = r0 + n;
-    const float lse = (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
-    if (p.cluster) {
-      if constexpr (C::PUSH)
-        st_dsmem_f32(map_to_rank(recv_lse + split * rpo + n / p.nsplit, static_cast<uint32_t>(n % p.nsplit)), lse);
-      else
-        reinterpret_cast<float*>(smem + C::CL_OFFSET)[C::kRows * D + n] = lse;
-    } else if (p.nsplit > 1 && r < r1) {
-      const int t = r / p.G, h = kvh * p.G + r % p.G;
-      p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] = lse;
-    }
-  }
-  __syncthreads();
-
-  // four consecutive head dimensions a thread: 16-byte shared-memory reads, and 16-byte stores
-  // to the owner rank (a quarter of the cluster-network transactions of scalar stores)
+  // Every thread derives the weights of the row it combines itself (the row's CTA max, each
+  // warp's weight and the total, in the same operations and order for every thread of the row):
+  // no serial statistics phase and no barrier before the combine.  The thread that takes a
+  // row's first four columns also publishes the row's log2-sum-exp.
+  // Four consecutive head dimensions a thread: 16-byte shared-memory reads, and 16-byte stores to
+  // the owner rank (a quarter of the cluster-network transactions of scalar stores).
   for (int idx = threadIdx.x; idx < C::kRows * (D / 4); idx += kAttnThreads) {
     const int n = idx / (D / 4);
     const int d = 4 * (idx - n * (D / 4));
     const int r = r0 + n;
+    float mmax = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w) mmax = fmaxf(mmax, stat_m[w * C::kRows + n]);
+    float fw[kAttnConsumerWarps];
+    float ltot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w) {
+      const float mw = stat_m[w * C::kRows + n];
+      fw[w] = (mw == -CUDART_INF_F) ? 0.f : fast_exp2((mw - mmax) * p.scale_log2);
+      ltot = fmaf(stat_l[w * C::kRows + n], fw[w], ltot);
+    }
+    const float inv = ltot > 0.f ? 1.f / ltot : 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w) fw[w] *= inv;
+    if (d == 0 && p.nsplit > 1) {
+      const float lse = (ltot > 0.f) ? mmax * p.scale_log2 + __log2f(ltot) : -CUDART_INF_F;
+      if (p.cluster) {
+        if constexpr (C::PUSH)
+          st_dsmem_f32(map_to_rank(recv_lse + split * rpo + n / p.nsplit, static_cast<uint32_t>(n % p.nsplit)), lse);
+        else
+          reinterpret_cast<float*>(smem + C::CL_OFFSET)[C::kRows * D + n] = lse;
+      } else if (r < r1) {
+        const int t = r / p.G, h = kvh * p.G + r % p.G;
+        p.part_lse[((static_cast<long long>(b) * p.T + t) * p.Hq + h) * p.nsplit + split] = lse;
+      }
+    }
     if (r >= r1) continue;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < kAttnConsumerWarps; ++w) {
       const float4 m4 = *reinterpret_cast<const float4*>(merge + (w * C::kRows + n) * C::OPITCH + d);
-      const float f = stat_f[w * C::kRows + n];
-      o.x = fmaf(m4.x, f, o.x);
-      o.y = fmaf(m4.y, f, o.y);
-      o.z = fmaf(m4.z, f, o.z);
-      o.w = fmaf(m4.w, f, o.w);
+      o.x = fmaf(m4.x, fw[w], o.x);
+      o.y = fmaf(m4.y, fw[w], o.y);
+      o.z = fmaf(m4.z, fw[w], o.z);
+      o.w = fmaf(m4.w, fw[w], o.w);
     }
     const int t = r / p.G, h = kvh * p.G + r % p.G;
     const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;

@@ -143,6 +143,11 @@ int mcb_kv_advance(int32_t* cache_seqlens, int32_t B, int32_t n, void* stream);
  *    fixed costs do not pay off, and for long rows of at most 128 row groups (2-16 splits).
  *  - prefill (num_ctas == 0, T >= 64, D 64 or 128): 128-query x 128-key tiles on the tcgen05
  *    tensor cores with TMEM accumulators (mcb_prefill_attn below); no workspace or counters.
+ * The split plan is launched with programmatic stream serialization and reads cache_seqlens and
+ * the keys and values below each row's cache_seqlens before it waits for the kernel ahead of it in
+ * the stream: that one kernel must not write them (every kernel before it has completed when
+ * this one starts, since the library's kernels let their successor start only after their own
+ * wait).  The new tokens' positions are read after the wait.
  * ------------------------------------------------------------------------------------------- */
 typedef struct {
   const void* q;              /* (B,T,Hq,D) bf16                                            */

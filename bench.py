@@ -795,7 +795,8 @@ def run_b200(args):
     _ensure_modelcore()
     import modelcore_b200
     from modelcore_b200 import step as _step
-    _step.USE_FUSED_PROJ = args.linear == "mcb"
+    _step.USE_FUSED_PROJ = args.linear == "fused"
+    _step.USE_LINEAR_PROJ = args.linear == "mcb"
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
     steps_needed = 1 + args.warmup + max(args.steps, args.e2e_steps or 0) + 2
@@ -908,7 +909,10 @@ def run_b200(args):
                                  "on libmcb200",
                         "plain": "modelcore's op-by-op forward around the libmcb200 append and "
                                  "attention"}[args.step],
-        "projections": {"mcb": "libmcb200 mcb_linear", "cublas": "torch F.linear (cuBLAS)"}[args.linear],
+        "projections": {"mcb": "q|k|v and c_proj (+ residual) on libmcb200 mcb_linear, gate|up and "
+                               "down_proj on cuBLAS",
+                        "fused": "libmcb200 mcb_linear with the norms and adds fused in, down_proj on cuBLAS",
+                        "cublas": "torch F.linear (cuBLAS)"}[args.linear],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
                     "step_gbs": round(kv_bytes_step / (ms / args.steps * 1e-3) / 1e9, 1),
                     "attention_kernel_gbs": round(roof["achieved_gbs"], 1),
@@ -947,9 +951,10 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--step", choices=("fused", "plain"), default="fused",
                     help="decode step around attention: fused (default) or modelcore's op-by-op")
-    ap.add_argument("--linear", choices=("mcb", "cublas"), default="cublas",
-                    help="decode projections: cuBLAS with the add + norm as a libmcb200 kernel "
-                         "(default), or libmcb200's mcb_linear with the norms and adds fused in")
+    ap.add_argument("--linear", choices=("mcb", "cublas", "fused"), default="mcb",
+                    help="decode projections: q|k|v and c_proj (+ residual) on libmcb200's "
+                         "mcb_linear, the MLP on cuBLAS (default); all on cuBLAS; or mcb_linear "
+                         "with the norms and adds fused in")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")

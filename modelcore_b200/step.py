@@ -18,7 +18,10 @@ arithmetic as
                 a = silu(gu[:, :H]) * gu[:, H:]    one libmcb200 kernel (mcb_gated_silu)
                 x, h = x + down(a), norm(x + ...)  one libmcb200 kernel; h feeds the next block
 
-9 launches a layer.  The residual stream lives in one buffer updated in place.
+9 launches a layer.  The residual stream lives in one buffer updated in place.  At most 64 rows
+of a decode step, q|k|v and c_proj run on libmcb200's mcb_linear instead of cuBLAS, c_proj with
+the residual add in its epilogue (USE_LINEAR_PROJ, body_forward_linear): projection, attention and
+c_proj then overlap under programmatic dependent launch.
 
 Numerics: each op rounds to bf16 where the reference's does; the add and silu * up are bit-exact
 against torch's CUDA ops; the norm's fp32 sum order (the kernel's own, restated by the oracle)
@@ -102,6 +105,16 @@ def packed_weight(owner, key, linears):
 # rows' reductions share one CTA -- against 2.6 us for the stand-alone kernel (config 2: 87k vs
 # 100k tokens/s).
 USE_FUSED_PROJ = False
+
+# With USE_LINEAR_PROJ (the default) a decode step of at most 64 rows runs its q|k|v and c_proj
+# projections on mcb_linear, c_proj with the residual add in its epilogue, launched with
+# programmatic dependent launch: projection, attention and c_proj then form one chain in which
+# each kernel's weight slice -- or, for the attention, the keys of earlier steps -- streams in
+# while the kernel ahead finishes, which a cuBLAS launch cannot join.  gate|up and down_proj stay
+# on cuBLAS (gate|up is slower on mcb_linear, 5.15 vs 4.40 us; down_proj's K, the MLP width, does
+# not fit its shared memory).  Measured on config 2 (64 rows, graph replay): 0.598 vs
+# 0.616 ms/step, the same greedy stream; c_proj alone on mcb_linear was slower (0.631).
+USE_LINEAR_PROJ = True
 
 
 def qkv_projection(attn, x):
@@ -197,6 +210,67 @@ def _proj_ok(body, rows, x):
     return True
 
 
+def _linear_ok(body, rows, T, x):
+    """body_forward_linear applies: a decode step (one new token a row; a prompt's forward keeps
+    cuBLAS, so the cache a prefill writes does not depend on how many prompts share the forward)
+    of at most 64 rows, every block's attention on the fused append
+    (modelcore's RMSNorm QK-norm and RotaryEmbedding, bf16 weights), n_embd and the attention
+    width multiples of 64 and at most 1,024 (mcb_linear holds the rows' K columns in shared
+    memory)."""
+    from .integration import _fusable
+    C = x.size(-1)
+    if not USE_LINEAR_PROJ or T != 1 or not 0 < rows <= ops.LINEAR_MAX_ROWS or C % 64 or C > 1024:
+        return False
+    for b in body.blocks:
+        a = b.mixer
+        nq = a.n_head * a.head_dim
+        if not _fusable(a, x) or nq % 64 or nq > 1024 or a.c_q.weight.dtype != x.dtype:
+            return False
+    return True
+
+
+def body_forward_linear(body, x2, h, kv_cache, B, T):
+    """body_forward with q|k|v and c_proj on mcb_linear (USE_LINEAR_PROJ):
+
+        per block:  qkv = h @ [Wq; Wk; Wv]^T          mcb_linear (c_q alone for a layer that
+                                                      reads another layer's slot)
+                    append + attention                 (integration.attend)
+                    x = x + attn @ Wo^T                mcb_linear, the add in its epilogue
+                    h = norm(x)                        mcb_add_rms_norm
+                    gu = h @ [Wg; Wu]^T                cuBLAS
+                    a = silu(gu[:, :H]) * gu[:, H:]    mcb_gated_silu
+                    x, h = x + a @ Wd^T, norm(...)     cuBLAS, then mcb_add_rms_norm
+
+    The adds and the norms round as body_forward's; the two projections differ from cuBLAS's in
+    fp32 summation order only.  Returns the final residual (a new buffer) and its norm h."""
+    from .integration import attend
+    rows, C = x2.shape
+    resid = torch.empty_like(x2)
+    src = x2
+    for block in body.blocks:
+        attn, ffn, eps = block.mixer, block.ffn, block.norm.eps
+        hd = attn.head_dim
+        nq = attn.n_head * hd
+        if attn.produces_kv:
+            w = packed_weight(attn, "qkv", (attn.c_q, attn.c_k, attn.c_v))
+        else:
+            w = attn.c_q.weight
+        qkv = ops.linear(h, w, pdl=True)
+        q = qkv[:, :nq].view(B, T, attn.n_head, hd)
+        k = v = None
+        if attn.produces_kv:
+            nk = attn.n_kv_head * hd
+            k = qkv[:, nq:nq + nk].view(B, T, attn.n_kv_head, hd)
+            v = qkv[:, nq + nk:].view(B, T, attn.n_kv_head, hd)
+        y = attend(attn, q, k, v, kv_cache)
+        ops.linear(y.reshape(rows, nq), attn.c_proj.weight, out=resid, res=src, pdl=True)
+        src = resid
+        ops.add_rms_norm(resid, eps=eps, h_out=h)
+        f = gated_mlp(ffn, h)
+        ops.add_rms_norm(resid, f, eps=eps, x_out=resid, h_out=h)
+    return resid, h
+
+
 def body_forward_proj(body, x2, kv_cache, B, T, inplace=False, want_h=True):
     """body_forward for a decode step's few rows with the projections around attention on
     mcb_linear:
@@ -269,7 +343,10 @@ def stack_forward(self, x, idx, kv_cache, doc_args=None):
         return body_forward_proj(self, x2, kv_cache, B, T, want_h=False)[0].view(B, T, C)
     h = torch.empty_like(x2)
     ops.add_rms_norm(x2, eps=self.blocks[0].norm.eps, h_out=h)
-    resid, _ = body_forward(self, x2, h, idx, kv_cache, B, T)
+    if _linear_ok(self, B * T, T, x):
+        resid, _ = body_forward_linear(self, x2, h, kv_cache, B, T)
+    else:
+        resid, _ = body_forward(self, x2, h, idx, kv_cache, B, T)
     return resid.view(B, T, C)
 
 
@@ -311,7 +388,10 @@ def _hidden(model, idx, kv_cache):
         _, h = body_forward_proj(model.body, x.view(B * T, C), kv_cache, B, T, inplace=True)
     else:
         x, h = ops.embed_rms_norm(idx, emb.wte.weight, eps=emb.norm.eps)
-        _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
+        if _linear_ok(model.body, B * T, T, probe):
+            _, h = body_forward_linear(model.body, x.view(B * T, C), h.view(B * T, C), kv_cache, B, T)
+        else:
+            _, h = body_forward(model.body, x.view(B * T, C), h.view(B * T, C), idx, kv_cache, B, T)
     kv_cache.advance(T)
     return h
 

@@ -289,15 +289,27 @@ def test_fused_step_decode_is_as_accurate_as_the_reference(env, name):
     assert e_fused <= 1.25 * e_ref + 1e-3
 
 
-@pytest.mark.parametrize("fused_proj", [False, True])
-def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
+PROJ_MODES = ["cublas", "linear", "fused_proj"]
+
+
+def _set_proj_mode(step, monkeypatch, mode):
+    """cublas: every projection on cuBLAS; linear: q|k|v and c_proj (+ residual) on mcb_linear
+    (USE_LINEAR_PROJ, the default); fused_proj: the projections on mcb_linear with the norms and
+    adds fused into them (USE_FUSED_PROJ)."""
+    monkeypatch.setattr(step, "USE_FUSED_PROJ", mode == "fused_proj")
+    monkeypatch.setattr(step, "USE_LINEAR_PROJ", mode == "linear")
+
+
+@pytest.mark.parametrize("mode", PROJ_MODES)
+def test_fused_step_launches_and_graph_replay(env, mode, monkeypatch):
     """One decode step of the fused 4-layer quickstart launches the libmcb200 kernels it should
-    (per layer: the three fused projections, c_proj, append, attention; plus the embedding, the
-    last add + norm, the advance and the LM-head epilogue),
+    (per layer: the projections it runs, the add + norms, silu * up, append, attention; plus the
+    embedding, the last add + norm, the advance and the LM-head epilogue),
     and the CUDA-graph decoder reproduces the eager fused decoder bit for bit."""
     modelcore, mcb = env
     from modelcore_b200 import integration, ops, step, workloads
-    monkeypatch.setattr(step, "USE_FUSED_PROJ", fused_proj)
+    _set_proj_mode(step, monkeypatch, mode)
+    fused_proj = mode == "fused_proj"
     mgr = mcb.ModelManager()
     model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
                                               device=torch.device("cuda"), seed=0))
@@ -319,6 +331,10 @@ def test_fused_step_launches_and_graph_replay(env, fused_proj, monkeypatch):
             # gate|up (norm inside), silu * up (down_proj is cuBLAS); the final add + norm, the
             # advance, the LM-head epilogue
             attn_launches = per_step - (1 + 4 * (4 + append) + 1 + 1 + 1)
+        elif mode == "linear":
+            # embedding + first norm, per layer q|k|v, c_proj (+ residual), the norm, silu * up,
+            # the add + norm and the append, the advance, the LM-head epilogue
+            attn_launches = per_step - (1 + 4 * (5 + append) + 1 + 1)
         else:
             # embedding + first norm, per layer two add + norms, silu * up and the append, the
             # advance, the LM-head epilogue
@@ -401,14 +417,15 @@ def copy_with_plain_forward(env, model):
         return mcb.ModelManager().new_decoder(other, prompts, max_tokens=4).step([5, 6]).float().clone()
 
 
-@pytest.mark.parametrize("fused_proj", [False, True])
-def test_fused_step_projection_paths_are_as_accurate(env, fused_proj, monkeypatch):
-    """The same bar with the decode projections on libmcb200's tcgen05 kernel with the norms and
-    residual adds fused into them (USE_FUSED_PROJ, body_forward_proj), and on cuBLAS with the
-    norms and adds as their own kernels."""
+@pytest.mark.parametrize("mode", PROJ_MODES)
+def test_fused_step_projection_paths_are_as_accurate(env, mode, monkeypatch):
+    """The same bar with every decode projection on cuBLAS, with q|k|v and c_proj (+ residual)
+    on libmcb200's mcb_linear (USE_LINEAR_PROJ, body_forward_linear), and with the projections on
+    mcb_linear with the norms and residual adds fused into them (USE_FUSED_PROJ,
+    body_forward_proj)."""
     from modelcore.tests.test_generate import RAGGED_PROMPTS
     from modelcore_b200 import step
-    monkeypatch.setattr(step, "USE_FUSED_PROJ", fused_proj)
+    _set_proj_mode(step, monkeypatch, mode)
     (rm, ref), (fm, fused), _, (m32, ref32) = _models(env, _configs()["quickstart"]())
     cols = torch.tensor([[(s * 7 + i * 3) % 100 + 1 for s in range(8)]
                          for i in range(len(RAGGED_PROMPTS))])

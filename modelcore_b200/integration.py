@@ -290,7 +290,10 @@ class GraphDecoder:
         self._static_logits = None
         self._rt_graph = None
         self._next = torch.zeros((B, 1), dtype=torch.long, device=dev)
-        self._next_host = torch.zeros((B, 1), dtype=torch.long).pin_memory()
+        # step_greedy's tokens go out through the same pinned buffer its column comes in by: a
+        # caller that feeds the returned tokens straight back (a greedy loop) needs no host copy
+        self._next_host = self._ids_host
+        self._next_view = self._ids_host.view(-1)
         self._rt_done = torch.cuda.Event()
         # recorded after each step()'s copy out of _ids_host: the next step() waits on it before
         # overwriting that pinned buffer (the copy reads it when the stream reaches it, not when
@@ -451,14 +454,18 @@ class GraphDecoder:
         temperature 0, modelcore/generate.py:23-24): returns the (B,) next tokens as a host int64
         tensor (a view of pinned memory, valid until the next call).  The host-to-device copy of
         the column, the decode forward with the pick fused into the LM-head epilogue and the
-        device-to-host copy of the tokens replay as one CUDA graph."""
+        device-to-host copy of the tokens replay as one CUDA graph.  The tokens come back in the
+        pinned buffer the next column goes in by: passing the returned tensor itself as the next
+        column skips the host copy."""
         self._room(1)
-        self._ids_host.copy_(torch.as_tensor(token_column, dtype=torch.long).view(-1, 1))
+        if token_column is not self._next_view:
+            self._h2d_done.synchronize()  # a step() may still be copying out of the buffer
+            self._ids_host.copy_(torch.as_tensor(token_column, dtype=torch.long).view(-1, 1))
         if self._rt_graph is None and self._eager_steps == 0:
             self._ids.copy_(self._ids_host, non_blocking=True)
             self._logits = self._eager(self._ids.clone())
             self._next_host.copy_(torch.argmax(self._logits, dim=-1, keepdim=True).cpu())
-            return self._next_host.view(-1)
+            return self._next_view
         if self._rt_graph is None:
             self._rt_graph, self._rt_logits = self._capture_roundtrip()
         self._rt_graph.replay()
@@ -466,7 +473,7 @@ class GraphDecoder:
         self._rt_done.record()
         self._rt_done.synchronize()
         self._logits = self._rt_logits
-        return self._next_host.view(-1)
+        return self._next_view
 
     def _eager(self, ids):
         logits = self.model.forward(ids, kv_cache=self.kv_cache)[:, -1, :]

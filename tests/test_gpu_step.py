@@ -365,6 +365,20 @@ def test_fused_step_launches_and_graph_replay(env, mode, monkeypatch):
             assert torch.equal(nxt, want)
             assert torch.equal(g3.logits, e3.logits)
             tok = nxt
+        # the returned tensor fed straight back as the next column (no host copy: the tokens
+        # come back in the buffer the column goes in by) gives the same stream
+        g4 = mgr.new_decoder(model, prompts, max_tokens=16, cuda_graph=True)
+        e4 = mgr.new_decoder(model, prompts, max_tokens=16)
+        tok = torch.argmax(e4.logits, dim=-1).cpu()
+        out = g4.step_greedy(tok)
+        for _ in range(8):
+            want = torch.argmax(e4.step(tok.tolist()), dim=-1).cpu()
+            assert torch.equal(out, want)
+            assert torch.equal(g4.logits, e4.logits)
+            tok = want
+            again = g4.step_greedy(out)
+            assert again is out  # the same pinned view, now holding the next tokens
+            out = again
 
 
 def test_packed_weights_follow_the_parameters(env):

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 7
+#define MCB_ABI_VERSION 8
 
 typedef enum {
   MCB_OK = 0,
@@ -354,6 +354,11 @@ int mcb_sample(const mcb_sample_args* args, void* stream);
  *                             (the residual add of the previous block's MLP; K <= 768);
  *   res != NULL               Y = bf16(res + bf16(X W^T)): the residual add after c_proj
  *                             (modelcore/components/block.py:58); res may be Y (in place).
+ *   flags & MCB_LINEAR_GATED  W is the packed [Wg; Wu] of 2N rows and Y (R, N) =
+ *                             bf16(bf16(silu(bf16(X Wg^T))) * bf16(X Wu^T)): GatedMLP's gate|up
+ *                             projection with act(gate) * up for act "silu"
+ *                             (modelcore/components/mlp.py:89-90) -- the bits of mcb_gated_silu
+ *                             over the plain projection; no norm, delta or res; N % 16 == 0.
  * X, delta, x_out (R, K), W (N, K) as nn.Linear stores it, Y and res (R, N), bf16, fp32
  * accumulation.  R <= 64, K a multiple of 64, x / delta / x_out / w rows 16-byte aligned; Y, res
  * and x_out must not overlap X or delta.  Every CTA takes 16 or 32 output features and all of K:
@@ -362,6 +367,7 @@ int mcb_sample(const mcb_sample_args* args, void* stream);
  * serialization: the W slice is requested while the previous kernel in the stream finishes; the
  * activations are read only after that kernel completed. */
 #define MCB_LINEAR_NORM 1
+#define MCB_LINEAR_GATED 2
 
 typedef struct {
   const void* x;              /* (R, K) bf16                                                */
@@ -372,7 +378,7 @@ typedef struct {
   void* x_out;                /* (R, K) bf16: x + delta (with delta)                        */
   int64_t x_stride, w_stride, y_stride, res_stride, delta_stride, x_out_stride;  /* elements */
   int32_t R, N, K;
-  int32_t flags;              /* MCB_LINEAR_NORM                                            */
+  int32_t flags;              /* MCB_LINEAR_NORM or MCB_LINEAR_GATED                        */
   float eps;                  /* the norm's eps                                             */
   int32_t pdl;
 } mcb_linear_args;

@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -169,6 +169,7 @@ class SampleArgs(ctypes.Structure):
 
 
 LINEAR_NORM = 1
+LINEAR_GATED = 2
 
 
 class LinearArgs(ctypes.Structure):

@@ -9,6 +9,13 @@
 //                                               of the previous block's MLP, then the norm)
 //   residual:    Y = bf16(res + bf16(X W^T))   (the residual add after c_proj, block.py:58; res
 //                                               may be Y itself: in place)
+//   gated:       Y = silu(X Wg^T) * (X Wu^T)   (GatedMLP's gate|up projection and act(gate) * up,
+//                                               modelcore/components/mlp.py:89-90, with W the
+//                                               packed [Wg; Wu]: each CTA takes F/2 gate rows
+//                                               and the matching F/2 up rows, and its epilogue
+//                                               rounds both sums to bf16 and applies
+//                                               silu_mul_bf16 -- the bits of mcb_gated_silu over
+//                                               the plain projection)
 //
 // At decode a projection multiplies R <= 64 rows (one token per sequence) by an N x K weight: the
 // work is streaming W from HBM once; the activation block (64 x K bf16, about 100 KB) sits in L2.
@@ -81,17 +88,19 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int F, bool NORM, bool ADD>
+template <int F, bool NORM, bool ADD, bool GATED = false>
 __global__ void __launch_bounds__(kProjThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap dmap, const ProjParams p) {
   static_assert(!ADD || NORM, "the add is fused only in front of the norm");
-  constexpr int NT = F / 8;  // n-tiles of 8 features
+  static_assert(!GATED || (!NORM && F % 16 == 0), "the gated epilogue stands alone, F/2 a multiple of 8");
+  constexpr int NT = F / 8;  // n-tiles of 8 features (of the W slice)
+  constexpr int FO = GATED ? F / 2 : F;  // output features a CTA
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int panels = p.panels;
-  const int n0 = static_cast<int>(blockIdx.x) * F;
+  const int n0 = static_cast<int>(blockIdx.x) * FO;
   uint8_t* wsm = smem;
   uint8_t* xsm = smem + proj_x_offset(F, panels);
   uint8_t* dsm = xsm + proj_x_bytes(F, panels);
@@ -110,7 +119,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     if (ADD) prefetch_tensormap(&dmap);
     const uint64_t pol = l2_policy_evict_first();
     mbar_arrive_expect_tx(w_full, static_cast<uint32_t>(panels * F * 128));
-    for (int i = 0; i < panels; ++i) tma_load_4d(wsm + i * F * 128, &wmap, w_full, i * 64, n0, 0, 0, pol);
+    for (int i = 0; i < panels; ++i) {
+      // gated: the gate rows n0 .. n0 + F/2 - 1, then the up rows N + n0 .. (boxes of F/2 rows;
+      // the second starts at a 1024-byte boundary of the panel, so the swizzle phase holds)
+      tma_load_4d(wsm + i * F * 128, &wmap, w_full, i * 64, n0, 0, 0, pol);
+      if (GATED) tma_load_4d(wsm + i * F * 128 + FO * 128, &wmap, w_full, i * 64, p.N + n0, 0, 0, pol);
+    }
   }
   __syncthreads();  // barriers initialised
   pdl_wait();       // the activations and the residual come from the kernels ahead
@@ -243,10 +257,10 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   __syncthreads();
   const bool have = !*abort_flag;
   // ---------------- epilogue: 8 features a thread, warps summed in order ----------------
-  for (int it = threadIdx.x; have && it < kProjRows * (F / 8); it += kProjThreads) {
-    const int row = it / (F / 8), f8 = (it % (F / 8)) * 8;
+  for (int it = threadIdx.x; have && it < kProjRows * (FO / 8); it += kProjThreads) {
+    const int row = it / (FO / 8), f8 = (it % (FO / 8)) * 8;
     if (row >= p.R) continue;
-    float o[8];
+    float o[8], ou[8];  // ou: the matching up features (gated)
 #pragma unroll
     for (int w = 0; w < kProjWarps; ++w) {
       const uint32_t ra = smem_u32(red + (w * kProjRows + row) * F + f8);
@@ -255,9 +269,21 @@ __global__ void __launch_bounds__(kProjThreads, 1)
                           __uint_as_float(hi.x), __uint_as_float(hi.y), __uint_as_float(hi.z), __uint_as_float(hi.w)};
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = w == 0 ? t[i] : __fadd_rn(o[i], t[i]);
+      if constexpr (GATED) {
+        const uint4 ulo = lds128(ra + FO * 4), uhi = lds128(ra + FO * 4 + 16);
+        const float tu[8] = {__uint_as_float(ulo.x), __uint_as_float(ulo.y), __uint_as_float(ulo.z),
+                             __uint_as_float(ulo.w), __uint_as_float(uhi.x), __uint_as_float(uhi.y),
+                             __uint_as_float(uhi.z), __uint_as_float(uhi.w)};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ou[i] = w == 0 ? tu[i] : __fadd_rn(ou[i], tu[i]);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = round_bf16(o[i]);
+    if constexpr (GATED) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = silu_mul_bf16(o[i], round_bf16(ou[i]));
+    }
     uint16_t* yr = p.y + static_cast<long long>(row) * p.ys + n0 + f8;
     const uint16_t* rr = p.res ? p.res + static_cast<long long>(row) * p.ress + n0 + f8 : nullptr;
     if (p.vec_out && n0 + f8 + 8 <= p.N) {

@@ -856,15 +856,16 @@ int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long lon
 
 constexpr int kMaxSmemOptin = 232448;
 
-template <int F, bool NORM, bool ADD>
+template <int F, bool NORM, bool ADD, bool GATED = false>
 int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& dm, const mcb::ProjParams& prm,
                 bool pdl, cudaStream_t st) {
   static std::atomic<uint64_t> done{0};
-  auto kernel = mcb::proj_kernel<F, NORM, ADD>;
+  auto kernel = mcb::proj_kernel<F, NORM, ADD, GATED>;
   cudaError_t e = ensure_smem(kernel, kMaxSmemOptin, done);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>((prm.N + F - 1) / F));
+  constexpr int FO = GATED ? F / 2 : F;  // output features a CTA
+  cfg.gridDim = dim3(static_cast<unsigned>((prm.N + FO - 1) / FO));
   cfg.blockDim = dim3(mcb::kProjThreads);
   cfg.dynamicSmemBytes = mcb::proj_smem_bytes(F, prm.panels, ADD);
   cfg.stream = st;
@@ -1242,10 +1243,16 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: args is NULL");
   if (a->R < 0 || a->N <= 0 || a->K <= 0)
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: R=%d N=%d K=%d", a->R, a->N, a->K);
-  if (a->flags & ~MCB_LINEAR_NORM) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: flags %d", a->flags);
+  if (a->flags & ~(MCB_LINEAR_NORM | MCB_LINEAR_GATED))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: flags %d", a->flags);
   const bool norm = (a->flags & MCB_LINEAR_NORM) != 0;
+  const bool gated = (a->flags & MCB_LINEAR_GATED) != 0;
   const bool add = a->delta != nullptr;
   if (add && !norm) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: delta needs MCB_LINEAR_NORM");
+  if (gated && (norm || add || a->res != nullptr))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: MCB_LINEAR_GATED takes no norm, delta or res");
+  if (gated && a->N % 16 != 0)
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: gated N=%d must be a multiple of 16", a->N);
   if (a->R > mcb::kProjRows || a->K % 64 != 0 || (norm && a->K > 32 * 8 * mcb::kProjNormCpl))
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most %d), K=%d (a multiple of 64%s)", a->R,
                 mcb::kProjRows, a->K, norm ? ", at most 1024 with the norm" : "");
@@ -1273,13 +1280,15 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   const int panels = a->K / 64;
   // the narrower feature slice while it keeps the grid within about one CTA per SM (always with
   // delta: its panels leave no room for a wider weight slice)
-  const int F = add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32;
+  // gated: 16 gate and 16 up rows of W a CTA (the epilogue pairs them)
+  const int F = gated ? 32 : (add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32);
   if (mcb::proj_smem_bytes(F, panels, add) > kMaxSmemOptin)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d does not fit the shared memory (%d features a CTA%s)",
                 a->K, F, add ? ", with delta" : "");
   if (a->R == 0) return MCB_OK;
   CUtensorMap wm, xm, dm;
-  int rc = encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, F);
+  int rc = gated ? encode_rows_map(&wm, a->w, 2ll * a->N, a->K, a->w_stride, F / 2)
+                 : encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, F);
   if (rc != MCB_OK) return rc;
   rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, mcb::kProjRows);
   if (rc != MCB_OK) return rc;
@@ -1305,6 +1314,7 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   p.eps = a->eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
+  if (gated) return launch_proj<32, false, false, true>(wm, xm, dm, p, pdl, st);
   return F == 16 ? launch_proj_f<16>(norm, add, wm, xm, dm, p, pdl, st)
                  : launch_proj_f<32>(norm, add, wm, xm, dm, p, pdl, st);
 }

@@ -199,6 +199,14 @@ struct GatedActParams {
   int rows, H;
 };
 
+// bf16(bf16(silu(g)) * u) for bf16 values g and u held as floats: silu in fp32 as
+// g / (1 + exp(-g)), rounded to bf16, then the product rounded -- torch's F.silu(g) * u on bf16
+// tensors.  Shared by gated_silu_kernel and the gated projection (decode_proj.cuh).
+__device__ __forceinline__ float silu_mul_bf16(float g, float u) {
+  const float s = round_bf16(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
+  return round_bf16(__fmul_rn(s, u));
+}
+
 // One thread per 8 elements (a 16-byte chunk); H a multiple of 8.
 __global__ void __launch_bounds__(256) gated_silu_kernel(const GatedActParams p) {
   pdl_wait();  // inputs come from the kernel ahead (programmatic dependent launch)
@@ -216,13 +224,7 @@ __global__ void __launch_bounds__(256) gated_silu_kernel(const GatedActParams p)
   for (int k = 0; k < 4; ++k) {
     float g[2] = {__uint_as_float(gw[k] << 16), __uint_as_float(gw[k] & 0xffff0000u)};
     float u[2] = {__uint_as_float(uw[k] << 16), __uint_as_float(uw[k] & 0xffff0000u)};
-    float o[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float s = round_bf16(__fdiv_rn(g[e], __fadd_rn(1.f, expf(-g[e]))));
-      o[e] = __fmul_rn(s, u[e]);
-    }
-    ow[k] = pack_bf16x2(o[0], o[1]);
+    ow[k] = pack_bf16x2(silu_mul_bf16(g[0], u[0]), silu_mul_bf16(g[1], u[1]));
   }
   *reinterpret_cast<uint4*>(p.out + row * p.os + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }

@@ -13,7 +13,7 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      LINEAR_NORM, LinearArgs, SampleArgs, SoftcapArgs, check)
+                      LINEAR_GATED, LINEAR_NORM, LinearArgs, SampleArgs, SoftcapArgs, check)
 
 
 def _stream(t):
@@ -569,7 +569,7 @@ LINEAR_MAX_ROWS = 64
 
 
 def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None, eps=None,
-           pdl=False):
+           pdl=False, gated=False):
     """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
     rows -- x (R, K) with R <= 64 and K a multiple of 64, weight (N, K), bf16, fp32 accumulation
     -- with the Block's elementwise ops around it fused in:
@@ -579,12 +579,19 @@ def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None,
       delta       (with norm) x' = x + delta is written to x_out (allocated when None) and
                   normed: the residual add of the previous block's MLP, K <= 768;
       res         res + (x @ weight^T), each rounded to bf16 (the residual add after c_proj,
-                  modelcore/components/block.py:58); out may be res (in place).
+                  modelcore/components/block.py:58); out may be res (in place);
+      gated=True  weight is the packed [Wg; Wu] (2H, K) and out (R, H) = silu(x @ Wg^T) *
+                  (x @ Wu^T) with mcb_gated_silu's rounding (GatedMLP, modelcore/components/
+                  mlp.py:89-90); H a multiple of 16, no norm, delta or res.
 
     pdl: launch with programmatic stream serialization (the weight slice streams in while the
     previous kernel finishes).  Returns out (R, N), or (x_out, out) with delta."""
     R, K = x.shape
     N = weight.shape[0]
+    if gated:
+        if N % 2 or norm or delta is not None or res is not None:
+            raise RuntimeError("gated: weight must be [Wg; Wu] (2H rows); no norm, delta or res")
+        N //= 2
     if weight.shape[1] != K:
         raise RuntimeError(f"weight must be (N, {K}), got {tuple(weight.shape)}")
     if out is None:
@@ -605,7 +612,7 @@ def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None,
         args.delta, args.delta_stride = delta.data_ptr(), _rows2d("delta", delta)
         args.x_out, args.x_out_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
     args.R, args.N, args.K = R, N, K
-    args.flags = LINEAR_NORM if norm else 0
+    args.flags = (LINEAR_NORM if norm else 0) | (LINEAR_GATED if gated else 0)
     args.eps = rms_norm_eps(eps)
     args.pdl = int(bool(pdl))
     check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))

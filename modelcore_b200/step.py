@@ -115,6 +115,9 @@ USE_FUSED_PROJ = False
 # not fit its shared memory).  Measured on config 2 (64 rows, graph replay): 0.598 vs
 # 0.616 ms/step, the same greedy stream; c_proj alone on mcb_linear was slower (0.631).
 USE_LINEAR_PROJ = True
+# ... and, on that path, gate|up with silu(gate) * up in its epilogue on mcb_linear (one launch
+# for two) unless USE_LINEAR_MLP is False
+USE_LINEAR_MLP = True
 
 
 def qkv_projection(attn, x):
@@ -134,13 +137,19 @@ def qkv_projection(attn, x):
     return q, k, v
 
 
-def gated_mlp(ffn, h):
+def gated_mlp(ffn, h, linear=False):
     """GatedMLP.forward (modelcore/components/mlp.py:89-90) for activation "silu" on (rows, C):
-    one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj."""
+    one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj; with linear (a decode step's few rows,
+    hidden width a multiple of 16) the first two as one mcb_linear launch whose epilogue applies
+    silu(gate) * up, launched with programmatic dependent launch."""
     w = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
-    gu = F.linear(h, w)
     H = ffn.hidden_dim
-    return F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
+    if linear and H % 16 == 0:
+        a = ops.linear(h, w, gated=True, pdl=True)
+    else:
+        gu = F.linear(h, w)
+        a = ops.gated_silu(gu[:, :H], gu[:, H:])
+    return F.linear(a, ffn.down_proj.weight)
 
 
 def _structure_ok(body):
@@ -266,7 +275,7 @@ def body_forward_linear(body, x2, h, kv_cache, B, T):
         ops.linear(y.reshape(rows, nq), attn.c_proj.weight, out=resid, res=src, pdl=True)
         src = resid
         ops.add_rms_norm(resid, eps=eps, h_out=h)
-        f = gated_mlp(ffn, h)
+        f = gated_mlp(ffn, h, linear=USE_LINEAR_MLP)
         ops.add_rms_norm(resid, f, eps=eps, x_out=resid, h_out=h)
     return resid, h
 

@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 7
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 8
 
 
 def test_every_declared_symbol_is_exported():
@@ -145,10 +145,11 @@ def test_attention_workspace_is_per_persistent_cta_not_per_length():
 
 
 def test_split_plan_counters_only_for_partials_through_memory():
-    """A split plan merged inside a cluster (here, without a device, up to 8 splits) needs no
-    workspace and no counters; more splits publish partials and count arrivals per row group."""
+    """A split plan merged inside a cluster (up to 8 splits without a device, 16 where the device
+    schedules clusters of 16) needs no workspace and no counters; more splits publish partials and
+    count arrivals per row group."""
     lib = _native.load()
-    for splits, partials in ((4, False), (8, False), (12, True), (40, True)):
+    for splits, partials in ((4, False), (8, False), (20, True), (40, True)):
         a = _attn(num_ctas=-splits, Tmax=4096)
         ws = lib.mcb_decode_attn_workspace_size(ctypes.byref(a))
         cnt = lib.mcb_decode_attn_counter_count(ctypes.byref(a))
@@ -255,8 +256,16 @@ def test_linear_rejects_bad_arguments_on_the_host():
             setattr(a, k, v)
         return a
 
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=2)), None))
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=4)), None))
     assert st == _native.MCB_ERR_INVALID_ARG and "flags" in msg
+    # the gated projection stands alone: no norm, delta or res, and N a multiple of 16
+    gated = _native.LINEAR_GATED
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=gated | _native.LINEAR_NORM)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "GATED" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=gated, res=base + (3 << 20), res_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "GATED" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=gated, N=24, y_stride=24)), None))
+    assert st == _native.MCB_ERR_UNSUPPORTED and "multiple of 16" in msg
     st, msg = _err(lib.mcb_linear(ctypes.byref(args(K=96, x_stride=96, w_stride=96)), None))
     assert st == _native.MCB_ERR_UNSUPPORTED and "multiple of 64" in msg
     st, msg = _err(lib.mcb_linear(ctypes.byref(args(R=65)), None))

@@ -50,6 +50,27 @@ def test_linear_matches_torch(ops, shape):
     assert torch.equal(y, y_pdl)  # the same summation order every launch
 
 
+@pytest.mark.parametrize("shape", [(64, 2048, 768), (3, 2048, 768), (37, 96, 640), (64, 16, 64)],
+                         ids=lambda s: "R{}H{}K{}".format(*s))
+def test_gated_projection_is_silu_times_up_of_the_plain_one(ops, shape):
+    """gated=True on the packed [Wg; Wu]: each output feature's sum is the same warp-ordered
+    reduction as the plain projection's, so the result equals mcb_gated_silu over the plain
+    projection's two halves -- and torch's F.silu(gate) * up on them -- bit for bit."""
+    R, H, K = shape
+    g = torch.Generator(device="cuda").manual_seed(R * 7 + H + K)
+    x = _rand(g, R, K)
+    w = _rand(g, 2 * H, K, scale=K ** -0.5)
+    a = ops.linear(x, w, gated=True)
+    a_pdl = ops.linear(x, w, gated=True, pdl=True)
+    gu = ops.linear(x, w)
+    want = ops.gated_silu(gu[:, :H], gu[:, H:])
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert a.shape == (R, H)
+    assert torch.equal(a, want) and torch.equal(a_pdl, want)
+    assert torch.equal(want, F.silu(gu[:, :H]) * gu[:, H:])
+
+
 def test_linear_rejects_what_it_does_not_cover(ops):
     from modelcore_b200._native import McbError
     x = torch.zeros(65, 768, device="cuda", dtype=torch.bfloat16)

@@ -73,22 +73,26 @@ struct ProjParams {
 __host__ __device__ __forceinline__ int proj_x_offset(int F, int panels) {
   return (panels * F * 128 + 1023) & ~1023;
 }
-__host__ __device__ __forceinline__ int proj_x_bytes(int F, int panels) {
-  const int a = panels * kProjPanel, b = kProjWarps * kProjRows * F * 4;
+// rb: the rows of one CTA's activation block (64; 32 when a row block splits over two CTAs)
+__host__ __device__ __forceinline__ int proj_x_bytes(int F, int panels, int rb = kProjRows) {
+  const int a = panels * rb * 128, b = kProjWarps * rb * F * 4;
   return a > b ? a : b;
 }
-__host__ __device__ __forceinline__ int proj_bar_offset(int F, int panels, bool add) {
-  return proj_x_offset(F, panels) + proj_x_bytes(F, panels) + (add ? panels * kProjPanel : 0);
+__host__ __device__ __forceinline__ int proj_bar_offset(int F, int panels, bool add, int rb = kProjRows) {
+  return proj_x_offset(F, panels) + proj_x_bytes(F, panels, rb) + (add ? panels * rb * 128 : 0);
 }
-__host__ __device__ __forceinline__ int proj_smem_bytes(int F, int panels, bool add) {
-  return proj_bar_offset(F, panels, add) + (panels + 2) * 8 + 1024;
+__host__ __device__ __forceinline__ int proj_smem_bytes(int F, int panels, bool add, int rb = kProjRows) {
+  return proj_bar_offset(F, panels, add, rb) + (panels + 2) * 8 + 1024;
 }
 
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int F, bool NORM, bool ADD, bool GATED = false>
+// RB = 32: the 64-row block is split over two CTAs (grid.y), each with all of K -- for the wide-K
+// projections (down_proj: K = the MLP width) whose 64-row activation block would not fit; every
+// output's sum is the same warp-ordered reduction over K as with RB = 64.
+template <int F, bool NORM, bool ADD, bool GATED = false, int RB = kProjRows>
 __global__ void __launch_bounds__(kProjThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap dmap, const ProjParams p) {
@@ -96,6 +100,10 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   static_assert(!GATED || (!NORM && F % 16 == 0), "the gated epilogue stands alone, F/2 a multiple of 8");
   constexpr int NT = F / 8;  // n-tiles of 8 features (of the W slice)
   constexpr int FO = GATED ? F / 2 : F;  // output features a CTA
+  static_assert(RB == kProjRows || (RB == 32 && !NORM), "row-split blocks: the plain product only");
+  constexpr int PANEL = RB * 128;        // one 64-column activation panel of the CTA's rows, bytes
+  constexpr int MT = RB / 16;            // m-tiles of 16 rows
+  const int row0 = static_cast<int>(blockIdx.y) * RB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -103,8 +111,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   const int n0 = static_cast<int>(blockIdx.x) * FO;
   uint8_t* wsm = smem;
   uint8_t* xsm = smem + proj_x_offset(F, panels);
-  uint8_t* dsm = xsm + proj_x_bytes(F, panels);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + proj_bar_offset(F, panels, ADD));
+  uint8_t* dsm = xsm + proj_x_bytes(F, panels, RB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + proj_bar_offset(F, panels, ADD, RB));
   uint64_t* w_full = full + panels;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(w_full + 1);
 
@@ -131,9 +139,9 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int i = 0; i < panels; ++i) {
-      mbar_arrive_expect_tx(&full[i], ADD ? 2 * kProjPanel : kProjPanel);
-      tma_load_4d(xsm + i * kProjPanel, &xmap, &full[i], i * 64, 0, 0, 0, 0ull);
-      if (ADD) tma_load_4d(dsm + i * kProjPanel, &dmap, &full[i], i * 64, 0, 0, 0, 0ull);
+      mbar_arrive_expect_tx(&full[i], ADD ? 2 * PANEL : PANEL);
+      tma_load_4d(xsm + i * PANEL, &xmap, &full[i], i * 64, row0, 0, 0, 0ull);
+      if (ADD) tma_load_4d(dsm + i * PANEL, &dmap, &full[i], i * 64, row0, 0, 0, 0ull);
     }
   }
   __syncwarp();  // lane 0 of warp 0 rejoins before its warp waits on anything
@@ -206,9 +214,9 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   ok = mbar_wait_or_abort(w_full, 0, abort_flag) && ok;
 
   // ---------------- products: warp w takes K steps [ks0, ks1) of 16 columns ----------------
-  float acc[4][NT][4];
+  float acc[MT][NT][4];
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -221,11 +229,11 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     if (!NORM && ok && (ks == ks0 || (ks & 3) == 0)) ok = mbar_wait_or_abort(&full[pnl], 0, abort_flag);
     if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: ldmatrix and mma are collective
     const int kc = (ks & 3) * 2;  // first 8-column chunk of the step within the panel
-    uint32_t a[4][4];
+    uint32_t a[MT][4];
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
+    for (int mt = 0; mt < MT; ++mt) {
       const int row = mt * 16 + (lane & 15);
-      ldsm_x4(xb + pnl * kProjPanel + swz128(row, kc + (lane >> 4)), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+      ldsm_x4(xb + pnl * PANEL + swz128(row, kc + (lane >> 4)), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
     }
     uint32_t b[NT][2];
 #pragma unroll
@@ -235,20 +243,20 @@ __global__ void __launch_bounds__(kProjThreads, 1)
               b[2 * np + 1][0], b[2 * np + 1][1]);
     }
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
         mma_16816(acc[mt][nt], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b[nt][0], b[nt][1]);
   }
   __syncthreads();  // every warp is done reading X: its bytes take the partial tiles
-  float* red = reinterpret_cast<float*>(xsm);  // [warp][64][F]
+  float* red = reinterpret_cast<float*>(xsm);  // [warp][RB][F]
   {
     const int g = lane >> 2, cq = (lane & 3) * 2;
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint32_t a0 = smem_u32(red + (warp * kProjRows + mt * 16 + g) * F + nt * 8 + cq);
+        const uint32_t a0 = smem_u32(red + (warp * RB + mt * 16 + g) * F + nt * 8 + cq);
         asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a0), "f"(acc[mt][nt][0]), "f"(acc[mt][nt][1]) : "memory");
         asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a0 + 32 * F), "f"(acc[mt][nt][2]), "f"(acc[mt][nt][3])
                      : "memory");
@@ -257,13 +265,14 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   __syncthreads();
   const bool have = !*abort_flag;
   // ---------------- epilogue: 8 features a thread, warps summed in order ----------------
-  for (int it = threadIdx.x; have && it < kProjRows * (FO / 8); it += kProjThreads) {
-    const int row = it / (FO / 8), f8 = (it % (FO / 8)) * 8;
+  for (int it = threadIdx.x; have && it < RB * (FO / 8); it += kProjThreads) {
+    const int lrow = it / (FO / 8), f8 = (it % (FO / 8)) * 8;
+    const int row = row0 + lrow;
     if (row >= p.R) continue;
     float o[8], ou[8];  // ou: the matching up features (gated)
 #pragma unroll
     for (int w = 0; w < kProjWarps; ++w) {
-      const uint32_t ra = smem_u32(red + (w * kProjRows + row) * F + f8);
+      const uint32_t ra = smem_u32(red + (w * RB + lrow) * F + f8);
       const uint4 lo = lds128(ra), hi = lds128(ra + 16);
       const float t[8] = {__uint_as_float(lo.x), __uint_as_float(lo.y), __uint_as_float(lo.z), __uint_as_float(lo.w),
                           __uint_as_float(hi.x), __uint_as_float(hi.y), __uint_as_float(hi.z), __uint_as_float(hi.w)};

@@ -856,18 +856,18 @@ int encode_rows_map(CUtensorMap* map, const void* base, long long rows, long lon
 
 constexpr int kMaxSmemOptin = 232448;
 
-template <int F, bool NORM, bool ADD, bool GATED = false>
+template <int F, bool NORM, bool ADD, bool GATED = false, int RB = mcb::kProjRows>
 int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& dm, const mcb::ProjParams& prm,
                 bool pdl, cudaStream_t st) {
   static std::atomic<uint64_t> done{0};
-  auto kernel = mcb::proj_kernel<F, NORM, ADD, GATED>;
+  auto kernel = mcb::proj_kernel<F, NORM, ADD, GATED, RB>;
   cudaError_t e = ensure_smem(kernel, kMaxSmemOptin, done);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchConfig_t cfg = {};
   constexpr int FO = GATED ? F / 2 : F;  // output features a CTA
-  cfg.gridDim = dim3(static_cast<unsigned>((prm.N + FO - 1) / FO));
+  cfg.gridDim = dim3(static_cast<unsigned>((prm.N + FO - 1) / FO), static_cast<unsigned>((prm.R + RB - 1) / RB));
   cfg.blockDim = dim3(mcb::kProjThreads);
-  cfg.dynamicSmemBytes = mcb::proj_smem_bytes(F, prm.panels, ADD);
+  cfg.dynamicSmemBytes = mcb::proj_smem_bytes(F, prm.panels, ADD, RB);
   cfg.stream = st;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1282,7 +1282,9 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   // delta: its panels leave no room for a wider weight slice)
   // gated: 16 gate and 16 up rows of W a CTA (the epilogue pairs them)
   const int F = gated ? 32 : (add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32);
-  if (mcb::proj_smem_bytes(F, panels, add) > kMaxSmemOptin)
+  // a plain product whose 64-row activation block does not fit splits the rows over two CTAs
+  const int rb = (!norm && !gated && mcb::proj_smem_bytes(F, panels, false) > kMaxSmemOptin) ? 32 : mcb::kProjRows;
+  if (mcb::proj_smem_bytes(F, panels, add, rb) > kMaxSmemOptin)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d does not fit the shared memory (%d features a CTA%s)",
                 a->K, F, add ? ", with delta" : "");
   if (a->R == 0) return MCB_OK;
@@ -1290,7 +1292,7 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   int rc = gated ? encode_rows_map(&wm, a->w, 2ll * a->N, a->K, a->w_stride, F / 2)
                  : encode_rows_map(&wm, a->w, a->N, a->K, a->w_stride, F);
   if (rc != MCB_OK) return rc;
-  rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, mcb::kProjRows);
+  rc = encode_rows_map(&xm, a->x, a->R, a->K, a->x_stride, rb);
   if (rc != MCB_OK) return rc;
   if (add) {
     rc = encode_rows_map(&dm, a->delta, a->R, a->K, a->delta_stride, mcb::kProjRows);
@@ -1315,6 +1317,9 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
   if (gated) return launch_proj<32, false, false, true>(wm, xm, dm, p, pdl, st);
+  if (rb == 32)
+    return F == 16 ? launch_proj<16, false, false, false, 32>(wm, xm, dm, p, pdl, st)
+                   : launch_proj<32, false, false, false, 32>(wm, xm, dm, p, pdl, st);
   return F == 16 ? launch_proj_f<16>(norm, add, wm, xm, dm, p, pdl, st)
                  : launch_proj_f<32>(norm, add, wm, xm, dm, p, pdl, st);
 }

@@ -110,13 +110,13 @@ USE_FUSED_PROJ = False
 # projections on mcb_linear, c_proj with the residual add in its epilogue, launched with
 # programmatic dependent launch: projection, attention and c_proj then form one chain in which
 # each kernel's weight slice -- or, for the attention, the keys of earlier steps -- streams in
-# while the kernel ahead finishes, which a cuBLAS launch cannot join.  gate|up and down_proj stay
-# on cuBLAS (gate|up is slower on mcb_linear, 5.15 vs 4.40 us; down_proj's K, the MLP width, does
-# not fit its shared memory).  Measured on config 2 (64 rows, graph replay): 0.598 vs
-# 0.616 ms/step, the same greedy stream; c_proj alone on mcb_linear was slower (0.631).
+# while the kernel ahead finishes, which a cuBLAS launch cannot join.  Measured on config 2 (64
+# rows, graph replay): 0.598 vs 0.616 ms/step with q|k|v and c_proj alone, the same greedy stream
+# (c_proj alone on mcb_linear was slower, 0.631: the chain is what pays).
 USE_LINEAR_PROJ = True
-# ... and, on that path, gate|up with silu(gate) * up in its epilogue on mcb_linear (one launch
-# for two) unless USE_LINEAR_MLP is False
+# ... and, on that path, the MLP too unless USE_LINEAR_MLP is False: gate|up with silu(gate) * up
+# in its epilogue (one launch for two) and down_proj (its K, the MLP width, split over two CTAs a
+# row block), so that every projection of the layer is in the programmatic-dependent-launch chain
 USE_LINEAR_MLP = True
 
 
@@ -140,16 +140,16 @@ def qkv_projection(attn, x):
 def gated_mlp(ffn, h, linear=False):
     """GatedMLP.forward (modelcore/components/mlp.py:89-90) for activation "silu" on (rows, C):
     one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj; with linear (a decode step's few rows,
-    hidden width a multiple of 16) the first two as one mcb_linear launch whose epilogue applies
-    silu(gate) * up, launched with programmatic dependent launch."""
+    hidden width a multiple of 64 and at most 2,048) gate|up as one mcb_linear launch whose
+    epilogue applies silu(gate) * up, and down_proj on mcb_linear too (two CTAs a row block, all
+    of K each), both launched with programmatic dependent launch."""
     w = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
     H = ffn.hidden_dim
-    if linear and H % 16 == 0:
+    if linear and H % 64 == 0 and H <= 2048:
         a = ops.linear(h, w, gated=True, pdl=True)
-    else:
-        gu = F.linear(h, w)
-        a = ops.gated_silu(gu[:, :H], gu[:, H:])
-    return F.linear(a, ffn.down_proj.weight)
+        return ops.linear(a, ffn.down_proj.weight, pdl=True)
+    gu = F.linear(h, w)
+    return F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
 
 
 def _structure_ok(body):

@@ -33,6 +33,7 @@ def _rand(g, *shape, scale=1.0):
 SHAPES = [  # R, N, K: the quickstart's projections, ragged R / N, the largest K, 32-wide slices
     (64, 2304, 768), (64, 768, 768), (64, 4096, 768), (1, 768, 768), (37, 300, 640),
     (17, 96, 64), (64, 1001, 768), (64, 768, 1408), (3, 5000, 512), (64, 8, 128),
+    (64, 768, 2048), (40, 768, 2048), (20, 96, 2048),  # down_proj: two CTAs a 64-row block
 ]
 
 
@@ -77,7 +78,7 @@ def test_linear_rejects_what_it_does_not_cover(ops):
     with pytest.raises(McbError, match="at most 64"):
         ops.linear(x, torch.zeros(64, 768, device="cuda", dtype=torch.bfloat16))
     with pytest.raises(McbError, match="shared memory"):
-        ops.linear(x[:64].new_zeros(64, 2048), torch.zeros(64, 2048, device="cuda", dtype=torch.bfloat16))
+        ops.linear(x[:64].new_zeros(64, 3840), torch.zeros(64, 3840, device="cuda", dtype=torch.bfloat16))
 
 
 def test_linear_reads_strided_rows_and_writes_strided_output(ops):

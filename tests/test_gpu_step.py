@@ -333,9 +333,9 @@ def test_fused_step_launches_and_graph_replay(env, mode, monkeypatch):
             attn_launches = per_step - (1 + 4 * (4 + append) + 1 + 1 + 1)
         elif mode == "linear":
             # embedding + first norm, per layer q|k|v, c_proj (+ residual), the norm, gate|up
-            # with silu * up in its epilogue, the add + norm and the append, the advance, the
-            # LM-head epilogue
-            attn_launches = per_step - (1 + 4 * (5 + append) + 1 + 1)
+            # with silu * up in its epilogue, down_proj, the add + norm and the append, the
+            # advance, the LM-head epilogue
+            attn_launches = per_step - (1 + 4 * (6 + append) + 1 + 1)
         else:
             # embedding + first norm, per layer two add + norms, silu * up and the append, the
             # advance, the LM-head epilogue

@@ -179,8 +179,9 @@ typedef struct {
   const float* k_scale;
   const float* v_scale;
   int32_t scale_tmax;
-  /* fused append (fuse_append = 1; T = 1, a bf16 slot, D = 64 or 128, and a split plan --
-     mcb_decode_attn_fusable): q is the RAW query projection (B, 1, Hq, D); the kernel does what
+  /* fused append (fuse_append = 1; T = 1, a bf16 slot, D = 64 or 128, and the split or the
+     persistent plan -- mcb_decode_attn_fusable): q is the RAW query projection (B, 1, Hq, D);
+     the kernel does what
      mcb_kv_append_rope does for this step (rope at position cache_seqlens[b] from rot_cos /
      rot_sin, rms_norm with norm_eps, x qk_scale, bit for bit) on the query and, with k_new /
      v_new, on the new key, writes the key and value into k_cache / v_cache at that position,
@@ -211,8 +212,9 @@ size_t mcb_decode_attn_workspace_size(const mcb_attn_args* args);
 size_t mcb_decode_attn_counter_count(const mcb_attn_args* args);
 
 /* 1 when mcb_decode_attn can run this call with fuse_append = 1 (one new token a row, a bf16
- * slot, D = 64 or 128, and the split plan: rows of at most 2,048 keys or few row groups), else
- * 0 -- the caller then runs mcb_kv_append_rope and mcb_decode_attn.  Decided on the host from
+ * slot, D = 64 or 128, and the split or the persistent plan -- not the prefill plan, which
+ * num_ctas = 0 picks for T >= 64), else 0 -- the caller then runs mcb_kv_append_rope and
+ * mcb_decode_attn.  Decided on the host from
  * the shapes alone (no device read).  Not in the reference, whose append and attention are two
  * calls (kernels/flash_attn.py:306-366). */
 int mcb_decode_attn_fusable(const mcb_attn_args* args);

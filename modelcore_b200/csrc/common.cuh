@@ -246,6 +246,14 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+// Asynchronous 16-byte global -> shared copies (both addresses 16-byte aligned), completed per
+// thread by cp_async_wait_all; a __syncwarp / barrier after the wait shows them to other threads.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------------------------
 // Warp-level tensor-core fragments.
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,

@@ -37,6 +37,7 @@
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "kv_append.cuh"  // rope_norm_vec: the fused append's arithmetic
 
 namespace mcb {
 
@@ -55,6 +56,21 @@ struct AttnParams {
   int n_entries;     // B * nqb
   int grid;          // persistent CTAs = ngroups * Hkv
   int ngroups;       // CTA groups; CTA c serves kv head c % Hkv of group c / Hkv
+  // fused append (bf16 slot, one new token a row, D = 64 or 128): q is the raw query projection;
+  // every CTA ropes, norms and scales the query heads of each row group it serves, and the CTA
+  // whose tile range holds a row's new position writes the new key (roped, normed, scaled unless
+  // raw) and value into the slot and into its own copy of that tile -- kv_append_rope_vec_kernel's
+  // arithmetic, the same bits
+  int fuse;
+  const uint16_t* k_new;       // (B, 1, Hkv, D) raw key / value projections; null: q only
+  const uint16_t* v_new;
+  long long kns[3], vns[3];
+  uint16_t* kc_out;            // the slot (B, Tmax, Hkv, D) the new key and value go to
+  uint16_t* vc_out;
+  const uint16_t* rot_cos;     // rotary tables (rot_len, D/2) bf16
+  const uint16_t* rot_sin;
+  int rot_len, rotate_k;
+  float norm_eps, qk_scale;
 };
 
 constexpr int kAttnConsumerWarps = 4;
@@ -80,10 +96,19 @@ struct AttnConfig {
   static constexpr int STAT_BYTES = 2 * 2 * kAttnConsumerWarps * kRows * 4;  // (m, l) x two copies
   static constexpr int CTL_OFFSET = STAT_OFFSET + STAT_BYTES;  // abort flag, start state, last flag
   static constexpr int CTL_BYTES = 64;
-  static constexpr int SMEM_BYTES = CTL_OFFSET + CTL_BYTES + 1024;  // + alignment slack
+  // fused append, by segment parity (this row group and the next), bf16: the processed query
+  // rows [2][kRows][D], the processed new key and value [2][2][D], and the staged raw inputs
+  // [2][STG]: query rows [kRows][D], key and value [2][D], the rotary rows cos | sin [D]
+  static constexpr int FUSE_OFFSET = CTL_OFFSET + CTL_BYTES;
+  static constexpr int FUSE_Q = kRows * D;          // elements
+  static constexpr int FUSE_KV = 2 * D;
+  static constexpr int FUSE_STG = (kRows + 3) * D;
+  static constexpr int FUSE_BYTES = (D == 64 || D == 128) ? 2 * (FUSE_Q + FUSE_KV + FUSE_STG) * 2 : 0;
+  static constexpr int SMEM_BYTES = FUSE_OFFSET + FUSE_BYTES + 1024;  // + alignment slack
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(KPW % 16 == 0, "keys per warp");
   static_assert(RING_BYTES % 1024 == 0, "ring alignment");
+  static_assert(FUSE_OFFSET % 16 == 0, "fused-append buffers: 16-byte vectors");
 };
 
 // Byte offset of the 16-byte chunk `chunk` (0 .. ROW_BYTES/16) of key row `key` in a panel,
@@ -216,6 +241,104 @@ __device__ __forceinline__ void load_q_frags(const AttnParams& p, const Entry& e
   }
 }
 
+// The same from a row group's query rows in shared memory ([kRows][D], nvalid of them).
+template <int D, int NQT>
+__device__ __forceinline__ void load_q_frags_smem(const uint16_t* qsrc, int nvalid,
+                                                  uint32_t (&qf)[NQT][D / 16][2]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < NQT; ++j) {
+    const int n = j * 8 + (lane >> 2);
+    const uint16_t* qrow = n < nvalid ? qsrc + n * D : nullptr;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int d0 = kk * 16 + 2 * (lane & 3);
+      qf[j][kk][0] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+      qf[j][kk][1] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+    }
+  }
+}
+
+// Fused append, step 1 (one warp; asynchronous): a row group's raw inputs staged into `stg` by
+// cp.async -- its query rows (T = 1: row r of the group is q head kvh * G + r), the raw key and
+// value (with k_new) and the rotary rows at its position.  Completed by cp_async_wait_all.
+template <int D, int ROWS>
+__device__ __forceinline__ void fuse_fetch(const AttnParams& p, const Entry& ent, int kvh, uint16_t* stg) {
+  constexpr int CH = D / 8;  // 16-byte chunks a vector
+  const int lane = threadIdx.x & 31;
+  const int nq = ent.r1 - ent.r0;
+  const uint32_t sq = smem_u32(stg), skv = smem_u32(stg + ROWS * D), srot = smem_u32(stg + (ROWS + 2) * D);
+  for (int c = lane; c < nq * CH; c += 32) {
+    const int v = c / CH, ch = c - v * CH;
+    cp_async16(sq + (v * D + ch * 8) * 2, p.q + ent.b * p.qs[0] + (kvh * p.G + ent.r0 + v) * p.qs[2] + ch * 8);
+  }
+  if (p.k_new != nullptr && lane < 2 * CH) {
+    const int isv = lane >= CH ? 1 : 0, ch = lane % CH;
+    const uint16_t* src = isv ? p.v_new + ent.b * p.vns[0] + kvh * p.vns[2]
+                              : p.k_new + ent.b * p.kns[0] + kvh * p.kns[2];
+    cp_async16(skv + (isv * D + ch * 8) * 2, src + ch * 8);
+  }
+  if (ent.L >= 0 && ent.L < p.rot_len && lane < CH) {  // D/2 cosines, then D/2 sines
+    const int is_sin = lane >= CH / 2 ? 1 : 0, ch = lane % (CH / 2);
+    const uint16_t* tab = is_sin ? p.rot_sin : p.rot_cos;
+    cp_async16(srot + (is_sin * (D / 2) + ch * 8) * 2,
+               tab + static_cast<long long>(ent.L) * (D / 2) + ch * 8);
+  }
+  cp_async_commit();
+}
+
+// Fused append, step 2 (the same warp, after cp_async_wait_all and __syncwarp): the staged query
+// rows roped, normed and scaled into qdst [kRows][D]; with_kv: the new key (roped, normed and
+// scaled when p.rotate_k) and the value into kvdst [2][D] and into the slot at the row's position
+// -- groups of D/16 lanes one vector each, kv_append_rope_vec_kernel's arithmetic, the same bits.
+template <int D, int ROWS>
+__device__ __forceinline__ void fuse_finish(const AttnParams& p, const Entry& ent, int kvh, const uint16_t* stg,
+                                            bool with_kv, uint16_t* qdst, uint16_t* kvdst) {
+  constexpr int LG = D / 16, VPW = 32 / LG, HALF = D / 2;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LG;
+  const int nq = ent.r1 - ent.r0;
+  const int nvec = nq + (with_kv ? 2 : 0);
+  const int L = ent.L;
+  const bool rot_ok = L >= 0 && L < p.rot_len;
+  const uint16_t* srot = stg + (ROWS + 2) * D;
+  const uint4 cv = rot_ok ? *reinterpret_cast<const uint4*>(srot + 8 * sub) : make_uint4(0, 0, 0, 0);
+  const uint4 sv = rot_ok ? *reinterpret_cast<const uint4*>(srot + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
+  for (int v0 = 0; v0 < nvec; v0 += VPW) {
+    const int vi = v0 + lane / LG;
+    const bool valid = vi < nvec;
+    const bool is_q = vi < nq, is_k = vi == nq;
+    const uint16_t* src = is_q ? stg + vi * D : stg + (ROWS + (is_k ? 0 : 1)) * D;
+    const bool rotate = valid && (is_q || (is_k && p.rotate_k));
+    if (rotate && !rot_ok && sub == 0) record_error(kErrPositionBeyondRotary);
+    const uint4 x1v = valid ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
+    const uint4 x2v = valid ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
+    uint4 w1, w2;
+    rope_norm_vec_tab<D>(x1v, x2v, cv, sv, rotate && rot_ok, p.norm_eps, p.qk_scale, w1, w2);
+    if (valid) {
+      uint16_t* dst = is_q ? qdst + vi * D : kvdst + (is_k ? 0 : D);
+      *reinterpret_cast<uint4*>(dst + 8 * sub) = w1;
+      *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = w2;
+      if (!is_q && (p.ring || L < p.Tmax)) {
+        const int idx = p.ring ? L % p.Tmax : L;
+        uint16_t* cdst = (is_k ? p.kc_out : p.vc_out) +
+                         ((static_cast<long long>(ent.b) * p.Tmax + idx) * p.Hkv + kvh) * D;
+        *reinterpret_cast<uint4*>(cdst + 8 * sub) = w1;
+        *reinterpret_cast<uint4*>(cdst + HALF + 8 * sub) = w2;
+      }
+    }
+  }
+}
+
+// Whether a CTA's segment of `seg` tiles from tile `local` of the entry holds the row's new
+// position (T = 1: the entry's last tile), and the new key's row in that tile.
+template <int TK>
+__device__ __forceinline__ bool segment_owns_new(const Entry& ent, int local, int seg, int* row) {
+  const int tile_new = ent.L >= 0 ? (ent.L - ent.kb) / TK : -1;
+  *row = ent.L - (ent.kb + tile_new * TK);
+  return tile_new >= local && tile_new < local + seg;
+}
+
 template <int D, int NQT, int KPW, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads)
     decode_attn_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -297,14 +420,47 @@ __global__ void __launch_bounds__(kAttnThreads)
   uint32_t g = 0;
   bool first_segment = true;
   int seg_index = 0;
+  // fused append, by segment parity: the processed query rows, new key and value, and the raw
+  // inputs staged for them
+  uint16_t* qbuf = reinterpret_cast<uint16_t*>(smem + C::FUSE_OFFSET);  // [2][FUSE_Q]
+  uint16_t* kvbuf = qbuf + 2 * C::FUSE_Q;                               // [2][FUSE_KV]
+  uint16_t* stg = kvbuf + 2 * C::FUSE_KV;                               // [2][FUSE_STG]
+  const bool fuse = C::FUSE_BYTES > 0 && p.fuse;
   uint32_t qf[NQT][D / 16][2];
-  load_q_frags<D, NQT>(p, w.ent, w.kvh, qf);
+  if (fuse) {
+    // the first row group's inputs in the open; later groups' are staged a segment ahead
+    if (warp == 0) {
+      const int seg0 = static_cast<int>(min(static_cast<long long>(w.ent.n - w.local), t_end - w.t));
+      int row;
+      const bool own0 = p.k_new != nullptr && segment_owns_new<TK>(w.ent, w.local, seg0, &row);
+      fuse_fetch<D, ROWS>(p, w.ent, w.kvh, stg);
+      cp_async_wait_all();
+      __syncwarp();
+      fuse_finish<D, ROWS>(p, w.ent, w.kvh, stg, own0, qbuf, kvbuf);
+    }
+    named_barrier(1, kAttnConsumerWarps * 32);
+    load_q_frags_smem<D, NQT>(qbuf, w.ent.r1 - w.ent.r0, qf);
+  } else {
+    load_q_frags<D, NQT>(p, w.ent, w.kvh, qf);
+  }
   while (w.t < t_end) {
     const Entry& ent = w.ent;
     const int seg = static_cast<int>(min(static_cast<long long>(ent.n - w.local), t_end - w.t));
     const bool complete = (w.local == 0 && seg == ent.n);
     const int slot = first_segment ? 0 : 1;
     const int nvalid = ent.r1 - ent.r0;
+    const int par = seg_index & 1;
+    // fused append: whether this segment's tiles hold the row's new position (its key and value
+    // are in kvbuf[par], prepared before the last merge barrier) and the new key's row there;
+    // warp 0 stages the next row group's raw inputs now and finishes them after its tiles
+    int new_row = 0;
+    const bool own_new = fuse && p.k_new != nullptr && segment_owns_new<TK>(ent, w.local, seg, &new_row);
+    if (fuse && warp == 0 && w.t + seg < t_end) {
+      Walk wq = w;  // the next row group
+      wq.local += seg;
+      walk_next_group<ROWS, TK>(p, wq);
+      fuse_fetch<D, ROWS>(p, wq.ent, wq.kvh, stg + (par ^ 1) * C::FUSE_STG);
+    }
 
     float m_run[NQT][2], l_run[NQT][2];
     float o_acc[NQT][D / 16][4];
@@ -338,6 +494,20 @@ __global__ void __launch_bounds__(kAttnThreads)
         const uint32_t kbase = smem_u32(smem + s * C::STAGE_BYTES);
         const uint32_t vbase = kbase + C::TILE_BYTES;
         const int tile_key0 = ent.kb + (w.local + i) * TK;
+        // fused append: the tile arrived with the slot's old bytes at the new position; the warp
+        // that owns that row writes the new key and value over it before reading the tile
+        if (own_new && tile_key0 <= ent.L && ent.L < tile_key0 + TK && new_row / KPW == warp) {
+          constexpr int NCHK = D / 8;  // 16-byte chunks per row
+          if (lane < 2 * NCHK) {
+            const int isv = lane >= NCHK ? 1 : 0;
+            const int col = (lane % NCHK) * 8;
+            const uint32_t dst = (isv ? vbase : kbase) + (col / C::PANEL) * C::PANEL_BYTES +
+                                 swz<C::ROW_BYTES, C::SWZ_MASK>(new_row, (col % C::PANEL) / 8);
+            sts128(dst, lds128(smem_u32(kvbuf + par * C::FUSE_KV + isv * D + col)));
+          }
+          fence_proxy_async_shared();  // TMA refills this stage later
+          __syncwarp();
+        }
 
         float sc[NCH][NQT][4];
 #pragma unroll
@@ -434,19 +604,28 @@ __global__ void __launch_bounds__(kAttnThreads)
       if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
 
-    // The next row group's Q fragments load while this one merges.
+    // The next row group's Q fragments load while this one merges (fused: from warp 0's rows,
+    // after the merge barrier below).
     Walk wn = w;
     wn.t += seg;
     wn.local += seg;
     if (wn.local == wn.ent.n) walk_next_group<ROWS, TK>(p, wn);
     uint32_t qf_next[NQT][D / 16][2];
-    if (wn.t < t_end) load_q_frags<D, NQT>(p, wn.ent, wn.kvh, qf_next);
+    if (!fuse && wn.t < t_end) load_q_frags<D, NQT>(p, wn.ent, wn.kvh, qf_next);
+    if (fuse && warp == 0 && wn.t < t_end) {  // the next row group's rows from the staged inputs
+      const int seg_n = static_cast<int>(min(static_cast<long long>(wn.ent.n - wn.local), t_end - wn.t));
+      int row;
+      const bool own_n = p.k_new != nullptr && segment_owns_new<TK>(wn.ent, wn.local, seg_n, &row);
+      cp_async_wait_all();
+      __syncwarp();
+      fuse_finish<D, ROWS>(p, wn.ent, wn.kvh, stg + (par ^ 1) * C::FUSE_STG, own_n,
+                           qbuf + (par ^ 1) * C::FUSE_Q, kvbuf + (par ^ 1) * C::FUSE_KV);
+    }
 
     // ---- merge the four warps' partial softmax states of this row group ----
     // The merge buffer, the statistics and the "last contributor" flag alternate between two
     // copies by row-group parity, so one barrier per row group suffices: a warp can only write
     // a copy again after the next row group's barrier, which every warp reaches after its reads.
-    const int par = seg_index & 1;
     float* mbuf = merge + par * (kAttnConsumerWarps * ROWS * C::OPITCH);
     float* st_m = stat_m + par * (2 * kAttnConsumerWarps * ROWS);
     float* st_l = st_m + kAttnConsumerWarps * ROWS;
@@ -473,6 +652,8 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
       }
     named_barrier(1, kAttnConsumerWarps * 32);
+    if (fuse && wn.t < t_end)
+      load_q_frags_smem<D, NQT>(qbuf + (par ^ 1) * C::FUSE_Q, wn.ent.r1 - wn.ent.r0, qf_next);
 
     for (int idx = threadIdx.x; idx < nvalid * D; idx += kAttnConsumerWarps * 32) {
       const int n = idx / D;

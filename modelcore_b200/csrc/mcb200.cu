@@ -676,9 +676,31 @@ int check_attn_pointers(const mcb_attn_args* a, const char* who) {
   return MCB_OK;
 }
 
-// Whether the planned call can fuse the append (the split kernel's bf16 path, one new token).
+// Whether the planned call can fuse the append (the split or persistent kernel's bf16 path, one
+// new token).
 bool plan_fusable(const mcb_attn_args* a, const AttnPlan& pl) {
-  return a->T == 1 && a->k_scale == nullptr && (a->D == 64 || a->D == 128) && pl.mode == kModeSplit;
+  return a->T == 1 && a->k_scale == nullptr && (a->D == 64 || a->D == 128) &&
+         (pl.mode == kModeSplit || pl.mode == kModePersistent);
+}
+
+// The fused-append fields shared by the split and the persistent kernels' parameters.
+template <class P>
+void fill_fused_append(P& p, const mcb_attn_args* a) {
+  p.fuse = a->fuse_append ? 1 : 0;
+  p.k_new = static_cast<const uint16_t*>(a->k_new);
+  p.v_new = static_cast<const uint16_t*>(a->v_new);
+  for (int i = 0; i < 3; ++i) {
+    p.kns[i] = a->k_new_stride[i];
+    p.vns[i] = a->v_new_stride[i];
+  }
+  p.kc_out = static_cast<uint16_t*>(const_cast<void*>(a->k_cache));  // written with fuse_append
+  p.vc_out = static_cast<uint16_t*>(const_cast<void*>(a->v_cache));
+  p.rot_cos = static_cast<const uint16_t*>(a->rot_cos);
+  p.rot_sin = static_cast<const uint16_t*>(a->rot_sin);
+  p.rot_len = a->rot_len;
+  p.rotate_k = a->rotate_k;
+  p.norm_eps = a->norm_eps;
+  p.qk_scale = a->qk_scale;
 }
 
 // q as a 4-D tensor map {D, Hq, T, B} with its own strides; 128-query boxes of 64-column panels.
@@ -734,7 +756,7 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
 int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* counters, cudaStream_t st) {
   if (a->fuse_append && !plan_fusable(a, pl))
     return fail(MCB_ERR_UNSUPPORTED, "mcb_decode_attn: the append fuses only for T = 1, a bf16 slot, D = 64 "
-                "or 128 and the split plan (mcb_decode_attn_fusable)");
+                "or 128 and the split or persistent plan (mcb_decode_attn_fusable)");
   if (pl.mode == kModePrefill) return run_prefill(a, st);
   const bool fp8 = a->k_scale != nullptr;
   CUtensorMap km, vm;
@@ -755,21 +777,7 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
     p.part_lse = pl.nsplit > 1 && !pl.cluster ? reinterpret_cast<float*>(w + pl.part_o_bytes) : nullptr;
     p.cluster = pl.cluster ? 1 : 0;
     p.counters = pl.counter_count > 0 ? counters : nullptr;
-    p.fuse = a->fuse_append ? 1 : 0;
-    p.k_new = static_cast<const uint16_t*>(a->k_new);
-    p.v_new = static_cast<const uint16_t*>(a->v_new);
-    for (int i = 0; i < 3; ++i) {
-      p.kns[i] = a->k_new_stride[i];
-      p.vns[i] = a->v_new_stride[i];
-    }
-    p.kc_out = static_cast<uint16_t*>(const_cast<void*>(a->k_cache));  // written with fuse_append
-    p.vc_out = static_cast<uint16_t*>(const_cast<void*>(a->v_cache));
-    p.rot_cos = static_cast<const uint16_t*>(a->rot_cos);
-    p.rot_sin = static_cast<const uint16_t*>(a->rot_sin);
-    p.rot_len = a->rot_len;
-    p.rotate_k = a->rotate_k;
-    p.norm_eps = a->norm_eps;
-    p.qk_scale = a->qk_scale;
+    fill_fused_append(p, a);
     p.ring = a->ring != 0;
     p.B = a->B;
     p.T = a->T;
@@ -814,6 +822,7 @@ int run_attn(const mcb_attn_args* a, const AttnPlan& pl, void* ws, int32_t* coun
   p.ring = a->ring != 0;
   p.grid = pl.grid;
   p.ngroups = pl.grid / a->Hkv;
+  fill_fused_append(p, a);
   return variant_launch(a->D, pl.nqt, pl.grid, km, vm, p, st);
 }
 

@@ -38,7 +38,7 @@ def _fusable(attn, x):
 
 
 # The decode step's append and attention in one launch where the plan allows it (T = 1, a bf16
-# slot, the split plan; ops.append_attn), with the bits of the two launches.
+# slot, the split or persistent plan; ops.append_attn), with the bits of the two launches.
 USE_FUSED_APPEND = True
 
 

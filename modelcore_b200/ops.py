@@ -350,8 +350,9 @@ def append_attn(q, k, v, k_cache, v_cache, cache_seqlens, cos, sin, *, eps=None,
     """kv_append_rope followed by decode_attn -- one decode step of an attention layer from its
     RAW projections q (B, T, Hq, D), k, v (B, T, Hkv, D; None for a layer that reads another
     layer's slot) -- in ONE launch where the plan allows it (T = 1, a bf16 slot, D = 64 or 128,
-    the split plan: mcb_decode_attn_fusable), with the same bits as the two launches; otherwise
-    the two launches.  cache_seqlens is not advanced.  Returns the attention output."""
+    the split or persistent plan: mcb_decode_attn_fusable), with the same bits as the two
+    launches; otherwise the two launches.  cache_seqlens is not advanced.  Returns the
+    attention output."""
     T, D = q.size(1), q.size(3)
     fusable = k_cache.dtype == torch.bfloat16 and T == 1 and D in (64, 128)
     if fusable:

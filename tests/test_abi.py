@@ -292,17 +292,19 @@ def test_linear_rejects_bad_arguments_on_the_host():
     assert st == _native.MCB_ERR_UNSUPPORTED and "shared memory" in msg
 
 
-def test_fused_append_is_offered_only_where_the_split_kernel_can_do_it():
+def test_fused_append_is_offered_only_where_the_decode_kernels_can_do_it():
     """mcb_decode_attn_fusable decides from the shapes on the host: one new token a row, a bf16
-    slot, head size 64 or 128 and the split plan; a fused call outside that is rejected before any
-    launch (the pointers are never read)."""
+    slot, head size 64 or 128 and the split or persistent plan; a fused call outside that is
+    rejected before any launch (the pointers are never read)."""
     lib = _native.load()
     fusable = lambda **kw: lib.mcb_decode_attn_fusable(ctypes.byref(_attn(**kw)))
     assert fusable() == 1                                     # 2 rows, 64-position slot: split
     assert fusable(D=64, Hq=4, Hkv=4) == 1
+    assert fusable(B=200, Tmax=65536) == 1                    # many groups of long rows: persistent
+    assert fusable(num_ctas=16) == 1                          # persistent, a given grid
     assert fusable(T=2) == 0                                  # several new tokens
+    assert fusable(T=64) == 0                                 # the prefill plan
     assert fusable(D=32) == 0
-    assert fusable(B=200, Tmax=65536) == 0                    # many groups of long rows: persistent
     assert fusable(k_scale=1 << 20, v_scale=1 << 21, scale_tmax=64) == 0   # an fp8 slot
     a = _attn(T=2, q=0x1000, k_cache=0x2000, v_cache=0x3000, out=0x4000, cache_seqlens=0x5000,
               fuse_append=1, rot_cos=0x6000, rot_sin=0x7000, rot_len=64)

@@ -2,8 +2,9 @@
 that ropes, norms and scales the raw query and key of a decode step, writes the key and value into
 the slot and attends over it must give exactly what the two launches give (mcb_kv_append_rope,
 then mcb_decode_attn): the same cache bytes and the same attention output, bit for bit, on every
-split plan (one split, a cluster merge, partials), with windows, ring slots, GQA groups and
-layers that read another layer's slot."""
+split plan (one split, a cluster merge, partials) and on the persistent plan (row groups cut
+between CTAs and merged by the last to arrive, several row groups a CTA, two query blocks a
+row), with windows, ring slots, GQA groups and layers that read another layer's slot."""
 import pytest
 import torch
 
@@ -29,6 +30,14 @@ CASES = [  # B, Hq, Hkv, D, Tmax, max_len, window, ring, produces_kv, num_ctas
     (40, 32, 8, 128, 1400, 1390, -1, False, True, -20), # partials and the combine kernel
     (2, 8, 2, 64, 512, 1500, 200, True, True, 0),       # a ring slot
     (5, 16, 4, 128, 1024, 1000, -1, False, False, 0),   # a layer that reads another's slot
+    # the persistent plan (num_ctas > 0 or many groups of long rows)
+    (64, 32, 8, 128, 2560, 2500, -1, False, True, 0),   # chosen by the planner (512 long groups)
+    (6, 16, 4, 64, 1024, 1000, -1, False, True, 16),    # groups cut between CTAs, merged last
+    (8, 16, 4, 128, 2048, 2000, 700, False, True, 20),  # a window
+    (3, 8, 2, 64, 512, 1500, 200, True, True, 6),       # a ring slot
+    (5, 16, 4, 128, 1024, 1000, -1, False, False, 8),   # a layer that reads another's slot
+    (4, 32, 2, 128, 1024, 1000, -1, False, True, 12),   # 16 query rows a group (two n-tiles)
+    (2, 64, 2, 64, 512, 500, -1, False, True, 4),       # two query blocks a row
 ]
 
 
@@ -116,7 +125,7 @@ def test_append_attn_picks_the_fused_launch_and_falls_back(ops):
         torch.cuda.synchronize()
         assert launches == 1
         assert torch.equal(kc1, kc2) and torch.equal(got, want)
-    # a persistent plan (many groups of long rows) falls back to the two launches
+    # a persistent plan (many groups of long rows) fuses too
     B2 = 64
     q2 = q.repeat(B2 // B, 1, 1, 1)
     k2, v2 = k.repeat(B2 // B, 1, 1, 1), v.repeat(B2 // B, 1, 1, 1)
@@ -126,14 +135,33 @@ def test_append_attn_picks_the_fused_launch_and_falls_back(ops):
     kc4, vc4 = kc3.clone(), vc3.clone()
     n0 = ops.launch_count()
     got = ops.append_attn(q2, k2, v2, kc3, vc3, sl2, cos, sin, eps=1e-6)
-    assert ops.launch_count() - n0 == 2
+    assert ops.launch_count() - n0 == 1
     qa = ops.kv_append_rope(q2, k2, v2, kc4, vc4, sl2, cos, sin, eps=1e-6, scale=1.2)
     want = ops.decode_attn(qa, kc4, vc4, sl2)
     torch.cuda.synchronize()
     assert torch.equal(kc3, kc4) and torch.equal(got, want)
+    # head_dim 32 has no fused kernel: the two launches
+    D3 = 32
+    q3 = torch.randn(B, 1, Hq, D3, device="cuda", generator=g).to(torch.bfloat16)
+    k3 = torch.randn(B, 1, Hkv, D3, device="cuda", generator=g).to(torch.bfloat16)
+    v3 = torch.randn(B, 1, Hkv, D3, device="cuda", generator=g).to(torch.bfloat16)
+    kc5 = torch.randn(B, 1024, Hkv, D3, device="cuda", generator=g).to(torch.bfloat16)
+    vc5 = torch.randn_like(kc5)
+    kc6, vc6 = kc5.clone(), vc5.clone()
+    sl3 = torch.randint(10, 1000, (B,), device="cuda", generator=g, dtype=torch.int32)
+    cos3, sin3 = tables(1032, D3)
+    n0 = ops.launch_count()
+    got = ops.append_attn(q3, k3, v3, kc5, vc5, sl3, cos3, sin3, eps=1e-6)
+    assert ops.launch_count() - n0 == 2
+    qa = ops.kv_append_rope(q3, k3, v3, kc6, vc6, sl3, cos3, sin3, eps=1e-6, scale=1.2)
+    want = ops.decode_attn(qa, kc6, vc6, sl3)
+    torch.cuda.synchronize()
+    assert torch.equal(kc5, kc6) and torch.equal(got, want)
 
 
-ORACLE_CASES = [CASES[1], CASES[2], CASES[5]]  # cluster merge; window + 12 splits; a reading layer
+# cluster merge; window + 12 splits; a reading layer; persistent: cut groups, a window, two
+# query blocks a row
+ORACLE_CASES = [CASES[1], CASES[2], CASES[5], CASES[7], CASES[8], CASES[12]]
 
 
 @pytest.mark.parametrize("case", ORACLE_CASES, ids=lambda c: "B{}Hq{}D{}w{}kv{}n{}".format(

@@ -796,7 +796,8 @@ def run_b200(args):
     import modelcore_b200
     from modelcore_b200 import step as _step
     _step.USE_FUSED_PROJ = args.linear == "fused"
-    _step.USE_LINEAR_PROJ = args.linear == "mcb"
+    _step.USE_LINEAR_PROJ = args.linear in ("mcb", "mcb-norm")
+    _step.USE_LINEAR_NORM_OUT = args.linear == "mcb"
     rank, world, local = _dist_setup(args.gpus)
     peak, peak_kind = _peaks()
     steps_needed = 1 + args.warmup + max(args.steps, args.e2e_steps or 0) + 2
@@ -909,8 +910,12 @@ def run_b200(args):
                                  "on libmcb200",
                         "plain": "modelcore's op-by-op forward around the libmcb200 append and "
                                  "attention"}[args.step],
-        "projections": {"mcb": "q|k|v and c_proj (+ residual) on libmcb200 mcb_linear, gate|up and "
-                               "down_proj on cuBLAS",
+        "projections": {"mcb": "every projection on libmcb200 mcb_linear under programmatic "
+                               "dependent launch: c_proj with the residual add and the next norm "
+                               "in its epilogue, gate|up with silu * up in its epilogue",
+                        "mcb-norm": "every projection on libmcb200 mcb_linear, c_proj with the "
+                                    "residual add in its epilogue, the norm after it a launch "
+                                    "of its own",
                         "fused": "libmcb200 mcb_linear with the norms and adds fused in, down_proj on cuBLAS",
                         "cublas": "torch F.linear (cuBLAS)"}[args.linear],
         "kv_read": {"bytes_per_step": int(kv_bytes_step),
@@ -951,10 +956,11 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--step", choices=("fused", "plain"), default="fused",
                     help="decode step around attention: fused (default) or modelcore's op-by-op")
-    ap.add_argument("--linear", choices=("mcb", "cublas", "fused"), default="mcb",
-                    help="decode projections: q|k|v and c_proj (+ residual) on libmcb200's "
-                         "mcb_linear, the MLP on cuBLAS (default); all on cuBLAS; or mcb_linear "
-                         "with the norms and adds fused in")
+    ap.add_argument("--linear", choices=("mcb", "mcb-norm", "cublas", "fused"), default="mcb",
+                    help="decode projections: all on libmcb200's mcb_linear, c_proj with the "
+                         "residual add and the next norm in its epilogue (default); the same with "
+                         "the norm a launch of its own; all on cuBLAS; or mcb_linear with the "
+                         "norms and adds fused in front")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep-only", action="store_true", help="run only the config-5 KV-read sweep")

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define MCB_ABI_VERSION 8
+#define MCB_ABI_VERSION 9
 
 typedef enum {
   MCB_OK = 0,
@@ -361,6 +361,14 @@ int mcb_sample(const mcb_sample_args* args, void* stream);
  *                             projection with act(gate) * up for act "silu"
  *                             (modelcore/components/mlp.py:89-90) -- the bits of mcb_gated_silu
  *                             over the plain projection; no norm, delta or res; N % 16 == 0.
+ *   flags & MCB_LINEAR_NORM_OUT  also h_out = rms_norm(Y, eps) (R, N): c_proj's residual add
+ *                             and the Block's next norm (modelcore/components/block.py:58-59)
+ *                             in one launch -- the bits of mcb_linear then mcb_add_rms_norm
+ *                             over Y.  The CTAs of one output row form a thread-block cluster of
+ *                             N / 64 (64 features each), whose per-row sums of squares meet in
+ *                             distributed shared memory; N a multiple of 64, at most 1024; y,
+ *                             res and h_out rows 16-byte aligned; no other flag.  Not in the
+ *                             reference, whose residual add and norm are separate torch ops.
  * X, delta, x_out (R, K), W (N, K) as nn.Linear stores it, Y and res (R, N), bf16, fp32
  * accumulation.  R <= 64, K a multiple of 64, x / delta / x_out / w rows 16-byte aligned; Y, res
  * and x_out must not overlap X or delta.  Every CTA takes 16 or 32 output features and all of K:
@@ -370,6 +378,7 @@ int mcb_sample(const mcb_sample_args* args, void* stream);
  * activations are read only after that kernel completed. */
 #define MCB_LINEAR_NORM 1
 #define MCB_LINEAR_GATED 2
+#define MCB_LINEAR_NORM_OUT 4
 
 typedef struct {
   const void* x;              /* (R, K) bf16                                                */
@@ -380,12 +389,19 @@ typedef struct {
   void* x_out;                /* (R, K) bf16: x + delta (with delta)                        */
   int64_t x_stride, w_stride, y_stride, res_stride, delta_stride, x_out_stride;  /* elements */
   int32_t R, N, K;
-  int32_t flags;              /* MCB_LINEAR_NORM or MCB_LINEAR_GATED                        */
+  int32_t flags;              /* MCB_LINEAR_NORM, MCB_LINEAR_GATED or MCB_LINEAR_NORM_OUT   */
   float eps;                  /* the norm's eps                                             */
   int32_t pdl;
+  void* h_out;                /* (R, N) bf16: rms_norm(Y) (MCB_LINEAR_NORM_OUT), or NULL    */
+  int64_t h_out_stride;       /* elements                                                   */
 } mcb_linear_args;
 
 int mcb_linear(const mcb_linear_args* args, void* stream);
+
+/* 1 when mcb_linear would run this call on the current device (the same host-side checks,
+ * including whether the device schedules MCB_LINEAR_NORM_OUT's clusters), else 0 with
+ * mcb_last_error saying why.  Nothing is launched or read from the device. */
+int mcb_linear_supported(const mcb_linear_args* args);
 
 /* ---------------------------------------------------------------------------------------------
  * Device-side status.  Kernels never trap: an out-of-range position (a cache or rotary table

@@ -36,7 +36,7 @@ DEVICE_ERRORS = {
     4: "token id outside the embedding table",
 }
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 # Size of the static scratch behind mcb_decode_attn_noalloc (MCB_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -59,6 +59,7 @@ EXPORTED_SYMBOLS = (
     "mcb_prefill_attn",
     "mcb_sample",
     "mcb_linear",
+    "mcb_linear_supported",
     "mcb_softcap_argmax",
     "mcb_device_error",
     "mcb_launch_count",
@@ -170,6 +171,7 @@ class SampleArgs(ctypes.Structure):
 
 LINEAR_NORM = 1
 LINEAR_GATED = 2
+LINEAR_NORM_OUT = 4
 
 
 class LinearArgs(ctypes.Structure):
@@ -181,6 +183,7 @@ class LinearArgs(ctypes.Structure):
         ("x_out_stride", ctypes.c_int64),
         ("R", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32),
         ("flags", ctypes.c_int32), ("eps", ctypes.c_float), ("pdl", ctypes.c_int32),
+        ("h_out", ctypes.c_void_p), ("h_out_stride", ctypes.c_int64),
     ]
 
 
@@ -224,6 +227,8 @@ def _declare(lib):
     lib.mcb_gated_silu.argtypes = [P(GatedSiluArgs), ctypes.c_void_p]
     lib.mcb_linear.restype = ctypes.c_int
     lib.mcb_linear.argtypes = [P(LinearArgs), ctypes.c_void_p]
+    lib.mcb_linear_supported.restype = ctypes.c_int
+    lib.mcb_linear_supported.argtypes = [P(LinearArgs)]
     lib.mcb_sample.restype = ctypes.c_int
     lib.mcb_sample.argtypes = [P(SampleArgs), ctypes.c_void_p]
     lib.mcb_prefill_attn.restype = ctypes.c_int

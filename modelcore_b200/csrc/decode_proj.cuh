@@ -9,6 +9,12 @@
 //                                               of the previous block's MLP, then the norm)
 //   residual:    Y = bf16(res + bf16(X W^T))   (the residual add after c_proj, block.py:58; res
 //                                               may be Y itself: in place)
+//   norm out:    Y = bf16(res + bf16(X W^T)), H = rms_norm(Y)   (c_proj's residual add and the
+//                                               Block's next norm, block.py:58-59: one output row
+//                                               spans the CTAs of a thread-block cluster, each
+//                                               holding one 64-column panel; the per-row panel
+//                                               sums of squares meet in distributed shared memory
+//                                               -- the bits of mcb_add_rms_norm over Y)
 //   gated:       Y = silu(X Wg^T) * (X Wu^T)   (GatedMLP's gate|up projection and act(gate) * up,
 //                                               modelcore/components/mlp.py:89-90, with W the
 //                                               packed [Wg; Wu]: each CTA takes F/2 gate rows
@@ -57,7 +63,8 @@ struct ProjParams {
   const uint16_t* res;   // residual (R, N) added to the product, or null
   uint16_t* y;           // (R, N)
   uint16_t* x_out;       // add + norm: X + delta (R, K), written by CTA 0
-  long long ress, ys, xos;  // row strides (elements)
+  uint16_t* h_out;       // norm out: rms_norm(Y) (R, N)
+  long long ress, ys, xos, hs;  // row strides (elements)
   int R, N, K;
   int panels;            // K / 64
   int vec_out;           // y (and res) rows 16-byte aligned, N % 8 == 0
@@ -91,8 +98,9 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
 
 // RB = 32: the 64-row block is split over two CTAs (grid.y), each with all of K -- for the wide-K
 // projections (down_proj: K = the MLP width) whose 64-row activation block would not fit; every
-// output's sum is the same warp-ordered reduction over K as with RB = 64.
-template <int F, bool NORM, bool ADD, bool GATED = false, int RB = kProjRows>
+// output's sum is the same warp-ordered reduction over K as with RB = 64.  RB = 16 (norm out):
+// four row blocks, each a cluster of N / 64 CTAs of 64 features.
+template <int F, bool NORM, bool ADD, bool GATED = false, int RB = kProjRows, bool NOUT = false>
 __global__ void __launch_bounds__(kProjThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap dmap, const ProjParams p) {
@@ -100,7 +108,9 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   static_assert(!GATED || (!NORM && F % 16 == 0), "the gated epilogue stands alone, F/2 a multiple of 8");
   constexpr int NT = F / 8;  // n-tiles of 8 features (of the W slice)
   constexpr int FO = GATED ? F / 2 : F;  // output features a CTA
-  static_assert(RB == kProjRows || (RB == 32 && !NORM), "row-split blocks: the plain product only");
+  static_assert(RB == kProjRows || ((RB == 32 || RB == 16) && !NORM), "row-split blocks: no norm in front");
+  static_assert(!NOUT || (F == 64 && !NORM && !GATED && RB * 8 <= kProjThreads),
+                "norm out: one 64-column panel a CTA, eight threads a row");
   constexpr int PANEL = RB * 128;        // one 64-column activation panel of the CTA's rows, bytes
   constexpr int MT = RB / 16;            // m-tiles of 16 rows
   const int row0 = static_cast<int>(blockIdx.y) * RB;
@@ -264,8 +274,69 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   }
   __syncthreads();
   const bool have = !*abort_flag;
+  if constexpr (NOUT) {
+    // ---------------- epilogue, norm out: thread (row, chunk) = (tid / 8, tid % 8) ----------------
+    // y = bf16(res + bf16(sum of the warps' partials in order)); the chunk's fp32 sum of squares
+    // element by element, the panel's pairwise tree over the row's eight lanes (xor 1, 2, 4), the
+    // panels -- one a CTA, cluster rank = panel -- added in order from 0: row_rms_rsqrt's order.
+    float* psum = reinterpret_cast<float*>(wsm);  // [RB] this panel's row sums (W is consumed)
+    const int lrow = threadIdx.x >> 3, c = threadIdx.x & 7;
+    const int row = row0 + lrow;
+    const bool act = threadIdx.x < RB * 8;      // whole warps: RB * 8 is a multiple of 32
+    const bool live = act && have && row < p.R;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    if (live) {
+#pragma unroll
+      for (int w = 0; w < kProjWarps; ++w) {
+        const uint32_t ra = smem_u32(red + (w * RB + lrow) * F + c * 8);
+        const uint4 lo = lds128(ra), hi = lds128(ra + 16);
+        const float t[8] = {__uint_as_float(lo.x), __uint_as_float(lo.y), __uint_as_float(lo.z), __uint_as_float(lo.w),
+                            __uint_as_float(hi.x), __uint_as_float(hi.y), __uint_as_float(hi.z), __uint_as_float(hi.w)};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = w == 0 ? t[i] : __fadd_rn(v[i], t[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = round_bf16(v[i]);
+      if (p.res != nullptr) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p.res + static_cast<long long>(row) * p.ress + n0 + c * 8);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = round_bf16(__fadd_rn(__uint_as_float(ws[i] << 16), v[2 * i]));
+          v[2 * i + 1] = round_bf16(__fadd_rn(__uint_as_float(ws[i] & 0xffff0000u), v[2 * i + 1]));
+        }
+      }
+      *reinterpret_cast<uint4*>(p.y + static_cast<long long>(row) * p.ys + n0 + c * 8) =
+          make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                     pack_bf16x2(v[6], v[7]));
+    }
+    if (act) {
+      float sq = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sq = __fadd_rn(sq, __fmul_rn(v[i], v[i]));
+      sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 1));
+      sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 2));
+      sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, 4));
+      if (c == 0) psum[lrow] = sq;
+    }
+    cluster_sync();  // every CTA's panel sums are published
+    if (live) {
+      float acc = 0.f;
+      const int npanel = static_cast<int>(gridDim.x);  // the cluster spans the row
+      for (int q = 0; q < npanel; ++q) acc = __fadd_rn(acc, ld_dsmem_f32(map_to_rank(psum + lrow, q)));
+      const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.N)), p.eps));
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[i] = pack_bf16x2(__fmul_rn(v[2 * i], r), __fmul_rn(v[2 * i + 1], r));
+      *reinterpret_cast<uint4*>(p.h_out + static_cast<long long>(row) * p.hs + n0 + c * 8) =
+          make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    cluster_sync();  // no CTA leaves while another still reads its panel sums
+  }
   // ---------------- epilogue: 8 features a thread, warps summed in order ----------------
-  for (int it = threadIdx.x; have && it < RB * (FO / 8); it += kProjThreads) {
+  for (int it = threadIdx.x; !NOUT && have && it < RB * (FO / 8); it += kProjThreads) {
     const int lrow = it / (FO / 8), f8 = (it % (FO / 8)) * 8;
     const int row = row0 + lrow;
     if (row >= p.R) continue;

@@ -8,8 +8,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <type_traits>
 
 #include "../../include/mcb200.h"
@@ -890,6 +892,82 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap&
   return MCB_OK;
 }
 
+// Norm out: 64 features a CTA, 16 rows a cluster of N / 64 CTAs (one per 64-column panel of the
+// output row); clusters above the portable 8 need the non-portable size, which the host checks
+// the device schedules (with this kernel's shared memory) before the first launch.
+constexpr int kProjNoutRows = 16;
+using ProjNoutKernel = decltype(&mcb::proj_kernel<64, false, false, false, kProjNoutRows, true>);
+
+cudaError_t nout_prepare(ProjNoutKernel kernel, int smem) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
+// Whether a norm-out launch with `npanel` CTAs a cluster and `smem` bytes each can be scheduled on
+// the current device (cached per device, cluster size and shared-memory size).
+bool nout_schedulable(int npanel, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, bool> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, npanel, smem);
+  auto itc = cache.find(key);
+  if (itc != cache.end()) return itc->second;
+  auto kernel = mcb::proj_kernel<64, false, false, false, kProjNoutRows, true>;
+  bool ok = nout_prepare(kernel, smem) == cudaSuccess;
+  if (ok) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(npanel), 1);
+    cfg.blockDim = dim3(mcb::kProjThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(npanel);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    ok = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0;
+  }
+  cudaGetLastError();
+  cache[key] = ok;
+  return ok;
+}
+
+int launch_proj_nout(const CUtensorMap& wm, const CUtensorMap& xm, const mcb::ProjParams& prm, bool pdl,
+                     cudaStream_t st) {
+  auto kernel = mcb::proj_kernel<64, false, false, false, kProjNoutRows, true>;
+  const int smem = mcb::proj_smem_bytes(64, prm.panels, false, kProjNoutRows);
+  cudaError_t e = nout_prepare(kernel, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(linear, norm out)");
+  cudaLaunchConfig_t cfg = {};
+  const int npanel = prm.N / 64;
+  cfg.gridDim = dim3(static_cast<unsigned>(npanel), static_cast<unsigned>((prm.R + kProjNoutRows - 1) / kProjNoutRows));
+  cfg.blockDim = dim3(mcb::kProjThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = static_cast<unsigned>(npanel);
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl ? 2 : 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, wm, xm, xm, prm);
+  g_launches++;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "linear launch (norm out)");
+  return MCB_OK;
+}
+
 template <int F>
 int launch_proj_f(bool norm, bool add, const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& dm,
                   const mcb::ProjParams& prm, bool pdl, cudaStream_t st) {
@@ -1248,33 +1326,52 @@ int mcb_sample(const mcb_sample_args* a, void* stream) {
   return MCB_OK;
 }
 
-int mcb_linear(const mcb_linear_args* a, void* stream) {
+}  // extern "C"
+
+// The checks of mcb_linear and its launch shape, without launching.
+struct LinearPlan {
+  int F, rb, panels;
+  bool norm, gated, add, nout;
+};
+
+int plan_linear(const mcb_linear_args* a, LinearPlan* pl) {
   if (a == nullptr) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: args is NULL");
   if (a->R < 0 || a->N <= 0 || a->K <= 0)
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: R=%d N=%d K=%d", a->R, a->N, a->K);
-  if (a->flags & ~(MCB_LINEAR_NORM | MCB_LINEAR_GATED))
+  if (a->flags & ~(MCB_LINEAR_NORM | MCB_LINEAR_GATED | MCB_LINEAR_NORM_OUT))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: flags %d", a->flags);
   const bool norm = (a->flags & MCB_LINEAR_NORM) != 0;
   const bool gated = (a->flags & MCB_LINEAR_GATED) != 0;
+  const bool nout = (a->flags & MCB_LINEAR_NORM_OUT) != 0;
   const bool add = a->delta != nullptr;
   if (add && !norm) return fail(MCB_ERR_INVALID_ARG, "mcb_linear: delta needs MCB_LINEAR_NORM");
   if (gated && (norm || add || a->res != nullptr))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: MCB_LINEAR_GATED takes no norm, delta or res");
+  if (nout && (norm || gated))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: MCB_LINEAR_NORM_OUT takes no other flag");
   if (gated && a->N % 16 != 0)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: gated N=%d must be a multiple of 16", a->N);
+  if (nout && (a->N % 64 != 0 || a->N > 64 * mcb::kMaxClusterSplits))
+    return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: MCB_LINEAR_NORM_OUT needs N a multiple of 64, at most %d (N=%d)",
+                64 * mcb::kMaxClusterSplits, a->N);
   if (a->R > mcb::kProjRows || a->K % 64 != 0 || (norm && a->K > 32 * 8 * mcb::kProjNormCpl))
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: R=%d (at most %d), K=%d (a multiple of 64%s)", a->R,
                 mcb::kProjRows, a->K, norm ? ", at most 1024 with the norm" : "");
-  if (a->x == nullptr || a->w == nullptr || a->y == nullptr || (add && a->x_out == nullptr))
+  if (a->x == nullptr || a->w == nullptr || a->y == nullptr || (add && a->x_out == nullptr) ||
+      (nout && a->h_out == nullptr))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: NULL pointer argument");
   if (a->x_stride < a->K || a->w_stride < a->K || a->y_stride < a->N ||
       (a->res != nullptr && a->res_stride < a->N) ||
-      (add && (a->delta_stride < a->K || a->x_out_stride < a->K)))
+      (add && (a->delta_stride < a->K || a->x_out_stride < a->K)) || (nout && a->h_out_stride < a->N))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: row strides shorter than the rows");
   if (!aligned(a->x, 16) || !aligned(a->w, 16) || !aligned(a->y, 2) || a->x_stride % 8 || a->w_stride % 8 ||
       (a->res != nullptr && !aligned(a->res, 2)) ||
       (add && (!aligned(a->delta, 16) || !aligned(a->x_out, 16) || a->delta_stride % 8 || a->x_out_stride % 8)))
     return fail(MCB_ERR_ALIGNMENT, "mcb_linear: x, delta, x_out and w rows must start on 16-byte boundaries");
+  if (nout && (!aligned(a->y, 16) || a->y_stride % 8 || !aligned(a->h_out, 16) || a->h_out_stride % 8 ||
+               (a->res != nullptr && (!aligned(a->res, 16) || a->res_stride % 8))))
+    return fail(MCB_ERR_ALIGNMENT, "mcb_linear: with MCB_LINEAR_NORM_OUT the y, res and h_out rows must start "
+                "on 16-byte boundaries");
   // every CTA reads all of x (and delta) while others write y and x_out
   if (ranges_overlap(a->y, a->y_stride, a->N, a->x, a->x_stride, a->K, a->R) ||
       ranges_overlap(a->res, a->res_stride, a->N, a->x, a->x_stride, a->K, a->R) ||
@@ -1283,19 +1380,55 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
                ranges_overlap(a->y, a->y_stride, a->N, a->delta, a->delta_stride, a->K, a->R) ||
                ranges_overlap(a->y, a->y_stride, a->N, a->x_out, a->x_out_stride, a->K, a->R))))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: y, res and x_out must not overlap x or delta");
+  if (nout && (ranges_overlap(a->h_out, a->h_out_stride, a->N, a->x, a->x_stride, a->K, a->R) ||
+               ranges_overlap(a->h_out, a->h_out_stride, a->N, a->y, a->y_stride, a->N, a->R) ||
+               ranges_overlap(a->h_out, a->h_out_stride, a->N, a->res, a->res_stride, a->N, a->R)))
+    return fail(MCB_ERR_INVALID_ARG, "mcb_linear: h_out must not overlap x, y or res");
   if (a->res != nullptr && a->res != a->y &&
       ranges_overlap(a->y, a->y_stride, a->N, a->res, a->res_stride, a->N, a->R))
     return fail(MCB_ERR_INVALID_ARG, "mcb_linear: res must be y itself or not overlap it");
-  const int panels = a->K / 64;
+  pl->panels = a->K / 64;
+  pl->norm = norm;
+  pl->gated = gated;
+  pl->add = add;
+  pl->nout = nout;
+  if (nout) {
+    pl->F = 64;
+    pl->rb = kProjNoutRows;
+    const int smem = mcb::proj_smem_bytes(64, pl->panels, false, kProjNoutRows);
+    if (smem > kMaxSmemOptin)
+      return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d does not fit the shared memory (norm out)", a->K);
+    if (!nout_schedulable(a->N / 64, smem))
+      return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: the device does not schedule clusters of %d CTAs with %d "
+                  "bytes of shared memory (norm out)", a->N / 64, smem);
+    return MCB_OK;
+  }
   // the narrower feature slice while it keeps the grid within about one CTA per SM (always with
   // delta: its panels leave no room for a wider weight slice)
   // gated: 16 gate and 16 up rows of W a CTA (the epilogue pairs them)
-  const int F = gated ? 32 : (add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32);
+  pl->F = gated ? 32 : (add || (a->N + 15) / 16 <= device_sm_count() + device_sm_count() / 8 ? 16 : 32);
   // a plain product whose 64-row activation block does not fit splits the rows over two CTAs
-  const int rb = (!norm && !gated && mcb::proj_smem_bytes(F, panels, false) > kMaxSmemOptin) ? 32 : mcb::kProjRows;
-  if (mcb::proj_smem_bytes(F, panels, add, rb) > kMaxSmemOptin)
+  pl->rb = (!norm && !gated && mcb::proj_smem_bytes(pl->F, pl->panels, false) > kMaxSmemOptin) ? 32
+                                                                                             : mcb::kProjRows;
+  if (mcb::proj_smem_bytes(pl->F, pl->panels, add, pl->rb) > kMaxSmemOptin)
     return fail(MCB_ERR_UNSUPPORTED, "mcb_linear: K=%d does not fit the shared memory (%d features a CTA%s)",
-                a->K, F, add ? ", with delta" : "");
+                a->K, pl->F, add ? ", with delta" : "");
+  return MCB_OK;
+}
+
+extern "C" {
+
+int mcb_linear_supported(const mcb_linear_args* a) {
+  LinearPlan pl;
+  return plan_linear(a, &pl) == MCB_OK ? 1 : 0;
+}
+
+int mcb_linear(const mcb_linear_args* a, void* stream) {
+  LinearPlan pl;
+  const int prc = plan_linear(a, &pl);
+  if (prc != MCB_OK) return prc;
+  const int F = pl.F, rb = pl.rb, panels = pl.panels;
+  const bool norm = pl.norm, gated = pl.gated, add = pl.add, nout = pl.nout;
   if (a->R == 0) return MCB_OK;
   CUtensorMap wm, xm, dm;
   int rc = gated ? encode_rows_map(&wm, a->w, 2ll * a->N, a->K, a->w_stride, F / 2)
@@ -1313,9 +1446,11 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   p.res = static_cast<const uint16_t*>(a->res);
   p.y = static_cast<uint16_t*>(a->y);
   p.x_out = add ? static_cast<uint16_t*>(a->x_out) : nullptr;
+  p.h_out = nout ? static_cast<uint16_t*>(a->h_out) : nullptr;
   p.ress = a->res_stride;
   p.ys = a->y_stride;
   p.xos = add ? a->x_out_stride : 0;
+  p.hs = nout ? a->h_out_stride : 0;
   p.R = a->R;
   p.N = a->N;
   p.K = a->K;
@@ -1325,6 +1460,7 @@ int mcb_linear(const mcb_linear_args* a, void* stream) {
   p.eps = a->eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
+  if (nout) return launch_proj_nout(wm, xm, p, pdl, st);
   if (gated) return launch_proj<32, false, false, true>(wm, xm, dm, p, pdl, st);
   if (rb == 32)
     return F == 16 ? launch_proj<16, false, false, false, 32>(wm, xm, dm, p, pdl, st)

@@ -13,7 +13,8 @@ import torch
 
 from . import _native
 from ._native import (AddNormArgs, AppendArgs, AttnArgs, CopyArgs, EmbedArgs, GatedSiluArgs,
-                      LINEAR_GATED, LINEAR_NORM, LinearArgs, SampleArgs, SoftcapArgs, check)
+                      LINEAR_GATED, LINEAR_NORM, LINEAR_NORM_OUT, LinearArgs, SampleArgs,
+                      SoftcapArgs, check)
 
 
 def _stream(t):
@@ -569,8 +570,49 @@ def sample(logits, uniforms, *, temperature=1.0, top_k=None, out=None):
 LINEAR_MAX_ROWS = 64
 
 
+def _linear_args(x, weight, out, res, norm, delta, x_out, eps, pdl, gated, h_out):
+    R, K = x.shape
+    N = weight.shape[0] // 2 if gated else weight.shape[0]
+    args = LinearArgs()
+    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
+    args.w, args.w_stride = weight.data_ptr(), _rows2d("weight", weight)
+    args.y, args.y_stride = out.data_ptr(), _rows2d("out", out)
+    if res is not None:
+        if tuple(res.shape) != (R, N):
+            raise RuntimeError(f"res must be ({R}, {N}), got {tuple(res.shape)}")
+        args.res, args.res_stride = res.data_ptr(), _rows2d("res", res)
+    if delta is not None:
+        if tuple(delta.shape) != (R, K):
+            raise RuntimeError(f"delta must be ({R}, {K}), got {tuple(delta.shape)}")
+        args.delta, args.delta_stride = delta.data_ptr(), _rows2d("delta", delta)
+        args.x_out, args.x_out_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
+    if h_out is not None:
+        if tuple(h_out.shape) != (R, N):
+            raise RuntimeError(f"h_out must be ({R}, {N}), got {tuple(h_out.shape)}")
+        args.h_out, args.h_out_stride = h_out.data_ptr(), _rows2d("h_out", h_out)
+    args.R, args.N, args.K = R, N, K
+    args.flags = ((LINEAR_NORM if norm else 0) | (LINEAR_GATED if gated else 0)
+                  | (LINEAR_NORM_OUT if h_out is not None else 0))
+    args.eps = rms_norm_eps(eps)
+    args.pdl = int(bool(pdl))
+    return args
+
+
+def linear_supported(x, weight, *, out=None, res=None, norm=False, delta=None, eps=None,
+                     gated=False, h_out=None):
+    """Whether linear() with these arguments runs on the current device (mcb_linear_supported:
+    the same host-side checks, nothing launched)."""
+    R, K = x.shape
+    N = weight.shape[0] // 2 if gated else weight.shape[0]
+    if out is None:
+        out = torch.empty((R, N), dtype=torch.bfloat16, device=x.device)
+    x_out = torch.empty((R, K), dtype=torch.bfloat16, device=x.device) if delta is not None else None
+    args = _linear_args(x, weight, out, res, norm, delta, x_out, eps, False, gated, h_out)
+    return bool(_native.load().mcb_linear_supported(ctypes.byref(args)))
+
+
 def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None, eps=None,
-           pdl=False, gated=False):
+           pdl=False, gated=False, h_out=None):
     """F.linear(x, weight) without bias (modelcore/components/linear.py:14) for the decode step's
     rows -- x (R, K) with R <= 64 and K a multiple of 64, weight (N, K), bf16, fp32 accumulation
     -- with the Block's elementwise ops around it fused in:
@@ -583,7 +625,11 @@ def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None,
                   modelcore/components/block.py:58); out may be res (in place);
       gated=True  weight is the packed [Wg; Wu] (2H, K) and out (R, H) = silu(x @ Wg^T) *
                   (x @ Wu^T) with mcb_gated_silu's rounding (GatedMLP, modelcore/components/
-                  mlp.py:89-90); H a multiple of 16, no norm, delta or res.
+                  mlp.py:89-90); H a multiple of 16, no norm, delta or res;
+      h_out       also h_out (R, N) = rms_norm(out, eps): c_proj's residual add and the Block's
+                  next norm (block.py:58-59) in one launch, the bits of add_rms_norm over out;
+                  N a multiple of 64 up to 1024, no norm, delta or gated (linear_supported says
+                  whether the device schedules it).
 
     pdl: launch with programmatic stream serialization (the weight slice streams in while the
     previous kernel finishes).  Returns out (R, N), or (x_out, out) with delta."""
@@ -597,25 +643,9 @@ def linear(x, weight, *, out=None, res=None, norm=False, delta=None, x_out=None,
         raise RuntimeError(f"weight must be (N, {K}), got {tuple(weight.shape)}")
     if out is None:
         out = torch.empty((R, N), dtype=torch.bfloat16, device=x.device)
-    args = LinearArgs()
-    args.x, args.x_stride = x.data_ptr(), _rows2d("x", x)
-    args.w, args.w_stride = weight.data_ptr(), _rows2d("weight", weight)
-    args.y, args.y_stride = out.data_ptr(), _rows2d("out", out)
-    if res is not None:
-        if tuple(res.shape) != (R, N):
-            raise RuntimeError(f"res must be ({R}, {N}), got {tuple(res.shape)}")
-        args.res, args.res_stride = res.data_ptr(), _rows2d("res", res)
-    if delta is not None:
-        if tuple(delta.shape) != (R, K):
-            raise RuntimeError(f"delta must be ({R}, {K}), got {tuple(delta.shape)}")
-        if x_out is None:
-            x_out = torch.empty((R, K), dtype=torch.bfloat16, device=x.device)
-        args.delta, args.delta_stride = delta.data_ptr(), _rows2d("delta", delta)
-        args.x_out, args.x_out_stride = x_out.data_ptr(), _rows2d("x_out", x_out)
-    args.R, args.N, args.K = R, N, K
-    args.flags = (LINEAR_NORM if norm else 0) | (LINEAR_GATED if gated else 0)
-    args.eps = rms_norm_eps(eps)
-    args.pdl = int(bool(pdl))
+    if delta is not None and x_out is None:
+        x_out = torch.empty((R, K), dtype=torch.bfloat16, device=x.device)
+    args = _linear_args(x, weight, out, res, norm, delta, x_out, eps, pdl, gated, h_out)
     check(_native.load().mcb_linear(ctypes.byref(args), _stream(x)))
     return (x_out, out) if delta is not None else out
 

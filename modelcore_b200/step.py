@@ -118,6 +118,18 @@ USE_LINEAR_PROJ = True
 # in its epilogue (one launch for two) and down_proj (its K, the MLP width, split over two CTAs a
 # row block), so that every projection of the layer is in the programmatic-dependent-launch chain
 USE_LINEAR_MLP = True
+# ... and c_proj's residual add and the next norm in one launch (mcb_linear's norm out: the CTAs
+# of a row form a thread-block cluster) where the device schedules it
+USE_LINEAR_NORM_OUT = True
+_NORM_OUT_OK = {}  # (device, rows, N, K) -> whether mcb_linear takes the norm out there
+
+
+def _norm_out_ok(x, w, out, res, h, eps):
+    key = (x.device.index, x.shape[0], w.shape[0], w.shape[1])
+    ok = _NORM_OUT_OK.get(key)
+    if ok is None:
+        ok = _NORM_OUT_OK[key] = ops.linear_supported(x, w, out=out, res=res, eps=eps, h_out=h)
+    return ok
 
 
 def qkv_projection(attn, x):
@@ -239,19 +251,20 @@ def _linear_ok(body, rows, T, x):
 
 
 def body_forward_linear(body, x2, h, kv_cache, B, T):
-    """body_forward with q|k|v and c_proj on mcb_linear (USE_LINEAR_PROJ):
+    """body_forward with the projections on mcb_linear (USE_LINEAR_PROJ):
 
         per block:  qkv = h @ [Wq; Wk; Wv]^T          mcb_linear (c_q alone for a layer that
                                                       reads another layer's slot)
                     append + attention                 (integration.attend)
-                    x = x + attn @ Wo^T                mcb_linear, the add in its epilogue
-                    h = norm(x)                        mcb_add_rms_norm
-                    gu = h @ [Wg; Wu]^T                cuBLAS
-                    a = silu(gu[:, :H]) * gu[:, H:]    mcb_gated_silu
-                    x, h = x + a @ Wd^T, norm(...)     cuBLAS, then mcb_add_rms_norm
+                    x = x + attn @ Wo^T, h = norm(x)   mcb_linear, the add and the norm in its
+                                                      epilogue (USE_LINEAR_NORM_OUT; else the
+                                                      add there and mcb_add_rms_norm)
+                    a = silu(h @ Wg^T) * (h @ Wu^T)    mcb_linear gated (USE_LINEAR_MLP; else
+                                                      cuBLAS and mcb_gated_silu)
+                    x, h = x + a @ Wd^T, norm(...)     mcb_linear, then mcb_add_rms_norm
 
-    The adds and the norms round as body_forward's; the two projections differ from cuBLAS's in
-    fp32 summation order only.  Returns the final residual (a new buffer) and its norm h."""
+    The adds and the norms round as body_forward's; the projections differ from cuBLAS's in fp32
+    summation order only.  Returns the final residual (a new buffer) and its norm h."""
     from .integration import attend
     rows, C = x2.shape
     resid = torch.empty_like(x2)
@@ -271,10 +284,14 @@ def body_forward_linear(body, x2, h, kv_cache, B, T):
             nk = attn.n_kv_head * hd
             k = qkv[:, nq:nq + nk].view(B, T, attn.n_kv_head, hd)
             v = qkv[:, nq + nk:].view(B, T, attn.n_kv_head, hd)
-        y = attend(attn, q, k, v, kv_cache)
-        ops.linear(y.reshape(rows, nq), attn.c_proj.weight, out=resid, res=src, pdl=True)
+        y = attend(attn, q, k, v, kv_cache).reshape(rows, nq)
+        wo = attn.c_proj.weight
+        if USE_LINEAR_NORM_OUT and _norm_out_ok(y, wo, resid, src, h, eps):
+            ops.linear(y, wo, out=resid, res=src, h_out=h, eps=eps, pdl=True)
+        else:
+            ops.linear(y, wo, out=resid, res=src, pdl=True)
+            ops.add_rms_norm(resid, eps=eps, h_out=h)
         src = resid
-        ops.add_rms_norm(resid, eps=eps, h_out=h)
         f = gated_mlp(ffn, h, linear=USE_LINEAR_MLP)
         ops.add_rms_norm(resid, f, eps=eps, x_out=resid, h_out=h)
     return resid, h

@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_its_abi_version():
     lib = _native.load()
-    assert lib.mcb_abi_version() == _native.ABI_VERSION == 8
+    assert lib.mcb_abi_version() == _native.ABI_VERSION == 9
 
 
 def test_every_declared_symbol_is_exported():
@@ -256,8 +256,27 @@ def test_linear_rejects_bad_arguments_on_the_host():
             setattr(a, k, v)
         return a
 
-    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=4)), None))
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=8)), None))
     assert st == _native.MCB_ERR_INVALID_ARG and "flags" in msg
+    assert lib.mcb_linear_supported(ctypes.byref(args())) == 1
+    assert lib.mcb_linear_supported(ctypes.byref(args(flags=8))) == 0
+    # the norm out: N a multiple of 64 up to 1024, no other flag, h_out given, aligned and apart
+    nout, h = _native.LINEAR_NORM_OUT, base + (3 << 20)
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=nout | _native.LINEAR_GATED, h_out=h,
+                                                    h_out_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "no other flag" in msg
+    for n in (96, 1088):
+        st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=nout, N=n, y_stride=n, h_out=h,
+                                                        h_out_stride=n)), None))
+        assert st == _native.MCB_ERR_UNSUPPORTED and "multiple of 64" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=nout)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "NULL" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=nout, h_out=h + 8, h_out_stride=768)), None))
+    assert st == _native.MCB_ERR_ALIGNMENT and "h_out" in msg
+    st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=nout, h_out=base + (2 << 20) + 64,
+                                                    h_out_stride=768)), None))
+    assert st == _native.MCB_ERR_INVALID_ARG and "h_out must not overlap" in msg
+    assert lib.mcb_linear_supported(ctypes.byref(args(flags=nout, h_out=h + 8, h_out_stride=768))) == 0
     # the gated projection stands alone: no norm, delta or res, and N a multiple of 16
     gated = _native.LINEAR_GATED
     st, msg = _err(lib.mcb_linear(ctypes.byref(args(flags=gated | _native.LINEAR_NORM)), None))

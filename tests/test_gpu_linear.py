@@ -187,3 +187,102 @@ def test_pdl_chain_in_a_cuda_graph(ops):
     torch.cuda.synchronize()
     assert ops.device_error()[0] == 0
     assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])
+
+
+NORM_OUT_SHAPES = [  # R, N, K: config 2's c_proj (clusters of 12), ragged rows, the widest
+    (64, 768, 768), (40, 768, 768), (1, 768, 768), (64, 1024, 512), (7, 128, 256), (64, 576, 1024),
+    (17, 64, 64),
+]
+
+
+@pytest.mark.parametrize("shape", NORM_OUT_SHAPES, ids=lambda s: "R{}N{}K{}".format(*s))
+def test_norm_out_is_the_residual_projection_then_add_rms_norm(ops, shape):
+    """h_out: the CTAs of one output row form a cluster and meet in distributed shared memory for
+    the norm.  y and h equal, bit for bit, the residual projection followed by mcb_add_rms_norm
+    over its output -- in place (out = res) and out of place, with and without PDL."""
+    R, N, K = shape
+    if not ops.linear_supported(torch.empty(R, K, device="cuda", dtype=torch.bfloat16),
+                                torch.empty(N, K, device="cuda", dtype=torch.bfloat16),
+                                h_out=torch.empty(R, N, device="cuda", dtype=torch.bfloat16)):
+        pytest.skip(f"the device does not schedule clusters of {N // 64}")
+    g = torch.Generator(device="cuda").manual_seed(R * 3 + N + K)
+    a = _rand(g, R, K)
+    w = _rand(g, N, K, scale=K ** -0.5)
+    res = _rand(g, R, N, scale=4.0)
+    want_y = ops.linear(a, w, res=res)
+    want_h = torch.empty_like(want_y)
+    ops.add_rms_norm(want_y, eps=1e-6, h_out=want_h)
+    y = torch.empty_like(res)
+    h = torch.empty_like(res)
+    ops.linear(a, w, out=y, res=res, h_out=h, eps=1e-6)
+    y2 = res.clone()
+    h2 = torch.full_like(res, 7.0)
+    ops.linear(a, w, out=y2, res=y2, h_out=h2, eps=1e-6, pdl=True)
+    # without a residual: h = rms_norm(bf16(a @ w^T))
+    y3 = torch.empty_like(res)
+    h3 = torch.empty_like(res)
+    ops.linear(a, w, out=y3, h_out=h3, eps=1e-6)
+    want_h3 = torch.empty_like(res)
+    ops.add_rms_norm(ops.linear(a, w), eps=1e-6, h_out=want_h3)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert torch.equal(y, want_y) and torch.equal(h, want_h)
+    assert torch.equal(y2, want_y) and torch.equal(h2, want_h)
+    assert torch.equal(h3, want_h3)
+
+
+def test_norm_out_rejects_what_it_does_not_cover(ops):
+    """N a multiple of 64 up to 1024 and no other flag; h_out apart from x, y and res."""
+    from modelcore_b200._native import McbError
+    a = torch.zeros(8, 128, device="cuda", dtype=torch.bfloat16)
+    for N in (96, 1088):
+        w = torch.zeros(N, 128, device="cuda", dtype=torch.bfloat16)
+        with pytest.raises(McbError, match="multiple of 64"):
+            ops.linear(a, w, h_out=torch.empty(8, N, device="cuda", dtype=torch.bfloat16))
+    w = torch.zeros(128, 128, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(8, 128, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(McbError, match="h_out must not overlap"):
+        ops.linear(a, w, out=y, h_out=y)
+    with pytest.raises(McbError, match="no other flag"):
+        ops.linear(a, w, norm=True, h_out=torch.empty(8, 128, device="cuda", dtype=torch.bfloat16))
+
+
+def test_norm_out_in_a_pdl_chain_in_a_cuda_graph(ops):
+    """The default decode layer's chain -- q|k|v, c_proj with the residual add and the norm,
+    gate|up with silu * up, down_proj, add + norm -- launched with programmatic dependent launch
+    and replayed in a graph: equal to the eager launches without PDL."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    h0 = _rand(g, 64, 768)
+    x0 = _rand(g, 64, 768, scale=4.0)
+    w_qkv = _rand(g, 2304, 768, scale=0.03)
+    w_o = _rand(g, 768, 768, scale=0.03)
+    w_gu = _rand(g, 4096, 768, scale=0.03)
+    w_d = _rand(g, 768, 2048, scale=0.02)
+    h = h0.clone()
+    x = x0.clone()
+    probe = ops.linear_supported(h0, w_o, out=x, res=x, h_out=h)
+    if not probe:
+        pytest.skip("the device does not schedule clusters of 12")
+
+    def layer(pdl):
+        h.copy_(h0)
+        x.copy_(x0)
+        qkv = ops.linear(h, w_qkv, pdl=pdl)
+        ops.linear(qkv[:, :768].contiguous(), w_o, out=x, res=x, h_out=h, eps=1e-6, pdl=pdl)
+        act = ops.linear(h, w_gu, gated=True, pdl=pdl)
+        f = ops.linear(act, w_d, pdl=pdl)
+        ops.add_rms_norm(x, f, eps=1e-6, x_out=x, h_out=h)
+        return x.clone(), h.clone()
+
+    want = layer(False)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(graph, stream=side):
+        got = layer(True)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])

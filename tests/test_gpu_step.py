@@ -289,15 +289,18 @@ def test_fused_step_decode_is_as_accurate_as_the_reference(env, name):
     assert e_fused <= 1.25 * e_ref + 1e-3
 
 
-PROJ_MODES = ["cublas", "linear", "fused_proj"]
+PROJ_MODES = ["cublas", "linear", "linear_norm_out", "fused_proj"]
 
 
 def _set_proj_mode(step, monkeypatch, mode):
-    """cublas: every projection on cuBLAS; linear: q|k|v and c_proj (+ residual) on mcb_linear
-    (USE_LINEAR_PROJ, the default); fused_proj: the projections on mcb_linear with the norms and
-    adds fused into them (USE_FUSED_PROJ)."""
+    """cublas: every projection on cuBLAS; linear: every projection on mcb_linear, c_proj with the
+    residual add in its epilogue (USE_LINEAR_PROJ) and the norm after it a launch of its own;
+    linear_norm_out: the same with c_proj's norm in its epilogue too (USE_LINEAR_NORM_OUT, the
+    default); fused_proj: the projections on mcb_linear with the norms and adds fused into them
+    (USE_FUSED_PROJ)."""
     monkeypatch.setattr(step, "USE_FUSED_PROJ", mode == "fused_proj")
-    monkeypatch.setattr(step, "USE_LINEAR_PROJ", mode == "linear")
+    monkeypatch.setattr(step, "USE_LINEAR_PROJ", mode in ("linear", "linear_norm_out"))
+    monkeypatch.setattr(step, "USE_LINEAR_NORM_OUT", mode == "linear_norm_out")
 
 
 @pytest.mark.parametrize("mode", PROJ_MODES)
@@ -336,6 +339,11 @@ def test_fused_step_launches_and_graph_replay(env, mode, monkeypatch):
             # with silu * up in its epilogue, down_proj, the add + norm and the append, the
             # advance, the LM-head epilogue
             attn_launches = per_step - (1 + 4 * (6 + append) + 1 + 1)
+        elif mode == "linear_norm_out":
+            # the same with the norm inside c_proj's launch, where the device schedules it
+            if not all(step._NORM_OUT_OK.values()):
+                pytest.skip("the device does not schedule mcb_linear's norm-out clusters")
+            attn_launches = per_step - (1 + 4 * (5 + append) + 1 + 1)
         else:
             # embedding + first norm, per layer two add + norms, silu * up and the append, the
             # advance, the LM-head epilogue

@@ -209,8 +209,10 @@ def _build_decoder(rank, world, steps_needed, fuse_step=True):
     begin, end = contiguous_rows(ROWS_PER_GPU * world, world, rank)
     mine = all_prompts[begin:end].tolist()
     with torch.inference_mode():
-        # one warm-up prefill (kernel modules, cuBLAS heuristics), then the timed one
-        mgr.new_decoder(model, mine[:2], max_tokens=8, cuda_graph=True)
+        # one warm-up prefill of the same prompts and cache (kernel modules, cuBLAS heuristics for
+        # these shapes, the allocator's blocks), then the timed one
+        warm = mgr.new_decoder(model, mine, max_tokens=DECODE_LEN, cuda_graph=True)
+        del warm
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         dec = mgr.new_decoder(model, mine, max_tokens=DECODE_LEN, cuda_graph=True)
@@ -225,6 +227,10 @@ def _per_prompt_prefill_ms(mgr, model, prompts):
     prefill_row), on the B200 kernels: wall time in ms."""
     import torch
     with torch.inference_mode():
+        # warm-up: the batch-1 shapes of this order (cuBLAS heuristics, kernel modules)
+        warm = mgr.new_decoder(model, prompts[:2], max_tokens=DECODE_LEN, cuda_graph=True,
+                               batched_prefill=False)
+        del warm
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         mgr.new_decoder(model, prompts, max_tokens=DECODE_LEN, cuda_graph=True, batched_prefill=False)

@@ -643,7 +643,7 @@ def _prefill(tflops_peak):
             if i:
                 ts.append(a.elapsed_time(b) * 1e3)
         us = statistics.median(ts)
-        rows.append({"workload": name, "kernel": "mcb::prefill_attn_kernel<%d>" % D, "us": round(us, 1),
+        rows.append({"workload": name, "kernel": ops.last_attn_kernel(), "us": round(us, 1),
                      "tflops": round(flops / us / 1e6, 1),
                      "frac": round(flops / us / 1e6 / tflops_peak, 3)})
         del q, kc, vc, out

@@ -36,6 +36,8 @@ void note_attn_kernel(const char* name, int D, int nqt, int stages, bool fp8) {
   if (nqt > 0)
     snprintf(g_last_attn_kernel, sizeof(g_last_attn_kernel), "mcb::%s<%d,%d,16,%d%s>", name, D, nqt,
              stages, fp8 ? ",true" : "");
+  else if (stages > 0)  // the prefill kernel: stages carries its query tiles an item
+    snprintf(g_last_attn_kernel, sizeof(g_last_attn_kernel), "mcb::%s<%d,%d>", name, D, stages);
   else
     snprintf(g_last_attn_kernel, sizeof(g_last_attn_kernel), "mcb::%s<%d>", name, D);
 }
@@ -191,18 +193,18 @@ constexpr int kAppendVecCtasPerSm = 4;
 // kernel (prefill_attn.cuh) runs instead: 128-query tiles on tcgen05, no workspace.
 constexpr int kPrefillMinT = 64;
 
-template <int D>
+template <int D, int QT>
 struct PrefillVariant {
-  using Cfg = mcb::PrefillConfig<D>;
-  static constexpr auto kernel = mcb::prefill_attn_kernel<D>;
+  using Cfg = mcb::PrefillConfig<D, QT>;
+  static constexpr auto kernel = mcb::prefill_attn_kernel<D, QT>;
   static int launch(long long grid, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                     const mcb::PrefillParams& prm, cudaStream_t st) {
     static std::atomic<uint64_t> done{0};
     cudaError_t e = ensure_smem(kernel, Cfg::kSmem, done);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_attn)");
-    kernel<<<static_cast<unsigned>(grid), mcb::kPfThreads, Cfg::kSmem, st>>>(qm, km, vm, prm);
+    kernel<<<static_cast<unsigned>(grid), mcb::pf_threads<QT>(), Cfg::kSmem, st>>>(qm, km, vm, prm);
     g_launches++;
-    note_attn_kernel("prefill_attn_kernel", D, 0, 0, false);
+    note_attn_kernel("prefill_attn_kernel", D, 0, QT, false);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "prefill_attn launch");
     return MCB_OK;
@@ -741,16 +743,19 @@ int run_prefill(const mcb_attn_args* a, cudaStream_t st) {
   p.G = a->Hq / a->Hkv;
   p.Tmax = a->Tmax;
   p.window = a->window;
-  p.n_qpairs = (a->T + 2 * mcb::kPfTile - 1) / (2 * mcb::kPfTile);
+  // head size 64: one query tile an item, two CTAs per SM (independent chains); 128: pairs
+  const int qt = a->D == 64 ? 1 : 2;
+  p.n_qgroups = (a->T + qt * mcb::kPfTile - 1) / (qt * mcb::kPfTile);
   p.ring = a->ring != 0;
   p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
-  const long long items = static_cast<long long>(p.n_qpairs) * a->B * a->Hq;
+  const long long items = static_cast<long long>(p.n_qgroups) * a->B * a->Hq;
   if (items > INT32_MAX) return fail(MCB_ERR_UNSUPPORTED, "mcb_prefill_attn: %lld work items", items);
   p.n_items = static_cast<int>(items);
-  // persistent: one CTA per SM (each holds all of its SM's TMEM), items strided over them
-  const long long grid = std::min<long long>(items, device_sm_count());
-  if (a->D == 64) return PrefillVariant<64>::launch(grid, qm, km, vm, p, st);
-  return PrefillVariant<128>::launch(grid, qm, km, vm, p, st);
+  // persistent: QT = 2, one CTA per SM (each holds all of its SM's TMEM); QT = 1, two per SM
+  // (256 TMEM columns each); items dealt over them
+  const long long grid = std::min<long long>(items, static_cast<long long>(3 - qt) * device_sm_count());
+  if (a->D == 64) return PrefillVariant<64, 1>::launch(grid, qm, km, vm, p, st);
+  return PrefillVariant<128, 2>::launch(grid, qm, km, vm, p, st);
 }
 
 // Encodes the tensor maps, fills the kernel parameters with the workspace `ws` (and, for the

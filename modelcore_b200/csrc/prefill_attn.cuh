@@ -9,7 +9,11 @@
 // A work item is two 128-query tiles (Q0, Q1: 256 consecutive queries) of one q head of one row;
 // its CTA walks 128-key tiles, each K/V tile serving both query tiles.  The grid is persistent
 // (one CTA per SM, items strided over the CTAs, longest first), so TMEM allocation, barrier setup
-// and the pipeline fill are paid once per CTA and the next item's loads overlap this one's end:
+// and the pipeline fill are paid once per CTA and the next item's loads overlap this one's end.
+// The QT = 1 copy (head size 64) takes one query tile an item with six warps (no Q1 softmax
+// warps) and 256 TMEM columns, two CTAs per SM: the two query-tile chains of an SM are then
+// independent -- neither waits for the other's extra causal key tile or epilogue, at the price
+// of K/V tiles read once per query tile instead of once per pair.  The roles (QT = 2):
 //
 //   warp 0       TMA producer: per item Q0 and Q1 (double-buffered for D = 64), then K_j and V_j
 //                into a two-stage ring that runs on across items
@@ -31,7 +35,8 @@
 // that held P_j once PV_j was issued before it, and a completed S_{j+1} implies a completed PV_j
 // (the softmax warps rescale O only then).
 //
-// TMEM: S0 columns [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).  Every wait is
+// TMEM: S0 columns [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D) (QT = 1: S0, then
+// O0 at 128).  Every wait is
 // bounded (2 s); a timeout raises the CTA's abort flag, every later wait returns at once, the MMA
 // issuer waits (bounded) for its committed MMAs, and TMEM is freed before the CTA exits.
 #pragma once
@@ -41,8 +46,12 @@
 namespace mcb {
 
 constexpr int kPfTile = 128;          // queries per query tile and keys per key tile
-constexpr int kPfThreads = 320;       // 10 warps
-constexpr uint32_t kPfTmemCols = 512;
+// QT query tiles an item (2: one CTA per SM, ten warps, all 512 TMEM columns; 1: two CTAs per SM,
+// six warps and 256 TMEM columns each, every query tile an independent chain)
+template <int QT>
+__host__ __device__ constexpr int pf_threads() { return (2 + 4 * QT) * 32; }
+template <int QT>
+__host__ __device__ constexpr uint32_t pf_tmem_cols() { return 256u * QT; }
 
 // ---------------------------------------------------------------------------------------------
 // tcgen05 helpers
@@ -201,26 +210,30 @@ struct PrefillParams {
   uint16_t* out;              // (B, T, Hq, D) bf16 contiguous
   const int* cache_seqlens;   // (B,) positions before the new tokens
   int B, T, Hq, Hkv, G, Tmax, window;
-  int n_qpairs;               // ceil(T / 256)
-  int n_items;                // n_qpairs * B * Hq work items: one (query-tile pair, row, q head) each
+  int n_qgroups;              // ceil(T / (QT * 128)): query-tile groups (pairs, or single tiles) a row
+  int n_items;                // n_qgroups * B * Hq work items: one (query-tile group, row, q head) each
   float scale_log2;           // softmax_scale * log2(e)
   int ring;                   // the slot is a ring of Tmax positions (key c at index c % Tmax)
 };
 
-template <int D>
+template <int D, int QT>
 struct PrefillConfig {
   static constexpr int kPanels = D / 64;
   static constexpr int kTileBytes = kPanels * kPfTile * 128;  // one Q / K / V tile
-  // Q (the pair Q0, Q1) is double-buffered where shared memory allows it (D = 64): the next
+  // Q (the item's QT tiles) is double-buffered where shared memory allows it (D = 64): the next
   // item's queries land while this item's last MMAs still read the current ones
   static constexpr int kQBufs = D <= 64 ? 2 : 1;
-  static constexpr int kQOff = 0;                                  // [kQBufs][Q0, Q1]
-  static constexpr int kKOff = kQOff + kQBufs * 2 * kTileBytes;    // K ring, 2 stages
+  static constexpr int kQOff = 0;                                  // [kQBufs][QT tiles]
+  static constexpr int kKOff = kQOff + kQBufs * QT * kTileBytes;   // K ring, 2 stages
   static constexpr int kVOff = kKOff + 2 * kTileBytes;             // V ring, 2 stages
   static constexpr int kBarOff = kVOff + 2 * kTileBytes;
   static constexpr int kBytes = kBarOff + 256;
-  // at least 116 KB so two CTAs never share an SM: each holds all 512 TMEM columns
-  static constexpr int kSmem = (kBytes + 1024 > 118784 ? kBytes + 1024 : 118784);
+  // TMEM bounds the CTAs an SM holds (QT = 2: all 512 columns; QT = 1: 256, two CTAs): the
+  // shared memory keeps a third CTA off the SM (more than a third of its 228 KB for QT = 1,
+  // more than half for QT = 2), so no CTA ever waits in tcgen05.alloc for another to finish
+  static constexpr int kMinSmem = QT == 2 ? 118784 : 78848;
+  static constexpr int kSmem = (kBytes + 1024 > kMinSmem ? kBytes + 1024 : kMinSmem);
+  static constexpr uint32_t kOCol = QT * kPfTile;                  // O0 (and O1) after the S tiles
 };
 
 // The first key tile a query tile needs and how many tiles (from k_first) it spans.
@@ -228,31 +241,32 @@ struct QTileRange {
   int qbase, j_begin, j_end;  // key tiles [j_begin, j_end) of the item's walk
 };
 
-// Work item i: query-tile pair qp (longest pairs first, so the short tail items fill the gaps
-// at the end) of row b, q head h.
+// Work item i: query-tile group qp -- QT consecutive query tiles -- (longest groups first, so the
+// short tail items fill the gaps at the end) of row b, q head h; rng[1] is empty for QT = 1.
 struct PfItem {
   int b, h, hk, L, q0, k_first, nkv;
   bool in_range;
   QTileRange rng[2];
 };
 
+template <int QT>
 __device__ __forceinline__ PfItem prefill_item(const PrefillParams& p, int i) {
   PfItem it;
   const int bh = p.B * p.Hq;
-  const int qp = p.n_qpairs - 1 - i / bh;
+  const int qp = p.n_qgroups - 1 - i / bh;
   it.b = (i % bh) / p.Hq;
   it.h = (i % bh) % p.Hq;
   it.hk = it.h / p.G;
   it.L = p.cache_seqlens[it.b];
-  it.q0 = qp * 2 * kPfTile;
-  const int pos_last = it.L + min(it.q0 + 2 * kPfTile, p.T) - 1;
+  it.q0 = qp * QT * kPfTile;
+  const int pos_last = it.L + min(it.q0 + QT * kPfTile, p.T) - 1;
   it.in_range = it.L >= 0 && (p.ring || pos_last < p.Tmax);
   it.k_first = (p.window >= 0 ? max(0, it.L + it.q0 - p.window) : 0) / kPfTile * kPfTile;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int qb = it.q0 + t * kPfTile;
     it.rng[t].qbase = qb;
-    if (!it.in_range || qb >= p.T) {
+    if (!it.in_range || qb >= p.T || t >= QT) {
       it.rng[t].j_begin = it.rng[t].j_end = 0;
     } else {
       const int first = (p.window >= 0 ? max(0, it.L + qb - p.window) : 0) / kPfTile * kPfTile;
@@ -282,12 +296,12 @@ __device__ __forceinline__ int prefill_round_item(const PrefillParams& p, int r)
 // even one with no query tile in an item (T <= 128), can find o_done two phases ahead.
 // 168 registers a thread: the 10 warps land three to a sub-partition on two of the four, whose
 // 16,384 registers each cap a thread at 170 (a higher cap fails to launch); a few bytes spill.
-template <int D>
-__global__ void __launch_bounds__(kPfThreads, 1)
+template <int D, int QT>
+__global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
-  using Cfg = PrefillConfig<D>;
+  using Cfg = PrefillConfig<D, QT>;
   constexpr int QB = Cfg::kQBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -301,7 +315,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* s_full = bars + 10;   // [2] per query tile
   uint64_t* p_full = bars + 12;   // [2] per query tile, 128 arrivals
   uint64_t* o_done = bars + 14;
-  uint64_t* epi_done = bars + 15;  // 256 arrivals: every softmax thread, once per item
+  uint64_t* epi_done = bars + 15;  // 128 QT arrivals: every softmax thread, once per item
   uint64_t* drained = bars + 16;
   constexpr int kNumBars = 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -311,12 +325,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bars + i, (i == 12 || i == 13) ? 128 : (i == 15 ? 256 : 1));
+      mbar_init(bars + i, (i == 12 || i == 13) ? 128 : (i == 15 ? 128 * QT : 1));
     *abort_flag = 0;
     fence_mbarrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kPfTmemCols);
+    tmem_alloc(tmem_slot, pf_tmem_cols<QT>());
     tmem_relinquish();
   }
   tc_fence_before();
@@ -338,17 +352,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
       if (i < 0) continue;
-      const PfItem it = prefill_item(p, i);
+      const PfItem it = prefill_item<QT>(p, i);
       if (!it.in_range) record_error(kErrPositionBeyondCache);
       if (it.nkv == 0) continue;
       const int qb = k % QB, qn = k / QB;
       if (qn > 0 && !mbar_wait_or_abort(&q_empty[qb], (qn - 1) & 1, abort_flag)) break;
-      mbar_arrive_expect_tx(&q_full[qb], 2 * Cfg::kTileBytes);
+      mbar_arrive_expect_tx(&q_full[qb], QT * Cfg::kTileBytes);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < QT; ++t)
 #pragma unroll
         for (int pn = 0; pn < Cfg::kPanels; ++pn)
-          tma_load_4d(smem + Cfg::kQOff + (qb * 2 + t) * Cfg::kTileBytes + pn * kPfTile * 128, &qmap,
+          tma_load_4d(smem + Cfg::kQOff + (qb * QT + t) * Cfg::kTileBytes + pn * kPfTile * 128, &qmap,
                       &q_full[qb], pn * 64, it.h, it.q0 + t * kPfTile, it.b, pol);
       q_last[qb] = qn;
       for (int j = 0; j < it.nkv; ++j, ++g) {
@@ -392,7 +406,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
       if (i < 0) continue;
-      const PfItem it = prefill_item(p, i);
+      const PfItem it = prefill_item<QT>(p, i);
       if (it.nkv == 0) continue;
       const int qb = k % QB;
       ok = mbar_wait_or_abort(&q_full[qb], (k / QB) & 1, abort_flag);
@@ -409,7 +423,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           k_waited = j;
         }
         tc_fence_after();
-        const uint32_t q_base = base + Cfg::kQOff + (qb * 2 + t) * Cfg::kTileBytes;
+        const uint32_t q_base = base + Cfg::kQOff + (qb * QT + t) * Cfg::kTileBytes;
         const uint32_t k_base = base + Cfg::kKOff + (gj & 1) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -432,7 +446,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t v_base = base + Cfg::kVOff + (gj & 1) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < kPfTile / 16; ++kk)
-          umma_ts(tmem + 256 + t * D, tmem + t * kPfTile + kk * 8,
+          umma_ts(tmem + Cfg::kOCol + t * D, tmem + t * kPfTile + kk * 8,
                   smem_desc_sw128(v_base + kk * 16 * 128, kPfTile * 128, 1024), idesc_o,
                   (pv_item[t] > 0 || kk > 0) ? 1u : 0u);
         ++pv_item[t];
@@ -463,14 +477,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int row = quarter * 32 + lane;          // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * kPfTile;
-    const uint32_t o_addr = tmem + lane_off + 256 + t * D;
+    const uint32_t o_addr = tmem + lane_off + Cfg::kOCol + t * D;
     int k = 0;       // items done
     int s_cnt = 0;   // S tiles of this query tile consumed (s_full phases)
     bool ok = true;
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
       if (i < 0) continue;
-      const PfItem it = prefill_item(p, i);
+      const PfItem it = prefill_item<QT>(p, i);
       if (it.nkv == 0) continue;
       // scalars, not it.rng[t]: a runtime index would put the array in local memory
       const int qbase = t ? it.rng[1].qbase : it.rng[0].qbase;
@@ -586,7 +600,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, kPfTmemCols);
+    tmem_dealloc(tmem, pf_tmem_cols<QT>());
   }
 }
 

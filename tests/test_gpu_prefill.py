@@ -73,6 +73,10 @@ CASES = [
     (3, 64, 8, 2, 128, [0, 1000, 333], 257, 1100),
     (1, 513, 12, 12, 64, [0], -1, 1024),      # config 2's prompt length
     (2, 97, 16, 4, 128, [4000, 7], 1024, 4100),
+    # head size 64 takes one query tile an item, two CTAs an SM: more items than CTAs, ragged
+    # prefixes, GQA, a window
+    (8, 640, 16, 4, 64, [0, 3, 129, 700, 1, 0, 64, 900], -1, 1600),
+    (4, 700, 12, 12, 64, [0, 10, 500, 1000], 300, 2048),
 ]
 
 

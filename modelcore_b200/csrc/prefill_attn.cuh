@@ -233,7 +233,12 @@ struct PrefillConfig {
   // more than half for QT = 2), so no CTA ever waits in tcgen05.alloc for another to finish
   static constexpr int kMinSmem = QT == 2 ? 118784 : 78848;
   static constexpr int kSmem = (kBytes + 1024 > kMinSmem ? kBytes + 1024 : kMinSmem);
-  static constexpr uint32_t kOCol = QT * kPfTile;                  // O0 (and O1) after the S tiles
+  // TMEM columns.  QT = 2: S0, S1, then O0, O1; P is written over S.  QT = 1: S, then P (packed
+  // bf16, 64 columns) apart from S, then O -- 256 columns for head size 64 -- so the next S can be
+  // computed while the softmax still works on this one.
+  static constexpr uint32_t kPCol = QT == 1 ? kPfTile : 0;
+  static constexpr uint32_t kOCol = QT == 1 ? kPfTile + kPfTile / 2 : QT * kPfTile;
+  static_assert(QT == 2 || D == 64, "one query tile an item: S, P and O in 256 TMEM columns");
 };
 
 // The first key tile a query tile needs and how many tiles (from k_first) it spans.
@@ -317,7 +322,9 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
   uint64_t* o_done = bars + 14;
   uint64_t* epi_done = bars + 15;  // 128 QT arrivals: every softmax thread, once per item
   uint64_t* drained = bars + 16;
-  constexpr int kNumBars = 17;
+  uint64_t* s_free = bars + 17;    // QT = 1: the softmax has read S (128 arrivals)
+  uint64_t* pv_done = bars + 18;   // QT = 1: a P V product has completed (P and O free again)
+  constexpr int kNumBars = 19;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars + 1);
 
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bars + i, (i == 12 || i == 13) ? 128 : (i == 15 ? 128 * QT : 1));
+      mbar_init(bars + i, (i == 12 || i == 13 || i == 17) ? 128 : (i == 15 ? 128 * QT : 1));
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -402,6 +409,7 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
     int g = 0;                   // K/V tiles consumed by earlier items
     int k = 0;                   // items done
     int pv_total[2] = {0, 0};    // PV MMAs issued per query tile (p_full phases)
+    int s_all = 0;               // QT = 1: S MMAs issued (s_free phases)
     bool ok = true;
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
@@ -446,21 +454,40 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
         const uint32_t v_base = base + Cfg::kVOff + (gj & 1) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < kPfTile / 16; ++kk)
-          umma_ts(tmem + Cfg::kOCol + t * D, tmem + t * kPfTile + kk * 8,
+          umma_ts(tmem + Cfg::kOCol + t * D, tmem + (QT == 1 ? Cfg::kPCol : t * kPfTile) + kk * 8,
                   smem_desc_sw128(v_base + kk * 16 * 128, kPfTile * 128, 1024), idesc_o,
                   (pv_item[t] > 0 || kk > 0) ? 1u : 0u);
         ++pv_item[t];
         ++pv_total[t];
         return true;
       };
-      if (ok && active(0, 0)) ok = issue_s(0, 0);
-      if (ok && active(1, 0)) ok = issue_s(1, 0);
-      for (int j = 0; ok && j < it.nkv; ++j) {
-        if (ok && active(0, j)) ok = issue_pv(0, j);
-        if (ok && active(0, j + 1)) ok = issue_s(0, j + 1);
-        if (ok && active(1, j)) ok = issue_pv(1, j);
-        if (ok) umma_commit(&kv_empty[(g + j) & 1]);
-        if (ok && active(1, j + 1)) ok = issue_s(1, j + 1);
+      if constexpr (QT == 1) {
+        // S_{j+1} goes in as soon as the softmax has read S_j (s_free: P has columns of its own),
+        // so it runs while the softmax exponentiates; P_j V_j follows once P_j is written
+        auto issue_s1 = [&](int j) -> bool {
+          if (s_all > 0 && !mbar_wait_or_abort(s_free, (s_all - 1) & 1, abort_flag)) return false;
+          ++s_all;
+          return issue_s(0, j);
+        };
+        if (ok) ok = issue_s1(0);
+        for (int j = 0; ok && j < it.nkv; ++j) {
+          if (ok && j + 1 < it.nkv) ok = issue_s1(j + 1);
+          if (ok) ok = issue_pv(0, j);
+          if (ok) {
+            umma_commit(pv_done);
+            umma_commit(&kv_empty[(g + j) & 1]);
+          }
+        }
+      } else {
+        if (ok && active(0, 0)) ok = issue_s(0, 0);
+        if (ok && active(1, 0)) ok = issue_s(1, 0);
+        for (int j = 0; ok && j < it.nkv; ++j) {
+          if (ok && active(0, j)) ok = issue_pv(0, j);
+          if (ok && active(0, j + 1)) ok = issue_s(0, j + 1);
+          if (ok && active(1, j)) ok = issue_pv(1, j);
+          if (ok) umma_commit(&kv_empty[(g + j) & 1]);
+          if (ok && active(1, j + 1)) ok = issue_s(1, j + 1);
+        }
       }
       if (ok && k > 0) ok = mbar_wait_or_abort(epi_done, (k - 1) & 1, abort_flag);
       if (ok) umma_commit(o_done);
@@ -478,8 +505,10 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * kPfTile;
     const uint32_t o_addr = tmem + lane_off + Cfg::kOCol + t * D;
+    const uint32_t p_addr = QT == 1 ? tmem + lane_off + Cfg::kPCol : s_addr;  // P: over S for QT = 2
     int k = 0;       // items done
     int s_cnt = 0;   // S tiles of this query tile consumed (s_full phases)
+    int pv_seen = 0; // QT = 1: P V products observed (pv_done phases), one per tile
     bool ok = true;
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
@@ -506,6 +535,10 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
         const int k0 = it.k_first + j * kPfTile;
         uint32_t sr[128];
         tmem_ld128(s_addr, sr);  // one round trip: TMEM load latency dominates a chunked read
+        if constexpr (QT == 1) {  // S is read: the issuer may compute the next one into it
+          tc_fence_before();
+          mbar_arrive(s_free);
+        }
         // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
         float mx = -INFINITY;
         const bool full = k0 + kPfTile - 1 <= L + qbase &&
@@ -529,6 +562,17 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
           m_used = mx;
           l *= alpha;
         }
+        if constexpr (QT == 1) {
+          // the previous tile's P V has completed before P is rewritten and O rescaled
+          if (cnt > 0) {
+            if (!__all_sync(0xffffffffu, mbar_wait_or_abort(pv_done, pv_seen & 1, abort_flag))) {
+              ok = false;
+              break;
+            }
+            ++pv_seen;
+            tc_fence_after();
+          }
+        }
         const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
         const uint64_t sc2 = pair_f32(p.scale_log2, p.scale_log2), nm2 = pair_f32(neg_m, neg_m);
         float sum0 = 0.f, sum1 = 0.f;
@@ -548,7 +592,7 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
             sr[32 * c + 2 * u] = pack_bf16x2_rn(e0, e1);
             sr[32 * c + 2 * u + 1] = pack_bf16x2_rn(e2, e3);
           }
-          tmem_st16_nowait(s_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
+          tmem_st16_nowait(p_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
         }
         const float sum = sum0 + sum1;
         l += sum;
@@ -566,7 +610,14 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
         tc_fence_before();
         mbar_arrive(&p_full[t]);
       }
-      // epilogue: O / l -> bf16 -> out[b, q, h, :]; every item's o_done phase is observed
+      // epilogue: O / l -> bf16 -> out[b, q, h, :]; every item's o_done phase is observed (QT = 1:
+      // and the pv_done phase of its last P V, so that one phase is observed per tile)
+      if constexpr (QT == 1) {
+        if (ok && cnt > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait_or_abort(pv_done, pv_seen & 1, abort_flag))) ok = false;
+          ++pv_seen;
+        }
+      }
       if (ok && !__all_sync(0xffffffffu, mbar_wait_or_abort(o_done, k & 1, abort_flag))) ok = false;
       if (ok && cnt > 0) {
         tc_fence_after();

@@ -173,6 +173,10 @@ def _dist_setup(n_gpus):
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     torch.cuda.set_device(local)
     if world > 1:
+        # NCCL's init lines (one per rank, with the communicator's rank count) stay in the log,
+        # so a reader of the run can count the ranks that joined; a caller's own setting wins
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     return rank, world, local

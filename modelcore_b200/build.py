@@ -63,12 +63,61 @@ def build(force=False, verbose=False, lib_path=LIB_PATH):
     return lib_path
 
 
+TORCH_OPS_PATH = os.path.join(PKG_DIR, "libmcb200_torch.so")
+TORCH_OPS_SRC = os.path.join(CSRC, "torch_ops.cpp")
+
+
+def torch_ops_needs_build(path=TORCH_OPS_PATH):
+    if not os.path.exists(path):
+        return True
+    t = os.path.getmtime(path)
+    deps = (TORCH_OPS_SRC, os.path.join(INCLUDE, "mcb200.h"), LIB_PATH)
+    return any(os.path.getmtime(s) > t for s in deps)
+
+
+def _torch_paths():
+    import torch.utils.cpp_extension as ce
+    try:
+        incs = ce.include_paths(device_type="cuda")
+    except TypeError:
+        incs = ce.include_paths(cuda=True)
+    import torch
+    return incs, os.path.join(os.path.dirname(torch.__file__), "lib")
+
+
+def build_torch_ops(force=False, path=TORCH_OPS_PATH):
+    """Compiles csrc/torch_ops.cpp -- the torch.ops.mcb200 operators over the C ABI -- against the
+    installed torch into path (default: modelcore_b200/libmcb200_torch.so), linked to
+    libmcb200.so beside it (built first when missing or stale)."""
+    build()
+    if not force and not torch_ops_needs_build(path):
+        return path
+    import torch
+    incs, torch_lib = _torch_paths()
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("no C++ compiler found to build libmcb200_torch.so")
+    tmp = path + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"]
+    for inc in incs:
+        cmd += ["-isystem", inc]
+    cmd += [TORCH_OPS_SRC, "-o", tmp, "-L", torch_lib, "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+            "-ltorch_cuda", "-L", PKG_DIR, "-lmcb200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("c++ failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    os.replace(tmp, path)
+    return path
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill usage")
     args = ap.parse_args(argv)
     print(build(force=args.force, verbose=args.verbose))
+    print(build_torch_ops(force=args.force))
 
 
 if __name__ == "__main__":

@@ -40,6 +40,18 @@ def _fusable(attn, x):
 # The decode step's append and attention in one launch where the plan allows it (T = 1, a bf16
 # slot, the split or persistent plan; ops.append_attn), with the bits of the two launches.
 USE_FUSED_APPEND = True
+# ... through the torch.ops.mcb200 operator (C++ over the same library: a third of the host cost
+# of the ctypes call, which an eager, ungraphed decode step pays once per layer) for bf16 slots
+USE_TORCH_OPS = True
+_TORCH_OPS = None
+
+
+def _torch_ops():
+    global _TORCH_OPS
+    if _TORCH_OPS is None:
+        from . import torch_ops  # loads libmcb200_torch.so; fails loudly when it is missing
+        _TORCH_OPS = torch.ops.mcb200
+    return _TORCH_OPS
 
 
 def attend(self, q, k, v, kv_cache):
@@ -54,6 +66,11 @@ def attend(self, q, k, v, kv_cache):
     seqlens = kv_cache.cache_seqlens
     rope = self.rope
     kv_cache.check_room(T, rope.cos.size(1))
+    if USE_FUSED_APPEND and USE_TORCH_OPS and k_scale is None:
+        return _torch_ops().append_attn(q, k if self.produces_kv else None,
+                                         v if self.produces_kv else None, k_cache, v_cache, seqlens,
+                                         rope.cos, rope.sin, eps=self.norm.eps, scale=1.2,
+                                         window=-1 if self.window is None else self.window, ring=ring)
     if USE_FUSED_APPEND:  # one launch where the plan allows it (ops.append_attn), else two
         return ops.append_attn(q, k if self.produces_kv else None, v if self.produces_kv else None,
                                k_cache, v_cache, seqlens, rope.cos, rope.sin, eps=self.norm.eps,

@@ -38,10 +38,13 @@ kv_copies  (N=1) the broadcast prefill copy, the per-step append and the append 
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
            sample of the same workload (rank 0, N = 1); cpu_baseline_config5 the reference's
            flash_attn_with_kvcache on config 5 at batch 8.
+reference_on_b200  (N=1) the reference's own decode path (modelcore's Decoder, KVCache and
+           flash_attn_with_kvcache, its SDPA path, bf16) on the same GPU and config-2 rows.
 
 Output: rank 0 prints every measurement but the headline as its own JSON line
 {"bench_extra": name, "n_gpus": N, "data": ...}, then the headline line last (compact, with a
-summary of the extras: kv_read_sweep_frac, gqa_decode_tokens_per_s, prefill_append_frac).
+summary of the extras: kv_read_sweep_frac, gqa_decode_tokens_per_s, prefill_append_frac,
+reference_on_b200_tokens_per_s).
 """
 import argparse
 import json
@@ -680,6 +683,40 @@ def _cpu_reference_decode(rows, steps, warmup, threads=None):
     return rows * steps / dt, dt / steps, threads
 
 
+def _gpu_reference_decode(rows, steps, warmup):
+    """The reference's own decode path on the same B200 (BASELINE's GPU comparison point): the
+    stock modelcore ModelManager, KVCache, Decoder and flash_attn_with_kvcache (its SDPA path on
+    this GPU), bf16, none of this repository's kernels, on `rows` of the same prompts; timed with
+    CUDA events around `steps` greedy steps of its own loop (a host read of the tokens each step,
+    as the reference's Decoder does).  Returns (tokens/s, ms per step, the attention path)."""
+    import torch
+    _ensure_modelcore()
+    import modelcore
+    from modelcore.kernels import flash_attn as ref_fa
+    from modelcore_b200 import workloads
+    mgr = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.bfloat16))
+    model = mgr.create_model(workloads.quickstart_config(), device=torch.device("cuda"), seed=0)
+    model = model.to(torch.bfloat16).eval()
+    prompts = workloads.prompts(rows, PROMPT_LEN, seed=1).tolist()
+    with torch.inference_mode():
+        dec = mgr.new_decoder(model, prompts, max_tokens=DECODE_LEN)
+        tok = torch.argmax(dec.logits, dim=-1)
+        for _ in range(warmup):
+            tok = torch.argmax(dec.step(tok.tolist()), dim=-1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            tok = torch.argmax(dec.step(tok.tolist()), dim=-1)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    path = "FA3" if getattr(ref_fa, "USE_FA3", False) else "SDPA"
+    del dec, model, mgr
+    torch.cuda.empty_cache()
+    return rows / (ms * 1e-3), ms, path
+
+
 def _cpu_reference_attention(B=8, windows=(-1, 4096), reps=2, threads=None):
     """Config 5 on the host cores through the reference's own kernel call: modelcore's
     flash_attn_with_kvcache on its SDPA path (modelcore/kernels/flash_attn.py:306-366), fp32,
@@ -896,6 +933,14 @@ def run_b200(args):
             extras["kv_copies"] = _copy_and_append(peak)
             extras["prefill_attention"] = _prefill(_bf16_peak())
     extras["prompt_prefill"] = prompt_prefill
+    if world == 1 and not args.no_sweep:
+        # BASELINE's GPU comparison point: the reference's own decode path on this B200
+        tps_ref, ms_ref, path = _gpu_reference_decode(ROWS_PER_GPU, 20, 3)
+        extras["reference_on_b200"] = {
+            "workload": f"config 2, {ROWS_PER_GPU} rows, 20 greedy steps after 3 warm-up steps",
+            "impl": f"modelcore's own Decoder + KVCache + flash_attn_with_kvcache ({path} path), bf16",
+            "tokens_per_s": round(tps_ref, 1), "ms_per_step": round(ms_ref, 3),
+            "this_path_over_it": round(value / tps_ref, 1)}
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tps, sps, cores = _cpu_reference_decode(CPU_SAMPLE_ROWS, 5, 1)
@@ -951,6 +996,8 @@ def run_b200(args):
         "kv_read_sweep_frac": _sweep_summary(sweep),
         "gqa_decode_tokens_per_s": {f"config {c}": r["tokens_per_s"] for c, r in zip((3, 4), gqa)} if gqa else None,
         "prefill_append_frac": [r["frac"] for r in copies["prefill_append"]] if copies else None,
+        "reference_on_b200_tokens_per_s": (extras["reference_on_b200"]["tokens_per_s"]
+                                           if "reference_on_b200" in extras else None),
         "extras_printed_above": [k for k, v in extras.items() if v is not None],
     }
     print(json.dumps(line), flush=True)

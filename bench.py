@@ -37,7 +37,9 @@ kv_copies  (N=1) the broadcast prefill copy, the per-step append and the append 
            (config 2's 64 x 512 tokens, config 3's 8,192) against the HBM copy roofline.
 cpu_baseline   the reference's own code (modelcore, SDPA path, fp32) on the host cores, a bounded
            sample of the same workload (rank 0, N = 1); cpu_baseline_config5 the reference's
-           flash_attn_with_kvcache on config 5 at batch 8.
+           flash_attn_with_kvcache on config 5 at batch 8; cpu_baseline_configs34 the reference's
+           Decoder on configs 3 (one row of the mean context) and 4 (two rows), per-row tokens/s
+           and KV GB/s.
 reference_on_b200  (N=1) the reference's own decode path (modelcore's Decoder, KVCache and
            flash_attn_with_kvcache, its SDPA path, bf16) on the same GPU and config-2 rows.
 
@@ -717,6 +719,60 @@ def _gpu_reference_decode(rows, steps, warmup):
     return rows / (ms * 1e-3), ms, path
 
 
+def _cpu_reference_gqa(config, steps=3, threads=None):
+    """Configs 3 and 4 on the host cores through the reference itself (modelcore's Decoder,
+    KVCache and SDPA path, fp32), at a reduced batch with the GPU run's per-row shapes: config 3
+    one row, the seeded prompt (seed 2, as the GPU run's) whose length is closest to the rows'
+    mean; config 4 the 4,096-token prompt (seed 3) broadcast to 2 rows, sampled at temperature
+    1.0, top_k 50.  Prefill untimed; `steps` timed decode steps.  Per-row tokens/s, and KV GB/s by
+    the GPU's formula (exact visible keys x 2 x Hkv x D x 2: the bf16 cache's bytes)."""
+    import numpy as np
+    import torch
+    _ensure_modelcore()
+    import modelcore
+    from modelcore.generate import sample_next_token
+    from modelcore_b200 import workloads
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    mgr = modelcore.ModelManager(runtime=modelcore.Runtime(compute_dtype=torch.float32))
+    model = mgr.create_model(workloads.gqa_window_config(kv_share=(config == 4)), device=torch.device("cpu"),
+                             seed=0).eval()
+    blocks = model.body.blocks
+    windows = [b.mixer.window for b in blocks]
+    Hkv, D = blocks[0].mixer.n_kv_head, blocks[0].mixer.head_dim
+    if config == 3:
+        lens = torch.randint(1024, 8193, (128,), generator=torch.Generator().manual_seed(2))
+        i = int(torch.argmin((lens.float() - lens.float().mean()).abs()))
+        prompts, samples = [workloads.prompts(128, 8192, seed=2)[i, :int(lens[i])].tolist()], 1
+    else:
+        prompts, samples = [workloads.prompts(1, 4096, seed=3)[0].tolist()], 2
+    gen = torch.Generator().manual_seed(4)
+    with torch.inference_mode():
+        dec = mgr.new_decoder(model, prompts, num_samples=samples, max_tokens=steps + 4)
+        L0 = int(dec.kv_cache.cache_seqlens[0])
+        rows = samples * len(prompts)
+
+        def pick(logits):
+            if config == 3:
+                return torch.argmax(logits, dim=-1)
+            return sample_next_token(logits, gen, temperature=1.0, top_k=50).view(-1)
+
+        tok = pick(dec.logits)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok = pick(dec.step(tok.tolist()))
+        dt = time.perf_counter() - t0
+    keys = 0
+    for j in range(steps):
+        L = L0 + j
+        keys += rows * sum(min(L + 1, w + 1) if w >= 0 else L + 1 for w in windows)
+    return {"config": config, "rows": rows, "context": L0, "steps": steps,
+            "tokens_per_s": round(rows * steps / dt, 3), "per_row_tokens_per_s": round(steps / dt, 3),
+            "kv_gbs": round(keys * 2 * Hkv * D * 2 / dt / 1e9, 3), "cores": threads,
+            "sample": f"modelcore Decoder + SDPA path fp32 on {threads} threads ({_cpu_model()}), "
+                      f"{rows} row(s) at context {L0}, {steps} timed steps, prefill untimed"}
+
+
 def _cpu_reference_attention(B=8, windows=(-1, 4096), reps=2, threads=None):
     """Config 5 on the host cores through the reference's own kernel call: modelcore's
     flash_attn_with_kvcache on its SDPA path (modelcore/kernels/flash_attn.py:306-366), fp32,
@@ -950,6 +1006,7 @@ def run_b200(args):
                          f"steps, modelcore Decoder + SDPA path fp32 ({_cpu_model()}); the "
                          f"--impl reference arm runs all 64 rows"}
         extras["cpu_baseline_config5"] = _cpu_reference_attention()
+        extras["cpu_baseline_configs34"] = [_cpu_reference_gqa(3), _cpu_reference_gqa(4)]
 
     if rank != 0:
         return

@@ -58,6 +58,13 @@ import sys
 import threading
 import time
 
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # NCCL's init lines (one per rank, with the communicator's rank count) stay in the log, so a
+    # reader of the run can count the ranks that joined; a caller's own setting wins.  Set before
+    # torch loads NCCL, which reads them once.
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
@@ -178,10 +185,6 @@ def _dist_setup(n_gpus):
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     torch.cuda.set_device(local)
     if world > 1:
-        # NCCL's init lines (one per rank, with the communicator's rank count) stay in the log,
-        # so a reader of the run can count the ranks that joined; a caller's own setting wins
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     return rank, world, local

@@ -1060,7 +1060,7 @@ def run_b200(args):
                                            if "reference_on_b200" in extras else None),
         "extras_printed_above": [k for k, v in extras.items() if v is not None],
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def main():
@@ -1105,10 +1105,12 @@ def main():
         peak, _ = _peaks()
         print(json.dumps({"gqa_decode": [_gqa_decode(c, peak) for c in args.gqa_configs]}), flush=True)
     else:
-        run_b200(args)
+        line = run_b200(args)
         import torch.distributed as dist
         if dist.is_initialized():
             dist.destroy_process_group()
+        if line is not None:  # rank 0: the headline last, after NCCL's teardown lines
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -12,6 +12,9 @@
 //                   (kernels/flash_attn.py:348-366)
 //   append_attn     kv_append_rope then decode_attn, in one launch where the plan allows it
 //   kv_advance      cache_seqlens += n (KVCache.advance, modelcore/cache.py:62-73)
+//   linear          mcb_linear's plain, residual, gated and norm-out projections (the decode
+//                   step's, modelcore/components/linear.py:14 with block.py:57-59, mlp.py:89-90)
+//   add_rms_norm    the residual add and the next RMSNorm (block.py:57-59, norm.py:43-44)
 //
 // Every op runs on the current CUDA stream of its tensors' device, checks dtypes, devices and
 // dimensions here (TORCH_CHECK: a RuntimeError in Python) and leaves sizes, strides and
@@ -305,6 +308,83 @@ void kv_advance(const at::Tensor& cache_seqlens, int64_t n) {
                "mcb200::kv_advance");
 }
 
+int64_t row_stride(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be a 2-D tensor with unit column stride");
+  return t.stride(0);
+}
+
+// mcb_linear's plain, residual, gated and norm-out modes (the decode step's projections)
+void linear(const at::Tensor& x, const at::Tensor& weight, const at::Tensor& out, const std::optional<at::Tensor>& res,
+            const std::optional<at::Tensor>& h_out, std::optional<double> eps, bool gated, bool pdl) {
+  for (const at::Tensor* t : {&x, &weight, &out}) {
+    need(*t, "x, weight and out", 2, at::kBFloat16);
+    same_device(x, *t, "weight and out");
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  mcb_linear_args a = {};
+  a.x = x.data_ptr();
+  a.w = weight.data_ptr();
+  a.y = out.data_ptr();
+  a.x_stride = row_stride(x, "x");
+  a.w_stride = row_stride(weight, "weight");
+  a.y_stride = row_stride(out, "out");
+  a.R = static_cast<int32_t>(x.size(0));
+  a.K = static_cast<int32_t>(x.size(1));
+  a.N = static_cast<int32_t>(gated ? weight.size(0) / 2 : weight.size(0));
+  TORCH_CHECK(weight.size(1) == x.size(1), "weight must be (N, ", x.size(1), "), got ", weight.sizes());
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == a.N, "out must be (", x.size(0), ", ", a.N, ")");
+  if (res.has_value()) {
+    need(*res, "res", 2, at::kBFloat16);
+    same_device(x, *res, "res");
+    TORCH_CHECK(res->sizes() == out.sizes(), "res must be shaped like out");
+    a.res = res->data_ptr();
+    a.res_stride = row_stride(*res, "res");
+  }
+  a.flags = gated ? MCB_LINEAR_GATED : 0;
+  if (h_out.has_value()) {
+    need(*h_out, "h_out", 2, at::kBFloat16);
+    same_device(x, *h_out, "h_out");
+    TORCH_CHECK(h_out->sizes() == out.sizes(), "h_out must be shaped like out");
+    a.h_out = h_out->data_ptr();
+    a.h_out_stride = row_stride(*h_out, "h_out");
+    a.flags |= MCB_LINEAR_NORM_OUT;
+  }
+  a.eps = norm_eps(eps);
+  a.pdl = pdl ? 1 : 0;
+  check_status(mcb_linear(&a, stream_of(x)), "mcb200::linear");
+}
+
+// x_out = x + delta (when delta is given; x_out may be x), h_out = rms_norm(that)
+void add_rms_norm(const at::Tensor& x, const std::optional<at::Tensor>& delta, const std::optional<at::Tensor>& x_out,
+                  const at::Tensor& h_out, std::optional<double> eps) {
+  need(x, "x", 2, at::kBFloat16);
+  need(h_out, "h_out", 2, at::kBFloat16);
+  same_device(x, h_out, "h_out");
+  TORCH_CHECK(h_out.sizes() == x.sizes(), "h_out must be shaped like x");
+  c10::cuda::CUDAGuard guard(x.device());
+  mcb_add_norm_args a = {};
+  a.x = x.data_ptr();
+  a.x_stride = row_stride(x, "x");
+  a.h_out = h_out.data_ptr();
+  a.h_stride = row_stride(h_out, "h_out");
+  a.rows = static_cast<int32_t>(x.size(0));
+  a.C = static_cast<int32_t>(x.size(1));
+  if (delta.has_value()) {
+    TORCH_CHECK(x_out.has_value(), "x_out is needed with delta");
+    for (const at::Tensor* t : {&*delta, &*x_out}) {
+      need(*t, "delta and x_out", 2, at::kBFloat16);
+      same_device(x, *t, "delta and x_out");
+      TORCH_CHECK(t->sizes() == x.sizes(), "delta and x_out must be shaped like x");
+    }
+    a.delta = delta->data_ptr();
+    a.delta_stride = row_stride(*delta, "delta");
+    a.x_out = x_out->data_ptr();
+    a.x_out_stride = row_stride(*x_out, "x_out");
+  }
+  a.eps = norm_eps(eps);
+  check_status(mcb_add_rms_norm(&a, stream_of(x)), "mcb200::add_rms_norm");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(mcb200, m) {
@@ -322,6 +402,10 @@ TORCH_LIBRARY(mcb200, m) {
       "Tensor cache_seqlens, Tensor cos, Tensor sin, float? eps=None, float scale=1.2, int window=-1, "
       "bool ring=False) -> Tensor");
   m.def("kv_advance(Tensor(a!) cache_seqlens, int n) -> ()");
+  m.def(
+      "linear(Tensor x, Tensor weight, Tensor(a!) out, Tensor? res=None, Tensor(b!)? h_out=None, "
+      "float? eps=None, bool gated=False, bool pdl=False) -> ()");
+  m.def("add_rms_norm(Tensor x, Tensor? delta, Tensor(a!)? x_out, Tensor(b!) h_out, float? eps=None) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(mcb200, CUDA, m) {
@@ -330,4 +414,6 @@ TORCH_LIBRARY_IMPL(mcb200, CUDA, m) {
   m.impl("decode_attn", &decode_attn);
   m.impl("append_attn", &append_attn);
   m.impl("kv_advance", &kv_advance);
+  m.impl("linear", &linear);
+  m.impl("add_rms_norm", &add_rms_norm);
 }

@@ -149,6 +149,31 @@ def qkv_projection(attn, x):
     return q, k, v
 
 
+# The default linear body's per-layer projections and add + norm go through the torch.ops.mcb200
+# operators (C++ over the same library: a fraction of the host cost of the ctypes call, which an
+# eager, ungraphed step pays per launch); the same kernels and bits either way
+USE_TORCH_OPS = True
+
+
+def _lin(x, w, out=None, res=None, h_out=None, eps=None, gated=False, pdl=True):
+    if not USE_TORCH_OPS:
+        return ops.linear(x, w, out=out, res=res, h_out=h_out, eps=eps, gated=gated, pdl=pdl)
+    from .integration import _torch_ops
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[0] // 2 if gated else w.shape[0]), dtype=torch.bfloat16,
+                          device=x.device)
+    _torch_ops().linear(x, w, out, res, h_out, eps, gated, pdl)
+    return out
+
+
+def _add_norm(x, delta=None, eps=None, x_out=None, h_out=None):
+    if not USE_TORCH_OPS:
+        ops.add_rms_norm(x, delta, eps=eps, x_out=x_out, h_out=h_out)
+        return
+    from .integration import _torch_ops
+    _torch_ops().add_rms_norm(x, delta, x_out if delta is not None else None, h_out, eps)
+
+
 def gated_mlp(ffn, h, linear=False):
     """GatedMLP.forward (modelcore/components/mlp.py:89-90) for activation "silu" on (rows, C):
     one GEMM on [Wg; Wu], mcb_gated_silu, then down_proj; with linear (a decode step's few rows,
@@ -158,8 +183,8 @@ def gated_mlp(ffn, h, linear=False):
     w = packed_weight(ffn, "gate_up", (ffn.gate_proj, ffn.up_proj))
     H = ffn.hidden_dim
     if linear and H % 64 == 0 and H <= 2048:
-        a = ops.linear(h, w, gated=True, pdl=True)
-        return ops.linear(a, ffn.down_proj.weight, pdl=True)
+        a = _lin(h, w, gated=True, pdl=True)
+        return _lin(a, ffn.down_proj.weight, pdl=True)
     gu = F.linear(h, w)
     return F.linear(ops.gated_silu(gu[:, :H], gu[:, H:]), ffn.down_proj.weight)
 
@@ -277,7 +302,7 @@ def body_forward_linear(body, x2, h, kv_cache, B, T):
             w = packed_weight(attn, "qkv", (attn.c_q, attn.c_k, attn.c_v))
         else:
             w = attn.c_q.weight
-        qkv = ops.linear(h, w, pdl=True)
+        qkv = _lin(h, w, pdl=True)
         q = qkv[:, :nq].view(B, T, attn.n_head, hd)
         k = v = None
         if attn.produces_kv:
@@ -287,13 +312,13 @@ def body_forward_linear(body, x2, h, kv_cache, B, T):
         y = attend(attn, q, k, v, kv_cache).reshape(rows, nq)
         wo = attn.c_proj.weight
         if USE_LINEAR_NORM_OUT and _norm_out_ok(y, wo, resid, src, h, eps):
-            ops.linear(y, wo, out=resid, res=src, h_out=h, eps=eps, pdl=True)
+            _lin(y, wo, out=resid, res=src, h_out=h, eps=eps, pdl=True)
         else:
-            ops.linear(y, wo, out=resid, res=src, pdl=True)
-            ops.add_rms_norm(resid, eps=eps, h_out=h)
+            _lin(y, wo, out=resid, res=src, pdl=True)
+            _add_norm(resid, eps=eps, h_out=h)
         src = resid
         f = gated_mlp(ffn, h, linear=USE_LINEAR_MLP)
-        ops.add_rms_norm(resid, f, eps=eps, x_out=resid, h_out=h)
+        _add_norm(resid, f, eps=eps, x_out=resid, h_out=h)
     return resid, h
 
 

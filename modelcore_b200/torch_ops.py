@@ -20,6 +20,11 @@ functions, so that torch.compile can trace through them:
         the two above in one launch where the plan allows it (a decode step), else two
     torch.ops.mcb200.kv_advance(cache_seqlens, n)
         KVCache.advance (modelcore/cache.py:62-73), in place
+    torch.ops.mcb200.linear(x, weight, out, res=None, h_out=None, eps=None, gated=False, pdl=False)
+        the decode step's projections (ops.linear's plain, residual, gated and norm-out modes),
+        into out (and h_out)
+    torch.ops.mcb200.add_rms_norm(x, delta, x_out, h_out, eps=None)
+        the residual add and the next RMSNorm (ops.add_rms_norm), into x_out and h_out
 
 bf16 slots only (the fp8 cache format is reached through modelcore_b200.ops).  The results are
 those of the ctypes entry points bit for bit: one library does the work.  Without the built
@@ -32,7 +37,8 @@ import torch
 from . import _native
 from .build import TORCH_OPS_PATH
 
-OPS = ("kv_append_rope", "kv_broadcast", "decode_attn", "append_attn", "kv_advance")
+OPS = ("kv_append_rope", "kv_broadcast", "decode_attn", "append_attn", "kv_advance", "linear",
+       "add_rms_norm")
 
 
 def _register_fakes():
@@ -43,7 +49,8 @@ def _register_fakes():
         return None
 
     for name, fn in (("kv_append_rope", like_q), ("decode_attn", like_q), ("append_attn", like_q),
-                     ("kv_broadcast", nothing), ("kv_advance", nothing)):
+                     ("kv_broadcast", nothing), ("kv_advance", nothing), ("linear", nothing),
+                     ("add_rms_norm", nothing)):
         torch.library.register_fake(f"mcb200::{name}")(fn)
 
 

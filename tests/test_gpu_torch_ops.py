@@ -115,3 +115,66 @@ def test_in_a_cuda_graph_and_under_torch_compile(env):
     for i in range(3):
         assert torch.equal(compiled(q, k, v, kc3, vc3, sl3), want[i])
     assert torch.equal(kc3, kc1) and torch.equal(sl3, sl1)
+
+
+def test_linear_and_add_rms_norm_ops_equal_the_ctypes_entry_points(env):
+    """torch.ops.mcb200.linear (plain, residual, gated, norm out) and add_rms_norm against
+    ops.linear / ops.add_rms_norm: the same library, the same bits."""
+    ops = env
+    from modelcore_b200 import step
+    g = torch.Generator(device="cuda").manual_seed(11)
+    r = lambda *s, sc=1.0: (torch.randn(*s, device="cuda", generator=g) * sc).to(torch.bfloat16)
+    x, w_qkv, w_o, w_gu, w_d = r(64, 768), r(2304, 768, sc=0.03), r(768, 768, sc=0.03), \
+        r(4096, 768, sc=0.03), r(768, 2048, sc=0.02)
+    res = r(64, 768, sc=4.0)
+    out = torch.empty(64, 2304, device="cuda", dtype=torch.bfloat16)
+    torch.ops.mcb200.linear(x, w_qkv, out)
+    assert torch.equal(out, ops.linear(x, w_qkv))
+    y1, h1 = res.clone(), torch.empty_like(res)
+    torch.ops.mcb200.linear(x, w_o, y1, y1, None, 1e-6, False, True)
+    assert torch.equal(y1, ops.linear(x, w_o, res=res))
+    if ops.linear_supported(x, w_o, out=y1, res=y1, h_out=h1):
+        y2, y3, h2, h3 = res.clone(), res.clone(), torch.empty_like(res), torch.empty_like(res)
+        torch.ops.mcb200.linear(x, w_o, y2, y2, h2, 1e-6)
+        ops.linear(x, w_o, out=y3, res=y3, h_out=h3, eps=1e-6)
+        assert torch.equal(y2, y3) and torch.equal(h2, h3)
+    a = torch.empty(64, 2048, device="cuda", dtype=torch.bfloat16)
+    torch.ops.mcb200.linear(x, w_gu, a, gated=True)
+    assert torch.equal(a, ops.linear(x, w_gu, gated=True))
+    f = torch.empty(64, 768, device="cuda", dtype=torch.bfloat16)
+    torch.ops.mcb200.linear(a, w_d, f)
+    assert torch.equal(f, ops.linear(a, w_d))
+    xa, ha = res.clone(), torch.empty_like(res)
+    torch.ops.mcb200.add_rms_norm(xa, f, xa, ha, 1e-6)
+    xb, hb = ops.add_rms_norm(res.clone(), f, eps=1e-6)
+    assert torch.equal(xa, xb) and torch.equal(ha, hb)
+    hc = torch.empty_like(res)
+    torch.ops.mcb200.add_rms_norm(res, None, None, hc)
+    assert torch.equal(hc, ops.add_rms_norm(res)[1])
+    # the decode step with and without the operators: the same bits (step.USE_TORCH_OPS)
+    assert step.USE_TORCH_OPS
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+
+
+def test_decode_step_bits_do_not_depend_on_the_binding(env):
+    """The fused decode step through the torch.ops operators (the default) and through ctypes
+    (step.USE_TORCH_OPS / integration.USE_TORCH_OPS off) give identical logits and caches."""
+    import modelcore_b200
+    from modelcore_b200 import integration, step, workloads
+    mgr = modelcore_b200.ModelManager()
+    model = workloads.awaken(mgr.create_model(workloads.quickstart_config(n_layer=4),
+                                              device=torch.device("cuda"), seed=0))
+    model = model.to(torch.bfloat16).eval()
+    prompts = workloads.prompts(5, 40, seed=3).tolist()
+    outs = []
+    for use in (True, False):
+        step.USE_TORCH_OPS = integration.USE_TORCH_OPS = use
+        try:
+            with torch.inference_mode():
+                dec = mgr.new_decoder(model, prompts, max_tokens=8)
+                logits = [dec.step([1, 2, 3, 4, 5]) for _ in range(3)]
+                outs.append((torch.stack(logits), dec.kv_cache.k_cache.clone()))
+        finally:
+            step.USE_TORCH_OPS = integration.USE_TORCH_OPS = True
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])

@@ -47,6 +47,13 @@ struct SplitAttnParams {
   // also writes the new key (roped, normed, scaled unless raw) and value into the slot and into
   // its own copy of that tile -- kv_append_rope_vec_kernel's arithmetic, the same bits
   int fuse;
+  // head pairs (D = 128 instance only, one split, bf16): the slot holds kv heads of 64 as pairs,
+  // kv "head" j = real heads 2j, 2j + 1 side by side (the same bytes), and query row r of row
+  // group j is real q head 2j + r (G = 2) -- its 64 dimensions in half r of a 128-dimension row,
+  // zeros in the other, so the dot product with the pair's key reads only its own head; the
+  // output keeps half r of row r and goes to the real (B, T, Hq, 64) layout.  q, k_new and v_new
+  // are the real 64-dimension heads (their strides), and the fused rope and norm work on them.
+  int pair;
   const uint16_t* k_new;       // (B, 1, Hkv, D) raw key / value projections; null: q only
   const uint16_t* v_new;
   long long kns[3], vns[3];
@@ -380,8 +387,53 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     pdl_launch_dependents();
     uint16_t* qbuf = reinterpret_cast<uint16_t*>(smem + C::FUSE_OFFSET);  // [kRows][D]
     uint16_t* kvbuf = qbuf + C::kRows * D;                                 // [2][D]
-    if (!FP8 && p.fuse) {
-      if (warp == 0) {
+    if (!FP8 && (p.fuse || (D == 128 && p.pair))) {
+      if (D == 128 && p.pair && warp == 0) {
+        // head pairs: groups of four lanes, one 64-dimension vector each -- the query heads (roped,
+        // normed and scaled when fused, else copied) into their half of the row, zeros in the
+        // other; then (the CTA with the new position) the pair's two keys and two values
+        constexpr int DH = 64, LG = DH / 16, VPW = 32 / LG, HALF = DH / 2;  // (D = 128 only)
+        const int nq = r1 - r0;
+        const int nvec = nq + (own_new ? 4 : 0);
+        const int sub = lane % LG;
+        const bool rot_ok = L >= 0 && L < p.rot_len;
+        for (int v0 = 0; v0 < nvec; v0 += VPW) {
+          const int vi = v0 + lane / LG;
+          const bool valid = vi < nvec;
+          const bool is_q = vi < nq;
+          const int kv = vi - nq;              // 0, 1: the keys of heads 2 kvh, 2 kvh + 1; 2, 3: values
+          const bool is_k = !is_q && kv < 2;
+          const int half = is_q ? (r0 + vi) & 1 : (kv & 1);
+          const uint16_t* src = nullptr;
+          if (valid)
+            src = is_q ? p.q + b * p.qs[0] + (kvh * p.G + r0 + vi) * p.qs[2]
+                       : (is_k ? p.k_new + b * p.kns[0] + (2 * kvh + half) * p.kns[2]
+                               : p.v_new + b * p.vns[0] + (2 * kvh + half) * p.vns[2]);
+          const bool rotate = valid && p.fuse && (is_q || (is_k && p.rotate_k));
+          if (rotate && !rot_ok && sub == 0) record_error(kErrPositionBeyondRotary);
+          const uint4 x1v = valid ? *reinterpret_cast<const uint4*>(src + 8 * sub) : make_uint4(0, 0, 0, 0);
+          const uint4 x2v = valid ? *reinterpret_cast<const uint4*>(src + HALF + 8 * sub) : make_uint4(0, 0, 0, 0);
+          uint4 w1, w2;
+          rope_norm_vec<DH>(x1v, x2v, p.rot_cos, p.rot_sin, L, sub, rotate && rot_ok, p.norm_eps, p.qk_scale, w1,
+                            w2);
+          if (valid) {
+            uint16_t* dst = (is_q ? qbuf + vi * D : kvbuf + (is_k ? 0 : D)) + half * DH;
+            *reinterpret_cast<uint4*>(dst + 8 * sub) = w1;
+            *reinterpret_cast<uint4*>(dst + HALF + 8 * sub) = w2;
+            if (is_q) {  // the other head's half of the row
+              uint16_t* other = qbuf + vi * D + (1 - half) * DH;
+              *reinterpret_cast<uint4*>(other + 8 * sub) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(other + HALF + 8 * sub) = make_uint4(0, 0, 0, 0);
+            } else if (p.ring || L < p.Tmax) {
+              const int idx = p.ring ? L % p.Tmax : L;
+              uint16_t* cdst = (is_k ? p.kc_out : p.vc_out) +
+                               ((static_cast<long long>(b) * p.Tmax + idx) * p.Hkv + kvh) * D + half * DH;
+              *reinterpret_cast<uint4*>(cdst + 8 * sub) = w1;
+              *reinterpret_cast<uint4*>(cdst + HALF + 8 * sub) = w2;
+            }
+          }
+        }
+      } else if (warp == 0) {
         // groups of D/16 lanes, one vector each: the query heads r0 .. r1-1, then (the CTA with
         // the new position) the key and the value
         constexpr int LG = D / 16, VPW = 32 / LG, HALF = D / 2;
@@ -427,7 +479,7 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
       const int r = r0 + j * 8 + (lane >> 2);
       const uint16_t* qrow = nullptr;
       if (r < r1) {
-        if (!FP8 && p.fuse) {
+        if (!FP8 && (p.fuse || (D == 128 && p.pair))) {
           qrow = qbuf + (r - r0) * D;
         } else {
           const int t = r / p.G, h = kvh * p.G + r % p.G;
@@ -769,7 +821,11 @@ __global__ void __launch_bounds__(kAttnThreads, (STAGES == 2 && D <= 64 && NQT =
     }
     const int t = r / p.G, h = kvh * p.G + r % p.G;
     const long long row = (static_cast<long long>(b) * p.T + t) * p.Hq + h;
-    if (p.nsplit == 1) {
+    if (D == 128 && !FP8 && p.pair) {  // half r of row r, to the real 64-dimension head
+      if ((d >> 6) == (h & 1))
+        *reinterpret_cast<uint2*>(p.out + row * (D / 2) + (d & 63)) =
+            make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+    } else if (p.nsplit == 1) {
       *reinterpret_cast<uint2*>(p.out + row * D + d) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
     } else if (p.cluster) {
       if constexpr (C::PUSH)

@@ -217,3 +217,46 @@ def test_fused_append_rejects_new_keys_with_the_wrong_head_count(ops):
     cos, sin = tables(Tmax + 8, D)
     with pytest.raises(RuntimeError, match="Hkv"):
         ops.append_attn(q, k, k.clone(), kc, vc, sl, cos, sin, eps=1e-6)
+
+
+PAIR_CASES = [  # B, H, Tmax, lengths, window, ring, produces_kv
+    (64, 12, 1024, (500, 1000), -1, False, True),   # config 2's shape
+    (32, 8, 1024, (10, 1000), 300, False, True),     # a window
+    (16, 4, 512, (600, 1500), 200, True, True),      # a ring slot
+    (24, 12, 1024, (100, 900), -1, False, False),    # a layer that reads another's slot
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES, ids=lambda c: "B{}H{}w{}r{}kv{}".format(c[0], c[1], c[4], int(c[5]),
+                                                                                     int(c[6])))
+def test_head_pairs_equal_the_one_head_kernel(ops, case):
+    """Head size 64 with one query head a kv head runs, on its one-split plan, as kv heads of 128
+    holding two real heads (the split kernel's pair mode): bit for bit the one-head kernel's output
+    (num_ctas = -1 keeps that kernel), fused with the append or not, cache bytes included."""
+    B, H, Tmax, (lo, hi), window, ring, produces = case
+    D = 64
+    g = torch.Generator(device="cuda").manual_seed(B + H + Tmax)
+    qkv = (torch.randn(B, 1, 3 * H, D, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    q, k, v = qkv[:, :, :H], qkv[:, :, H:2 * H], qkv[:, :, 2 * H:]
+    kc = torch.randn(B, Tmax, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    sl = torch.randint(lo, hi, (B,), device="cuda", generator=g, dtype=torch.int32)
+    cos, sin = tables(max(Tmax, hi) + 8, D)
+    kc1, vc1, kc2, vc2 = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+    # unfused: the append, then the attention paired (auto plan) and one-head (num_ctas = -1)
+    if produces:
+        qa = ops.kv_append_rope(q, k, v, kc1, vc1, sl, cos, sin, eps=1e-6, scale=1.2, ring=ring)
+    else:
+        qa = ops.kv_append_rope(q, None, None, None, None, sl, cos, sin, rotate_q=True, rotate_k=False,
+                                write_kv=False, eps=1e-6, scale=1.2)
+    paired = ops.decode_attn(qa, kc1, vc1, sl, window=window, ring=ring)
+    name = ops.last_attn_kernel()
+    single = ops.decode_attn(qa, kc1, vc1, sl, window=window, ring=ring, num_ctas=-1)
+    # fused: one launch, paired
+    got = fused(ops, q, k if produces else None, v if produces else None, kc2, vc2, sl, cos, sin,
+                window, ring, 0)
+    torch.cuda.synchronize()
+    assert ops.device_error()[0] == 0
+    assert "<128,1,16," in name, name
+    assert torch.equal(paired, single) and torch.equal(got, single)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)

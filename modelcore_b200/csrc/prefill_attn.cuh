@@ -540,20 +540,28 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
           mbar_arrive(s_free);
         }
         // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
-        float mx = -INFINITY;
         const bool full = k0 + kPfTile - 1 <= L + qbase &&
                           (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
                           qbase + kPfTile <= p.T;
         if (!full) {
+          // this query row sees the key columns [c_lo, c_hi) of the tile (key <= pos, and
+          // pos - key <= window): one unsigned compare a column against the interval's width
+          const int c_hi = valid ? min(kPfTile, pos - k0 + 1) : 0;
+          const int c_lo = p.window >= 0 ? max(0, pos - p.window - k0) : 0;
+          const uint32_t width = c_hi > c_lo ? static_cast<uint32_t>(c_hi - c_lo) : 0u;
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            const int key = k0 + c;
-            const bool vis = valid && key <= pos && (p.window < 0 || pos - key <= p.window);
-            if (!vis) sr[c] = __float_as_uint(-INFINITY);
-          }
+          for (int c = 0; c < 128; ++c)
+            if (static_cast<uint32_t>(c - c_lo) >= width) sr[c] = __float_as_uint(-INFINITY);
         }
+        // the row maximum in four independent chains (one chain would serialise 64 dependent
+        // max instructions); max is exact, so the order does not change the result
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < 64; ++c) mx = fmax3(mx, __uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1]));
+        for (int c = 0; c < 16; ++c)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            m4[u] = fmax3(m4[u], __uint_as_float(sr[8 * c + 2 * u]), __uint_as_float(sr[8 * c + 2 * u + 1]));
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         mx *= p.scale_log2;
         // lazy rescale: move the running max only when it grows by more than 2^8
         float alpha = 1.f;

@@ -10,10 +10,11 @@
 // its CTA walks 128-key tiles, each K/V tile serving both query tiles.  The grid is persistent
 // (one CTA per SM, items strided over the CTAs, longest first), so TMEM allocation, barrier setup
 // and the pipeline fill are paid once per CTA and the next item's loads overlap this one's end.
-// The QT = 1 copy (head size 64) takes one query tile an item with six warps (no Q1 softmax
-// warps) and 256 TMEM columns, two CTAs per SM: the two query-tile chains of an SM are then
-// independent -- neither waits for the other's extra causal key tile or epilogue, at the price
-// of K/V tiles read once per query tile instead of once per pair.  The roles (QT = 2):
+// The QT = 1 copy (head size 64) takes one query tile an item with ten warps (no Q1 softmax
+// warps; two softmax warps a row quarter, 64 key columns each) and 256 TMEM columns, two CTAs
+// per SM: the two query-tile chains of an SM are then independent -- neither waits for the
+// other's extra causal key tile or epilogue, at the price of K/V tiles read once per query tile
+// instead of once per pair.  The roles (QT = 2):
 //
 //   warp 0       TMA producer: per item Q0 and Q1 (double-buffered for D = 64), then K_j and V_j
 //                into a two-stage ring that runs on across items
@@ -25,8 +26,11 @@
 //                in the order S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | ... so the
 //                tensor core computes one tile's S while the other tile's softmax runs
 //   warps 2-5    softmax of Q0, warps 6-9 softmax of Q1: one thread per query row (TMEM lane =
-//                row; warp w reaches lanes 32 (w % 4) .. +31, so each group of four covers all 128): S from TMEM, mask only on tiles that cross the diagonal, the window edge or
-//                the end of the rows; online max with a lazy rescale (the running max moves, and
+//                row; warp w reaches lanes 32 (w % 4) .. +31, so each group of four covers all
+//                128; QT = 1: warps 2-9, two a row quarter, each on 64 of the tile's key columns
+//                and 32 of O's, the partial row maxima and sums exchanged through shared
+//                memory): S from TMEM, mask only on tiles that cross the diagonal, the window
+//                edge or the end of the rows; online max with a lazy rescale (the running max moves, and
 //                O and the row sum are rescaled, only when a row's max grows by more than 2^8);
 //                P = exp2(S * scale * log2 e - max) written back into TMEM as bf16; at the end
 //                O / sum as bf16 to the output
@@ -48,8 +52,15 @@ namespace mcb {
 constexpr int kPfTile = 128;          // queries per query tile and keys per key tile
 // QT query tiles an item (2: one CTA per SM, ten warps, all 512 TMEM columns; 1: two CTAs per SM,
 // six warps and 256 TMEM columns each, every query tile an independent chain)
+// Softmax warps a row quarter, each taking 128 / pf_split of a tile's key columns.  One query tile
+// an item (two CTAs an SM, one softmax chain each): two, so that an SM sub-partition holds four
+// softmax warps that hide one another's exponential and TMEM-load latency (config 2's 64 x 512
+// prefill 118.8 -> 112.6 us).  Pairs: one -- the two query tiles' chains already interleave,
+// and 18 warps would cut a thread's registers from 168 to 96 (8k prompt 289 -> 305 us).
 template <int QT>
-__host__ __device__ constexpr int pf_threads() { return (2 + 4 * QT) * 32; }
+__host__ __device__ constexpr int pf_split() { return QT == 1 ? 2 : 1; }
+template <int QT>
+__host__ __device__ constexpr int pf_threads() { return (2 + 4 * QT * pf_split<QT>()) * 32; }
 template <int QT>
 __host__ __device__ constexpr uint32_t pf_tmem_cols() { return 256u * QT; }
 
@@ -108,6 +119,17 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
       : "r"(taddr + 0u), "r"(taddr + 32u), "r"(taddr + 64u), "r"(taddr + 96u)
+      : "memory");
+}
+
+// 64 consecutive 32-bit TMEM columns of this warp's 32 lanes, waited for inside the same asm.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr + 0u), "r"(taddr + 32u)
       : "memory");
 }
 
@@ -227,7 +249,10 @@ struct PrefillConfig {
   static constexpr int kKOff = kQOff + kQBufs * QT * kTileBytes;   // K ring, 2 stages
   static constexpr int kVOff = kKOff + 2 * kTileBytes;             // V ring, 2 stages
   static constexpr int kBarOff = kVOff + 2 * kTileBytes;
-  static constexpr int kBytes = kBarOff + 256;
+  // the partial row maxima and sums the softmax warps of a row quarter exchange: two slots x QT
+  // query tiles x 4 quarters x pf_split warps x 32 rows, fp32
+  static constexpr int kXchOff = kBarOff + 256;
+  static constexpr int kBytes = kXchOff + (pf_split<QT>() > 1 ? 2 * QT * 4 * pf_split<QT>() * 32 * 4 : 0);
   // TMEM bounds the CTAs an SM holds (QT = 2: all 512 columns; QT = 1: 256, two CTAs): the
   // shared memory keeps a third CTA off the SM (more than a third of its 228 KB for QT = 1,
   // more than half for QT = 2), so no CTA ever waits in tcgen05.alloc for another to finish
@@ -299,8 +324,9 @@ __device__ __forceinline__ int prefill_round_item(const PrefillParams& p, int r)
 // refilled) and o_done; every softmax thread waits for o_done, reads its O, and arrives on
 // epi_done, which the issuer waits for before the next item's o_done -- so no softmax group, not
 // even one with no query tile in an item (T <= 128), can find o_done two phases ahead.
-// 168 registers a thread: the 10 warps land three to a sub-partition on two of the four, whose
-// 16,384 registers each cap a thread at 170 (a higher cap fails to launch); a few bytes spill.
+// Registers: QT = 2, 168 a thread -- the 10 warps land three to a sub-partition on two of the
+// four, whose 16,384 registers each cap a thread at 170 (a higher cap fails to launch); QT = 1,
+// 96 -- two CTAs of 10 warps, five a sub-partition; a few bytes spill in both.
 template <int D, int QT>
 __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -324,7 +350,10 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
   uint64_t* drained = bars + 16;
   uint64_t* s_free = bars + 17;    // QT = 1: the softmax has read S (128 arrivals)
   uint64_t* pv_done = bars + 18;   // QT = 1: a P V product has completed (P and O free again)
-  constexpr int kNumBars = 19;
+  constexpr int SPL = pf_split<QT>();
+  uint64_t* pair_bars = bars + 19; // [QT][4] when SPL > 1: the SPL softmax warps of a row quarter
+  constexpr int kNumBars = 19 + (SPL > 1 ? 4 * QT : 0);
+  static_assert((kNumBars + 2) * 8 <= 256, "the barriers, the TMEM slot and the abort flag in 256 bytes");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kNumBars + 1);
 
@@ -332,7 +361,10 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bars + i, (i == 12 || i == 13 || i == 17) ? 128 : (i == 15 ? 128 * QT : 1));
+      mbar_init(bars + i, (i == 12 || i == 13 || i == 17) ? 128 * SPL
+                          : i == 15                         ? 128 * QT * SPL
+                          : i >= 19                         ? 32 * SPL
+                                                            : 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -498,18 +530,51 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
     umma_commit(drained);
     mbar_wait(drained, 0);
   } else if (warp >= 2) {
-    // ---------------- softmax: warps 2-5 query tile 0, warps 6-9 query tile 1 ----------------
-    const int t = (warp - 2) >> 2;
-    const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
-    const int row = quarter * 32 + lane;          // query row within the tile
+    // ---------------- softmax: 4 SPL warps a query tile ----------------
+    // Warp w reaches TMEM lanes 32 (w % 4) .. +31 (its row quarter); the SPL warps of one
+    // quarter take consecutive slices of KC key columns of the tile (and DC columns of O) and
+    // meet twice an item: the partial row maxima every tile, the partial row sums at the end.
+    constexpr int KC = kPfTile / SPL;   // key columns a thread
+    constexpr int DC = D / SPL;         // O columns a thread rescales and stores
+    const int idx = warp - 2;
+    const int t = idx / (4 * SPL);
+    const int h = (idx >> 2) % SPL;     // slice of the row quarter
+    const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31
+    const int row = quarter * 32 + lane;     // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + t * kPfTile;
-    const uint32_t o_addr = tmem + lane_off + Cfg::kOCol + t * D;
-    const uint32_t p_addr = QT == 1 ? tmem + lane_off + Cfg::kPCol : s_addr;  // P: over S for QT = 2
+    const uint32_t s_addr = tmem + lane_off + t * kPfTile + h * KC;
+    const uint32_t o_addr = tmem + lane_off + Cfg::kOCol + t * D + h * DC;
+    // P (packed bf16, KC / 2 columns a slice): its own columns for QT = 1, over S for QT = 2
+    const uint32_t p_addr = (QT == 1 ? tmem + lane_off + Cfg::kPCol : tmem + lane_off + t * kPfTile) + h * (KC / 2);
+    uint64_t* pair_bar = pair_bars + t * 4 + quarter;
+    float* xch = reinterpret_cast<float*>(smem + Cfg::kXchOff);
     int k = 0;       // items done
     int s_cnt = 0;   // S tiles of this query tile consumed (s_full phases)
     int pv_seen = 0; // QT = 1: P V products observed (pv_done phases), one per tile
+    int ex = 0;      // exchanges with the other warps of the quarter (pair_bar phases)
     bool ok = true;
+    // The other slices' value of this row, combined by `op` in slice order: written to slot
+    // ex % 2, arrive, wait (bounded) for the quarter's phase.  A slot is rewritten two exchanges
+    // later, after every warp of the quarter has arrived at the exchange between (so has read it).
+    // The fences order this warp's TMEM loads before the other slices' P stores over S.
+    auto exchange = [&](float v, auto op) -> float {
+      if constexpr (SPL == 1) return v;
+      float* slot = xch + (((ex & 1) * QT + t) * 4 + quarter) * (SPL * 32);
+      slot[h * 32 + lane] = v;
+      tc_fence_before();
+      mbar_arrive(pair_bar);
+      const bool w = __all_sync(0xffffffffu, mbar_wait_or_abort(pair_bar, ex & 1, abort_flag));
+      tc_fence_after();
+      ++ex;
+      if (!w) {
+        ok = false;
+        return v;
+      }
+      float acc = slot[lane];
+#pragma unroll
+      for (int o = 1; o < SPL; ++o) acc = op(acc, slot[o * 32 + lane]);
+      return acc;
+    };
     for (int r = 0; ok && r * static_cast<int>(gridDim.x) < p.n_items; ++r) {
       const int i = prefill_round_item(p, r);
       if (i < 0) continue;
@@ -532,38 +597,43 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
           break;
         }
         tc_fence_after();
-        const int k0 = it.k_first + j * kPfTile;
-        uint32_t sr[128];
-        tmem_ld128(s_addr, sr);  // one round trip: TMEM load latency dominates a chunked read
+        const int kt = it.k_first + j * kPfTile;  // the tile's first key
+        const int k0 = kt + h * KC;               // this slice's first key
+        uint32_t sr[KC];
+        if constexpr (KC == 128) tmem_ld128(s_addr, sr);  // one round trip: the latency dominates
+        else tmem_ld64(s_addr, sr);
         if constexpr (QT == 1) {  // S is read: the issuer may compute the next one into it
           tc_fence_before();
           mbar_arrive(s_free);
         }
         // raw scores; the scale is applied inside the exponent's FMA (scale > 0 keeps the max)
-        const bool full = k0 + kPfTile - 1 <= L + qbase &&
-                          (p.window < 0 || L + qbase + kPfTile - 1 - k0 <= p.window) &&
+        const bool full = kt + kPfTile - 1 <= L + qbase &&
+                          (p.window < 0 || L + qbase + kPfTile - 1 - kt <= p.window) &&
                           qbase + kPfTile <= p.T;
         if (!full) {
-          // this query row sees the key columns [c_lo, c_hi) of the tile (key <= pos, and
+          // this query row sees the key columns [c_lo, c_hi) of the slice (key <= pos, and
           // pos - key <= window): one unsigned compare a column against the interval's width
-          const int c_hi = valid ? min(kPfTile, pos - k0 + 1) : 0;
+          const int c_hi = valid ? min(KC, pos - k0 + 1) : 0;
           const int c_lo = p.window >= 0 ? max(0, pos - p.window - k0) : 0;
           const uint32_t width = c_hi > c_lo ? static_cast<uint32_t>(c_hi - c_lo) : 0u;
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < KC; ++c)
             if (static_cast<uint32_t>(c - c_lo) >= width) sr[c] = __float_as_uint(-INFINITY);
         }
-        // the row maximum in four independent chains (one chain would serialise 64 dependent
-        // max instructions); max is exact, so the order does not change the result
+        // the slice's row maximum in four independent chains, then the other slices' (max is
+        // exact: neither order changes the result)
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
+        for (int c = 0; c < KC / 8; ++c)
 #pragma unroll
           for (int u = 0; u < 4; ++u)
             m4[u] = fmax3(m4[u], __uint_as_float(sr[8 * c + 2 * u]), __uint_as_float(sr[8 * c + 2 * u + 1]));
         float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx = exchange(mx, [](float a, float b) { return fmaxf(a, b); });
+        if (!ok) break;
         mx *= p.scale_log2;
-        // lazy rescale: move the running max only when it grows by more than 2^8
+        // lazy rescale: move the running max only when it grows by more than 2^8 (every slice of
+        // the row takes the same decision: the same max, the same m_used)
         float alpha = 1.f;
         if (mx > m_used + 8.f) {
           alpha = fast_exp2(m_used - mx);  // 0 when m_used is -inf
@@ -585,7 +655,7 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
         const uint64_t sc2 = pair_f32(p.scale_log2, p.scale_log2), nm2 = pair_f32(neg_m, neg_m);
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 columns of packed bf16 P over S
+        for (int c = 0; c < KC / 32; ++c) {  // 32 keys -> 16 columns of packed bf16 P
 #pragma unroll
           for (int u = 0; u < 8; ++u) {  // 4 keys: three exponentials on MUFU, one on the FMA pipe
             const int kx = 32 * c + 4 * u;
@@ -603,11 +673,11 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
           tmem_st16_nowait(p_addr + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&sr[32 * c]));
         }
         const float sum = sum0 + sum1;
-        l += sum;
+        l += sum;  // this slice's part of the row sum
         tmem_st_wait();
         if (cnt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < DC / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(o_addr + c * 32, o);
 #pragma unroll
@@ -628,14 +698,16 @@ __global__ void __launch_bounds__(pf_threads<QT>(), 3 - QT)
       }
       if (ok && !__all_sync(0xffffffffu, mbar_wait_or_abort(o_done, k & 1, abort_flag))) ok = false;
       if (ok && cnt > 0) {
+        // the row sum: the slices' parts added in slice order
+        const float lt = exchange(l, [](float a, float b) { return a + b; });
         tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint16_t* dst = p.out + ((static_cast<long long>(it.b) * p.T + q) * p.Hq + it.h) * D;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        uint16_t* dst = p.out + ((static_cast<long long>(it.b) * p.T + q) * p.Hq + it.h) * D + h * DC;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < DC / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
-          if (valid) {
+          if (valid && ok) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               uint4 w;

@@ -1,6 +1,7 @@
-"""torch.ops.mcb200 without a GPU: libmcb200_torch.so loads, the five operators carry the schemas
-SURVEY's boundary plans (kv_append_rope, kv_broadcast, decode_attn, plus the fused append_attn and
-kv_advance), and their shape functions answer on meta tensors -- what torch.compile traces with."""
+"""torch.ops.mcb200 without a GPU: libmcb200_torch.so loads, the operators carry the boundary's
+schemas (kv_append_rope, kv_broadcast, decode_attn, the fused append_attn, kv_advance, and the
+decode step's linear and add_rms_norm), and their shape functions answer on meta tensors -- what
+torch.compile traces with."""
 import torch
 
 

@@ -187,6 +187,15 @@ def _dist_setup(n_gpus):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
+        # every rank counts the communicator's members with one all_reduce and says so on stderr,
+        # beside NCCL's own init lines
+        t = torch.ones(1, device="cuda")
+        dist.all_reduce(t)
+        n = int(t.item())
+        print(f"bench: rank {rank} of {world} on cuda:{local}: an NCCL all_reduce over the process group "
+              f"counted {n} ranks", file=sys.stderr, flush=True)
+        if n != world:
+            raise SystemExit(f"the NCCL communicator holds {n} ranks, WORLD_SIZE={world}")
     return rank, world, local
 
 

@@ -51,7 +51,8 @@ namespace mcb {
 
 constexpr int kPfTile = 128;          // queries per query tile and keys per key tile
 // QT query tiles an item (2: one CTA per SM, ten warps, all 512 TMEM columns; 1: two CTAs per SM,
-// six warps and 256 TMEM columns each, every query tile an independent chain)
+// ten warps -- two softmax warps a row quarter -- and 256 TMEM columns each, every query tile an
+// independent chain)
 // Softmax warps a row quarter, each taking 128 / pf_split of a tile's key columns.  One query tile
 // an item (two CTAs an SM, one softmax chain each): two, so that an SM sub-partition holds four
 // softmax warps that hide one another's exponential and TMEM-load latency (config 2's 64 x 512

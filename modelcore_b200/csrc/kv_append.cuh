@@ -411,11 +411,18 @@ __global__ void __launch_bounds__(kAppendVecThreads, 4)
   const long long warps = static_cast<long long>(gridDim.x) * (kAppendVecThreads / 32);
   const long long stride = warps * VPW;  // vectors per sweep of the grid
   const long long first = (static_cast<long long>(blockIdx.x) * (kAppendVecThreads / 32) + (threadIdx.x >> 5)) * VPW;
-  for (long long base = first; base < p.total_vectors; base += stride) {  // warp-uniform
-    AppendVecLoad v;
-    append_vec_load<D>(p, base + lane / L, sub, v);
-    append_vec_tables<D>(p, sub, v);
-    append_vec_store<D, FP8>(p, v, sub);
+  // two vector groups a sweep, both groups' loads issued before either's arithmetic and stores:
+  // twice the bytes in flight a warp (a group past the end loads vector 0 and stores nothing);
+  // one for an fp8 cache, whose scale butterfly would spill at the 64-register cap
+  constexpr int U = FP8 ? 1 : 2;
+  for (long long base = first; base < p.total_vectors; base += U * stride) {  // warp-uniform
+    AppendVecLoad v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) append_vec_load<D>(p, base + u * stride + lane / L, sub, v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) append_vec_tables<D>(p, sub, v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) append_vec_store<D, FP8>(p, v[u], sub);
   }
 }
 

@@ -60,9 +60,12 @@ import time
 
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
     # NCCL's init lines (one per rank, with the communicator's rank count) stay in the log, so a
-    # reader of the run can count the ranks that joined; a caller's own setting wins.  Set before
-    # torch loads NCCL, which reads them once.
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    # reader of the run can count the ranks that joined.  A preset level below INFO (the GPU
+    # boxes' environment sets VERSION, which prints one version line and no rank) is raised to
+    # INFO, limited to the INIT subsystem unless the caller chose subsystems.  Set before torch
+    # loads NCCL, which reads them once.
+    if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+        os.environ["NCCL_DEBUG"] = "INFO"
     os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
 REPO = os.path.dirname(os.path.abspath(__file__))

@@ -90,3 +90,23 @@ def test_a_rank_that_leaves_before_the_gather_is_reported_not_waited_on():
     res = _run("leave")
     assert res[1] == "left"
     assert str(res[0]).startswith("error:")
+
+
+@pytest.mark.parametrize("world,preset,expected", [("2", "VERSION", "INFO"), ("2", None, "INFO"),
+                                                   ("2", "TRACE", "TRACE"), ("1", "VERSION", "VERSION")])
+def test_bench_raises_nccl_logging_to_init_lines_at_more_than_one_rank(world, preset, expected):
+    # bench.py's module top only touches the environment (stdlib imports): load it in a child
+    import subprocess
+    import sys
+    env = {k: v for k, v in os.environ.items() if not k.startswith("NCCL_DEBUG")}
+    env["WORLD_SIZE"] = world
+    if preset is not None:
+        env["NCCL_DEBUG"] = preset
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import os, runpy; runpy.run_path(os.path.join(%r, 'bench.py'), run_name='not_main'); "
+            "print(os.environ.get('NCCL_DEBUG'), os.environ.get('NCCL_DEBUG_SUBSYS'))" % root)
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    level, subsys = out.stdout.split()
+    assert level == expected
+    assert subsys == ("INIT" if world == "2" else "None")
